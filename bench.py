@@ -1,0 +1,455 @@
+"""Benchmark of the quantized-weight decode GEMV (the reference's headline path).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mlq|reference]
+
+Workload: one Qwen2-7B-shaped layer plus lm_head
+in q4_0 -- QKV 4608x3584, O 3584x3584, gate/up 18944x3584, down 3584x18944,
+lm_head 152064x3584 -- decoded at batch 1 with fp32 activations.  A step is
+one pass over the six matrices (437,649,408 bytes of packed weights, larger
+than the 126 MB L2, so no L2 flush is needed between steps).  Weights are
+seeded N(0, 0.02) fp32 quantized by the library's reference-exact q4_0
+quantizer; activations are seeded N(0, 1).
+
+Metric: effective weight GB/s = packed weight bytes / time.  One JSON line on
+stdout (rank 0).  --impl reference times the reference's own CPU
+implementation (src/quant.cc linearQ40 through ThreadPool, compiled from
+the reference's sources into oracle/_ref/) on this machine's host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import importlib.util
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+PKG_DIR = ROOT / "mini-llama_b200"
+MB = 1_000_000
+
+WORKLOAD = {
+    "name": "qwen2-7b-layer+lm_head q4_0 decode (BASELINE configs[1])",
+    "fmt": "q4_0",
+    "rows": 1,
+    "matrices": [("qkv", 4608, 3584), ("o", 3584, 3584), ("gate", 18944, 3584),
+                 ("up", 18944, 3584), ("down", 3584, 18944), ("lm_head", 152064, 3584)],
+}
+METRIC = "effective weight GB/s (q4_0 decode GEMV, Qwen2-7B layer + lm_head, batch 1)"
+UNIT = "GB/s"
+
+
+def load_pkg():
+    spec = importlib.util.spec_from_file_location(
+        "mini_llama_b200", PKG_DIR / "__init__.py", submodule_search_locations=[str(PKG_DIR)])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["mini_llama_b200"] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def weight_bytes(fmt, out_f, in_f):
+    bs = {"q8_0": 34, "q4_0": 18, "q4_1": 20}[fmt]
+    return out_f * ((in_f + 31) // 32) * bs
+
+
+def hbm_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return 6650.0, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region (NVML, the data nvidia-smi reports)
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    REASONS = {
+        "gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4,
+        "hw_slowdown": 0x8, "sync_boost": 0x10, "sw_thermal_slowdown": 0x20,
+        "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80,
+    }
+
+    def __init__(self, device_index: int, period_s: float = 0.02):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self.period = period_s
+        self._stop = threading.Event()
+        self.ok = False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            self.ok = False
+
+    def _run(self):
+        nv = self.nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                mask = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for k, bit in self.REASONS.items():
+                    if mask & bit and k != "gpu_idle":
+                        self.reasons.add(k)
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.ok:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self.ok:
+            self._stop.set()
+            self.t.join()
+
+    def summary(self):
+        if not self.ok or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                    "samples": len(self.samples)}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the reference's own CPU path (oracle/_ref), all host threads
+# ---------------------------------------------------------------------------
+def host_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def cpu_has_avx2():
+    try:
+        return "avx2" in Path("/proc/cpuinfo").read_text()
+    except Exception:
+        return False
+
+
+class ReferenceCPU:
+    """The reference's CPU linearQ40 (oracle/_ref, built from its sources)
+    over row samples of the workload's matrices, all host threads."""
+
+    def __init__(self):
+        sys.path.insert(0, str(ROOT))
+        from oracle.oracle import Oracle, Reference  # checker / CPU baseline only
+        variant = "avx2" if (cpu_has_avx2() and Reference.available("avx2")) else "scalar"
+        if not Reference.available(variant):
+            raise FileNotFoundError("oracle/_ref was not built")
+        self.ref = Reference(variant)
+        self.variant = f"libref_{variant}.so"
+        self.cores = host_cores()
+        self.ref.set_threads(self.cores)
+        self.orc = Oracle()
+        self.handles = []
+
+    def load(self, pkg, frac):
+        """Quantize the first ceil(frac*out) rows of every matrix (seeded)."""
+        self.release()
+        fmt = WORKLOAD["fmt"]
+        self.parts = []
+        for i, (name, out_f, in_f) in enumerate(WORKLOAD["matrices"]):
+            rows = min(out_f, max(16 * self.cores, int(np.ceil(out_f * frac))))
+            w = pkg.synth.normal((rows, in_f), seed=1000 + i, std=0.02)
+            h = self.ref.hold(fmt, self.orc.quantize(fmt, w))
+            x = pkg.synth.normal((WORKLOAD["rows"], in_f), seed=2000 + i)
+            self.parts.append((h, x, rows, in_f, np.zeros((WORKLOAD["rows"], rows), np.float32)))
+            self.handles.append(h)
+        self.bytes = sum(weight_bytes(fmt, r, i) for _, _, r, i, _ in self.parts)
+
+    def step(self):
+        t0 = time.perf_counter()
+        for h, x, rows, in_f, y in self.parts:
+            self.ref.linear_held(WORKLOAD["fmt"], x, h, rows, y)
+        return time.perf_counter() - t0
+
+    def release(self):
+        for h in self.handles:
+            self.ref.release(WORKLOAD["fmt"], h)
+        self.handles = []
+
+    def calibrate(self, pkg):
+        """Seconds for one full pass over the workload, from a 1/32 sample."""
+        self.load(pkg, 1 / 32)
+        self.step()
+        t = min(self.step() for _ in range(2))
+        return t * (sum(weight_bytes(WORKLOAD["fmt"], o, i) for _, o, i in WORKLOAD["matrices"])
+                    / self.bytes)
+
+
+def reference_cpu_baseline(pkg, seconds):
+    """Bounded sample (~`seconds` of CPU work) of the workload on the
+    reference's CPU path; returns the cpu_baseline dict."""
+    try:
+        rc = ReferenceCPU()
+    except FileNotFoundError as e:
+        return {"unavailable": str(e)}
+    t_pass = rc.calibrate(pkg)
+    frac = min(1.0, seconds / 4 / t_pass)
+    rc.load(pkg, frac)
+    rc.step()
+    total, steps = 0.0, 0
+    while total < seconds and steps < 1000:
+        total += rc.step()
+        steps += 1
+    gbs = rc.bytes * steps / total / 1e9
+    rc.release()
+    return {"value": round(gbs, 3), "unit": UNIT, "kind": "reference", "cores": rc.cores,
+            "sample": f"{steps} passes of linearQ40 over the first {frac:.1%} of every matrix's "
+                      f"rows ({rc.bytes / MB:.1f} MB/pass), {total:.1f} s, "
+                      f"ThreadPool threads = {rc.cores}, {rc.variant}"}
+
+
+# ---------------------------------------------------------------------------
+def make_inputs(torch, pkg, device):
+    """Quantized weights on the device (+ host copies) and x vectors."""
+    fmt = WORKLOAD["fmt"]
+    g = torch.Generator(device=device)
+    ws, xs_dev, xs_host = [], [], []
+    for i, (name, out_f, in_f) in enumerate(WORKLOAD["matrices"]):
+        g.manual_seed(1000 + i)
+        w32 = torch.randn((out_f, in_f), generator=g, device=device, dtype=torch.float32) * 0.02
+        ws.append(pkg.mlq.quantize(fmt, w32))
+        del w32
+        x = pkg.synth.normal((WORKLOAD["rows"], in_f), seed=2000 + i)
+        xs_host.append(x)
+        xs_dev.append(torch.from_numpy(x).to(device))
+    torch.cuda.synchronize(device)
+    return ws, xs_dev, xs_host
+
+
+def run_mlq(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+    pkg = load_pkg()
+    mlq = pkg.mlq
+    fmt = WORKLOAD["fmt"]
+    mats = WORKLOAD["matrices"]
+    ws, xs, xs_host = make_inputs(torch, pkg, device)
+    ys = [torch.empty((WORKLOAD["rows"], o), dtype=torch.float32, device=device) for _, o, _ in mats]
+    bytes_step = sum(weight_bytes(fmt, o, i) for _, o, i in mats)
+    nblocks = [w.numel() // mlq.BLOCK_BYTES[fmt] for w in ws]
+    stream = torch.cuda.Stream(device)
+    sh = stream.cuda_stream
+    L = mlq.lib()
+
+    def step(events=None):
+        for j, (name, out_f, in_f) in enumerate(mats):
+            if events is not None:
+                events[j][0].record(stream)
+            st = L.mlq_linear(2, ws[j].data_ptr(), nblocks[j], out_f, in_f, xs[j].data_ptr(),
+                              WORKLOAD["rows"], ys[j].data_ptr(), sh)
+            if st != 0:
+                raise RuntimeError(L.mlq_last_error().decode())
+            if events is not None:
+                events[j][1].record(stream)
+
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, args.warmup)):
+            step()
+    torch.cuda.synchronize(device)
+
+    # ---- headline: K steps on the device, inputs resident in HBM ----
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        t0.record(stream)
+        with torch.cuda.stream(stream):
+            for _ in range(args.steps):
+                step()
+        t1.record(stream)
+        t1.synchronize()
+    ms = t0.elapsed_time(t1)
+    if world > 1:
+        tm = torch.tensor([ms], device=device)
+        dist.all_reduce(tm, op=dist.ReduceOp.MAX)
+        ms = float(tm.item())
+    torch.cuda.synchronize(device)
+    value = bytes_step * args.steps * world / (ms / 1e3) / 1e9
+
+    # ---- per-launch durations of the dominant kernel (CUDA events on its stream) ----
+    k2 = max(20, min(args.steps, 400))
+    evs = [[[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)]
+            for _ in mats] for _ in range(k2)]
+    with torch.cuda.stream(stream):
+        for k in range(k2):
+            step(evs[k])
+    torch.cuda.synchronize(device)
+    per = {name: statistics.mean(evs[k][j][0].elapsed_time(evs[k][j][1]) for k in range(k2))
+           for j, (name, _, _) in enumerate(mats)}
+    peak, peak_kind = hbm_peak()
+    dom = "lm_head"
+    dom_bytes = weight_bytes(fmt, 152064, 3584)
+    achieved = dom_bytes / (per[dom] / 1e3) / 1e9
+    kernel_sum_ms = sum(per.values())
+    traffic = read_traffic()
+
+    # ---- e2e: host x / host y through the C ABI (copies inside the timed region) ----
+    e2e = None
+    if not args.no_e2e:
+        xh = [torch.from_numpy(x).pin_memory() for x in xs_host]
+        yh = [torch.empty((WORKLOAD["rows"], o), dtype=torch.float32).pin_memory() for _, o, _ in mats]
+        ke = max(3, min(args.steps, 300))
+
+        def e2e_step():
+            for j, (name, out_f, in_f) in enumerate(mats):
+                st = L.mlq_linear_host(2, ws[j].data_ptr(), nblocks[j], out_f, in_f,
+                                       xh[j].data_ptr(), WORKLOAD["rows"], None, yh[j].data_ptr(),
+                                       local, sh)
+                if st != 0:
+                    raise RuntimeError(L.mlq_last_error().decode())
+        for _ in range(3):
+            e2e_step()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(ke):
+            e2e_step()
+        e1.record(stream)
+        e1.synchronize()
+        ems = e0.elapsed_time(e1)
+        if world > 1:
+            tm = torch.tensor([ems], device=device)
+            dist.all_reduce(tm, op=dist.ReduceOp.MAX)
+            ems = float(tm.item())
+        e2e = {"value": round(bytes_step * ke * world / (ems / 1e3) / 1e9, 2), "unit": UNIT,
+               "h2d_bytes_per_step": sum(4 * WORKLOAD["rows"] * i for _, _, i in mats),
+               "d2h_bytes_per_step": sum(4 * WORKLOAD["rows"] * o for _, o, _ in mats),
+               "steps": ke, "path": "mlq_linear_host (device weights, pinned host x/y)"}
+
+    err = mlq.device_error(local)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = reference_cpu_baseline(pkg, args.cpu_seconds)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5),
+            "higher_is_better": True, "scaling": "weak" if world > 1 else "weak",
+            "vs_baseline": None, "dtype": "fp32 activations x q4_0 weights",
+            "data": "synthetic (seeded N(0,0.02) weights quantized to q4_0; N(0,1) x)",
+            "config": {"workload": WORKLOAD["name"], "format": fmt, "batch": WORKLOAD["rows"],
+                       "matrices": {n: [o, i] for n, o, i in mats},
+                       "weight_bytes_per_step": bytes_step,
+                       "l2": "inputs larger than L2 (437.6 MB per step vs 126 MB L2); no flush"},
+            "roofline": {"bound": "hbm", "kernel": "gemv_stream_kernel<q4_0,1,4> (lm_head launch)",
+                         "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                         "traffic": traffic, "algorithmic_bytes_per_launch": dom_bytes,
+                         "launch_ms": round(per[dom], 5),
+                         "all_launches_GBps": round(bytes_step / (kernel_sum_ms / 1e3) / 1e9, 1),
+                         "per_launch_ms": {k: round(v, 5) for k, v in per.items()}},
+            "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps * len(mats),
+            "clocks": clocks.summary(), "device_error": err,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def read_traffic():
+    """DRAM bytes per lm_head launch from the committed ncu summary, if any."""
+    p = ROOT / "profiles" / "gemv_q4_0_lm_head.txt"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_launch:"):
+            try:
+                return int(line.split(":", 1)[1].strip())
+            except ValueError:
+                return None
+    return None
+
+
+def run_reference(args):
+    """--impl reference: the reference's own CPU implementation of the path
+    (oracle/_ref) on this host's cores; each step is a row sample of the
+    workload sized so the whole run stays within ~2.5 minutes."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return  # single-process CPU code: only rank 0 runs and prints
+    pkg = load_pkg()
+    fmt = WORKLOAD["fmt"]
+    base = {"impl": "reference", "metric": METRIC, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "fp32 activations x q4_0 weights",
+            "data": "synthetic (seeded N(0,0.02) weights quantized to q4_0; N(0,1) x)",
+            "config": {"workload": WORKLOAD["name"], "format": fmt, "batch": WORKLOAD["rows"]}}
+    try:
+        rc = ReferenceCPU()
+    except FileNotFoundError as e:
+        print(json.dumps({"impl": "reference", "unavailable": str(e)}), flush=True)
+        return
+    t_pass = rc.calibrate(pkg)
+    budget = 150.0
+    frac = min(1.0, budget / (max(1, args.steps + args.warmup) * t_pass))
+    rc.load(pkg, frac)
+    for _ in range(max(1, args.warmup)):
+        rc.step()
+    total = sum(rc.step() for _ in range(args.steps))
+    value = rc.bytes * args.steps / total / 1e9
+    rc.release()
+    sample = (f"each step: linearQ40 over the first {frac:.2%} of every matrix's rows "
+              f"({rc.bytes / MB:.1f} MB), ThreadPool threads = {rc.cores}, {rc.variant}")
+    line = dict(base)
+    line.update({
+        "value": round(value, 3), "ms_per_step": round(total / args.steps * 1e3, 3),
+        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "kind": "reference",
+                         "cores": rc.cores, "sample": sample},
+        "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    })
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="mlq", choices=["mlq", "reference"])
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_mlq(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,146 @@
+/*
+ * mlq.h -- C ABI of the B200 quantized-matmul library (libmlq.so).
+ *
+ * Replaces the GPU half of the reference's quantized linear path
+ * (Haobin-Lee/mini-llama): include/mini_llama/cuda_quant.h and the kernels
+ * in src/cuda_quant.cu.  Plain C: pointers, sizes, status codes, a CUDA
+ * stream handle.  No C++ types, no exceptions, no torch types cross it.
+ *
+ * Conventions shared by every entry point
+ *   - Weights are the reference's packed block arrays, byte-identical to
+ *     std::vector<BlockQ80/BlockQ40/BlockQ41>::data()
+ *     (include/mini_llama/quantized_tensor.h:36-72): row-major [out][bpr]
+ *     with bpr = ceil(in/32) blocks per row.
+ *   - x is fp32 row-major [rows][in]; y is fp32 row-major [rows][out];
+ *     y = x * W^T, overwritten (not accumulated into).
+ *   - Arguments are validated on the host BEFORE any CUDA call, with the
+ *     reference's checks (src/cuda_quant.cu:188-227, 305-307, 342-345);
+ *     a failing check returns a status and leaves the GPU untouched.
+ *     mlq_last_error() then returns a message (per host thread).
+ *   - `stream` is a cudaStream_t (NULL = the legacy default stream, which
+ *     is what the reference launches on).  Device-side entry points are
+ *     asynchronous on that stream; *_host entry points are synchronous.
+ *   - The current CUDA device must own every device pointer passed.
+ */
+#ifndef MLQ_H_
+#define MLQ_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define MLQ_API __attribute__((visibility("default")))
+#else
+#define MLQ_API
+#endif
+
+/* A cudaStream_t, spelled without including the CUDA headers. */
+typedef struct CUstream_st* mlq_stream;
+
+/* Block formats; the values are the GGUF tensor type ids the reference's
+ * loader maps to QuantType (include/mini_llama/gguf.h:16-22). */
+typedef enum mlq_format {
+    MLQ_Q4_0 = 2, /* BlockQ40: fp16 d + 16 nibble bytes, 18 B / 32 values */
+    MLQ_Q4_1 = 3, /* BlockQ41: fp16 d, fp16 m + 16 bytes, 20 B / 32 values */
+    MLQ_Q8_0 = 8  /* BlockQ80: fp16 d + 32 int8,          34 B / 32 values */
+} mlq_format;
+
+typedef enum mlq_status {
+    MLQ_OK = 0,
+    MLQ_ERR_FORMAT = 1,      /* unknown mlq_format */
+    MLQ_ERR_NULL = 2,        /* null pointer ("null weight pointer", cuda_quant.cu:305-307) */
+    MLQ_ERR_EMPTY = 3,       /* a dimension <= 0 ("empty tensors are not supported", :209-212) */
+    MLQ_ERR_SHAPE = 4,       /* x/W in_features mismatch (:213-218) */
+    MLQ_ERR_BLOCK_COUNT = 5, /* block_count != out*ceil(in/32) (:219-226) */
+    MLQ_ERR_DEVICE = 6,      /* bad device id / pointer on another device (:342-345) */
+    MLQ_ERR_CUDA = 7,        /* a CUDA runtime call failed (:20-29) */
+    MLQ_ERR_TIMEOUT = 8,     /* a kernel's bounded wait expired (device error flag set) */
+    MLQ_ERR_RANGE = 9,       /* a size too large for this entry point */
+    MLQ_ERR_COMM = 10        /* a sharded call's peer/rank arguments are inconsistent */
+} mlq_status;
+
+/* ---------------------------------------------------------------------------
+ * Library facts
+ * ------------------------------------------------------------------------- */
+
+/* 1 when the CUDA kernels are compiled in.  Replaces cudaQuantBuilt()
+ * (include/mini_llama/cuda_quant.h:13). */
+MLQ_API int mlq_built(void);
+
+/* Bytes of one block (34/18/20) or 0 for an unknown format
+ * (sizeof(BlockQ80/Q40/Q41), quantized_tensor.h:41,55,71). */
+MLQ_API size_t mlq_block_bytes(mlq_format fmt);
+
+/* out * ceil(in/32): the block count the validation expects
+ * (src/cuda_quant.cu:219-220); 0 when a dimension is not positive. */
+MLQ_API size_t mlq_block_count(int out_features, int in_features);
+
+MLQ_API const char* mlq_status_string(mlq_status status);
+
+/* Message for the last failing call on this host thread ("" if none). */
+MLQ_API const char* mlq_last_error(void);
+
+/* Reads and clears the device-side error flag of `device` (non-zero after
+ * a kernel gave up on a bounded wait).  Synchronizes that device. */
+MLQ_API mlq_status mlq_device_error(int device, int* code);
+
+/* ---------------------------------------------------------------------------
+ * Quantized linear
+ * ------------------------------------------------------------------------- */
+
+/* Device weight, device x, device y:  y[rows,out] = x[rows,in] * W^T.
+ * Replaces cudaQ80LinearDeviceInput / cudaQ40LinearDeviceInput /
+ * cudaQ41LinearDeviceInput (include/mini_llama/cuda_quant.h:29-33, 50-54,
+ * 69-73; src/cuda_quant.cu:333-361, 411-439, 489-517), except that the
+ * caller passes y instead of receiving a freshly cudaMalloc'd CudaTensor.
+ * rows >= 1 (the reference's rank-1 x is rows == 1).  Asynchronous. */
+MLQ_API mlq_status mlq_linear(mlq_format fmt, const void* w, size_t block_count,
+                              int out_features, int in_features, const float* x, int rows,
+                              float* y, mlq_stream stream);
+
+/* Device weight, HOST x, HOST y, optional HOST bias[out] added to every row
+ * after the product.  Replaces cudaQ80LinearDeviceWeight /
+ * cudaQ40LinearDeviceWeight / cudaQ41LinearDeviceWeight
+ * (cuda_quant.h:22-27, 43-48, 62-67; src/cuda_quant.cu:300-331).  Runs on
+ * `device` and returns after y is on the host.  x/y may be pageable; with
+ * pinned memory the copies are asynchronous DMA on `stream`. */
+MLQ_API mlq_status mlq_linear_host(mlq_format fmt, const void* w, size_t block_count,
+                                   int out_features, int in_features, const float* x_host,
+                                   int rows, const float* bias_host, float* y_host, int device,
+                                   mlq_stream stream);
+
+/* HOST weight blocks, HOST x, HOST y, optional HOST bias.  Uploads the
+ * weights for this one call.  Replaces cudaQ80Linear / cudaQ40Linear /
+ * cudaQ41Linear (cuda_quant.h:17-20, 39-41, 58-60; cuda_quant.cu:289-298). */
+MLQ_API mlq_status mlq_linear_host_weight(mlq_format fmt, const void* w_host, size_t block_count,
+                                          int out_features, int in_features,
+                                          const float* x_host, int rows, const float* bias_host,
+                                          float* y_host, int device);
+
+/* ---------------------------------------------------------------------------
+ * Format conversion on the device
+ * ------------------------------------------------------------------------- */
+
+/* Blocks -> fp32 [out][in], bit-identical to the reference's
+ * dequantizeFromQ80/Q40/Q41 (src/quant.cc:192-223, 304-345, 350-392). */
+MLQ_API mlq_status mlq_dequantize(mlq_format fmt, const void* w, size_t block_count,
+                                  int out_features, int in_features, float* dst,
+                                  mlq_stream stream);
+
+/* fp32 [rows][cols] -> blocks.  q8_0 and q4_0 are bit-identical to the
+ * reference's quantizeToQ80 / quantizeToQ40 (src/quant.cc:130-190,
+ * 228-302).  q4_1 has no reference quantizer; this library's rule is
+ * d = (max-min)/15, m = min (fp16, the reference's encoder), codes
+ * round((x - m)/d) against the stored d, m. */
+MLQ_API mlq_status mlq_quantize(mlq_format fmt, const float* src, int rows, int cols,
+                                void* blocks, mlq_stream stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif /* MLQ_H_ */

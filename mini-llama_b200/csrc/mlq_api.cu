@@ -1,0 +1,326 @@
+// mlq_api.cu -- the C ABI of libmlq.so (declared in include/mlq.h).
+//
+// Host-side validation follows the reference's checks
+// (src/cuda_quant.cu:188-227, 305-307, 342-345) and runs before any CUDA
+// call, so a rejected call never touches the GPU.  Nothing here throws
+// across the ABI: failures return an mlq_status and leave a message for
+// mlq_last_error().
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/mlq.h"
+#include "mlq_device.cuh"
+#include "mlq_kernels.h"
+
+// Device-side error flag, one per device context (see mlq_device_error).
+__device__ int g_mlq_device_error = 0;
+
+namespace {
+
+thread_local std::string t_last_error;
+
+mlq_status fail(mlq_status st, const std::string& msg) {
+    t_last_error = msg;
+    return st;
+}
+
+mlq_status fail_cuda(const char* what, cudaError_t e) {
+    cudaGetLastError();  // clear a sticky launch error so the next call starts clean
+    return fail(MLQ_ERR_CUDA, std::string("CUDA error in ") + what + ": " + cudaGetErrorString(e));
+}
+
+constexpr int kMaxDevices = 64;
+constexpr int kSmemBudget = 232448 - 1024;  // dynamic smem per CTA, leaving room for static
+
+struct DeviceState {
+    std::once_flag once;
+    cudaError_t init_err = cudaSuccess;
+    int sm_count = 0;
+    int* err_flag = nullptr;  // device address of g_mlq_device_error
+    std::mutex host_mu;       // serialises the *_host entry points' staging
+    float* x_stage = nullptr;
+    float* y_stage = nullptr;
+    size_t x_cap = 0, y_cap = 0;
+};
+
+DeviceState g_dev[kMaxDevices];
+
+// Must be called with `dev` current.
+DeviceState* device_state(int dev, mlq_status* st) {
+    if (dev < 0 || dev >= kMaxDevices) {
+        *st = fail(MLQ_ERR_DEVICE, "device id out of range");
+        return nullptr;
+    }
+    DeviceState& s = g_dev[dev];
+    std::call_once(s.once, [&] {
+        cudaError_t e = cudaDeviceGetAttribute(&s.sm_count, cudaDevAttrMultiProcessorCount, dev);
+        if (e == cudaSuccess) e = cudaGetSymbolAddress(reinterpret_cast<void**>(&s.err_flag), g_mlq_device_error);
+        s.init_err = e;
+    });
+    if (s.init_err != cudaSuccess) {
+        *st = fail_cuda("device setup", s.init_err);
+        return nullptr;
+    }
+    return &s;
+}
+
+bool known_format(int fmt) { return fmt == MLQ_Q8_0 || fmt == MLQ_Q4_0 || fmt == MLQ_Q4_1; }
+
+const char* fmt_name(int fmt) {
+    return fmt == MLQ_Q8_0 ? "Q80" : (fmt == MLQ_Q4_0 ? "Q40" : (fmt == MLQ_Q4_1 ? "Q41" : "?"));
+}
+
+// The reference's validateQuantLinearShape (src/cuda_quant.cu:198-227) plus
+// its null-weight check (:305-307), in the same order.
+mlq_status validate_linear(int fmt, const void* w, size_t block_count, int out, int in,
+                           const void* x, int rows, const void* y, const char* caller) {
+    if (!known_format(fmt)) return fail(MLQ_ERR_FORMAT, std::string(caller) + ": unknown block format");
+    const std::string who = std::string(caller) + "(" + fmt_name(fmt) + ")";
+    if (w == nullptr) return fail(MLQ_ERR_NULL, who + ": null weight pointer");
+    if (in <= 0 || out <= 0 || rows <= 0)
+        return fail(MLQ_ERR_EMPTY, who + ": empty tensors are not supported");
+    if (x == nullptr || y == nullptr) return fail(MLQ_ERR_NULL, who + ": null input/output pointer");
+    const size_t expected = mlq_block_count(out, in);
+    if (block_count != expected)
+        return fail(MLQ_ERR_BLOCK_COUNT, who + ": block count mismatch: expected " +
+                                             std::to_string(expected) + ", got " +
+                                             std::to_string(block_count));
+    return MLQ_OK;
+}
+
+mlq_status run_linear(int fmt, const void* w, int out, int in, const float* x, int rows, float* y,
+                      cudaStream_t stream) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return fail_cuda("cudaGetDevice", e);
+    mlq_status st = MLQ_OK;
+    DeviceState* ds = device_state(dev, &st);
+    if (!ds) return st;
+
+    const int bpr = (in + mlq::kQK - 1) / mlq::kQK;
+    const int gblocks = fmt == MLQ_Q4_1 ? 1 : 2;
+    const uintptr_t wa = reinterpret_cast<uintptr_t>(w);
+    const uintptr_t xa = reinterpret_cast<uintptr_t>(x);
+    const bool streamable = (wa % 16 == 0) && (xa % 16 == 0) && (bpr % gblocks == 0) && (in % 4 == 0);
+    if (!streamable) {
+        e = mlq::launch_gemv_generic(fmt, static_cast<const uint8_t*>(w), x, y, out, in, rows, bpr, stream);
+        return e == cudaSuccess ? MLQ_OK : fail_cuda("gemv_generic launch", e);
+    }
+    mlq::GemvArgs a{};
+    a.w = static_cast<const uint8_t*>(w);
+    a.out = out;
+    a.in = in;
+    a.bpr = bpr;
+    a.gpr = bpr / gblocks;
+    a.ktiles = (a.gpr + 31) / 32;
+    a.y_stride = out;
+    a.row_bytes = (long long)bpr * mlq::block_bytes(fmt);
+    a.total_bytes = a.row_bytes * out;
+    a.err = ds->err_flag;
+    const int grid = out < ds->sm_count ? out : ds->sm_count;
+    for (int m0 = 0; m0 < rows;) {
+        const int mt = mlq::gemv_tokens_per_pass(rows - m0);
+        a.x = x + (long long)m0 * in;
+        a.y = y + (long long)m0 * out;
+        a.M = rows - m0 < mt ? rows - m0 : mt;
+        e = mlq::launch_gemv_stream(fmt, a, mt, grid, kSmemBudget, stream);
+        if (e != cudaSuccess) return fail_cuda("gemv_stream launch", e);
+        m0 += a.M;
+    }
+    return MLQ_OK;
+}
+
+// Grows a per-device staging buffer (called under host_mu, device current).
+mlq_status ensure(float** buf, size_t* cap, size_t bytes) {
+    if (*cap >= bytes) return MLQ_OK;
+    if (*buf) cudaFree(*buf);
+    *buf = nullptr;
+    *cap = 0;
+    cudaError_t e = cudaMalloc(reinterpret_cast<void**>(buf), bytes);
+    if (e != cudaSuccess) return fail_cuda("cudaMalloc (staging)", e);
+    *cap = bytes;
+    return MLQ_OK;
+}
+
+mlq_status set_device(int device) {
+    int count = 0;
+    cudaError_t e = cudaGetDeviceCount(&count);
+    if (e != cudaSuccess) return fail_cuda("cudaGetDeviceCount", e);
+    if (device < 0 || device >= count)
+        return fail(MLQ_ERR_DEVICE, "device id " + std::to_string(device) + " not present (" +
+                                        std::to_string(count) + " devices)");
+    e = cudaSetDevice(device);
+    return e == cudaSuccess ? MLQ_OK : fail_cuda("cudaSetDevice", e);
+}
+
+}  // namespace
+
+extern "C" {
+
+MLQ_API int mlq_built(void) { return 1; }
+
+MLQ_API size_t mlq_block_bytes(mlq_format fmt) { return (size_t)mlq::block_bytes((int)fmt); }
+
+MLQ_API size_t mlq_block_count(int out_features, int in_features) {
+    if (out_features <= 0 || in_features <= 0) return 0;
+    return (size_t)out_features * (size_t)((in_features + mlq::kQK - 1) / mlq::kQK);
+}
+
+MLQ_API const char* mlq_status_string(mlq_status s) {
+    switch (s) {
+        case MLQ_OK: return "ok";
+        case MLQ_ERR_FORMAT: return "unknown block format";
+        case MLQ_ERR_NULL: return "null pointer";
+        case MLQ_ERR_EMPTY: return "empty tensors are not supported";
+        case MLQ_ERR_SHAPE: return "dimension mismatch";
+        case MLQ_ERR_BLOCK_COUNT: return "block count mismatch";
+        case MLQ_ERR_DEVICE: return "invalid device";
+        case MLQ_ERR_CUDA: return "CUDA error";
+        case MLQ_ERR_TIMEOUT: return "kernel wait timed out";
+        case MLQ_ERR_RANGE: return "size out of range";
+        case MLQ_ERR_COMM: return "inconsistent sharding arguments";
+    }
+    return "unknown status";
+}
+
+MLQ_API const char* mlq_last_error(void) { return t_last_error.c_str(); }
+
+MLQ_API mlq_status mlq_device_error(int device, int* code) {
+    try {
+        if (!code) return fail(MLQ_ERR_NULL, "mlq_device_error: null code pointer");
+        int prev = 0;
+        cudaGetDevice(&prev);
+        mlq_status st = set_device(device);
+        if (st != MLQ_OK) return st;
+        DeviceState* ds = device_state(device, &st);
+        if (ds) {
+            cudaError_t e = cudaDeviceSynchronize();
+            int v = 0;
+            if (e == cudaSuccess) e = cudaMemcpy(&v, ds->err_flag, sizeof(int), cudaMemcpyDeviceToHost);
+            if (e == cudaSuccess) e = cudaMemset(ds->err_flag, 0, sizeof(int));
+            if (e == cudaSuccess) e = cudaDeviceSynchronize();
+            if (e != cudaSuccess) st = fail_cuda("mlq_device_error", e);
+            *code = v;
+        }
+        cudaSetDevice(prev);
+        return st;
+    } catch (...) {
+        return fail(MLQ_ERR_CUDA, "mlq_device_error: host exception");
+    }
+}
+
+MLQ_API mlq_status mlq_linear(mlq_format fmt, const void* w, size_t block_count, int out_features,
+                              int in_features, const float* x, int rows, float* y,
+                              mlq_stream stream) {
+    try {
+        mlq_status st =
+            validate_linear(fmt, w, block_count, out_features, in_features, x, rows, y, "mlq_linear");
+        if (st != MLQ_OK) return st;
+        return run_linear(fmt, w, out_features, in_features, x, rows, y,
+                          reinterpret_cast<cudaStream_t>(stream));
+    } catch (...) {
+        return fail(MLQ_ERR_CUDA, "mlq_linear: host exception");
+    }
+}
+
+MLQ_API mlq_status mlq_linear_host(mlq_format fmt, const void* w, size_t block_count,
+                                   int out_features, int in_features, const float* x_host,
+                                   int rows, const float* bias_host, float* y_host, int device,
+                                   mlq_stream stream) {
+    try {
+        mlq_status st = validate_linear(fmt, w, block_count, out_features, in_features, x_host, rows,
+                                        y_host, "mlq_linear_host");
+        if (st != MLQ_OK) return st;
+        st = set_device(device);
+        if (st != MLQ_OK) return st;
+        DeviceState* ds = device_state(device, &st);
+        if (!ds) return st;
+        cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+        std::lock_guard<std::mutex> lock(ds->host_mu);
+        const size_t xb = (size_t)rows * in_features * sizeof(float);
+        const size_t yb = (size_t)rows * out_features * sizeof(float);
+        if ((st = ensure(&ds->x_stage, &ds->x_cap, xb)) != MLQ_OK) return st;
+        if ((st = ensure(&ds->y_stage, &ds->y_cap, yb)) != MLQ_OK) return st;
+        cudaError_t e = cudaMemcpyAsync(ds->x_stage, x_host, xb, cudaMemcpyHostToDevice, s);
+        if (e != cudaSuccess) return fail_cuda("cudaMemcpyAsync (x upload)", e);
+        st = run_linear(fmt, w, out_features, in_features, ds->x_stage, rows, ds->y_stage, s);
+        if (st != MLQ_OK) return st;
+        e = cudaMemcpyAsync(y_host, ds->y_stage, yb, cudaMemcpyDeviceToHost, s);
+        if (e != cudaSuccess) return fail_cuda("cudaMemcpyAsync (y download)", e);
+        e = cudaStreamSynchronize(s);
+        if (e != cudaSuccess) return fail_cuda("cudaStreamSynchronize", e);
+        if (bias_host) {
+            // Bias on the host after the download, as src/cuda_quant.cu:326-329 does.
+            for (int r = 0; r < rows; ++r) {
+                float* yr = y_host + (size_t)r * out_features;
+                for (int c = 0; c < out_features; ++c) yr[c] += bias_host[c];
+            }
+        }
+        return MLQ_OK;
+    } catch (...) {
+        return fail(MLQ_ERR_CUDA, "mlq_linear_host: host exception");
+    }
+}
+
+MLQ_API mlq_status mlq_linear_host_weight(mlq_format fmt, const void* w_host, size_t block_count,
+                                          int out_features, int in_features,
+                                          const float* x_host, int rows, const float* bias_host,
+                                          float* y_host, int device) {
+    try {
+        mlq_status st = validate_linear(fmt, w_host, block_count, out_features, in_features, x_host,
+                                        rows, y_host, "mlq_linear_host_weight");
+        if (st != MLQ_OK) return st;
+        st = set_device(device);
+        if (st != MLQ_OK) return st;
+        const size_t wb = block_count * mlq_block_bytes(fmt);
+        void* wd = nullptr;
+        cudaError_t e = cudaMalloc(&wd, wb);
+        if (e != cudaSuccess) return fail_cuda("cudaMalloc (weights)", e);
+        e = cudaMemcpy(wd, w_host, wb, cudaMemcpyHostToDevice);
+        if (e == cudaSuccess) {
+            st = mlq_linear_host(fmt, wd, block_count, out_features, in_features, x_host, rows,
+                                 bias_host, y_host, device, nullptr);
+        } else {
+            st = fail_cuda("cudaMemcpy (weights)", e);
+        }
+        cudaFree(wd);
+        return st;
+    } catch (...) {
+        return fail(MLQ_ERR_CUDA, "mlq_linear_host_weight: host exception");
+    }
+}
+
+MLQ_API mlq_status mlq_dequantize(mlq_format fmt, const void* w, size_t block_count,
+                                  int out_features, int in_features, float* dst,
+                                  mlq_stream stream) {
+    try {
+        mlq_status st = validate_linear(fmt, w, block_count, out_features, in_features, dst, 1, dst,
+                                        "mlq_dequantize");
+        if (st != MLQ_OK) return st;
+        cudaError_t e = mlq::launch_dequantize(fmt, static_cast<const uint8_t*>(w), out_features,
+                                               in_features, dst, reinterpret_cast<cudaStream_t>(stream));
+        return e == cudaSuccess ? MLQ_OK : fail_cuda("dequantize launch", e);
+    } catch (...) {
+        return fail(MLQ_ERR_CUDA, "mlq_dequantize: host exception");
+    }
+}
+
+MLQ_API mlq_status mlq_quantize(mlq_format fmt, const float* src, int rows, int cols, void* blocks,
+                                mlq_stream stream) {
+    try {
+        if (!known_format(fmt)) return fail(MLQ_ERR_FORMAT, "mlq_quantize: unknown block format");
+        if (rows <= 0 || cols <= 0) return fail(MLQ_ERR_EMPTY, "mlq_quantize: empty tensors are not supported");
+        if (!src || !blocks) return fail(MLQ_ERR_NULL, "mlq_quantize: null pointer");
+        cudaError_t e = mlq::launch_quantize(fmt, src, rows, cols, static_cast<uint8_t*>(blocks),
+                                             reinterpret_cast<cudaStream_t>(stream));
+        return e == cudaSuccess ? MLQ_OK : fail_cuda("quantize launch", e);
+    } catch (...) {
+        return fail(MLQ_ERR_CUDA, "mlq_quantize: host exception");
+    }
+}
+
+}  // extern "C"

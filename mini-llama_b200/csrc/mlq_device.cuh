@@ -1,0 +1,170 @@
+// mlq_device.cuh -- device primitives shared by the mlq kernels (sm_100a).
+//
+// Block formats (the reference's include/mini_llama/quantized_tensor.h:36-72):
+//   q8_0 { u16 d; i8 qs[32]; }          34 B   w = d*q
+//   q4_0 { u16 d; u8 qs[16]; }          18 B   w = d*(q-8)
+//   q4_1 { u16 d; u16 m; u8 qs[16]; }   20 B   w = d*q + m
+// q4 nibble order: element j is the low nibble of qs[j], element 16+j the
+// high nibble (src/quant.cc:329-340).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace mlq {
+
+enum Format : int { kQ4_0 = 2, kQ4_1 = 3, kQ8_0 = 8 };
+
+constexpr int kQK = 32;  // values per block
+
+// Static facts per format for the streaming GEMV.  A "group" is the unit one
+// lane decodes from shared memory: 2 blocks for q8_0/q4_0, 1 for q4_1, chosen
+// so the group is a whole, ODD number of 32-bit words (17, 9, 5).  Lanes then
+// read consecutive groups with 32-bit loads that hit 32 distinct banks.
+template <int F>
+struct Fmt;
+template <>
+struct Fmt<kQ8_0> {
+    static constexpr int kBlockBytes = 34;
+    static constexpr int kGroupBlocks = 2;
+};
+template <>
+struct Fmt<kQ4_0> {
+    static constexpr int kBlockBytes = 18;
+    static constexpr int kGroupBlocks = 2;
+};
+template <>
+struct Fmt<kQ4_1> {
+    static constexpr int kBlockBytes = 20;
+    static constexpr int kGroupBlocks = 1;
+};
+
+__host__ __device__ constexpr int block_bytes(int f) {
+    return f == kQ8_0 ? 34 : (f == kQ4_0 ? 18 : (f == kQ4_1 ? 20 : 0));
+}
+
+// Exact fp16 -> fp32 of a raw bit pattern (hardware conversion; exact for
+// every finite value and for infinities).
+__device__ __forceinline__ float half_bits_to_float(uint32_t bits16) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(bits16)));
+}
+
+// ---------------------------------------------------------------------------
+// Error reporting from kernels.  A kernel that gives up (a bounded wait ran
+// out) records a code here and returns; the host reads it back with
+// mlq_device_error().  Codes: 1 = pipeline "full" wait, 2 = "empty" wait,
+// 3 = drain wait, 4 = peer flag wait.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void report_error(int* err, int code) {
+    if (err) atomicCAS(err, 0, code);
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Wall-clock bound for every spin in this library.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+
+// ---------------------------------------------------------------------------
+// mbarrier (shared::cta) helpers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.release.cta.shared::cta.b64 st, [%0];\n\t}"
+                 ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(1000000u)  // suspend-time hint: 1 ms
+        : "memory");
+    return ok != 0;
+}
+
+// Waits for the phase with the given parity to complete.  Returns false
+// when kWaitLimitNs elapses first (the caller then reports and bails out).
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    while (!mbar_try_wait(bar, parity)) {
+        if (global_ns() - t0 > kWaitLimitNs) return false;
+    }
+    return true;
+}
+
+// 1-D bulk copy global -> shared (TMA, no tensor map), completion counted in
+// bytes on an mbarrier.  dst/src 16-B aligned, bytes a multiple of 16.
+// No multicast: every copy reads this GPU's own memory into this CTA only.
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes,
+                                         uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            dst),
+        "l"(src), "r"(bytes), "r"(bar)
+        : "memory");
+}
+
+// Read-only, L1-bypassing 128-bit global load (x tiles: each CTA touches
+// them once per stage, the L2 keeps them for the other CTAs).
+__device__ __forceinline__ float4 ldg_nc_f4(const float* p) {
+    float4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ uint32_t lds_u32(uint32_t addr) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+    return v;
+}
+
+__device__ __forceinline__ float4 lds_f4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(addr));
+    return v;
+}
+
+__device__ __forceinline__ void sts_f4(uint32_t addr, float4 v) {
+    asm volatile("st.shared.v4.f32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z),
+                 "f"(v.w)
+                 : "memory");
+}
+
+__device__ __forceinline__ void sts_f32(uint32_t addr, float v) {
+    asm volatile("st.shared.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+
+__device__ __forceinline__ void sts_u8(uint32_t addr, uint32_t v) {
+    asm volatile("st.shared.u8 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+
+}  // namespace mlq

@@ -1,0 +1,500 @@
+// mlq_gemv.cu -- dequant-fused GEMV for decode (rows of x <= 8 per launch).
+//
+// Replaces q80LinearKernel / q40LinearKernel / q41LinearKernel
+// (src/cuda_quant.cu:78-182 of the reference).  Same arithmetic contract:
+// fp32 activations, exact decode of the packed weights, fp32 accumulation;
+// only the summation order differs.
+//
+// Design (HBM-bound streaming, one persistent CTA per SM):
+//  * The CTA owns a contiguous, balanced range of output rows
+//    [blockIdx*out/grid, (blockIdx+1)*out/grid) and walks it in row tiles of
+//    RT = 8 warps x RPW rows, each tile over the full K extent in K-tiles of
+//    32 lane-groups (2048 values for q8_0/q4_0, 1024 for q4_1).
+//  * Warp 0 is the producer.  Lane i streams tile row i's K-tile segment
+//    (a contiguous byte run of the AoS block array) into a shared-memory
+//    stage with one cp.async.bulk; the 32 lanes then load the
+//    matching x K-tile with coalesced 128-bit loads, compute per-block sums
+//    of x, and store x into the stage in the lane-major, XOR-swizzled order
+//    the consumers read.  An mbarrier per stage counts the bulk bytes and
+//    the 32 producer arrivals; a second one returns the stage.
+//  * Warps 1..8 consume: lane l decodes lane-group l (2 blocks = 9 or 17
+//    words, or 1 q4_1 block = 5 words; odd word counts make the 32 lanes'
+//    32-bit shared loads bank-conflict free) of RPW rows, reusing every x
+//    value it loads for all RPW rows and all tokens.
+//  * Decode without int->float conversions: a nibble (or a sign-flipped
+//    byte) is dropped into the mantissa of a float constant with one PRMT:
+//      q4:  float(0x43000000 | q<<16) = 128 + q      (exact)
+//      q8:  float(0x4B000000 | (q^0x80)) = 2^23+128+q (exact), minus 2^23+128
+//    so a q4 block costs one PRMT + one FFMA per value; the per-block
+//    constant is folded back with the block's x-sum S:
+//      q4_0:  d * (sum (128+q) x - 136 S)
+//      q4_1:  d * (sum (128+q) x - 128 S) + m S
+//      q8_0:  d * sum q x
+//  * Every mbarrier wait is bounded (2 s); on expiry the kernel records an
+//    error code in *err and returns after its in-flight copies land.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "mlq_device.cuh"
+#include "mlq_kernels.h"
+
+namespace mlq {
+namespace {
+
+constexpr int kConsumerWarps = 8;
+constexpr int kThreads = 32 * (1 + kConsumerWarps);
+constexpr int kMaxStages = 8;
+
+template <int F, int MT, int RPW>
+struct GemvCfg {
+    static constexpr int G = Fmt<F>::kGroupBlocks;
+    static constexpr int BS = Fmt<F>::kBlockBytes;
+    static constexpr int GB = G * BS;            // bytes per lane-group
+    static constexpr int WPG = GB / 4;           // 32-bit words per lane-group (odd)
+    static constexpr int KTE = 32 * G * kQK;     // x values per K-tile
+    static constexpr int RT = kConsumerWarps * RPW;
+    static constexpr int SLOT = 32 * GB + 16;    // one tile row segment + align slack
+    static constexpr int W_BYTES = RT * SLOT;
+    static constexpr int X_BYTES = MT * KTE * 4;
+    static constexpr int S_BYTES = MT * 32 * G * 4;
+    static constexpr int STAGE = W_BYTES + X_BYTES + S_BYTES;
+    static_assert(WPG % 2 == 1, "lane-group word count must be odd");
+    static_assert(SLOT % 16 == 0 && STAGE % 16 == 0, "stage alignment");
+};
+
+// x-tile row ("part") p of block bg holds 4 consecutive x values; the 8
+// parts of a block in the order the consumers walk the packed codes:
+//   q4:  p = 2j + h  ->  values 16h + 4j .. +3   (qs word j, nibble half h)
+//   q8:  p = j       ->  values 4j .. +3         (qs word j)
+template <int F>
+__device__ __forceinline__ int part_of(int e) {
+    if constexpr (F == kQ8_0) {
+        return e >> 2;
+    } else {
+        return (((e & 15) >> 2) << 1) | (e >> 4);
+    }
+}
+
+// Four packed codes -> four floats.  q4: `nib` holds one nibble per byte.
+__device__ __forceinline__ void q4_to_f(uint32_t nib, float f[4]) {
+    f[0] = __uint_as_float(__byte_perm(nib, 0x43000000u, 0x7044));
+    f[1] = __uint_as_float(__byte_perm(nib, 0x43000000u, 0x7144));
+    f[2] = __uint_as_float(__byte_perm(nib, 0x43000000u, 0x7244));
+    f[3] = __uint_as_float(__byte_perm(nib, 0x43000000u, 0x7344));
+}
+
+__device__ __forceinline__ void q8_to_f(uint32_t word, float f[4]) {
+    const uint32_t u = word ^ 0x80808080u;
+    const float c = 8388736.0f;  // 2^23 + 128
+    f[0] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7540)) - c;
+    f[1] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7541)) - c;
+    f[2] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7542)) - c;
+    f[3] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7543)) - c;
+}
+
+// qs word j (0-based) of block bg inside the lane-group words wv[].
+template <int F>
+__device__ __forceinline__ uint32_t qs_word(const uint32_t* wv, int bg, int j) {
+    if constexpr (F == kQ4_1) {
+        return wv[1 + j];
+    } else if constexpr (F == kQ4_0) {
+        // block 0: bytes 2..17 (misaligned by 2), block 1: bytes 20..35 = words 5..8
+        return bg == 0 ? __byte_perm(wv[j], wv[j + 1], 0x5432) : wv[5 + j];
+    } else {
+        // block 0: bytes 2..33, block 1: bytes 36..67 = words 9..16
+        return bg == 0 ? __byte_perm(wv[j], wv[j + 1], 0x5432) : wv[9 + j];
+    }
+}
+
+template <int F>
+__device__ __forceinline__ uint32_t d_bits(const uint32_t* wv, int bg) {
+    if constexpr (F == kQ4_1) return wv[0] & 0xFFFFu;
+    if constexpr (F == kQ4_0) return bg == 0 ? (wv[0] & 0xFFFFu) : (wv[4] >> 16);
+    return bg == 0 ? (wv[0] & 0xFFFFu) : (wv[8] >> 16);
+}
+
+template <int F, int MT, int RPW>
+__global__ void __launch_bounds__(kThreads, 1) gemv_stream_kernel(GemvArgs a) {
+    using C = GemvCfg<F, MT, RPW>;
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ __align__(8) uint64_t full_bar[kMaxStages];
+    __shared__ __align__(8) uint64_t empty_bar[kMaxStages];
+    __shared__ int abort_flag;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int S = a.nstages;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(smem_u32(&full_bar[s]), 32);
+            mbar_init(smem_u32(&empty_bar[s]), kConsumerWarps);
+        }
+        abort_flag = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    const long long r_begin = (long long)blockIdx.x * a.out / gridDim.x;
+    const long long r_end = (long long)(blockIdx.x + 1) * a.out / gridDim.x;
+    const int nrows_cta = (int)(r_end - r_begin);
+    const int ntiles = (nrows_cta + C::RT - 1) / C::RT;
+    const uint32_t smem_base = smem_u32(smem);
+    const uintptr_t wbase = reinterpret_cast<uintptr_t>(a.w);
+    const uintptr_t wend16 = (wbase + (uintptr_t)a.total_bytes) & ~(uintptr_t)15;
+
+    if (warp == 0) {
+        // ------------------------------ producer ------------------------------
+        uint32_t seq = 0;
+        for (int t = 0; t < ntiles; ++t) {
+            const long long row0 = r_begin + (long long)t * C::RT;
+            const int nrows = (int)min((long long)C::RT, r_end - row0);
+            for (int kt = 0; kt < a.ktiles; ++kt, ++seq) {
+                const int s = (int)(seq % (uint32_t)S);
+                const uint32_t round = seq / (uint32_t)S;
+                const uint32_t fb = smem_u32(&full_bar[s]);
+                if (!mbar_wait(smem_u32(&empty_bar[s]), (round & 1u) ^ 1u)) {
+                    report_error(a.err, 2);
+                    abort_flag = 1;
+                }
+                if (*(volatile int*)&abort_flag) goto producer_drain;
+                const uint32_t stage = smem_base + (uint32_t)s * C::STAGE;
+                const int groups = min(32, a.gpr - kt * 32);
+                const uint32_t seg = (uint32_t)(groups * C::GB);
+                // lane i streams tile row i's segment (RT <= 32 rows per tile)
+                uintptr_t src = 0, lo = 0, hi = 0;
+                uint32_t bytes = 0;
+                if (lane < nrows) {
+                    src = wbase + (uintptr_t)((row0 + lane) * a.row_bytes) + (uintptr_t)kt * 32u * C::GB;
+                    lo = src & ~(uintptr_t)15;
+                    hi = (src + seg + 15) & ~(uintptr_t)15;
+                    if (hi > wend16) hi = wend16;  // never read past the array
+                    bytes = hi > lo ? (uint32_t)(hi - lo) : 0u;
+                }
+                uint32_t tx = bytes;
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1) tx += __shfl_xor_sync(0xffffffffu, tx, off);
+                if (lane == 0) mbar_expect_tx(fb, tx);
+                __syncwarp();
+                if (bytes) bulk_g2s(stage + (uint32_t)lane * C::SLOT, reinterpret_cast<const void*>(lo), bytes, fb);
+                if (lane < nrows) {
+                    // bytes past the array's last 16-B boundary: plain copy
+                    for (uintptr_t q = (bytes ? hi : lo); q < src + seg; ++q)
+                        sts_u8(stage + (uint32_t)lane * C::SLOT + (uint32_t)(q - lo),
+                               *reinterpret_cast<const uint8_t*>(q));
+                }
+                // x K-tile: coalesced loads (all in flight together), block sums,
+                // swizzled lane-major stores
+                const uint32_t xs = stage + C::W_BYTES;
+                const uint32_t ss = xs + C::X_BYTES;
+                const long long k0 = (long long)kt * C::KTE;
+                constexpr int NV = C::KTE / 128;  // float4 loads per lane per token
+#pragma unroll 1
+                for (int m = 0; m < MT; ++m) {
+                    const float* xr = a.x + (long long)m * a.in;
+                    float4 v[NV];
+#pragma unroll
+                    for (int i = 0; i < NV; ++i) {
+                        const int e4 = (i * 32 + lane) * 4;
+                        v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+                        if (m < a.M && k0 + e4 < a.in) v[i] = ldg_nc_f4(xr + k0 + e4);
+                    }
+#pragma unroll
+                    for (int i = 0; i < NV; ++i) {
+                        const int e4 = (i * 32 + lane) * 4;  // value offset inside the K-tile
+                        float sum = (v[i].x + v[i].y) + (v[i].z + v[i].w);
+                        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+                        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+                        sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+                        const int blk = e4 >> 5;    // block inside the K-tile
+                        const int g = blk / C::G;   // lane-group
+                        const int bg = blk % C::G;  // block inside the group
+                        const int p = part_of<F>(e4 & 31);
+                        const int row = bg * 8 + p;
+                        const int col = g ^ p;
+                        sts_f4(xs + (uint32_t)(((m * C::G * 8 + row) * 32 + col) * 16), v[i]);
+                        if ((lane & 7) == 0) sts_f32(ss + (uint32_t)((m * 32 * C::G + blk) * 4), sum);
+                    }
+                }
+                mbar_arrive(fb);
+            }
+        }
+        return;
+    producer_drain:
+        // Abort: the stages already issued may still have copies in flight;
+        // wait (bounded) for each of them before the CTA's smem goes away.
+        for (uint32_t k = (seq >= (uint32_t)S ? seq - (uint32_t)S : 0); k < seq; ++k) {
+            const int s = (int)(k % (uint32_t)S);
+            if (!mbar_wait(smem_u32(&full_bar[s]), (k / (uint32_t)S) & 1u)) {
+                report_error(a.err, 3);
+                break;
+            }
+        }
+        return;
+    }
+
+    // -------------------------------- consumers --------------------------------
+    const int wc = warp - 1;
+    uint32_t seq = 0;
+    for (int t = 0; t < ntiles; ++t) {
+        const long long row0 = r_begin + (long long)t * C::RT;
+        const int nrows = (int)min((long long)C::RT, r_end - row0);
+        float tot[RPW][MT];
+#pragma unroll
+        for (int r = 0; r < RPW; ++r)
+#pragma unroll
+            for (int m = 0; m < MT; ++m) tot[r][m] = 0.f;
+
+        for (int kt = 0; kt < a.ktiles; ++kt, ++seq) {
+            const int s = (int)(seq % (uint32_t)S);
+            const uint32_t round = seq / (uint32_t)S;
+            if (!mbar_wait(smem_u32(&full_bar[s]), round & 1u)) {
+                report_error(a.err, 1);
+                abort_flag = 1;
+            }
+            if (*(volatile int*)&abort_flag) return;
+            const uint32_t stage = smem_base + (uint32_t)s * C::STAGE;
+            const uint32_t xs = stage + C::W_BYTES;
+            const uint32_t ss = xs + C::X_BYTES;
+            const int groups = min(32, a.gpr - kt * 32);
+
+            uint32_t wv[RPW][C::WPG];
+#pragma unroll
+            for (int r = 0; r < RPW; ++r) {
+                const int i = wc + r * kConsumerWarps;
+                if (i < nrows && lane < groups) {
+                    const uintptr_t src = wbase + (uintptr_t)((row0 + i) * a.row_bytes) +
+                                          (uintptr_t)kt * 32u * C::GB;
+                    const uint32_t base = stage + (uint32_t)i * C::SLOT + (uint32_t)(src & 15) +
+                                          (uint32_t)lane * C::GB;
+#pragma unroll
+                    for (int j = 0; j < C::WPG; ++j) wv[r][j] = lds_u32(base + 4 * j);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < C::WPG; ++j) wv[r][j] = 0u;
+                }
+            }
+
+#pragma unroll
+            for (int bg = 0; bg < C::G; ++bg) {
+                float2 acc[RPW][MT];  // two partial sums per (row, token): packed FFMA2
+#pragma unroll
+                for (int r = 0; r < RPW; ++r)
+#pragma unroll
+                    for (int m = 0; m < MT; ++m) acc[r][m] = make_float2(0.f, 0.f);
+
+#pragma unroll
+                for (int p = 0; p < 8; ++p) {
+                    float4 xv[MT];
+                    const int row = bg * 8 + p;
+#pragma unroll
+                    for (int m = 0; m < MT; ++m)
+                        xv[m] = lds_f4(xs + (uint32_t)(((m * C::G * 8 + row) * 32 + (lane ^ p)) * 16));
+#pragma unroll
+                    for (int r = 0; r < RPW; ++r) {
+                        float f[4];
+                        if constexpr (F == kQ8_0) {
+                            q8_to_f(qs_word<F>(wv[r], bg, p), f);
+                        } else {
+                            const uint32_t qw = qs_word<F>(wv[r], bg, p >> 1);
+                            const uint32_t nib = (p & 1) ? ((qw >> 4) & 0x0F0F0F0Fu) : (qw & 0x0F0F0F0Fu);
+                            q4_to_f(nib, f);
+                        }
+#pragma unroll
+                        for (int m = 0; m < MT; ++m) {
+                            acc[r][m] = __ffma2_rn(make_float2(f[0], f[1]), make_float2(xv[m].x, xv[m].y), acc[r][m]);
+                            acc[r][m] = __ffma2_rn(make_float2(f[2], f[3]), make_float2(xv[m].z, xv[m].w), acc[r][m]);
+                        }
+                    }
+                }
+                // fold the block back: scale, offset constant, q4_1 minimum
+                float sx[MT];
+#pragma unroll
+                for (int m = 0; m < MT; ++m) {
+                    uint32_t addr = ss + (uint32_t)((m * 32 * C::G + lane * C::G + bg) * 4);
+                    sx[m] = __uint_as_float(lds_u32(addr));
+                }
+#pragma unroll
+                for (int r = 0; r < RPW; ++r) {
+                    const float d = half_bits_to_float(d_bits<F>(wv[r], bg));
+#pragma unroll
+                    for (int m = 0; m < MT; ++m) {
+                        const float blk = acc[r][m].x + acc[r][m].y;
+                        if constexpr (F == kQ8_0) {
+                            tot[r][m] = fmaf(d, blk, tot[r][m]);
+                        } else if constexpr (F == kQ4_0) {
+                            tot[r][m] = fmaf(d, fmaf(-136.0f, sx[m], blk), tot[r][m]);
+                        } else {
+                            const float mn = half_bits_to_float(wv[r][0] >> 16);
+                            tot[r][m] = fmaf(d, fmaf(-128.0f, sx[m], blk), tot[r][m]);
+                            tot[r][m] = fmaf(mn, sx[m], tot[r][m]);
+                        }
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&empty_bar[s]));
+        }
+
+        // reduce the 32 lane partials of every (row, token) and store
+#pragma unroll
+        for (int r = 0; r < RPW; ++r) {
+            const int i = wc + r * kConsumerWarps;
+#pragma unroll
+            for (int m = 0; m < MT; ++m) {
+                float v = tot[r][m];
+                v += __shfl_xor_sync(0xffffffffu, v, 16);
+                v += __shfl_xor_sync(0xffffffffu, v, 8);
+                v += __shfl_xor_sync(0xffffffffu, v, 4);
+                v += __shfl_xor_sync(0xffffffffu, v, 2);
+                v += __shfl_xor_sync(0xffffffffu, v, 1);
+                if (i < nrows && m < a.M && lane == ((r * MT + m) & 31))
+                    a.y[(long long)m * a.y_stride + row0 + i] = v;
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Fallback for layouts the streaming kernel does not take (odd block count
+// per row for q8_0/q4_0, weights or x not 16-B aligned, in % 4 != 0): one
+// warp per output row, byte loads, any alignment.  Same arithmetic as above
+// but each weight is decoded to its fp32 value w and accumulated as w * x.
+// ---------------------------------------------------------------------------
+template <int F>
+__global__ void __launch_bounds__(256) gemv_generic_kernel(const uint8_t* __restrict__ w,
+                                                           const float* __restrict__ x,
+                                                           float* __restrict__ y, int out, int in,
+                                                           int M, int bpr) {
+    constexpr int BS = Fmt<F>::kBlockBytes;
+    const int o = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (o >= out) return;
+    const uint8_t* wr = w + (long long)o * bpr * BS;
+    for (int m0 = 0; m0 < M; m0 += 8) {
+        float acc[8];
+#pragma unroll
+        for (int m = 0; m < 8; ++m) acc[m] = 0.f;
+        for (int b = lane; b < bpr; b += 32) {
+            const uint8_t* blk = wr + (long long)b * BS;
+            const float d = half_bits_to_float((uint32_t)blk[0] | ((uint32_t)blk[1] << 8));
+            float mn = 0.f;
+            if constexpr (F == kQ4_1) mn = half_bits_to_float((uint32_t)blk[2] | ((uint32_t)blk[3] << 8));
+            const int k0 = b * kQK;
+            const int n = min(kQK, in - k0);
+            for (int e = 0; e < n; ++e) {
+                float wv;
+                if constexpr (F == kQ8_0) {
+                    wv = d * (float)(int8_t)blk[2 + e];
+                } else if constexpr (F == kQ4_0) {
+                    const int q = e < 16 ? (blk[2 + e] & 15) : (blk[2 + e - 16] >> 4);
+                    wv = d * (float)(q - 8);
+                } else {
+                    const int q = e < 16 ? (blk[4 + e] & 15) : (blk[4 + e - 16] >> 4);
+                    wv = fmaf(d, (float)q, mn);
+                }
+#pragma unroll
+                for (int m = 0; m < 8; ++m)
+                    if (m0 + m < M) acc[m] = fmaf(wv, __ldg(x + (long long)(m0 + m) * in + k0 + e), acc[m]);
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+            float v = acc[m];
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+            if (lane == 0 && m0 + m < M) y[(long long)(m0 + m) * out + o] = v;
+        }
+    }
+}
+
+template <int F, int MT, int RPW>
+cudaError_t launch_stream_t(const GemvArgs& args, int grid, int smem_budget, cudaStream_t stream) {
+    using C = GemvCfg<F, MT, RPW>;
+    static int attr_bytes[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int smem = args.nstages * C::STAGE;
+    if (dev >= 64 || attr_bytes[dev] < smem) {
+        // opt in to the whole budget once per device (budget + static smem
+        // stays under the 227 KB per-block limit)
+        cudaError_t e = cudaFuncSetAttribute(gemv_stream_kernel<F, MT, RPW>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem_budget);
+        if (e != cudaSuccess) return e;
+        if (dev < 64) attr_bytes[dev] = smem_budget;
+    }
+    gemv_stream_kernel<F, MT, RPW><<<grid, kThreads, smem, stream>>>(args);
+    return cudaGetLastError();
+}
+
+template <int F, int MT, int RPW>
+int stage_bytes_t() {
+    return GemvCfg<F, MT, RPW>::STAGE;
+}
+
+// rows-per-warp choice per format: keeps the lane-group words of all RPW
+// rows in registers (q8_0: 17 words per row, so 2 rows; q4: 4 rows).
+template <int F>
+constexpr int rpw_for() {
+    return F == kQ8_0 ? 2 : 4;
+}
+
+template <int F, int MT>
+cudaError_t dispatch_mt(GemvArgs args, int grid, int smem_budget, cudaStream_t stream) {
+    constexpr int RPW = rpw_for<F>();
+    const int stage = stage_bytes_t<F, MT, RPW>();
+    int S = smem_budget / stage;
+    if (S > kMaxStages) S = kMaxStages;
+    if (S < 2) return cudaErrorInvalidConfiguration;
+    args.nstages = S;
+    return launch_stream_t<F, MT, RPW>(args, grid, smem_budget, stream);
+}
+
+}  // namespace
+
+int gemv_tokens_per_pass(int rows_left) {
+    return rows_left >= 5 ? 8 : (rows_left >= 3 ? 4 : (rows_left == 2 ? 2 : 1));
+}
+
+cudaError_t launch_gemv_stream(int fmt, GemvArgs args, int mt, int grid, int smem_budget,
+                               cudaStream_t stream) {
+    switch (fmt) {
+        case kQ8_0:
+            switch (mt) {
+                case 1: return dispatch_mt<kQ8_0, 1>(args, grid, smem_budget, stream);
+                case 2: return dispatch_mt<kQ8_0, 2>(args, grid, smem_budget, stream);
+                case 4: return dispatch_mt<kQ8_0, 4>(args, grid, smem_budget, stream);
+                default: return dispatch_mt<kQ8_0, 8>(args, grid, smem_budget, stream);
+            }
+        case kQ4_0:
+            switch (mt) {
+                case 1: return dispatch_mt<kQ4_0, 1>(args, grid, smem_budget, stream);
+                case 2: return dispatch_mt<kQ4_0, 2>(args, grid, smem_budget, stream);
+                case 4: return dispatch_mt<kQ4_0, 4>(args, grid, smem_budget, stream);
+                default: return dispatch_mt<kQ4_0, 8>(args, grid, smem_budget, stream);
+            }
+        case kQ4_1:
+            switch (mt) {
+                case 1: return dispatch_mt<kQ4_1, 1>(args, grid, smem_budget, stream);
+                case 2: return dispatch_mt<kQ4_1, 2>(args, grid, smem_budget, stream);
+                case 4: return dispatch_mt<kQ4_1, 4>(args, grid, smem_budget, stream);
+                default: return dispatch_mt<kQ4_1, 8>(args, grid, smem_budget, stream);
+            }
+    }
+    return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_gemv_generic(int fmt, const uint8_t* w, const float* x, float* y, int out,
+                                int in, int M, int bpr, cudaStream_t stream) {
+    const dim3 block(256);
+    const dim3 grid((out + 7) / 8);
+    switch (fmt) {
+        case kQ8_0: gemv_generic_kernel<kQ8_0><<<grid, block, 0, stream>>>(w, x, y, out, in, M, bpr); break;
+        case kQ4_0: gemv_generic_kernel<kQ4_0><<<grid, block, 0, stream>>>(w, x, y, out, in, M, bpr); break;
+        case kQ4_1: gemv_generic_kernel<kQ4_1><<<grid, block, 0, stream>>>(w, x, y, out, in, M, bpr); break;
+        default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+}  // namespace mlq

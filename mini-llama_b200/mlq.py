@@ -1,0 +1,190 @@
+"""ctypes bindings of libmlq.so (include/mlq.h) for Python callers.
+
+Device buffers are torch CUDA tensors (torch is only the allocator and the
+stream provider here); their data pointers and the current stream handle are
+passed straight through the C ABI.  Every failure raises ``MLQError`` with
+the library's message.  There is no CPU fallback: if ``lib/libmlq.so`` is
+missing, ``lib()`` raises.
+"""
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+import numpy as np
+
+PKG = Path(__file__).resolve().parent
+LIB_PATH = PKG / "lib" / "libmlq.so"
+
+FORMATS = {"q8_0": 8, "q4_0": 2, "q4_1": 3}
+BLOCK_BYTES = {"q8_0": 34, "q4_0": 18, "q4_1": 20}
+QK = 32
+
+STATUS = {0: "MLQ_OK", 1: "MLQ_ERR_FORMAT", 2: "MLQ_ERR_NULL", 3: "MLQ_ERR_EMPTY",
+          4: "MLQ_ERR_SHAPE", 5: "MLQ_ERR_BLOCK_COUNT", 6: "MLQ_ERR_DEVICE", 7: "MLQ_ERR_CUDA",
+          8: "MLQ_ERR_TIMEOUT", 9: "MLQ_ERR_RANGE", 10: "MLQ_ERR_COMM"}
+
+
+class MLQError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"{STATUS.get(status, status)}: {message}")
+        self.status = status
+        self.message = message
+
+
+_lib = None
+_vp = ctypes.c_void_p
+_i = ctypes.c_int
+_sz = ctypes.c_size_t
+
+
+def lib() -> ctypes.CDLL:
+    """Load libmlq.so once (raises FileNotFoundError when it was not built)."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise FileNotFoundError(f"{LIB_PATH} is missing: run `python mini-llama_b200/build.py`")
+        L = ctypes.CDLL(str(LIB_PATH))
+        L.mlq_built.restype = _i
+        L.mlq_block_bytes.argtypes = [_i]
+        L.mlq_block_bytes.restype = _sz
+        L.mlq_block_count.argtypes = [_i, _i]
+        L.mlq_block_count.restype = _sz
+        L.mlq_status_string.argtypes = [_i]
+        L.mlq_status_string.restype = ctypes.c_char_p
+        L.mlq_last_error.restype = ctypes.c_char_p
+        L.mlq_device_error.argtypes = [_i, ctypes.POINTER(_i)]
+        L.mlq_linear.argtypes = [_i, _vp, _sz, _i, _i, _vp, _i, _vp, _vp]
+        L.mlq_linear_host.argtypes = [_i, _vp, _sz, _i, _i, _vp, _i, _vp, _vp, _i, _vp]
+        L.mlq_linear_host_weight.argtypes = [_i, _vp, _sz, _i, _i, _vp, _i, _vp, _vp, _i]
+        L.mlq_dequantize.argtypes = [_i, _vp, _sz, _i, _i, _vp, _vp]
+        L.mlq_quantize.argtypes = [_i, _vp, _i, _i, _vp, _vp]
+        for name in ("mlq_linear", "mlq_linear_host", "mlq_linear_host_weight", "mlq_dequantize",
+                     "mlq_quantize", "mlq_device_error"):
+            getattr(L, name).restype = _i
+        _lib = L
+    return _lib
+
+
+def check(status: int) -> None:
+    if status != 0:
+        raise MLQError(status, lib().mlq_last_error().decode())
+
+
+def fmt_id(fmt) -> int:
+    if isinstance(fmt, str):
+        if fmt not in FORMATS:
+            raise ValueError(f"unknown format {fmt!r}")
+        return FORMATS[fmt]
+    return int(fmt)
+
+
+def blocks_per_row(in_features: int) -> int:
+    return (in_features + QK - 1) // QK
+
+
+def block_count(out_features: int, in_features: int) -> int:
+    return int(lib().mlq_block_count(out_features, in_features))
+
+
+def weight_bytes(fmt: str, out_features: int, in_features: int) -> int:
+    return out_features * blocks_per_row(in_features) * BLOCK_BYTES[fmt]
+
+
+def _stream_handle(stream) -> int | None:
+    if stream is None:
+        import torch
+        return torch.cuda.current_stream().cuda_stream
+    if isinstance(stream, int):
+        return stream
+    return stream.cuda_stream
+
+
+def _np_ptr(a: np.ndarray | None):
+    return None if a is None else a.ctypes.data
+
+
+# ---------------------------------------------------------------------------
+# device entry points (torch CUDA tensors)
+# ---------------------------------------------------------------------------
+def linear(fmt, w, out_features: int, in_features: int, x, y=None, stream=None):
+    """y = x @ W^T on the device.  x: float32 [rows, in] (or [in]); w: uint8
+    blocks.  Returns y (float32 [rows, out], or [out] for 1-D x)."""
+    import torch
+    rows = 1 if x.dim() == 1 else x.shape[0]
+    if y is None:
+        shape = (out_features,) if x.dim() == 1 else (rows, out_features)
+        y = torch.empty(shape, dtype=torch.float32, device=x.device)
+    nb = w.numel() // BLOCK_BYTES[_fmt_name(fmt)]
+    check(lib().mlq_linear(fmt_id(fmt), w.data_ptr(), nb, out_features, in_features, x.data_ptr(),
+                           rows, y.data_ptr(), _stream_handle(stream)))
+    return y
+
+
+def linear_raw(fmt, w_ptr: int, nblocks: int, out_features: int, in_features: int, x_ptr: int,
+               rows: int, y_ptr: int, stream: int | None) -> None:
+    """Pointer-level call (for CUDA-graph capture and timing loops)."""
+    check(lib().mlq_linear(fmt_id(fmt), w_ptr, nblocks, out_features, in_features, x_ptr, rows,
+                           y_ptr, stream))
+
+
+def linear_host(fmt, w, out_features: int, in_features: int, x: np.ndarray, bias=None,
+                device: int = 0, y: np.ndarray | None = None, stream=None) -> np.ndarray:
+    """Device weights, host x / y (synchronous)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    rows = 1 if x.ndim == 1 else x.shape[0]
+    if y is None:
+        y = np.empty((out_features,) if x.ndim == 1 else (rows, out_features), dtype=np.float32)
+    b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+    wp = w if isinstance(w, int) else w.data_ptr()
+    nb = block_count(out_features, in_features)
+    check(lib().mlq_linear_host(fmt_id(fmt), wp, nb, out_features, in_features, x.ctypes.data, rows,
+                                _np_ptr(b), y.ctypes.data, device,
+                                None if stream is None else _stream_handle(stream)))
+    return y
+
+
+def linear_host_weight(fmt, blocks: np.ndarray, out_features: int, in_features: int,
+                       x: np.ndarray, bias=None, device: int = 0) -> np.ndarray:
+    """Host weights, host x / y (uploads the weights for this call)."""
+    blocks = np.ascontiguousarray(blocks, dtype=np.uint8)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    rows = 1 if x.ndim == 1 else x.shape[0]
+    y = np.empty((out_features,) if x.ndim == 1 else (rows, out_features), dtype=np.float32)
+    b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+    nb = blocks.size // BLOCK_BYTES[_fmt_name(fmt)]
+    check(lib().mlq_linear_host_weight(fmt_id(fmt), blocks.ctypes.data, nb, out_features,
+                                       in_features, x.ctypes.data, rows, _np_ptr(b), y.ctypes.data,
+                                       device))
+    return y
+
+
+def quantize(fmt, src, stream=None):
+    """float32 CUDA [rows, cols] -> uint8 CUDA blocks."""
+    import torch
+    rows, cols = src.shape
+    out = torch.empty(weight_bytes(_fmt_name(fmt), rows, cols), dtype=torch.uint8, device=src.device)
+    check(lib().mlq_quantize(fmt_id(fmt), src.data_ptr(), rows, cols, out.data_ptr(),
+                             _stream_handle(stream)))
+    return out
+
+
+def dequantize(fmt, w, out_features: int, in_features: int, stream=None):
+    import torch
+    dst = torch.empty((out_features, in_features), dtype=torch.float32, device=w.device)
+    nb = w.numel() // BLOCK_BYTES[_fmt_name(fmt)]
+    check(lib().mlq_dequantize(fmt_id(fmt), w.data_ptr(), nb, out_features, in_features,
+                               dst.data_ptr(), _stream_handle(stream)))
+    return dst
+
+
+def device_error(device: int = 0) -> int:
+    code = ctypes.c_int(0)
+    check(lib().mlq_device_error(device, ctypes.byref(code)))
+    return code.value
+
+
+def _fmt_name(fmt) -> str:
+    if isinstance(fmt, str):
+        return fmt
+    return {v: k for k, v in FORMATS.items()}[int(fmt)]

@@ -1,0 +1,200 @@
+"""Python access to the CPU checkers.  TEST INFRASTRUCTURE ONLY.
+
+Two libraries, both built by ``oracle/Makefile``:
+
+* ``Oracle`` wraps ``oracle/_lib/liboracle.so`` -- the C restatement of the
+  reference's quant path (``oracle/oracle.c``; each function there cites the
+  reference file:line it follows).
+* ``Reference`` wraps ``oracle/_ref/libref_{scalar,avx2}.so`` -- the
+  reference's OWN CPU sources (``src/quant.cc`` and friends) compiled here,
+  behind the small C layer ``oracle/ref/ref_capi.cc``.  Present only where it
+  was built (it is built in the development container and ships to the GPU
+  box with the repository snapshot).
+
+Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline
+legs may import this module.  The product never does.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB = HERE / "_lib" / "liboracle.so"
+REF_DIR = HERE / "_ref"
+
+FMT_IDS = {"q8_0": 8, "q4_0": 2, "q4_1": 3}
+BLOCK_BYTES = {"q8_0": 34, "q4_0": 18, "q4_1": 20}
+QK = 32
+
+_f32p = ctypes.POINTER(ctypes.c_float)
+_u8p = ctypes.POINTER(ctypes.c_uint8)
+
+
+def _fp(a: np.ndarray):
+    return a.ctypes.data_as(_f32p)
+
+
+def _bp(a: np.ndarray):
+    return a.ctypes.data_as(_u8p)
+
+
+def build(force: bool = False) -> None:
+    """Compile liboracle.so (plain gcc); cheap and always possible."""
+    if force or not LIB.exists() or LIB.stat().st_mtime < (HERE / "oracle.c").stat().st_mtime:
+        subprocess.run(["make", "-C", str(HERE), "oracle"], check=True,
+                       stdout=subprocess.DEVNULL)
+
+
+def blocks_per_row(cols: int) -> int:
+    return (cols + QK - 1) // QK
+
+
+def nbytes(fmt: str, rows: int, cols: int) -> int:
+    return rows * blocks_per_row(cols) * BLOCK_BYTES[fmt]
+
+
+class Oracle:
+    """The C restatement (``oracle/oracle.c``)."""
+
+    def __init__(self) -> None:
+        build()
+        lib = ctypes.CDLL(str(LIB))
+        lib.orc_fp16_from_f32.argtypes = [ctypes.c_float]
+        lib.orc_fp16_from_f32.restype = ctypes.c_uint16
+        lib.orc_f32_from_fp16.argtypes = [ctypes.c_uint16]
+        lib.orc_f32_from_fp16.restype = ctypes.c_float
+        lib.orc_quantize.argtypes = [ctypes.c_int, _f32p, ctypes.c_int64, ctypes.c_int64, _u8p]
+        lib.orc_dequantize.argtypes = [ctypes.c_int, _u8p, ctypes.c_int64, ctypes.c_int64, _f32p]
+        lib.orc_linear.argtypes = [ctypes.c_int, _f32p, ctypes.c_int64, ctypes.c_int64, _u8p,
+                                   ctypes.c_int64, _f32p, ctypes.c_int]
+        self.lib = lib
+
+    def fp16_from_f32(self, v: float) -> int:
+        return int(self.lib.orc_fp16_from_f32(float(v)))
+
+    def f32_from_fp16(self, h: int) -> float:
+        return float(self.lib.orc_f32_from_fp16(int(h)))
+
+    def quantize(self, fmt: str, w: np.ndarray) -> np.ndarray:
+        w = np.ascontiguousarray(w, dtype=np.float32)
+        rows, cols = w.shape
+        out = np.zeros(nbytes(fmt, rows, cols), dtype=np.uint8)
+        rc = self.lib.orc_quantize(FMT_IDS[fmt], _fp(w), rows, cols, _bp(out))
+        assert rc == 0
+        return out
+
+    def dequantize(self, fmt: str, blocks: np.ndarray, rows: int, cols: int) -> np.ndarray:
+        blocks = np.ascontiguousarray(blocks, dtype=np.uint8)
+        assert blocks.size == nbytes(fmt, rows, cols)
+        out = np.zeros((rows, cols), dtype=np.float32)
+        rc = self.lib.orc_dequantize(FMT_IDS[fmt], _bp(blocks), rows, cols, _fp(out))
+        assert rc == 0
+        return out
+
+    def linear(self, fmt: str, x: np.ndarray, blocks: np.ndarray, out_features: int,
+               threads: int | None = None) -> np.ndarray:
+        """y = x @ W^T with x [rows, in] (or [in]); result rank follows x."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        one_d = x.ndim == 1
+        x2 = x.reshape(1, -1) if one_d else x
+        rows, in_f = x2.shape
+        blocks = np.ascontiguousarray(blocks, dtype=np.uint8)
+        assert blocks.size == nbytes(fmt, out_features, in_f)
+        y = np.zeros((rows, out_features), dtype=np.float32)
+        n = threads if threads else (os.cpu_count() or 1)
+        rc = self.lib.orc_linear(FMT_IDS[fmt], _fp(x2), rows, in_f, _bp(blocks), out_features,
+                                 _fp(y), n)
+        assert rc == 0
+        return y.reshape(out_features) if one_d else y
+
+
+class Reference:
+    """The reference's own CPU path, compiled from its sources (oracle/_ref)."""
+
+    def __init__(self, variant: str = "scalar") -> None:
+        path = REF_DIR / f"libref_{variant}.so"
+        if not path.exists():
+            raise FileNotFoundError(f"{path} was not built (make -C oracle ref)")
+        lib = ctypes.CDLL(str(path))
+        lib.ref_quantize.argtypes = [ctypes.c_int, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]
+        lib.ref_quantize.restype = ctypes.c_longlong
+        lib.ref_dequantize.argtypes = [ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int,
+                                       ctypes.c_int, _f32p]
+        lib.ref_linear.argtypes = [ctypes.c_int, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
+                                   ctypes.c_size_t, ctypes.c_int, _f32p]
+        lib.ref_set_threads.argtypes = [ctypes.c_int]
+        lib.ref_get_threads.restype = ctypes.c_int
+        lib.ref_blocks_new.argtypes = [ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t]
+        lib.ref_blocks_new.restype = ctypes.c_void_p
+        lib.ref_blocks_free.argtypes = [ctypes.c_int, ctypes.c_void_p]
+        lib.ref_linear_held.argtypes = [ctypes.c_int, _f32p, ctypes.c_int, ctypes.c_int,
+                                        ctypes.c_void_p, ctypes.c_int, _f32p]
+        self.lib = lib
+        self.variant = variant
+        self.path = path
+
+    @staticmethod
+    def available(variant: str = "scalar") -> bool:
+        return (REF_DIR / f"libref_{variant}.so").exists()
+
+    def set_threads(self, n: int) -> None:
+        self.lib.ref_set_threads(int(n))
+
+    def threads(self) -> int:
+        return int(self.lib.ref_get_threads())
+
+    def quantize(self, fmt: str, w: np.ndarray) -> np.ndarray:
+        w = np.ascontiguousarray(w, dtype=np.float32)
+        rows, cols = w.shape
+        out = np.zeros(nbytes(fmt, rows, cols), dtype=np.uint8)
+        n = self.lib.ref_quantize(FMT_IDS[fmt], _fp(w), rows, cols, out.ctypes.data)
+        assert n == rows * blocks_per_row(cols), n
+        return out
+
+    def dequantize(self, fmt: str, blocks: np.ndarray, rows: int, cols: int) -> np.ndarray:
+        blocks = np.ascontiguousarray(blocks, dtype=np.uint8)
+        nb = blocks.size // BLOCK_BYTES[fmt]
+        out = np.zeros((rows, cols), dtype=np.float32)
+        rc = self.lib.ref_dequantize(FMT_IDS[fmt], blocks.ctypes.data, nb, rows, cols, _fp(out))
+        assert rc == 0
+        return out
+
+    def linear(self, fmt: str, x: np.ndarray, blocks: np.ndarray, out_features: int) -> np.ndarray:
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        one_d = x.ndim == 1
+        rows = 0 if one_d else x.shape[0]
+        in_f = x.shape[-1]
+        blocks = np.ascontiguousarray(blocks, dtype=np.uint8)
+        nb = blocks.size // BLOCK_BYTES[fmt]
+        y = np.zeros((max(rows, 1), out_features), dtype=np.float32)
+        rc = self.lib.ref_linear(FMT_IDS[fmt], _fp(x), rows, in_f, blocks.ctypes.data, nb,
+                                 out_features, _fp(y))
+        assert rc == 0, rc
+        return y.reshape(out_features) if one_d else y
+
+    def hold(self, fmt: str, blocks: np.ndarray):
+        """Copy blocks into a reference-owned std::vector once (for timing)."""
+        blocks = np.ascontiguousarray(blocks, dtype=np.uint8)
+        nb = blocks.size // BLOCK_BYTES[fmt]
+        h = self.lib.ref_blocks_new(FMT_IDS[fmt], blocks.ctypes.data, nb)
+        return h
+
+    def release(self, fmt: str, handle) -> None:
+        self.lib.ref_blocks_free(FMT_IDS[fmt], handle)
+
+    def linear_held(self, fmt: str, x: np.ndarray, handle, out_features: int,
+                    y: np.ndarray | None = None) -> np.ndarray:
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        rows = x.shape[0] if x.ndim == 2 else 0
+        in_f = x.shape[-1]
+        if y is None:
+            y = np.zeros((max(rows, 1), out_features), dtype=np.float32)
+        rc = self.lib.ref_linear_held(FMT_IDS[fmt], _fp(x), rows, in_f, handle, out_features,
+                                      _fp(y))
+        assert rc == 0, rc
+        return y

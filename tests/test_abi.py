@@ -1,0 +1,108 @@
+"""CPU tests of the C ABI: the library loads, exports every entry point
+include/mlq.h declares, and rejects bad arguments on the host before any
+CUDA call (so these run without a GPU)."""
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+HEADERS = sorted((ROOT / "include").glob("*.h"))
+
+
+def declared_symbols():
+    names = []
+    for h in HEADERS:
+        text = h.read_text()
+        names += re.findall(r"MLQ_API\s+[\w\s\*]+?\b(mlq_\w+)\s*\(", text)
+    return sorted(set(names))
+
+
+def test_headers_declare_entry_points():
+    names = declared_symbols()
+    assert "mlq_linear" in names and "mlq_quantize" in names and len(names) >= 10
+
+
+def test_library_exports_every_declared_symbol(pkg):
+    lib = pkg.mlq.lib()
+    missing = [n for n in declared_symbols() if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_library_facts(pkg):
+    lib = pkg.mlq.lib()
+    assert lib.mlq_built() == 1
+    assert [lib.mlq_block_bytes(f) for f in (8, 2, 3, 0)] == [34, 18, 20, 0]
+    assert lib.mlq_block_count(4864, 896) == 4864 * 28
+    assert lib.mlq_block_count(3, 100) == 12
+    assert lib.mlq_block_count(0, 5) == 0
+    assert lib.mlq_status_string(5) == b"block count mismatch"
+
+
+def _linear_status(pkg, fmt=8, w=0x1000, nb=4, out=4, inf=32, x=0x2000, rows=1, y=0x3000):
+    lib = pkg.mlq.lib()
+    return lib.mlq_linear(fmt, w, nb, out, inf, x, rows, y, None)
+
+
+def test_validation_before_any_cuda_call(pkg):
+    """The reference's checks (src/cuda_quant.cu:198-227, 305-307); the
+    pointers are never dereferenced because validation fails first."""
+    mlq = pkg.mlq
+    lib = mlq.lib()
+    assert _linear_status(pkg, fmt=7) == 1                    # unknown format
+    assert _linear_status(pkg, w=None) == 2                   # null weight pointer
+    assert b"null weight pointer" in lib.mlq_last_error()
+    assert _linear_status(pkg, out=0) == 3                    # empty
+    assert b"empty tensors are not supported" in lib.mlq_last_error()
+    assert _linear_status(pkg, inf=-1) == 3
+    assert _linear_status(pkg, rows=0) == 3
+    assert _linear_status(pkg, x=None) == 2
+    assert _linear_status(pkg, nb=3) == 5                     # short block vector
+    assert b"expected 4, got 3" in lib.mlq_last_error()
+    assert _linear_status(pkg, nb=4, inf=33) == 5             # 33 values -> 2 blocks per row
+    assert b"expected 8, got 4" in lib.mlq_last_error()
+    # (no call here ever passes validation: the pointers above are fake)
+
+
+def test_host_entry_points_validate_first(pkg):
+    mlq = pkg.mlq
+    x = np.zeros(32, np.float32)
+    with pytest.raises(mlq.MLQError) as e:
+        mlq.linear_host_weight("q8_0", np.zeros(3 * 34, np.uint8), 4, 32, x)  # 3 blocks for 4 rows
+    assert e.value.status == 5
+    with pytest.raises(mlq.MLQError) as e:
+        mlq.linear_host("q4_0", 0, 4, 32, x)  # null device weight
+    assert e.value.status == 2
+    lib = mlq.lib()
+    assert lib.mlq_quantize(8, None, 4, 32, None, None) == 2
+    assert lib.mlq_quantize(8, 0x1000, 0, 32, 0x2000, None) == 3
+    assert lib.mlq_dequantize(2, 0x1000, 5, 4, 32, 0x2000, None) == 5
+
+
+def test_cuda_quant_shape_errors_raise_runtime_error(pkg):
+    """Reference-named entry points raise RuntimeError like the reference
+    (tests/test_cuda.cc:776-809): bad in_features, short blocks, null
+    weight pointer, rank-3 x -- all caught before the GPU."""
+    import importlib
+    cq = importlib.import_module("mini_llama_b200.cuda_quant")
+    blocks = np.zeros(4 * 34, np.uint8)
+    with pytest.raises(RuntimeError):
+        cq.cudaQ80Linear(np.zeros(16, np.float32), blocks, [4, 32])
+    with pytest.raises(RuntimeError):
+        cq.cudaQ80Linear(np.zeros(32, np.float32), blocks[:-34], [4, 32])
+    with pytest.raises(RuntimeError):
+        cq.cudaQ80LinearDeviceWeight(np.zeros(32, np.float32), None, 4, [4, 32])
+    with pytest.raises(RuntimeError):
+        cq.cudaQ80Linear(np.zeros((1, 1, 32), np.float32), blocks, [4, 32])
+
+
+def test_missing_library_fails_loudly(pkg, tmp_path, monkeypatch):
+    mlq = pkg.mlq
+    monkeypatch.setattr(mlq, "_lib", None)
+    monkeypatch.setattr(mlq, "LIB_PATH", tmp_path / "libmlq.so")
+    with pytest.raises(FileNotFoundError):
+        mlq.lib()
