@@ -228,6 +228,7 @@ def make_inputs(torch, pkg, device):
         w32 = torch.randn((out_f, in_f), generator=g, device=device, dtype=torch.float32) * 0.02
         ws.append(pkg.mlq.quantize(fmt, w32))
         del w32
+        torch.cuda.empty_cache()  # keep only the packed weights resident
         x = pkg.synth.normal((WORKLOAD["rows"], in_f), seed=2000 + i)
         xs_host.append(x)
         xs_dev.append(torch.from_numpy(x).to(device))
@@ -306,8 +307,9 @@ def run_mlq(args):
     per = {name: statistics.mean(evs[k][j][0].elapsed_time(evs[k][j][1]) for k in range(k2))
            for j, (name, _, _) in enumerate(mats)}
     peak, peak_kind = hbm_peak()
-    dom = "lm_head"
-    dom_bytes = weight_bytes(fmt, 152064, 3584)
+    dom = max(mats, key=lambda m: weight_bytes(fmt, m[1], m[2]))
+    dom_bytes = weight_bytes(fmt, dom[1], dom[2])
+    dom = dom[0]
     achieved = dom_bytes / (per[dom] / 1e3) / 1e9
     kernel_sum_ms = sum(per.values())
     traffic = read_traffic()
@@ -363,7 +365,7 @@ def run_mlq(args):
                        "matrices": {n: [o, i] for n, o, i in mats},
                        "weight_bytes_per_step": bytes_step,
                        "l2": "inputs larger than L2 (437.6 MB per step vs 126 MB L2); no flush"},
-            "roofline": {"bound": "hbm", "kernel": "gemv_stream_kernel<q4_0,1,4> (lm_head launch)",
+            "roofline": {"bound": "hbm", "kernel": f"gemv_stream_kernel<q4_0,1,4> ({dom} launch)",
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                          "traffic": traffic, "algorithmic_bytes_per_launch": dom_bytes,
@@ -444,7 +446,14 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--only", default=None,
+                    help="run one matrix of the workload (qkv/o/gate/up/down/lm_head), for profiling")
     args = ap.parse_args()
+    if args.only:
+        WORKLOAD["matrices"] = [m for m in WORKLOAD["matrices"] if m[0] == args.only]
+        if not WORKLOAD["matrices"]:
+            ap.error(f"--only: no matrix named {args.only!r}")
+        args.no_cpu_baseline = True
     if args.impl == "reference":
         run_reference(args)
     else:

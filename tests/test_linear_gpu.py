@@ -114,12 +114,13 @@ def test_unaligned_weight_pointer(oracle, pkg, fmt):
     blocks = make_weights(oracle, pkg, fmt, out_f, in_f, seed=5)
     x = pkg.synth.normal((3, in_f), seed=6)
     ref = oracle.linear(fmt, x, blocks, out_f)
+    x_d = dev(x)  # keep every device buffer referenced until the kernel has run
     for off in (2, 16):
         buf = torch.zeros(blocks.size + 64, dtype=torch.uint8, device="cuda")
         buf[off:off + blocks.size] = dev(blocks)
         y = torch.empty((3, out_f), dtype=torch.float32, device="cuda")
         pkg.mlq.linear_raw(fmt, buf.data_ptr() + off, blocks.size // pkg.mlq.BLOCK_BYTES[fmt], out_f,
-                           in_f, dev(x).data_ptr(), 3, y.data_ptr(),
+                           in_f, x_d.data_ptr(), 3, y.data_ptr(),
                            torch.cuda.current_stream().cuda_stream)
         torch.cuda.synchronize()
         assert rel_l2_rows(y.cpu().numpy(), ref).max() <= TOL, off
@@ -133,8 +134,9 @@ def test_output_guard_and_overwrite(oracle, pkg, fmt):
     x = pkg.synth.normal((rows, in_f), seed=9)
     guard = 256
     buf = torch.full((rows * out_f + 2 * guard,), 12345.0, dtype=torch.float32, device="cuda")
-    pkg.mlq.linear_raw(fmt, dev(blocks).data_ptr(), blocks.size // pkg.mlq.BLOCK_BYTES[fmt], out_f,
-                       in_f, dev(x).data_ptr(), rows, buf.data_ptr() + guard * 4,
+    w_d, x_d = dev(blocks), dev(x)  # held until the kernel has run (caching allocator reuse)
+    pkg.mlq.linear_raw(fmt, w_d.data_ptr(), blocks.size // pkg.mlq.BLOCK_BYTES[fmt], out_f,
+                       in_f, x_d.data_ptr(), rows, buf.data_ptr() + guard * 4,
                        torch.cuda.current_stream().cuda_stream)
     torch.cuda.synchronize()
     h = buf.cpu().numpy()
