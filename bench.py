@@ -218,25 +218,42 @@ def reference_cpu_baseline(pkg, seconds):
 
 
 # ---------------------------------------------------------------------------
-def make_inputs(torch, pkg, device):
-    """Quantized weights on the device (+ host copies) and x vectors."""
+# Placement of the workload's matrices on N GPUs (north_star: large
+# matrices row-sharded, small ones on one GPU).  "local0": rank 0 only, no
+# gather (QKV feeds attention on rank 0); "bcast0": rank 0 computes, the
+# fused gather stores the result into every rank's y (O feeds the FFN on all
+# ranks); "shard": rows split across all ranks, fused all-gather.
+PLACEMENT = {"qkv": "local0", "o": "bcast0", "gate": "shard", "up": "shard", "down": "shard",
+             "lm_head": "shard"}
+
+
+def make_inputs(torch, pkg, device, world=1, rank=0):
+    """Quantized weights on the device (this rank's rows) and x vectors."""
+    import importlib
+    sh = importlib.import_module("mini_llama_b200.sharding")
     fmt = WORKLOAD["fmt"]
     g = torch.Generator(device=device)
-    ws, xs_dev, xs_host = [], [], []
+    ws, xs_dev, xs_host, ranges = [], [], [], []
     for i, (name, out_f, in_f) in enumerate(WORKLOAD["matrices"]):
+        place = PLACEMENT.get(name, "shard") if world > 1 else "shard"
+        rg = sh.shard_rows(out_f, world, owners=[0] if place in ("local0", "bcast0") else None)
+        b, e = rg[rank]
+        ranges.append(rg)
         g.manual_seed(1000 + i)
         w32 = torch.randn((out_f, in_f), generator=g, device=device, dtype=torch.float32) * 0.02
-        ws.append(pkg.mlq.quantize(fmt, w32))
+        ws.append(pkg.mlq.quantize(fmt, w32[b:e].contiguous()) if e > b else None)
         del w32
         torch.cuda.empty_cache()  # keep only the packed weights resident
         x = pkg.synth.normal((WORKLOAD["rows"], in_f), seed=2000 + i)
         xs_host.append(x)
         xs_dev.append(torch.from_numpy(x).to(device))
     torch.cuda.synchronize(device)
-    return ws, xs_dev, xs_host
+    return ws, xs_dev, xs_host, ranges
 
 
 def run_mlq(args):
+    import importlib
+
     import torch
     import torch.distributed as dist
 
@@ -250,24 +267,60 @@ def run_mlq(args):
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
     pkg = load_pkg()
     mlq = pkg.mlq
+    sh = importlib.import_module("mini_llama_b200.sharding")
     fmt = WORKLOAD["fmt"]
     mats = WORKLOAD["matrices"]
-    ws, xs, xs_host = make_inputs(torch, pkg, device)
-    ys = [torch.empty((WORKLOAD["rows"], o), dtype=torch.float32, device=device) for _, o, _ in mats]
+    rows = WORKLOAD["rows"]
+    ws, xs, xs_host, ranges = make_inputs(torch, pkg, device, world, rank)
     bytes_step = sum(weight_bytes(fmt, o, i) for _, o, i in mats)
-    nblocks = [w.numel() // mlq.BLOCK_BYTES[fmt] for w in ws]
     stream = torch.cuda.Stream(device)
-    sh = stream.cuda_stream
+    sh_stream = stream.cuda_stream
     L = mlq.lib()
+    fid = mlq.FORMATS[fmt]
+
+    # per matrix: a callable launching this rank's share of it
+    calls, ybufs, launches_per_step = [], [], 0
+    group = None
+    if world > 1:
+        group = sh.PeerGroup(mlq, dist, rank, world)
+        flags = group.alloc(mlq.flag_bytes())
+    epoch = [0]
+    for j, (name, out_f, in_f) in enumerate(mats):
+        b, e = ranges[j][rank]
+        if world == 1 or PLACEMENT.get(name) == "local0":
+            if e == b:
+                calls.append(None)
+                ybufs.append(None)
+                continue
+            y = torch.empty((rows, out_f), dtype=torch.float32, device=device)
+            nb = ws[j].numel() // mlq.BLOCK_BYTES[fmt]
+
+            def call(j=j, out_f=out_f, in_f=in_f, y=y, nb=nb):
+                st = L.mlq_linear(fid, ws[j].data_ptr(), nb, out_f, in_f, xs[j].data_ptr(), rows,
+                                  y.data_ptr(), sh_stream)
+                if st != 0:
+                    raise RuntimeError(L.mlq_last_error().decode())
+                return y.data_ptr()
+            calls.append(call)
+            ybufs.append(lambda y=y: y.data_ptr())
+        else:
+            lin = sh.ShardedLinear(mlq, fmt, out_f, in_f, rows, ranges[j], rank, group, flags)
+
+            def call(j=j, lin=lin):
+                epoch[0] += 1
+                return lin(ws[j].data_ptr() if ws[j] is not None else 0, xs[j].data_ptr(), epoch[0],
+                           sh_stream)
+            calls.append(call)
+            ybufs.append(lambda lin=lin: lin.y_ptr(epoch[0]))
+        launches_per_step += 2  # x-prep + streaming kernel
 
     def step(events=None):
-        for j, (name, out_f, in_f) in enumerate(mats):
+        for j, call in enumerate(calls):
+            if call is None:
+                continue
             if events is not None:
                 events[j][0].record(stream)
-            st = L.mlq_linear(2, ws[j].data_ptr(), nblocks[j], out_f, in_f, xs[j].data_ptr(),
-                              WORKLOAD["rows"], ys[j].data_ptr(), sh)
-            if st != 0:
-                raise RuntimeError(L.mlq_last_error().decode())
+            call()
             if events is not None:
                 events[j][1].record(stream)
 
@@ -294,40 +347,55 @@ def run_mlq(args):
         dist.all_reduce(tm, op=dist.ReduceOp.MAX)
         ms = float(tm.item())
     torch.cuda.synchronize(device)
-    value = bytes_step * args.steps * world / (ms / 1e3) / 1e9
+    value = bytes_step * args.steps / (ms / 1e3) / 1e9
 
-    # ---- per-launch durations of the dominant kernel (CUDA events on its stream) ----
+    # ---- per-launch durations (CUDA events on the launching stream) ----
     k2 = max(20, min(args.steps, 400))
     evs = [[[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)]
             for _ in mats] for _ in range(k2)]
+    if world > 1:
+        dist.barrier()
     with torch.cuda.stream(stream):
         for k in range(k2):
             step(evs[k])
     torch.cuda.synchronize(device)
     per = {name: statistics.mean(evs[k][j][0].elapsed_time(evs[k][j][1]) for k in range(k2))
-           for j, (name, _, _) in enumerate(mats)}
+           for j, (name, _, _) in enumerate(mats) if calls[j] is not None}
     peak, peak_kind = hbm_peak()
-    dom = max(mats, key=lambda m: weight_bytes(fmt, m[1], m[2]))
-    dom_bytes = weight_bytes(fmt, dom[1], dom[2])
-    dom = dom[0]
+    # dominant launch: the largest share of weight bytes on this rank
+    def local_bytes(j):
+        b, e = ranges[j][rank]
+        return weight_bytes(fmt, e - b, mats[j][2])
+    dj = max((j for j in range(len(mats)) if calls[j] is not None), key=local_bytes)
+    dom, dom_bytes = mats[dj][0], local_bytes(dj)
     achieved = dom_bytes / (per[dom] / 1e3) / 1e9
     kernel_sum_ms = sum(per.values())
-    traffic = read_traffic()
+    traffic = read_traffic() if world == 1 else None
 
-    # ---- e2e: host x / host y through the C ABI (copies inside the timed region) ----
+    # ---- e2e: host x / host y around every call, copies inside the timed region ----
     e2e = None
     if not args.no_e2e:
         xh = [torch.from_numpy(x).pin_memory() for x in xs_host]
-        yh = [torch.empty((WORKLOAD["rows"], o), dtype=torch.float32).pin_memory() for _, o, _ in mats]
+        yh = [torch.empty((rows, o), dtype=torch.float32).pin_memory() for _, o, _ in mats]
         ke = max(3, min(args.steps, 300))
 
         def e2e_step():
-            for j, (name, out_f, in_f) in enumerate(mats):
-                st = L.mlq_linear_host(2, ws[j].data_ptr(), nblocks[j], out_f, in_f,
-                                       xh[j].data_ptr(), WORKLOAD["rows"], None, yh[j].data_ptr(),
-                                       local, sh)
-                if st != 0:
-                    raise RuntimeError(L.mlq_last_error().decode())
+            if world == 1:
+                for j, (name, out_f, in_f) in enumerate(mats):
+                    st = L.mlq_linear_host(fid, ws[j].data_ptr(), ws[j].numel() // mlq.BLOCK_BYTES[fmt],
+                                           out_f, in_f, xh[j].data_ptr(), rows, None,
+                                           yh[j].data_ptr(), local, sh_stream)
+                    if st != 0:
+                        raise RuntimeError(L.mlq_last_error().decode())
+                return
+            with torch.cuda.stream(stream):
+                for j, (name, out_f, in_f) in enumerate(mats):
+                    if calls[j] is None:
+                        continue
+                    xs[j].copy_(xh[j], non_blocking=True)
+                    yp = calls[j]()
+                    yh[j].copy_(sh.device_view(yp, (rows, out_f)), non_blocking=True)
+                stream.synchronize()
         for _ in range(3):
             e2e_step()
         if world > 1:
@@ -344,10 +412,12 @@ def run_mlq(args):
             tm = torch.tensor([ems], device=device)
             dist.all_reduce(tm, op=dist.ReduceOp.MAX)
             ems = float(tm.item())
-        e2e = {"value": round(bytes_step * ke * world / (ems / 1e3) / 1e9, 2), "unit": UNIT,
-               "h2d_bytes_per_step": sum(4 * WORKLOAD["rows"] * i for _, _, i in mats),
-               "d2h_bytes_per_step": sum(4 * WORKLOAD["rows"] * o for _, o, _ in mats),
-               "steps": ke, "path": "mlq_linear_host (device weights, pinned host x/y)"}
+        h2d = sum(4 * rows * i for j, (_, _, i) in enumerate(mats) if calls[j] is not None)
+        d2h = sum(4 * rows * o for j, (_, o, _) in enumerate(mats) if calls[j] is not None)
+        e2e = {"value": round(bytes_step * ke / (ems / 1e3) / 1e9, 2), "unit": UNIT,
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": ke,
+               "path": ("mlq_linear_host (device weights, pinned host x/y)" if world == 1 else
+                        "pinned x H2D + mlq_linear_allgather / mlq_linear + y D2H, per matrix")}
 
     err = mlq.device_error(local)
     cpu = None
@@ -358,26 +428,30 @@ def run_mlq(args):
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5),
-            "higher_is_better": True, "scaling": "weak" if world > 1 else "weak",
+            "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "fp32 activations x q4_0 weights",
             "data": "synthetic (seeded N(0,0.02) weights quantized to q4_0; N(0,1) x)",
-            "config": {"workload": WORKLOAD["name"], "format": fmt, "batch": WORKLOAD["rows"],
+            "config": {"workload": WORKLOAD["name"], "format": fmt, "batch": rows,
                        "matrices": {n: [o, i] for n, o, i in mats},
                        "weight_bytes_per_step": bytes_step,
+                       "placement": PLACEMENT if world > 1 else "all on one GPU",
                        "l2": "inputs larger than L2 (437.6 MB per step vs 126 MB L2); no flush"},
-            "roofline": {"bound": "hbm", "kernel": f"gemv_stream_kernel<q4_0,1,4> ({dom} launch)",
+            "roofline": {"bound": "hbm", "kernel": f"gemv_stream_kernel<q4_0,1,4,2> ({dom} launch, rank 0)",
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                          "traffic": traffic, "algorithmic_bytes_per_launch": dom_bytes,
                          "launch_ms": round(per[dom], 5),
-                         "all_launches_GBps": round(bytes_step / (kernel_sum_ms / 1e3) / 1e9, 1),
+                         "all_launches_GBps": round(sum(local_bytes(j) for j in range(len(mats))
+                                                        if calls[j] is not None)
+                                                    / (kernel_sum_ms / 1e3) / 1e9, 1),
                          "per_launch_ms": {k: round(v, 5) for k, v in per.items()}},
-            "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps * len(mats),
+            "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps * launches_per_step,
             "clocks": clocks.summary(), "device_error": err,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
+        group.close()
         dist.destroy_process_group()
 
 

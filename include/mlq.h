@@ -139,6 +139,56 @@ MLQ_API mlq_status mlq_dequantize(mlq_format fmt, const void* w, size_t block_co
 MLQ_API mlq_status mlq_quantize(mlq_format fmt, const float* src, int rows, int cols,
                                 void* blocks, mlq_stream stream);
 
+/* ---------------------------------------------------------------------------
+ * Row-sharded linear with the all-gather fused into the kernel
+ * (one process per GPU, peers reachable over NVLink)
+ *
+ * The reference runs every linear on one device (cuda_weight_upload.h:46,
+ * backend.h:15-19) and has no multi-GPU code.  This is the sharded form of
+ * forwardLinearDevice (src/forward.cc:190-225): rank r keeps rows
+ * [row_begin, row_end) of W resident (w_shard = those rows' blocks, e.g.
+ * w + row_begin * ceil(in/32) blocks), computes those outputs and stores
+ * them straight into EVERY rank's y over NVLink (peer_y[q] is rank q's y
+ * mapped into this process, peer_y[rank] the local one; each y is
+ * [rows][out_features]).  The kernel then signals the peers and waits,
+ * bounded (2 s, then MLQ_ERR_TIMEOUT via mlq_device_error), until every
+ * rank's rows have landed in its own y -- when it completes, y is complete
+ * on this GPU.  The row ranges of all ranks must tile [0, out_features);
+ * a rank may own zero rows (it then only takes part in the handshake).
+ *
+ * peer_flags[q] is rank q's flag buffer (mlq_flag_bytes() bytes, zeroed
+ * once before the first call).  `epoch` is 1 on the first call and grows
+ * by one per call on every rank, in the same call order on every rank.
+ * Consecutive calls should alternate between two y buffers, so a fast rank
+ * never overwrites a y a slow peer is still reading.  Requirements: weights
+ * and x 16-B aligned, an even block count per row for q8_0/q4_0,
+ * in_features % 4 == 0, rows <= 64, world_size <= 8.
+ * ------------------------------------------------------------------------- */
+MLQ_API mlq_status mlq_linear_allgather(mlq_format fmt, const void* w_shard,
+                                        size_t shard_block_count, int out_features,
+                                        int in_features, int row_begin, int row_end,
+                                        const float* x, int rows, float* const* peer_y,
+                                        uint32_t* const* peer_flags, int world_size, int rank,
+                                        uint32_t epoch, mlq_stream stream);
+
+/* Bytes of one rank's flag buffer for mlq_linear_allgather (256). */
+MLQ_API size_t mlq_flag_bytes(void);
+
+/* Device memory shared with the other ranks' processes (CUDA IPC; plain
+ * peer mappings, no multicast objects).  mlq_peer_alloc allocates `bytes`
+ * on the current device, zeroes it and returns an opaque handle to send to
+ * the peers; mlq_peer_open maps a peer's handle into this process (peer
+ * access enabled lazily); mlq_peer_close unmaps it, mlq_peer_free frees the
+ * local allocation. */
+typedef struct mlq_ipc_handle {
+    unsigned char bytes[64];
+} mlq_ipc_handle;
+
+MLQ_API mlq_status mlq_peer_alloc(size_t bytes, void** ptr, mlq_ipc_handle* handle);
+MLQ_API mlq_status mlq_peer_open(const mlq_ipc_handle* handle, void** ptr);
+MLQ_API mlq_status mlq_peer_close(void* ptr);
+MLQ_API mlq_status mlq_peer_free(void* ptr);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

@@ -9,6 +9,7 @@
 
 #include <cstdio>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <string>
 
@@ -34,13 +35,23 @@ mlq_status fail_cuda(const char* what, cudaError_t e) {
 }
 
 constexpr int kMaxDevices = 64;
-constexpr int kSmemBudget = 232448 - 1024;  // dynamic smem per CTA, leaving room for static
+constexpr int kFlagBytes = 256;  // per-rank flag buffer of the sharded calls
+constexpr int kDoneWord = 32;    // its CTA completion counter (own 128-B line)
+
+// Device workspace of one stream (the prepared x of the streaming GEMV).
+struct Workspace {
+    void* ptr = nullptr;
+    size_t cap = 0;
+};
 
 struct DeviceState {
     std::once_flag once;
     cudaError_t init_err = cudaSuccess;
     int sm_count = 0;
+    int smem_per_sm = 0;
     int* err_flag = nullptr;  // device address of g_mlq_device_error
+    std::mutex ws_mu;
+    std::map<cudaStream_t, Workspace> ws;  // one per stream: calls on a stream are ordered
     std::mutex host_mu;       // serialises the *_host entry points' staging
     float* x_stage = nullptr;
     float* y_stage = nullptr;
@@ -58,6 +69,8 @@ DeviceState* device_state(int dev, mlq_status* st) {
     DeviceState& s = g_dev[dev];
     std::call_once(s.once, [&] {
         cudaError_t e = cudaDeviceGetAttribute(&s.sm_count, cudaDevAttrMultiProcessorCount, dev);
+        if (e == cudaSuccess)
+            e = cudaDeviceGetAttribute(&s.smem_per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
         if (e == cudaSuccess) e = cudaGetSymbolAddress(reinterpret_cast<void**>(&s.err_flag), g_mlq_device_error);
         s.init_err = e;
     });
@@ -66,6 +79,30 @@ DeviceState* device_state(int dev, mlq_status* st) {
         return nullptr;
     }
     return &s;
+}
+
+// Workspace of at least `bytes` for `stream`.  Growing it waits for the
+// stream (the old buffer may still be read by queued kernels), so the first
+// call with the largest shape on a stream should come before any stream
+// capture.
+mlq_status stream_workspace(DeviceState* ds, cudaStream_t stream, size_t bytes, void** out) {
+    std::lock_guard<std::mutex> lock(ds->ws_mu);
+    Workspace& w = ds->ws[stream];
+    if (w.cap < bytes) {
+        if (w.ptr) {
+            cudaError_t e = cudaStreamSynchronize(stream);
+            if (e != cudaSuccess) return fail_cuda("cudaStreamSynchronize (workspace)", e);
+            cudaFree(w.ptr);
+            w.ptr = nullptr;
+            w.cap = 0;
+        }
+        size_t cap = bytes < (1u << 20) ? (1u << 20) : bytes;
+        cudaError_t e = cudaMalloc(&w.ptr, cap);
+        if (e != cudaSuccess) return fail_cuda("cudaMalloc (workspace)", e);
+        w.cap = cap;
+    }
+    *out = w.ptr;
+    return MLQ_OK;
 }
 
 bool known_format(int fmt) { return fmt == MLQ_Q8_0 || fmt == MLQ_Q4_0 || fmt == MLQ_Q4_1; }
@@ -92,24 +129,35 @@ mlq_status validate_linear(int fmt, const void* w, size_t block_count, int out, 
     return MLQ_OK;
 }
 
-mlq_status run_linear(int fmt, const void* w, int out, int in, const float* x, int rows, float* y,
-                      cudaStream_t stream) {
+// Shard/gather description of one streaming call (a plain call is world 1).
+struct Gather {
+    int world = 1, rank = 0;
+    int row_offset = 0;          // global row of the streamed rows' first row
+    int y_stride = 0;            // total output features
+    float* const* ys = nullptr;  // world output bases (plain call: &y)
+    uint32_t* const* flags = nullptr;
+    uint32_t epoch = 0;
+};
+
+bool streamable(int fmt, const void* w, const float* x, int in) {
+    const int bpr = (in + mlq::kQK - 1) / mlq::kQK;
+    const int gblocks = fmt == MLQ_Q4_1 ? 1 : 2;
+    return reinterpret_cast<uintptr_t>(w) % 16 == 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0 &&
+           bpr % gblocks == 0 && in % 4 == 0;
+}
+
+// Streams `out` rows starting at w through the x-prep + streaming kernels,
+// one pass per <= 8 rows of x.
+mlq_status run_stream(int fmt, const void* w, int out, int in, const float* x, int rows,
+                      const Gather& g, cudaStream_t stream) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return fail_cuda("cudaGetDevice", e);
     mlq_status st = MLQ_OK;
     DeviceState* ds = device_state(dev, &st);
     if (!ds) return st;
-
     const int bpr = (in + mlq::kQK - 1) / mlq::kQK;
     const int gblocks = fmt == MLQ_Q4_1 ? 1 : 2;
-    const uintptr_t wa = reinterpret_cast<uintptr_t>(w);
-    const uintptr_t xa = reinterpret_cast<uintptr_t>(x);
-    const bool streamable = (wa % 16 == 0) && (xa % 16 == 0) && (bpr % gblocks == 0) && (in % 4 == 0);
-    if (!streamable) {
-        e = mlq::launch_gemv_generic(fmt, static_cast<const uint8_t*>(w), x, y, out, in, rows, bpr, stream);
-        return e == cudaSuccess ? MLQ_OK : fail_cuda("gemv_generic launch", e);
-    }
     mlq::GemvArgs a{};
     a.w = static_cast<const uint8_t*>(w);
     a.out = out;
@@ -117,21 +165,61 @@ mlq_status run_linear(int fmt, const void* w, int out, int in, const float* x, i
     a.bpr = bpr;
     a.gpr = bpr / gblocks;
     a.ktiles = (a.gpr + 31) / 32;
-    a.y_stride = out;
+    a.y_stride = g.y_stride;
+    a.row_offset = g.row_offset;
+    a.ny = g.world;
     a.row_bytes = (long long)bpr * mlq::block_bytes(fmt);
     a.total_bytes = a.row_bytes * out;
     a.err = ds->err_flag;
-    const int grid = out < ds->sm_count ? out : ds->sm_count;
+    a.rank = g.rank;
+    a.epoch = g.epoch;
+    if (g.world > 1) {
+        for (int r = 0; r < g.world; ++r) a.peer_flags[r] = g.flags[r];
+        a.local_flags = g.flags[g.rank];
+        a.done_counter = reinterpret_cast<unsigned int*>(g.flags[g.rank] + kDoneWord);
+    }
+    // one prepared-x region per pass, so no pass overwrites another's input
+    size_t ws_total = 0;
+    for (int m0 = 0; m0 < rows;) {
+        const int mt = mlq::gemv_tokens_per_pass(rows - m0);
+        ws_total += mlq::gemv_xprep_bytes(fmt, mt, a.ktiles);
+        m0 += rows - m0 < mt ? rows - m0 : mt;
+    }
+    void* ws = nullptr;
+    st = stream_workspace(ds, stream, ws_total, &ws);
+    if (st != MLQ_OK) return st;
+    uint8_t* wsp = static_cast<uint8_t*>(ws);
     for (int m0 = 0; m0 < rows;) {
         const int mt = mlq::gemv_tokens_per_pass(rows - m0);
         a.x = x + (long long)m0 * in;
-        a.y = y + (long long)m0 * out;
         a.M = rows - m0 < mt ? rows - m0 : mt;
-        e = mlq::launch_gemv_stream(fmt, a, mt, grid, kSmemBudget, stream);
+        for (int r = 0; r < g.world; ++r) a.ys[r] = g.ys[r] + (long long)m0 * g.y_stride;
+        // only the last pass runs the cross-rank handshake: it is stream-ordered
+        // after the earlier passes' stores
+        a.world = (m0 + a.M >= rows) ? g.world : 1;
+        a.xprep = wsp;
+        e = mlq::launch_gemv_xprep(fmt, a.x, in, a.M, mt, a.ktiles, wsp, stream);
+        if (e != cudaSuccess) return fail_cuda("gemv x-prep launch", e);
+        e = mlq::launch_gemv_stream(fmt, a, mt, ds->sm_count, ds->smem_per_sm, stream);
         if (e != cudaSuccess) return fail_cuda("gemv_stream launch", e);
+        wsp += mlq::gemv_xprep_bytes(fmt, mt, a.ktiles);
         m0 += a.M;
     }
     return MLQ_OK;
+}
+
+mlq_status run_linear(int fmt, const void* w, int out, int in, const float* x, int rows, float* y,
+                      cudaStream_t stream) {
+    if (!streamable(fmt, w, x, in)) {
+        const int bpr = (in + mlq::kQK - 1) / mlq::kQK;
+        cudaError_t e = mlq::launch_gemv_generic(fmt, static_cast<const uint8_t*>(w), x, y, out, in,
+                                                 rows, bpr, stream);
+        return e == cudaSuccess ? MLQ_OK : fail_cuda("gemv_generic launch", e);
+    }
+    Gather g;
+    g.y_stride = out;
+    g.ys = &y;
+    return run_stream(fmt, w, out, in, x, rows, g, stream);
 }
 
 // Grows a per-device staging buffer (called under host_mu, device current).
@@ -321,6 +409,104 @@ MLQ_API mlq_status mlq_quantize(mlq_format fmt, const float* src, int rows, int 
     } catch (...) {
         return fail(MLQ_ERR_CUDA, "mlq_quantize: host exception");
     }
+}
+
+MLQ_API size_t mlq_flag_bytes(void) { return kFlagBytes; }
+
+MLQ_API mlq_status mlq_linear_allgather(mlq_format fmt, const void* w_shard,
+                                        size_t shard_block_count, int out_features,
+                                        int in_features, int row_begin, int row_end,
+                                        const float* x, int rows, float* const* peer_y,
+                                        uint32_t* const* peer_flags, int world_size, int rank,
+                                        uint32_t epoch, mlq_stream stream) {
+    try {
+        const char* who = "mlq_linear_allgather";
+        if (!known_format(fmt)) return fail(MLQ_ERR_FORMAT, std::string(who) + ": unknown block format");
+        if (in_features <= 0 || out_features <= 0 || rows <= 0)
+            return fail(MLQ_ERR_EMPTY, std::string(who) + ": empty tensors are not supported");
+        if (rows > 64) return fail(MLQ_ERR_RANGE, std::string(who) + ": at most 64 rows of x");
+        if (world_size < 1 || world_size > mlq::kMaxWorld || rank < 0 || rank >= world_size)
+            return fail(MLQ_ERR_COMM, std::string(who) + ": world_size must be 1..8 and 0 <= rank < world_size");
+        if (row_begin < 0 || row_end < row_begin || row_end > out_features)
+            return fail(MLQ_ERR_COMM, std::string(who) + ": row range outside [0, out_features]");
+        if (epoch == 0) return fail(MLQ_ERR_COMM, std::string(who) + ": epoch starts at 1");
+        if (!x || !peer_y || !peer_flags) return fail(MLQ_ERR_NULL, std::string(who) + ": null pointer");
+        for (int r = 0; r < world_size; ++r)
+            if (!peer_y[r] || !peer_flags[r])
+                return fail(MLQ_ERR_NULL, std::string(who) + ": null peer pointer for rank " + std::to_string(r));
+        const int shard_rows = row_end - row_begin;
+        const size_t expected = (size_t)shard_rows * (size_t)((in_features + mlq::kQK - 1) / mlq::kQK);
+        if (shard_block_count != expected)
+            return fail(MLQ_ERR_BLOCK_COUNT, std::string(who) + ": block count mismatch: expected " +
+                                                 std::to_string(expected) + ", got " +
+                                                 std::to_string(shard_block_count));
+        if (shard_rows > 0 && !w_shard) return fail(MLQ_ERR_NULL, std::string(who) + ": null weight pointer");
+        static const uint8_t kAligned[16] = {};
+        const void* wcheck = shard_rows > 0 ? w_shard : kAligned;
+        if (!streamable(fmt, wcheck, x, in_features) ||
+            reinterpret_cast<uintptr_t>(w_shard) % 16 != 0)
+            return fail(MLQ_ERR_SHAPE, std::string(who) +
+                                           ": needs 16-B aligned weights and x, an even block count per "
+                                           "row (q8_0/q4_0) and in_features % 4 == 0");
+        Gather g;
+        g.world = world_size;
+        g.rank = rank;
+        g.row_offset = row_begin;
+        g.y_stride = out_features;
+        g.ys = peer_y;
+        g.flags = peer_flags;
+        g.epoch = epoch;
+        return run_stream(fmt, w_shard, shard_rows, in_features, x, rows, g,
+                          reinterpret_cast<cudaStream_t>(stream));
+    } catch (...) {
+        return fail(MLQ_ERR_CUDA, "mlq_linear_allgather: host exception");
+    }
+}
+
+MLQ_API mlq_status mlq_peer_alloc(size_t bytes, void** ptr, mlq_ipc_handle* handle) {
+    try {
+        if (!ptr || !handle) return fail(MLQ_ERR_NULL, "mlq_peer_alloc: null pointer");
+        if (bytes == 0) return fail(MLQ_ERR_EMPTY, "mlq_peer_alloc: zero bytes");
+        *ptr = nullptr;
+        cudaError_t e = cudaMalloc(ptr, bytes);
+        if (e != cudaSuccess) return fail_cuda("cudaMalloc (peer buffer)", e);
+        e = cudaMemset(*ptr, 0, bytes);
+        if (e == cudaSuccess) e = cudaDeviceSynchronize();
+        cudaIpcMemHandle_t h;
+        if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, *ptr);
+        if (e != cudaSuccess) {
+            cudaFree(*ptr);
+            *ptr = nullptr;
+            return fail_cuda("cudaIpcGetMemHandle", e);
+        }
+        static_assert(sizeof(h) == sizeof(handle->bytes), "IPC handle size");
+        std::memcpy(handle->bytes, &h, sizeof(h));
+        return MLQ_OK;
+    } catch (...) {
+        return fail(MLQ_ERR_CUDA, "mlq_peer_alloc: host exception");
+    }
+}
+
+MLQ_API mlq_status mlq_peer_open(const mlq_ipc_handle* handle, void** ptr) {
+    try {
+        if (!ptr || !handle) return fail(MLQ_ERR_NULL, "mlq_peer_open: null pointer");
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, handle->bytes, sizeof(h));
+        cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+        return e == cudaSuccess ? MLQ_OK : fail_cuda("cudaIpcOpenMemHandle", e);
+    } catch (...) {
+        return fail(MLQ_ERR_CUDA, "mlq_peer_open: host exception");
+    }
+}
+
+MLQ_API mlq_status mlq_peer_close(void* ptr) {
+    cudaError_t e = cudaIpcCloseMemHandle(ptr);
+    return e == cudaSuccess ? MLQ_OK : fail_cuda("cudaIpcCloseMemHandle", e);
+}
+
+MLQ_API mlq_status mlq_peer_free(void* ptr) {
+    cudaError_t e = cudaFree(ptr);
+    return e == cudaSuccess ? MLQ_OK : fail_cuda("cudaFree (peer buffer)", e);
 }
 
 }  // extern "C"

@@ -54,7 +54,7 @@ __device__ __forceinline__ float half_bits_to_float(uint32_t bits16) {
 // Error reporting from kernels.  A kernel that gives up (a bounded wait ran
 // out) records a code here and returns; the host reads it back with
 // mlq_device_error().  Codes: 1 = pipeline "full" wait, 2 = "empty" wait,
-// 3 = drain wait, 4 = peer flag wait.
+// 3 = drain wait, 4 = peer flag wait, 5 = consumer rendezvous.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void report_error(int* err, int code) {
     if (err) atomicCAS(err, 0, code);
@@ -136,6 +136,17 @@ __device__ __forceinline__ float4 ldg_nc_f4(const float* p) {
     asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0,%1,%2,%3}, [%4];"
                  : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
                  : "l"(p));
+    return v;
+}
+
+// System-scope release store / acquire load of a 32-bit flag (peer memory).
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
 

@@ -57,7 +57,8 @@ struct GemvCfg {
     static constexpr int W_BYTES = RT * SLOT;
     static constexpr int X_BYTES = MT * KTE * 4;
     static constexpr int S_BYTES = MT * 32 * G * 4;
-    static constexpr int STAGE = W_BYTES + X_BYTES + S_BYTES;
+    static constexpr int XT_BYTES = X_BYTES + S_BYTES;  // prepared x tile (x + block sums)
+    static constexpr int STAGE = W_BYTES + XT_BYTES;
     static_assert(WPG % 2 == 1, "lane-group word count must be odd");
     static_assert(SLOT % 16 == 0 && STAGE % 16 == 0, "stage alignment");
 };
@@ -113,13 +114,50 @@ __device__ __forceinline__ uint32_t d_bits(const uint32_t* wv, int bg) {
     return bg == 0 ? (wv[0] & 0xFFFFu) : (wv[8] >> 16);
 }
 
-template <int F, int MT, int RPW>
-__global__ void __launch_bounds__(kThreads, 1) gemv_stream_kernel(GemvArgs a) {
+// ---------------------------------------------------------------------------
+// x preparation, once per call: x[M][in] -> per K-tile blocks of
+//   [m][part row = bg*8 + p][lane-group g ^ p] float4   (the consumers' order)
+//   [m][block] float                                    (x sum of each block)
+// zero-padded past `in` and for tokens m >= M.  One CTA per (K-tile, token).
+// ---------------------------------------------------------------------------
+template <int F, int MT>
+__global__ void __launch_bounds__(128) xprep_kernel(const float* __restrict__ x, int in, int M,
+                                                    uint8_t* __restrict__ out) {
+    constexpr int G = Fmt<F>::kGroupBlocks;
+    constexpr int KTE = 32 * G * kQK;
+    constexpr int X_BYTES = MT * KTE * 4;
+    constexpr int XT_BYTES = X_BYTES + MT * 32 * G * 4;
+    const int kt = blockIdx.x / MT;
+    const int m = blockIdx.x % MT;
+    float4* xs = reinterpret_cast<float4*>(out + (size_t)kt * XT_BYTES) + (size_t)m * (KTE / 4);
+    float* ss = reinterpret_cast<float*>(out + (size_t)kt * XT_BYTES + X_BYTES) + m * 32 * G;
+    const long long k0 = (long long)kt * KTE;
+    for (int q = threadIdx.x; q < KTE / 4; q += blockDim.x) {
+        const int e4 = q * 4;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (m < M && k0 + e4 < in) v = *reinterpret_cast<const float4*>(x + (long long)m * in + k0 + e4);
+        float sum = (v.x + v.y) + (v.z + v.w);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+        const int blk = e4 >> 5;
+        const int g = blk / G;
+        const int bg = blk % G;
+        const int p = part_of<F>(e4 & 31);
+        xs[(bg * 8 + p) * 32 + (g ^ p)] = v;
+        if ((q & 7) == 0) ss[blk] = sum;
+    }
+}
+
+template <int F, int MT, int RPW, int MINB>
+__global__ void __launch_bounds__(kThreads, MINB) gemv_stream_kernel(GemvArgs a) {
     using C = GemvCfg<F, MT, RPW>;
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(8) uint64_t full_bar[kMaxStages];
     __shared__ __align__(8) uint64_t empty_bar[kMaxStages];
     __shared__ int abort_flag;
+    __shared__ float tile_res[2][MT * C::RT];  // per-tile results, double-buffered
+    __shared__ __align__(8) uint64_t tile_bar;  // consumer warps' per-tile rendezvous
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -130,6 +168,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_stream_kernel(GemvArgs a) {
             mbar_init(smem_u32(&full_bar[s]), 32);
             mbar_init(smem_u32(&empty_bar[s]), kConsumerWarps);
         }
+        mbar_init(smem_u32(&tile_bar), kConsumerWarps);
         abort_flag = 0;
         fence_mbar_init();
     }
@@ -174,47 +213,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_stream_kernel(GemvArgs a) {
                 uint32_t tx = bytes;
 #pragma unroll
                 for (int off = 16; off > 0; off >>= 1) tx += __shfl_xor_sync(0xffffffffu, tx, off);
-                if (lane == 0) mbar_expect_tx(fb, tx);
+                if (lane == 0) mbar_expect_tx(fb, tx + (uint32_t)C::XT_BYTES);
                 __syncwarp();
                 if (bytes) bulk_g2s(stage + (uint32_t)lane * C::SLOT, reinterpret_cast<const void*>(lo), bytes, fb);
+                // the x tile of this K-tile, prepared once per call by xprep_kernel
+                if (lane == 31)
+                    bulk_g2s(stage + C::W_BYTES, a.xprep + (size_t)kt * C::XT_BYTES, (uint32_t)C::XT_BYTES, fb);
                 if (lane < nrows) {
                     // bytes past the array's last 16-B boundary: plain copy
                     for (uintptr_t q = (bytes ? hi : lo); q < src + seg; ++q)
                         sts_u8(stage + (uint32_t)lane * C::SLOT + (uint32_t)(q - lo),
                                *reinterpret_cast<const uint8_t*>(q));
-                }
-                // x K-tile: coalesced loads (all in flight together), block sums,
-                // swizzled lane-major stores
-                const uint32_t xs = stage + C::W_BYTES;
-                const uint32_t ss = xs + C::X_BYTES;
-                const long long k0 = (long long)kt * C::KTE;
-                constexpr int NV = C::KTE / 128;  // float4 loads per lane per token
-#pragma unroll 1
-                for (int m = 0; m < MT; ++m) {
-                    const float* xr = a.x + (long long)m * a.in;
-                    float4 v[NV];
-#pragma unroll
-                    for (int i = 0; i < NV; ++i) {
-                        const int e4 = (i * 32 + lane) * 4;
-                        v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-                        if (m < a.M && k0 + e4 < a.in) v[i] = ldg_nc_f4(xr + k0 + e4);
-                    }
-#pragma unroll
-                    for (int i = 0; i < NV; ++i) {
-                        const int e4 = (i * 32 + lane) * 4;  // value offset inside the K-tile
-                        float sum = (v[i].x + v[i].y) + (v[i].z + v[i].w);
-                        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-                        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-                        sum += __shfl_xor_sync(0xffffffffu, sum, 4);
-                        const int blk = e4 >> 5;    // block inside the K-tile
-                        const int g = blk / C::G;   // lane-group
-                        const int bg = blk % C::G;  // block inside the group
-                        const int p = part_of<F>(e4 & 31);
-                        const int row = bg * 8 + p;
-                        const int col = g ^ p;
-                        sts_f4(xs + (uint32_t)(((m * C::G * 8 + row) * 32 + col) * 16), v[i]);
-                        if ((lane & 7) == 0) sts_f32(ss + (uint32_t)((m * 32 * C::G + blk) * 4), sum);
-                    }
                 }
                 mbar_arrive(fb);
             }
@@ -235,6 +244,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_stream_kernel(GemvArgs a) {
 
     // -------------------------------- consumers --------------------------------
     const int wc = warp - 1;
+    // byte offset of this lane's float4 in x-tile part row p: (lane ^ p) * 16
+    uint32_t xoff[8];
+#pragma unroll
+    for (int p = 0; p < 8; ++p) xoff[p] = (uint32_t)((lane ^ p) * 16);
     uint32_t seq = 0;
     for (int t = 0; t < ntiles; ++t) {
         const long long row0 = r_begin + (long long)t * C::RT;
@@ -244,6 +257,18 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_stream_kernel(GemvArgs a) {
         for (int r = 0; r < RPW; ++r)
 #pragma unroll
             for (int m = 0; m < MT; ++m) tot[r][m] = 0.f;
+        // shared-memory offset of this lane's group in each of its rows' slots:
+        // a row segment's misalignment (its address mod 16) is the same for
+        // every K-tile, because a K-tile spans 32 groups = a multiple of 16 B
+        uint32_t soff[RPW];
+        bool row_on[RPW];
+#pragma unroll
+        for (int r = 0; r < RPW; ++r) {
+            const int i = wc + r * kConsumerWarps;
+            row_on[r] = i < nrows;
+            const uintptr_t rowaddr = wbase + (uintptr_t)((row0 + i) * a.row_bytes);
+            soff[r] = (uint32_t)i * C::SLOT + (uint32_t)(rowaddr & 15) + (uint32_t)lane * C::GB;
+        }
 
         for (int kt = 0; kt < a.ktiles; ++kt, ++seq) {
             const int s = (int)(seq % (uint32_t)S);
@@ -255,20 +280,15 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_stream_kernel(GemvArgs a) {
             if (*(volatile int*)&abort_flag) return;
             const uint32_t stage = smem_base + (uint32_t)s * C::STAGE;
             const uint32_t xs = stage + C::W_BYTES;
-            const uint32_t ss = xs + C::X_BYTES;
-            const int groups = min(32, a.gpr - kt * 32);
+            const uint32_t ss = stage + C::W_BYTES + C::X_BYTES + (uint32_t)lane * C::G * 4;
+            const bool lane_on = lane < a.gpr - kt * 32;
 
             uint32_t wv[RPW][C::WPG];
 #pragma unroll
             for (int r = 0; r < RPW; ++r) {
-                const int i = wc + r * kConsumerWarps;
-                if (i < nrows && lane < groups) {
-                    const uintptr_t src = wbase + (uintptr_t)((row0 + i) * a.row_bytes) +
-                                          (uintptr_t)kt * 32u * C::GB;
-                    const uint32_t base = stage + (uint32_t)i * C::SLOT + (uint32_t)(src & 15) +
-                                          (uint32_t)lane * C::GB;
+                if (row_on[r] && lane_on) {
 #pragma unroll
-                    for (int j = 0; j < C::WPG; ++j) wv[r][j] = lds_u32(base + 4 * j);
+                    for (int j = 0; j < C::WPG; ++j) wv[r][j] = lds_u32(stage + soff[r] + 4 * j);
                 } else {
 #pragma unroll
                     for (int j = 0; j < C::WPG; ++j) wv[r][j] = 0u;
@@ -277,11 +297,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_stream_kernel(GemvArgs a) {
 
 #pragma unroll
             for (int bg = 0; bg < C::G; ++bg) {
-                float2 acc[RPW][MT];  // two partial sums per (row, token): packed FFMA2
+                // two partial sums per (row, token): even and odd parts
+                float acc0[RPW][MT], acc1[RPW][MT];
 #pragma unroll
                 for (int r = 0; r < RPW; ++r)
 #pragma unroll
-                    for (int m = 0; m < MT; ++m) acc[r][m] = make_float2(0.f, 0.f);
+                    for (int m = 0; m < MT; ++m) acc0[r][m] = acc1[r][m] = 0.f;
 
 #pragma unroll
                 for (int p = 0; p < 8; ++p) {
@@ -289,7 +310,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_stream_kernel(GemvArgs a) {
                     const int row = bg * 8 + p;
 #pragma unroll
                     for (int m = 0; m < MT; ++m)
-                        xv[m] = lds_f4(xs + (uint32_t)(((m * C::G * 8 + row) * 32 + (lane ^ p)) * 16));
+                        xv[m] = lds_f4(xs + (uint32_t)((m * C::G * 8 + row) * 512) + xoff[p]);
 #pragma unroll
                     for (int r = 0; r < RPW; ++r) {
                         float f[4];
@@ -297,29 +318,33 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_stream_kernel(GemvArgs a) {
                             q8_to_f(qs_word<F>(wv[r], bg, p), f);
                         } else {
                             const uint32_t qw = qs_word<F>(wv[r], bg, p >> 1);
-                            const uint32_t nib = (p & 1) ? ((qw >> 4) & 0x0F0F0F0Fu) : (qw & 0x0F0F0F0Fu);
+                            // high nibbles: the shift runs on the FMA pipe (IMAD.HI),
+                            // which has room; the ALU pipe carries the PRMTs
+                            const uint32_t nib = (p & 1) ? (__umulhi(qw, 0x10000000u) & 0x0F0F0F0Fu)
+                                                         : (qw & 0x0F0F0F0Fu);
                             q4_to_f(nib, f);
                         }
 #pragma unroll
                         for (int m = 0; m < MT; ++m) {
-                            acc[r][m] = __ffma2_rn(make_float2(f[0], f[1]), make_float2(xv[m].x, xv[m].y), acc[r][m]);
-                            acc[r][m] = __ffma2_rn(make_float2(f[2], f[3]), make_float2(xv[m].z, xv[m].w), acc[r][m]);
+                            float& acc = (p & 1) ? acc1[r][m] : acc0[r][m];
+                            acc = fmaf(f[0], xv[m].x, acc);
+                            acc = fmaf(f[1], xv[m].y, acc);
+                            acc = fmaf(f[2], xv[m].z, acc);
+                            acc = fmaf(f[3], xv[m].w, acc);
                         }
                     }
                 }
                 // fold the block back: scale, offset constant, q4_1 minimum
                 float sx[MT];
 #pragma unroll
-                for (int m = 0; m < MT; ++m) {
-                    uint32_t addr = ss + (uint32_t)((m * 32 * C::G + lane * C::G + bg) * 4);
-                    sx[m] = __uint_as_float(lds_u32(addr));
-                }
+                for (int m = 0; m < MT; ++m)
+                    sx[m] = __uint_as_float(lds_u32(ss + (uint32_t)((m * 32 * C::G + bg) * 4)));
 #pragma unroll
                 for (int r = 0; r < RPW; ++r) {
                     const float d = half_bits_to_float(d_bits<F>(wv[r], bg));
 #pragma unroll
                     for (int m = 0; m < MT; ++m) {
-                        const float blk = acc[r][m].x + acc[r][m].y;
+                        const float blk = acc0[r][m] + acc1[r][m];
                         if constexpr (F == kQ8_0) {
                             tot[r][m] = fmaf(d, blk, tot[r][m]);
                         } else if constexpr (F == kQ4_0) {
@@ -336,7 +361,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_stream_kernel(GemvArgs a) {
             if (lane == 0) mbar_arrive(smem_u32(&empty_bar[s]));
         }
 
-        // reduce the 32 lane partials of every (row, token) and store
+        // reduce the 32 lane partials of every (row, token) into the tile's
+        // result buffer, then store it with coalesced writes: RT consecutive
+        // floats per token, to this GPU's y and, in a sharded call, to every
+        // peer's y over NVLink.
+        float* res = tile_res[t & 1];
 #pragma unroll
         for (int r = 0; r < RPW; ++r) {
             const int i = wc + r * kConsumerWarps;
@@ -348,8 +377,55 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_stream_kernel(GemvArgs a) {
                 v += __shfl_xor_sync(0xffffffffu, v, 4);
                 v += __shfl_xor_sync(0xffffffffu, v, 2);
                 v += __shfl_xor_sync(0xffffffffu, v, 1);
-                if (i < nrows && m < a.M && lane == ((r * MT + m) & 31))
-                    a.y[(long long)m * a.y_stride + row0 + i] = v;
+                if (lane == ((r * MT + m) & 31)) res[m * C::RT + i] = v;
+            }
+        }
+        // all 8 consumer warps rendezvous (bounded: an mbarrier, not bar.sync,
+        // so a warp that left on an abort cannot hang the others)
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&tile_bar));
+        if (!mbar_wait(smem_u32(&tile_bar), (uint32_t)t & 1u)) {
+            report_error(a.err, 5);
+            return;
+        }
+        {
+            const int c = threadIdx.x - 32;  // 0 .. 255
+            const int m = c / C::RT, i = c % C::RT;
+            if (m < a.M && i < nrows) {
+                const float v = res[m * C::RT + i];
+                const long long off = (long long)m * a.y_stride + a.row_offset + row0 + i;
+                for (int d = 0; d < a.ny; ++d) a.ys[d][off] = v;
+            }
+        }
+    }
+
+    if (a.world > 1) {
+        // Sharded call: this CTA's rows are in every rank's y.  The last CTA
+        // of this rank to finish publishes the epoch to every peer, then
+        // waits (bounded) until every rank's slice has landed here.
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&tile_bar));
+        if (threadIdx.x == 32) {
+            if (!mbar_wait(smem_u32(&tile_bar), (uint32_t)ntiles & 1u)) {
+                report_error(a.err, 5);
+                return;
+            }
+            __threadfence_system();
+            const unsigned int prev = atomicAdd(a.done_counter, 1u);
+            if (prev == gridDim.x - 1) {
+                *a.done_counter = 0u;  // every CTA of this launch has counted
+                __threadfence_system();
+                for (int r = 0; r < a.world; ++r) st_release_sys(a.peer_flags[r] + a.rank, a.epoch);
+                const uint64_t t0 = global_ns();
+                for (int r = 0; r < a.world; ++r) {
+                    while ((int)(ld_acquire_sys(a.local_flags + r) - a.epoch) < 0) {
+                        if (global_ns() - t0 > kWaitLimitNs) {
+                            report_error(a.err, 4);
+                            return;
+                        }
+                        __nanosleep(64);
+                    }
+                }
             }
         }
     }
@@ -408,28 +484,31 @@ __global__ void __launch_bounds__(256) gemv_generic_kernel(const uint8_t* __rest
     }
 }
 
-template <int F, int MT, int RPW>
-cudaError_t launch_stream_t(const GemvArgs& args, int grid, int smem_budget, cudaStream_t stream) {
+template <int F, int MT, int RPW, int MINB>
+cudaError_t launch_stream_t(GemvArgs args, int sm_count, int smem_per_sm, cudaStream_t stream) {
     using C = GemvCfg<F, MT, RPW>;
+    // Per-CTA budget: the SM's shared memory split MINB ways, minus the 1 KB
+    // the driver reserves per CTA and this kernel's static barriers.
+    const int budget = smem_per_sm / MINB - 1024 - 512;
+    int S = budget / C::STAGE;
+    if (S > kMaxStages) S = kMaxStages;
+    if (S < 2) return cudaErrorInvalidConfiguration;
+    args.nstages = S;
+    const int smem = S * C::STAGE;
     static int attr_bytes[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
-    const int smem = args.nstages * C::STAGE;
     if (dev >= 64 || attr_bytes[dev] < smem) {
-        // opt in to the whole budget once per device (budget + static smem
-        // stays under the 227 KB per-block limit)
-        cudaError_t e = cudaFuncSetAttribute(gemv_stream_kernel<F, MT, RPW>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem_budget);
+        cudaError_t e = cudaFuncSetAttribute(gemv_stream_kernel<F, MT, RPW, MINB>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
-        if (dev < 64) attr_bytes[dev] = smem_budget;
+        if (dev < 64) attr_bytes[dev] = smem;
     }
-    gemv_stream_kernel<F, MT, RPW><<<grid, kThreads, smem, stream>>>(args);
+    const long long want = (long long)sm_count * MINB;
+    int grid = (int)(args.out < want ? args.out : want);
+    if (grid < 1) grid = 1;  // a rank holding no rows still runs the handshake
+    gemv_stream_kernel<F, MT, RPW, MINB><<<grid, kThreads, smem, stream>>>(args);
     return cudaGetLastError();
-}
-
-template <int F, int MT, int RPW>
-int stage_bytes_t() {
-    return GemvCfg<F, MT, RPW>::STAGE;
 }
 
 // rows-per-warp choice per format: keeps the lane-group words of all RPW
@@ -439,15 +518,19 @@ constexpr int rpw_for() {
     return F == kQ8_0 ? 2 : 4;
 }
 
+// One or two tokens per pass: two CTAs per SM (16 consumer warps per SM,
+// registers capped at 113); more tokens: one CTA per SM with deeper stages.
 template <int F, int MT>
-cudaError_t dispatch_mt(GemvArgs args, int grid, int smem_budget, cudaStream_t stream) {
+cudaError_t dispatch_mt(const GemvArgs& args, int sm_count, int smem_per_sm, cudaStream_t stream) {
     constexpr int RPW = rpw_for<F>();
-    const int stage = stage_bytes_t<F, MT, RPW>();
-    int S = smem_budget / stage;
-    if (S > kMaxStages) S = kMaxStages;
-    if (S < 2) return cudaErrorInvalidConfiguration;
-    args.nstages = S;
-    return launch_stream_t<F, MT, RPW>(args, grid, smem_budget, stream);
+    constexpr int MINB = MT <= 2 ? 2 : 1;
+    return launch_stream_t<F, MT, RPW, MINB>(args, sm_count, smem_per_sm, stream);
+}
+
+template <int F, int MT>
+cudaError_t prep_t(const float* x, int in, int M, int ktiles, uint8_t* out, cudaStream_t stream) {
+    xprep_kernel<F, MT><<<ktiles * MT, 128, 0, stream>>>(x, in, M, out);
+    return cudaGetLastError();
 }
 
 }  // namespace
@@ -456,31 +539,45 @@ int gemv_tokens_per_pass(int rows_left) {
     return rows_left >= 5 ? 8 : (rows_left >= 3 ? 4 : (rows_left == 2 ? 2 : 1));
 }
 
-cudaError_t launch_gemv_stream(int fmt, GemvArgs args, int mt, int grid, int smem_budget,
-                               cudaStream_t stream) {
-    switch (fmt) {
-        case kQ8_0:
-            switch (mt) {
-                case 1: return dispatch_mt<kQ8_0, 1>(args, grid, smem_budget, stream);
-                case 2: return dispatch_mt<kQ8_0, 2>(args, grid, smem_budget, stream);
-                case 4: return dispatch_mt<kQ8_0, 4>(args, grid, smem_budget, stream);
-                default: return dispatch_mt<kQ8_0, 8>(args, grid, smem_budget, stream);
-            }
-        case kQ4_0:
-            switch (mt) {
-                case 1: return dispatch_mt<kQ4_0, 1>(args, grid, smem_budget, stream);
-                case 2: return dispatch_mt<kQ4_0, 2>(args, grid, smem_budget, stream);
-                case 4: return dispatch_mt<kQ4_0, 4>(args, grid, smem_budget, stream);
-                default: return dispatch_mt<kQ4_0, 8>(args, grid, smem_budget, stream);
-            }
-        case kQ4_1:
-            switch (mt) {
-                case 1: return dispatch_mt<kQ4_1, 1>(args, grid, smem_budget, stream);
-                case 2: return dispatch_mt<kQ4_1, 2>(args, grid, smem_budget, stream);
-                case 4: return dispatch_mt<kQ4_1, 4>(args, grid, smem_budget, stream);
-                default: return dispatch_mt<kQ4_1, 8>(args, grid, smem_budget, stream);
-            }
+size_t gemv_xprep_bytes(int fmt, int mt, int ktiles) {
+    const int G = fmt == kQ4_1 ? 1 : 2;
+    const size_t kte = 32 * G * kQK;
+    return (size_t)ktiles * mt * (kte * 4 + 32 * G * 4);
+}
+
+cudaError_t launch_gemv_xprep(int fmt, const float* x, int in, int M, int mt, int ktiles,
+                              uint8_t* out, cudaStream_t stream) {
+#define MLQ_PREP(F)                                                             \
+    switch (mt) {                                                               \
+        case 1: return prep_t<F, 1>(x, in, M, ktiles, out, stream);             \
+        case 2: return prep_t<F, 2>(x, in, M, ktiles, out, stream);             \
+        case 4: return prep_t<F, 4>(x, in, M, ktiles, out, stream);             \
+        default: return prep_t<F, 8>(x, in, M, ktiles, out, stream);            \
     }
+    switch (fmt) {
+        case kQ8_0: MLQ_PREP(kQ8_0)
+        case kQ4_0: MLQ_PREP(kQ4_0)
+        case kQ4_1: MLQ_PREP(kQ4_1)
+    }
+#undef MLQ_PREP
+    return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_gemv_stream(int fmt, const GemvArgs& args, int mt, int sm_count, int smem_per_sm,
+                               cudaStream_t stream) {
+#define MLQ_STREAM(F)                                                                  \
+    switch (mt) {                                                                      \
+        case 1: return dispatch_mt<F, 1>(args, sm_count, smem_per_sm, stream);         \
+        case 2: return dispatch_mt<F, 2>(args, sm_count, smem_per_sm, stream);         \
+        case 4: return dispatch_mt<F, 4>(args, sm_count, smem_per_sm, stream);         \
+        default: return dispatch_mt<F, 8>(args, sm_count, smem_per_sm, stream);        \
+    }
+    switch (fmt) {
+        case kQ8_0: MLQ_STREAM(kQ8_0)
+        case kQ4_0: MLQ_STREAM(kQ4_0)
+        case kQ4_1: MLQ_STREAM(kQ4_1)
+    }
+#undef MLQ_STREAM
     return cudaErrorInvalidValue;
 }
 

@@ -11,8 +11,11 @@ namespace mlq {
 struct GemvArgs {
     const uint8_t* w;        // packed blocks, row-major [out][bpr]
     const float* x;          // [M][in]
-    float* y;                // [M][y_stride]
-    int out, in, M;          // M <= the launch's tokens-per-pass
+    const uint8_t* xprep;    // x prepared by launch_gemv_xprep (16-B aligned)
+    float* ys[8];            // output copies: [0] = this GPU's y, then peers' y
+    int ny;                  // number of valid ys
+    int row_offset;          // global index of this launch's row 0 (row shard start)
+    int out, in, M;          // out = rows streamed here; M <= tokens per pass
     int bpr;                 // blocks per row
     int gpr;                 // lane-groups per row (bpr / blocks per group)
     int ktiles;              // ceil(gpr / 32)
@@ -21,15 +24,31 @@ struct GemvArgs {
     long long row_bytes;     // bpr * block bytes
     long long total_bytes;   // out * row_bytes
     int* err;                // device error flag
+    // sharded calls only (world > 1): completion handshake
+    int world, rank;
+    uint32_t epoch;
+    uint32_t* peer_flags[8];     // rank r's flag words, mapped here
+    uint32_t* local_flags;       // this rank's flag words (world entries)
+    unsigned int* done_counter;  // this rank's CTA completion counter
 };
+
+constexpr int kMaxWorld = 8;
 
 // Tokens per pass for `rows_left` remaining rows of x: 1, 2, 4 or 8.
 int gemv_tokens_per_pass(int rows_left);
 
-// Streaming GEMV, tokens-per-pass `mt` in {1,2,4,8}; `grid` CTAs (one per
-// SM), `smem_budget` bytes of dynamic shared memory at most.
-cudaError_t launch_gemv_stream(int fmt, GemvArgs args, int mt, int grid, int smem_budget,
-                               cudaStream_t stream);
+// Bytes of the prepared-x workspace of one pass (tokens-per-pass `mt`).
+size_t gemv_xprep_bytes(int fmt, int mt, int ktiles);
+
+// x[M][in] -> the streaming kernel's x tiles (lane-major, swizzled) + block sums.
+cudaError_t launch_gemv_xprep(int fmt, const float* x, int in, int M, int mt, int ktiles,
+                              uint8_t* out, cudaStream_t stream);
+
+// Streaming GEMV, tokens-per-pass `mt` in {1,2,4,8}; persistent grid of one
+// or two CTAs per SM (`sm_count` SMs with `smem_per_sm` bytes of shared
+// memory each); args.xprep must hold this pass's prepared x.
+cudaError_t launch_gemv_stream(int fmt, const GemvArgs& args, int mt, int sm_count,
+                               int smem_per_sm, cudaStream_t stream);
 
 // Any-alignment fallback GEMV (one warp per output row).
 cudaError_t launch_gemv_generic(int fmt, const uint8_t* w, const float* x, float* y, int out,

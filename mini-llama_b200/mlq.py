@@ -59,8 +59,16 @@ def lib() -> ctypes.CDLL:
         L.mlq_linear_host_weight.argtypes = [_i, _vp, _sz, _i, _i, _vp, _i, _vp, _vp, _i]
         L.mlq_dequantize.argtypes = [_i, _vp, _sz, _i, _i, _vp, _vp]
         L.mlq_quantize.argtypes = [_i, _vp, _i, _i, _vp, _vp]
+        L.mlq_flag_bytes.restype = _sz
+        L.mlq_linear_allgather.argtypes = [_i, _vp, _sz, _i, _i, _i, _i, _vp, _i, _vp, _vp, _i, _i,
+                                           ctypes.c_uint32, _vp]
+        L.mlq_peer_alloc.argtypes = [_sz, ctypes.POINTER(_vp), ctypes.c_char_p]
+        L.mlq_peer_open.argtypes = [ctypes.c_char_p, ctypes.POINTER(_vp)]
+        L.mlq_peer_close.argtypes = [_vp]
+        L.mlq_peer_free.argtypes = [_vp]
         for name in ("mlq_linear", "mlq_linear_host", "mlq_linear_host_weight", "mlq_dequantize",
-                     "mlq_quantize", "mlq_device_error"):
+                     "mlq_quantize", "mlq_device_error", "mlq_linear_allgather", "mlq_peer_alloc",
+                     "mlq_peer_open", "mlq_peer_close", "mlq_peer_free"):
             getattr(L, name).restype = _i
         _lib = L
     return _lib
@@ -176,6 +184,44 @@ def dequantize(fmt, w, out_features: int, in_features: int, stream=None):
     check(lib().mlq_dequantize(fmt_id(fmt), w.data_ptr(), nb, out_features, in_features,
                                dst.data_ptr(), _stream_handle(stream)))
     return dst
+
+
+def linear_allgather(fmt, w_shard_ptr: int, shard_blocks: int, out_features: int,
+                     in_features: int, row_begin: int, row_end: int, x_ptr: int, rows: int,
+                     peer_y_ptrs, peer_flag_ptrs, rank: int, epoch: int, stream: int | None) -> None:
+    """Row-sharded linear with the all-gather fused in (include/mlq.h)."""
+    world = len(peer_y_ptrs)
+    ys = (ctypes.c_void_p * world)(*peer_y_ptrs)
+    fs = (ctypes.c_void_p * world)(*peer_flag_ptrs)
+    check(lib().mlq_linear_allgather(fmt_id(fmt), w_shard_ptr, shard_blocks, out_features,
+                                     in_features, row_begin, row_end, x_ptr, rows, ys, fs, world,
+                                     rank, epoch, stream))
+
+
+def peer_alloc(nbytes: int):
+    """Zeroed device buffer on the current device + its 64-byte IPC handle."""
+    ptr = ctypes.c_void_p()
+    h = ctypes.create_string_buffer(64)
+    check(lib().mlq_peer_alloc(nbytes, ctypes.byref(ptr), h))
+    return int(ptr.value), bytes(h.raw)
+
+
+def peer_open(handle: bytes) -> int:
+    ptr = ctypes.c_void_p()
+    check(lib().mlq_peer_open(ctypes.create_string_buffer(handle, 64), ctypes.byref(ptr)))
+    return int(ptr.value)
+
+
+def peer_close(ptr: int) -> None:
+    check(lib().mlq_peer_close(ptr))
+
+
+def peer_free(ptr: int) -> None:
+    check(lib().mlq_peer_free(ptr))
+
+
+def flag_bytes() -> int:
+    return int(lib().mlq_flag_bytes())
 
 
 def device_error(device: int = 0) -> int:
