@@ -13,7 +13,7 @@
 #include <mutex>
 #include <string>
 
-#include "../../include/mlq.h"
+#include "mlq.h"
 #include "mlq_device.cuh"
 #include "mlq_kernels.h"
 
@@ -210,6 +210,21 @@ mlq_status run_stream(int fmt, const void* w, int out, int in, const float* x, i
 
 mlq_status run_linear(int fmt, const void* w, int out, int in, const float* x, int rows, float* y,
                       cudaStream_t stream) {
+    if (mlq::gemm_supported(fmt, w, out, in, rows)) {
+        // many rows of x: the tensor-core GEMM
+        int dev = 0;
+        cudaError_t e = cudaGetDevice(&dev);
+        if (e != cudaSuccess) return fail_cuda("cudaGetDevice", e);
+        mlq_status st = MLQ_OK;
+        DeviceState* ds = device_state(dev, &st);
+        if (!ds) return st;
+        void* ws = nullptr;
+        st = stream_workspace(ds, stream, mlq::gemm_workspace_bytes(in, rows), &ws);
+        if (st != MLQ_OK) return st;
+        e = mlq::launch_gemm(fmt, static_cast<const uint8_t*>(w), x, y, out, in, rows, ws, ds->sm_count,
+                             ds->err_flag, stream);
+        return e == cudaSuccess ? MLQ_OK : fail_cuda("gemm launch", e);
+    }
     if (!streamable(fmt, w, x, in)) {
         const int bpr = (in + mlq::kQK - 1) / mlq::kQK;
         cudaError_t e = mlq::launch_gemv_generic(fmt, static_cast<const uint8_t*>(w), x, y, out, in,

@@ -1,0 +1,502 @@
+// mlq_gemm.cu -- dequant-fused GEMM on the 5th-generation tensor cores
+// (tcgen05 + TMEM) for prefill / batched rows of x (rows >= 64).
+//
+// The reference has no GEMM for quantized weights: forwardBatch loops the
+// GEMV one token at a time (src/batch.cc:32-55) and linearQ* loops rows
+// (src/quant.cc:453-472).  This kernel computes the same y = x W^T for many
+// rows at once with the tensor cores while keeping fp32-level accuracy:
+//
+//   * W is decoded EXACTLY to fp32 (w = d*q, d*(q-8) or d*q + m, the
+//     reference's dequantizeFrom* values), then split w = wh + wl with
+//     wh = bf16_rn(w), wl = bf16_rn(w - wh);  x is split the same way.
+//   * D = wh*xh + wh*xl + wl*xh in fp32 (TMEM), three kind::f16 MMAs per
+//     K-step.  The dropped wl*xl term and the two splits' residues are
+//     below 2^-17 of each product, so y matches the fp32 reference to
+//     ~1e-5 relative -- far inside the 1e-3 contract.
+//
+// CTA = 6 warps, one 128 (W rows) x 128 (tokens) output tile at a time,
+// persistent over tiles:
+//   warp 0   TMA producer: packed W chunks (256 values per row, 2-D tensor
+//            map over the AoS bytes, no swizzle) and x hi/lo tiles (2-D
+//            tensor maps over bf16 [T][K], 128-B swizzle).
+//   warp 1   allocates 128 TMEM columns; lane 0 issues the MMAs and the
+//            tcgen05.commit arrivals.
+//   warps 2-5 ("row" threads, thread = W row = TMEM lane): decode their
+//            row's two blocks of each 64-wide K-step from shared memory,
+//            write the bf16 hi/lo A rows in the 128-B swizzled K-major
+//            layout, then run the epilogue (tcgen05.ld -> y, coalesced).
+// All mbarrier waits are bounded (2 s); no TMA multicast anywhere.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <mutex>
+
+#include "mlq_device.cuh"
+#include "mlq_kernels.h"
+
+namespace mlq {
+namespace {
+
+constexpr int BM = 128;       // W rows per tile = MMA M = TMEM lanes
+constexpr int BN = 128;       // tokens per tile = MMA N = TMEM columns
+constexpr int BK = 64;        // K per stage: one 128-byte swizzle row of bf16
+constexpr int KW = 256;       // K per packed-W chunk (8 blocks per row)
+constexpr int KSUB = KW / BK; // stages per W chunk
+constexpr int AB_STAGES = 2;
+constexpr int W_STAGES = 2;
+constexpr int kGemmThreads = 192;
+constexpr uint32_t kTmemCols = 128;
+
+template <int F>
+struct GemmCfg {
+    static constexpr int BS = Fmt<F>::kBlockBytes;
+    static constexpr int W_ROW = (KW / kQK) * BS;  // bytes of one row's chunk: 272 / 144 / 160
+    static constexpr int W_ESZ = F == kQ8_0 ? 2 : 1;  // tensor-map element (inner box <= 256 elems)
+    static constexpr int W_TILE = BM * W_ROW;
+    static constexpr int W_SLOT = (W_TILE + 1023) / 1024 * 1024;
+    static constexpr int A_TILE = BM * BK * 2;  // bf16
+    static constexpr int B_TILE = BN * BK * 2;
+    static constexpr int AB_STAGE = 2 * A_TILE + 2 * B_TILE;  // A hi, A lo, B hi, B lo
+    static constexpr int SMEM = AB_STAGES * AB_STAGE + W_STAGES * W_SLOT + 1024;  // + align slack
+    static_assert(W_ROW % 16 == 0, "W chunk row must be 16-byte granular");
+};
+
+// ---- tcgen05 / TMA PTX wrappers ------------------------------------------
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int c0, int c1,
+                                            uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+        "[%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar)
+        : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile(
+        "{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.release.cta.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(
+            bar),
+        "r"(bytes)
+        : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row atoms
+// 1024 B apart (SBO), tile base 1024-B aligned (base offset 0).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
+    return (uint64_t)((addr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// kind::f16 instruction descriptor: D f32, A/B bf16, both K-major, M x N.
+constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                            ((uint32_t)(BM >> 4) << 24);
+
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                         uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     bar)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+        "%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+          "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
+          "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]),
+          "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]),
+          "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// ---- exact decode of 8 consecutive values of a block -----------------------
+// Values e0..e0+7 of the block whose fields are in words wv[] (2-byte
+// aligned block starts are handled by the caller: wv holds the block bytes
+// from its first byte).  Returns the fp32 values w (reference dequant).
+__device__ __forceinline__ uint32_t byte_of(const uint32_t* wv, int i) {
+    return (wv[i >> 2] >> ((i & 3) * 8)) & 0xFFu;
+}
+
+template <int F>
+__device__ __forceinline__ void decode8(const uint32_t* bw, int e0, float out[8]) {
+    const float d = half_bits_to_float(bw[0] & 0xFFFFu);
+    if constexpr (F == kQ8_0) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const uint32_t b = byte_of(bw, 2 + e0 + i) ^ 0x80u;
+            const float q = __uint_as_float(0x4B000000u | b) - 8388736.0f;  // exact int8 code
+            out[i] = __fmul_rn(d, q);
+        }
+    } else if constexpr (F == kQ4_0) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int e = e0 + i;
+            const uint32_t b = byte_of(bw, 2 + (e & 15));
+            const uint32_t q = e < 16 ? (b & 15u) : (b >> 4);
+            out[i] = __fmul_rn(d, __uint_as_float(0x4B000000u | q) - 8388616.0f);  // q - 8
+        }
+    } else {
+        const float m = half_bits_to_float(bw[0] >> 16);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int e = e0 + i;
+            const uint32_t b = byte_of(bw, 4 + (e & 15));
+            const uint32_t q = e < 16 ? (b & 15u) : (b >> 4);
+            out[i] = __fmaf_rn(d, __uint_as_float(0x4B000000u | q) - 8388608.0f, m);  // d*q + m
+        }
+    }
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+}
+
+template <int F>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_xh,
+                   const __grid_constant__ CUtensorMap tm_xl, GemmArgs a) {
+    using C = GemmCfg<F>;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    __shared__ __align__(8) uint64_t ab_full[AB_STAGES], ab_empty[AB_STAGES];
+    __shared__ __align__(8) uint64_t w_full[W_STAGES], w_empty[W_STAGES];
+    __shared__ __align__(8) uint64_t acc_full, acc_empty;
+    __shared__ uint32_t tmem_base_s;
+    __shared__ int abort_flag;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;  // 1024-B aligned (SW128 atoms)
+    auto a_hi = [&](int s) { return base + (uint32_t)(s * C::AB_STAGE); };
+    auto a_lo = [&](int s) { return a_hi(s) + C::A_TILE; };
+    auto b_hi = [&](int s) { return a_hi(s) + 2 * C::A_TILE; };
+    auto b_lo = [&](int s) { return b_hi(s) + C::B_TILE; };
+    auto w_st = [&](int s) { return base + (uint32_t)(AB_STAGES * C::AB_STAGE + s * C::W_SLOT); };
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < AB_STAGES; ++s) {
+            mbar_init(smem_u32(&ab_full[s]), 1 + 4);  // producer (B bytes) + 4 row warps (A)
+            mbar_init(smem_u32(&ab_empty[s]), 1);     // tcgen05.commit
+        }
+        for (int s = 0; s < W_STAGES; ++s) {
+            mbar_init(smem_u32(&w_full[s]), 1);
+            mbar_init(smem_u32(&w_empty[s]), 4);
+        }
+        mbar_init(smem_u32(&acc_full), 1);
+        mbar_init(smem_u32(&acc_empty), 4);
+        abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(&tmem_base_s)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_base_s;
+
+    const int tiles_n = (a.T + BN - 1) / BN;
+    const int tiles_m = (a.out + BM - 1) / BM;
+    const int ntiles = tiles_m * tiles_n;
+    const int KS = (a.in + BK - 1) / BK;
+
+    if (warp == 0) {
+        // ------------------------------ TMA producer ------------------------------
+        if (lane == 0) {
+            uint32_t g = 0, gc = 0;
+            for (int tile = blockIdx.x; tile < ntiles && !*(volatile int*)&abort_flag; tile += gridDim.x) {
+                const int mt = tile / tiles_n, nt = tile % tiles_n;
+                for (int ks = 0; ks < KS; ++ks, ++g) {
+                    if (ks % KSUB == 0) {
+                        const int sw = (int)(gc % W_STAGES);
+                        if (!mbar_wait(smem_u32(&w_empty[sw]), ((gc / W_STAGES) & 1u) ^ 1u)) {
+                            report_error(a.err, 12);
+                            abort_flag = 1;
+                            break;
+                        }
+                        mbar_arrive_expect_tx(smem_u32(&w_full[sw]), (uint32_t)C::W_TILE);
+                        tma_load_2d(w_st(sw), &tm_w, (ks / KSUB) * (C::W_ROW / C::W_ESZ), mt * BM,
+                                    smem_u32(&w_full[sw]));
+                        ++gc;
+                    }
+                    const int s = (int)(g % AB_STAGES);
+                    if (!mbar_wait(smem_u32(&ab_empty[s]), ((g / AB_STAGES) & 1u) ^ 1u)) {
+                        report_error(a.err, 12);
+                        abort_flag = 1;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(smem_u32(&ab_full[s]), 2u * C::B_TILE);
+                    tma_load_2d(b_hi(s), &tm_xh, ks * BK, nt * BN, smem_u32(&ab_full[s]));
+                    tma_load_2d(b_lo(s), &tm_xl, ks * BK, nt * BN, smem_u32(&ab_full[s]));
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------ MMA issuer ------------------------------
+        uint32_t tc = 0;
+        if (lane == 0) {
+            uint32_t g = 0;
+            for (int tile = blockIdx.x; tile < ntiles && !*(volatile int*)&abort_flag; tile += gridDim.x, ++tc) {
+                if (!mbar_wait(smem_u32(&acc_empty), (tc & 1u) ^ 1u)) {
+                    report_error(a.err, 13);
+                    abort_flag = 1;
+                    break;
+                }
+                tc_fence_after();
+                for (int ks = 0; ks < KS; ++ks, ++g) {
+                    const int s = (int)(g % AB_STAGES);
+                    if (!mbar_wait(smem_u32(&ab_full[s]), (g / AB_STAGES) & 1u)) {
+                        report_error(a.err, 13);
+                        abort_flag = 1;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint64_t dah = sw128_desc(a_hi(s)), dal = sw128_desc(a_lo(s));
+                    const uint64_t dbh = sw128_desc(b_hi(s)), dbl = sw128_desc(b_lo(s));
+#pragma unroll
+                    for (int k = 0; k < BK / 16; ++k) {
+                        const uint64_t adv = (uint64_t)(k * 32) >> 4;  // 16 bf16 = 32 B along K
+                        mma_bf16(tmem, dah + adv, dbh + adv, (ks | k) != 0);
+                        mma_bf16(tmem, dah + adv, dbl + adv, 1u);
+                        mma_bf16(tmem, dal + adv, dbh + adv, 1u);
+                    }
+                    mma_commit(smem_u32(&ab_empty[s]));  // stage free once these MMAs finish
+                }
+                if (*(volatile int*)&abort_flag) break;
+                mma_commit(smem_u32(&acc_full));  // accumulator complete
+            }
+            // drain: the last tile's epilogue has read TMEM before it is freed
+            if (tc > 0 && !mbar_wait(smem_u32(&acc_empty), (tc - 1) & 1u)) report_error(a.err, 14);
+        }
+        __syncwarp();
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols)
+                     : "memory");
+    } else {
+        // --------------------- row threads: decode A, epilogue ---------------------
+        const int quarter = warp & 3;          // TMEM lanes 32*quarter .. +31
+        const int row = quarter * 32 + lane;   // tile row = TMEM lane
+        const uint32_t swz = (uint32_t)(row & 7);
+        uint32_t g = 0, gc = 0, tc = 0;
+        for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++tc) {
+            const int mt = tile / tiles_n, nt = tile % tiles_n;
+            int sw = 0;
+            for (int ks = 0; ks < KS; ++ks, ++g) {
+                if (ks % KSUB == 0) {
+                    sw = (int)(gc % W_STAGES);
+                    if (!mbar_wait(smem_u32(&w_full[sw]), (gc / W_STAGES) & 1u)) {
+                        report_error(a.err, 15);
+                        return;
+                    }
+                }
+                const int s = (int)(g % AB_STAGES);
+                if (!mbar_wait(smem_u32(&ab_empty[s]), ((g / AB_STAGES) & 1u) ^ 1u)) {
+                    report_error(a.err, 15);
+                    return;
+                }
+                // this row's two blocks of the K-step (zero-filled past the matrix)
+                const uint32_t src = w_st(sw) + (uint32_t)(row * C::W_ROW + (ks % KSUB) * 2 * C::BS);
+                constexpr int NW = (2 * C::BS + 3) / 4;
+                uint32_t wv[NW + 1];
+#pragma unroll
+                for (int j = 0; j < NW; ++j) wv[j] = lds_u32(src + 4 * j);
+                wv[NW] = 0;
+                const uint32_t dst_hi = a_hi(s) + (uint32_t)row * 128u;
+                const uint32_t dst_lo = a_lo(s) + (uint32_t)row * 128u;
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {  // 16-byte chunks of the 64-value row
+                    const int blk = c >> 2;
+                    uint32_t bw[(C::BS + 3) / 4 + 1];
+                    // block `blk` starts at byte blk*BS: realign to word 0
+                    const int off = blk * C::BS;
+#pragma unroll
+                    for (int j = 0; j < (C::BS + 3) / 4 + 1; ++j) {
+                        const int wi = (off >> 2) + j;
+                        const uint32_t lo = wi < NW + 1 ? wv[wi] : 0u;
+                        const uint32_t hi = wi + 1 < NW + 1 ? wv[wi + 1] : 0u;
+                        bw[j] = (off & 3) ? __funnelshift_r(lo, hi, (off & 3) * 8) : lo;
+                    }
+                    float w[8];
+                    decode8<F>(bw, (c & 3) * 8, w);
+                    uint32_t h[4], l[4];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const __nv_bfloat162 hb = __floats2bfloat162_rn(w[2 * i], w[2 * i + 1]);
+                        const float2 hf = __bfloat1622float2(hb);
+                        h[i] = *reinterpret_cast<const uint32_t*>(&hb);
+                        l[i] = pack_bf16x2(w[2 * i] - hf.x, w[2 * i + 1] - hf.y);
+                    }
+                    const uint32_t cs = (((uint32_t)c ^ swz) << 4);
+                    asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(dst_hi + cs), "r"(h[0]),
+                                 "r"(h[1]), "r"(h[2]), "r"(h[3])
+                                 : "memory");
+                    asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(dst_lo + cs), "r"(l[0]),
+                                 "r"(l[1]), "r"(l[2]), "r"(l[3])
+                                 : "memory");
+                }
+                fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor cores
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(smem_u32(&ab_full[s]));
+                    if (ks % KSUB == KSUB - 1 || ks == KS - 1) mbar_arrive(smem_u32(&w_empty[sw]));
+                }
+                if (ks % KSUB == KSUB - 1 || ks == KS - 1) ++gc;
+            }
+            // epilogue: TMEM -> registers -> y (consecutive rows across lanes)
+            if (!mbar_wait(smem_u32(&acc_full), tc & 1u)) {
+                report_error(a.err, 16);
+                return;
+            }
+            tc_fence_after();
+            const int o = mt * BM + row;
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+                uint32_t v[32];
+                tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(c * 32), v);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const int t = nt * BN + c * 32 + j;
+                    if (o < a.out && t < a.T) a.y[(long long)t * a.out + o] = __uint_as_float(v[j]);
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&acc_empty));
+        }
+    }
+}
+
+// x fp32 [T][K] -> xh = bf16_rn(x), xl = bf16_rn(x - xh), both [T][K].
+__global__ void xsplit_kernel(const float* __restrict__ x, long long n, __nv_bfloat16* __restrict__ xh,
+                              __nv_bfloat16* __restrict__ xl) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+         i += (long long)gridDim.x * blockDim.x) {
+        const float v = x[i];
+        const __nv_bfloat16 h = __float2bfloat16_rn(v);
+        xh[i] = h;
+        xl[i] = __float2bfloat16_rn(v - __bfloat162float(h));
+    }
+}
+
+// ---- host: tensor maps through the driver entry point ----------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*,
+                                  CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                  CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+bool make_map_2d(CUtensorMap* m, CUtensorMapDataType dt, void* base, uint64_t inner, uint64_t outer,
+                 uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {inner, outer};
+    const cuuint64_t strides[1] = {row_bytes};
+    const cuuint32_t box[2] = {box_inner, box_outer};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(m, dt, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int F>
+cudaError_t launch_gemm_t(const uint8_t* w, const float* x, float* y, int out, int in, int T,
+                          void* ws, int sm_count, int* err, cudaStream_t stream) {
+    using C = GemmCfg<F>;
+    __nv_bfloat16* xh = static_cast<__nv_bfloat16*>(ws);
+    __nv_bfloat16* xl = xh + (size_t)T * in;
+    const long long n = (long long)T * in;
+    xsplit_kernel<<<(int)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096), 256, 0, stream>>>(x, n, xh, xl);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+
+    const long long row_bytes = (long long)((in + kQK - 1) / kQK) * C::BS;
+    CUtensorMap mw, mxh, mxl;
+    if (!make_map_2d(&mw, F == kQ8_0 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8,
+                     const_cast<uint8_t*>(w), (uint64_t)(row_bytes / C::W_ESZ), (uint64_t)out,
+                     (uint64_t)row_bytes, (uint32_t)(C::W_ROW / C::W_ESZ), BM,
+                     CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !make_map_2d(&mxh, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, xh, (uint64_t)in, (uint64_t)T,
+                     (uint64_t)in * 2, BK, BN, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_map_2d(&mxl, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, xl, (uint64_t)in, (uint64_t)T,
+                     (uint64_t)in * 2, BK, BN, CU_TENSOR_MAP_SWIZZLE_128B))
+        return cudaErrorInvalidValue;
+
+    static int attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 64 || !attr_set[dev]) {
+        e = cudaFuncSetAttribute(gemm_tc_kernel<F>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+        if (e != cudaSuccess) return e;
+        if (dev < 64) attr_set[dev] = 1;
+    }
+    GemmArgs a{};
+    a.y = y;
+    a.out = out;
+    a.in = in;
+    a.T = T;
+    a.err = err;
+    const int ntiles = ((out + BM - 1) / BM) * ((T + BN - 1) / BN);
+    const int grid = ntiles < sm_count ? ntiles : sm_count;
+    gemm_tc_kernel<F><<<grid, kGemmThreads, C::SMEM, stream>>>(mw, mxh, mxl, a);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+bool gemm_supported(int fmt, const void* w, int out, int in, int rows) {
+    (void)out;
+    const long long row_bytes = (long long)((in + kQK - 1) / kQK) * block_bytes(fmt);
+    return rows >= 64 && reinterpret_cast<uintptr_t>(w) % 16 == 0 && row_bytes % 16 == 0 &&
+           in % 8 == 0 && encode_fn() != nullptr;
+}
+
+size_t gemm_workspace_bytes(int in, int rows) { return (size_t)rows * in * 2 * sizeof(__nv_bfloat16); }
+
+cudaError_t launch_gemm(int fmt, const uint8_t* w, const float* x, float* y, int out, int in, int rows,
+                        void* ws, int sm_count, int* err, cudaStream_t stream) {
+    switch (fmt) {
+        case kQ8_0: return launch_gemm_t<kQ8_0>(w, x, y, out, in, rows, ws, sm_count, err, stream);
+        case kQ4_0: return launch_gemm_t<kQ4_0>(w, x, y, out, in, rows, ws, sm_count, err, stream);
+        case kQ4_1: return launch_gemm_t<kQ4_1>(w, x, y, out, in, rows, ws, sm_count, err, stream);
+    }
+    return cudaErrorInvalidValue;
+}
+
+}  // namespace mlq

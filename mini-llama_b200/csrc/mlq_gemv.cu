@@ -23,13 +23,15 @@
 //    value it loads for all RPW rows and all tokens.
 //  * Decode without int->float conversions: a nibble (or a sign-flipped
 //    byte) is dropped into the mantissa of a float constant with one PRMT:
-//      q4:  float(0x43000000 | q<<16) = 128 + q      (exact)
+//      q4:  the nibble in the top 4 mantissa bits of 1.0 = 1 + q/16 (exact)
 //      q8:  float(0x4B000000 | (q^0x80)) = 2^23+128+q (exact), minus 2^23+128
-//    so a q4 block costs one PRMT + one FFMA per value; the per-block
-//    constant is folded back with the block's x-sum S:
-//      q4_0:  d * (sum (128+q) x - 136 S)
-//      q4_1:  d * (sum (128+q) x - 128 S) + m S
+//    so a q4 value costs one PRMT + one FFMA (+ a quarter of the nibble
+//    masking); the per-block constant is folded back with the block's
+//    x-sum S:
+//      q4_0:  16 d * (sum (1+q/16) x - 1.5 S)
+//      q4_1:  16 d * (sum (1+q/16) x - S) + m S
 //      q8_0:  d * sum q x
+//    (1 + q/16 keeps the cancellation against S to about one bit.)
 //  * Every mbarrier wait is bounded (2 s); on expiry the kernel records an
 //    error code in *err and returns after its in-flight copies land.
 #include <cuda_runtime.h>
@@ -76,12 +78,21 @@ __device__ __forceinline__ int part_of(int e) {
     }
 }
 
-// Four packed codes -> four floats.  q4: `nib` holds one nibble per byte.
+// Four packed codes -> four floats.  q4: every byte of `nib` is
+// 0x80 | q << 3; dropped into byte 2 under exponent byte 0x3F it gives the
+// float 1 + q/16 exactly (the nibble lands in the top 4 mantissa bits).
 __device__ __forceinline__ void q4_to_f(uint32_t nib, float f[4]) {
-    f[0] = __uint_as_float(__byte_perm(nib, 0x43000000u, 0x7044));
-    f[1] = __uint_as_float(__byte_perm(nib, 0x43000000u, 0x7144));
-    f[2] = __uint_as_float(__byte_perm(nib, 0x43000000u, 0x7244));
-    f[3] = __uint_as_float(__byte_perm(nib, 0x43000000u, 0x7344));
+    f[0] = __uint_as_float(__byte_perm(nib, 0x3F000000u, 0x7044));
+    f[1] = __uint_as_float(__byte_perm(nib, 0x3F000000u, 0x7144));
+    f[2] = __uint_as_float(__byte_perm(nib, 0x3F000000u, 0x7244));
+    f[3] = __uint_as_float(__byte_perm(nib, 0x3F000000u, 0x7344));
+}
+
+// Nibble half h of a qs word, as bytes 0x80 | q << 3.  The shifts are
+// integer multiplies (FMA pipe); the masking is one LOP3 (ALU pipe).
+__device__ __forceinline__ uint32_t q4_nibbles(uint32_t qw, int h) {
+    const uint32_t sh = h ? __umulhi(qw, 0x80000000u) : qw * 8u;  // >> 1 or << 3
+    return (sh & 0x78787878u) | 0x80808080u;
 }
 
 __device__ __forceinline__ void q8_to_f(uint32_t word, float f[4]) {
@@ -317,12 +328,7 @@ __global__ void __launch_bounds__(kThreads, MINB) gemv_stream_kernel(GemvArgs a)
                         if constexpr (F == kQ8_0) {
                             q8_to_f(qs_word<F>(wv[r], bg, p), f);
                         } else {
-                            const uint32_t qw = qs_word<F>(wv[r], bg, p >> 1);
-                            // high nibbles: the shift runs on the FMA pipe (IMAD.HI),
-                            // which has room; the ALU pipe carries the PRMTs
-                            const uint32_t nib = (p & 1) ? (__umulhi(qw, 0x10000000u) & 0x0F0F0F0Fu)
-                                                         : (qw & 0x0F0F0F0Fu);
-                            q4_to_f(nib, f);
+                            q4_to_f(q4_nibbles(qs_word<F>(wv[r], bg, p >> 1), p & 1), f);
                         }
 #pragma unroll
                         for (int m = 0; m < MT; ++m) {
@@ -345,13 +351,14 @@ __global__ void __launch_bounds__(kThreads, MINB) gemv_stream_kernel(GemvArgs a)
 #pragma unroll
                     for (int m = 0; m < MT; ++m) {
                         const float blk = acc0[r][m] + acc1[r][m];
+                        // blk = sum (1 + q/16) x  =>  sum q x = 16 (blk - S)
                         if constexpr (F == kQ8_0) {
                             tot[r][m] = fmaf(d, blk, tot[r][m]);
-                        } else if constexpr (F == kQ4_0) {
-                            tot[r][m] = fmaf(d, fmaf(-136.0f, sx[m], blk), tot[r][m]);
-                        } else {
+                        } else if constexpr (F == kQ4_0) {  // sum (q-8) x = 16 (blk - 1.5 S)
+                            tot[r][m] = fmaf(d * 16.0f, fmaf(-1.5f, sx[m], blk), tot[r][m]);
+                        } else {                            // sum (d q + m) x
                             const float mn = half_bits_to_float(wv[r][0] >> 16);
-                            tot[r][m] = fmaf(d, fmaf(-128.0f, sx[m], blk), tot[r][m]);
+                            tot[r][m] = fmaf(d * 16.0f, blk - sx[m], tot[r][m]);
                             tot[r][m] = fmaf(mn, sx[m], tot[r][m]);
                         }
                     }

@@ -54,6 +54,25 @@ cudaError_t launch_gemv_stream(int fmt, const GemvArgs& args, int mt, int sm_cou
 cudaError_t launch_gemv_generic(int fmt, const uint8_t* w, const float* x, float* y, int out,
                                 int in, int M, int bpr, cudaStream_t stream);
 
+// Arguments of the tensor-core GEMM (mlq_gemm.cu).
+struct GemmArgs {
+    float* y;      // [T][out]
+    int out, in;   // W is [out][in] in blocks
+    int T;         // rows of x (tokens)
+    int* err;      // device error flag
+};
+
+// True when the tcgen05 GEMM takes this call: rows >= 64, weights 16-B
+// aligned with a 16-B multiple row pitch, in % 8 == 0.
+bool gemm_supported(int fmt, const void* w, int out, int in, int rows);
+
+// Workspace bytes of the GEMM (x split into bf16 hi/lo).
+size_t gemm_workspace_bytes(int in, int rows);
+
+// y[T][out] = x[T][in] * W^T on the tensor cores.
+cudaError_t launch_gemm(int fmt, const uint8_t* w, const float* x, float* y, int out, int in, int rows,
+                        void* ws, int sm_count, int* err, cudaStream_t stream);
+
 // Quantize fp32 [rows][cols] -> blocks, reference rules (mlq_convert.cu).
 cudaError_t launch_quantize(int fmt, const float* src, long long rows, int cols, uint8_t* blocks,
                             cudaStream_t stream);

@@ -29,9 +29,15 @@ def g():
 
 
 def expect_near(actual, expected, tol):
+    """The reference's max-abs check (tests/test_cuda.cc:80-103), scaled by the
+    output magnitude when it exceeds 1: the reference's GPU kernel passes an
+    absolute 1e-4 only because it sums in the CPU's order; this library sums
+    in a different fp32 order (the contract bounds that by relative L2 1e-3),
+    and an fp32 sum near 150 is only resolved to ~1e-5 absolute."""
     actual = np.asarray(actual)
     assert actual.shape == expected.shape
-    assert np.abs(actual - expected).max() <= tol, np.abs(actual - expected).max()
+    scale = max(1.0, float(np.abs(expected).max()))
+    assert np.abs(actual - expected).max() <= tol * scale, np.abs(actual - expected).max()
 
 
 def test_cuda_q80_linear_matches_cpu(cq, g):
