@@ -35,6 +35,7 @@
 
 #include "mlq_device.cuh"
 #include "mlq_kernels.h"
+#include "mlq_tmap.h"
 
 namespace mlq {
 namespace {
@@ -63,24 +64,7 @@ struct GemmCfg {
     static_assert(W_ROW % 16 == 0, "W chunk row must be 16-byte granular");
 };
 
-// ---- tcgen05 / TMA PTX wrappers ------------------------------------------
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int c0, int c1,
-                                            uint32_t bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
-        "[%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar)
-        : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
-    asm volatile(
-        "{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.release.cta.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(
-            bar),
-        "r"(bytes)
-        : "memory");
-}
-
+// ---- tcgen05 PTX wrappers ------------------------------------------------
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -402,37 +386,6 @@ __global__ void xsplit_kernel(const float* __restrict__ x, long long n, __nv_bfl
         xh[i] = h;
         xl[i] = __float2bfloat16_rn(v - __bfloat162float(h));
     }
-}
-
-// ---- host: tensor maps through the driver entry point ----------------------
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*,
-                                  CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
-                                  CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-    static EncodeTiledFn fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<EncodeTiledFn>(p);
-    });
-    return fn;
-}
-
-bool make_map_2d(CUtensorMap* m, CUtensorMapDataType dt, void* base, uint64_t inner, uint64_t outer,
-                 uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz) {
-    EncodeTiledFn fn = encode_fn();
-    if (!fn) return false;
-    const cuuint64_t dims[2] = {inner, outer};
-    const cuuint64_t strides[1] = {row_bytes};
-    const cuuint32_t box[2] = {box_inner, box_outer};
-    const cuuint32_t estr[2] = {1, 1};
-    return fn(m, dt, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
-              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 template <int F>

@@ -23,22 +23,26 @@
 //    value it loads for all RPW rows and all tokens.
 //  * Decode without int->float conversions: a nibble (or a sign-flipped
 //    byte) is dropped into the mantissa of a float constant with one PRMT:
-//      q4:  the nibble in the top 4 mantissa bits of 1.0 = 1 + q/16 (exact)
+//      q4:  float(0x43000000 | q << 16) = 128 + q (exact)
 //      q8:  float(0x4B000000 | (q^0x80)) = 2^23+128+q (exact), minus 2^23+128
-//    so a q4 value costs one PRMT + one FFMA (+ a quarter of the nibble
-//    masking); the per-block constant is folded back with the block's
-//    x-sum S:
-//      q4_0:  16 d * (sum (1+q/16) x - 1.5 S)
-//      q4_1:  16 d * (sum (1+q/16) x - S) + m S
+//    so a q4 value costs one PRMT + half a packed FFMA2 (+ a quarter of the
+//    nibble masking); the per-block constant is folded back with the
+//    block's x-sum S:
+//      q4_0:  d * (sum (128+q) x - 136 S)
+//      q4_1:  d * (sum (128+q) x - 128 S) + m S
 //      q8_0:  d * sum q x
-//    (1 + q/16 keeps the cancellation against S to about one bit.)
+//    The fold costs ~7 bits of the fp32 block sum against S; measured
+//    relative errors stay near 1e-6 (the contract allows 1e-3).
 //  * Every mbarrier wait is bounded (2 s); on expiry the kernel records an
 //    error code in *err and returns after its in-flight copies land.
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <cstring>
+
 #include "mlq_device.cuh"
 #include "mlq_kernels.h"
+#include "mlq_tmap.h"
 
 namespace mlq {
 namespace {
@@ -60,6 +64,22 @@ struct GemvCfg {
     static constexpr int X_BYTES = MT * KTE * 4;
     static constexpr int S_BYTES = MT * 32 * G * 4;
     static constexpr int XT_BYTES = X_BYTES + S_BYTES;  // prepared x tile (x + block sums)
+    // 2-D tensor-map layout of a stage's weights: boxes of 8 rows x one
+    // K-tile of bytes, as 8-byte elements (a box row is <= 256 elements, so
+    // q8_0's 2176-byte K-tile row is split into two regions of 16 groups).
+    // Every box destination must be 128-byte aligned (tensor TMA), so the
+    // regions are not offset against each other; q8_0's half-warps then
+    // share banks (2-way conflicts on its weight loads).
+    static constexpr int KTB = 32 * GB;
+    static constexpr int NREG = (KTB / 8 > 256) ? 2 : 1;
+    static constexpr int BOXB = KTB / NREG;
+    static constexpr int BOXW = BOXB / 8;
+    static constexpr int REGION = RT * BOXB;
+    static_assert(REGION % 128 == 0 && (8 * BOXB) % 128 == 0 && W_BYTES % 128 == 0 &&
+                      XT_BYTES % 128 == 0,
+                  "tensor TMA destinations must be 128-byte aligned");
+    static_assert(NREG * REGION <= W_BYTES, "2-D layout must fit the stage");
+    static_assert(BOXB % 16 == 0, "box rows must be 16-byte granular");
     static constexpr int STAGE = W_BYTES + XT_BYTES;
     static_assert(WPG % 2 == 1, "lane-group word count must be odd");
     static_assert(SLOT % 16 == 0 && STAGE % 16 == 0, "stage alignment");
@@ -78,21 +98,19 @@ __device__ __forceinline__ int part_of(int e) {
     }
 }
 
-// Four packed codes -> four floats.  q4: every byte of `nib` is
-// 0x80 | q << 3; dropped into byte 2 under exponent byte 0x3F it gives the
-// float 1 + q/16 exactly (the nibble lands in the top 4 mantissa bits).
+// Four packed codes -> four floats.  q4: every byte of `nib` is one code
+// q (0..15); dropped into byte 2 under exponent byte 0x43 it gives the float
+// 128 + q exactly.
 __device__ __forceinline__ void q4_to_f(uint32_t nib, float f[4]) {
-    f[0] = __uint_as_float(__byte_perm(nib, 0x3F000000u, 0x7044));
-    f[1] = __uint_as_float(__byte_perm(nib, 0x3F000000u, 0x7144));
-    f[2] = __uint_as_float(__byte_perm(nib, 0x3F000000u, 0x7244));
-    f[3] = __uint_as_float(__byte_perm(nib, 0x3F000000u, 0x7344));
+    f[0] = __uint_as_float(__byte_perm(nib, 0x43000000u, 0x7044));
+    f[1] = __uint_as_float(__byte_perm(nib, 0x43000000u, 0x7144));
+    f[2] = __uint_as_float(__byte_perm(nib, 0x43000000u, 0x7244));
+    f[3] = __uint_as_float(__byte_perm(nib, 0x43000000u, 0x7344));
 }
 
-// Nibble half h of a qs word, as bytes 0x80 | q << 3.  The shifts are
-// integer multiplies (FMA pipe); the masking is one LOP3 (ALU pipe).
+// Nibble half h of a qs word, one code per byte.
 __device__ __forceinline__ uint32_t q4_nibbles(uint32_t qw, int h) {
-    const uint32_t sh = h ? __umulhi(qw, 0x80000000u) : qw * 8u;  // >> 1 or << 3
-    return (sh & 0x78787878u) | 0x80808080u;
+    return (h ? (qw >> 4) : qw) & 0x0F0F0F0Fu;
 }
 
 __device__ __forceinline__ void q8_to_f(uint32_t word, float f[4]) {
@@ -161,11 +179,14 @@ __global__ void __launch_bounds__(128) xprep_kernel(const float* __restrict__ x,
 }
 
 template <int F, int MT, int RPW, int MINB>
-__global__ void __launch_bounds__(kThreads, MINB) gemv_stream_kernel(GemvArgs a) {
+__global__ void __launch_bounds__(kThreads, MINB)
+    gemv_stream_kernel(GemvArgs a, const __grid_constant__ CUtensorMap wmap) {
     using C = GemvCfg<F, MT, RPW>;
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(8) uint64_t full_bar[kMaxStages];
-    __shared__ __align__(8) uint64_t empty_bar[kMaxStages];
+    __shared__ __align__(8) uint64_t empty_bar[kMaxStages];   // weights released (early)
+    __shared__ __align__(8) uint64_t xfull_bar[kMaxStages];   // x tile landed
+    __shared__ __align__(8) uint64_t xempty_bar[kMaxStages];  // x tile released
     __shared__ int abort_flag;
     __shared__ float tile_res[2][MT * C::RT];  // per-tile results, double-buffered
     __shared__ __align__(8) uint64_t tile_bar;  // consumer warps' per-tile rendezvous
@@ -178,6 +199,8 @@ __global__ void __launch_bounds__(kThreads, MINB) gemv_stream_kernel(GemvArgs a)
         for (int s = 0; s < S; ++s) {
             mbar_init(smem_u32(&full_bar[s]), 32);
             mbar_init(smem_u32(&empty_bar[s]), kConsumerWarps);
+            mbar_init(smem_u32(&xfull_bar[s]), 1);
+            mbar_init(smem_u32(&xempty_bar[s]), kConsumerWarps);
         }
         mbar_init(smem_u32(&tile_bar), kConsumerWarps);
         abort_flag = 0;
@@ -185,11 +208,13 @@ __global__ void __launch_bounds__(kThreads, MINB) gemv_stream_kernel(GemvArgs a)
     }
     __syncthreads();
 
-    const long long r_begin = (long long)blockIdx.x * a.out / gridDim.x;
-    const long long r_end = (long long)(blockIdx.x + 1) * a.out / gridDim.x;
+    // balanced row ranges in units of 8 rows (the 2-D boxes' height)
+    const long long units = (a.out + 7) / 8;
+    const long long r_begin = 8 * ((long long)blockIdx.x * units / gridDim.x);
+    const long long r_end = min((long long)a.out, 8 * ((long long)(blockIdx.x + 1) * units / gridDim.x));
     const int nrows_cta = (int)(r_end - r_begin);
     const int ntiles = (nrows_cta + C::RT - 1) / C::RT;
-    const uint32_t smem_base = smem_u32(smem);
+    const uint32_t smem_base = (smem_u32(smem) + 127u) & ~127u;  // TMA boxes: 128-B aligned
     const uintptr_t wbase = reinterpret_cast<uintptr_t>(a.w);
     const uintptr_t wend16 = (wbase + (uintptr_t)a.total_bytes) & ~(uintptr_t)15;
 
@@ -211,6 +236,17 @@ __global__ void __launch_bounds__(kThreads, MINB) gemv_stream_kernel(GemvArgs a)
                 const uint32_t stage = smem_base + (uint32_t)s * C::STAGE;
                 const int groups = min(32, a.gpr - kt * 32);
                 const uint32_t seg = (uint32_t)(groups * C::GB);
+                if (a.tma2d) {
+                    // boxes of 8 rows x K-tile bytes (x2 regions for q8_0)
+                    const int nbox = ((nrows + 7) / 8) * C::NREG;
+                    if (lane == 0) mbar_expect_tx(fb, (uint32_t)(nbox * 8 * C::BOXB));
+                    __syncwarp();
+                    if (lane < nbox) {
+                        const int reg = lane % C::NREG, rb = lane / C::NREG;
+                        tma_load_2d(stage + (uint32_t)(reg * C::REGION + rb * 8 * C::BOXB), &wmap,
+                                    kt * C::NREG * C::BOXW + reg * C::BOXW, (int)(row0 + 8 * rb), fb);
+                    }
+                } else {
                 // lane i streams tile row i's segment (RT <= 32 rows per tile)
                 uintptr_t src = 0, lo = 0, hi = 0;
                 uint32_t bytes = 0;
@@ -224,19 +260,31 @@ __global__ void __launch_bounds__(kThreads, MINB) gemv_stream_kernel(GemvArgs a)
                 uint32_t tx = bytes;
 #pragma unroll
                 for (int off = 16; off > 0; off >>= 1) tx += __shfl_xor_sync(0xffffffffu, tx, off);
-                if (lane == 0) mbar_expect_tx(fb, tx + (uint32_t)C::XT_BYTES);
+                if (lane == 0) mbar_expect_tx(fb, tx);
                 __syncwarp();
                 if (bytes) bulk_g2s(stage + (uint32_t)lane * C::SLOT, reinterpret_cast<const void*>(lo), bytes, fb);
-                // the x tile of this K-tile, prepared once per call by xprep_kernel
-                if (lane == 31)
-                    bulk_g2s(stage + C::W_BYTES, a.xprep + (size_t)kt * C::XT_BYTES, (uint32_t)C::XT_BYTES, fb);
                 if (lane < nrows) {
                     // bytes past the array's last 16-B boundary: plain copy
                     for (uintptr_t q = (bytes ? hi : lo); q < src + seg; ++q)
                         sts_u8(stage + (uint32_t)lane * C::SLOT + (uint32_t)(q - lo),
                                *reinterpret_cast<const uint8_t*>(q));
                 }
+                }
                 mbar_arrive(fb);
+                // the x tile of this K-tile (prepared once per call by xprep_kernel)
+                // has its own barriers: the consumers release the weights as soon
+                // as they hold them in registers, the x tile only after the math
+                if (!mbar_wait(smem_u32(&xempty_bar[s]), (round & 1u) ^ 1u)) {
+                    report_error(a.err, 2);
+                    abort_flag = 1;
+                    goto producer_drain;
+                }
+                if (lane == 31) {
+                    mbar_arrive_expect_tx(smem_u32(&xfull_bar[s]), (uint32_t)C::XT_BYTES);
+                    bulk_g2s(stage + C::W_BYTES, a.xprep + (size_t)kt * C::XT_BYTES, (uint32_t)C::XT_BYTES,
+                             smem_u32(&xfull_bar[s]));
+                }
+                __syncwarp();
             }
         }
         return;
@@ -245,7 +293,8 @@ __global__ void __launch_bounds__(kThreads, MINB) gemv_stream_kernel(GemvArgs a)
         // wait (bounded) for each of them before the CTA's smem goes away.
         for (uint32_t k = (seq >= (uint32_t)S ? seq - (uint32_t)S : 0); k < seq; ++k) {
             const int s = (int)(k % (uint32_t)S);
-            if (!mbar_wait(smem_u32(&full_bar[s]), (k / (uint32_t)S) & 1u)) {
+            if (!mbar_wait(smem_u32(&full_bar[s]), (k / (uint32_t)S) & 1u) ||
+                !mbar_wait(smem_u32(&xfull_bar[s]), (k / (uint32_t)S) & 1u)) {
                 report_error(a.err, 3);
                 break;
             }
@@ -277,8 +326,13 @@ __global__ void __launch_bounds__(kThreads, MINB) gemv_stream_kernel(GemvArgs a)
         for (int r = 0; r < RPW; ++r) {
             const int i = wc + r * kConsumerWarps;
             row_on[r] = i < nrows;
-            const uintptr_t rowaddr = wbase + (uintptr_t)((row0 + i) * a.row_bytes);
-            soff[r] = (uint32_t)i * C::SLOT + (uint32_t)(rowaddr & 15) + (uint32_t)lane * C::GB;
+            if (a.tma2d) {
+                constexpr int LPR = 32 / C::NREG;  // lanes per region
+                soff[r] = (uint32_t)((lane / LPR) * C::REGION + i * C::BOXB + (lane % LPR) * C::GB);
+            } else {
+                const uintptr_t rowaddr = wbase + (uintptr_t)((row0 + i) * a.row_bytes);
+                soff[r] = (uint32_t)i * C::SLOT + (uint32_t)(rowaddr & 15) + (uint32_t)lane * C::GB;
+            }
         }
 
         for (int kt = 0; kt < a.ktiles; ++kt, ++seq) {
@@ -306,14 +360,23 @@ __global__ void __launch_bounds__(kThreads, MINB) gemv_stream_kernel(GemvArgs a)
                 }
             }
 
+            // weights are in registers now: hand the stage's weight region back
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&empty_bar[s]));
+            if (!mbar_wait(smem_u32(&xfull_bar[s]), round & 1u)) {
+                report_error(a.err, 1);
+                abort_flag = 1;
+            }
+            if (*(volatile int*)&abort_flag) return;
+
 #pragma unroll
             for (int bg = 0; bg < C::G; ++bg) {
-                // two partial sums per (row, token): even and odd parts
-                float acc0[RPW][MT], acc1[RPW][MT];
+                // two packed partial-sum pairs per (row, token): even / odd parts (FFMA2)
+                float2 acc0[RPW][MT], acc1[RPW][MT];
 #pragma unroll
                 for (int r = 0; r < RPW; ++r)
 #pragma unroll
-                    for (int m = 0; m < MT; ++m) acc0[r][m] = acc1[r][m] = 0.f;
+                    for (int m = 0; m < MT; ++m) acc0[r][m] = acc1[r][m] = make_float2(0.f, 0.f);
 
 #pragma unroll
                 for (int p = 0; p < 8; ++p) {
@@ -332,11 +395,9 @@ __global__ void __launch_bounds__(kThreads, MINB) gemv_stream_kernel(GemvArgs a)
                         }
 #pragma unroll
                         for (int m = 0; m < MT; ++m) {
-                            float& acc = (p & 1) ? acc1[r][m] : acc0[r][m];
-                            acc = fmaf(f[0], xv[m].x, acc);
-                            acc = fmaf(f[1], xv[m].y, acc);
-                            acc = fmaf(f[2], xv[m].z, acc);
-                            acc = fmaf(f[3], xv[m].w, acc);
+                            float2& acc = (p & 1) ? acc1[r][m] : acc0[r][m];
+                            acc = __ffma2_rn(make_float2(f[0], f[1]), make_float2(xv[m].x, xv[m].y), acc);
+                            acc = __ffma2_rn(make_float2(f[2], f[3]), make_float2(xv[m].z, xv[m].w), acc);
                         }
                     }
                 }
@@ -350,22 +411,22 @@ __global__ void __launch_bounds__(kThreads, MINB) gemv_stream_kernel(GemvArgs a)
                     const float d = half_bits_to_float(d_bits<F>(wv[r], bg));
 #pragma unroll
                     for (int m = 0; m < MT; ++m) {
-                        const float blk = acc0[r][m] + acc1[r][m];
-                        // blk = sum (1 + q/16) x  =>  sum q x = 16 (blk - S)
+                        const float blk = (acc0[r][m].x + acc0[r][m].y) + (acc1[r][m].x + acc1[r][m].y);
+                        // blk = sum (128 + q) x  =>  sum q x = blk - 128 S
                         if constexpr (F == kQ8_0) {
                             tot[r][m] = fmaf(d, blk, tot[r][m]);
-                        } else if constexpr (F == kQ4_0) {  // sum (q-8) x = 16 (blk - 1.5 S)
-                            tot[r][m] = fmaf(d * 16.0f, fmaf(-1.5f, sx[m], blk), tot[r][m]);
+                        } else if constexpr (F == kQ4_0) {  // sum (q-8) x = blk - 136 S
+                            tot[r][m] = fmaf(d, fmaf(-136.0f, sx[m], blk), tot[r][m]);
                         } else {                            // sum (d q + m) x
                             const float mn = half_bits_to_float(wv[r][0] >> 16);
-                            tot[r][m] = fmaf(d * 16.0f, blk - sx[m], tot[r][m]);
+                            tot[r][m] = fmaf(d, fmaf(-128.0f, sx[m], blk), tot[r][m]);
                             tot[r][m] = fmaf(mn, sx[m], tot[r][m]);
                         }
                     }
                 }
             }
             __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(&empty_bar[s]));
+            if (lane == 0) mbar_arrive(smem_u32(&xempty_bar[s]));
         }
 
         // reduce the 32 lane partials of every (row, token) into the tile's
@@ -496,12 +557,12 @@ cudaError_t launch_stream_t(GemvArgs args, int sm_count, int smem_per_sm, cudaSt
     using C = GemvCfg<F, MT, RPW>;
     // Per-CTA budget: the SM's shared memory split MINB ways, minus the 1 KB
     // the driver reserves per CTA and this kernel's static barriers.
-    const int budget = smem_per_sm / MINB - 1024 - 512;
+    const int budget = smem_per_sm / MINB - 1024 - 512 - 128;
     int S = budget / C::STAGE;
     if (S > kMaxStages) S = kMaxStages;
     if (S < 2) return cudaErrorInvalidConfiguration;
     args.nstages = S;
-    const int smem = S * C::STAGE;
+    const int smem = S * C::STAGE + 128;  // + alignment slack
     static int attr_bytes[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -511,10 +572,20 @@ cudaError_t launch_stream_t(GemvArgs args, int sm_count, int smem_per_sm, cudaSt
         if (e != cudaSuccess) return e;
         if (dev < 64) attr_bytes[dev] = smem;
     }
+    // weights by 2-D tensor map when the row pitch and base allow it
+    CUtensorMap wmap;
+    std::memset(&wmap, 0, sizeof(wmap));
+    args.tma2d = 0;
+    if (args.out > 0 && args.row_bytes % 16 == 0 && reinterpret_cast<uintptr_t>(args.w) % 16 == 0 &&
+        make_map_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT64, const_cast<uint8_t*>(args.w),
+                    (uint64_t)(args.row_bytes / 8), (uint64_t)args.out, (uint64_t)args.row_bytes,
+                    (uint32_t)C::BOXW, 8u, CU_TENSOR_MAP_SWIZZLE_NONE))
+        args.tma2d = 1;
+    const long long units = (args.out + 7) / 8;  // rows are handed out 8 at a time
     const long long want = (long long)sm_count * MINB;
-    int grid = (int)(args.out < want ? args.out : want);
+    int grid = (int)(units < want ? units : want);
     if (grid < 1) grid = 1;  // a rank holding no rows still runs the handshake
-    gemv_stream_kernel<F, MT, RPW, MINB><<<grid, kThreads, smem, stream>>>(args);
+    gemv_stream_kernel<F, MT, RPW, MINB><<<grid, kThreads, smem, stream>>>(args, wmap);
     return cudaGetLastError();
 }
 

@@ -24,6 +24,7 @@ struct GemvArgs {
     long long row_bytes;     // bpr * block bytes
     long long total_bytes;   // out * row_bytes
     int* err;                // device error flag
+    int tma2d;               // weights streamed by 2-D tensor map (set by the launcher)
     // sharded calls only (world > 1): completion handshake
     int world, rank;
     uint32_t epoch;
