@@ -38,7 +38,7 @@ constexpr int kMaxDevices = 64;
 constexpr int kFlagBytes = 256;  // per-rank flag buffer of the sharded calls
 constexpr int kDoneWord = 32;    // its CTA completion counter (own 128-B line)
 
-// Device workspace of one stream (the prepared x of the streaming GEMV).
+// Device workspace of one stream (the bf16 hi/lo split of x for the GEMM).
 struct Workspace {
     void* ptr = nullptr;
     size_t cap = 0;
@@ -178,17 +178,6 @@ mlq_status run_stream(int fmt, const void* w, int out, int in, const float* x, i
         a.local_flags = g.flags[g.rank];
         a.done_counter = reinterpret_cast<unsigned int*>(g.flags[g.rank] + kDoneWord);
     }
-    // one prepared-x region per pass, so no pass overwrites another's input
-    size_t ws_total = 0;
-    for (int m0 = 0; m0 < rows;) {
-        const int mt = mlq::gemv_tokens_per_pass(rows - m0);
-        ws_total += mlq::gemv_xprep_bytes(fmt, mt, a.ktiles);
-        m0 += rows - m0 < mt ? rows - m0 : mt;
-    }
-    void* ws = nullptr;
-    st = stream_workspace(ds, stream, ws_total, &ws);
-    if (st != MLQ_OK) return st;
-    uint8_t* wsp = static_cast<uint8_t*>(ws);
     for (int m0 = 0; m0 < rows;) {
         const int mt = mlq::gemv_tokens_per_pass(rows - m0);
         a.x = x + (long long)m0 * in;
@@ -197,12 +186,8 @@ mlq_status run_stream(int fmt, const void* w, int out, int in, const float* x, i
         // only the last pass runs the cross-rank handshake: it is stream-ordered
         // after the earlier passes' stores
         a.world = (m0 + a.M >= rows) ? g.world : 1;
-        a.xprep = wsp;
-        e = mlq::launch_gemv_xprep(fmt, a.x, in, a.M, mt, a.ktiles, wsp, stream);
-        if (e != cudaSuccess) return fail_cuda("gemv x-prep launch", e);
         e = mlq::launch_gemv_stream(fmt, a, mt, ds->sm_count, ds->smem_per_sm, stream);
         if (e != cudaSuccess) return fail_cuda("gemv_stream launch", e);
-        wsp += mlq::gemv_xprep_bytes(fmt, mt, a.ktiles);
         m0 += a.M;
     }
     return MLQ_OK;

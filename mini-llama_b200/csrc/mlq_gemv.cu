@@ -10,13 +10,13 @@
 //    [blockIdx*out/grid, (blockIdx+1)*out/grid) and walks it in row tiles of
 //    RT = 8 warps x RPW rows, each tile over the full K extent in K-tiles of
 //    32 lane-groups (2048 values for q8_0/q4_0, 1024 for q4_1).
-//  * Warp 0 is the producer.  Lane i streams tile row i's K-tile segment
-//    (a contiguous byte run of the AoS block array) into a shared-memory
-//    stage with one cp.async.bulk; the 32 lanes then load the
-//    matching x K-tile with coalesced 128-bit loads, compute per-block sums
-//    of x, and store x into the stage in the lane-major, XOR-swizzled order
-//    the consumers read.  An mbarrier per stage counts the bulk bytes and
-//    the 32 producer arrivals; a second one returns the stage.
+//  * Warp 0 streams the weights: a stage is RT rows x one K-tile, fetched
+//    as 2-D tensor-map boxes of 8 rows (or, when the row pitch is not a
+//    multiple of 16 B, one 1-D cp.async.bulk per row segment).  Warp 9
+//    builds the stage's x tile: coalesced 128-bit loads, per-block sums,
+//    stored lane-major with an XOR swizzle in the order the consumers read.
+//    Weights and x have separate full/empty mbarriers, so the consumers can
+//    hand the weight region back as soon as they hold it in registers.
 //  * Warps 1..8 consume: lane l decodes lane-group l (2 blocks = 9 or 17
 //    words, or 1 q4_1 block = 5 words; odd word counts make the 32 lanes'
 //    32-bit shared loads bank-conflict free) of RPW rows, reusing every x
@@ -48,7 +48,8 @@ namespace mlq {
 namespace {
 
 constexpr int kConsumerWarps = 8;
-constexpr int kThreads = 32 * (1 + kConsumerWarps);
+constexpr int kXWarp = 1 + kConsumerWarps;  // warp 9 builds the x tiles
+constexpr int kThreads = 32 * (2 + kConsumerWarps);
 constexpr int kMaxStages = 8;
 
 template <int F, int MT, int RPW>
@@ -63,7 +64,7 @@ struct GemvCfg {
     static constexpr int W_BYTES = RT * SLOT;
     static constexpr int X_BYTES = MT * KTE * 4;
     static constexpr int S_BYTES = MT * 32 * G * 4;
-    static constexpr int XT_BYTES = X_BYTES + S_BYTES;  // prepared x tile (x + block sums)
+    static constexpr int XT_BYTES = X_BYTES + S_BYTES;  // x tile (x + block sums) of a stage
     // 2-D tensor-map layout of a stage's weights: boxes of 8 rows x one
     // K-tile of bytes, as 8-byte elements (a box row is <= 256 elements, so
     // q8_0's 2176-byte K-tile row is split into two regions of 16 groups).
@@ -141,41 +142,6 @@ __device__ __forceinline__ uint32_t d_bits(const uint32_t* wv, int bg) {
     if constexpr (F == kQ4_1) return wv[0] & 0xFFFFu;
     if constexpr (F == kQ4_0) return bg == 0 ? (wv[0] & 0xFFFFu) : (wv[4] >> 16);
     return bg == 0 ? (wv[0] & 0xFFFFu) : (wv[8] >> 16);
-}
-
-// ---------------------------------------------------------------------------
-// x preparation, once per call: x[M][in] -> per K-tile blocks of
-//   [m][part row = bg*8 + p][lane-group g ^ p] float4   (the consumers' order)
-//   [m][block] float                                    (x sum of each block)
-// zero-padded past `in` and for tokens m >= M.  One CTA per (K-tile, token).
-// ---------------------------------------------------------------------------
-template <int F, int MT>
-__global__ void __launch_bounds__(128) xprep_kernel(const float* __restrict__ x, int in, int M,
-                                                    uint8_t* __restrict__ out) {
-    constexpr int G = Fmt<F>::kGroupBlocks;
-    constexpr int KTE = 32 * G * kQK;
-    constexpr int X_BYTES = MT * KTE * 4;
-    constexpr int XT_BYTES = X_BYTES + MT * 32 * G * 4;
-    const int kt = blockIdx.x / MT;
-    const int m = blockIdx.x % MT;
-    float4* xs = reinterpret_cast<float4*>(out + (size_t)kt * XT_BYTES) + (size_t)m * (KTE / 4);
-    float* ss = reinterpret_cast<float*>(out + (size_t)kt * XT_BYTES + X_BYTES) + m * 32 * G;
-    const long long k0 = (long long)kt * KTE;
-    for (int q = threadIdx.x; q < KTE / 4; q += blockDim.x) {
-        const int e4 = q * 4;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (m < M && k0 + e4 < in) v = *reinterpret_cast<const float4*>(x + (long long)m * in + k0 + e4);
-        float sum = (v.x + v.y) + (v.z + v.w);
-        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-        sum += __shfl_xor_sync(0xffffffffu, sum, 4);
-        const int blk = e4 >> 5;
-        const int g = blk / G;
-        const int bg = blk % G;
-        const int p = part_of<F>(e4 & 31);
-        xs[(bg * 8 + p) * 32 + (g ^ p)] = v;
-        if ((q & 7) == 0) ss[blk] = sum;
-    }
 }
 
 template <int F, int MT, int RPW, int MINB>
@@ -271,19 +237,6 @@ __global__ void __launch_bounds__(kThreads, MINB)
                 }
                 }
                 mbar_arrive(fb);
-                // the x tile of this K-tile (prepared once per call by xprep_kernel)
-                // has its own barriers: the consumers release the weights as soon
-                // as they hold them in registers, the x tile only after the math
-                if (!mbar_wait(smem_u32(&xempty_bar[s]), (round & 1u) ^ 1u)) {
-                    report_error(a.err, 2);
-                    abort_flag = 1;
-                    goto producer_drain;
-                }
-                if (lane == 31) {
-                    mbar_arrive_expect_tx(smem_u32(&xfull_bar[s]), (uint32_t)C::XT_BYTES);
-                    bulk_g2s(stage + C::W_BYTES, a.xprep + (size_t)kt * C::XT_BYTES, (uint32_t)C::XT_BYTES,
-                             smem_u32(&xfull_bar[s]));
-                }
                 __syncwarp();
             }
         }
@@ -293,10 +246,61 @@ __global__ void __launch_bounds__(kThreads, MINB)
         // wait (bounded) for each of them before the CTA's smem goes away.
         for (uint32_t k = (seq >= (uint32_t)S ? seq - (uint32_t)S : 0); k < seq; ++k) {
             const int s = (int)(k % (uint32_t)S);
-            if (!mbar_wait(smem_u32(&full_bar[s]), (k / (uint32_t)S) & 1u) ||
-                !mbar_wait(smem_u32(&xfull_bar[s]), (k / (uint32_t)S) & 1u)) {
+            if (!mbar_wait(smem_u32(&full_bar[s]), (k / (uint32_t)S) & 1u)) {
                 report_error(a.err, 3);
                 break;
+            }
+        }
+        return;
+    }
+
+    if (warp == kXWarp) {
+        // ------------------------------ x loader ------------------------------
+        // Per stage: the K-tile of x for MT tokens with coalesced 128-bit loads
+        // (all in flight together), per-block sums by shuffles, stored
+        // lane-major with an XOR swizzle -- the order the consumers read.
+        // Runs up to S stages ahead, off the weight producer's path.
+        uint32_t seq = 0;
+        constexpr int NV = C::KTE / 128;  // float4 loads per lane per token
+        for (int t = 0; t < ntiles; ++t) {
+            for (int kt = 0; kt < a.ktiles; ++kt, ++seq) {
+                const int s = (int)(seq % (uint32_t)S);
+                const uint32_t round = seq / (uint32_t)S;
+                if (!mbar_wait(smem_u32(&xempty_bar[s]), (round & 1u) ^ 1u)) {
+                    report_error(a.err, 6);
+                    abort_flag = 1;
+                }
+                if (*(volatile int*)&abort_flag) return;
+                const uint32_t xs = smem_base + (uint32_t)s * C::STAGE + C::W_BYTES;
+                const uint32_t ss = xs + C::X_BYTES;
+                const long long k0 = (long long)kt * C::KTE;
+#pragma unroll 1
+                for (int m = 0; m < MT; ++m) {
+                    const float* xr = a.x + (long long)m * a.in;
+                    float4 v[NV];
+#pragma unroll
+                    for (int i = 0; i < NV; ++i) {
+                        const int e4 = (i * 32 + lane) * 4;
+                        v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+                        if (m < a.M && k0 + e4 < a.in) v[i] = ldg_nc_f4(xr + k0 + e4);
+                    }
+#pragma unroll
+                    for (int i = 0; i < NV; ++i) {
+                        const int e4 = (i * 32 + lane) * 4;
+                        float sum = (v[i].x + v[i].y) + (v[i].z + v[i].w);
+                        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+                        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+                        sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+                        const int blk = e4 >> 5;
+                        const int g = blk / C::G;
+                        const int bg = blk % C::G;
+                        const int p = part_of<F>(e4 & 31);
+                        sts_f4(xs + (uint32_t)(((m * C::G * 8 + bg * 8 + p) * 32 + (g ^ p)) * 16), v[i]);
+                        if ((lane & 7) == 0) sts_f32(ss + (uint32_t)((m * 32 * C::G + blk) * 4), sum);
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(&xfull_bar[s]));
             }
         }
         return;
@@ -605,40 +609,10 @@ cudaError_t dispatch_mt(const GemvArgs& args, int sm_count, int smem_per_sm, cud
     return launch_stream_t<F, MT, RPW, MINB>(args, sm_count, smem_per_sm, stream);
 }
 
-template <int F, int MT>
-cudaError_t prep_t(const float* x, int in, int M, int ktiles, uint8_t* out, cudaStream_t stream) {
-    xprep_kernel<F, MT><<<ktiles * MT, 128, 0, stream>>>(x, in, M, out);
-    return cudaGetLastError();
-}
-
 }  // namespace
 
 int gemv_tokens_per_pass(int rows_left) {
     return rows_left >= 5 ? 8 : (rows_left >= 3 ? 4 : (rows_left == 2 ? 2 : 1));
-}
-
-size_t gemv_xprep_bytes(int fmt, int mt, int ktiles) {
-    const int G = fmt == kQ4_1 ? 1 : 2;
-    const size_t kte = 32 * G * kQK;
-    return (size_t)ktiles * mt * (kte * 4 + 32 * G * 4);
-}
-
-cudaError_t launch_gemv_xprep(int fmt, const float* x, int in, int M, int mt, int ktiles,
-                              uint8_t* out, cudaStream_t stream) {
-#define MLQ_PREP(F)                                                             \
-    switch (mt) {                                                               \
-        case 1: return prep_t<F, 1>(x, in, M, ktiles, out, stream);             \
-        case 2: return prep_t<F, 2>(x, in, M, ktiles, out, stream);             \
-        case 4: return prep_t<F, 4>(x, in, M, ktiles, out, stream);             \
-        default: return prep_t<F, 8>(x, in, M, ktiles, out, stream);            \
-    }
-    switch (fmt) {
-        case kQ8_0: MLQ_PREP(kQ8_0)
-        case kQ4_0: MLQ_PREP(kQ4_0)
-        case kQ4_1: MLQ_PREP(kQ4_1)
-    }
-#undef MLQ_PREP
-    return cudaErrorInvalidValue;
 }
 
 cudaError_t launch_gemv_stream(int fmt, const GemvArgs& args, int mt, int sm_count, int smem_per_sm,

@@ -11,7 +11,6 @@ namespace mlq {
 struct GemvArgs {
     const uint8_t* w;        // packed blocks, row-major [out][bpr]
     const float* x;          // [M][in]
-    const uint8_t* xprep;    // x prepared by launch_gemv_xprep (16-B aligned)
     float* ys[8];            // output copies: [0] = this GPU's y, then peers' y
     int ny;                  // number of valid ys
     int row_offset;          // global index of this launch's row 0 (row shard start)
@@ -38,16 +37,9 @@ constexpr int kMaxWorld = 8;
 // Tokens per pass for `rows_left` remaining rows of x: 1, 2, 4 or 8.
 int gemv_tokens_per_pass(int rows_left);
 
-// Bytes of the prepared-x workspace of one pass (tokens-per-pass `mt`).
-size_t gemv_xprep_bytes(int fmt, int mt, int ktiles);
-
-// x[M][in] -> the streaming kernel's x tiles (lane-major, swizzled) + block sums.
-cudaError_t launch_gemv_xprep(int fmt, const float* x, int in, int M, int mt, int ktiles,
-                              uint8_t* out, cudaStream_t stream);
-
 // Streaming GEMV, tokens-per-pass `mt` in {1,2,4,8}; persistent grid of one
 // or two CTAs per SM (`sm_count` SMs with `smem_per_sm` bytes of shared
-// memory each); args.xprep must hold this pass's prepared x.
+// memory each).  Needs no workspace.
 cudaError_t launch_gemv_stream(int fmt, const GemvArgs& args, int mt, int sm_count,
                                int smem_per_sm, cudaStream_t stream);
 
