@@ -149,6 +149,18 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
         : "memory");
 }
 
+// Programmatic dependent launch.  A kernel launched with programmatic
+// stream serialization may start before its predecessor in the stream has
+// finished; grid_dependency_wait() blocks the calling thread until the
+// predecessor has completed and its memory is visible.  launch_dependents()
+// lets the next kernel in the stream be scheduled early.
+__device__ __forceinline__ void grid_dependency_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Read-only, L1-bypassing 128-bit global load (x tiles: each CTA touches
 // them once per stage, the L2 keeps them for the other CTAs).
 __device__ __forceinline__ float4 ldg_nc_f4(const float* p) {

@@ -173,6 +173,8 @@ __global__ void __launch_bounds__(kThreads, MINB)
         fence_mbar_init();
     }
     __syncthreads();
+    // The next kernel in the stream may come up on SMs this grid frees.
+    launch_dependents();
 
     // balanced row ranges in units of 8 rows (the 2-D boxes' height)
     const long long units = (a.out + 7) / 8;
@@ -262,6 +264,9 @@ __global__ void __launch_bounds__(kThreads, MINB)
         // Runs up to S stages ahead, off the weight producer's path.
         uint32_t seq = 0;
         constexpr int NV = C::KTE / 128;  // float4 loads per lane per token
+        // x may be the previous kernel's output: wait for it (weights are
+        // read-only, so warp 0 started streaming them without waiting)
+        grid_dependency_wait();
         for (int t = 0; t < ntiles; ++t) {
             for (int kt = 0; kt < a.ktiles; ++kt, ++seq) {
                 const int s = (int)(seq % (uint32_t)S);
@@ -307,6 +312,8 @@ __global__ void __launch_bounds__(kThreads, MINB)
     }
 
     // -------------------------------- consumers --------------------------------
+    // y (and the peers' y) may still be read by the previous kernel
+    grid_dependency_wait();
     const int wc = warp - 1;
     // byte offset of this lane's float4 in x-tile part row p: (lane ^ p) * 16
     uint32_t xoff[8];
@@ -589,8 +596,17 @@ cudaError_t launch_stream_t(GemvArgs args, int sm_count, int smem_per_sm, cudaSt
     const long long want = (long long)sm_count * MINB;
     int grid = (int)(units < want ? units : want);
     if (grid < 1) grid = 1;  // a rank holding no rows still runs the handshake
-    gemv_stream_kernel<F, MT, RPW, MINB><<<grid, kThreads, smem, stream>>>(args, wmap);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = (size_t)smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, gemv_stream_kernel<F, MT, RPW, MINB>, args, wmap);
 }
 
 // rows-per-warp choice per format: keeps the lane-group words of all RPW
