@@ -102,6 +102,33 @@ MLQ_API mlq_status mlq_linear(mlq_format fmt, const void* w, size_t block_count,
                               int out_features, int in_features, const float* x, int rows,
                               float* y, mlq_stream stream);
 
+/* mlq_linear that never allocates device memory.  No counterpart in the
+ * reference (its GPU linear cudaMallocs its output on every call,
+ * src/cuda_quant.cu:333-361).
+ *
+ * Meant for callers that must not allocate: a serving loop that reserved
+ * the whole device up front (weights + KV cache) and treats any later
+ * cudaMalloc as an out-of-memory risk, or a latency-critical loop that
+ * cannot afford cudaFree's device-wide synchronisation (mlq_linear grows
+ * its per-stream workspace by free + malloc when a larger shape arrives).
+ *
+ * Same arguments, results and validation as mlq_linear.  The tensor-core
+ * path (rows >= 64) keeps the bf16 hi/lo split of x in a static
+ * MLQ_NOALLOC_SCRATCH_BYTES array of the library's device module instead of
+ * a workspace; so rows >= 64 with rows * in_features * 4 bytes above that
+ * size returns MLQ_ERR_RANGE before any CUDA call.  The array is one per
+ * device, shared by every call: calls ordered on one stream are fine,
+ * calls whose kernels may overlap (several streams, several host threads)
+ * race on it.  Nothing in it needs to start zeroed.  The first call on a
+ * device does one-time setup (attribute queries, the scratch's address via
+ * cudaGetSymbolAddress, kernel shared-memory attributes); make that first
+ * call before any stream capture. */
+#define MLQ_NOALLOC_SCRATCH_BYTES (16u << 20)
+
+MLQ_API mlq_status mlq_linear_noalloc(mlq_format fmt, const void* w, size_t block_count,
+                                      int out_features, int in_features, const float* x, int rows,
+                                      float* y, mlq_stream stream);
+
 /* Device weight, HOST x, HOST y, optional HOST bias[out] added to every row
  * after the product.  Replaces cudaQ80LinearDeviceWeight /
  * cudaQ40LinearDeviceWeight / cudaQ41LinearDeviceWeight

@@ -20,6 +20,17 @@
 // Device-side error flag, one per device context (see mlq_device_error).
 __device__ int g_mlq_device_error = 0;
 
+// Scratch of mlq_linear_noalloc: the bf16 hi/lo split of x that its
+// tensor-core GEMM calls read.  It lives in the module's own device memory
+// (one copy per device context, created when the module loads), so that
+// entry point never calls cudaMalloc/cudaFree.  Every call on a device uses
+// this one array: a GEMM call rewrites the part it reads before reading it,
+// so nothing in it has to start at zero, but two such calls whose kernels
+// overlap in time (different streams, or host threads without stream order
+// between them) race on it.
+static_assert(MLQ_NOALLOC_SCRATCH_BYTES % 256 == 0, "scratch size");
+static __device__ __align__(256) unsigned char g_mlq_noalloc_scratch[MLQ_NOALLOC_SCRATCH_BYTES];
+
 namespace {
 
 thread_local std::string t_last_error;
@@ -222,6 +233,38 @@ mlq_status run_linear(int fmt, const void* w, int out, int in, const float* x, i
     return run_stream(fmt, w, out, in, x, rows, g, stream);
 }
 
+// Device address of g_mlq_noalloc_scratch, looked up once per device (with
+// that device current) and kept.
+struct ScratchSlot {
+    std::once_flag once;
+    cudaError_t err = cudaSuccess;
+    void* ptr = nullptr;
+};
+
+ScratchSlot g_scratch[kMaxDevices];
+
+// mlq_linear without any device allocation.  The GEMV kernels need no
+// scratch, so every call they take goes through run_linear unchanged; only
+// the tensor-core GEMM differs, reading its x split from the static array
+// instead of the per-stream workspace.
+mlq_status run_linear_noalloc(int fmt, const void* w, int out, int in, const float* x, int rows,
+                              float* y, cudaStream_t stream) {
+    if (!mlq::gemm_supported(fmt, w, out, in, rows)) return run_linear(fmt, w, out, in, x, rows, y, stream);
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return fail_cuda("cudaGetDevice", e);
+    mlq_status st = MLQ_OK;
+    DeviceState* ds = device_state(dev, &st);
+    if (!ds) return st;
+    ScratchSlot& s = g_scratch[dev];
+    std::call_once(s.once, [&] { s.err = cudaGetSymbolAddress(&s.ptr, g_mlq_noalloc_scratch); });
+    if (s.err != cudaSuccess || s.ptr == nullptr)
+        return fail_cuda("cudaGetSymbolAddress (static scratch)", s.err != cudaSuccess ? s.err : cudaErrorInvalidSymbol);
+    e = mlq::launch_gemm(fmt, static_cast<const uint8_t*>(w), x, y, out, in, rows, s.ptr, ds->sm_count,
+                         ds->err_flag, stream);
+    return e == cudaSuccess ? MLQ_OK : fail_cuda("gemm launch", e);
+}
+
 // Grows a per-device staging buffer (called under host_mu, device current).
 mlq_status ensure(float** buf, size_t* cap, size_t bytes) {
     if (*cap >= bytes) return MLQ_OK;
@@ -312,6 +355,27 @@ MLQ_API mlq_status mlq_linear(mlq_format fmt, const void* w, size_t block_count,
                           reinterpret_cast<cudaStream_t>(stream));
     } catch (...) {
         return fail(MLQ_ERR_CUDA, "mlq_linear: host exception");
+    }
+}
+
+MLQ_API mlq_status mlq_linear_noalloc(mlq_format fmt, const void* w, size_t block_count,
+                                      int out_features, int in_features, const float* x, int rows,
+                                      float* y, mlq_stream stream) {
+    try {
+        mlq_status st = validate_linear(fmt, w, block_count, out_features, in_features, x, rows, y,
+                                        "mlq_linear_noalloc");
+        if (st != MLQ_OK) return st;
+        const size_t need = mlq::gemm_workspace_bytes(in_features, rows);
+        if (rows >= 64 && need > (size_t)MLQ_NOALLOC_SCRATCH_BYTES)
+            return fail(MLQ_ERR_RANGE,
+                        "mlq_linear_noalloc: rows * in_features * 4 = " + std::to_string(need) +
+                            " bytes of x split exceed the " +
+                            std::to_string((size_t)MLQ_NOALLOC_SCRATCH_BYTES) +
+                            "-byte static scratch (use mlq_linear, or fewer rows per call)");
+        return run_linear_noalloc(fmt, w, out_features, in_features, x, rows, y,
+                                  reinterpret_cast<cudaStream_t>(stream));
+    } catch (...) {
+        return fail(MLQ_ERR_CUDA, "mlq_linear_noalloc: host exception");
     }
 }
 

@@ -55,6 +55,7 @@ def lib() -> ctypes.CDLL:
         L.mlq_last_error.restype = ctypes.c_char_p
         L.mlq_device_error.argtypes = [_i, ctypes.POINTER(_i)]
         L.mlq_linear.argtypes = [_i, _vp, _sz, _i, _i, _vp, _i, _vp, _vp]
+        L.mlq_linear_noalloc.argtypes = [_i, _vp, _sz, _i, _i, _vp, _i, _vp, _vp]
         L.mlq_linear_host.argtypes = [_i, _vp, _sz, _i, _i, _vp, _i, _vp, _vp, _i, _vp]
         L.mlq_linear_host_weight.argtypes = [_i, _vp, _sz, _i, _i, _vp, _i, _vp, _vp, _i]
         L.mlq_dequantize.argtypes = [_i, _vp, _sz, _i, _i, _vp, _vp]
@@ -66,9 +67,10 @@ def lib() -> ctypes.CDLL:
         L.mlq_peer_open.argtypes = [ctypes.c_char_p, ctypes.POINTER(_vp)]
         L.mlq_peer_close.argtypes = [_vp]
         L.mlq_peer_free.argtypes = [_vp]
-        for name in ("mlq_linear", "mlq_linear_host", "mlq_linear_host_weight", "mlq_dequantize",
-                     "mlq_quantize", "mlq_device_error", "mlq_linear_allgather", "mlq_peer_alloc",
-                     "mlq_peer_open", "mlq_peer_close", "mlq_peer_free"):
+        for name in ("mlq_linear", "mlq_linear_noalloc", "mlq_linear_host",
+                     "mlq_linear_host_weight", "mlq_dequantize", "mlq_quantize", "mlq_device_error",
+                     "mlq_linear_allgather", "mlq_peer_alloc", "mlq_peer_open", "mlq_peer_close",
+                     "mlq_peer_free"):
             getattr(L, name).restype = _i
         _lib = L
     return _lib
@@ -134,6 +136,21 @@ def linear_raw(fmt, w_ptr: int, nblocks: int, out_features: int, in_features: in
     """Pointer-level call (for CUDA-graph capture and timing loops)."""
     check(lib().mlq_linear(fmt_id(fmt), w_ptr, nblocks, out_features, in_features, x_ptr, rows,
                            y_ptr, stream))
+
+
+# MLQ_NOALLOC_SCRATCH_BYTES of include/mlq.h
+NOALLOC_SCRATCH_BYTES = 16 << 20
+
+
+def linear_noalloc(fmt, w, out_features: int, in_features: int, x, y, stream=None):
+    """mlq_linear_noalloc: like linear() but the library allocates no device
+    memory (the caller passes y; rows >= 64 need rows * in * 4 bytes <=
+    NOALLOC_SCRATCH_BYTES)."""
+    rows = 1 if x.dim() == 1 else x.shape[0]
+    nb = w.numel() // BLOCK_BYTES[_fmt_name(fmt)]
+    check(lib().mlq_linear_noalloc(fmt_id(fmt), w.data_ptr(), nb, out_features, in_features,
+                                   x.data_ptr(), rows, y.data_ptr(), _stream_handle(stream)))
+    return y
 
 
 def linear_host(fmt, w, out_features: int, in_features: int, x: np.ndarray, bias=None,
