@@ -312,7 +312,7 @@ def run_mlq(args):
                            sh_stream)
             calls.append(call)
             ybufs.append(lambda lin=lin: lin.y_ptr(epoch[0]))
-        launches_per_step += 2  # x-prep + streaming kernel
+        launches_per_step += 1  # one gemv_stream_kernel launch per call (batch 1: one pass)
 
     def step(events=None):
         for j, call in enumerate(calls):

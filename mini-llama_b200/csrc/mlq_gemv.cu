@@ -52,7 +52,7 @@ constexpr int kXWarp = 1 + kConsumerWarps;  // warp 9 builds the x tiles
 constexpr int kThreads = 32 * (2 + kConsumerWarps);
 constexpr int kMaxStages = 8;
 
-template <int F, int MT, int RPW>
+template <int F, int MT, int RPW, bool INT>
 struct GemvCfg {
     static constexpr int G = Fmt<F>::kGroupBlocks;
     static constexpr int BS = Fmt<F>::kBlockBytes;
@@ -62,8 +62,11 @@ struct GemvCfg {
     static constexpr int RT = kConsumerWarps * RPW;
     static constexpr int SLOT = 32 * GB + 16;    // one tile row segment + align slack
     static constexpr int W_BYTES = RT * SLOT;
-    static constexpr int X_BYTES = MT * KTE * 4;
-    static constexpr int S_BYTES = MT * 32 * G * 4;
+    // x tile of a K-tile: fp32 values (FP mode) or three int8 slices per
+    // value, as 6 rows of 32 lanes x 16 B per block of a lane-group (INT mode)
+    static constexpr int X_BYTES = INT ? MT * G * 6 * 512 : MT * KTE * 4;
+    // per block: x sum (FP mode) or (slice scale, x sum) (INT mode)
+    static constexpr int S_BYTES = MT * 32 * G * (INT ? 8 : 4);
     static constexpr int XT_BYTES = X_BYTES + S_BYTES;  // x tile (x + block sums) of a stage
     // 2-D tensor-map layout of a stage's weights: boxes of 8 rows x one
     // K-tile of bytes, as 8-byte elements (a box row is <= 256 elements, so
@@ -84,6 +87,7 @@ struct GemvCfg {
     static constexpr int STAGE = W_BYTES + XT_BYTES;
     static_assert(WPG % 2 == 1, "lane-group word count must be odd");
     static_assert(SLOT % 16 == 0 && STAGE % 16 == 0, "stage alignment");
+    static_assert(!INT || MT == 1, "integer mode is the one-token path");
 };
 
 // x-tile row ("part") p of block bg holds 4 consecutive x values; the 8
@@ -144,10 +148,40 @@ __device__ __forceinline__ uint32_t d_bits(const uint32_t* wv, int bg) {
     return bg == 0 ? (wv[0] & 0xFFFFu) : (wv[8] >> 16);
 }
 
-template <int F, int MT, int RPW, int MINB>
+// --- integer mode -----------------------------------------------------------
+// One token: x is carried as three int8 slices per value, relative to its
+// 32-value block's scale s = max|x| / 127:
+//     x / s = h + m / 254 + l / 254^2 + e,   h, m, l in [-127, 127], |e| <= 1/(2*254^2)
+// i.e. 24-bit block fixed point, |x - s (h + m/254 + l/254^2)| <= 6.1e-8 max|x| --
+// the size of one fp32 rounding of the block's largest value.  The codes
+// (q4: 0..15, q8: -128..127) then meet the slices in DP4A: four 8-bit
+// products summed exactly per instruction, one int32 sum per slice, block
+// and row.  The fold per block:
+//     sum q x = s * (H + (254 M + L) / 254^2)          (H, M, L the slice sums)
+//     q4_0:  d * (that - 8 S),  q4_1:  d * that + m S,  q8_0:  d * that
+// with S the block's x sum.
+constexpr float kRound = 12582912.0f;        // 1.5 * 2^23: x + kRound rounds x to an integer
+constexpr float kInvSlice2 = 1.0f / 64516.0f;  // 1 / 254^2
+
+// Low byte of a kRound-biased float = its integer as a two's-complement byte.
+__device__ __forceinline__ uint32_t pack_low_bytes(float a, float b, float c, float d) {
+    const uint32_t ab = __byte_perm(__float_as_uint(a), __float_as_uint(b), 0x0040);
+    const uint32_t cd = __byte_perm(__float_as_uint(c), __float_as_uint(d), 0x0040);
+    return __byte_perm(ab, cd, 0x5410);
+}
+
+// Column (16-byte unit) of lane-group g's quad q (q = 2*bg + half) in an
+// INT-mode x-tile row: lanes of one 8-lane store phase land in 8 distinct
+// bank groups, and every reader lane of a row in a distinct one.
+template <int G>
+__device__ __forceinline__ uint32_t xcol(int g, int q) {
+    return (uint32_t)((g + (4 / G) * q) & 31) * 16u;
+}
+
+template <int F, int MT, int RPW, int MINB, bool INT>
 __global__ void __launch_bounds__(kThreads, MINB)
     gemv_stream_kernel(GemvArgs a, const __grid_constant__ CUtensorMap wmap) {
-    using C = GemvCfg<F, MT, RPW>;
+    using C = GemvCfg<F, MT, RPW, INT>;
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(8) uint64_t full_bar[kMaxStages];
     __shared__ __align__(8) uint64_t empty_bar[kMaxStages];   // weights released (early)
@@ -160,6 +194,7 @@ __global__ void __launch_bounds__(kThreads, MINB)
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int S = a.nstages;
+    const bool xres = a.x_resident != 0;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
@@ -189,14 +224,14 @@ __global__ void __launch_bounds__(kThreads, MINB)
     if (warp == 0) {
         // ------------------------------ producer ------------------------------
         uint32_t seq = 0;
+        int s = 0;
+        uint32_t ph = 0;
         for (int t = 0; t < ntiles; ++t) {
             const long long row0 = r_begin + (long long)t * C::RT;
             const int nrows = (int)min((long long)C::RT, r_end - row0);
             for (int kt = 0; kt < a.ktiles; ++kt, ++seq) {
-                const int s = (int)(seq % (uint32_t)S);
-                const uint32_t round = seq / (uint32_t)S;
                 const uint32_t fb = smem_u32(&full_bar[s]);
-                if (!mbar_wait(smem_u32(&empty_bar[s]), (round & 1u) ^ 1u)) {
+                if (!mbar_wait(smem_u32(&empty_bar[s]), ph ^ 1u)) {
                     report_error(a.err, 2);
                     abort_flag = 1;
                 }
@@ -240,6 +275,10 @@ __global__ void __launch_bounds__(kThreads, MINB)
                 }
                 mbar_arrive(fb);
                 __syncwarp();
+                if (++s == S) {
+                    s = 0;
+                    ph ^= 1u;
+                }
             }
         }
         return;
@@ -247,8 +286,8 @@ __global__ void __launch_bounds__(kThreads, MINB)
         // Abort: the stages already issued may still have copies in flight;
         // wait (bounded) for each of them before the CTA's smem goes away.
         for (uint32_t k = (seq >= (uint32_t)S ? seq - (uint32_t)S : 0); k < seq; ++k) {
-            const int s = (int)(k % (uint32_t)S);
-            if (!mbar_wait(smem_u32(&full_bar[s]), (k / (uint32_t)S) & 1u)) {
+            const int ks = (int)(k % (uint32_t)S);
+            if (!mbar_wait(smem_u32(&full_bar[ks]), (k / (uint32_t)S) & 1u)) {
                 report_error(a.err, 3);
                 break;
             }
@@ -258,54 +297,119 @@ __global__ void __launch_bounds__(kThreads, MINB)
 
     if (warp == kXWarp) {
         // ------------------------------ x loader ------------------------------
-        // Per stage: the K-tile of x for MT tokens with coalesced 128-bit loads
-        // (all in flight together), per-block sums by shuffles, stored
-        // lane-major with an XOR swizzle -- the order the consumers read.
-        // Runs up to S stages ahead, off the weight producer's path.
-        uint32_t seq = 0;
-        constexpr int NV = C::KTE / 128;  // float4 loads per lane per token
+        // Per K-tile: x for MT tokens with coalesced 128-bit loads (all in
+        // flight together), per-block sums by shuffles, stored in the order
+        // the consumers read.  Resident mode (every K-tile has its own slot):
+        // each x tile is built once and kept for all row tiles; otherwise the
+        // tiles ride the stage ring, up to S stages ahead of the consumers.
         // x may be the previous kernel's output: wait for it (weights are
         // read-only, so warp 0 started streaming them without waiting)
         grid_dependency_wait();
-        for (int t = 0; t < ntiles; ++t) {
-            for (int kt = 0; kt < a.ktiles; ++kt, ++seq) {
-                const int s = (int)(seq % (uint32_t)S);
-                const uint32_t round = seq / (uint32_t)S;
-                if (!mbar_wait(smem_u32(&xempty_bar[s]), (round & 1u) ^ 1u)) {
+        const int nt = xres ? min(ntiles, 1) : ntiles;
+        int s = 0;
+        uint32_t ph = 0;
+        for (int t = 0; t < nt; ++t) {
+            for (int kt = 0; kt < a.ktiles; ++kt) {
+                const int slot = xres ? kt : s;
+                if (!xres && !mbar_wait(smem_u32(&xempty_bar[s]), ph ^ 1u)) {
                     report_error(a.err, 6);
                     abort_flag = 1;
                 }
                 if (*(volatile int*)&abort_flag) return;
-                const uint32_t xs = smem_base + (uint32_t)s * C::STAGE + C::W_BYTES;
+                const uint32_t xs = smem_base + (uint32_t)slot * C::STAGE + C::W_BYTES;
                 const uint32_t ss = xs + C::X_BYTES;
                 const long long k0 = (long long)kt * C::KTE;
-#pragma unroll 1
-                for (int m = 0; m < MT; ++m) {
-                    const float* xr = a.x + (long long)m * a.in;
-                    float4 v[NV];
+                if constexpr (INT) {
+                    // lane takes 16-value pieces gi = i*32 + lane: piece = half of block gi/2
+                    constexpr int NQ = 2 * C::G;
+                    float v[NQ][16];
 #pragma unroll
-                    for (int i = 0; i < NV; ++i) {
-                        const int e4 = (i * 32 + lane) * 4;
-                        v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-                        if (m < a.M && k0 + e4 < a.in) v[i] = ldg_nc_f4(xr + k0 + e4);
+                    for (int i = 0; i < NQ; ++i) {
+                        const long long e0 = k0 + 16LL * (i * 32 + lane);
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            float4 q4 = make_float4(0.f, 0.f, 0.f, 0.f);
+                            if (a.M > 0 && e0 + 4 * j < a.in) q4 = ldg_nc_f4(a.x + e0 + 4 * j);
+                            v[i][4 * j] = q4.x;
+                            v[i][4 * j + 1] = q4.y;
+                            v[i][4 * j + 2] = q4.z;
+                            v[i][4 * j + 3] = q4.w;
+                        }
                     }
 #pragma unroll
-                    for (int i = 0; i < NV; ++i) {
-                        const int e4 = (i * 32 + lane) * 4;
-                        float sum = (v[i].x + v[i].y) + (v[i].z + v[i].w);
+                    for (int i = 0; i < NQ; ++i) {
+                        const int gi = i * 32 + lane;
+                        const int blk = gi >> 1, half = gi & 1;
+                        const int g = blk / C::G, bg = blk % C::G;
+                        float mx = 0.f, sum = 0.f;
+#pragma unroll
+                        for (int e = 0; e < 16; ++e) {
+                            mx = fmaxf(mx, fabsf(v[i][e]));
+                            sum += v[i][e];
+                        }
+                        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
                         sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-                        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-                        sum += __shfl_xor_sync(0xffffffffu, sum, 4);
-                        const int blk = e4 >> 5;
-                        const int g = blk / C::G;
-                        const int bg = blk % C::G;
-                        const int p = part_of<F>(e4 & 31);
-                        sts_f4(xs + (uint32_t)(((m * C::G * 8 + bg * 8 + p) * 32 + (g ^ p)) * 16), v[i]);
-                        if ((lane & 7) == 0) sts_f32(ss + (uint32_t)((m * 32 * C::G + blk) * 4), sum);
+                        // blocks of (near-)zero magnitude carry no slices
+                        const float inv = mx > 1e-30f ? __fdiv_rn(127.0f, mx) : 0.0f;
+                        uint32_t wh[4], wm[4], wl[4];
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            float fh[4], fm[4], fl[4];
+#pragma unroll
+                            for (int u = 0; u < 4; ++u) {
+                                const float xv = v[i][4 * q + u];
+                                fh[u] = fmaf(xv, inv, kRound);
+                                const float r = fmaf(xv, inv, -(fh[u] - kRound));  // exact, |r| <= 1/2
+                                fm[u] = fmaf(r, 254.0f, kRound);
+                                const float r2 = fmaf(r, 254.0f, -(fm[u] - kRound));
+                                fl[u] = fmaf(r2, 254.0f, kRound);
+                            }
+                            wh[q] = pack_low_bytes(fh[0], fh[1], fh[2], fh[3]);
+                            wm[q] = pack_low_bytes(fm[0], fm[1], fm[2], fm[3]);
+                            wl[q] = pack_low_bytes(fl[0], fl[1], fl[2], fl[3]);
+                        }
+                        const uint32_t col = xcol<C::G>(g, 2 * bg + half);
+                        const uint32_t row = (uint32_t)(bg * 6 + half) * 512u;
+                        sts_u4(xs + row + col, make_uint4(wh[0], wh[1], wh[2], wh[3]));
+                        sts_u4(xs + row + 1024u + col, make_uint4(wm[0], wm[1], wm[2], wm[3]));
+                        sts_u4(xs + row + 2048u + col, make_uint4(wl[0], wl[1], wl[2], wl[3]));
+                        // scale (NaN/Inf in x poison it, as they would the fp32 sum) and x sum
+                        if (half == 0) sts_f2(ss + (uint32_t)blk * 8u, make_float2(fmaf(0.0f, sum, mx * (1.0f / 127.0f)), sum));
+                    }
+                } else {
+                    constexpr int NV = C::KTE / 128;  // float4 loads per lane per token
+#pragma unroll 1
+                    for (int m = 0; m < MT; ++m) {
+                        const float* xr = a.x + (long long)m * a.in;
+                        float4 v[NV];
+#pragma unroll
+                        for (int i = 0; i < NV; ++i) {
+                            const int e4 = (i * 32 + lane) * 4;
+                            v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+                            if (m < a.M && k0 + e4 < a.in) v[i] = ldg_nc_f4(xr + k0 + e4);
+                        }
+#pragma unroll
+                        for (int i = 0; i < NV; ++i) {
+                            const int e4 = (i * 32 + lane) * 4;
+                            float sum = (v[i].x + v[i].y) + (v[i].z + v[i].w);
+                            sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+                            sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+                            sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+                            const int blk = e4 >> 5;
+                            const int g = blk / C::G;
+                            const int bg = blk % C::G;
+                            const int p = part_of<F>(e4 & 31);
+                            sts_f4(xs + (uint32_t)(((m * C::G * 8 + bg * 8 + p) * 32 + (g ^ p)) * 16), v[i]);
+                            if ((lane & 7) == 0) sts_f32(ss + (uint32_t)((m * 32 * C::G + blk) * 4), sum);
+                        }
                     }
                 }
                 __syncwarp();
-                if (lane == 0) mbar_arrive(smem_u32(&xfull_bar[s]));
+                if (lane == 0) mbar_arrive(smem_u32(&xfull_bar[slot]));
+                if (!xres && ++s == S) {
+                    s = 0;
+                    ph ^= 1u;
+                }
             }
         }
         return;
@@ -315,11 +419,13 @@ __global__ void __launch_bounds__(kThreads, MINB)
     // y (and the peers' y) may still be read by the previous kernel
     grid_dependency_wait();
     const int wc = warp - 1;
-    // byte offset of this lane's float4 in x-tile part row p: (lane ^ p) * 16
+    // FP mode: byte offset of this lane's float4 in x-tile part row p: (lane ^ p) * 16
+    // INT mode: this lane's column in quad q's rows
     uint32_t xoff[8];
 #pragma unroll
-    for (int p = 0; p < 8; ++p) xoff[p] = (uint32_t)((lane ^ p) * 16);
-    uint32_t seq = 0;
+    for (int p = 0; p < 8; ++p) xoff[p] = INT ? xcol<C::G>(lane, p & (2 * C::G - 1)) : (uint32_t)((lane ^ p) * 16);
+    int s = 0;
+    uint32_t ph = 0;
     for (int t = 0; t < ntiles; ++t) {
         const long long row0 = r_begin + (long long)t * C::RT;
         const int nrows = (int)min((long long)C::RT, r_end - row0);
@@ -346,17 +452,16 @@ __global__ void __launch_bounds__(kThreads, MINB)
             }
         }
 
-        for (int kt = 0; kt < a.ktiles; ++kt, ++seq) {
-            const int s = (int)(seq % (uint32_t)S);
-            const uint32_t round = seq / (uint32_t)S;
-            if (!mbar_wait(smem_u32(&full_bar[s]), round & 1u)) {
+        for (int kt = 0; kt < a.ktiles; ++kt) {
+            if (!mbar_wait(smem_u32(&full_bar[s]), ph)) {
                 report_error(a.err, 1);
                 abort_flag = 1;
             }
             if (*(volatile int*)&abort_flag) return;
             const uint32_t stage = smem_base + (uint32_t)s * C::STAGE;
-            const uint32_t xs = stage + C::W_BYTES;
-            const uint32_t ss = stage + C::W_BYTES + C::X_BYTES + (uint32_t)lane * C::G * 4;
+            const int xslot = xres ? kt : s;
+            const uint32_t xs = smem_base + (uint32_t)xslot * C::STAGE + C::W_BYTES;
+            const uint32_t ss = xs + C::X_BYTES + (uint32_t)lane * C::G * (INT ? 8 : 4);
             const bool lane_on = lane < a.gpr - kt * 32;
 
             uint32_t wv[RPW][C::WPG];
@@ -374,12 +479,62 @@ __global__ void __launch_bounds__(kThreads, MINB)
             // weights are in registers now: hand the stage's weight region back
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(&empty_bar[s]));
-            if (!mbar_wait(smem_u32(&xfull_bar[s]), round & 1u)) {
+            if (!mbar_wait(smem_u32(&xfull_bar[xslot]), xres ? 0u : ph)) {
                 report_error(a.err, 1);
                 abort_flag = 1;
             }
             if (*(volatile int*)&abort_flag) return;
 
+            if constexpr (INT) {
+#pragma unroll
+                for (int bg = 0; bg < C::G; ++bg) {
+                    const float2 sc = lds_f2(ss + (uint32_t)bg * 8u);
+                    uint4 xq[6];  // (slice, half): x slices of this lane's block bg
+#pragma unroll
+                    for (int k = 0; k < 6; ++k)
+                        xq[k] = lds_u4(xs + (uint32_t)(bg * 6 + k) * 512u + xoff[2 * bg + (k & 1)]);
+#pragma unroll
+                    for (int r = 0; r < RPW; ++r) {
+                        uint32_t c[8];
+                        if constexpr (F == kQ8_0) {
+#pragma unroll
+                            for (int j = 0; j < 8; ++j) c[j] = qs_word<F>(wv[r], bg, j);
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) {
+                                const uint32_t qw = qs_word<F>(wv[r], bg, j);
+                                c[j] = qw & 0x0F0F0F0Fu;
+                                c[4 + j] = (qw >> 4) & 0x0F0F0F0Fu;
+                            }
+                        }
+                        int acc[3];
+#pragma unroll
+                        for (int sl = 0; sl < 3; ++sl) {
+                            const uint4 lo = xq[2 * sl], hi = xq[2 * sl + 1];
+                            int v = __dp4a((int)c[0], (int)lo.x, 0);
+                            v = __dp4a((int)c[1], (int)lo.y, v);
+                            v = __dp4a((int)c[2], (int)lo.z, v);
+                            v = __dp4a((int)c[3], (int)lo.w, v);
+                            v = __dp4a((int)c[4], (int)hi.x, v);
+                            v = __dp4a((int)c[5], (int)hi.y, v);
+                            v = __dp4a((int)c[6], (int)hi.z, v);
+                            v = __dp4a((int)c[7], (int)hi.w, v);
+                            acc[sl] = v;
+                        }
+                        const float qx = sc.x * fmaf(__int2float_rn(acc[1] * 254 + acc[2]), kInvSlice2,
+                                                     __int2float_rn(acc[0]));
+                        const float d = half_bits_to_float(d_bits<F>(wv[r], bg));
+                        if constexpr (F == kQ4_0) {
+                            tot[r][0] = fmaf(d, fmaf(-8.0f, sc.y, qx), tot[r][0]);
+                        } else if constexpr (F == kQ4_1) {
+                            tot[r][0] = fmaf(d, qx, tot[r][0]);
+                            tot[r][0] = fmaf(half_bits_to_float(wv[r][0] >> 16), sc.y, tot[r][0]);
+                        } else {
+                            tot[r][0] = fmaf(d, qx, tot[r][0]);
+                        }
+                    }
+                }
+            } else {
 #pragma unroll
             for (int bg = 0; bg < C::G; ++bg) {
                 // two packed partial-sum pairs per (row, token): even / odd parts (FFMA2)
@@ -436,8 +591,15 @@ __global__ void __launch_bounds__(kThreads, MINB)
                     }
                 }
             }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(&xempty_bar[s]));
+            }
+            if (!xres) {
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(&xempty_bar[s]));
+            }
+            if (++s == S) {
+                s = 0;
+                ph ^= 1u;
+            }
         }
 
         // reduce the 32 lane partials of every (row, token) into the tile's
@@ -563,9 +725,9 @@ __global__ void __launch_bounds__(256) gemv_generic_kernel(const uint8_t* __rest
     }
 }
 
-template <int F, int MT, int RPW, int MINB>
+template <int F, int MT, int RPW, int MINB, bool INT>
 cudaError_t launch_stream_t(GemvArgs args, int sm_count, int smem_per_sm, cudaStream_t stream) {
-    using C = GemvCfg<F, MT, RPW>;
+    using C = GemvCfg<F, MT, RPW, INT>;
     // Per-CTA budget: the SM's shared memory split MINB ways, minus the 1 KB
     // the driver reserves per CTA and this kernel's static barriers.
     const int budget = smem_per_sm / MINB - 1024 - 512 - 128;
@@ -573,12 +735,14 @@ cudaError_t launch_stream_t(GemvArgs args, int sm_count, int smem_per_sm, cudaSt
     if (S > kMaxStages) S = kMaxStages;
     if (S < 2) return cudaErrorInvalidConfiguration;
     args.nstages = S;
+    // x tiles stay resident when every K-tile has its own stage slot
+    args.x_resident = args.ktiles <= S ? 1 : 0;
     const int smem = S * C::STAGE + 128;  // + alignment slack
     static int attr_bytes[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 64 || attr_bytes[dev] < smem) {
-        cudaError_t e = cudaFuncSetAttribute(gemv_stream_kernel<F, MT, RPW, MINB>,
+        cudaError_t e = cudaFuncSetAttribute(gemv_stream_kernel<F, MT, RPW, MINB, INT>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
         if (dev < 64) attr_bytes[dev] = smem;
@@ -606,7 +770,7 @@ cudaError_t launch_stream_t(GemvArgs args, int sm_count, int smem_per_sm, cudaSt
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, gemv_stream_kernel<F, MT, RPW, MINB>, args, wmap);
+    return cudaLaunchKernelEx(&cfg, gemv_stream_kernel<F, MT, RPW, MINB, INT>, args, wmap);
 }
 
 // rows-per-warp choice per format: keeps the lane-group words of all RPW
@@ -617,12 +781,15 @@ constexpr int rpw_for() {
 }
 
 // One or two tokens per pass: two CTAs per SM (16 consumer warps per SM,
-// registers capped at 113); more tokens: one CTA per SM with deeper stages.
+// registers capped at 102); more tokens: one CTA per SM with deeper stages.
+// One token takes the integer (DP4A) mode: 24 four-way integer dot products
+// and ~12 mask ops per block and row, against ~32 byte-permutes + 16 packed
+// FMAs in the fp32 mode, whose decode cost is shared only from two tokens on.
 template <int F, int MT>
 cudaError_t dispatch_mt(const GemvArgs& args, int sm_count, int smem_per_sm, cudaStream_t stream) {
     constexpr int RPW = rpw_for<F>();
     constexpr int MINB = MT <= 2 ? 2 : 1;
-    return launch_stream_t<F, MT, RPW, MINB>(args, sm_count, smem_per_sm, stream);
+    return launch_stream_t<F, MT, RPW, MINB, MT == 1>(args, sm_count, smem_per_sm, stream);
 }
 
 }  // namespace

@@ -24,6 +24,7 @@ struct GemvArgs {
     long long total_bytes;   // out * row_bytes
     int* err;                // device error flag
     int tma2d;               // weights streamed by 2-D tensor map (set by the launcher)
+    int x_resident;          // ktiles <= nstages: x tiles built once, kept for every row tile
     // sharded calls only (world > 1): completion handshake
     int world, rank;
     uint32_t epoch;
