@@ -84,9 +84,8 @@ struct GemvCfg {
                   "tensor TMA destinations must be 128-byte aligned");
     static_assert(NREG * REGION <= W_BYTES, "2-D layout must fit the stage");
     static_assert(BOXB % 16 == 0, "box rows must be 16-byte granular");
-    static constexpr int STAGE = W_BYTES + XT_BYTES;
     static_assert(WPG % 2 == 1, "lane-group word count must be odd");
-    static_assert(SLOT % 16 == 0 && STAGE % 16 == 0, "stage alignment");
+    static_assert(SLOT % 16 == 0, "stage alignment");
     static_assert(!INT || MT == 1, "integer mode is the one-token path");
 };
 
@@ -178,6 +177,67 @@ __device__ __forceinline__ uint32_t xcol(int g, int q) {
     return (uint32_t)((g + (4 / G) * q) & 31) * 16u;
 }
 
+// INT mode x tile, piece i of K-tile k0 for this lane: 16 values
+// [k0 + 16 (32 i + lane), +16) = one half of block (32 i + lane) / 2.
+template <int G>
+__device__ __forceinline__ void int_piece_load(const float* x, int in, long long k0, int i, int lane,
+                                               float v[16]) {
+    const long long e0 = k0 + 16LL * (i * 32 + lane);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        float4 q4 = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (e0 + 4 * j < in) q4 = ldg_nc_f4(x + e0 + 4 * j);
+        v[4 * j] = q4.x;
+        v[4 * j + 1] = q4.y;
+        v[4 * j + 2] = q4.z;
+        v[4 * j + 3] = q4.w;
+    }
+}
+
+// Slices of one piece into x tile `xs` (+ scale/sum pair into `ss`).  The two
+// lanes holding a block's halves are neighbours (shuffle partners).
+template <int G>
+__device__ __forceinline__ void int_piece_store(const float v[16], int i, int lane, uint32_t xs,
+                                                uint32_t ss) {
+    const int gi = i * 32 + lane;
+    const int blk = gi >> 1, half = gi & 1;
+    const int g = blk / G, bg = blk % G;
+    float mx = 0.f, sum = 0.f;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+        mx = fmaxf(mx, fabsf(v[e]));
+        sum += v[e];
+    }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    // blocks of (near-)zero magnitude carry no slices
+    const float inv = mx > 1e-30f ? __fdiv_rn(127.0f, mx) : 0.0f;
+    uint32_t wh[4], wm[4], wl[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        float fh[4], fm[4], fl[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const float xv = v[4 * q + u];
+            fh[u] = fmaf(xv, inv, kRound);
+            const float r = fmaf(xv, inv, -(fh[u] - kRound));  // exact, |r| <= 1/2
+            fm[u] = fmaf(r, 254.0f, kRound);
+            const float r2 = fmaf(r, 254.0f, -(fm[u] - kRound));
+            fl[u] = fmaf(r2, 254.0f, kRound);
+        }
+        wh[q] = pack_low_bytes(fh[0], fh[1], fh[2], fh[3]);
+        wm[q] = pack_low_bytes(fm[0], fm[1], fm[2], fm[3]);
+        wl[q] = pack_low_bytes(fl[0], fl[1], fl[2], fl[3]);
+    }
+    const uint32_t col = xcol<G>(g, 2 * bg + half);
+    const uint32_t row = (uint32_t)(bg * 6 + half) * 512u;
+    sts_u4(xs + row + col, make_uint4(wh[0], wh[1], wh[2], wh[3]));
+    sts_u4(xs + row + 1024u + col, make_uint4(wm[0], wm[1], wm[2], wm[3]));
+    sts_u4(xs + row + 2048u + col, make_uint4(wl[0], wl[1], wl[2], wl[3]));
+    // scale (NaN/Inf in x poison it, as they would the fp32 sum) and x sum
+    if (half == 0) sts_f2(ss + (uint32_t)blk * 8u, make_float2(fmaf(0.0f, sum, mx * (1.0f / 127.0f)), sum));
+}
+
 template <int F, int MT, int RPW, int MINB, bool INT>
 __global__ void __launch_bounds__(kThreads, MINB)
     gemv_stream_kernel(GemvArgs a, const __grid_constant__ CUtensorMap wmap) {
@@ -190,6 +250,7 @@ __global__ void __launch_bounds__(kThreads, MINB)
     __shared__ int abort_flag;
     __shared__ float tile_res[2][MT * C::RT];  // per-tile results, double-buffered
     __shared__ __align__(8) uint64_t tile_bar;  // consumer warps' per-tile rendezvous
+    __shared__ __align__(8) uint64_t xready_bar;  // INT resident mode: all x tiles built
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -197,13 +258,14 @@ __global__ void __launch_bounds__(kThreads, MINB)
     const bool xres = a.x_resident != 0;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < S; ++s) {
+        for (int s = 0; s < kMaxStages; ++s) {
             mbar_init(smem_u32(&full_bar[s]), 32);
             mbar_init(smem_u32(&empty_bar[s]), kConsumerWarps);
             mbar_init(smem_u32(&xfull_bar[s]), 1);
             mbar_init(smem_u32(&xempty_bar[s]), kConsumerWarps);
         }
         mbar_init(smem_u32(&tile_bar), kConsumerWarps);
+        mbar_init(smem_u32(&xready_bar), kConsumerWarps + 1);
         abort_flag = 0;
         fence_mbar_init();
     }
@@ -218,6 +280,8 @@ __global__ void __launch_bounds__(kThreads, MINB)
     const int nrows_cta = (int)(r_end - r_begin);
     const int ntiles = (nrows_cta + C::RT - 1) / C::RT;
     const uint32_t smem_base = (smem_u32(smem) + 127u) & ~127u;  // TMA boxes: 128-B aligned
+    // S weight stages, then the x slots (one per K-tile when resident, else one per stage)
+    const uint32_t x_base = smem_base + (uint32_t)S * C::W_BYTES;
     const uintptr_t wbase = reinterpret_cast<uintptr_t>(a.w);
     const uintptr_t wend16 = (wbase + (uintptr_t)a.total_bytes) & ~(uintptr_t)15;
 
@@ -236,7 +300,7 @@ __global__ void __launch_bounds__(kThreads, MINB)
                     abort_flag = 1;
                 }
                 if (*(volatile int*)&abort_flag) goto producer_drain;
-                const uint32_t stage = smem_base + (uint32_t)s * C::STAGE;
+                const uint32_t stage = smem_base + (uint32_t)s * C::W_BYTES;
                 const int groups = min(32, a.gpr - kt * 32);
                 const uint32_t seg = (uint32_t)(groups * C::GB);
                 if (a.tma2d) {
@@ -295,6 +359,33 @@ __global__ void __launch_bounds__(kThreads, MINB)
         return;
     }
 
+    if (INT && xres) {
+        // ------------------- x tiles, built once by warps 1..9 -------------------
+        // Resident integer mode: the consumers and the x loader split the
+        // pieces of every K-tile between them, then meet on xready_bar.
+        // x may be the previous kernel's output: wait for it (weights are
+        // read-only, so warp 0 started streaming them without waiting)
+        grid_dependency_wait();
+        constexpr int NQ = 2 * C::G;
+        const int items = a.ktiles * NQ;
+        for (int it = warp - 1; it < items; it += 2 * (kConsumerWarps + 1)) {
+            // two pieces in flight per warp
+            const int it2 = it + kConsumerWarps + 1;
+            float v0[16], v1[16];
+            int_piece_load<C::G>(a.x, a.in, (long long)(it / NQ) * C::KTE, it % NQ, lane, v0);
+            if (it2 < items) int_piece_load<C::G>(a.x, a.in, (long long)(it2 / NQ) * C::KTE, it2 % NQ, lane, v1);
+            const uint32_t xs0 = x_base + (uint32_t)(it / NQ) * C::XT_BYTES;
+            int_piece_store<C::G>(v0, it % NQ, lane, xs0, xs0 + C::X_BYTES);
+            if (it2 < items) {
+                const uint32_t xs1 = x_base + (uint32_t)(it2 / NQ) * C::XT_BYTES;
+                int_piece_store<C::G>(v1, it2 % NQ, lane, xs1, xs1 + C::X_BYTES);
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&xready_bar));
+        if (warp == kXWarp) return;
+    }
+
     if (warp == kXWarp) {
         // ------------------------------ x loader ------------------------------
         // Per K-tile: x for MT tokens with coalesced 128-bit loads (all in
@@ -316,66 +407,17 @@ __global__ void __launch_bounds__(kThreads, MINB)
                     abort_flag = 1;
                 }
                 if (*(volatile int*)&abort_flag) return;
-                const uint32_t xs = smem_base + (uint32_t)slot * C::STAGE + C::W_BYTES;
+                const uint32_t xs = x_base + (uint32_t)slot * C::XT_BYTES;
                 const uint32_t ss = xs + C::X_BYTES;
                 const long long k0 = (long long)kt * C::KTE;
                 if constexpr (INT) {
-                    // lane takes 16-value pieces gi = i*32 + lane: piece = half of block gi/2
+                    // lane takes 16-value pieces 32 i + lane (all loads in flight first)
                     constexpr int NQ = 2 * C::G;
                     float v[NQ][16];
 #pragma unroll
-                    for (int i = 0; i < NQ; ++i) {
-                        const long long e0 = k0 + 16LL * (i * 32 + lane);
+                    for (int i = 0; i < NQ; ++i) int_piece_load<C::G>(a.x, a.in, k0, i, lane, v[i]);
 #pragma unroll
-                        for (int j = 0; j < 4; ++j) {
-                            float4 q4 = make_float4(0.f, 0.f, 0.f, 0.f);
-                            if (a.M > 0 && e0 + 4 * j < a.in) q4 = ldg_nc_f4(a.x + e0 + 4 * j);
-                            v[i][4 * j] = q4.x;
-                            v[i][4 * j + 1] = q4.y;
-                            v[i][4 * j + 2] = q4.z;
-                            v[i][4 * j + 3] = q4.w;
-                        }
-                    }
-#pragma unroll
-                    for (int i = 0; i < NQ; ++i) {
-                        const int gi = i * 32 + lane;
-                        const int blk = gi >> 1, half = gi & 1;
-                        const int g = blk / C::G, bg = blk % C::G;
-                        float mx = 0.f, sum = 0.f;
-#pragma unroll
-                        for (int e = 0; e < 16; ++e) {
-                            mx = fmaxf(mx, fabsf(v[i][e]));
-                            sum += v[i][e];
-                        }
-                        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-                        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-                        // blocks of (near-)zero magnitude carry no slices
-                        const float inv = mx > 1e-30f ? __fdiv_rn(127.0f, mx) : 0.0f;
-                        uint32_t wh[4], wm[4], wl[4];
-#pragma unroll
-                        for (int q = 0; q < 4; ++q) {
-                            float fh[4], fm[4], fl[4];
-#pragma unroll
-                            for (int u = 0; u < 4; ++u) {
-                                const float xv = v[i][4 * q + u];
-                                fh[u] = fmaf(xv, inv, kRound);
-                                const float r = fmaf(xv, inv, -(fh[u] - kRound));  // exact, |r| <= 1/2
-                                fm[u] = fmaf(r, 254.0f, kRound);
-                                const float r2 = fmaf(r, 254.0f, -(fm[u] - kRound));
-                                fl[u] = fmaf(r2, 254.0f, kRound);
-                            }
-                            wh[q] = pack_low_bytes(fh[0], fh[1], fh[2], fh[3]);
-                            wm[q] = pack_low_bytes(fm[0], fm[1], fm[2], fm[3]);
-                            wl[q] = pack_low_bytes(fl[0], fl[1], fl[2], fl[3]);
-                        }
-                        const uint32_t col = xcol<C::G>(g, 2 * bg + half);
-                        const uint32_t row = (uint32_t)(bg * 6 + half) * 512u;
-                        sts_u4(xs + row + col, make_uint4(wh[0], wh[1], wh[2], wh[3]));
-                        sts_u4(xs + row + 1024u + col, make_uint4(wm[0], wm[1], wm[2], wm[3]));
-                        sts_u4(xs + row + 2048u + col, make_uint4(wl[0], wl[1], wl[2], wl[3]));
-                        // scale (NaN/Inf in x poison it, as they would the fp32 sum) and x sum
-                        if (half == 0) sts_f2(ss + (uint32_t)blk * 8u, make_float2(fmaf(0.0f, sum, mx * (1.0f / 127.0f)), sum));
-                    }
+                    for (int i = 0; i < NQ; ++i) int_piece_store<C::G>(v[i], i, lane, xs, ss);
                 } else {
                     constexpr int NV = C::KTE / 128;  // float4 loads per lane per token
 #pragma unroll 1
@@ -418,6 +460,10 @@ __global__ void __launch_bounds__(kThreads, MINB)
     // -------------------------------- consumers --------------------------------
     // y (and the peers' y) may still be read by the previous kernel
     grid_dependency_wait();
+    if (INT && xres && !mbar_wait(smem_u32(&xready_bar), 0u)) {
+        report_error(a.err, 7);
+        abort_flag = 1;
+    }
     const int wc = warp - 1;
     // FP mode: byte offset of this lane's float4 in x-tile part row p: (lane ^ p) * 16
     // INT mode: this lane's column in quad q's rows
@@ -458,9 +504,9 @@ __global__ void __launch_bounds__(kThreads, MINB)
                 abort_flag = 1;
             }
             if (*(volatile int*)&abort_flag) return;
-            const uint32_t stage = smem_base + (uint32_t)s * C::STAGE;
+            const uint32_t stage = smem_base + (uint32_t)s * C::W_BYTES;
             const int xslot = xres ? kt : s;
-            const uint32_t xs = smem_base + (uint32_t)xslot * C::STAGE + C::W_BYTES;
+            const uint32_t xs = x_base + (uint32_t)xslot * C::XT_BYTES;
             const uint32_t ss = xs + C::X_BYTES + (uint32_t)lane * C::G * (INT ? 8 : 4);
             const bool lane_on = lane < a.gpr - kt * 32;
 
@@ -479,7 +525,7 @@ __global__ void __launch_bounds__(kThreads, MINB)
             // weights are in registers now: hand the stage's weight region back
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(&empty_bar[s]));
-            if (!mbar_wait(smem_u32(&xfull_bar[xslot]), xres ? 0u : ph)) {
+            if (!(INT && xres) && !mbar_wait(smem_u32(&xfull_bar[xslot]), xres ? 0u : ph)) {
                 report_error(a.err, 1);
                 abort_flag = 1;
             }
@@ -729,15 +775,27 @@ template <int F, int MT, int RPW, int MINB, bool INT>
 cudaError_t launch_stream_t(GemvArgs args, int sm_count, int smem_per_sm, cudaStream_t stream) {
     using C = GemvCfg<F, MT, RPW, INT>;
     // Per-CTA budget: the SM's shared memory split MINB ways, minus the 1 KB
-    // the driver reserves per CTA and this kernel's static barriers.
-    const int budget = smem_per_sm / MINB - 1024 - 512 - 128;
-    int S = budget / C::STAGE;
+    // the driver reserves per CTA, this kernel's static shared memory
+    // (barriers + tile results, < 2.5 KB) and the alignment slack.
+    const int budget = smem_per_sm / MINB - 1024 - 2560 - 128;
+    // Resident x (every K-tile's x tile kept, built once) when it fits next
+    // to two weight stages; the fp32 mode also needs a barrier per K-tile.
+    const long long xres_bytes = (long long)args.ktiles * C::XT_BYTES;
+    int S, nx;
+    if (xres_bytes + 2LL * C::W_BYTES <= budget && (INT || args.ktiles <= kMaxStages)) {
+        args.x_resident = 1;
+        nx = args.ktiles;
+        S = (int)((budget - xres_bytes) / C::W_BYTES);
+    } else {
+        args.x_resident = 0;
+        S = budget / (C::W_BYTES + C::XT_BYTES);
+        nx = S;
+    }
     if (S > kMaxStages) S = kMaxStages;
+    if (!args.x_resident) nx = S;
     if (S < 2) return cudaErrorInvalidConfiguration;
     args.nstages = S;
-    // x tiles stay resident when every K-tile has its own stage slot
-    args.x_resident = args.ktiles <= S ? 1 : 0;
-    const int smem = S * C::STAGE + 128;  // + alignment slack
+    const int smem = S * C::W_BYTES + nx * C::XT_BYTES + 128;  // + the alignment slack
     static int attr_bytes[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -745,7 +803,7 @@ cudaError_t launch_stream_t(GemvArgs args, int sm_count, int smem_per_sm, cudaSt
         cudaError_t e = cudaFuncSetAttribute(gemv_stream_kernel<F, MT, RPW, MINB, INT>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
-        if (dev < 64) attr_bytes[dev] = smem;
+        if (dev < 64 && smem > attr_bytes[dev]) attr_bytes[dev] = smem;
     }
     // weights by 2-D tensor map when the row pitch and base allow it
     CUtensorMap wmap;
@@ -785,11 +843,20 @@ constexpr int rpw_for() {
 // One token takes the integer (DP4A) mode: 24 four-way integer dot products
 // and ~12 mask ops per block and row, against ~32 byte-permutes + 16 packed
 // FMAs in the fp32 mode, whose decode cost is shared only from two tokens on.
+// A one-token call whose rows fill at most half of one tile per CTA runs
+// with half the rows per warp, so fewer tile rows sit idle.
 template <int F, int MT>
 cudaError_t dispatch_mt(const GemvArgs& args, int sm_count, int smem_per_sm, cudaStream_t stream) {
     constexpr int RPW = rpw_for<F>();
     constexpr int MINB = MT <= 2 ? 2 : 1;
-    return launch_stream_t<F, MT, RPW, MINB, MT == 1>(args, sm_count, smem_per_sm, stream);
+    if constexpr (MT == 1) {
+        const long long ctas = (long long)sm_count * MINB;
+        if ((long long)args.out <= ctas * kConsumerWarps * (RPW / 2))
+            return launch_stream_t<F, 1, RPW / 2, MINB, true>(args, sm_count, smem_per_sm, stream);
+        return launch_stream_t<F, 1, RPW, MINB, true>(args, sm_count, smem_per_sm, stream);
+    } else {
+        return launch_stream_t<F, MT, RPW, MINB, false>(args, sm_count, smem_per_sm, stream);
+    }
 }
 
 }  // namespace
