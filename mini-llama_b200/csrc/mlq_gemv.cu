@@ -238,6 +238,41 @@ __device__ __forceinline__ void int_piece_store(const float v[16], int i, int la
     if (half == 0) sts_f2(ss + (uint32_t)blk * 8u, make_float2(fmaf(0.0f, sum, mx * (1.0f / 127.0f)), sum));
 }
 
+constexpr int log2_of(int n) { return n <= 1 ? 0 : 1 + log2_of(n / 2); }
+
+// Sum of v[r][0] over the 32 lanes for every row r < RPW (1, 2 or 4), as a
+// reduce-scatter: after it, the lanes of block k of 32/RPW consecutive lanes
+// hold row k's total.
+template <int RPW, int MT>
+__device__ __forceinline__ float reduce_rows(float (&v)[RPW][MT], int lane) {
+    float k;
+    if constexpr (RPW == 4) {
+        const bool up = lane & 16;
+        float k0 = up ? v[2][0] : v[0][0], k1 = up ? v[3][0] : v[1][0];
+        const float s0 = up ? v[0][0] : v[2][0], s1 = up ? v[1][0] : v[3][0];
+        k0 += __shfl_xor_sync(0xffffffffu, s0, 16);
+        k1 += __shfl_xor_sync(0xffffffffu, s1, 16);
+        const bool up8 = lane & 8;
+        k = up8 ? k1 : k0;
+        k += __shfl_xor_sync(0xffffffffu, up8 ? k0 : k1, 8);
+        k += __shfl_xor_sync(0xffffffffu, k, 4);
+    } else if constexpr (RPW == 2) {
+        const bool up = lane & 16;
+        k = up ? v[1][0] : v[0][0];
+        k += __shfl_xor_sync(0xffffffffu, up ? v[0][0] : v[1][0], 16);
+        k += __shfl_xor_sync(0xffffffffu, k, 8);
+        k += __shfl_xor_sync(0xffffffffu, k, 4);
+    } else {
+        k = v[0][0];
+        k += __shfl_xor_sync(0xffffffffu, k, 16);
+        k += __shfl_xor_sync(0xffffffffu, k, 8);
+        k += __shfl_xor_sync(0xffffffffu, k, 4);
+    }
+    k += __shfl_xor_sync(0xffffffffu, k, 2);
+    k += __shfl_xor_sync(0xffffffffu, k, 1);
+    return k;
+}
+
 template <int F, int MT, int RPW, int MINB, bool INT>
 __global__ void __launch_bounds__(kThreads, MINB)
     gemv_stream_kernel(GemvArgs a, const __grid_constant__ CUtensorMap wmap) {
@@ -648,6 +683,17 @@ __global__ void __launch_bounds__(kThreads, MINB)
             }
         }
 
+        if (MT == 1 && a.ny == 1) {
+            // One token, one destination: reduce-scatter the RPW row sums
+            // across the lanes (RPW-1 + 5 - log2 RPW shuffles instead of 5 RPW)
+            // and let the lane that ends up with row r's total store it.
+            float v = reduce_rows<RPW>(tot, lane);
+            const int r = lane >> (5 - log2_of(RPW));  // row held by this lane
+            const int i = wc + r * kConsumerWarps;
+            if ((lane & (31 >> log2_of(RPW))) == 0 && i < nrows)
+                a.ys[0][a.row_offset + row0 + i] = v;
+            continue;
+        }
         // reduce the 32 lane partials of every (row, token) into the tile's
         // result buffer, then store it with coalesced writes: RT consecutive
         // floats per token, to this GPU's y and, in a sharded call, to every
@@ -843,17 +889,16 @@ constexpr int rpw_for() {
 // One token takes the integer (DP4A) mode: 24 four-way integer dot products
 // and ~12 mask ops per block and row, against ~32 byte-permutes + 16 packed
 // FMAs in the fp32 mode, whose decode cost is shared only from two tokens on.
-// A one-token call whose rows fill at most half of one tile per CTA runs
-// with half the rows per warp, so fewer tile rows sit idle.
 template <int F, int MT>
 cudaError_t dispatch_mt(const GemvArgs& args, int sm_count, int smem_per_sm, cudaStream_t stream) {
     constexpr int RPW = rpw_for<F>();
     constexpr int MINB = MT <= 2 ? 2 : 1;
     if constexpr (MT == 1) {
-        const long long ctas = (long long)sm_count * MINB;
-        if ((long long)args.out <= ctas * kConsumerWarps * (RPW / 2))
-            return launch_stream_t<F, 1, RPW / 2, MINB, true>(args, sm_count, smem_per_sm, stream);
-        return launch_stream_t<F, 1, RPW, MINB, true>(args, sm_count, smem_per_sm, stream);
+        // fewer than one full tile per CTA at two CTAs per SM: one CTA per SM
+        // (a full tile each, and the whole shared memory for weight stages)
+        if ((long long)args.out < 2LL * sm_count * kConsumerWarps * RPW)
+            return launch_stream_t<F, 1, RPW, 1, true>(args, sm_count, smem_per_sm, stream);
+        return launch_stream_t<F, 1, RPW, 2, true>(args, sm_count, smem_per_sm, stream);
     } else {
         return launch_stream_t<F, MT, RPW, MINB, false>(args, sm_count, smem_per_sm, stream);
     }
