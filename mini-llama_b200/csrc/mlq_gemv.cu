@@ -38,6 +38,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <cstring>
 
 #include "mlq_device.cuh"
@@ -45,6 +46,14 @@
 #include "mlq_tmap.h"
 
 namespace mlq {
+
+// Dynamic row-tile queues: one {next tile, finished CTAs} pair per launch,
+// taken round-robin from this ring (zero at module load; the last CTA of a
+// launch puts its pair back to zero).  A slot is reused only after 255 other
+// launches on the device, far more than can run at once.
+constexpr int kTileSlots = 256;
+__device__ unsigned int g_gemv_tile_slots[2 * kTileSlots];
+
 namespace {
 
 constexpr int kConsumerWarps = 8;
@@ -286,6 +295,7 @@ __global__ void __launch_bounds__(kThreads, MINB)
     __shared__ float tile_res[2][MT * C::RT];  // per-tile results, double-buffered
     __shared__ __align__(8) uint64_t tile_bar;  // consumer warps' per-tile rendezvous
     __shared__ __align__(8) uint64_t xready_bar;  // INT resident mode: all x tiles built
+    __shared__ int stage_row[kMaxStages];         // dynamic mode: first row of each stage's tile (-1: end)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -320,14 +330,30 @@ __global__ void __launch_bounds__(kThreads, MINB)
     const uintptr_t wbase = reinterpret_cast<uintptr_t>(a.w);
     const uintptr_t wend16 = (wbase + (uintptr_t)a.total_bytes) & ~(uintptr_t)15;
 
+    // Dynamic tiles (one token, resident x, plain call): CTAs take row tiles
+    // from a global queue instead of a fixed row range, so SMs that stream
+    // faster do more tiles and all CTAs finish together.
+    const bool dyn = INT && xres && a.tiles != nullptr && a.ny == 1 && a.world == 1;
+    const long long ntiles_all = (a.out + C::RT - 1) / C::RT;
+
     if (warp == 0) {
         // ------------------------------ producer ------------------------------
         uint32_t seq = 0;
         int s = 0;
         uint32_t ph = 0;
-        for (int t = 0; t < ntiles; ++t) {
-            const long long row0 = r_begin + (long long)t * C::RT;
-            const int nrows = (int)min((long long)C::RT, r_end - row0);
+        // lane 0 holds the next queue ticket, fetched one tile ahead
+        unsigned int ticket = (dyn && lane == 0) ? atomicAdd(a.tiles, 1u) : 0u;
+        for (int t = 0; dyn || t < ntiles; ++t) {
+            long long row0;
+            if (dyn) {
+                const unsigned int cur = __shfl_sync(0xffffffffu, ticket, 0);
+                if ((long long)cur >= ntiles_all) break;
+                if (lane == 0) ticket = atomicAdd(a.tiles, 1u);
+                row0 = (long long)cur * C::RT;
+            } else {
+                row0 = r_begin + (long long)t * C::RT;
+            }
+            const int nrows = (int)min((long long)C::RT, (dyn ? (long long)a.out : r_end) - row0);
             for (int kt = 0; kt < a.ktiles; ++kt, ++seq) {
                 const uint32_t fb = smem_u32(&full_bar[s]);
                 if (!mbar_wait(smem_u32(&empty_bar[s]), ph ^ 1u)) {
@@ -336,6 +362,7 @@ __global__ void __launch_bounds__(kThreads, MINB)
                 }
                 if (*(volatile int*)&abort_flag) goto producer_drain;
                 const uint32_t stage = smem_base + (uint32_t)s * C::W_BYTES;
+                if (dyn && lane == 0) stage_row[s] = (int)row0;
                 const int groups = min(32, a.gpr - kt * 32);
                 const uint32_t seg = (uint32_t)(groups * C::GB);
                 if (a.tma2d) {
@@ -377,6 +404,25 @@ __global__ void __launch_bounds__(kThreads, MINB)
                 if (++s == S) {
                     s = 0;
                     ph ^= 1u;
+                }
+            }
+        }
+        if (dyn) {
+            // end marker for the consumers: a stage with no bytes and row -1
+            if (!mbar_wait(smem_u32(&empty_bar[s]), ph ^ 1u)) {
+                report_error(a.err, 2);
+                abort_flag = 1;
+            }
+            if (*(volatile int*)&abort_flag) goto producer_drain;
+            if (lane == 0) stage_row[s] = -1;
+            __syncwarp();
+            mbar_arrive(smem_u32(&full_bar[s]));
+            // the last CTA to finish puts the queue back to zero for a later launch
+            if (lane == 0) {
+                __threadfence();
+                if (atomicAdd(a.tiles + 1, 1u) == gridDim.x - 1) {
+                    atomicExch(a.tiles, 0u);
+                    atomicExch(a.tiles + 1, 0u);
                 }
             }
         }
@@ -507,9 +553,22 @@ __global__ void __launch_bounds__(kThreads, MINB)
     for (int p = 0; p < 8; ++p) xoff[p] = INT ? xcol<C::G>(lane, p & (2 * C::G - 1)) : (uint32_t)((lane ^ p) * 16);
     int s = 0;
     uint32_t ph = 0;
-    for (int t = 0; t < ntiles; ++t) {
-        const long long row0 = r_begin + (long long)t * C::RT;
-        const int nrows = (int)min((long long)C::RT, r_end - row0);
+    for (int t = 0; dyn || t < ntiles; ++t) {
+        long long row0;
+        if (dyn) {
+            // the tile's first stage names its rows
+            if (!mbar_wait(smem_u32(&full_bar[s]), ph)) {
+                report_error(a.err, 1);
+                abort_flag = 1;
+            }
+            if (*(volatile int*)&abort_flag) return;
+            const int r0 = *(volatile int*)&stage_row[s];
+            if (r0 < 0) break;
+            row0 = r0;
+        } else {
+            row0 = r_begin + (long long)t * C::RT;
+        }
+        const int nrows = (int)min((long long)C::RT, (dyn ? (long long)a.out : r_end) - row0);
         float tot[RPW][MT];
 #pragma unroll
         for (int r = 0; r < RPW; ++r)
@@ -534,7 +593,7 @@ __global__ void __launch_bounds__(kThreads, MINB)
         }
 
         for (int kt = 0; kt < a.ktiles; ++kt) {
-            if (!mbar_wait(smem_u32(&full_bar[s]), ph)) {
+            if (!(dyn && kt == 0) && !mbar_wait(smem_u32(&full_bar[s]), ph)) {
                 report_error(a.err, 1);
                 abort_flag = 1;
             }
@@ -817,8 +876,45 @@ __global__ void __launch_bounds__(256) gemv_generic_kernel(const uint8_t* __rest
     }
 }
 
+// This device's tile-queue ring (looked up once per device, that device current).
+unsigned int* tile_slots(int dev) {
+    static std::atomic<unsigned int*> ptrs[64];
+    if (dev < 0 || dev >= 64) return nullptr;
+    unsigned int* p = ptrs[dev].load(std::memory_order_acquire);
+    if (!p) {
+        void* q = nullptr;
+        if (cudaGetSymbolAddress(&q, g_gemv_tile_slots) != cudaSuccess) {
+            cudaGetLastError();
+            return nullptr;
+        }
+        p = static_cast<unsigned int*>(q);
+        ptrs[dev].store(p, std::memory_order_release);
+    }
+    return p;
+}
+
+// A queue for one launch on `stream`, or null (static row ranges) when the
+// stream is being captured: a graph would replay the same slot forever.
+unsigned int* tile_queue(int dev, cudaStream_t stream) {
+    static std::atomic<unsigned int> seq[64];
+    if (dev < 0 || dev >= 64) return nullptr;
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(stream, &cs) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    if (cs != cudaStreamCaptureStatusNone) return nullptr;
+    unsigned int* base = tile_slots(dev);
+    if (!base) return nullptr;
+    return base + 2u * (seq[dev].fetch_add(1u, std::memory_order_relaxed) % kTileSlots);
+}
+
+// MINB: CTAs per SM the kernel's registers and shared memory are sized for;
+// cps: CTAs per SM actually launched (cps < MINB leaves room on every SM for
+// the next kernel in the stream to start its weight stream early).
 template <int F, int MT, int RPW, int MINB, bool INT>
-cudaError_t launch_stream_t(GemvArgs args, int sm_count, int smem_per_sm, cudaStream_t stream) {
+cudaError_t launch_stream_t(GemvArgs args, int sm_count, int smem_per_sm, cudaStream_t stream,
+                            int cps = MINB) {
     using C = GemvCfg<F, MT, RPW, INT>;
     // Per-CTA budget: the SM's shared memory split MINB ways, minus the 1 KB
     // the driver reserves per CTA, this kernel's static shared memory
@@ -861,9 +957,15 @@ cudaError_t launch_stream_t(GemvArgs args, int sm_count, int smem_per_sm, cudaSt
                     (uint32_t)C::BOXW, 8u, CU_TENSOR_MAP_SWIZZLE_NONE))
         args.tma2d = 1;
     const long long units = (args.out + 7) / 8;  // rows are handed out 8 at a time
-    const long long want = (long long)sm_count * MINB;
+    const long long want = (long long)sm_count * cps;
     int grid = (int)(units < want ? units : want);
     if (grid < 1) grid = 1;  // a rank holding no rows still runs the handshake
+    // Dynamic tiles only pay with many tiles per CTA: with few, whole CTAs
+    // would sit idle at the end and each queue ticket's latency shows.
+    args.tiles = nullptr;
+    if (INT && args.x_resident && args.ny == 1 && args.world == 1 &&
+        (args.out + C::RT - 1) / C::RT >= 8LL * grid)
+        args.tiles = tile_queue(dev, stream);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kThreads);

@@ -25,6 +25,7 @@ struct GemvArgs {
     int* err;                // device error flag
     int tma2d;               // weights streamed by 2-D tensor map (set by the launcher)
     int x_resident;          // ktiles <= nstages: x tiles built once, kept for every row tile
+    unsigned int* tiles;     // dynamic row-tile queue {next, done} of this launch, or null
     // sharded calls only (world > 1): completion handshake
     int world, rank;
     uint32_t epoch;
