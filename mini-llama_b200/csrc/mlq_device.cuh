@@ -55,7 +55,8 @@ __device__ __forceinline__ float half_bits_to_float(uint32_t bits16) {
 // Error reporting from kernels.  A kernel that gives up (a bounded wait ran
 // out) records a code here and returns; the host reads it back with
 // mlq_device_error().  Codes: 1 = pipeline "full" wait, 2 = "empty" wait,
-// 3 = drain wait, 4 = peer flag wait, 5 = consumer rendezvous.
+// 3 = drain wait, 4 = peer flag wait, 5 = consumer rendezvous, 6 = x-tile
+// "empty" wait, 7 = resident x tiles ready wait, 12-16 = GEMM waits.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void report_error(int* err, int code) {
     if (err) atomicCAS(err, 0, code);
@@ -147,6 +148,11 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
         "[%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar)
         : "memory");
+}
+
+// Hint: bring [src, src + bytes) into L2 (16-B aligned, bytes % 16 == 0).
+__device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 
 // Programmatic dependent launch.  A kernel launched with programmatic

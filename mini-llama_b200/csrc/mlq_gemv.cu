@@ -338,6 +338,18 @@ __global__ void __launch_bounds__(kThreads, MINB)
 
     if (warp == 0) {
         // ------------------------------ producer ------------------------------
+        // x into L2 ahead of the weight stream: the first CTAs each take a
+        // 4 KB chunk.  Only a hint -- the x loads proper come after the grid
+        // dependency, so a producer kernel still writing x is harmless.
+        {
+            const long long xbytes = (long long)a.M * a.in * 4;
+            const long long nchunk = (xbytes + 4095) / 4096;
+            if (lane == 0 && blockIdx.x < nchunk) {
+                const long long off = (long long)blockIdx.x * 4096;
+                const long long len = min(4096LL, xbytes - off);
+                prefetch_l2(reinterpret_cast<const uint8_t*>(a.x) + off, (uint32_t)len);
+            }
+        }
         uint32_t seq = 0;
         int s = 0;
         uint32_t ph = 0;
@@ -355,6 +367,12 @@ __global__ void __launch_bounds__(kThreads, MINB)
             }
             const int nrows = (int)min((long long)C::RT, (dyn ? (long long)a.out : r_end) - row0);
             for (int kt = 0; kt < a.ktiles; ++kt, ++seq) {
+                // resident integer mode: one stage in flight until the x tiles
+                // are built, so the x loads do not queue behind the weights
+                if (INT && xres && seq == 1 && !mbar_wait(smem_u32(&xready_bar), 0u)) {
+                    report_error(a.err, 7);
+                    abort_flag = 1;
+                }
                 const uint32_t fb = smem_u32(&full_bar[s]);
                 if (!mbar_wait(smem_u32(&empty_bar[s]), ph ^ 1u)) {
                     report_error(a.err, 2);
