@@ -102,6 +102,10 @@ MLQ_API mlq_status mlq_linear(mlq_format fmt, const void* w, size_t block_count,
                               int out_features, int in_features, const float* x, int rows,
                               float* y, mlq_stream stream);
 
+/* Calls with at least this many rows of x take the tensor-core (tcgen05)
+ * GEMM; fewer rows take the streaming GEMV. */
+#define MLQ_GEMM_MIN_ROWS 16
+
 /* mlq_linear that never allocates device memory.  No counterpart in the
  * reference (its GPU linear cudaMallocs its output on every call,
  * src/cuda_quant.cu:333-361).
@@ -113,9 +117,10 @@ MLQ_API mlq_status mlq_linear(mlq_format fmt, const void* w, size_t block_count,
  * its per-stream workspace by free + malloc when a larger shape arrives).
  *
  * Same arguments, results and validation as mlq_linear.  The tensor-core
- * path (rows >= 64) keeps the bf16 hi/lo split of x in a static
- * MLQ_NOALLOC_SCRATCH_BYTES array of the library's device module instead of
- * a workspace; so rows >= 64 with rows * in_features * 4 bytes above that
+ * path (rows >= MLQ_GEMM_MIN_ROWS) keeps the bf16 hi/lo split of x in a
+ * static MLQ_NOALLOC_SCRATCH_BYTES array of the library's device module
+ * instead of a workspace; so rows >= MLQ_GEMM_MIN_ROWS with
+ * rows * in_features * 4 bytes above that
  * size returns MLQ_ERR_RANGE before any CUDA call.  The array is one per
  * device, shared by every call: calls ordered on one stream are fine,
  * calls whose kernels may overlap (several streams, several host threads)

@@ -1,5 +1,5 @@
 // mlq_gemm.cu -- dequant-fused GEMM on the 5th-generation tensor cores
-// (tcgen05 + TMEM) for prefill / batched rows of x (rows >= 64).
+// (tcgen05 + TMEM) for prefill / batched rows of x (rows >= MLQ_GEMM_MIN_ROWS = 16).
 //
 // The reference has no GEMM for quantized weights: forwardBatch loops the
 // GEMV one token at a time (src/batch.cc:32-55) and linearQ* loops rows
@@ -33,6 +33,7 @@
 
 #include <mutex>
 
+#include "mlq.h"
 #include "mlq_device.cuh"
 #include "mlq_kernels.h"
 #include "mlq_tmap.h"
@@ -436,7 +437,7 @@ cudaError_t launch_gemm_t(const uint8_t* w, const float* x, float* y, int out, i
 bool gemm_supported(int fmt, const void* w, int out, int in, int rows) {
     (void)out;
     const long long row_bytes = (long long)((in + kQK - 1) / kQK) * block_bytes(fmt);
-    return rows >= 64 && reinterpret_cast<uintptr_t>(w) % 16 == 0 && row_bytes % 16 == 0 &&
+    return rows >= MLQ_GEMM_MIN_ROWS && reinterpret_cast<uintptr_t>(w) % 16 == 0 && row_bytes % 16 == 0 &&
            in % 8 == 0 && encode_fn() != nullptr;
 }
 

@@ -138,13 +138,14 @@ def linear_raw(fmt, w_ptr: int, nblocks: int, out_features: int, in_features: in
                            y_ptr, stream))
 
 
-# MLQ_NOALLOC_SCRATCH_BYTES of include/mlq.h
+# MLQ_NOALLOC_SCRATCH_BYTES and MLQ_GEMM_MIN_ROWS of include/mlq.h
 NOALLOC_SCRATCH_BYTES = 16 << 20
+GEMM_MIN_ROWS = 16
 
 
 def linear_noalloc(fmt, w, out_features: int, in_features: int, x, y, stream=None):
     """mlq_linear_noalloc: like linear() but the library allocates no device
-    memory (the caller passes y; rows >= 64 need rows * in * 4 bytes <=
+    memory (the caller passes y; rows >= GEMM_MIN_ROWS need rows * in * 4 bytes <=
     NOALLOC_SCRATCH_BYTES)."""
     rows = 1 if x.dim() == 1 else x.shape[0]
     nb = w.numel() // BLOCK_BYTES[_fmt_name(fmt)]

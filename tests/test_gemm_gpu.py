@@ -1,4 +1,4 @@
-"""The tensor-core GEMM path (rows of x >= 64) against the CPU oracle.
+"""The tensor-core GEMM path (rows of x >= 16) against the CPU oracle.
 
 Same contract as the GEMV: relative L2 error of every output row <= 1e-3.
 The bf16x3 split keeps the GEMM within ~1e-5 of fp32, so the tests also
@@ -33,6 +33,9 @@ CASES = [
     ("q4_1", 129, 96, 65),       # in: one full and one partial 64-wide K-step
     ("q8_0", 384, 1280, 256),    # in: 5 K-chunks of 256
     ("q4_1", 640, 4160, 96),     # in % 256 = 64
+    ("q8_0", 512, 4096, 16),     # smallest GEMM row count (batched decode)
+    ("q4_0", 300, 2048, 20),
+    ("q4_1", 256, 1024, 33),
 ]
 
 
