@@ -625,7 +625,11 @@ __global__ void __launch_bounds__(kThreads, MINB)
             uint32_t wv[RPW][C::WPG];
 #pragma unroll
             for (int r = 0; r < RPW; ++r) {
-                if (row_on[r] && lane_on) {
+                // 2-D boxes need no guard: bytes past a row's end arrive as
+                // zeros (tensor-map bounds), and rows past the tile hold stale
+                // but finite-or-not data that only feeds that row's discarded
+                // sum (rows never mix in the reduction)
+                if (a.tma2d || (row_on[r] && lane_on)) {
 #pragma unroll
                     for (int j = 0; j < C::WPG; ++j) wv[r][j] = lds_u32(stage + soff[r] + 4 * j);
                 } else {
