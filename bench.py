@@ -436,7 +436,7 @@ def run_mlq(args):
                        "weight_bytes_per_step": bytes_step,
                        "placement": PLACEMENT if world > 1 else "all on one GPU",
                        "l2": "inputs larger than L2 (437.6 MB per step vs 126 MB L2); no flush"},
-            "roofline": {"bound": "hbm", "kernel": f"gemv_stream_kernel<q4_0,1,4,2> ({dom} launch, rank 0)",
+            "roofline": {"bound": "hbm", "kernel": f"gemv_stream_kernel<q4_0,MT=1,RPW=4,MINB=2,INT> integer mode ({dom} launch, rank 0)",
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                          "traffic": traffic, "algorithmic_bytes_per_launch": dom_bytes,
