@@ -824,12 +824,16 @@ __global__ void __launch_bounds__(kThreads, MINB)
                 report_error(a.err, 5);
                 return;
             }
-            __threadfence_system();
-            const unsigned int prev = atomicAdd(a.done_counter, 1u);
+            // Ordering without system-wide fences per CTA: this CTA's y stores
+            // (local and peer) happen before this point (tile_bar, CTA scope);
+            // the GPU-scope acquire-release count carries them to the last CTA,
+            // whose one system-scope release fence then publishes every CTA's
+            // stores ahead of the epoch flags (the fence is cumulative).
+            const unsigned int prev = atom_add_acq_rel_gpu(a.done_counter, 1u);
             if (prev == gridDim.x - 1) {
                 *a.done_counter = 0u;  // every CTA of this launch has counted
-                __threadfence_system();
-                for (int r = 0; r < a.world; ++r) st_release_sys(a.peer_flags[r] + a.rank, a.epoch);
+                fence_acq_rel_sys();
+                for (int r = 0; r < a.world; ++r) st_relaxed_sys(a.peer_flags[r] + a.rank, a.epoch);
                 const uint64_t t0 = global_ns();
                 for (int r = 0; r < a.world; ++r) {
                     while ((int)(ld_acquire_sys(a.local_flags + r) - a.epoch) < 0) {
