@@ -34,14 +34,36 @@ ROOT = Path(__file__).resolve().parent
 PKG_DIR = ROOT / "mini-llama_b200"
 MB = 1_000_000
 
-WORKLOAD = {
-    "name": "qwen2-7b-layer+lm_head q4_0 decode (BASELINE configs[1])",
-    "fmt": "q4_0",
-    "rows": 1,
-    "matrices": [("qkv", 4608, 3584), ("o", 3584, 3584), ("gate", 18944, 3584),
-                 ("up", 18944, 3584), ("down", 3584, 18944), ("lm_head", 152064, 3584)],
+# The bench line's workload is BASELINE configs[1]; --workload picks one of
+# the other decode configs for scaling studies (configs[4]: 70B-shaped shards).
+WORKLOADS = {
+    "qwen7b": {
+        "name": "qwen2-7b-layer+lm_head q4_0 decode (BASELINE configs[1])",
+        "metric": "effective weight GB/s (q4_0 decode GEMV, Qwen2-7B layer + lm_head, batch 1)",
+        "fmt": "q4_0",
+        "rows": 1,
+        "matrices": [("qkv", 4608, 3584), ("o", 3584, 3584), ("gate", 18944, 3584),
+                     ("up", 18944, 3584), ("down", 3584, 18944), ("lm_head", 152064, 3584)],
+    },
+    "llama70b": {
+        "name": "llama-3-70b FFN + lm_head q4_0 decode shards, batch 1 (BASELINE configs[4])",
+        "metric": "effective weight GB/s (q4_0 decode GEMV, Llama-3-70B FFN + lm_head, batch 1)",
+        "fmt": "q4_0",
+        "rows": 1,
+        "matrices": [("gate", 28672, 8192), ("up", 28672, 8192), ("down", 8192, 28672),
+                     ("lm_head", 128256, 8192)],
+    },
+    "llama70b-b8": {
+        "name": "llama-3-70b FFN + lm_head q4_0 decode shards, batch 8 (BASELINE configs[4])",
+        "metric": "effective weight GB/s (q4_0 decode GEMV, Llama-3-70B FFN + lm_head, batch 8)",
+        "fmt": "q4_0",
+        "rows": 8,
+        "matrices": [("gate", 28672, 8192), ("up", 28672, 8192), ("down", 8192, 28672),
+                     ("lm_head", 128256, 8192)],
+    },
 }
-METRIC = "effective weight GB/s (q4_0 decode GEMV, Qwen2-7B layer + lm_head, batch 1)"
+WORKLOAD = WORKLOADS["qwen7b"]
+METRIC = WORKLOAD["metric"]
 UNIT = "GB/s"
 
 
@@ -370,7 +392,7 @@ def run_mlq(args):
     dom, dom_bytes = mats[dj][0], local_bytes(dj)
     achieved = dom_bytes / (per[dom] / 1e3) / 1e9
     kernel_sum_ms = sum(per.values())
-    traffic = read_traffic() if world == 1 else None
+    traffic = read_traffic() if world == 1 and WORKLOAD["name"] == WORKLOADS["qwen7b"]["name"] and dom == "lm_head" else None
 
     # ---- e2e: host x / host y around every call, copies inside the timed region ----
     e2e = None
@@ -435,8 +457,8 @@ def run_mlq(args):
                        "matrices": {n: [o, i] for n, o, i in mats},
                        "weight_bytes_per_step": bytes_step,
                        "placement": PLACEMENT if world > 1 else "all on one GPU",
-                       "l2": "inputs larger than L2 (437.6 MB per step vs 126 MB L2); no flush"},
-            "roofline": {"bound": "hbm", "kernel": f"gemv_stream_kernel<q4_0,MT=1,RPW=4,MINB=2,INT> integer mode ({dom} launch, rank 0)",
+                       "l2": f"inputs larger than L2 ({bytes_step / 1e6:.1f} MB per step vs 126 MB L2); no flush"},
+            "roofline": {"bound": "hbm", "kernel": (f"gemv_stream_kernel<{fmt}, MT={rows}, integer mode>" if rows == 1 else f"gemv_stream_kernel<{fmt}, MT={min(rows, 8)}, fp32 mode>" if rows < 16 else f"gemm_tc_kernel<{fmt}>") + f" ({dom} launch, rank 0)",
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                          "traffic": traffic, "algorithmic_bytes_per_launch": dom_bytes,
@@ -522,7 +544,12 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--only", default=None,
                     help="run one matrix of the workload (qkv/o/gate/up/down/lm_head), for profiling")
+    ap.add_argument("--workload", default="qwen7b", choices=sorted(WORKLOADS),
+                    help="qwen7b (default, the bench line) or a 70B-shaped scaling study")
     args = ap.parse_args()
+    global WORKLOAD, METRIC
+    WORKLOAD = dict(WORKLOADS[args.workload])
+    METRIC = WORKLOAD["metric"]
     if args.only:
         WORKLOAD["matrices"] = [m for m in WORKLOAD["matrices"] if m[0] == args.only]
         if not WORKLOAD["matrices"]:

@@ -330,10 +330,10 @@ __global__ void __launch_bounds__(kThreads, MINB)
     const uintptr_t wbase = reinterpret_cast<uintptr_t>(a.w);
     const uintptr_t wend16 = (wbase + (uintptr_t)a.total_bytes) & ~(uintptr_t)15;
 
-    // Dynamic tiles (one token, resident x, plain call): CTAs take row tiles
+    // Dynamic tiles (one token, resident x, many tiles): CTAs take row tiles
     // from a global queue instead of a fixed row range, so SMs that stream
     // faster do more tiles and all CTAs finish together.
-    const bool dyn = INT && xres && a.tiles != nullptr && a.ny == 1 && a.world == 1;
+    const bool dyn = INT && xres && a.tiles != nullptr;
     const long long ntiles_all = (a.out + C::RT - 1) / C::RT;
 
     if (warp == 0) {
@@ -571,7 +571,8 @@ __global__ void __launch_bounds__(kThreads, MINB)
     for (int p = 0; p < 8; ++p) xoff[p] = INT ? xcol<C::G>(lane, p & (2 * C::G - 1)) : (uint32_t)((lane ^ p) * 16);
     int s = 0;
     uint32_t ph = 0;
-    for (int t = 0; dyn || t < ntiles; ++t) {
+    int t = 0;  // after the loop: the tiles this CTA processed
+    for (; dyn || t < ntiles; ++t) {
         long long row0;
         if (dyn) {
             // the tile's first stage names its rows
@@ -820,7 +821,7 @@ __global__ void __launch_bounds__(kThreads, MINB)
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(&tile_bar));
         if (threadIdx.x == 32) {
-            if (!mbar_wait(smem_u32(&tile_bar), (uint32_t)ntiles & 1u)) {
+            if (!mbar_wait(smem_u32(&tile_bar), (uint32_t)t & 1u)) {
                 report_error(a.err, 5);
                 return;
             }
@@ -989,7 +990,7 @@ cudaError_t launch_stream_t(GemvArgs args, int sm_count, int smem_per_sm, cudaSt
     // Dynamic tiles only pay with many tiles per CTA: with few, whole CTAs
     // would sit idle at the end and each queue ticket's latency shows.
     args.tiles = nullptr;
-    if (INT && args.x_resident && args.ny == 1 && args.world == 1 &&
+    if (INT && args.x_resident &&
         (args.out + C::RT - 1) / C::RT >= 8LL * grid)
         args.tiles = tile_queue(dev, stream);
     cudaLaunchConfig_t cfg = {};
