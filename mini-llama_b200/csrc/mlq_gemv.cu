@@ -57,8 +57,11 @@ __device__ unsigned int g_gemv_tile_slots[2 * kTileSlots];
 namespace {
 
 constexpr int kConsumerWarps = 8;
-constexpr int kXWarp = 1 + kConsumerWarps;  // warp 9 builds the x tiles
-constexpr int kThreads = 32 * (2 + kConsumerWarps);
+constexpr int kXWarp = 1 + kConsumerWarps;  // warps 9.. build the x tiles
+// x-loader warps: one; four for eight tokens (a stage's x tile is then
+// 64 KB, more than one warp turns around in a consumer's stage time)
+constexpr int xw_for(int mt) { return mt >= 8 ? 4 : 1; }
+constexpr int threads_for(int mt) { return 32 * (1 + kConsumerWarps + xw_for(mt)); }
 constexpr int kMaxStages = 8;
 
 template <int F, int MT, int RPW, bool INT>
@@ -283,7 +286,7 @@ __device__ __forceinline__ float reduce_rows(float (&v)[RPW][MT], int lane) {
 }
 
 template <int F, int MT, int RPW, int MINB, bool INT>
-__global__ void __launch_bounds__(kThreads, MINB)
+__global__ void __launch_bounds__(threads_for(MT), MINB)
     gemv_stream_kernel(GemvArgs a, const __grid_constant__ CUtensorMap wmap) {
     using C = GemvCfg<F, MT, RPW, INT>;
     extern __shared__ __align__(128) uint8_t smem[];
@@ -306,7 +309,7 @@ __global__ void __launch_bounds__(kThreads, MINB)
         for (int s = 0; s < kMaxStages; ++s) {
             mbar_init(smem_u32(&full_bar[s]), 32);
             mbar_init(smem_u32(&empty_bar[s]), kConsumerWarps);
-            mbar_init(smem_u32(&xfull_bar[s]), 1);
+            mbar_init(smem_u32(&xfull_bar[s]), xw_for(MT));
             mbar_init(smem_u32(&xempty_bar[s]), kConsumerWarps);
         }
         mbar_init(smem_u32(&tile_bar), kConsumerWarps);
@@ -485,7 +488,7 @@ __global__ void __launch_bounds__(kThreads, MINB)
         if (warp == kXWarp) return;
     }
 
-    if (warp == kXWarp) {
+    if (warp >= kXWarp) {
         // ------------------------------ x loader ------------------------------
         // Per K-tile: x for MT tokens with coalesced 128-bit loads (all in
         // flight together), per-block sums by shuffles, stored in the order
@@ -520,7 +523,7 @@ __global__ void __launch_bounds__(kThreads, MINB)
                 } else {
                     constexpr int NV = C::KTE / 128;  // float4 loads per lane per token
 #pragma unroll 1
-                    for (int m = 0; m < MT; ++m) {
+                    for (int m = warp - kXWarp; m < MT; m += xw_for(MT)) {
                         const float* xr = a.x + (long long)m * a.in;
                         float4 v[NV];
 #pragma unroll
@@ -995,7 +998,7 @@ cudaError_t launch_stream_t(GemvArgs args, int sm_count, int smem_per_sm, cudaSt
         args.tiles = tile_queue(dev, stream);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3(threads_for(MT));
     cfg.dynamicSmemBytes = (size_t)smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
@@ -1029,7 +1032,12 @@ cudaError_t dispatch_mt(const GemvArgs& args, int sm_count, int smem_per_sm, cud
             return launch_stream_t<F, 1, RPW, 1, true>(args, sm_count, smem_per_sm, stream);
         return launch_stream_t<F, 1, RPW, 2, true>(args, sm_count, smem_per_sm, stream);
     } else {
-        return launch_stream_t<F, MT, RPW, MINB, false>(args, sm_count, smem_per_sm, stream);
+        // fp32 mode, measured per token count (q4_0 28672 x 8192): 2 tokens
+        // and 8 tokens run best with two rows per warp (fewer live
+        // accumulators; 8 tokens also need the four x-loader warps' registers),
+        // 4 tokens with four.
+        constexpr int RPW_FP = (MT == 4 || RPW < 4) ? RPW : RPW / 2;
+        return launch_stream_t<F, MT, RPW_FP, MINB, false>(args, sm_count, smem_per_sm, stream);
     }
 }
 
