@@ -392,6 +392,25 @@ def run_mlq(args):
     dom, dom_bytes = mats[dj][0], local_bytes(dj)
     achieved = dom_bytes / (per[dom] / 1e3) / 1e9
     kernel_sum_ms = sum(per.values())
+    # the dominant matrix alone, R launches back to back between two events
+    # (consecutive launches overlap as in the step; the isolated per-launch
+    # figure above includes each launch's ramp and drain)
+    rb = 50
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        b0.record(stream)
+        for _ in range(rb):
+            calls[dj]()
+        b1.record(stream)
+    b1.synchronize()
+    b2b_ms = b0.elapsed_time(b1) / rb
+    if world > 1:
+        tm = torch.tensor([b2b_ms], device=device)
+        dist.all_reduce(tm, op=dist.ReduceOp.MAX)
+        b2b_ms = float(tm.item())
     traffic = read_traffic() if world == 1 and WORKLOAD["name"] == WORKLOADS["qwen7b"]["name"] and dom == "lm_head" else None
 
     # ---- e2e: host x / host y around every call, copies inside the timed region ----
@@ -463,6 +482,8 @@ def run_mlq(args):
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                          "traffic": traffic, "algorithmic_bytes_per_launch": dom_bytes,
                          "launch_ms": round(per[dom], 5),
+                         "launch_ms_back_to_back": round(b2b_ms, 5),
+                         "achieved_back_to_back": round(dom_bytes / (b2b_ms / 1e3) / 1e9, 1),
                          "all_launches_GBps": round(sum(local_bytes(j) for j in range(len(mats))
                                                         if calls[j] is not None)
                                                     / (kernel_sum_ms / 1e3) / 1e9, 1),
