@@ -42,16 +42,23 @@ namespace mlq {
 namespace {
 
 constexpr int BM = 128;       // W rows per tile = MMA M = TMEM lanes
-constexpr int BN = 128;       // tokens per tile = MMA N = TMEM columns
+// Tokens per tile (MMA N, TMEM columns) is a template parameter NT: 16, 32,
+// 64 or 128, the smallest that covers the call's rows of x (up to 128), so
+// a batched-decode call does not run 128-wide MMAs on 16 real columns.
 constexpr int BK = 64;        // K per stage: one 128-byte swizzle row of bf16
 constexpr int KW = 256;       // K per packed-W chunk (8 blocks per row)
 constexpr int KSUB = KW / BK; // stages per W chunk
-constexpr int AB_STAGES = 2;
+// A/B stages: 2 at N = 128 (64 KB each); 4 for narrow tiles, whose B
+// half is small, to keep more K-steps of decoded A in flight.
+constexpr int ab_stages_for(int nt) { return nt <= 32 ? 4 : 2; }
 constexpr int W_STAGES = 2;
-constexpr int kGemmThreads = 192;
-constexpr uint32_t kTmemCols = 128;
+constexpr int kRowWarps = 8;  // warps 2..9: two per TMEM lane quarter, one K-step block each
+constexpr int kGemmThreads = 32 * (2 + kRowWarps);
+constexpr uint32_t tmem_cols_for(int nt) { return nt < 32 ? 32u : (uint32_t)nt; }  // power of 2, >= 32
 
-template <int F>
+constexpr int kGemmSmemMax = 232448;  // dynamic shared memory per CTA (227 KB)
+
+template <int F, int NT>
 struct GemmCfg {
     static constexpr int BS = Fmt<F>::kBlockBytes;
     static constexpr int W_ROW = (KW / kQK) * BS;  // bytes of one row's chunk: 272 / 144 / 160
@@ -59,9 +66,13 @@ struct GemmCfg {
     static constexpr int W_TILE = BM * W_ROW;
     static constexpr int W_SLOT = (W_TILE + 1023) / 1024 * 1024;
     static constexpr int A_TILE = BM * BK * 2;  // bf16
-    static constexpr int B_TILE = BN * BK * 2;
+    static constexpr int B_TILE = NT * BK * 2;
     static constexpr int AB_STAGE = 2 * A_TILE + 2 * B_TILE;  // A hi, A lo, B hi, B lo
+    static constexpr int AB_FIT = (kGemmSmemMax - W_STAGES * W_SLOT - 1024) / AB_STAGE;
+    static constexpr int AB_STAGES = ab_stages_for(NT) < AB_FIT ? ab_stages_for(NT) : AB_FIT;
     static constexpr int SMEM = AB_STAGES * AB_STAGE + W_STAGES * W_SLOT + 1024;  // + align slack
+    static_assert(AB_STAGES >= 2 && SMEM <= kGemmSmemMax, "GEMM stages must fit shared memory");
+    static_assert(AB_STAGE % 1024 == 0 && W_SLOT % 1024 == 0, "SW128 atoms need 1024-B aligned tiles");
     static_assert(W_ROW % 16 == 0, "W chunk row must be 16-byte granular");
 };
 
@@ -85,11 +96,14 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
 }
 
 // kind::f16 instruction descriptor: D f32, A/B bf16, both K-major, M x N.
-constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
-                            ((uint32_t)(BM >> 4) << 24);
+constexpr uint32_t idesc_for(int nt) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(nt >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
 
+template <int NT>
 __device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
                                          uint32_t accumulate) {
+    constexpr uint32_t kIdesc = idesc_for(NT);
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
@@ -116,54 +130,69 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// ---- exact decode of 8 consecutive values of a block -----------------------
-// Values e0..e0+7 of the block whose fields are in words wv[] (2-byte
-// aligned block starts are handled by the caller: wv holds the block bytes
-// from its first byte).  Returns the fp32 values w (reference dequant).
-__device__ __forceinline__ uint32_t byte_of(const uint32_t* wv, int i) {
-    return (wv[i >> 2] >> ((i & 3) * 8)) & 0xFFu;
+// ---- exact decode of one block into bf16 hi/lo pairs --------------------------
+// bw[] holds the block's bytes from its first byte (word 0 = its first 4
+// bytes).  Writes the 32 values w (the reference's dequantized fp32 values,
+// exactly) as 16 bf16x2 words hi[] and lo[] with w = hi + lo to ~2^-17:
+//   q4_0:  w = d*(q-8) = fma(128+q, d, -136d)      (128+q by a byte permute
+//          into the mantissa of 128.0f; 136d and the product are exact)
+//   q4_1:  w = fma(d, q, m)                         (d*q exact, one rounding,
+//          the same value as the reference's d*q + m)
+//   q8_0:  w = d*q                                  (exact)
+__device__ __forceinline__ void split_pair(float w0, float w1, uint32_t& h, uint32_t& l) {
+    const __nv_bfloat162 hb = __floats2bfloat162_rn(w0, w1);
+    h = *reinterpret_cast<const uint32_t*>(&hb);
+    const float h0 = __uint_as_float(h << 16), h1 = __uint_as_float(h & 0xFFFF0000u);
+    const __nv_bfloat162 lb = __floats2bfloat162_rn(w0 - h0, w1 - h1);
+    l = *reinterpret_cast<const uint32_t*>(&lb);
 }
 
 template <int F>
-__device__ __forceinline__ void decode8(const uint32_t* bw, int e0, float out[8]) {
+__device__ __forceinline__ void decode_block_bf16(const uint32_t* bw, uint32_t hi[16], uint32_t lo[16]) {
     const float d = half_bits_to_float(bw[0] & 0xFFFFu);
     if constexpr (F == kQ8_0) {
+        // bytes 2..33: value e at byte 2+e
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const uint32_t b = byte_of(bw, 2 + e0 + i) ^ 0x80u;
-            const float q = __uint_as_float(0x4B000000u | b) - 8388736.0f;  // exact int8 code
-            out[i] = __fmul_rn(d, q);
-        }
-    } else if constexpr (F == kQ4_0) {
+        for (int j = 0; j < 8; ++j) {  // values 4j..4j+3
+            const uint32_t word = __funnelshift_r(bw[j], bw[j + 1], 16) ^ 0x80808080u;
+            float w[4];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const int e = e0 + i;
-            const uint32_t b = byte_of(bw, 2 + (e & 15));
-            const uint32_t q = e < 16 ? (b & 15u) : (b >> 4);
-            out[i] = __fmul_rn(d, __uint_as_float(0x4B000000u | q) - 8388616.0f);  // q - 8
+            for (int u = 0; u < 4; ++u)
+                w[u] = __fmul_rn(d, __uint_as_float(__byte_perm(word, 0x4B000000u, 0x7540 + u)) - 8388736.0f);
+            split_pair(w[0], w[1], hi[2 * j], lo[2 * j]);
+            split_pair(w[2], w[3], hi[2 * j + 1], lo[2 * j + 1]);
         }
     } else {
-        const float m = half_bits_to_float(bw[0] >> 16);
+        constexpr int QS = F == kQ4_0 ? 2 : 4;  // first qs byte
+        const float mn = F == kQ4_1 ? half_bits_to_float(bw[0] >> 16) : 0.0f;
+        const float c = -136.0f * d;  // q4_0: exact (8-bit x 11-bit)
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const int e = e0 + i;
-            const uint32_t b = byte_of(bw, 4 + (e & 15));
-            const uint32_t q = e < 16 ? (b & 15u) : (b >> 4);
-            out[i] = __fmaf_rn(d, __uint_as_float(0x4B000000u | q) - 8388608.0f, m);  // d*q + m
+        for (int j = 0; j < 4; ++j) {  // qs word j: values 4j..4j+3 (low nibbles), 16+4j.. (high)
+            const uint32_t qw = QS == 2 ? __funnelshift_r(bw[j], bw[j + 1], 16) : bw[1 + j];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const uint32_t nib = (h ? (qw >> 4) : qw) & 0x0F0F0F0Fu;
+                float w[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const float f = __uint_as_float(__byte_perm(nib, 0x43000000u, 0x7044 + 0x100 * u));  // 128 + q
+                    w[u] = F == kQ4_0 ? __fmaf_rn(f, d, c) : __fmaf_rn(d, f - 128.0f, mn);
+                }
+                const int e2 = (16 * h + 4 * j) / 2;  // pair index of value 16h + 4j
+                split_pair(w[0], w[1], hi[e2], lo[e2]);
+                split_pair(w[2], w[3], hi[e2 + 1], lo[e2 + 1]);
+            }
         }
     }
 }
 
-__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
-    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
-    return *reinterpret_cast<uint32_t*>(&v);
-}
-
-template <int F>
+template <int F, int NT>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_xh,
                    const __grid_constant__ CUtensorMap tm_xl, GemmArgs a) {
-    using C = GemmCfg<F>;
+    using C = GemmCfg<F, NT>;
+    constexpr int AB_STAGES = C::AB_STAGES;
+    constexpr uint32_t kTmemCols = tmem_cols_for(NT);
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     __shared__ __align__(8) uint64_t ab_full[AB_STAGES], ab_empty[AB_STAGES];
     __shared__ __align__(8) uint64_t w_full[W_STAGES], w_empty[W_STAGES];
@@ -182,15 +211,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < AB_STAGES; ++s) {
-            mbar_init(smem_u32(&ab_full[s]), 1 + 4);  // producer (B bytes) + 4 row warps (A)
+            mbar_init(smem_u32(&ab_full[s]), 1 + kRowWarps);  // producer (B bytes) + row warps (A)
             mbar_init(smem_u32(&ab_empty[s]), 1);     // tcgen05.commit
         }
         for (int s = 0; s < W_STAGES; ++s) {
             mbar_init(smem_u32(&w_full[s]), 1);
-            mbar_init(smem_u32(&w_empty[s]), 4);
+            mbar_init(smem_u32(&w_empty[s]), kRowWarps);
         }
         mbar_init(smem_u32(&acc_full), 1);
-        mbar_init(smem_u32(&acc_empty), 4);
+        mbar_init(smem_u32(&acc_empty), kRowWarps);
         abort_flag = 0;
         fence_mbar_init();
     }
@@ -206,7 +235,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tc_fence_after();
     const uint32_t tmem = tmem_base_s;
 
-    const int tiles_n = (a.T + BN - 1) / BN;
+    const int tiles_n = (a.T + NT - 1) / NT;
     const int tiles_m = (a.out + BM - 1) / BM;
     const int ntiles = tiles_m * tiles_n;
     const int KS = (a.in + BK - 1) / BK;
@@ -237,8 +266,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         break;
                     }
                     mbar_arrive_expect_tx(smem_u32(&ab_full[s]), 2u * C::B_TILE);
-                    tma_load_2d(b_hi(s), &tm_xh, ks * BK, nt * BN, smem_u32(&ab_full[s]));
-                    tma_load_2d(b_lo(s), &tm_xl, ks * BK, nt * BN, smem_u32(&ab_full[s]));
+                    tma_load_2d(b_hi(s), &tm_xh, ks * BK, nt * NT, smem_u32(&ab_full[s]));
+                    tma_load_2d(b_lo(s), &tm_xl, ks * BK, nt * NT, smem_u32(&ab_full[s]));
                 }
             }
         }
@@ -267,9 +296,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
                     for (int k = 0; k < BK / 16; ++k) {
                         const uint64_t adv = (uint64_t)(k * 32) >> 4;  // 16 bf16 = 32 B along K
-                        mma_bf16(tmem, dah + adv, dbh + adv, (ks | k) != 0);
-                        mma_bf16(tmem, dah + adv, dbl + adv, 1u);
-                        mma_bf16(tmem, dal + adv, dbh + adv, 1u);
+                        mma_bf16<NT>(tmem, dah + adv, dbh + adv, (ks | k) != 0);
+                        mma_bf16<NT>(tmem, dah + adv, dbl + adv, 1u);
+                        mma_bf16<NT>(tmem, dal + adv, dbh + adv, 1u);
                     }
                     mma_commit(smem_u32(&ab_empty[s]));  // stage free once these MMAs finish
                 }
@@ -285,7 +314,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                      : "memory");
     } else {
         // --------------------- row threads: decode A, epilogue ---------------------
+        // Two warps per TMEM lane quarter: `half` 0 decodes block 0 of each
+        // 64-wide K-step and reads accumulator columns 0..63, half 1 block 1
+        // and columns 64..127.
         const int quarter = warp & 3;          // TMEM lanes 32*quarter .. +31
+        const int half = (warp - 2) >> 2;      // 0: warps 2..5, 1: warps 6..9
         const int row = quarter * 32 + lane;   // tile row = TMEM lane
         const uint32_t swz = (uint32_t)(row & 7);
         uint32_t g = 0, gc = 0, tc = 0;
@@ -305,44 +338,32 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     report_error(a.err, 15);
                     return;
                 }
-                // this row's two blocks of the K-step (zero-filled past the matrix)
-                const uint32_t src = w_st(sw) + (uint32_t)(row * C::W_ROW + (ks % KSUB) * 2 * C::BS);
-                constexpr int NW = (2 * C::BS + 3) / 4;
-                uint32_t wv[NW + 1];
+                // this row's block `half` of the K-step (zero-filled past the matrix)
+                const int off = ((ks % KSUB) * 2 + half) * C::BS;  // block's first byte in the row chunk
+                const uint32_t src = w_st(sw) + (uint32_t)(row * C::W_ROW + (off & ~3));
+                // words covering the block from the 4-B boundary below it (18- and
+                // 34-byte blocks start 2 bytes past one half the time); never past
+                // the row chunk's end
+                constexpr int NW = (C::BS + (C::BS % 4 ? 2 : 0) + 3) / 4;
+                uint32_t raw[NW + 1];
 #pragma unroll
-                for (int j = 0; j < NW; ++j) wv[j] = lds_u32(src + 4 * j);
-                wv[NW] = 0;
+                for (int j = 0; j < NW; ++j) raw[j] = lds_u32(src + 4 * j);
+                raw[NW] = 0;
+                uint32_t bw[NW];  // the block's bytes from its first byte
+#pragma unroll
+                for (int j = 0; j < NW; ++j) bw[j] = (off & 3) ? __funnelshift_r(raw[j], raw[j + 1], (off & 3) * 8) : raw[j];
+                uint32_t h[16], l[16];
+                decode_block_bf16<F>(bw, h, l);
                 const uint32_t dst_hi = a_hi(s) + (uint32_t)row * 128u;
                 const uint32_t dst_lo = a_lo(s) + (uint32_t)row * 128u;
 #pragma unroll
-                for (int c = 0; c < 8; ++c) {  // 16-byte chunks of the 64-value row
-                    const int blk = c >> 2;
-                    uint32_t bw[(C::BS + 3) / 4 + 1];
-                    // block `blk` starts at byte blk*BS: realign to word 0
-                    const int off = blk * C::BS;
-#pragma unroll
-                    for (int j = 0; j < (C::BS + 3) / 4 + 1; ++j) {
-                        const int wi = (off >> 2) + j;
-                        const uint32_t lo = wi < NW + 1 ? wv[wi] : 0u;
-                        const uint32_t hi = wi + 1 < NW + 1 ? wv[wi + 1] : 0u;
-                        bw[j] = (off & 3) ? __funnelshift_r(lo, hi, (off & 3) * 8) : lo;
-                    }
-                    float w[8];
-                    decode8<F>(bw, (c & 3) * 8, w);
-                    uint32_t h[4], l[4];
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const __nv_bfloat162 hb = __floats2bfloat162_rn(w[2 * i], w[2 * i + 1]);
-                        const float2 hf = __bfloat1622float2(hb);
-                        h[i] = *reinterpret_cast<const uint32_t*>(&hb);
-                        l[i] = pack_bf16x2(w[2 * i] - hf.x, w[2 * i + 1] - hf.y);
-                    }
-                    const uint32_t cs = (((uint32_t)c ^ swz) << 4);
-                    asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(dst_hi + cs), "r"(h[0]),
-                                 "r"(h[1]), "r"(h[2]), "r"(h[3])
+                for (int c = 0; c < 4; ++c) {  // 16-byte chunks 4*half + c of the 64-value row
+                    const uint32_t cs = ((((uint32_t)(4 * half + c)) ^ swz) << 4);
+                    asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(dst_hi + cs), "r"(h[4 * c]),
+                                 "r"(h[4 * c + 1]), "r"(h[4 * c + 2]), "r"(h[4 * c + 3])
                                  : "memory");
-                    asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(dst_lo + cs), "r"(l[0]),
-                                 "r"(l[1]), "r"(l[2]), "r"(l[3])
+                    asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(dst_lo + cs), "r"(l[4 * c]),
+                                 "r"(l[4 * c + 1]), "r"(l[4 * c + 2]), "r"(l[4 * c + 3])
                                  : "memory");
                 }
                 fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor cores
@@ -360,13 +381,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
             tc_fence_after();
             const int o = mt * BM + row;
+            // 32-column chunks of the accumulator, split between the halves
+            constexpr int NCH = NT < 32 ? 1 : NT / 32;
+            constexpr int PER = NCH >= 2 ? NCH / 2 : 1;
 #pragma unroll 1
-            for (int c = 0; c < BN / 32; ++c) {
+            for (int c = half * PER; c < (half + 1) * PER && c < NCH; ++c) {
                 uint32_t v[32];
                 tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(c * 32), v);
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
-                    const int t = nt * BN + c * 32 + j;
+                    const int t = nt * NT + c * 32 + j;
+                    if (c * 32 + j >= NT) break;
                     if (o < a.out && t < a.T) a.y[(long long)t * a.out + o] = __uint_as_float(v[j]);
                 }
             }
@@ -389,10 +414,10 @@ __global__ void xsplit_kernel(const float* __restrict__ x, long long n, __nv_bfl
     }
 }
 
-template <int F>
+template <int F, int NT>
 cudaError_t launch_gemm_t(const uint8_t* w, const float* x, float* y, int out, int in, int T,
                           void* ws, int sm_count, int* err, cudaStream_t stream) {
-    using C = GemmCfg<F>;
+    using C = GemmCfg<F, NT>;
     __nv_bfloat16* xh = static_cast<__nv_bfloat16*>(ws);
     __nv_bfloat16* xl = xh + (size_t)T * in;
     const long long n = (long long)T * in;
@@ -407,16 +432,16 @@ cudaError_t launch_gemm_t(const uint8_t* w, const float* x, float* y, int out, i
                      (uint64_t)row_bytes, (uint32_t)(C::W_ROW / C::W_ESZ), BM,
                      CU_TENSOR_MAP_SWIZZLE_NONE) ||
         !make_map_2d(&mxh, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, xh, (uint64_t)in, (uint64_t)T,
-                     (uint64_t)in * 2, BK, BN, CU_TENSOR_MAP_SWIZZLE_128B) ||
+                     (uint64_t)in * 2, BK, NT, CU_TENSOR_MAP_SWIZZLE_128B) ||
         !make_map_2d(&mxl, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, xl, (uint64_t)in, (uint64_t)T,
-                     (uint64_t)in * 2, BK, BN, CU_TENSOR_MAP_SWIZZLE_128B))
+                     (uint64_t)in * 2, BK, NT, CU_TENSOR_MAP_SWIZZLE_128B))
         return cudaErrorInvalidValue;
 
     static int attr_set[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 64 || !attr_set[dev]) {
-        e = cudaFuncSetAttribute(gemm_tc_kernel<F>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+        e = cudaFuncSetAttribute(gemm_tc_kernel<F, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
         if (e != cudaSuccess) return e;
         if (dev < 64) attr_set[dev] = 1;
     }
@@ -426,10 +451,20 @@ cudaError_t launch_gemm_t(const uint8_t* w, const float* x, float* y, int out, i
     a.in = in;
     a.T = T;
     a.err = err;
-    const int ntiles = ((out + BM - 1) / BM) * ((T + BN - 1) / BN);
+    const int ntiles = ((out + BM - 1) / BM) * ((T + NT - 1) / NT);
     const int grid = ntiles < sm_count ? ntiles : sm_count;
-    gemm_tc_kernel<F><<<grid, kGemmThreads, C::SMEM, stream>>>(mw, mxh, mxl, a);
+    gemm_tc_kernel<F, NT><<<grid, kGemmThreads, C::SMEM, stream>>>(mw, mxh, mxl, a);
     return cudaGetLastError();
+}
+
+// Narrowest tile that covers the rows of x (wider calls tile by 128).
+template <int F>
+cudaError_t launch_gemm_f(const uint8_t* w, const float* x, float* y, int out, int in, int T, void* ws,
+                          int sm_count, int* err, cudaStream_t stream) {
+    if (T <= 16) return launch_gemm_t<F, 16>(w, x, y, out, in, T, ws, sm_count, err, stream);
+    if (T <= 32) return launch_gemm_t<F, 32>(w, x, y, out, in, T, ws, sm_count, err, stream);
+    if (T <= 64) return launch_gemm_t<F, 64>(w, x, y, out, in, T, ws, sm_count, err, stream);
+    return launch_gemm_t<F, 128>(w, x, y, out, in, T, ws, sm_count, err, stream);
 }
 
 }  // namespace
@@ -446,9 +481,9 @@ size_t gemm_workspace_bytes(int in, int rows) { return (size_t)rows * in * 2 * s
 cudaError_t launch_gemm(int fmt, const uint8_t* w, const float* x, float* y, int out, int in, int rows,
                         void* ws, int sm_count, int* err, cudaStream_t stream) {
     switch (fmt) {
-        case kQ8_0: return launch_gemm_t<kQ8_0>(w, x, y, out, in, rows, ws, sm_count, err, stream);
-        case kQ4_0: return launch_gemm_t<kQ4_0>(w, x, y, out, in, rows, ws, sm_count, err, stream);
-        case kQ4_1: return launch_gemm_t<kQ4_1>(w, x, y, out, in, rows, ws, sm_count, err, stream);
+        case kQ8_0: return launch_gemm_f<kQ8_0>(w, x, y, out, in, rows, ws, sm_count, err, stream);
+        case kQ4_0: return launch_gemm_f<kQ4_0>(w, x, y, out, in, rows, ws, sm_count, err, stream);
+        case kQ4_1: return launch_gemm_f<kQ4_1>(w, x, y, out, in, rows, ws, sm_count, err, stream);
     }
     return cudaErrorInvalidValue;
 }

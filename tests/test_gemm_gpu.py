@@ -36,6 +36,8 @@ CASES = [
     ("q8_0", 512, 4096, 16),     # smallest GEMM row count (batched decode)
     ("q4_0", 300, 2048, 20),
     ("q4_1", 256, 1024, 33),
+    ("q8_0", 384, 1024, 24),     # 32-wide tile, stage count trimmed to fit shared memory
+    ("q4_0", 200, 3584, 48),     # 64-wide tile
 ]
 
 
