@@ -53,6 +53,13 @@ WORKLOADS = {
         "matrices": [("gate", 28672, 8192), ("up", 28672, 8192), ("down", 8192, 28672),
                      ("lm_head", 128256, 8192)],
     },
+    "prefill-q4_1": {
+        "name": "llama-3-8b FFN prefill q4_1, 512 rows of x (BASELINE configs[2])",
+        "metric": "effective weight GB/s (q4_1 prefill GEMM, Llama-3-8B FFN, 512 rows)",
+        "fmt": "q4_1",
+        "rows": 512,
+        "matrices": [("gate", 14336, 4096), ("up", 14336, 4096), ("down", 4096, 14336)],
+    },
     "llama70b-b8": {
         "name": "llama-3-70b FFN + lm_head q4_0 decode shards, batch 8 (BASELINE configs[4])",
         "metric": "effective weight GB/s (q4_0 decode GEMV, Llama-3-70B FFN + lm_head, batch 8)",
@@ -79,6 +86,17 @@ def load_pkg():
 def weight_bytes(fmt, out_f, in_f):
     bs = {"q8_0": 34, "q4_0": 18, "q4_1": 20}[fmt]
     return out_f * ((in_f + 31) // 32) * bs
+
+
+def bf16_peak():
+    """Measured dense bf16 TFLOP/s (burst: each GEMM launch is timed alone)."""
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["bf16_tflops"]), "measured"
+        except Exception:
+            pass
+    return 1590.0, "fallback"
 
 
 def hbm_peak():
@@ -166,8 +184,8 @@ def cpu_has_avx2():
 
 
 class ReferenceCPU:
-    """The reference's CPU linearQ40 (oracle/_ref, built from its sources)
-    over row samples of the workload's matrices, all host threads."""
+    """The reference's CPU linearQ80/Q40/Q41 (oracle/_ref, built from its
+    sources) over row samples of the workload's matrices, all host threads."""
 
     def __init__(self):
         sys.path.insert(0, str(ROOT))
@@ -241,12 +259,20 @@ def reference_cpu_baseline(pkg, seconds):
 
 # ---------------------------------------------------------------------------
 # Placement of the workload's matrices on N GPUs (north_star: large
-# matrices row-sharded, small ones on one GPU).  "local0": rank 0 only, no
-# gather (QKV feeds attention on rank 0); "bcast0": rank 0 computes, the
-# fused gather stores the result into every rank's y (O feeds the FFN on all
-# ranks); "shard": rows split across all ranks, fused all-gather.
-PLACEMENT = {"qkv": "local0", "o": "bcast0", "gate": "shard", "up": "shard", "down": "shard",
-             "lm_head": "shard"}
+# matrices row-sharded, small ones on one GPU).  A sharded call costs ~8 us
+# more than a local one (fused all-gather epilogue + cross-GPU completion
+# handshake), so a matrix is sharded only from SHARD_MIN_BYTES of packed
+# weights on (every 70B-shaped matrix; the 7B layer's lm_head, not its
+# 38 MB FFN matrices).  "local0": rank 0 computes, no gather (its consumer
+# runs on rank 0); "shard": rows split across all ranks, fused all-gather.
+SHARD_MIN_BYTES = 100 * MB
+
+
+def placement(world):
+    if world == 1:
+        return {name: "shard" for name, _, _ in WORKLOAD["matrices"]}
+    return {name: ("shard" if weight_bytes(WORKLOAD["fmt"], o, i) >= SHARD_MIN_BYTES else "local0")
+            for name, o, i in WORKLOAD["matrices"]}
 
 
 def make_inputs(torch, pkg, device, world=1, rank=0):
@@ -257,7 +283,7 @@ def make_inputs(torch, pkg, device, world=1, rank=0):
     g = torch.Generator(device=device)
     ws, xs_dev, xs_host, ranges = [], [], [], []
     for i, (name, out_f, in_f) in enumerate(WORKLOAD["matrices"]):
-        place = PLACEMENT.get(name, "shard") if world > 1 else "shard"
+        place = placement(world)[name]
         rg = sh.shard_rows(out_f, world, owners=[0] if place in ("local0", "bcast0") else None)
         b, e = rg[rank]
         ranges.append(rg)
@@ -309,7 +335,7 @@ def run_mlq(args):
     epoch = [0]
     for j, (name, out_f, in_f) in enumerate(mats):
         b, e = ranges[j][rank]
-        if world == 1 or PLACEMENT.get(name) == "local0":
+        if world == 1 or placement(world)[name] == "local0":
             if e == b:
                 calls.append(None)
                 ybufs.append(None)
@@ -465,29 +491,43 @@ def run_mlq(args):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = reference_cpu_baseline(pkg, args.cpu_seconds)
 
+    kernel = (f"gemv_stream_kernel<{fmt}, MT={rows}, integer mode>" if rows == 1 else
+              f"gemv_stream_kernel<{fmt}, MT={min(rows, 8)}, fp32 mode>" if rows < 16 else
+              f"gemm_tc_kernel<{fmt}>") + f" ({dom} launch, rank 0)"
+    roof = {"bound": "hbm", "kernel": kernel, "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+            "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+            "traffic": traffic, "algorithmic_bytes_per_launch": dom_bytes,
+            "launch_ms": round(per[dom], 5),
+            "launch_ms_back_to_back": round(b2b_ms, 5),
+            "achieved_back_to_back": round(dom_bytes / (b2b_ms / 1e3) / 1e9, 1),
+            "all_launches_GBps": round(sum(local_bytes(j) for j in range(len(mats)) if calls[j] is not None)
+                                       / (kernel_sum_ms / 1e3) / 1e9, 1),
+            "per_launch_ms": {k: round(v, 5) for k, v in per.items()}}
+    if rows >= 16:
+        # the GEMM is tensor-bound: algorithmic flops of the dominant launch
+        # (2 * rows * its rows of W * in) against the measured bf16 peak
+        b_, e_ = ranges[dj][rank]
+        flops = 2.0 * rows * (e_ - b_) * mats[dj][2]
+        tpk, tpk_kind = bf16_peak()
+        tach = flops / (per[dom] / 1e3) / 1e12
+        roof.update({"bound": "tensor", "achieved": round(tach, 1), "peak": tpk, "unit": "TFLOP/s",
+                     "frac": round(tach / tpk, 4), "peak_kind": tpk_kind,
+                     "algorithmic_flops_per_launch": flops,
+                     "achieved_back_to_back": round(flops / (b2b_ms / 1e3) / 1e12, 1),
+                     "note": "three bf16 MMAs per K-step (x and W split into hi/lo): executed flops are ~3x"})
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5),
             "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "fp32 activations x q4_0 weights",
-            "data": "synthetic (seeded N(0,0.02) weights quantized to q4_0; N(0,1) x)",
+            "vs_baseline": None, "dtype": f"fp32 activations x {fmt} weights",
+            "data": f"synthetic (seeded N(0,0.02) weights quantized to {fmt}; N(0,1) x)",
             "config": {"workload": WORKLOAD["name"], "format": fmt, "batch": rows,
                        "matrices": {n: [o, i] for n, o, i in mats},
                        "weight_bytes_per_step": bytes_step,
-                       "placement": PLACEMENT if world > 1 else "all on one GPU",
+                       "placement": placement(world) if world > 1 else "all on one GPU",
                        "l2": f"inputs larger than L2 ({bytes_step / 1e6:.1f} MB per step vs 126 MB L2); no flush"},
-            "roofline": {"bound": "hbm", "kernel": (f"gemv_stream_kernel<{fmt}, MT={rows}, integer mode>" if rows == 1 else f"gemv_stream_kernel<{fmt}, MT={min(rows, 8)}, fp32 mode>" if rows < 16 else f"gemm_tc_kernel<{fmt}>") + f" ({dom} launch, rank 0)",
-                         "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                         "traffic": traffic, "algorithmic_bytes_per_launch": dom_bytes,
-                         "launch_ms": round(per[dom], 5),
-                         "launch_ms_back_to_back": round(b2b_ms, 5),
-                         "achieved_back_to_back": round(dom_bytes / (b2b_ms / 1e3) / 1e9, 1),
-                         "all_launches_GBps": round(sum(local_bytes(j) for j in range(len(mats))
-                                                        if calls[j] is not None)
-                                                    / (kernel_sum_ms / 1e3) / 1e9, 1),
-                         "per_launch_ms": {k: round(v, 5) for k, v in per.items()}},
+            "roofline": roof,
             "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps * launches_per_step,
             "clocks": clocks.summary(), "device_error": err,
         }
@@ -524,8 +564,8 @@ def run_reference(args):
     fmt = WORKLOAD["fmt"]
     base = {"impl": "reference", "metric": METRIC, "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "fp32 activations x q4_0 weights",
-            "data": "synthetic (seeded N(0,0.02) weights quantized to q4_0; N(0,1) x)",
+            "scaling": "strong", "vs_baseline": None, "dtype": f"fp32 activations x {fmt} weights",
+            "data": f"synthetic (seeded N(0,0.02) weights quantized to {fmt}; N(0,1) x)",
             "config": {"workload": WORKLOAD["name"], "format": fmt, "batch": WORKLOAD["rows"]}}
     try:
         rc = ReferenceCPU()
