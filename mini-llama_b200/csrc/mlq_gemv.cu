@@ -5,34 +5,44 @@
 // fp32 activations, exact decode of the packed weights, fp32 accumulation;
 // only the summation order differs.
 //
-// Design (HBM-bound streaming, one persistent CTA per SM):
-//  * The CTA owns a contiguous, balanced range of output rows
-//    [blockIdx*out/grid, (blockIdx+1)*out/grid) and walks it in row tiles of
-//    RT = 8 warps x RPW rows, each tile over the full K extent in K-tiles of
-//    32 lane-groups (2048 values for q8_0/q4_0, 1024 for q4_1).
+// Design (HBM-bound streaming, persistent grid of one or two CTAs per SM):
+//  * Rows are processed in tiles of RT = 8 consumer warps x RPW rows, each
+//    tile over the full K extent in K-tiles of 32 lane-groups (2048 values
+//    for q8_0/q4_0, 1024 for q4_1).  A CTA takes a balanced contiguous row
+//    range, or -- one token and at least 8 tiles per CTA -- row tiles from a
+//    per-launch global queue, so faster SMs do more tiles.
 //  * Warp 0 streams the weights: a stage is RT rows x one K-tile, fetched
 //    as 2-D tensor-map boxes of 8 rows (or, when the row pitch is not a
-//    multiple of 16 B, one 1-D cp.async.bulk per row segment).  Warp 9
-//    builds the stage's x tile: coalesced 128-bit loads, per-block sums,
-//    stored lane-major with an XOR swizzle in the order the consumers read.
-//    Weights and x have separate full/empty mbarriers, so the consumers can
-//    hand the weight region back as soon as they hold it in registers.
+//    multiple of 16 B, one 1-D cp.async.bulk per row segment); consumers
+//    hand a stage back as soon as its words are in registers.
+//  * x tiles: kept resident (every K-tile's tile built once) when they fit
+//    next to two weight stages, otherwise riding a ring with the stages.
+//    Warps 9.. build them (coalesced 128-bit loads, per-block sums); in the
+//    one-token mode all nine non-producer warps build the resident tiles
+//    together before the consumers start.
 //  * Warps 1..8 consume: lane l decodes lane-group l (2 blocks = 9 or 17
 //    words, or 1 q4_1 block = 5 words; odd word counts make the 32 lanes'
 //    32-bit shared loads bank-conflict free) of RPW rows, reusing every x
-//    value it loads for all RPW rows and all tokens.
-//  * Decode without int->float conversions: a nibble (or a sign-flipped
-//    byte) is dropped into the mantissa of a float constant with one PRMT:
+//    value it loads for all RPW rows.
+//  * One token (integer mode): x as three int8 slices per value against its
+//    block's scale (24-bit block fixed point), codes x slices by DP4A, one
+//    fold per block (see the integer-mode section below).
+//  * Two to eight tokens (fp32 mode): decode without int->float
+//    conversions -- a nibble (or a sign-flipped byte) is dropped into the
+//    mantissa of a float constant with one PRMT:
 //      q4:  float(0x43000000 | q << 16) = 128 + q (exact)
 //      q8:  float(0x4B000000 | (q^0x80)) = 2^23+128+q (exact), minus 2^23+128
-//    so a q4 value costs one PRMT + half a packed FFMA2 (+ a quarter of the
-//    nibble masking); the per-block constant is folded back with the
-//    block's x-sum S:
+//    accumulated with packed FFMA2; the per-block constant is folded back
+//    with the block's x-sum S:
 //      q4_0:  d * (sum (128+q) x - 136 S)
 //      q4_1:  d * (sum (128+q) x - 128 S) + m S
 //      q8_0:  d * sum q x
 //    The fold costs ~7 bits of the fp32 block sum against S; measured
 //    relative errors stay near 1e-6 (the contract allows 1e-3).
+//  * Launched with programmatic stream serialization: weights stream while
+//    the previous kernel drains; x and y wait for it (griddepcontrol).
+//  * Sharded calls store every row into every rank's y (NVLink peer
+//    stores) and end with a cross-GPU completion handshake.
 //  * Every mbarrier wait is bounded (2 s); on expiry the kernel records an
 //    error code in *err and returns after its in-flight copies land.
 #include <cuda_runtime.h>
