@@ -157,8 +157,8 @@ bool streamable(int fmt, const void* w, const float* x, int in) {
            bpr % gblocks == 0 && in % 4 == 0;
 }
 
-// Streams `out` rows starting at w through the x-prep + streaming kernels,
-// one pass per <= 8 rows of x.
+// Streams `out` rows starting at w through the streaming GEMV, one launch
+// per <= 8 rows of x.
 mlq_status run_stream(int fmt, const void* w, int out, int in, const float* x, int rows,
                       const Gather& g, cudaStream_t stream) {
     int dev = 0;
