@@ -45,6 +45,18 @@ WORKLOADS = {
         "matrices": [("qkv", 4608, 3584), ("o", 3584, 3584), ("gate", 18944, 3584),
                      ("up", 18944, 3584), ("down", 3584, 18944), ("lm_head", 152064, 3584)],
     },
+    # The same layer through the fused entry points: the q/k/v bias added in
+    # the QKV launch's store (mlq_linear_bias) and gate/up as one SwiGLU-pair
+    # launch writing silu(gate) * up (mlq_linear_swiglu); same weight bytes.
+    "qwen7b-fused": {
+        "name": "qwen2-7b-layer+lm_head q4_0 decode, fused bias + SwiGLU (BASELINE configs[1])",
+        "metric": "effective weight GB/s (q4_0 decode GEMV, Qwen2-7B layer + lm_head, batch 1)",
+        "fmt": "q4_0",
+        "rows": 1,
+        "matrices": [("qkv", 4608, 3584), ("o", 3584, 3584), ("gate", 18944, 3584),
+                     ("up", 18944, 3584), ("down", 3584, 18944), ("lm_head", 152064, 3584)],
+        "fused": {"bias": ["qkv"], "pair": ["gate", "up"]},
+    },
     "llama70b": {
         "name": "llama-3-70b FFN + lm_head q4_0 decode shards, batch 1 (BASELINE configs[4])",
         "metric": "effective weight GB/s (q4_0 decode GEMV, Llama-3-70B FFN + lm_head, batch 1)",
@@ -328,6 +340,10 @@ def run_mlq(args):
 
     # per matrix: a callable launching this rank's share of it
     calls, ybufs, launches_per_step = [], [], 0
+    fused = WORKLOAD.get("fused", {})
+    pair = fused.get("pair")
+    if pair and world > 1 and any(placement(world)[n] != "local0" for n in pair):
+        raise SystemExit("bench: a SwiGLU pair is launched on one GPU (placement local0)")
     group = None
     if world > 1:
         group = sh.PeerGroup(mlq, dist, rank, world)
@@ -340,15 +356,38 @@ def run_mlq(args):
                 calls.append(None)
                 ybufs.append(None)
                 continue
+            if pair and name == pair[1]:
+                # the up projection streams inside the gate's pair launch
+                calls.append(None)
+                ybufs.append(None)
+                continue
             y = torch.empty((rows, out_f), dtype=torch.float32, device=device)
             nb = ws[j].numel() // mlq.BLOCK_BYTES[fmt]
+            if pair and name == pair[0]:
+                ju = [m[0] for m in mats].index(pair[1])
 
-            def call(j=j, out_f=out_f, in_f=in_f, y=y, nb=nb):
-                st = L.mlq_linear(fid, ws[j].data_ptr(), nb, out_f, in_f, xs[j].data_ptr(), rows,
-                                  y.data_ptr(), sh_stream)
-                if st != 0:
-                    raise RuntimeError(L.mlq_last_error().decode())
-                return y.data_ptr()
+                def call(j=j, ju=ju, out_f=out_f, in_f=in_f, y=y, nb=nb):
+                    st = L.mlq_linear_swiglu(fid, ws[j].data_ptr(), ws[ju].data_ptr(), nb, out_f, in_f,
+                                             xs[j].data_ptr(), rows, y.data_ptr(), sh_stream)
+                    if st != 0:
+                        raise RuntimeError(L.mlq_last_error().decode())
+                    return y.data_ptr()
+            elif name in fused.get("bias", ()):
+                bias = torch.from_numpy(pkg.synth.normal((out_f,), seed=3000 + j, std=0.02)).to(device)
+
+                def call(j=j, out_f=out_f, in_f=in_f, y=y, nb=nb, bias=bias):
+                    st = L.mlq_linear_bias(fid, ws[j].data_ptr(), nb, out_f, in_f, xs[j].data_ptr(), rows,
+                                           bias.data_ptr(), y.data_ptr(), sh_stream)
+                    if st != 0:
+                        raise RuntimeError(L.mlq_last_error().decode())
+                    return y.data_ptr()
+            else:
+                def call(j=j, out_f=out_f, in_f=in_f, y=y, nb=nb):
+                    st = L.mlq_linear(fid, ws[j].data_ptr(), nb, out_f, in_f, xs[j].data_ptr(), rows,
+                                      y.data_ptr(), sh_stream)
+                    if st != 0:
+                        raise RuntimeError(L.mlq_last_error().decode())
+                    return y.data_ptr()
             calls.append(call)
             ybufs.append(lambda y=y: y.data_ptr())
         else:
@@ -413,7 +452,8 @@ def run_mlq(args):
     # dominant launch: the largest share of weight bytes on this rank
     def local_bytes(j):
         b, e = ranges[j][rank]
-        return weight_bytes(fmt, e - b, mats[j][2])
+        nbytes = weight_bytes(fmt, e - b, mats[j][2])
+        return 2 * nbytes if pair and mats[j][0] == pair[0] else nbytes  # a pair launch reads both
     dj = max((j for j in range(len(mats)) if calls[j] is not None), key=local_bytes)
     dom, dom_bytes = mats[dj][0], local_bytes(dj)
     achieved = dom_bytes / (per[dom] / 1e3) / 1e9
@@ -447,7 +487,7 @@ def run_mlq(args):
         ke = max(3, min(args.steps, 300))
 
         def e2e_step():
-            if world == 1:
+            if world == 1 and not fused:
                 for j, (name, out_f, in_f) in enumerate(mats):
                     st = L.mlq_linear_host(fid, ws[j].data_ptr(), ws[j].numel() // mlq.BLOCK_BYTES[fmt],
                                            out_f, in_f, xh[j].data_ptr(), rows, None,
@@ -483,8 +523,8 @@ def run_mlq(args):
         d2h = sum(4 * rows * o for j, (_, o, _) in enumerate(mats) if calls[j] is not None)
         e2e = {"value": round(bytes_step * ke / (ems / 1e3) / 1e9, 2), "unit": UNIT,
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": ke,
-               "path": ("mlq_linear_host (device weights, pinned host x/y)" if world == 1 else
-                        "pinned x H2D + mlq_linear_allgather / mlq_linear + y D2H, per matrix")}
+               "path": ("mlq_linear_host (device weights, pinned host x/y)" if world == 1 and not fused else
+                        "pinned x H2D + the step's device call + y D2H, per launch")}
 
     err = mlq.device_error(local)
     cpu = None
@@ -525,6 +565,7 @@ def run_mlq(args):
             "config": {"workload": WORKLOAD["name"], "format": fmt, "batch": rows,
                        "matrices": {n: [o, i] for n, o, i in mats},
                        "weight_bytes_per_step": bytes_step,
+                       **({"fused": fused} if fused else {}),
                        "placement": placement(world) if world > 1 else "all on one GPU",
                        "l2": f"inputs larger than L2 ({bytes_step / 1e6:.1f} MB per step vs 126 MB L2); no flush"},
             "roofline": roof,

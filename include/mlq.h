@@ -134,6 +134,30 @@ MLQ_API mlq_status mlq_linear_noalloc(mlq_format fmt, const void* w, size_t bloc
                                       int out_features, int in_features, const float* x, int rows,
                                       float* y, mlq_stream stream);
 
+/* mlq_linear plus a device bias: y[r][o] = (x W^T)[r][o] + bias[o], one fp32
+ * add per output in the kernel's own store (no extra pass over y).
+ * Replaces a DeviceInput linear followed by addOptionalBiasDevice
+ * (src/forward.cc:384-400, used for the q/k/v biases at :432-434), whose
+ * cudaElementwiseAddDeviceWeight makes the same fp32 add in a second
+ * kernel.  bias: out_features floats of device memory; null = no bias. */
+MLQ_API mlq_status mlq_linear_bias(mlq_format fmt, const void* w, size_t block_count,
+                                   int out_features, int in_features, const float* x, int rows,
+                                   const float* bias, float* y, mlq_stream stream);
+
+/* The SwiGLU input of a feed-forward block in one call:
+ *     h = silu(x W_gate^T) * (x W_up^T),   silu(v) = v / (1 + exp(-v)),
+ * with the reference's fp32 steps.  Both matrices have one format and the
+ * shape [out_features, in_features] (block_count blocks each); h is
+ * rows x out_features.  Replaces the gate and up forwardLinearDevice calls
+ * and forwardSwiGluDevice of ffnForwardDevice (src/forward.cc:573-581,
+ * 361-369).  Below MLQ_GEMM_MIN_ROWS rows it is one streaming launch whose
+ * row tiles carry matching rows of both matrices, so gate and up are never
+ * stored; from MLQ_GEMM_MIN_ROWS rows on, one tensor-core GEMM per matrix
+ * (up into the per-stream workspace) and one elementwise pass. */
+MLQ_API mlq_status mlq_linear_swiglu(mlq_format fmt, const void* w_gate, const void* w_up,
+                                     size_t block_count, int out_features, int in_features,
+                                     const float* x, int rows, float* h, mlq_stream stream);
+
 /* Device weight, HOST x, HOST y, optional HOST bias[out] added to every row
  * after the product.  Replaces cudaQ80LinearDeviceWeight /
  * cudaQ40LinearDeviceWeight / cudaQ41LinearDeviceWeight

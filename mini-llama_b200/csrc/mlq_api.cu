@@ -157,10 +157,17 @@ bool streamable(int fmt, const void* w, const float* x, int in) {
            bpr % gblocks == 0 && in % 4 == 0;
 }
 
+// What follows the product in one call: nothing, a bias add, or the SwiGLU
+// of a gate/up pair (w being the gate).
+struct Epilogue {
+    const void* w2 = nullptr;     // up projection of a SwiGLU pair, or null
+    const float* bias = nullptr;  // [out] added to every row, or null
+};
+
 // Streams `out` rows starting at w through the streaming GEMV, one launch
 // per <= 8 rows of x.
 mlq_status run_stream(int fmt, const void* w, int out, int in, const float* x, int rows,
-                      const Gather& g, cudaStream_t stream) {
+                      const Gather& g, cudaStream_t stream, const Epilogue& ep = Epilogue()) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return fail_cuda("cudaGetDevice", e);
@@ -171,6 +178,8 @@ mlq_status run_stream(int fmt, const void* w, int out, int in, const float* x, i
     const int gblocks = fmt == MLQ_Q4_1 ? 1 : 2;
     mlq::GemvArgs a{};
     a.w = static_cast<const uint8_t*>(w);
+    a.w2 = static_cast<const uint8_t*>(ep.w2);
+    a.bias = ep.bias;
     a.out = out;
     a.in = in;
     a.bpr = bpr;
@@ -205,32 +214,55 @@ mlq_status run_stream(int fmt, const void* w, int out, int in, const float* x, i
 }
 
 mlq_status run_linear(int fmt, const void* w, int out, int in, const float* x, int rows, float* y,
-                      cudaStream_t stream) {
-    if (mlq::gemm_supported(fmt, w, out, in, rows)) {
-        // many rows of x: the tensor-core GEMM
+                      cudaStream_t stream, const Epilogue& ep = Epilogue()) {
+    const bool gemm = mlq::gemm_supported(fmt, w, out, in, rows) &&
+                      (ep.w2 == nullptr || mlq::gemm_supported(fmt, ep.w2, out, in, rows));
+    const bool stream_ok = streamable(fmt, w, x, in) && (ep.w2 == nullptr || streamable(fmt, ep.w2, x, in));
+    if (gemm || !stream_ok) {
         int dev = 0;
         cudaError_t e = cudaGetDevice(&dev);
         if (e != cudaSuccess) return fail_cuda("cudaGetDevice", e);
         mlq_status st = MLQ_OK;
         DeviceState* ds = device_state(dev, &st);
         if (!ds) return st;
+        // workspace: the GEMM's x split, then (pair) the up projection's output
+        const size_t xsplit = gemm ? (mlq::gemm_workspace_bytes(in, rows) + 255) & ~(size_t)255 : 0;
+        const size_t ubytes = ep.w2 ? (size_t)rows * out * sizeof(float) : 0;
         void* ws = nullptr;
-        st = stream_workspace(ds, stream, mlq::gemm_workspace_bytes(in, rows), &ws);
-        if (st != MLQ_OK) return st;
-        e = mlq::launch_gemm(fmt, static_cast<const uint8_t*>(w), x, y, out, in, rows, ws, ds->sm_count,
-                             ds->err_flag, stream);
-        return e == cudaSuccess ? MLQ_OK : fail_cuda("gemm launch", e);
-    }
-    if (!streamable(fmt, w, x, in)) {
-        const int bpr = (in + mlq::kQK - 1) / mlq::kQK;
-        cudaError_t e = mlq::launch_gemv_generic(fmt, static_cast<const uint8_t*>(w), x, y, out, in,
-                                                 rows, bpr, stream);
-        return e == cudaSuccess ? MLQ_OK : fail_cuda("gemv_generic launch", e);
+        if (xsplit + ubytes > 0) {
+            st = stream_workspace(ds, stream, xsplit + ubytes, &ws);
+            if (st != MLQ_OK) return st;
+        }
+        float* u = ep.w2 ? reinterpret_cast<float*>(static_cast<char*>(ws) + xsplit) : nullptr;
+        if (gemm) {
+            // many rows of x: the tensor-core GEMM (bias in its store; a pair
+            // runs it per matrix, then one SwiGLU pass)
+            e = mlq::launch_gemm(fmt, static_cast<const uint8_t*>(w), x, y, out, in, rows, ep.bias, ws,
+                                 ds->sm_count, ds->err_flag, stream);
+            if (e == cudaSuccess && ep.w2)
+                e = mlq::launch_gemm(fmt, static_cast<const uint8_t*>(ep.w2), x, u, out, in, rows, nullptr, ws,
+                                     ds->sm_count, ds->err_flag, stream);
+            if (e != cudaSuccess) return fail_cuda("gemm launch", e);
+        } else {
+            // layouts the streaming kernel does not take: the any-alignment GEMV
+            const int bpr = (in + mlq::kQK - 1) / mlq::kQK;
+            e = mlq::launch_gemv_generic(fmt, static_cast<const uint8_t*>(w), x, y, out, in, rows, bpr, stream);
+            if (e == cudaSuccess && ep.w2)
+                e = mlq::launch_gemv_generic(fmt, static_cast<const uint8_t*>(ep.w2), x, u, out, in, rows, bpr,
+                                             stream);
+            if (e == cudaSuccess && ep.bias && !ep.w2) e = mlq::launch_add_bias(y, ep.bias, rows, out, stream);
+            if (e != cudaSuccess) return fail_cuda("gemv_generic launch", e);
+        }
+        if (ep.w2) {
+            e = mlq::launch_swiglu(y, u, (long long)rows * out, stream);
+            if (e != cudaSuccess) return fail_cuda("swiglu launch", e);
+        }
+        return MLQ_OK;
     }
     Gather g;
     g.y_stride = out;
     g.ys = &y;
-    return run_stream(fmt, w, out, in, x, rows, g, stream);
+    return run_stream(fmt, w, out, in, x, rows, g, stream, ep);
 }
 
 // Device address of g_mlq_noalloc_scratch, looked up once per device (with
@@ -260,8 +292,8 @@ mlq_status run_linear_noalloc(int fmt, const void* w, int out, int in, const flo
     std::call_once(s.once, [&] { s.err = cudaGetSymbolAddress(&s.ptr, g_mlq_noalloc_scratch); });
     if (s.err != cudaSuccess || s.ptr == nullptr)
         return fail_cuda("cudaGetSymbolAddress (static scratch)", s.err != cudaSuccess ? s.err : cudaErrorInvalidSymbol);
-    e = mlq::launch_gemm(fmt, static_cast<const uint8_t*>(w), x, y, out, in, rows, s.ptr, ds->sm_count,
-                         ds->err_flag, stream);
+    e = mlq::launch_gemm(fmt, static_cast<const uint8_t*>(w), x, y, out, in, rows, nullptr, s.ptr,
+                         ds->sm_count, ds->err_flag, stream);
     return e == cudaSuccess ? MLQ_OK : fail_cuda("gemm launch", e);
 }
 
@@ -376,6 +408,41 @@ MLQ_API mlq_status mlq_linear_noalloc(mlq_format fmt, const void* w, size_t bloc
                                   reinterpret_cast<cudaStream_t>(stream));
     } catch (...) {
         return fail(MLQ_ERR_CUDA, "mlq_linear_noalloc: host exception");
+    }
+}
+
+MLQ_API mlq_status mlq_linear_bias(mlq_format fmt, const void* w, size_t block_count,
+                                   int out_features, int in_features, const float* x, int rows,
+                                   const float* bias, float* y, mlq_stream stream) {
+    try {
+        mlq_status st = validate_linear(fmt, w, block_count, out_features, in_features, x, rows, y,
+                                        "mlq_linear_bias");
+        if (st != MLQ_OK) return st;
+        Epilogue ep;
+        ep.bias = bias;
+        return run_linear(fmt, w, out_features, in_features, x, rows, y,
+                          reinterpret_cast<cudaStream_t>(stream), ep);
+    } catch (...) {
+        return fail(MLQ_ERR_CUDA, "mlq_linear_bias: host exception");
+    }
+}
+
+MLQ_API mlq_status mlq_linear_swiglu(mlq_format fmt, const void* w_gate, const void* w_up,
+                                     size_t block_count, int out_features, int in_features,
+                                     const float* x, int rows, float* h, mlq_stream stream) {
+    try {
+        mlq_status st = validate_linear(fmt, w_gate, block_count, out_features, in_features, x, rows, h,
+                                        "mlq_linear_swiglu");
+        if (st != MLQ_OK) return st;
+        if (w_up == nullptr)
+            return fail(MLQ_ERR_NULL, std::string("mlq_linear_swiglu(") + fmt_name(fmt) +
+                                          "): null up-projection weight pointer");
+        Epilogue ep;
+        ep.w2 = w_up;
+        return run_linear(fmt, w_gate, out_features, in_features, x, rows, h,
+                          reinterpret_cast<cudaStream_t>(stream), ep);
+    } catch (...) {
+        return fail(MLQ_ERR_CUDA, "mlq_linear_swiglu: host exception");
     }
 }
 

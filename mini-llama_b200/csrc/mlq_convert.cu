@@ -160,6 +160,12 @@ __global__ void add_bias_kernel(float* __restrict__ y, const float* __restrict__
         y[i] = __fadd_rn(y[i], bias[i % cols]);
 }
 
+__global__ void swiglu_kernel(float* __restrict__ h, const float* __restrict__ u, long long n) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+         i += (long long)gridDim.x * blockDim.x)
+        h[i] = silu_mul(h[i], u[i]);
+}
+
 int grid_for(long long n, int block) {
     long long g = (n + block - 1) / block;
     if (g > 148LL * 32) g = 148LL * 32;
@@ -195,6 +201,11 @@ cudaError_t launch_dequantize(int fmt, const uint8_t* blocks, long long rows, in
 
 cudaError_t launch_add_bias(float* y, const float* bias, int rows, int cols, cudaStream_t stream) {
     add_bias_kernel<<<grid_for((long long)rows * cols, 256), 256, 0, stream>>>(y, bias, rows, cols);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_swiglu(float* h, const float* u, long long n, cudaStream_t stream) {
+    swiglu_kernel<<<grid_for(n, 256), 256, 0, stream>>>(h, u, n);
     return cudaGetLastError();
 }
 

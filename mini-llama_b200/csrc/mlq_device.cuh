@@ -51,6 +51,13 @@ __device__ __forceinline__ float half_bits_to_float(uint32_t bits16) {
     return __half2float(__ushort_as_half(static_cast<unsigned short>(bits16)));
 }
 
+// SwiGLU of one output: silu(g) * u with silu(v) = v / (1 + exp(-v)), in the
+// reference's fp32 steps (siluKernel, then elementwiseMulKernel:
+// src/cuda_ops.cu:147-160), each rounded on its own.
+__device__ __forceinline__ float silu_mul(float g, float u) {
+    return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+}
+
 // ---------------------------------------------------------------------------
 // Error reporting from kernels.  A kernel that gives up (a bounded wait ran
 // out) records a code here and returns; the host reads it back with

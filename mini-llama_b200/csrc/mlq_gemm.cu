@@ -381,6 +381,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
             tc_fence_after();
             const int o = mt * BM + row;
+            // this thread's output feature: one bias value for all its columns
+            const bool has_bias = a.bias != nullptr && o < a.out;
+            const float bo = has_bias ? a.bias[o] : 0.0f;
             // 32-column chunks of the accumulator, split between the halves
             constexpr int NCH = NT < 32 ? 1 : NT / 32;
             constexpr int PER = NCH >= 2 ? NCH / 2 : 1;
@@ -392,7 +395,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 for (int j = 0; j < 32; ++j) {
                     const int t = nt * NT + c * 32 + j;
                     if (c * 32 + j >= NT) break;
-                    if (o < a.out && t < a.T) a.y[(long long)t * a.out + o] = __uint_as_float(v[j]);
+                    if (o < a.out && t < a.T) {
+                        const float yv = __uint_as_float(v[j]);
+                        a.y[(long long)t * a.out + o] = has_bias ? __fadd_rn(yv, bo) : yv;
+                    }
                 }
             }
             tc_fence_before();
@@ -416,7 +422,7 @@ __global__ void xsplit_kernel(const float* __restrict__ x, long long n, __nv_bfl
 
 template <int F, int NT>
 cudaError_t launch_gemm_t(const uint8_t* w, const float* x, float* y, int out, int in, int T,
-                          void* ws, int sm_count, int* err, cudaStream_t stream) {
+                          const float* bias, void* ws, int sm_count, int* err, cudaStream_t stream) {
     using C = GemmCfg<F, NT>;
     __nv_bfloat16* xh = static_cast<__nv_bfloat16*>(ws);
     __nv_bfloat16* xl = xh + (size_t)T * in;
@@ -447,6 +453,7 @@ cudaError_t launch_gemm_t(const uint8_t* w, const float* x, float* y, int out, i
     }
     GemmArgs a{};
     a.y = y;
+    a.bias = bias;
     a.out = out;
     a.in = in;
     a.T = T;
@@ -459,12 +466,12 @@ cudaError_t launch_gemm_t(const uint8_t* w, const float* x, float* y, int out, i
 
 // Narrowest tile that covers the rows of x (wider calls tile by 128).
 template <int F>
-cudaError_t launch_gemm_f(const uint8_t* w, const float* x, float* y, int out, int in, int T, void* ws,
-                          int sm_count, int* err, cudaStream_t stream) {
-    if (T <= 16) return launch_gemm_t<F, 16>(w, x, y, out, in, T, ws, sm_count, err, stream);
-    if (T <= 32) return launch_gemm_t<F, 32>(w, x, y, out, in, T, ws, sm_count, err, stream);
-    if (T <= 64) return launch_gemm_t<F, 64>(w, x, y, out, in, T, ws, sm_count, err, stream);
-    return launch_gemm_t<F, 128>(w, x, y, out, in, T, ws, sm_count, err, stream);
+cudaError_t launch_gemm_f(const uint8_t* w, const float* x, float* y, int out, int in, int T,
+                          const float* bias, void* ws, int sm_count, int* err, cudaStream_t stream) {
+    if (T <= 16) return launch_gemm_t<F, 16>(w, x, y, out, in, T, bias, ws, sm_count, err, stream);
+    if (T <= 32) return launch_gemm_t<F, 32>(w, x, y, out, in, T, bias, ws, sm_count, err, stream);
+    if (T <= 64) return launch_gemm_t<F, 64>(w, x, y, out, in, T, bias, ws, sm_count, err, stream);
+    return launch_gemm_t<F, 128>(w, x, y, out, in, T, bias, ws, sm_count, err, stream);
 }
 
 }  // namespace
@@ -479,11 +486,11 @@ bool gemm_supported(int fmt, const void* w, int out, int in, int rows) {
 size_t gemm_workspace_bytes(int in, int rows) { return (size_t)rows * in * 2 * sizeof(__nv_bfloat16); }
 
 cudaError_t launch_gemm(int fmt, const uint8_t* w, const float* x, float* y, int out, int in, int rows,
-                        void* ws, int sm_count, int* err, cudaStream_t stream) {
+                        const float* bias, void* ws, int sm_count, int* err, cudaStream_t stream) {
     switch (fmt) {
-        case kQ8_0: return launch_gemm_f<kQ8_0>(w, x, y, out, in, rows, ws, sm_count, err, stream);
-        case kQ4_0: return launch_gemm_f<kQ4_0>(w, x, y, out, in, rows, ws, sm_count, err, stream);
-        case kQ4_1: return launch_gemm_f<kQ4_1>(w, x, y, out, in, rows, ws, sm_count, err, stream);
+        case kQ8_0: return launch_gemm_f<kQ8_0>(w, x, y, out, in, rows, bias, ws, sm_count, err, stream);
+        case kQ4_0: return launch_gemm_f<kQ4_0>(w, x, y, out, in, rows, bias, ws, sm_count, err, stream);
+        case kQ4_1: return launch_gemm_f<kQ4_1>(w, x, y, out, in, rows, bias, ws, sm_count, err, stream);
     }
     return cudaErrorInvalidValue;
 }

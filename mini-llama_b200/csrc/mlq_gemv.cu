@@ -262,6 +262,20 @@ __device__ __forceinline__ void int_piece_store(const float v[16], int i, int la
 
 constexpr int log2_of(int n) { return n <= 1 ? 0 : 1 + log2_of(n / 2); }
 
+// What a launch does after the sums: store y (+ bias, when the call has one:
+// a runtime check, so plain and bias calls share one kernel), or -- a
+// separate instantiation -- store silu(gate) * up for a SwiGLU pair.
+// (Measured on the decode step: a separate bias instantiation cost ~3 us per
+// step more than the runtime check, and a plain kernel carrying the pair's
+// code as runtime branches ~3 us more than without it.)
+constexpr int kEpiPlain = 0, kEpiPair = 2;
+
+// The weights' tensor maps: one, or gate and up for a pair.
+template <int N>
+struct WMaps {
+    CUtensorMap m[N];
+};
+
 // Sum of v[r][0] over the 32 lanes for every row r < RPW (1, 2 or 4), as a
 // reduce-scatter: after it, the lanes of block k of 32/RPW consecutive lanes
 // hold row k's total.
@@ -295,9 +309,9 @@ __device__ __forceinline__ float reduce_rows(float (&v)[RPW][MT], int lane) {
     return k;
 }
 
-template <int F, int MT, int RPW, int MINB, bool INT>
+template <int F, int MT, int RPW, int MINB, bool INT, int EPI>
 __global__ void __launch_bounds__(threads_for(MT), MINB)
-    gemv_stream_kernel(GemvArgs a, const __grid_constant__ CUtensorMap wmap) {
+    gemv_stream_kernel(GemvArgs a, const __grid_constant__ WMaps<EPI == kEpiPair ? 2 : 1> wm) {
     using C = GemvCfg<F, MT, RPW, INT>;
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(8) uint64_t full_bar[kMaxStages];
@@ -314,6 +328,13 @@ __global__ void __launch_bounds__(threads_for(MT), MINB)
     const int lane = threadIdx.x & 31;
     const int S = a.nstages;
     const bool xres = a.x_resident != 0;
+    // SwiGLU pair: a tile holds TR rows of each matrix (gate rows in stage
+    // rows [0, TR), the same rows of up in [TR, RT)); otherwise RT rows of one
+    constexpr bool pair = EPI == kEpiPair;
+    constexpr int TR = pair ? C::RT / 2 : C::RT;
+    const bool has_bias = !pair && a.bias != nullptr;
+    const CUtensorMap& wmap = wm.m[0];
+    const CUtensorMap& wmap2 = wm.m[pair ? 1 : 0];
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kMaxStages; ++s) {
@@ -336,18 +357,20 @@ __global__ void __launch_bounds__(threads_for(MT), MINB)
     const long long r_begin = 8 * ((long long)blockIdx.x * units / gridDim.x);
     const long long r_end = min((long long)a.out, 8 * ((long long)(blockIdx.x + 1) * units / gridDim.x));
     const int nrows_cta = (int)(r_end - r_begin);
-    const int ntiles = (nrows_cta + C::RT - 1) / C::RT;
+    const int ntiles = (nrows_cta + TR - 1) / TR;
     const uint32_t smem_base = (smem_u32(smem) + 127u) & ~127u;  // TMA boxes: 128-B aligned
     // S weight stages, then the x slots (one per K-tile when resident, else one per stage)
     const uint32_t x_base = smem_base + (uint32_t)S * C::W_BYTES;
     const uintptr_t wbase = reinterpret_cast<uintptr_t>(a.w);
     const uintptr_t wend16 = (wbase + (uintptr_t)a.total_bytes) & ~(uintptr_t)15;
+    const uintptr_t w2base = reinterpret_cast<uintptr_t>(a.w2);
+    const uintptr_t w2end16 = (w2base + (uintptr_t)a.total_bytes) & ~(uintptr_t)15;
 
     // Dynamic tiles (one token, resident x, many tiles): CTAs take row tiles
     // from a global queue instead of a fixed row range, so SMs that stream
     // faster do more tiles and all CTAs finish together.
     const bool dyn = INT && xres && a.tiles != nullptr;
-    const long long ntiles_all = (a.out + C::RT - 1) / C::RT;
+    const long long ntiles_all = (a.out + TR - 1) / TR;
 
     if (warp == 0) {
         // ------------------------------ producer ------------------------------
@@ -374,11 +397,11 @@ __global__ void __launch_bounds__(threads_for(MT), MINB)
                 const unsigned int cur = __shfl_sync(0xffffffffu, ticket, 0);
                 if ((long long)cur >= ntiles_all) break;
                 if (lane == 0) ticket = atomicAdd(a.tiles, 1u);
-                row0 = (long long)cur * C::RT;
+                row0 = (long long)cur * TR;
             } else {
-                row0 = r_begin + (long long)t * C::RT;
+                row0 = r_begin + (long long)t * TR;
             }
-            const int nrows = (int)min((long long)C::RT, (dyn ? (long long)a.out : r_end) - row0);
+            const int nrows = (int)min((long long)TR, (dyn ? (long long)a.out : r_end) - row0);
             for (int kt = 0; kt < a.ktiles; ++kt, ++seq) {
                 // resident integer mode: one stage in flight until the x tiles
                 // are built, so the x loads do not queue behind the weights
@@ -397,24 +420,35 @@ __global__ void __launch_bounds__(threads_for(MT), MINB)
                 const int groups = min(32, a.gpr - kt * 32);
                 const uint32_t seg = (uint32_t)(groups * C::GB);
                 if (a.tma2d) {
-                    // boxes of 8 rows x K-tile bytes (x2 regions for q8_0)
-                    const int nbox = ((nrows + 7) / 8) * C::NREG;
+                    // boxes of 8 rows x K-tile bytes (x2 regions for q8_0); a
+                    // pair's second matrix fills the boxes from stage row TR on
+                    const int nb = (nrows + 7) / 8;
+                    const int nbox = (pair ? 2 * nb : nb) * C::NREG;
                     if (lane == 0) mbar_expect_tx(fb, (uint32_t)(nbox * 8 * C::BOXB));
                     __syncwarp();
                     if (lane < nbox) {
-                        const int reg = lane % C::NREG, rb = lane / C::NREG;
-                        tma_load_2d(stage + (uint32_t)(reg * C::REGION + rb * 8 * C::BOXB), &wmap,
-                                    kt * C::NREG * C::BOXW + reg * C::BOXW, (int)(row0 + 8 * rb), fb);
+                        const int reg = lane % C::NREG, b = lane / C::NREG;
+                        const bool second = pair && b >= nb;
+                        const int k = second ? b - nb : b;
+                        const int rb = second ? C::RT / 16 + k : k;
+                        tma_load_2d(stage + (uint32_t)(reg * C::REGION + rb * 8 * C::BOXB), second ? &wmap2 : &wmap,
+                                    kt * C::NREG * C::BOXW + reg * C::BOXW, (int)(row0 + 8 * k), fb);
                     }
                 } else {
-                // lane i streams tile row i's segment (RT <= 32 rows per tile)
+                // lane i streams stage row i's segment (RT <= 32 rows per tile;
+                // a pair's second matrix from stage row TR on)
+                const bool second = pair && lane >= TR;
+                const int ri = second ? lane - TR : lane;
+                const bool row_ok = ri < nrows && (pair || lane < TR);
                 uintptr_t src = 0, lo = 0, hi = 0;
                 uint32_t bytes = 0;
-                if (lane < nrows) {
-                    src = wbase + (uintptr_t)((row0 + lane) * a.row_bytes) + (uintptr_t)kt * 32u * C::GB;
+                if (row_ok) {
+                    src = (second ? w2base : wbase) + (uintptr_t)((row0 + ri) * a.row_bytes) +
+                          (uintptr_t)kt * 32u * C::GB;
                     lo = src & ~(uintptr_t)15;
                     hi = (src + seg + 15) & ~(uintptr_t)15;
-                    if (hi > wend16) hi = wend16;  // never read past the array
+                    const uintptr_t end16 = second ? w2end16 : wend16;
+                    if (hi > end16) hi = end16;  // never read past the array
                     bytes = hi > lo ? (uint32_t)(hi - lo) : 0u;
                 }
                 uint32_t tx = bytes;
@@ -423,7 +457,7 @@ __global__ void __launch_bounds__(threads_for(MT), MINB)
                 if (lane == 0) mbar_expect_tx(fb, tx);
                 __syncwarp();
                 if (bytes) bulk_g2s(stage + (uint32_t)lane * C::SLOT, reinterpret_cast<const void*>(lo), bytes, fb);
-                if (lane < nrows) {
+                if (row_ok) {
                     // bytes past the array's last 16-B boundary: plain copy
                     for (uintptr_t q = (bytes ? hi : lo); q < src + seg; ++q)
                         sts_u8(stage + (uint32_t)lane * C::SLOT + (uint32_t)(q - lo),
@@ -469,6 +503,20 @@ __global__ void __launch_bounds__(threads_for(MT), MINB)
             }
         }
         return;
+    }
+
+    // Bias of the first tile's row that this thread stores, loaded before any
+    // wait: like the weights it is read-only, so it need not wait for the
+    // previous kernel (one-token stores: the reduce-scatter's row of this
+    // lane; tile stores: row c % TR of thread c).  Later tiles load theirs
+    // when they start.
+    float bias_first = 0.f;
+    if (has_bias) {
+        if (!dyn && warp >= 1 && warp <= kConsumerWarps) {
+            const int i = (MT == 1 && a.ny == 1) ? (warp - 1) + (lane >> (5 - log2_of(RPW))) * kConsumerWarps
+                                                 : (int)(threadIdx.x - 32) % TR;
+            if (i < min(TR, nrows_cta)) bias_first = __ldg(a.bias + a.row_offset + r_begin + i);
+        }
     }
 
     if (INT && xres) {
@@ -598,9 +646,19 @@ __global__ void __launch_bounds__(threads_for(MT), MINB)
             if (r0 < 0) break;
             row0 = r0;
         } else {
-            row0 = r_begin + (long long)t * C::RT;
+            row0 = r_begin + (long long)t * TR;
         }
-        const int nrows = (int)min((long long)C::RT, (dyn ? (long long)a.out : r_end) - row0);
+        const int nrows = (int)min((long long)TR, (dyn ? (long long)a.out : r_end) - row0);
+        // bias of the row this thread stores (the first tile's was loaded at
+        // the start; a later tile's is loaded here, ahead of its K loop)
+        float bias_v = bias_first;
+        if (has_bias) {
+            if (dyn || t > 0) {
+                const int i = (MT == 1 && a.ny == 1) ? wc + (lane >> (5 - log2_of(RPW))) * kConsumerWarps
+                                                     : (int)(threadIdx.x - 32) % TR;
+                bias_v = i < nrows ? __ldg(a.bias + a.row_offset + row0 + i) : 0.f;
+            }
+        }
         float tot[RPW][MT];
 #pragma unroll
         for (int r = 0; r < RPW; ++r)
@@ -613,13 +671,15 @@ __global__ void __launch_bounds__(threads_for(MT), MINB)
         bool row_on[RPW];
 #pragma unroll
         for (int r = 0; r < RPW; ++r) {
-            const int i = wc + r * kConsumerWarps;
-            row_on[r] = i < nrows;
+            const int i = wc + r * kConsumerWarps;  // stage row
+            const bool second = pair && i >= TR;
+            const int ri = second ? i - TR : i;     // row within the tile
+            row_on[r] = ri < nrows;
             if (a.tma2d) {
                 constexpr int LPR = 32 / C::NREG;  // lanes per region
                 soff[r] = (uint32_t)((lane / LPR) * C::REGION + i * C::BOXB + (lane % LPR) * C::GB);
             } else {
-                const uintptr_t rowaddr = wbase + (uintptr_t)((row0 + i) * a.row_bytes);
+                const uintptr_t rowaddr = (second ? w2base : wbase) + (uintptr_t)((row0 + ri) * a.row_bytes);
                 soff[r] = (uint32_t)i * C::SLOT + (uint32_t)(rowaddr & 15) + (uint32_t)lane * C::GB;
             }
         }
@@ -785,8 +845,17 @@ __global__ void __launch_bounds__(threads_for(MT), MINB)
             float v = reduce_rows<RPW>(tot, lane);
             const int r = lane >> (5 - log2_of(RPW));  // row held by this lane
             const int i = wc + r * kConsumerWarps;
-            if ((lane & (31 >> log2_of(RPW))) == 0 && i < nrows)
-                a.ys[0][a.row_offset + row0 + i] = v;
+            const bool lead = (lane & (31 >> log2_of(RPW))) == 0;
+            if constexpr (pair) {
+                // the second matrix's row i sits in stage row TR + i, whose
+                // total the reduce-scatter leaves 16 lanes further on
+                const float u = __shfl_xor_sync(0xffffffffu, v, 16);
+                if (lead && i < TR && i < nrows) a.ys[0][a.row_offset + row0 + i] = silu_mul(v, u);
+            } else if (lead && i < nrows) {
+                const long long o = a.row_offset + row0 + i;
+                if (has_bias) v = __fadd_rn(v, bias_v);
+                a.ys[0][o] = v;
+            }
             continue;
         }
         // reduce the 32 lane partials of every (row, token) into the tile's
@@ -818,9 +887,14 @@ __global__ void __launch_bounds__(threads_for(MT), MINB)
         }
         {
             const int c = threadIdx.x - 32;  // 0 .. 255
-            const int m = c / C::RT, i = c % C::RT;
+            const int m = c / TR, i = c % TR;
             if (m < a.M && i < nrows) {
-                const float v = res[m * C::RT + i];
+                float v = res[m * C::RT + i];
+                if constexpr (pair) {
+                    v = silu_mul(v, res[m * C::RT + TR + i]);
+                } else if (has_bias) {
+                    v = __fadd_rn(v, bias_v);
+                }
                 const long long off = (long long)m * a.y_stride + a.row_offset + row0 + i;
                 for (int d = 0; d < a.ny; ++d) a.ys[d][off] = v;
             }
@@ -952,7 +1026,7 @@ unsigned int* tile_queue(int dev, cudaStream_t stream) {
 // MINB: CTAs per SM the kernel's registers and shared memory are sized for;
 // cps: CTAs per SM actually launched (cps < MINB leaves room on every SM for
 // the next kernel in the stream to start its weight stream early).
-template <int F, int MT, int RPW, int MINB, bool INT>
+template <int F, int MT, int RPW, int MINB, bool INT, int EPI>
 cudaError_t launch_stream_t(GemvArgs args, int sm_count, int smem_per_sm, cudaStream_t stream,
                             int cps = MINB) {
     using C = GemvCfg<F, MT, RPW, INT>;
@@ -982,20 +1056,28 @@ cudaError_t launch_stream_t(GemvArgs args, int sm_count, int smem_per_sm, cudaSt
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 64 || attr_bytes[dev] < smem) {
-        cudaError_t e = cudaFuncSetAttribute(gemv_stream_kernel<F, MT, RPW, MINB, INT>,
+        cudaError_t e = cudaFuncSetAttribute(gemv_stream_kernel<F, MT, RPW, MINB, INT, EPI>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
         if (dev < 64 && smem > attr_bytes[dev]) attr_bytes[dev] = smem;
     }
-    // weights by 2-D tensor map when the row pitch and base allow it
-    CUtensorMap wmap;
-    std::memset(&wmap, 0, sizeof(wmap));
+    // weights by 2-D tensor map when the row pitch and base (both bases of a
+    // pair) allow it
+    constexpr bool pair = EPI == kEpiPair;
+    WMaps<pair ? 2 : 1> wm;
+    std::memset(&wm, 0, sizeof(wm));
+    auto map_of = [&](CUtensorMap* m, const uint8_t* base) {
+        return reinterpret_cast<uintptr_t>(base) % 16 == 0 &&
+               make_map_2d(m, CU_TENSOR_MAP_DATA_TYPE_UINT64, const_cast<uint8_t*>(base),
+                           (uint64_t)(args.row_bytes / 8), (uint64_t)args.out, (uint64_t)args.row_bytes,
+                           (uint32_t)C::BOXW, 8u, CU_TENSOR_MAP_SWIZZLE_NONE);
+    };
     args.tma2d = 0;
-    if (args.out > 0 && args.row_bytes % 16 == 0 && reinterpret_cast<uintptr_t>(args.w) % 16 == 0 &&
-        make_map_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT64, const_cast<uint8_t*>(args.w),
-                    (uint64_t)(args.row_bytes / 8), (uint64_t)args.out, (uint64_t)args.row_bytes,
-                    (uint32_t)C::BOXW, 8u, CU_TENSOR_MAP_SWIZZLE_NONE))
+    if (args.out > 0 && args.row_bytes % 16 == 0 && map_of(&wm.m[0], args.w) &&
+        (!pair || map_of(&wm.m[pair ? 1 : 0], args.w2)))
         args.tma2d = 1;
+    // output rows per row tile (a pair's tile holds that many rows of each matrix)
+    constexpr int tile_rows = pair ? C::RT / 2 : C::RT;
     const long long units = (args.out + 7) / 8;  // rows are handed out 8 at a time
     const long long want = (long long)sm_count * cps;
     int grid = (int)(units < want ? units : want);
@@ -1004,7 +1086,7 @@ cudaError_t launch_stream_t(GemvArgs args, int sm_count, int smem_per_sm, cudaSt
     // would sit idle at the end and each queue ticket's latency shows.
     args.tiles = nullptr;
     if (INT && args.x_resident &&
-        (args.out + C::RT - 1) / C::RT >= 8LL * grid)
+        (args.out + tile_rows - 1) / tile_rows >= 8LL * grid)
         args.tiles = tile_queue(dev, stream);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
@@ -1016,7 +1098,7 @@ cudaError_t launch_stream_t(GemvArgs args, int sm_count, int smem_per_sm, cudaSt
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, gemv_stream_kernel<F, MT, RPW, MINB, INT>, args, wmap);
+    return cudaLaunchKernelEx(&cfg, gemv_stream_kernel<F, MT, RPW, MINB, INT, EPI>, args, wm);
 }
 
 // rows-per-warp choice per format: keeps the lane-group words of all RPW
@@ -1031,23 +1113,24 @@ constexpr int rpw_for() {
 // One token takes the integer (DP4A) mode: 24 four-way integer dot products
 // and ~12 mask ops per block and row, against ~32 byte-permutes + 16 packed
 // FMAs in the fp32 mode, whose decode cost is shared only from two tokens on.
-template <int F, int MT>
+template <int F, int MT, int EPI>
 cudaError_t dispatch_mt(const GemvArgs& args, int sm_count, int smem_per_sm, cudaStream_t stream) {
     constexpr int RPW = rpw_for<F>();
     constexpr int MINB = MT <= 2 ? 2 : 1;
     if constexpr (MT == 1) {
         // fewer than one full tile per CTA at two CTAs per SM: one CTA per SM
         // (a full tile each, and the whole shared memory for weight stages)
-        if ((long long)args.out < 2LL * sm_count * kConsumerWarps * RPW)
-            return launch_stream_t<F, 1, RPW, 1, true>(args, sm_count, smem_per_sm, stream);
-        return launch_stream_t<F, 1, RPW, 2, true>(args, sm_count, smem_per_sm, stream);
+        const long long streamed_rows = (long long)args.out * (EPI == kEpiPair ? 2 : 1);
+        if (streamed_rows < 2LL * sm_count * kConsumerWarps * RPW)
+            return launch_stream_t<F, 1, RPW, 1, true, EPI>(args, sm_count, smem_per_sm, stream);
+        return launch_stream_t<F, 1, RPW, 2, true, EPI>(args, sm_count, smem_per_sm, stream);
     } else {
         // fp32 mode, measured per token count (q4_0 28672 x 8192): 2 tokens
         // and 8 tokens run best with two rows per warp (fewer live
         // accumulators; 8 tokens also need the four x-loader warps' registers),
         // 4 tokens with four.
         constexpr int RPW_FP = (MT == 4 || RPW < 4) ? RPW : RPW / 2;
-        return launch_stream_t<F, MT, RPW_FP, MINB, false>(args, sm_count, smem_per_sm, stream);
+        return launch_stream_t<F, MT, RPW_FP, MINB, false, EPI>(args, sm_count, smem_per_sm, stream);
     }
 }
 
@@ -1059,19 +1142,24 @@ int gemv_tokens_per_pass(int rows_left) {
 
 cudaError_t launch_gemv_stream(int fmt, const GemvArgs& args, int mt, int sm_count, int smem_per_sm,
                                cudaStream_t stream) {
-#define MLQ_STREAM(F)                                                                  \
+    const int epi = args.w2 ? kEpiPair : kEpiPlain;
+#define MLQ_STREAM_MT(F, E)                                                            \
     switch (mt) {                                                                      \
-        case 1: return dispatch_mt<F, 1>(args, sm_count, smem_per_sm, stream);         \
-        case 2: return dispatch_mt<F, 2>(args, sm_count, smem_per_sm, stream);         \
-        case 4: return dispatch_mt<F, 4>(args, sm_count, smem_per_sm, stream);         \
-        default: return dispatch_mt<F, 8>(args, sm_count, smem_per_sm, stream);        \
+        case 1: return dispatch_mt<F, 1, E>(args, sm_count, smem_per_sm, stream);      \
+        case 2: return dispatch_mt<F, 2, E>(args, sm_count, smem_per_sm, stream);      \
+        case 4: return dispatch_mt<F, 4, E>(args, sm_count, smem_per_sm, stream);      \
+        default: return dispatch_mt<F, 8, E>(args, sm_count, smem_per_sm, stream);     \
     }
+#define MLQ_STREAM(F)                                                                  \
+    if (epi == kEpiPair) MLQ_STREAM_MT(F, kEpiPair)                                    \
+    MLQ_STREAM_MT(F, kEpiPlain)
     switch (fmt) {
         case kQ8_0: MLQ_STREAM(kQ8_0)
         case kQ4_0: MLQ_STREAM(kQ4_0)
         case kQ4_1: MLQ_STREAM(kQ4_1)
     }
 #undef MLQ_STREAM
+#undef MLQ_STREAM_MT
     return cudaErrorInvalidValue;
 }
 

@@ -10,6 +10,10 @@ namespace mlq {
 // Arguments of the streaming GEMV (mlq_gemv.cu).
 struct GemvArgs {
     const uint8_t* w;        // packed blocks, row-major [out][bpr]
+    // SwiGLU pair: a second matrix of w's shape and format (the up
+    // projection, w being the gate); y = silu(x W^T) * (x W2^T).  Null: plain.
+    const uint8_t* w2;
+    const float* bias;       // [global rows] added to every output row, or null (not with w2)
     const float* x;          // [M][in]
     float* ys[8];            // output copies: [0] = this GPU's y, then peers' y
     int ny;                  // number of valid ys
@@ -52,6 +56,7 @@ cudaError_t launch_gemv_generic(int fmt, const uint8_t* w, const float* x, float
 // Arguments of the tensor-core GEMM (mlq_gemm.cu).
 struct GemmArgs {
     float* y;      // [T][out]
+    const float* bias;  // [out] added to every row of y, or null
     int out, in;   // W is [out][in] in blocks
     int T;         // rows of x (tokens)
     int* err;      // device error flag
@@ -64,9 +69,9 @@ bool gemm_supported(int fmt, const void* w, int out, int in, int rows);
 // Workspace bytes of the GEMM (x split into bf16 hi/lo).
 size_t gemm_workspace_bytes(int in, int rows);
 
-// y[T][out] = x[T][in] * W^T on the tensor cores.
+// y[T][out] = x[T][in] * W^T (+ bias[out], when not null) on the tensor cores.
 cudaError_t launch_gemm(int fmt, const uint8_t* w, const float* x, float* y, int out, int in, int rows,
-                        void* ws, int sm_count, int* err, cudaStream_t stream);
+                        const float* bias, void* ws, int sm_count, int* err, cudaStream_t stream);
 
 // Quantize fp32 [rows][cols] -> blocks, reference rules (mlq_convert.cu).
 cudaError_t launch_quantize(int fmt, const float* src, long long rows, int cols, uint8_t* blocks,
@@ -78,5 +83,8 @@ cudaError_t launch_dequantize(int fmt, const uint8_t* blocks, long long rows, in
 
 // y[r][c] += bias[c] for r < rows, c < cols.
 cudaError_t launch_add_bias(float* y, const float* bias, int rows, int cols, cudaStream_t stream);
+
+// h[i] = silu(h[i]) * u[i] for i < n (silu(v) = v / (1 + exp(-v))).
+cudaError_t launch_swiglu(float* h, const float* u, long long n, cudaStream_t stream);
 
 }  // namespace mlq

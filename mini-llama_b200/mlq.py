@@ -56,6 +56,8 @@ def lib() -> ctypes.CDLL:
         L.mlq_device_error.argtypes = [_i, ctypes.POINTER(_i)]
         L.mlq_linear.argtypes = [_i, _vp, _sz, _i, _i, _vp, _i, _vp, _vp]
         L.mlq_linear_noalloc.argtypes = [_i, _vp, _sz, _i, _i, _vp, _i, _vp, _vp]
+        L.mlq_linear_bias.argtypes = [_i, _vp, _sz, _i, _i, _vp, _i, _vp, _vp, _vp]
+        L.mlq_linear_swiglu.argtypes = [_i, _vp, _vp, _sz, _i, _i, _vp, _i, _vp, _vp]
         L.mlq_linear_host.argtypes = [_i, _vp, _sz, _i, _i, _vp, _i, _vp, _vp, _i, _vp]
         L.mlq_linear_host_weight.argtypes = [_i, _vp, _sz, _i, _i, _vp, _i, _vp, _vp, _i]
         L.mlq_dequantize.argtypes = [_i, _vp, _sz, _i, _i, _vp, _vp]
@@ -67,7 +69,8 @@ def lib() -> ctypes.CDLL:
         L.mlq_peer_open.argtypes = [ctypes.c_char_p, ctypes.POINTER(_vp)]
         L.mlq_peer_close.argtypes = [_vp]
         L.mlq_peer_free.argtypes = [_vp]
-        for name in ("mlq_linear", "mlq_linear_noalloc", "mlq_linear_host",
+        for name in ("mlq_linear", "mlq_linear_noalloc", "mlq_linear_bias", "mlq_linear_swiglu",
+                     "mlq_linear_host",
                      "mlq_linear_host_weight", "mlq_dequantize", "mlq_quantize", "mlq_device_error",
                      "mlq_linear_allgather", "mlq_peer_alloc", "mlq_peer_open", "mlq_peer_close",
                      "mlq_peer_free"):
@@ -136,6 +139,54 @@ def linear_raw(fmt, w_ptr: int, nblocks: int, out_features: int, in_features: in
     """Pointer-level call (for CUDA-graph capture and timing loops)."""
     check(lib().mlq_linear(fmt_id(fmt), w_ptr, nblocks, out_features, in_features, x_ptr, rows,
                            y_ptr, stream))
+
+
+def _out_like(x, out_features: int, y):
+    import torch
+    if y is not None:
+        return y
+    rows = 1 if x.dim() == 1 else x.shape[0]
+    shape = (out_features,) if x.dim() == 1 else (rows, out_features)
+    return torch.empty(shape, dtype=torch.float32, device=x.device)
+
+
+def linear_bias(fmt, w, out_features: int, in_features: int, x, bias, y=None, stream=None):
+    """mlq_linear_bias: y = x @ W^T + bias (bias: float32 CUDA [out], or None),
+    the add made in the kernel's store."""
+    rows = 1 if x.dim() == 1 else x.shape[0]
+    y = _out_like(x, out_features, y)
+    nb = w.numel() // BLOCK_BYTES[_fmt_name(fmt)]
+    check(lib().mlq_linear_bias(fmt_id(fmt), w.data_ptr(), nb, out_features, in_features,
+                                x.data_ptr(), rows, None if bias is None else bias.data_ptr(),
+                                y.data_ptr(), _stream_handle(stream)))
+    return y
+
+
+def linear_swiglu(fmt, w_gate, w_up, out_features: int, in_features: int, x, h=None, stream=None):
+    """mlq_linear_swiglu: h = silu(x @ Wg^T) * (x @ Wu^T), both matrices
+    [out, in] in one format."""
+    rows = 1 if x.dim() == 1 else x.shape[0]
+    h = _out_like(x, out_features, h)
+    nb = w_gate.numel() // BLOCK_BYTES[_fmt_name(fmt)]
+    check(lib().mlq_linear_swiglu(fmt_id(fmt), w_gate.data_ptr(),
+                                  None if w_up is None else w_up.data_ptr(), nb, out_features,
+                                  in_features, x.data_ptr(), rows, h.data_ptr(),
+                                  _stream_handle(stream)))
+    return h
+
+
+def linear_swiglu_raw(fmt, wg_ptr: int, wu_ptr: int, nblocks: int, out_features: int,
+                      in_features: int, x_ptr: int, rows: int, h_ptr: int, stream: int | None) -> None:
+    """Pointer-level mlq_linear_swiglu (for CUDA-graph capture and timing loops)."""
+    check(lib().mlq_linear_swiglu(fmt_id(fmt), wg_ptr, wu_ptr, nblocks, out_features, in_features,
+                                  x_ptr, rows, h_ptr, stream))
+
+
+def linear_bias_raw(fmt, w_ptr: int, nblocks: int, out_features: int, in_features: int, x_ptr: int,
+                    rows: int, bias_ptr: int | None, y_ptr: int, stream: int | None) -> None:
+    """Pointer-level mlq_linear_bias."""
+    check(lib().mlq_linear_bias(fmt_id(fmt), w_ptr, nblocks, out_features, in_features, x_ptr, rows,
+                                bias_ptr, y_ptr, stream))
 
 
 # MLQ_NOALLOC_SCRATCH_BYTES and MLQ_GEMM_MIN_ROWS of include/mlq.h

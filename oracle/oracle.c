@@ -272,3 +272,30 @@ int orc_linear(int fmt, const float* x, int64_t xrows, int64_t in, const uint8_t
     for (int t = 1; t < threads; ++t) pthread_join(th[t], NULL);
     return 0;
 }
+
+/* ---------------------------------------------------------------------------
+ * Epilogues that follow the linear in the reference's forward path.
+ * ------------------------------------------------------------------------- */
+
+/* h[i] = silu(gate[i]) * up[i], as the reference's swiGlu (src/ops.cc:111-145):
+ * silu computes val / (1.0 + std::exp(-val)) -- std::exp of a float is the
+ * float exp, the sum and quotient are double -- stored as float, then
+ * elementwiseMul multiplies two floats. */
+int orc_swiglu(const float* gate, const float* up, int64_t n, float* h) {
+    if (n < 0) return -1;
+    for (int64_t i = 0; i < n; ++i) {
+        const float v = gate[i];
+        const float s = (float)((double)v / (1.0 + (double)expf(-v)));
+        h[i] = s * up[i];
+    }
+    return 0;
+}
+
+/* y[r][c] += bias[c]: the host variants' bias add after the download
+ * (src/cuda_quant.cu:326-329), one float add per output. */
+int orc_add_bias(float* y, const float* bias, int64_t rows, int64_t cols) {
+    if (rows < 0 || cols < 0) return -1;
+    for (int64_t r = 0; r < rows; ++r)
+        for (int64_t c = 0; c < cols; ++c) y[r * cols + c] = y[r * cols + c] + bias[c];
+    return 0;
+}

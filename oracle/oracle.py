@@ -72,6 +72,8 @@ class Oracle:
         lib.orc_dequantize.argtypes = [ctypes.c_int, _u8p, ctypes.c_int64, ctypes.c_int64, _f32p]
         lib.orc_linear.argtypes = [ctypes.c_int, _f32p, ctypes.c_int64, ctypes.c_int64, _u8p,
                                    ctypes.c_int64, _f32p, ctypes.c_int]
+        lib.orc_swiglu.argtypes = [_f32p, _f32p, ctypes.c_int64, _f32p]
+        lib.orc_add_bias.argtypes = [_f32p, _f32p, ctypes.c_int64, ctypes.c_int64]
         self.lib = lib
 
     def fp16_from_f32(self, v: float) -> int:
@@ -112,6 +114,24 @@ class Oracle:
         assert rc == 0
         return y.reshape(out_features) if one_d else y
 
+    def swiglu(self, gate: np.ndarray, up: np.ndarray) -> np.ndarray:
+        """silu(gate) * up elementwise (oracle.c orc_swiglu)."""
+        g = np.ascontiguousarray(gate, dtype=np.float32)
+        u = np.ascontiguousarray(up, dtype=np.float32)
+        assert g.shape == u.shape
+        h = np.zeros_like(g)
+        assert self.lib.orc_swiglu(_fp(g), _fp(u), g.size, _fp(h)) == 0
+        return h
+
+    def add_bias(self, y: np.ndarray, bias: np.ndarray) -> np.ndarray:
+        """y + bias over the last axis (oracle.c orc_add_bias); returns a copy."""
+        out = np.array(y, dtype=np.float32, copy=True, order="C")
+        b = np.ascontiguousarray(bias, dtype=np.float32)
+        cols = b.size
+        assert out.shape[-1] == cols
+        assert self.lib.orc_add_bias(_fp(out), _fp(b), out.size // cols, cols) == 0
+        return out
+
 
 class Reference:
     """The reference's own CPU path, compiled from its sources (oracle/_ref)."""
@@ -134,6 +154,7 @@ class Reference:
         lib.ref_blocks_free.argtypes = [ctypes.c_int, ctypes.c_void_p]
         lib.ref_linear_held.argtypes = [ctypes.c_int, _f32p, ctypes.c_int, ctypes.c_int,
                                         ctypes.c_void_p, ctypes.c_int, _f32p]
+        lib.ref_swiglu.argtypes = [_f32p, _f32p, ctypes.c_int, _f32p]
         self.lib = lib
         self.variant = variant
         self.path = path
@@ -176,6 +197,14 @@ class Reference:
                                  out_features, _fp(y))
         assert rc == 0, rc
         return y.reshape(out_features) if one_d else y
+
+    def swiglu(self, gate: np.ndarray, up: np.ndarray) -> np.ndarray:
+        """The reference's swiGlu on 1-D tensors."""
+        g = np.ascontiguousarray(gate, dtype=np.float32).reshape(-1)
+        u = np.ascontiguousarray(up, dtype=np.float32).reshape(-1)
+        h = np.zeros_like(g)
+        assert self.lib.ref_swiglu(_fp(g), _fp(u), g.size, _fp(h)) == 0
+        return h.reshape(np.shape(gate))
 
     def hold(self, fmt: str, blocks: np.ndarray):
         """Copy blocks into a reference-owned std::vector once (for timing)."""

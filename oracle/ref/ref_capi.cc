@@ -13,10 +13,12 @@
 //   dequantizeFromQ80 / Q40 / Q41          quant.h:269, 279, 285
 //   linearQ80 / linearQ40 / linearQ41      quant.h:293-298
 //   ThreadPool::setThreadCount             threadpool.h:39
+//   swiGlu (silu(gate) * up)               ops.h:35-36
 #include <cstdint>
 #include <cstring>
 #include <vector>
 
+#include "mini_llama/ops.h"
 #include "mini_llama/quant.h"
 #include "mini_llama/quantized_tensor.h"
 #include "mini_llama/tensor.h"
@@ -113,6 +115,16 @@ void ref_blocks_free(int fmt, void* h) {
     if (fmt == 8) delete static_cast<std::vector<BlockQ80>*>(h);
     else if (fmt == 2) delete static_cast<std::vector<BlockQ40>*>(h);
     else if (fmt == 3) delete static_cast<std::vector<BlockQ41>*>(h);
+}
+
+// h[i] = silu(gate[i]) * up[i] through the reference's swiGlu (1-D tensors).
+int ref_swiglu(const float* gate, const float* up, int n, float* h) {
+    Tensor g = makeMatrix(gate, 0, n);
+    Tensor u = makeMatrix(up, 0, n);
+    Tensor r = swiGlu(g, u);
+    if (r.data.size() != static_cast<size_t>(n)) return -2;
+    std::memcpy(h, r.data.data(), r.data.size() * sizeof(float));
+    return 0;
 }
 
 int ref_linear_held(int fmt, const float* x, int xrows, int in, const void* handle, int out,

@@ -16,6 +16,9 @@ Cases
     dequantizeFromQ41 and linearQ41 (quant.cc:350-392, 646-650).
   * The fillLinear inputs of the reference's GPU tests
     (tests/test_cuda.cc:66-77, 679-743, makeQ41Blocks :115-131).
+  * swiGlu (src/ops.cc:111-145) on gate values spanning -100..100 (exp
+    overflow and underflow included) and on the outputs of two q4_0 linears
+    sharing one x (the fused gate/up case).
 The inputs come from the seeded generator of mini-llama_b200/synth.py.
 """
 from __future__ import annotations
@@ -104,6 +107,19 @@ def main() -> None:
     b41 = q41_test_blocks(4, 32)
     out["tc_q4_1_blocks"] = b41
     out["tc_q4_1_y"] = ref.linear("q4_1", xt, b41, 4)
+    # swiGlu: elementwise edge values, then a gate/up pair of q4_0 linears
+    g = np.concatenate([np.linspace(-100.0, 100.0, 101, dtype=np.float32),
+                        synth.normal((155,), seed=5000, std=4.0)]).astype(np.float32)
+    u = synth.normal((256,), seed=5001, std=1.0)
+    out["swiglu_gate"], out["swiglu_up"] = g, u
+    out["swiglu_h"] = ref.swiglu(g, u)
+    wg = synth.normal((48, 256), seed=5002, std=0.02)
+    wu = synth.normal((48, 256), seed=5003, std=0.02)
+    xs = synth.normal((3, 256), seed=5004, std=1.0)
+    bg, bu = ref.quantize("q4_0", wg), ref.quantize("q4_0", wu)
+    yg, yu = ref.linear("q4_0", xs, bg, 48), ref.linear("q4_0", xs, bu, 48)
+    out["ffn_gate_blocks"], out["ffn_up_blocks"], out["ffn_x"] = bg, bu, xs
+    out["ffn_h"] = np.stack([ref.swiglu(yg[r], yu[r]) for r in range(3)])
     np.savez_compressed(HERE / "reference_quant.npz", **out)
     print(f"wrote {len(out)} arrays to {HERE / 'reference_quant.npz'}")
 

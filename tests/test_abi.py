@@ -68,6 +68,22 @@ def test_validation_before_any_cuda_call(pkg):
     # (no call here ever passes validation: the pointers above are fake)
 
 
+def test_fused_entry_points_validate_first(pkg):
+    """mlq_linear_bias / mlq_linear_swiglu run mlq_linear's checks, and the
+    pair's second weight pointer is checked too, all before any CUDA call."""
+    lib = pkg.mlq.lib()
+    assert lib.mlq_linear_bias(7, 0x1000, 4, 4, 32, 0x2000, 1, 0x4000, 0x3000, None) == 1
+    assert lib.mlq_linear_bias(8, None, 4, 4, 32, 0x2000, 1, 0x4000, 0x3000, None) == 2
+    assert lib.mlq_linear_bias(8, 0x1000, 3, 4, 32, 0x2000, 1, 0x4000, 0x3000, None) == 5
+    assert b"mlq_linear_bias(Q80)" in lib.mlq_last_error()
+    assert lib.mlq_linear_swiglu(2, 0x1000, None, 4, 4, 32, 0x2000, 1, 0x3000, None) == 2
+    assert b"null up-projection weight pointer" in lib.mlq_last_error()
+    assert lib.mlq_linear_swiglu(2, None, 0x1800, 4, 4, 32, 0x2000, 1, 0x3000, None) == 2
+    assert lib.mlq_linear_swiglu(2, 0x1000, 0x1800, 4, 4, 32, 0x2000, 0, 0x3000, None) == 3
+    assert lib.mlq_linear_swiglu(2, 0x1000, 0x1800, 4, 4, 32, None, 1, 0x3000, None) == 2
+    assert lib.mlq_linear_swiglu(3, 0x1000, 0x1800, 5, 4, 32, 0x2000, 1, 0x3000, None) == 5
+
+
 def test_host_entry_points_validate_first(pkg):
     mlq = pkg.mlq
     x = np.zeros(32, np.float32)

@@ -59,6 +59,32 @@ def test_reference_gpu_test_inputs(oracle, golden):
     assert np.array_equal(bits(y), bits(golden["tc_q4_1_y"]))
 
 
+def test_swiglu_matches_reference(oracle, golden):
+    """orc_swiglu against the reference's swiGlu (src/ops.cc:111-145), gate
+    values -100..100 (exp overflow / underflow) and random ones: bit-exact."""
+    h = oracle.swiglu(golden["swiglu_gate"], golden["swiglu_up"])
+    assert np.array_equal(bits(h), bits(golden["swiglu_h"]))
+
+
+def test_gate_up_pair_matches_reference(oracle, golden):
+    """The SwiGLU of two q4_0 linears sharing x (ffnForwardDevice's gate, up
+    and forwardSwiGluDevice, src/forward.cc:573-581): oracle linear + swiglu
+    reproduces the reference's outputs bit for bit."""
+    x = golden["ffn_x"]
+    g = oracle.linear("q4_0", x, golden["ffn_gate_blocks"], 48)
+    u = oracle.linear("q4_0", x, golden["ffn_up_blocks"], 48)
+    assert np.array_equal(bits(oracle.swiglu(g, u)), bits(golden["ffn_h"]))
+
+
+def test_add_bias_matches_host_add(oracle, golden):
+    """orc_add_bias = the reference host variants' y[r][c] += bias[c]
+    (src/cuda_quant.cu:326-329) on the reference GPU tests' bias."""
+    y = golden["tc_q8_0_y2"]
+    out = oracle.add_bias(y, golden["tc_bias"])
+    assert np.array_equal(bits(out), bits((y + golden["tc_bias"][None, :]).astype(np.float32)))
+    assert np.array_equal(bits(y), bits(golden["tc_q8_0_y2"]))  # input untouched
+
+
 # --- the reference's known-answer tests (tests/test_quant.cc) ------------------------------
 def test_block_layout(pkg):
     # test_quant.cc:11-15, 184-194
