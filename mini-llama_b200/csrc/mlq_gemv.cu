@@ -43,6 +43,11 @@
 //    the previous kernel drains; x and y wait for it (griddepcontrol).
 //  * Sharded calls store every row into every rank's y (NVLink peer
 //    stores) and end with a cross-GPU completion handshake.
+//  * Epilogues: an optional bias add in the store (runtime check), or -- a
+//    separate instantiation -- a SwiGLU pair: each row tile carries the
+//    same rows of the gate and up matrices (two tensor maps), and the store
+//    writes silu(gate) * up (the feed-forward input of the reference's
+//    ffnForwardDevice, src/forward.cc:573-581).
 //  * Every mbarrier wait is bounded (2 s); on expiry the kernel records an
 //    error code in *err and returns after its in-flight copies land.
 #include <cuda_runtime.h>
