@@ -394,6 +394,8 @@ __global__ void __launch_bounds__(threads_for(MT), MINB)
         uint32_t seq = 0;
         int s = 0;
         uint32_t ph = 0;
+        // every weight byte is read once per launch: evict-first in L2
+        const uint64_t wpol = l2_evict_first_policy();
         // lane 0 holds the next queue ticket, fetched one tile ahead
         unsigned int ticket = (dyn && lane == 0) ? atomicAdd(a.tiles, 1u) : 0u;
         for (int t = 0; dyn || t < ntiles; ++t) {
@@ -436,8 +438,9 @@ __global__ void __launch_bounds__(threads_for(MT), MINB)
                         const bool second = pair && b >= nb;
                         const int k = second ? b - nb : b;
                         const int rb = second ? C::RT / 16 + k : k;
-                        tma_load_2d(stage + (uint32_t)(reg * C::REGION + rb * 8 * C::BOXB), second ? &wmap2 : &wmap,
-                                    kt * C::NREG * C::BOXW + reg * C::BOXW, (int)(row0 + 8 * k), fb);
+                        tma_load_2d_hint(stage + (uint32_t)(reg * C::REGION + rb * 8 * C::BOXB),
+                                         second ? &wmap2 : &wmap, kt * C::NREG * C::BOXW + reg * C::BOXW,
+                                         (int)(row0 + 8 * k), fb, wpol);
                     }
                 } else {
                 // lane i streams stage row i's segment (RT <= 32 rows per tile;
@@ -461,7 +464,8 @@ __global__ void __launch_bounds__(threads_for(MT), MINB)
                 for (int off = 16; off > 0; off >>= 1) tx += __shfl_xor_sync(0xffffffffu, tx, off);
                 if (lane == 0) mbar_expect_tx(fb, tx);
                 __syncwarp();
-                if (bytes) bulk_g2s(stage + (uint32_t)lane * C::SLOT, reinterpret_cast<const void*>(lo), bytes, fb);
+                if (bytes)
+                    bulk_g2s_hint(stage + (uint32_t)lane * C::SLOT, reinterpret_cast<const void*>(lo), bytes, fb, wpol);
                 if (row_ok) {
                     // bytes past the array's last 16-B boundary: plain copy
                     for (uintptr_t q = (bytes ? hi : lo); q < src + seg; ++q)
