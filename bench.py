@@ -280,6 +280,25 @@ def reference_cpu_baseline(pkg, seconds):
 SHARD_MIN_BYTES = 100 * MB
 
 
+def gemv_passes(rows):
+    """Streaming-GEMV launches for `rows` rows of x (passes of 8, 4, 2, 1
+    tokens: gemv_tokens_per_pass in csrc/mlq_gemv.cu)."""
+    n = 0
+    while rows > 0:
+        rows -= min(rows, 8 if rows >= 5 else 4 if rows >= 3 else 2 if rows == 2 else 1)
+        n += 1
+    return n
+
+
+def launches_per_call(mlq, rows, out_f, local, pair):
+    """Kernel launches of one library call in this bench (all shapes here are
+    aligned for every kernel): the GEMM is an x-split launch plus the GEMM
+    (per matrix of a pair, plus the SwiGLU pass); the GEMV one launch per pass."""
+    if local and mlq.takes_gemm(rows, out_f):
+        return 5 if pair else 2
+    return gemv_passes(rows)
+
+
 def placement(world):
     if world == 1:
         return {name: "shard" for name, _, _ in WORKLOAD["matrices"]}
@@ -399,7 +418,8 @@ def run_mlq(args):
                            sh_stream)
             calls.append(call)
             ybufs.append(lambda lin=lin: lin.y_ptr(epoch[0]))
-        launches_per_step += 1  # one gemv_stream_kernel launch per call (batch 1: one pass)
+        on_one_gpu = world == 1 or placement(world)[name] == "local0"
+        launches_per_step += launches_per_call(mlq, rows, out_f, on_one_gpu, bool(pair) and name == pair[0])
 
     def step(events=None):
         for j, call in enumerate(calls):
@@ -531,8 +551,12 @@ def run_mlq(args):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = reference_cpu_baseline(pkg, args.cpu_seconds)
 
+    # the dominant launch's kernel: sharded calls always stream; local calls
+    # follow the library's routing rule (MLQ_GEMM_ROWS_RULE)
+    dom_local = world == 1 or placement(world)[dom] == "local0"
+    dom_gemm = dom_local and mlq.takes_gemm(rows, mats[dj][1])
     kernel = (f"gemv_stream_kernel<{fmt}, MT={rows}, integer mode>" if rows == 1 else
-              f"gemv_stream_kernel<{fmt}, MT={min(rows, 8)}, fp32 mode>" if rows < 16 else
+              f"gemv_stream_kernel<{fmt}, MT={min(rows, 8)}, fp32 mode>" if not dom_gemm else
               f"gemm_tc_kernel<{fmt}>") + f" ({dom} launch, rank 0)"
     roof = {"bound": "hbm", "kernel": kernel, "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
             "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
@@ -543,7 +567,7 @@ def run_mlq(args):
             "all_launches_GBps": round(sum(local_bytes(j) for j in range(len(mats)) if calls[j] is not None)
                                        / (kernel_sum_ms / 1e3) / 1e9, 1),
             "per_launch_ms": {k: round(v, 5) for k, v in per.items()}}
-    if rows >= 16:
+    if dom_gemm:
         # the GEMM is tensor-bound: algorithmic flops of the dominant launch
         # (2 * rows * its rows of W * in) against the measured bf16 peak
         b_, e_ = ranges[dj][rank]

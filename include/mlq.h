@@ -102,9 +102,22 @@ MLQ_API mlq_status mlq_linear(mlq_format fmt, const void* w, size_t block_count,
                               int out_features, int in_features, const float* x, int rows,
                               float* y, mlq_stream stream);
 
-/* Calls with at least this many rows of x take the tensor-core (tcgen05)
- * GEMM; fewer rows take the streaming GEMV. */
-#define MLQ_GEMM_MIN_ROWS 16
+/* Which kernel a call takes.  The tensor-core (tcgen05) GEMM's time hardly
+ * depends on the rows of x (one decode of every weight per 128-row tile),
+ * the streaming GEMV's grows with every pass of <= 8 rows.  A call takes
+ * the GEMM when it has at least MLQ_GEMM_MIN_ROWS rows of x, or at least
+ * MLQ_GEMM_WIDE_MIN_ROWS rows on a matrix with at least
+ * MLQ_GEMM_WIDE_MIN_OUT output features (enough 128-row tiles to occupy
+ * the GPU); MLQ_GEMM_ROWS_RULE(rows, out) is that test.  The GEMM also
+ * needs 16-B aligned weights with a 16-B multiple row pitch and
+ * in_features % 8 == 0; other calls take the streaming GEMV.  (Measured on
+ * B200: q4_0 28672x8192 at 8 rows, GEMM 174 us vs GEMV 205 us; q4_0
+ * 8192x28672 at 8 rows, GEMM 293 us vs GEMV 213 us.) */
+#define MLQ_GEMM_MIN_ROWS 9
+#define MLQ_GEMM_WIDE_MIN_ROWS 5
+#define MLQ_GEMM_WIDE_MIN_OUT 12288
+#define MLQ_GEMM_ROWS_RULE(rows, out) \
+    ((rows) >= MLQ_GEMM_MIN_ROWS || ((rows) >= MLQ_GEMM_WIDE_MIN_ROWS && (out) >= MLQ_GEMM_WIDE_MIN_OUT))
 
 /* mlq_linear that never allocates device memory.  No counterpart in the
  * reference (its GPU linear cudaMallocs its output on every call,
@@ -117,11 +130,11 @@ MLQ_API mlq_status mlq_linear(mlq_format fmt, const void* w, size_t block_count,
  * its per-stream workspace by free + malloc when a larger shape arrives).
  *
  * Same arguments, results and validation as mlq_linear.  The tensor-core
- * path (rows >= MLQ_GEMM_MIN_ROWS) keeps the bf16 hi/lo split of x in a
- * static MLQ_NOALLOC_SCRATCH_BYTES array of the library's device module
- * instead of a workspace; so rows >= MLQ_GEMM_MIN_ROWS with
- * rows * in_features * 4 bytes above that
- * size returns MLQ_ERR_RANGE before any CUDA call.  The array is one per
+ * path keeps the bf16 hi/lo split of x in a static
+ * MLQ_NOALLOC_SCRATCH_BYTES array of the library's device module instead
+ * of a workspace; so a call with MLQ_GEMM_ROWS_RULE(rows, out_features)
+ * true and rows * in_features * 4 bytes above that size returns
+ * MLQ_ERR_RANGE before any CUDA call.  The array is one per
  * device, shared by every call: calls ordered on one stream are fine,
  * calls whose kernels may overlap (several streams, several host threads)
  * race on it.  Nothing in it needs to start zeroed.  The first call on a
@@ -150,10 +163,10 @@ MLQ_API mlq_status mlq_linear_bias(mlq_format fmt, const void* w, size_t block_c
  * shape [out_features, in_features] (block_count blocks each); h is
  * rows x out_features.  Replaces the gate and up forwardLinearDevice calls
  * and forwardSwiGluDevice of ffnForwardDevice (src/forward.cc:573-581,
- * 361-369).  Below MLQ_GEMM_MIN_ROWS rows it is one streaming launch whose
- * row tiles carry matching rows of both matrices, so gate and up are never
- * stored; from MLQ_GEMM_MIN_ROWS rows on, one tensor-core GEMM per matrix
- * (up into the per-stream workspace) and one elementwise pass. */
+ * 361-369).  A call that takes the GEMV (see MLQ_GEMM_ROWS_RULE) is one
+ * streaming launch whose row tiles carry matching rows of both matrices, so
+ * gate and up are never stored; a GEMM call runs one tensor-core GEMM per
+ * matrix (up into the per-stream workspace) and one elementwise pass. */
 MLQ_API mlq_status mlq_linear_swiglu(mlq_format fmt, const void* w_gate, const void* w_up,
                                      size_t block_count, int out_features, int in_features,
                                      const float* x, int rows, float* h, mlq_stream stream);

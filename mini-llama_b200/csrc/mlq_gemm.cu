@@ -1,5 +1,5 @@
 // mlq_gemm.cu -- dequant-fused GEMM on the 5th-generation tensor cores
-// (tcgen05 + TMEM) for prefill / batched rows of x (rows >= MLQ_GEMM_MIN_ROWS = 16).
+// (tcgen05 + TMEM) for prefill / batched rows of x (MLQ_GEMM_ROWS_RULE in mlq.h).
 //
 // The reference has no GEMM for quantized weights: forwardBatch loops the
 // GEMV one token at a time (src/batch.cc:32-55) and linearQ* loops rows
@@ -477,9 +477,8 @@ cudaError_t launch_gemm_f(const uint8_t* w, const float* x, float* y, int out, i
 }  // namespace
 
 bool gemm_supported(int fmt, const void* w, int out, int in, int rows) {
-    (void)out;
     const long long row_bytes = (long long)((in + kQK - 1) / kQK) * block_bytes(fmt);
-    return rows >= MLQ_GEMM_MIN_ROWS && reinterpret_cast<uintptr_t>(w) % 16 == 0 && row_bytes % 16 == 0 &&
+    return MLQ_GEMM_ROWS_RULE(rows, out) && reinterpret_cast<uintptr_t>(w) % 16 == 0 && row_bytes % 16 == 0 &&
            in % 8 == 0 && encode_fn() != nullptr;
 }
 

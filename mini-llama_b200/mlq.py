@@ -189,14 +189,22 @@ def linear_bias_raw(fmt, w_ptr: int, nblocks: int, out_features: int, in_feature
                                 bias_ptr, y_ptr, stream))
 
 
-# MLQ_NOALLOC_SCRATCH_BYTES and MLQ_GEMM_MIN_ROWS of include/mlq.h
+# MLQ_NOALLOC_SCRATCH_BYTES and the GEMM routing constants of include/mlq.h
 NOALLOC_SCRATCH_BYTES = 16 << 20
-GEMM_MIN_ROWS = 16
+GEMM_MIN_ROWS = 9
+GEMM_WIDE_MIN_ROWS = 5
+GEMM_WIDE_MIN_OUT = 12288
+
+
+def takes_gemm(rows: int, out_features: int) -> bool:
+    """MLQ_GEMM_ROWS_RULE of include/mlq.h: the row/width part of the routing
+    between the tensor-core GEMM and the streaming GEMV."""
+    return rows >= GEMM_MIN_ROWS or (rows >= GEMM_WIDE_MIN_ROWS and out_features >= GEMM_WIDE_MIN_OUT)
 
 
 def linear_noalloc(fmt, w, out_features: int, in_features: int, x, y, stream=None):
     """mlq_linear_noalloc: like linear() but the library allocates no device
-    memory (the caller passes y; rows >= GEMM_MIN_ROWS need rows * in * 4 bytes <=
+    memory (the caller passes y; calls that take the GEMM need rows * in * 4 bytes <=
     NOALLOC_SCRATCH_BYTES)."""
     rows = 1 if x.dim() == 1 else x.shape[0]
     nb = w.numel() // BLOCK_BYTES[_fmt_name(fmt)]

@@ -4,7 +4,8 @@
   linear per matrix, then orc_swiglu, which is bit-exact with the
   reference's swiGlu), relative L2 <= 1e-3 per output row (the linear
   contract), over every route a call can take: the one-token integer GEMV,
-  the fp32 GEMV passes (2..15 rows), the tensor-core GEMM (>= 16 rows), the
+  the fp32 GEMV passes (2..8 rows; 13 rows where the GEMM does not take the
+  row pitch), the tensor-core GEMM (from 9 rows, or 5 on a wide matrix), the
   1-D bulk-copy stream (row pitch not a multiple of 16 B), the any-alignment
   fallback, the dynamic row-tile queue and a captured CUDA graph.  The fused
   launch is also checked against the unfused library calls (mlq_linear per
@@ -45,7 +46,8 @@ def oracle_h(oracle, fmt, x, wg, wu, out_f):
     return oracle.swiglu(oracle.linear(fmt, x, wg, out_f), oracle.linear(fmt, x, wu, out_f))
 
 
-# (fmt, out, in, rows): one token (integer mode), fp32 passes, GEMM, partial tiles,
+# (fmt, out, in, rows): one token (integer mode), fp32 passes, GEMM (13 and 16+
+# rows, and 8 rows of a wide matrix below), partial tiles,
 # the 1-D bulk stream (q4_0 in=320: 180-byte rows), the generic fallback (q8_0
 # in=96: odd block count per row)
 PAIR_CASES = [
@@ -62,8 +64,10 @@ PAIR_CASES = [
     ("q8_0", 300, 1280, 40),
     ("q4_0", 200, 320, 1),
     ("q4_0", 200, 320, 5),
+    ("q4_0", 200, 320, 13),      # no GEMM for this row pitch: GEMV passes of 8 + 5 rows
     ("q8_0", 100, 96, 1),
     ("q8_0", 100, 96, 20),
+    ("q4_1", 12288, 512, 8),     # wide: the GEMM pair from 5 rows
 ]
 
 

@@ -1,4 +1,5 @@
-"""The tensor-core GEMM path (rows of x >= 16) against the CPU oracle.
+"""The tensor-core GEMM path against the CPU oracle (calls with >= 9 rows of
+x, or >= 5 rows on matrices with >= 12288 output features: MLQ_GEMM_ROWS_RULE).
 
 Same contract as the GEMV: relative L2 error of every output row <= 1e-3.
 The bf16x3 split keeps the GEMM within ~1e-5 of fp32, so the tests also
@@ -33,7 +34,10 @@ CASES = [
     ("q4_1", 129, 96, 65),       # in: one full and one partial 64-wide K-step
     ("q8_0", 384, 1280, 256),    # in: 5 K-chunks of 256
     ("q4_1", 640, 4160, 96),     # in % 256 = 64
-    ("q8_0", 512, 4096, 16),     # smallest GEMM row count (batched decode)
+    ("q8_0", 512, 4096, 16),     # batched decode
+    ("q8_0", 512, 4096, 9),      # smallest GEMM row count on a narrow matrix
+    ("q4_0", 12288, 1024, 5),    # wide matrix: the GEMM from 5 rows
+    ("q4_1", 12300, 512, 7),     # wide, partial last row tile
     ("q4_0", 300, 2048, 20),
     ("q4_1", 256, 1024, 33),
     ("q8_0", 384, 1024, 24),     # 32-wide tile, stage count trimmed to fit shared memory

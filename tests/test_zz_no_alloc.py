@@ -38,7 +38,7 @@ def _pair(pkg, oracle, fmt, out_f, in_f, rows, seed):
     ("q4_0", 512, 4096, 128),   # tensor-core GEMM
     ("q8_0", 384, 1280, 200),   # GEMM, partial tiles
     ("q4_1", 300, 1024, 64),
-    ("q8_0", 256, 1024, 16),    # GEMM at its smallest row count
+    ("q8_0", 256, 1024, 9),     # GEMM at its smallest row count
     ("q4_0", 256, 2048, 3),     # GEMV (no scratch at all)
 ])
 def test_noalloc_matches_linear_two_calls(pkg, oracle, fmt, out_f, in_f, rows):
@@ -93,8 +93,9 @@ def test_noalloc_rejects_oversize_gemm(pkg, oracle):
 def test_noalloc_large_x_below_gemm_rows(pkg, oracle):
     """rows below the GEMM threshold take the GEMV, which needs no scratch:
     x larger than the scratch is accepted and matches mlq_linear."""
-    fmt, out_f, in_f = "q8_0", 64, 280064
+    fmt, out_f, in_f = "q8_0", 64, 524352
     rows = pkg.mlq.GEMM_MIN_ROWS - 1
+    assert not pkg.mlq.takes_gemm(rows, out_f)
     assert rows * in_f * 4 > pkg.mlq.NOALLOC_SCRATCH_BYTES
     w, xs = _pair(pkg, oracle, fmt, out_f, in_f, rows, seed=31)
     y = torch.empty((rows, out_f), dtype=torch.float32, device="cuda")
