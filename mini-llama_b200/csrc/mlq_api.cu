@@ -225,8 +225,10 @@ mlq_status run_linear(int fmt, const void* w, int out, int in, const float* x, i
         mlq_status st = MLQ_OK;
         DeviceState* ds = device_state(dev, &st);
         if (!ds) return st;
-        // workspace: the GEMM's x split, then (pair) the up projection's output
-        const size_t xsplit = gemm ? (mlq::gemm_workspace_bytes(in, rows) + 255) & ~(size_t)255 : 0;
+        // workspace: the GEMM's x split and split-K partials, then (pair) the
+        // up projection's output
+        const int split = gemm ? mlq::gemm_split(out, in, rows, ds->sm_count) : 1;
+        const size_t xsplit = gemm ? (mlq::gemm_workspace_bytes(in, rows, out, split) + 255) & ~(size_t)255 : 0;
         const size_t ubytes = ep.w2 ? (size_t)rows * out * sizeof(float) : 0;
         void* ws = nullptr;
         if (xsplit + ubytes > 0) {
@@ -237,11 +239,11 @@ mlq_status run_linear(int fmt, const void* w, int out, int in, const float* x, i
         if (gemm) {
             // many rows of x: the tensor-core GEMM (bias in its store; a pair
             // runs it per matrix, then one SwiGLU pass)
-            e = mlq::launch_gemm(fmt, static_cast<const uint8_t*>(w), x, y, out, in, rows, ep.bias, ws,
+            e = mlq::launch_gemm(fmt, static_cast<const uint8_t*>(w), x, y, out, in, rows, ep.bias, ws, split,
                                  ds->sm_count, ds->err_flag, stream);
             if (e == cudaSuccess && ep.w2)
                 e = mlq::launch_gemm(fmt, static_cast<const uint8_t*>(ep.w2), x, u, out, in, rows, nullptr, ws,
-                                     ds->sm_count, ds->err_flag, stream);
+                                     split, ds->sm_count, ds->err_flag, stream);
             if (e != cudaSuccess) return fail_cuda("gemm launch", e);
         } else {
             // layouts the streaming kernel does not take: the any-alignment GEMV
@@ -292,7 +294,10 @@ mlq_status run_linear_noalloc(int fmt, const void* w, int out, int in, const flo
     std::call_once(s.once, [&] { s.err = cudaGetSymbolAddress(&s.ptr, g_mlq_noalloc_scratch); });
     if (s.err != cudaSuccess || s.ptr == nullptr)
         return fail_cuda("cudaGetSymbolAddress (static scratch)", s.err != cudaSuccess ? s.err : cudaErrorInvalidSymbol);
-    e = mlq::launch_gemm(fmt, static_cast<const uint8_t*>(w), x, y, out, in, rows, nullptr, s.ptr,
+    // split-K only when its partials fit the scratch next to the x split
+    int split = mlq::gemm_split(out, in, rows, ds->sm_count);
+    if (mlq::gemm_workspace_bytes(in, rows, out, split) > (size_t)MLQ_NOALLOC_SCRATCH_BYTES) split = 1;
+    e = mlq::launch_gemm(fmt, static_cast<const uint8_t*>(w), x, y, out, in, rows, nullptr, s.ptr, split,
                          ds->sm_count, ds->err_flag, stream);
     return e == cudaSuccess ? MLQ_OK : fail_cuda("gemm launch", e);
 }
@@ -397,7 +402,7 @@ MLQ_API mlq_status mlq_linear_noalloc(mlq_format fmt, const void* w, size_t bloc
         mlq_status st = validate_linear(fmt, w, block_count, out_features, in_features, x, rows, y,
                                         "mlq_linear_noalloc");
         if (st != MLQ_OK) return st;
-        const size_t need = mlq::gemm_workspace_bytes(in_features, rows);
+        const size_t need = mlq::gemm_workspace_bytes(in_features, rows, out_features, 1);
         if (MLQ_GEMM_ROWS_RULE(rows, out_features) && need > (size_t)MLQ_NOALLOC_SCRATCH_BYTES)
             return fail(MLQ_ERR_RANGE,
                         "mlq_linear_noalloc: rows * in_features * 4 = " + std::to_string(need) +

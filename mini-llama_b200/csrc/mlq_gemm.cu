@@ -237,16 +237,27 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
     const int tiles_n = (a.T + NT - 1) / NT;
     const int tiles_m = (a.out + BM - 1) / BM;
-    const int ntiles = tiles_m * tiles_n;
+    const int ntiles = tiles_m * tiles_n * a.split;  // (row tile, token tile, K range)
     const int KS = (a.in + BK - 1) / BK;
+    const int KSR = a.kchunks_per_split * KSUB;      // K-steps per range (whole W chunks)
+    // tile -> row tile mt, token tile nt, K-steps [ks0, ks1) of range kr
+    auto decompose = [&](int tile, int& mt, int& nt, int& kr, int& ks0, int& ks1) {
+        kr = tile % a.split;
+        const int mn = tile / a.split;
+        mt = mn / tiles_n;
+        nt = mn % tiles_n;
+        ks0 = kr * KSR;
+        ks1 = min(KS, ks0 + KSR);
+    };
 
     if (warp == 0) {
         // ------------------------------ TMA producer ------------------------------
         if (lane == 0) {
             uint32_t g = 0, gc = 0;
             for (int tile = blockIdx.x; tile < ntiles && !*(volatile int*)&abort_flag; tile += gridDim.x) {
-                const int mt = tile / tiles_n, nt = tile % tiles_n;
-                for (int ks = 0; ks < KS; ++ks, ++g) {
+                int mt, nt, kr, ks0, ks1;
+                decompose(tile, mt, nt, kr, ks0, ks1);
+                for (int ks = ks0; ks < ks1; ++ks, ++g) {
                     if (ks % KSUB == 0) {
                         const int sw = (int)(gc % W_STAGES);
                         if (!mbar_wait(smem_u32(&w_empty[sw]), ((gc / W_STAGES) & 1u) ^ 1u)) {
@@ -283,7 +294,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     break;
                 }
                 tc_fence_after();
-                for (int ks = 0; ks < KS; ++ks, ++g) {
+                int mt, nt, kr, ks0, ks1;
+                decompose(tile, mt, nt, kr, ks0, ks1);
+                for (int ks = ks0; ks < ks1; ++ks, ++g) {
                     const int s = (int)(g % AB_STAGES);
                     if (!mbar_wait(smem_u32(&ab_full[s]), (g / AB_STAGES) & 1u)) {
                         report_error(a.err, 13);
@@ -296,7 +309,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
                     for (int k = 0; k < BK / 16; ++k) {
                         const uint64_t adv = (uint64_t)(k * 32) >> 4;  // 16 bf16 = 32 B along K
-                        mma_bf16<NT>(tmem, dah + adv, dbh + adv, (ks | k) != 0);
+                        mma_bf16<NT>(tmem, dah + adv, dbh + adv, (ks != ks0 || k != 0) ? 1u : 0u);
                         mma_bf16<NT>(tmem, dah + adv, dbl + adv, 1u);
                         mma_bf16<NT>(tmem, dal + adv, dbh + adv, 1u);
                     }
@@ -323,9 +336,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const uint32_t swz = (uint32_t)(row & 7);
         uint32_t g = 0, gc = 0, tc = 0;
         for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++tc) {
-            const int mt = tile / tiles_n, nt = tile % tiles_n;
+            int mt, nt, kr, ks0, ks1;
+            decompose(tile, mt, nt, kr, ks0, ks1);
             int sw = 0;
-            for (int ks = 0; ks < KS; ++ks, ++g) {
+            for (int ks = ks0; ks < ks1; ++ks, ++g) {
                 if (ks % KSUB == 0) {
                     sw = (int)(gc % W_STAGES);
                     if (!mbar_wait(smem_u32(&w_full[sw]), (gc / W_STAGES) & 1u)) {
@@ -370,9 +384,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 __syncwarp();
                 if (lane == 0) {
                     mbar_arrive(smem_u32(&ab_full[s]));
-                    if (ks % KSUB == KSUB - 1 || ks == KS - 1) mbar_arrive(smem_u32(&w_empty[sw]));
+                    if (ks % KSUB == KSUB - 1 || ks == ks1 - 1) mbar_arrive(smem_u32(&w_empty[sw]));
                 }
-                if (ks % KSUB == KSUB - 1 || ks == KS - 1) ++gc;
+                if (ks % KSUB == KSUB - 1 || ks == ks1 - 1) ++gc;
             }
             // epilogue: TMEM -> registers -> y (consecutive rows across lanes)
             if (!mbar_wait(smem_u32(&acc_full), tc & 1u)) {
@@ -382,8 +396,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             tc_fence_after();
             const int o = mt * BM + row;
             // this thread's output feature: one bias value for all its columns
-            const bool has_bias = a.bias != nullptr && o < a.out;
+            // (split-K: the partials carry none; the reduction adds it)
+            const bool has_bias = a.split == 1 && a.bias != nullptr && o < a.out;
             const float bo = has_bias ? a.bias[o] : 0.0f;
+            float* const dst = a.split == 1 ? a.y : a.part + (long long)kr * a.T * a.out;
             // 32-column chunks of the accumulator, split between the halves
             constexpr int NCH = NT < 32 ? 1 : NT / 32;
             constexpr int PER = NCH >= 2 ? NCH / 2 : 1;
@@ -397,7 +413,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     if (c * 32 + j >= NT) break;
                     if (o < a.out && t < a.T) {
                         const float yv = __uint_as_float(v[j]);
-                        a.y[(long long)t * a.out + o] = has_bias ? __fadd_rn(yv, bo) : yv;
+                        dst[(long long)t * a.out + o] = has_bias ? __fadd_rn(yv, bo) : yv;
                     }
                 }
             }
@@ -406,6 +422,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             if (lane == 0) mbar_arrive(smem_u32(&acc_empty));
         }
     }
+}
+
+// Byte offset of the split-K partials in the workspace: after the x split,
+// 256-B aligned.
+size_t split_offset(int in, int T) {
+    return ((size_t)T * in * 2 * sizeof(__nv_bfloat16) + 255) & ~(size_t)255;
 }
 
 // x fp32 [T][K] -> xh = bf16_rn(x), xl = bf16_rn(x - xh), both [T][K].
@@ -420,9 +442,21 @@ __global__ void xsplit_kernel(const float* __restrict__ x, long long n, __nv_bfl
     }
 }
 
+// y[i] = sum over the split K ranges of part[r][i] (range order), + bias.
+__global__ void splitk_reduce_kernel(const float* __restrict__ part, int split, long long n, int out,
+                                     const float* __restrict__ bias, float* __restrict__ y) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+         i += (long long)gridDim.x * blockDim.x) {
+        float v = part[i];
+        for (int r = 1; r < split; ++r) v = __fadd_rn(v, part[(long long)r * n + i]);
+        if (bias) v = __fadd_rn(v, bias[i % out]);
+        y[i] = v;
+    }
+}
+
 template <int F, int NT>
 cudaError_t launch_gemm_t(const uint8_t* w, const float* x, float* y, int out, int in, int T,
-                          const float* bias, void* ws, int sm_count, int* err, cudaStream_t stream) {
+                          const float* bias, void* ws, int split, int sm_count, int* err, cudaStream_t stream) {
     using C = GemmCfg<F, NT>;
     __nv_bfloat16* xh = static_cast<__nv_bfloat16*>(ws);
     __nv_bfloat16* xl = xh + (size_t)T * in;
@@ -458,20 +492,31 @@ cudaError_t launch_gemm_t(const uint8_t* w, const float* x, float* y, int out, i
     a.in = in;
     a.T = T;
     a.err = err;
-    const int ntiles = ((out + BM - 1) / BM) * ((T + NT - 1) / NT);
+    const int chunks = (in + KW - 1) / KW;  // W chunks along K
+    if (split < 1) split = 1;
+    a.kchunks_per_split = (chunks + split - 1) / split;
+    a.split = (chunks + a.kchunks_per_split - 1) / a.kchunks_per_split;  // no empty range
+    a.part = a.split > 1 ? reinterpret_cast<float*>(static_cast<char*>(ws) + split_offset(in, T)) : nullptr;
+    const int ntiles = ((out + BM - 1) / BM) * ((T + NT - 1) / NT) * a.split;
     const int grid = ntiles < sm_count ? ntiles : sm_count;
     gemm_tc_kernel<F, NT><<<grid, kGemmThreads, C::SMEM, stream>>>(mw, mxh, mxl, a);
+    e = cudaGetLastError();
+    if (e != cudaSuccess || a.split == 1) return e;
+    const long long ny = (long long)T * out;
+    const long long nb = (ny + 255) / 256;
+    splitk_reduce_kernel<<<(int)(nb < 4 * sm_count ? nb : 4 * sm_count), 256, 0, stream>>>(a.part, a.split, ny,
+                                                                                         out, bias, y);
     return cudaGetLastError();
 }
 
 // Narrowest tile that covers the rows of x (wider calls tile by 128).
 template <int F>
 cudaError_t launch_gemm_f(const uint8_t* w, const float* x, float* y, int out, int in, int T,
-                          const float* bias, void* ws, int sm_count, int* err, cudaStream_t stream) {
-    if (T <= 16) return launch_gemm_t<F, 16>(w, x, y, out, in, T, bias, ws, sm_count, err, stream);
-    if (T <= 32) return launch_gemm_t<F, 32>(w, x, y, out, in, T, bias, ws, sm_count, err, stream);
-    if (T <= 64) return launch_gemm_t<F, 64>(w, x, y, out, in, T, bias, ws, sm_count, err, stream);
-    return launch_gemm_t<F, 128>(w, x, y, out, in, T, bias, ws, sm_count, err, stream);
+                          const float* bias, void* ws, int split, int sm_count, int* err, cudaStream_t stream) {
+    if (T <= 16) return launch_gemm_t<F, 16>(w, x, y, out, in, T, bias, ws, split, sm_count, err, stream);
+    if (T <= 32) return launch_gemm_t<F, 32>(w, x, y, out, in, T, bias, ws, split, sm_count, err, stream);
+    if (T <= 64) return launch_gemm_t<F, 64>(w, x, y, out, in, T, bias, ws, split, sm_count, err, stream);
+    return launch_gemm_t<F, 128>(w, x, y, out, in, T, bias, ws, split, sm_count, err, stream);
 }
 
 }  // namespace
@@ -482,14 +527,28 @@ bool gemm_supported(int fmt, const void* w, int out, int in, int rows) {
            in % 8 == 0 && encode_fn() != nullptr;
 }
 
-size_t gemm_workspace_bytes(int in, int rows) { return (size_t)rows * in * 2 * sizeof(__nv_bfloat16); }
+int gemm_split(int out, int in, int rows, int sm_count) {
+    const int nt = rows <= 16 ? 16 : rows <= 32 ? 32 : rows <= 64 ? 64 : 128;
+    const long long tiles = (long long)((out + BM - 1) / BM) * ((rows + nt - 1) / nt);
+    const int chunks = (in + KW - 1) / KW;
+    if (tiles >= sm_count || chunks < 2) return 1;
+    long long s = sm_count / tiles;
+    if (s > 8) s = 8;  // past 8 ranges the partial traffic outweighs the extra SMs
+    if (s > chunks) s = chunks;
+    return s < 1 ? 1 : (int)s;
+}
+
+size_t gemm_workspace_bytes(int in, int rows, int out, int split) {
+    const size_t xs = split_offset(in, rows);
+    return split > 1 ? xs + (size_t)split * rows * out * sizeof(float) : (size_t)rows * in * 2 * sizeof(__nv_bfloat16);
+}
 
 cudaError_t launch_gemm(int fmt, const uint8_t* w, const float* x, float* y, int out, int in, int rows,
-                        const float* bias, void* ws, int sm_count, int* err, cudaStream_t stream) {
+                        const float* bias, void* ws, int split, int sm_count, int* err, cudaStream_t stream) {
     switch (fmt) {
-        case kQ8_0: return launch_gemm_f<kQ8_0>(w, x, y, out, in, rows, bias, ws, sm_count, err, stream);
-        case kQ4_0: return launch_gemm_f<kQ4_0>(w, x, y, out, in, rows, bias, ws, sm_count, err, stream);
-        case kQ4_1: return launch_gemm_f<kQ4_1>(w, x, y, out, in, rows, bias, ws, sm_count, err, stream);
+        case kQ8_0: return launch_gemm_f<kQ8_0>(w, x, y, out, in, rows, bias, ws, split, sm_count, err, stream);
+        case kQ4_0: return launch_gemm_f<kQ4_0>(w, x, y, out, in, rows, bias, ws, split, sm_count, err, stream);
+        case kQ4_1: return launch_gemm_f<kQ4_1>(w, x, y, out, in, rows, bias, ws, split, sm_count, err, stream);
     }
     return cudaErrorInvalidValue;
 }

@@ -60,18 +60,31 @@ struct GemmArgs {
     int out, in;   // W is [out][in] in blocks
     int T;         // rows of x (tokens)
     int* err;      // device error flag
+    // split-K: the K extent in `split` ranges (whole 256-value W chunks),
+    // each tile's partial sums to part[range][T][out], summed in range
+    // order by a second kernel.  split == 1: y directly.
+    int split;
+    int kchunks_per_split;  // W chunks (KSUB K-steps each) per range
+    float* part;
 };
 
 // True when the tcgen05 GEMM takes this call: MLQ_GEMM_ROWS_RULE(rows, out), weights 16-B
 // aligned with a 16-B multiple row pitch, in % 8 == 0.
 bool gemm_supported(int fmt, const void* w, int out, int in, int rows);
 
-// Workspace bytes of the GEMM (x split into bf16 hi/lo).
-size_t gemm_workspace_bytes(int in, int rows);
+// Split-K ranges for a GEMM call on `sm_count` SMs: 1 when its output
+// tiles already occupy the SMs, else enough ranges to (about) fill them.
+int gemm_split(int out, int in, int rows, int sm_count);
 
-// y[T][out] = x[T][in] * W^T (+ bias[out], when not null) on the tensor cores.
+// Workspace bytes of the GEMM: x split into bf16 hi/lo, plus the partial
+// sums of `split` K ranges when split > 1.
+size_t gemm_workspace_bytes(int in, int rows, int out, int split);
+
+// y[T][out] = x[T][in] * W^T (+ bias[out], when not null) on the tensor
+// cores, over `split` K ranges (gemm_split); ws holds
+// gemm_workspace_bytes(in, rows, out, split) bytes.
 cudaError_t launch_gemm(int fmt, const uint8_t* w, const float* x, float* y, int out, int in, int rows,
-                        const float* bias, void* ws, int sm_count, int* err, cudaStream_t stream);
+                        const float* bias, void* ws, int split, int sm_count, int* err, cudaStream_t stream);
 
 // Quantize fp32 [rows][cols] -> blocks, reference rules (mlq_convert.cu).
 cudaError_t launch_quantize(int fmt, const float* src, long long rows, int cols, uint8_t* blocks,

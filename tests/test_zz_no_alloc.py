@@ -5,7 +5,8 @@ GEMM's x split lives in a static device array instead of a per-stream
 workspace.  Each case makes two calls in a row on one stream (the second
 reuses the scratch the first one wrote) and checks both against mlq_linear
 at relative L2 1e-5 per output row (the contract is 1e-3; the same kernels
-should agree to the last bit).  This file is collected last so that it also
+should agree to the last bit, unless the scratch is too small for the
+GEMM's split-K partials -- see test_noalloc_full_scratch_allocates_nothing).  This file is collected last so that it also
 runs after every other GPU test in one process."""
 from __future__ import annotations
 
@@ -57,7 +58,10 @@ def test_noalloc_matches_linear_two_calls(pkg, oracle, fmt, out_f, in_f, rows):
 def test_noalloc_full_scratch_allocates_nothing(pkg, oracle):
     """rows * in * 4 == MLQ_NOALLOC_SCRATCH_BYTES exactly, on a fresh stream:
     free device memory is unchanged across two calls (mlq_linear would
-    allocate a workspace for a new stream)."""
+    allocate a workspace for a new stream).  The x split fills the scratch,
+    so this call runs the GEMM over the whole K extent where mlq_linear
+    splits K into ranges (its workspace holds their partial sums): the two
+    differ by summation order, checked at the GEMM's 1e-4."""
     fmt, out_f, in_f = "q4_0", 256, 4096
     rows = pkg.mlq.NOALLOC_SCRATCH_BYTES // (4 * in_f)
     w, xs = _pair(pkg, oracle, fmt, out_f, in_f, rows, seed=11)
@@ -75,7 +79,7 @@ def test_noalloc_full_scratch_allocates_nothing(pkg, oracle):
     for x, y in zip(xs, ys):
         ref = pkg.mlq.linear(fmt, w, out_f, in_f, x)
         torch.cuda.synchronize()
-        assert rel_l2_rows(y.cpu().numpy(), ref.cpu().numpy()).max() <= 1e-5
+        assert rel_l2_rows(y.cpu().numpy(), ref.cpu().numpy()).max() <= 1e-4
 
 
 def test_noalloc_rejects_oversize_gemm(pkg, oracle):
