@@ -290,11 +290,11 @@ def gemv_passes(rows):
     return n
 
 
-def launches_per_call(mlq, rows, out_f, local, pair):
+def launches_per_call(mlq, rows, out_f, in_f, local, pair):
     """Kernel launches of one library call in this bench (all shapes here are
     aligned for every kernel): the GEMM is an x-split launch plus the GEMM
     (per matrix of a pair, plus the SwiGLU pass); the GEMV one launch per pass."""
-    if local and mlq.takes_gemm(rows, out_f):
+    if local and mlq.takes_gemm(rows, out_f, in_f):
         return 5 if pair else 2
     return gemv_passes(rows)
 
@@ -419,7 +419,8 @@ def run_mlq(args):
             calls.append(call)
             ybufs.append(lambda lin=lin: lin.y_ptr(epoch[0]))
         on_one_gpu = world == 1 or placement(world)[name] == "local0"
-        launches_per_step += launches_per_call(mlq, rows, out_f, on_one_gpu, bool(pair) and name == pair[0])
+        launches_per_step += launches_per_call(mlq, rows, out_f, in_f, on_one_gpu,
+                                               bool(pair) and name == pair[0])
 
     def step(events=None):
         for j, call in enumerate(calls):
@@ -554,7 +555,7 @@ def run_mlq(args):
     # the dominant launch's kernel: sharded calls always stream; local calls
     # follow the library's routing rule (MLQ_GEMM_ROWS_RULE)
     dom_local = world == 1 or placement(world)[dom] == "local0"
-    dom_gemm = dom_local and mlq.takes_gemm(rows, mats[dj][1])
+    dom_gemm = dom_local and mlq.takes_gemm(rows, mats[dj][1], mats[dj][2])
     kernel = (f"gemv_stream_kernel<{fmt}, MT={rows}, integer mode>" if rows == 1 else
               f"gemv_stream_kernel<{fmt}, MT={min(rows, 8)}, fp32 mode>" if not dom_gemm else
               f"gemm_tc_kernel<{fmt}>") + f" ({dom} launch, rank 0)"

@@ -103,21 +103,23 @@ MLQ_API mlq_status mlq_linear(mlq_format fmt, const void* w, size_t block_count,
                               float* y, mlq_stream stream);
 
 /* Which kernel a call takes.  The tensor-core (tcgen05) GEMM's time hardly
- * depends on the rows of x (one decode of every weight per 128-row tile),
- * the streaming GEMV's grows with every pass of <= 8 rows.  A call takes
- * the GEMM when it has at least MLQ_GEMM_MIN_ROWS rows of x, or at least
- * MLQ_GEMM_WIDE_MIN_ROWS rows on a matrix with at least
- * MLQ_GEMM_WIDE_MIN_OUT output features (enough 128-row tiles to occupy
- * the GPU); MLQ_GEMM_ROWS_RULE(rows, out) is that test.  The GEMM also
- * needs 16-B aligned weights with a 16-B multiple row pitch and
- * in_features % 8 == 0; other calls take the streaming GEMV.  (Measured on
- * B200: q4_0 28672x8192 at 8 rows, GEMM 174 us vs GEMV 205 us; q4_0
- * 8192x28672 at 8 rows, GEMM 293 us vs GEMV 213 us.) */
+ * depends on the rows of x (one decode of every weight per 128-row tile,
+ * split along K when the tiles cannot fill the SMs), the streaming GEMV's
+ * grows with every pass of <= 8 rows.  A call takes the GEMM when it has
+ * at least MLQ_GEMM_MIN_ROWS rows of x, or at least MLQ_GEMM_LARGE_MIN_ROWS
+ * rows on a matrix of at least MLQ_GEMM_LARGE_MIN_WEIGHTS weights
+ * (out_features * in_features); MLQ_GEMM_ROWS_RULE(rows, out, in) is that
+ * test.  The GEMM also needs 16-B aligned weights with a 16-B multiple row
+ * pitch and in_features % 8 == 0; other calls take the streaming GEMV.
+ * (Measured on B200 at 8 rows: q4_0 8192x28672, GEMM 158 us vs GEMV
+ * 213 us; q4_0 4608x3584, GEMM 24.8 us vs GEMV 18.6 us.) */
 #define MLQ_GEMM_MIN_ROWS 9
-#define MLQ_GEMM_WIDE_MIN_ROWS 5
-#define MLQ_GEMM_WIDE_MIN_OUT 12288
-#define MLQ_GEMM_ROWS_RULE(rows, out) \
-    ((rows) >= MLQ_GEMM_MIN_ROWS || ((rows) >= MLQ_GEMM_WIDE_MIN_ROWS && (out) >= MLQ_GEMM_WIDE_MIN_OUT))
+#define MLQ_GEMM_LARGE_MIN_ROWS 5
+#define MLQ_GEMM_LARGE_MIN_WEIGHTS (1LL << 25)
+#define MLQ_GEMM_ROWS_RULE(rows, out, in)                                         \
+    ((rows) >= MLQ_GEMM_MIN_ROWS ||                                               \
+     ((rows) >= MLQ_GEMM_LARGE_MIN_ROWS &&                                        \
+      (long long)(out) * (long long)(in) >= MLQ_GEMM_LARGE_MIN_WEIGHTS))
 
 /* mlq_linear that never allocates device memory.  No counterpart in the
  * reference (its GPU linear cudaMallocs its output on every call,
@@ -132,8 +134,8 @@ MLQ_API mlq_status mlq_linear(mlq_format fmt, const void* w, size_t block_count,
  * Same arguments, results and validation as mlq_linear.  The tensor-core
  * path keeps the bf16 hi/lo split of x in a static
  * MLQ_NOALLOC_SCRATCH_BYTES array of the library's device module instead
- * of a workspace; so a call with MLQ_GEMM_ROWS_RULE(rows, out_features)
- * true and rows * in_features * 4 bytes above that size returns
+ * of a workspace; so a call with MLQ_GEMM_ROWS_RULE(rows, out_features,
+ * in_features) true and rows * in_features * 4 bytes above that size returns
  * MLQ_ERR_RANGE before any CUDA call.  The array is one per
  * device, shared by every call: calls ordered on one stream are fine,
  * calls whose kernels may overlap (several streams, several host threads)

@@ -403,7 +403,7 @@ MLQ_API mlq_status mlq_linear_noalloc(mlq_format fmt, const void* w, size_t bloc
                                         "mlq_linear_noalloc");
         if (st != MLQ_OK) return st;
         const size_t need = mlq::gemm_workspace_bytes(in_features, rows, out_features, 1);
-        if (MLQ_GEMM_ROWS_RULE(rows, out_features) && need > (size_t)MLQ_NOALLOC_SCRATCH_BYTES)
+        if (MLQ_GEMM_ROWS_RULE(rows, out_features, in_features) && need > (size_t)MLQ_NOALLOC_SCRATCH_BYTES)
             return fail(MLQ_ERR_RANGE,
                         "mlq_linear_noalloc: rows * in_features * 4 = " + std::to_string(need) +
                             " bytes of x split exceed the " +

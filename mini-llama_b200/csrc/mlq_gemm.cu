@@ -523,7 +523,7 @@ cudaError_t launch_gemm_f(const uint8_t* w, const float* x, float* y, int out, i
 
 bool gemm_supported(int fmt, const void* w, int out, int in, int rows) {
     const long long row_bytes = (long long)((in + kQK - 1) / kQK) * block_bytes(fmt);
-    return MLQ_GEMM_ROWS_RULE(rows, out) && reinterpret_cast<uintptr_t>(w) % 16 == 0 && row_bytes % 16 == 0 &&
+    return MLQ_GEMM_ROWS_RULE(rows, out, in) && reinterpret_cast<uintptr_t>(w) % 16 == 0 && row_bytes % 16 == 0 &&
            in % 8 == 0 && encode_fn() != nullptr;
 }
 

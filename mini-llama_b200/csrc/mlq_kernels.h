@@ -68,7 +68,7 @@ struct GemmArgs {
     float* part;
 };
 
-// True when the tcgen05 GEMM takes this call: MLQ_GEMM_ROWS_RULE(rows, out), weights 16-B
+// True when the tcgen05 GEMM takes this call: MLQ_GEMM_ROWS_RULE(rows, out, in), weights 16-B
 // aligned with a 16-B multiple row pitch, in % 8 == 0.
 bool gemm_supported(int fmt, const void* w, int out, int in, int rows);
 

@@ -192,14 +192,15 @@ def linear_bias_raw(fmt, w_ptr: int, nblocks: int, out_features: int, in_feature
 # MLQ_NOALLOC_SCRATCH_BYTES and the GEMM routing constants of include/mlq.h
 NOALLOC_SCRATCH_BYTES = 16 << 20
 GEMM_MIN_ROWS = 9
-GEMM_WIDE_MIN_ROWS = 5
-GEMM_WIDE_MIN_OUT = 12288
+GEMM_LARGE_MIN_ROWS = 5
+GEMM_LARGE_MIN_WEIGHTS = 1 << 25
 
 
-def takes_gemm(rows: int, out_features: int) -> bool:
-    """MLQ_GEMM_ROWS_RULE of include/mlq.h: the row/width part of the routing
+def takes_gemm(rows: int, out_features: int, in_features: int) -> bool:
+    """MLQ_GEMM_ROWS_RULE of include/mlq.h: the row/size part of the routing
     between the tensor-core GEMM and the streaming GEMV."""
-    return rows >= GEMM_MIN_ROWS or (rows >= GEMM_WIDE_MIN_ROWS and out_features >= GEMM_WIDE_MIN_OUT)
+    return rows >= GEMM_MIN_ROWS or (rows >= GEMM_LARGE_MIN_ROWS
+                                      and out_features * in_features >= GEMM_LARGE_MIN_WEIGHTS)
 
 
 def linear_noalloc(fmt, w, out_features: int, in_features: int, x, y, stream=None):

@@ -5,7 +5,7 @@
   reference's swiGlu), relative L2 <= 1e-3 per output row (the linear
   contract), over every route a call can take: the one-token integer GEMV,
   the fp32 GEMV passes (2..8 rows; 13 rows where the GEMM does not take the
-  row pitch), the tensor-core GEMM (from 9 rows, or 5 on a wide matrix), the
+  row pitch), the tensor-core GEMM (from 9 rows, or 5 on a large matrix), the
   1-D bulk-copy stream (row pitch not a multiple of 16 B), the any-alignment
   fallback, the dynamic row-tile queue and a captured CUDA graph.  The fused
   launch is also checked against the unfused library calls (mlq_linear per
@@ -47,7 +47,7 @@ def oracle_h(oracle, fmt, x, wg, wu, out_f):
 
 
 # (fmt, out, in, rows): one token (integer mode), fp32 passes, GEMM (13 and 16+
-# rows, and 8 rows of a wide matrix below), partial tiles,
+# rows, and 8 rows of a large matrix below), partial tiles,
 # the 1-D bulk stream (q4_0 in=320: 180-byte rows), the generic fallback (q8_0
 # in=96: odd block count per row)
 PAIR_CASES = [
@@ -67,7 +67,7 @@ PAIR_CASES = [
     ("q4_0", 200, 320, 13),      # no GEMM for this row pitch: GEMV passes of 8 + 5 rows
     ("q8_0", 100, 96, 1),
     ("q8_0", 100, 96, 20),
-    ("q4_1", 12288, 512, 8),     # wide: the GEMM pair from 5 rows
+    ("q4_1", 8192, 4096, 8),     # large (2^25 weights): the GEMM pair from 5 rows
 ]
 
 

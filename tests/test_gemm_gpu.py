@@ -1,5 +1,7 @@
 """The tensor-core GEMM path against the CPU oracle (calls with >= 9 rows of
-x, or >= 5 rows on matrices with >= 12288 output features: MLQ_GEMM_ROWS_RULE).
+x, or >= 5 rows on matrices of >= 2^25 weights: MLQ_GEMM_ROWS_RULE), with and
+without split-K (ranges of whole 256-value weight chunks when the output
+tiles cannot fill the SMs).
 
 Same contract as the GEMV: relative L2 error of every output row <= 1e-3.
 The bf16x3 split keeps the GEMM within ~1e-5 of fp32, so the tests also
@@ -36,8 +38,10 @@ CASES = [
     ("q4_1", 640, 4160, 96),     # in % 256 = 64
     ("q8_0", 512, 4096, 16),     # batched decode
     ("q8_0", 512, 4096, 9),      # smallest GEMM row count on a narrow matrix
-    ("q4_0", 12288, 1024, 5),    # wide matrix: the GEMM from 5 rows
-    ("q4_1", 12300, 512, 7),     # wide, partial last row tile
+    ("q4_0", 12288, 4096, 5),    # large matrix: the GEMM from 5 rows
+    ("q4_1", 12300, 3072, 7),    # large, partial last row tile
+    ("q8_0", 1024, 8192, 16),    # 8 row tiles: split-K into 8 ranges of 4 weight chunks
+    ("q4_0", 640, 4864, 12),     # 5 row tiles, 19 weight chunks: 7 ranges, the last of 1 chunk
     ("q4_0", 300, 2048, 20),
     ("q4_1", 256, 1024, 33),
     ("q8_0", 384, 1024, 24),     # 32-wide tile, stage count trimmed to fit shared memory

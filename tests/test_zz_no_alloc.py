@@ -97,9 +97,9 @@ def test_noalloc_rejects_oversize_gemm(pkg, oracle):
 def test_noalloc_large_x_below_gemm_rows(pkg, oracle):
     """rows below the GEMM threshold take the GEMV, which needs no scratch:
     x larger than the scratch is accepted and matches mlq_linear."""
-    fmt, out_f, in_f = "q8_0", 64, 524352
+    fmt, out_f, in_f = "q8_0", 32, 524352
     rows = pkg.mlq.GEMM_MIN_ROWS - 1
-    assert not pkg.mlq.takes_gemm(rows, out_f)
+    assert not pkg.mlq.takes_gemm(rows, out_f, in_f)
     assert rows * in_f * 4 > pkg.mlq.NOALLOC_SCRATCH_BYTES
     w, xs = _pair(pkg, oracle, fmt, out_f, in_f, rows, seed=31)
     y = torch.empty((rows, out_f), dtype=torch.float32, device="cuda")
