@@ -197,3 +197,25 @@ def test_non_default_stream_and_determinism(oracle, pkg):
 
 def test_no_device_error_recorded(pkg):
     assert pkg.mlq.device_error(0) == 0
+
+
+@pytest.mark.parametrize("fmt,out_f,in_f,rows", [("q4_0", 4608, 3584, 1), ("q8_0", 1000, 1024, 3),
+                                                  ("q4_1", 512, 4096, 16)])
+def test_host_entry_pinned_buffers(oracle, pkg, fmt, out_f, in_f, rows):
+    """mlq_linear_host with pinned x/y (the bench's e2e path, asynchronous DMA)
+    gives the same values as with pageable buffers, with and without the
+    host bias."""
+    blocks = oracle.quantize(fmt, pkg.synth.normal((out_f, in_f), seed=out_f + rows, std=0.02))
+    w = torch.from_numpy(blocks).cuda()
+    x = pkg.synth.normal((rows, in_f), seed=rows + 40)
+    bias = pkg.synth.normal((out_f,), seed=41, std=0.5)
+    y_page = pkg.mlq.linear_host(fmt, w, out_f, in_f, x)
+    yt = torch.full((rows, out_f), float("nan"), dtype=torch.float32).pin_memory()
+    y_pin = pkg.mlq.linear_host(fmt, w, out_f, in_f, x, y=yt.numpy())
+    assert np.array_equal(y_pin, y_page)
+    assert rel_l2_rows(y_pin, oracle.linear(fmt, x, blocks, out_f)).max() <= TOL
+    yb_page = pkg.mlq.linear_host(fmt, w, out_f, in_f, x, bias=bias)
+    ybt = torch.zeros((rows, out_f), dtype=torch.float32).pin_memory()
+    yb_pin = pkg.mlq.linear_host(fmt, w, out_f, in_f, x, bias=bias, y=ybt.numpy())
+    assert np.array_equal(yb_pin, yb_page)
+    assert pkg.mlq.device_error(0) == 0
