@@ -533,7 +533,7 @@ int gemm_split(int out, int in, int rows, int sm_count) {
     const int chunks = (in + KW - 1) / KW;
     if (tiles >= sm_count || chunks < 2) return 1;
     long long s = sm_count / tiles;
-    if (s > 8) s = 8;  // past 8 ranges the partial traffic outweighs the extra SMs
+    if (s > 8) s = 8;  // each range adds a T x out partial to write and read back
     if (s > chunks) s = chunks;
     return s < 1 ? 1 : (int)s;
 }

@@ -122,3 +122,35 @@ def test_missing_library_fails_loudly(pkg, tmp_path, monkeypatch):
     monkeypatch.setattr(mlq, "LIB_PATH", tmp_path / "libmlq.so")
     with pytest.raises(FileNotFoundError):
         mlq.lib()
+
+
+def test_gemm_routing_rule_matches_header(pkg, tmp_path):
+    """mlq.takes_gemm (Python) and MLQ_GEMM_ROWS_RULE (include/mlq.h, the rule
+    the library compiles) agree on a grid of rows x matrix sizes, and the
+    Python constants equal the header's.  The header is plain C: gcc builds
+    a probe that prints the macro's answers."""
+    import shutil
+    import subprocess
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        pytest.skip("gcc not found")
+    rows = [1, 2, 4, 5, 8, 9, 15, 16, 512]
+    shapes = [(32, 524352), (4608, 3584), (4096, 4096), (8192, 4096), (8191, 4096), (3584, 18944),
+              (152064, 3584)]
+    src = tmp_path / "rule.c"
+    lines = ['#include <stdio.h>', '#include "mlq.h"', "int main(void) {",
+             '  printf("%d %d %lld\\n", MLQ_GEMM_MIN_ROWS, MLQ_GEMM_LARGE_MIN_ROWS, '
+             "(long long)MLQ_GEMM_LARGE_MIN_WEIGHTS);"]
+    for r in rows:
+        for o, i in shapes:
+            lines.append(f'  printf("%d\\n", (int)(MLQ_GEMM_ROWS_RULE({r}, {o}, {i})));')
+    lines.append("  return 0;\n}")
+    src.write_text("\n".join(lines) + "\n")
+    exe = tmp_path / "rule"
+    subprocess.run([gcc, "-std=c99", "-I", str(ROOT / "include"), str(src), "-o", str(exe)], check=True)
+    out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split("\n")
+    mlq = pkg.mlq
+    assert out[0].split() == [str(mlq.GEMM_MIN_ROWS), str(mlq.GEMM_LARGE_MIN_ROWS), str(mlq.GEMM_LARGE_MIN_WEIGHTS)]
+    got = [int(v) for v in out[1:] if v.strip()]
+    want = [int(mlq.takes_gemm(r, o, i)) for r in rows for o, i in shapes]
+    assert got == want
