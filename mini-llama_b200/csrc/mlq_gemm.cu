@@ -31,6 +31,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "mlq.h"
@@ -477,13 +478,13 @@ cudaError_t launch_gemm_t(const uint8_t* w, const float* x, float* y, int out, i
                      (uint64_t)in * 2, BK, NT, CU_TENSOR_MAP_SWIZZLE_128B))
         return cudaErrorInvalidValue;
 
-    static int attr_set[64] = {};
+    static std::atomic<bool> attr_set[64];  // one value per instantiation: racing first calls agree
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 64 || !attr_set[dev]) {
+    if (dev >= 64 || !attr_set[dev].load(std::memory_order_acquire)) {
         e = cudaFuncSetAttribute(gemm_tc_kernel<F, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
         if (e != cudaSuccess) return e;
-        if (dev < 64) attr_set[dev] = 1;
+        if (dev < 64) attr_set[dev].store(true, std::memory_order_release);
     }
     GemmArgs a{};
     a.y = y;

@@ -1061,14 +1061,17 @@ cudaError_t launch_stream_t(GemvArgs args, int sm_count, int smem_per_sm, cudaSt
     if (S < 2) return cudaErrorInvalidConfiguration;
     args.nstages = S;
     const int smem = S * C::W_BYTES + nx * C::XT_BYTES + 128;  // + the alignment slack
-    static int attr_bytes[64] = {};
+    // Every launch of this instantiation uses at most budget + 128 bytes
+    // (stages and x slots are sized to the budget), so the attribute is set
+    // to that once per device; concurrent first calls set the same value.
+    static std::atomic<bool> attr_done[64];
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 64 || attr_bytes[dev] < smem) {
+    if (dev >= 64 || !attr_done[dev].load(std::memory_order_acquire)) {
         cudaError_t e = cudaFuncSetAttribute(gemv_stream_kernel<F, MT, RPW, MINB, INT, EPI>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, budget + 128);
         if (e != cudaSuccess) return e;
-        if (dev < 64 && smem > attr_bytes[dev]) attr_bytes[dev] = smem;
+        if (dev < 64) attr_done[dev].store(true, std::memory_order_release);
     }
     // weights by 2-D tensor map when the row pitch and base (both bases of a
     // pair) allow it
