@@ -154,3 +154,25 @@ def test_gemm_routing_rule_matches_header(pkg, tmp_path):
     got = [int(v) for v in out[1:] if v.strip()]
     want = [int(mlq.takes_gemm(r, o, i)) for r in rows for o, i in shapes]
     assert got == want
+
+
+def test_noalloc_range_rule_before_any_cuda_call(pkg):
+    """mlq_linear_noalloc rejects, before any CUDA call, exactly the calls
+    that take the GEMM (MLQ_GEMM_ROWS_RULE) with an x split above the static
+    scratch: 9 rows on any matrix, 5 rows on a matrix of >= 2^25 weights.
+    (Pointers are fake: a rejected call never touches them.)"""
+    mlq = pkg.mlq
+    lib = mlq.lib()
+    scratch = mlq.NOALLOC_SCRATCH_BYTES
+
+    def status(rows, out_f, in_f):
+        nb = mlq.block_count(out_f, in_f)
+        return lib.mlq_linear_noalloc(8, 0x1000, nb, out_f, in_f, 0x2000, rows, 0x3000, None)
+
+    in_f = scratch // (4 * 5) + 64  # 5 rows of x exceed the scratch
+    assert mlq.takes_gemm(9, 32, in_f) and 9 * in_f * 4 > scratch
+    assert status(9, 32, in_f) == 9
+    assert b"static scratch" in lib.mlq_last_error()
+    big_out = -(-mlq.GEMM_LARGE_MIN_WEIGHTS // in_f)  # out * in >= 2^25
+    assert mlq.takes_gemm(5, big_out, in_f) and status(5, big_out, in_f) == 9
+    assert not mlq.takes_gemm(5, 32, in_f)  # a small matrix at 5 rows streams: no scratch needed
