@@ -14,18 +14,24 @@
 //     below 2^-17 of each product, so y matches the fp32 reference to
 //     ~1e-5 relative -- far inside the 1e-3 contract.
 //
-// CTA = 6 warps, one 128 (W rows) x 128 (tokens) output tile at a time,
-// persistent over tiles:
+// CTA = 10 warps, one output tile of 128 W rows x NT tokens at a time (NT =
+// 16/32/64/128, the narrowest covering the call's rows), persistent over
+// tiles:
 //   warp 0   TMA producer: packed W chunks (256 values per row, 2-D tensor
 //            map over the AoS bytes, no swizzle) and x hi/lo tiles (2-D
 //            tensor maps over bf16 [T][K], 128-B swizzle).
-//   warp 1   allocates 128 TMEM columns; lane 0 issues the MMAs and the
+//   warp 1   allocates the TMEM columns; lane 0 issues the MMAs and the
 //            tcgen05.commit arrivals.
-//   warps 2-5 ("row" threads, thread = W row = TMEM lane): decode their
-//            row's two blocks of each 64-wide K-step from shared memory,
-//            write the bf16 hi/lo A rows in the 128-B swizzled K-major
-//            layout, then run the epilogue (tcgen05.ld -> y, coalesced).
-// All mbarrier waits are bounded (2 s); no TMA multicast anywhere.
+//   warps 2-9 ("row" threads, thread = W row = TMEM lane, two warps per
+//            lane quarter): each decodes its row's block of every 64-wide
+//            K-step from shared memory, writes the bf16 hi/lo A halves in
+//            the 128-B swizzled K-major layout, then runs its share of the
+//            epilogue (tcgen05.ld -> y, + bias).
+// When the tiles cannot fill the SMs, the K extent is split into ranges of
+// whole W chunks (split-K): a work item is (row tile, token tile, K range),
+// the epilogue writes partial sums to the workspace and a second kernel adds
+// them in range order.  All mbarrier waits are bounded (2 s); no TMA
+// multicast anywhere.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
