@@ -2,23 +2,30 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mlq|reference]
 
-Workload: one Qwen2-7B-shaped layer plus lm_head
-in q4_0 -- QKV 4608x3584, O 3584x3584, gate/up 18944x3584, down 3584x18944,
-lm_head 152064x3584 -- decoded at batch 1 with fp32 activations.  A step is
-one pass over the six matrices (437,649,408 bytes of packed weights, larger
-than the 126 MB L2, so no L2 flush is needed between steps).  Weights are
-seeded N(0, 0.02) fp32 quantized by the library's reference-exact q4_0
-quantizer; activations are seeded N(0, 1).
+Headline workload: one Qwen2-7B-shaped layer plus
+lm_head in q4_0 -- QKV 4608x3584, O 3584x3584, gate/up 18944x3584, down
+3584x18944, lm_head 152064x3584 -- decoded at batch 1 with fp32 activations.
+A step is one pass over the six matrices (437,649,408 bytes of packed
+weights, larger than the 126 MB L2, so no L2 flush is needed between steps),
+launched as one batch (mlq_linear_batch).  Weights are seeded N(0, 0.02) fp32
+drawn by mini-llama_b200/synth.py (the same numbers the CPU arm draws) and
+quantized by the library's reference-exact quantizer; activations are seeded
+N(0, 1).
 
 Metric: effective weight GB/s = packed weight bytes / time.  One JSON line on
-stdout (rank 0).  --impl reference times the reference's own CPU
-implementation (src/quant.cc linearQ40 through ThreadPool, compiled from
-the reference's sources into oracle/_ref/) on this machine's host cores.
+stdout (rank 0).  The line also carries, under "extra", the other BASELINE
+configs measured in the same run (config 1 q8_0 with rotating weight copies,
+config 3 prefill, config 4 batched decode, config 5 70B shards at batch 1
+and 8) and per-format decode fractions ("formats").
+
+--impl reference times the reference's own CPU implementation (src/quant.cc
+linearQ40 through ThreadPool, compiled from the reference's sources into
+oracle/_ref/) on this machine's host cores.
 """
 from __future__ import annotations
 
 import argparse
-import ctypes
+import importlib
 import importlib.util
 import json
 import os
@@ -34,59 +41,80 @@ ROOT = Path(__file__).resolve().parent
 PKG_DIR = ROOT / "mini-llama_b200"
 MB = 1_000_000
 
-# The bench line's workload is BASELINE configs[1]; --workload picks one of
-# the other decode configs for scaling studies (configs[4]: 70B-shaped shards).
+
+def llama8b_layers():
+    """Config 4: 32 Llama-3-8B layers (Q, K, V, O, gate, up, down) + lm_head."""
+    mats = []
+    for l in range(32):
+        mats += [(f"l{l}.q", 4096, 4096), (f"l{l}.k", 1024, 4096), (f"l{l}.v", 1024, 4096),
+                 (f"l{l}.o", 4096, 4096), (f"l{l}.gate", 14336, 4096), (f"l{l}.up", 14336, 4096),
+                 (f"l{l}.down", 4096, 14336)]
+    return mats + [("lm_head", 128256, 4096)]
+
+
+QWEN7B = [("qkv", 4608, 3584), ("o", 3584, 3584), ("gate", 18944, 3584), ("up", 18944, 3584),
+          ("down", 3584, 18944), ("lm_head", 152064, 3584)]
+LLAMA70B = [("gate", 28672, 8192), ("up", 28672, 8192), ("down", 8192, 28672), ("lm_head", 128256, 8192)]
+
+# At N > 1 the matrices named in "shard" are row-sharded across every GPU
+# (fused all-gather); the others run on rank 0 (north_star: FFN and lm_head
+# sharded, small matrices on one GPU).
 WORKLOADS = {
     "qwen7b": {
         "name": "qwen2-7b-layer+lm_head q4_0 decode (BASELINE configs[1])",
         "metric": "effective weight GB/s (q4_0 decode GEMV, Qwen2-7B layer + lm_head, batch 1)",
-        "fmt": "q4_0",
-        "rows": 1,
-        "matrices": [("qkv", 4608, 3584), ("o", 3584, 3584), ("gate", 18944, 3584),
-                     ("up", 18944, 3584), ("down", 3584, 18944), ("lm_head", 152064, 3584)],
+        "fmt": "q4_0", "rows": 1, "matrices": QWEN7B,
+        "shard": {"gate", "up", "down", "lm_head"},
     },
     # The same layer through the fused entry points: the q/k/v bias added in
-    # the QKV launch's store (mlq_linear_bias) and gate/up as one SwiGLU-pair
-    # launch writing silu(gate) * up (mlq_linear_swiglu); same weight bytes.
+    # the QKV launch's store and gate/up as one SwiGLU-pair launch writing
+    # silu(gate) * up (mlq_linear_swiglu); same weight bytes.  One GPU.
     "qwen7b-fused": {
         "name": "qwen2-7b-layer+lm_head q4_0 decode, fused bias + SwiGLU (BASELINE configs[1])",
         "metric": "effective weight GB/s (q4_0 decode GEMV, Qwen2-7B layer + lm_head, batch 1)",
-        "fmt": "q4_0",
-        "rows": 1,
-        "matrices": [("qkv", 4608, 3584), ("o", 3584, 3584), ("gate", 18944, 3584),
-                     ("up", 18944, 3584), ("down", 3584, 18944), ("lm_head", 152064, 3584)],
+        "fmt": "q4_0", "rows": 1, "matrices": QWEN7B, "shard": set(),
         "fused": {"bias": ["qkv"], "pair": ["gate", "up"]},
     },
-    "llama70b": {
-        "name": "llama-3-70b FFN + lm_head q4_0 decode shards, batch 1 (BASELINE configs[4])",
-        "metric": "effective weight GB/s (q4_0 decode GEMV, Llama-3-70B FFN + lm_head, batch 1)",
-        "fmt": "q4_0",
-        "rows": 1,
-        "matrices": [("gate", 28672, 8192), ("up", 28672, 8192), ("down", 8192, 28672),
-                     ("lm_head", 128256, 8192)],
+    "config1-q8_0": {
+        "name": "qwen2-0.5b FFN-up q8_0 decode, 4864x896 (BASELINE configs[0])",
+        "metric": "effective weight GB/s (q8_0 decode GEMV, 4864x896, batch 1)",
+        "fmt": "q8_0", "rows": 1, "matrices": [("up", 4864, 896)], "shard": set(),
+        # 4.6 MB fits in L2: every step reads the next of 64 copies (296 MB)
+        "rotate": 64,
     },
     "prefill-q4_1": {
         "name": "llama-3-8b FFN prefill q4_1, 512 rows of x (BASELINE configs[2])",
         "metric": "effective weight GB/s (q4_1 prefill GEMM, Llama-3-8B FFN, 512 rows)",
-        "fmt": "q4_1",
-        "rows": 512,
+        "fmt": "q4_1", "rows": 512,
         "matrices": [("gate", 14336, 4096), ("up", 14336, 4096), ("down", 4096, 14336)],
+        "shard": set(),
+    },
+    "llama8b-b16": {
+        "name": "llama-3-8b 32 layers + lm_head q8_0 batched decode, batch 16 (BASELINE configs[3])",
+        "metric": "effective weight GB/s (q8_0 batched decode, Llama-3-8B, batch 16)",
+        "fmt": "q8_0", "rows": 16, "matrices": llama8b_layers(),
+        "shard": {n for n, _, _ in llama8b_layers() if n.split(".")[-1] in ("gate", "up", "down", "lm_head")},
+    },
+    "llama70b": {
+        "name": "llama-3-70b FFN + lm_head q4_0 decode shards, batch 1 (BASELINE configs[4])",
+        "metric": "effective weight GB/s (q4_0 decode GEMV, Llama-3-70B FFN + lm_head, batch 1)",
+        "fmt": "q4_0", "rows": 1, "matrices": LLAMA70B, "shard": {"gate", "up", "down", "lm_head"},
     },
     "llama70b-b8": {
         "name": "llama-3-70b FFN + lm_head q4_0 decode shards, batch 8 (BASELINE configs[4])",
-        "metric": "effective weight GB/s (q4_0 decode GEMV, Llama-3-70B FFN + lm_head, batch 8)",
-        "fmt": "q4_0",
-        "rows": 8,
-        "matrices": [("gate", 28672, 8192), ("up", 28672, 8192), ("down", 8192, 28672),
-                     ("lm_head", 128256, 8192)],
+        "metric": "effective weight GB/s (q4_0 decode, Llama-3-70B FFN + lm_head, batch 8)",
+        "fmt": "q4_0", "rows": 8, "matrices": LLAMA70B, "shard": {"gate", "up", "down", "lm_head"},
     },
 }
-WORKLOAD = WORKLOADS["qwen7b"]
-METRIC = WORKLOAD["metric"]
+# measured after the headline in the default run (extra key of the line)
+EXTRAS_N1 = ["config1-q8_0", "prefill-q4_1", "llama8b-b16", "llama70b", "llama70b-b8"]
+EXTRAS_NGT1 = ["llama8b-b16", "llama70b", "llama70b-b8"]
 UNIT = "GB/s"
 
 
 def load_pkg():
+    if "mini_llama_b200" in sys.modules:
+        return sys.modules["mini_llama_b200"]
     spec = importlib.util.spec_from_file_location(
         "mini_llama_b200", PKG_DIR / "__init__.py", submodule_search_locations=[str(PKG_DIR)])
     mod = importlib.util.module_from_spec(spec)
@@ -100,25 +128,37 @@ def weight_bytes(fmt, out_f, in_f):
     return out_f * ((in_f + 31) // 32) * bs
 
 
-def bf16_peak():
-    """Measured dense bf16 TFLOP/s (burst: each GEMM launch is timed alone)."""
+def _peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         try:
-            return float(json.loads(p.read_text())["bf16_tflops"]), "measured"
+            return json.loads(p.read_text())
         except Exception:
             pass
-    return 1590.0, "fallback"
+    return None
 
 
 def hbm_peak():
-    p = ROOT / "MEASURED_PEAKS.json"
-    if p.exists():
-        try:
-            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
-        except Exception:
-            pass
-    return 6650.0, "fallback"
+    pk = _peaks()
+    return (float(pk["hbm_gbs"]), "measured") if pk else (6650.0, "fallback")
+
+
+def bf16_peak():
+    """Measured dense bf16 TFLOP/s (burst: each GEMM launch is timed alone)."""
+    pk = _peaks()
+    return (float(pk["bf16_tflops"]), "measured") if pk else (1590.0, "fallback")
+
+
+def config_of(wl, world):
+    """The config dict both arms print (same keys, same values)."""
+    return {"workload": wl["name"], "format": wl["fmt"], "batch": wl["rows"],
+            "matrices": {n: [o, i] for n, o, i in wl["matrices"]} if len(wl["matrices"]) <= 8
+            else f"{len(wl['matrices'])} matrices",
+            "weight_bytes_per_step": sum(weight_bytes(wl["fmt"], o, i) for _, o, i in wl["matrices"]),
+            "sharded_at_n_gt_1": sorted(wl["shard"]) if len(wl["shard"]) <= 8 else "FFN + lm_head",
+            "placement": "all on one GPU" if world == 1 else "listed matrices row-sharded, others on rank 0",
+            "l2": "inputs larger than L2 (no flush)" if not wl.get("rotate")
+            else f"{wl['rotate']} rotating weight copies per pass (> 2x L2)"}
 
 
 # ---------------------------------------------------------------------------
@@ -171,11 +211,9 @@ class ClockSampler:
             self.t.join()
 
     def summary(self):
-        if not self.ok or not self.samples:
-            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
-                    "samples": len(self.samples)}
-        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
-                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+        med = statistics.median(self.samples) if self.ok and self.samples else None
+        return {"sm_mhz": med, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                "samples": len(self.samples)}
 
 
 # ---------------------------------------------------------------------------
@@ -197,14 +235,16 @@ def cpu_has_avx2():
 
 class ReferenceCPU:
     """The reference's CPU linearQ80/Q40/Q41 (oracle/_ref, built from its
-    sources) over row samples of the workload's matrices, all host threads."""
+    sources) over the first rows of the workload's matrices (the same seeded
+    weights and x as the GPU arm), all host threads."""
 
-    def __init__(self):
+    def __init__(self, wl):
         sys.path.insert(0, str(ROOT))
         from oracle.oracle import Oracle, Reference  # checker / CPU baseline only
         variant = "avx2" if (cpu_has_avx2() and Reference.available("avx2")) else "scalar"
         if not Reference.available(variant):
             raise FileNotFoundError("oracle/_ref was not built")
+        self.wl = wl
         self.ref = Reference(variant)
         self.variant = f"libref_{variant}.so"
         self.cores = host_cores()
@@ -213,28 +253,28 @@ class ReferenceCPU:
         self.handles = []
 
     def load(self, pkg, frac):
-        """Quantize the first ceil(frac*out) rows of every matrix (seeded)."""
+        """Quantize the first ceil(frac*out) rows of every matrix."""
         self.release()
-        fmt = WORKLOAD["fmt"]
+        fmt = self.wl["fmt"]
         self.parts = []
-        for i, (name, out_f, in_f) in enumerate(WORKLOAD["matrices"]):
+        for i, (name, out_f, in_f) in enumerate(self.wl["matrices"]):
             rows = min(out_f, max(16 * self.cores, int(np.ceil(out_f * frac))))
             w = pkg.synth.normal((rows, in_f), seed=1000 + i, std=0.02)
             h = self.ref.hold(fmt, self.orc.quantize(fmt, w))
-            x = pkg.synth.normal((WORKLOAD["rows"], in_f), seed=2000 + i)
-            self.parts.append((h, x, rows, in_f, np.zeros((WORKLOAD["rows"], rows), np.float32)))
+            x = pkg.synth.normal((self.wl["rows"], in_f), seed=2000 + i)
+            self.parts.append((h, x, rows, in_f, np.zeros((self.wl["rows"], rows), np.float32)))
             self.handles.append(h)
         self.bytes = sum(weight_bytes(fmt, r, i) for _, _, r, i, _ in self.parts)
 
     def step(self):
         t0 = time.perf_counter()
         for h, x, rows, in_f, y in self.parts:
-            self.ref.linear_held(WORKLOAD["fmt"], x, h, rows, y)
+            self.ref.linear_held(self.wl["fmt"], x, h, rows, y)
         return time.perf_counter() - t0
 
     def release(self):
         for h in self.handles:
-            self.ref.release(WORKLOAD["fmt"], h)
+            self.ref.release(self.wl["fmt"], h)
         self.handles = []
 
     def calibrate(self, pkg):
@@ -242,15 +282,15 @@ class ReferenceCPU:
         self.load(pkg, 1 / 32)
         self.step()
         t = min(self.step() for _ in range(2))
-        return t * (sum(weight_bytes(WORKLOAD["fmt"], o, i) for _, o, i in WORKLOAD["matrices"])
+        return t * (sum(weight_bytes(self.wl["fmt"], o, i) for _, o, i in self.wl["matrices"])
                     / self.bytes)
 
 
-def reference_cpu_baseline(pkg, seconds):
+def reference_cpu_baseline(pkg, wl, seconds):
     """Bounded sample (~`seconds` of CPU work) of the workload on the
     reference's CPU path; returns the cpu_baseline dict."""
     try:
-        rc = ReferenceCPU()
+        rc = ReferenceCPU(wl)
     except FileNotFoundError as e:
         return {"unavailable": str(e)}
     t_pass = rc.calibrate(pkg)
@@ -264,25 +304,33 @@ def reference_cpu_baseline(pkg, seconds):
     gbs = rc.bytes * steps / total / 1e9
     rc.release()
     return {"value": round(gbs, 3), "unit": UNIT, "kind": "reference", "cores": rc.cores,
-            "sample": f"{steps} passes of linearQ40 over the first {frac:.1%} of every matrix's "
-                      f"rows ({rc.bytes / MB:.1f} MB/pass), {total:.1f} s, "
+            "sample": f"{steps} passes of linearQ{wl['fmt'][1]}{wl['fmt'][3]} over the first {frac:.1%} of "
+                      f"every matrix's rows ({rc.bytes / MB:.1f} MB/pass), {total:.1f} s, "
                       f"ThreadPool threads = {rc.cores}, {rc.variant}"}
 
 
 # ---------------------------------------------------------------------------
-# Placement of the workload's matrices on N GPUs (north_star: large
-# matrices row-sharded, small ones on one GPU).  A sharded call costs ~8 us
-# more than a local one (fused all-gather epilogue + cross-GPU completion
-# handshake), so a matrix is sharded only from SHARD_MIN_BYTES of packed
-# weights on (every 70B-shaped matrix; the 7B layer's lm_head, not its
-# 38 MB FFN matrices).  "local0": rank 0 computes, no gather (its consumer
-# runs on rank 0); "shard": rows split across all ranks, fused all-gather.
-SHARD_MIN_BYTES = 100 * MB
+# the GPU arm
+# ---------------------------------------------------------------------------
+def gemm_split(out_f, in_f, rows, sms):
+    """gemm_split of csrc/mlq_gemm.cu (launch counting only)."""
+    nt = 16 if rows <= 16 else 32 if rows <= 32 else 64 if rows <= 64 else 128
+    tiles = -(-out_f // 128) * -(-rows // nt)
+    chunks = -(-in_f // 256)
+    if tiles >= sms or chunks < 2:
+        return 1
+    s = max(1, min(sms // tiles, 8, chunks))
+    per = -(-chunks // s)
+    return -(-chunks // per)
 
 
-def gemv_passes(rows):
-    """Streaming-GEMV launches for `rows` rows of x (passes of 8, 4, 2, 1
-    tokens: gemv_tokens_per_pass in csrc/mlq_gemv.cu)."""
+def launches_of(mlq, rows, out_f, in_f, gemm_ok, pair, sms):
+    """Kernel launches of one library call: the GEMM is an x-split launch, the
+    GEMM and (split-K) a reduction, per matrix of a pair plus the SwiGLU
+    pass; the GEMV one launch per pass of <= 8 rows (pairs stream together)."""
+    if gemm_ok and mlq.takes_gemm(rows, out_f, in_f):
+        per = 2 + (gemm_split(out_f, in_f, rows, sms) > 1)
+        return 2 * per + 1 if pair else per
     n = 0
     while rows > 0:
         rows -= min(rows, 8 if rows >= 5 else 4 if rows >= 3 else 2 if rows == 2 else 1)
@@ -290,318 +338,416 @@ def gemv_passes(rows):
     return n
 
 
-def launches_per_call(mlq, rows, out_f, in_f, local, pair):
-    """Kernel launches of one library call in this bench (all shapes here are
-    aligned for every kernel): the GEMM is an x-split launch plus the GEMM
-    (per matrix of a pair, plus the SwiGLU pass); the GEMV one launch per pass."""
-    if local and mlq.takes_gemm(rows, out_f, in_f):
-        return 5 if pair else 2
-    return gemv_passes(rows)
+class Ctx:
+    """Process-wide state of the GPU arm (one process per GPU)."""
+
+    def __init__(self):
+        import torch
+        import torch.distributed as dist
+        self.torch, self.dist = torch, dist
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(self.local)
+        self.device = torch.device("cuda", self.local)
+        if self.world > 1:
+            from datetime import timedelta
+            dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=self.device)
+        self.pkg = load_pkg()
+        self.mlq = self.pkg.mlq
+        self.sh = importlib.import_module("mini_llama_b200.sharding")
+        self.stream = torch.cuda.Stream(self.device)
+        self.sms = torch.cuda.get_device_properties(self.device).multi_processor_count
+        self.group = self.flags = None
+        if self.world > 1:
+            self.group = self.sh.PeerGroup(self.mlq, dist, self.rank, self.world)
+            self.flags = self.group.alloc(self.mlq.flag_bytes())
+        self.tok = torch.zeros(1, device=self.device)
+
+    def max_over_ranks(self, v):
+        if self.world == 1:
+            return v
+        t = self.torch.tensor([v], device=self.device)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def timed(self, fn):
+        """ms of fn()'s GPU work on the bench stream, CUDA events, max over
+        ranks.  At N > 1 the ranks first meet in an NCCL all-reduce on the
+        bench stream, so every rank's start event fires after the same device
+        rendezvous (not after a host barrier, which releases ranks at
+        different times)."""
+        torch = self.torch
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            self.dist.barrier()
+            with torch.cuda.stream(self.stream):
+                self.dist.all_reduce(self.tok)
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(self.stream)
+        fn()
+        t1.record(self.stream)
+        t1.synchronize()
+        return self.max_over_ranks(t0.elapsed_time(t1))
+
+    def close(self):
+        if self.world > 1:
+            self.dist.barrier()
+            self.group.close()
+            self.dist.destroy_process_group()
 
 
-def placement(world):
-    if world == 1:
-        return {name: "shard" for name, _, _ in WORKLOAD["matrices"]}
-    return {name: ("shard" if weight_bytes(WORKLOAD["fmt"], o, i) >= SHARD_MIN_BYTES else "local0")
-            for name, o, i in WORKLOAD["matrices"]}
+class Step:
+    """One workload on this rank: resident packed weights (this rank's rows),
+    x, y, and the batches that launch a whole step with one library call."""
+
+    def __init__(self, ctx, wl):
+        torch, mlq, sh, pkg = ctx.torch, ctx.mlq, ctx.sh, ctx.pkg
+        self.ctx, self.wl = ctx, wl
+        fmt, rows, mats = wl["fmt"], wl["rows"], wl["matrices"]
+        self.fmt, self.rows = fmt, rows
+        self.plan = sh.StepPlan(mats, ctx.world, ctx.rank, shard=wl["shard"])
+        fused = wl.get("fused", {})
+        pair = fused.get("pair")
+        if pair and ctx.world > 1:
+            raise SystemExit("bench: the fused workload runs on one GPU")
+        self.keep = []
+        self.w, self.x, self.y = {}, {}, {}
+        self.bytes_step = sum(weight_bytes(fmt, o, i) for _, o, i in mats)
+        # packed weights of this rank's rows, drawn row chunk by row chunk
+        for i, (name, out_f, in_f) in enumerate(mats):
+            b, e = self.plan.rows(name)
+            if not self.plan.active(name) or e == b:
+                self.w[name] = None
+            else:
+                self.w[name] = self._weights(i, b, e, in_f)
+            self.x[name] = torch.from_numpy(pkg.synth.normal((rows, in_f), seed=2000 + i)).to(ctx.device)
+        torch.cuda.empty_cache()
+        # per op (call order): the matrix, the launch count, the ops of both y parities
+        shard_names = self.plan.sharded
+        self.slab = None
+        if shard_names:
+            self.slab = sh.GatherSlab(ctx.group, [4 * rows * dict((n, o) for n, o, _ in mats)[n]
+                                                  for n in shard_names])
+        self.gathers = [[], []]
+        self.names, self.op_bytes, self.launches = [], [], []
+        ops = [[], []]
+        for i, (name, out_f, in_f) in enumerate(mats):
+            if not self.plan.active(name) or (pair and name == pair[1]):
+                continue
+            b, e = self.plan.rows(name)
+            wp = self.w[name].data_ptr() if self.w[name] is not None else 0
+            if self.plan.place[name] == "shard":
+                k = shard_names.index(name)
+                for p in (0, 1):
+                    g = mlq.make_gather(ctx.world, ctx.rank, b, e, self.slab.peer_ptrs(p, k),
+                                        ctx.flags.peers, epoch=1)
+                    self.gathers[p].append(g)
+                    ops[p].append(mlq.linear_op(fmt, wp, out_f, in_f, self.x[name].data_ptr(), rows,
+                                                self.slab.local_ptr(p, k), gather=g))
+                self.launches.append(launches_of(mlq, rows, e - b, in_f, False, False, ctx.sms))
+            else:
+                y = torch.empty((rows, out_f), dtype=torch.float32, device=ctx.device)
+                self.y[name] = y
+                w_up = bias = None
+                if pair and name == pair[0]:
+                    w_up = self.w[pair[1]].data_ptr()
+                if name in fused.get("bias", ()):
+                    bt = torch.from_numpy(pkg.synth.normal((out_f,), seed=3000 + i, std=0.02)).to(ctx.device)
+                    self.keep.append(bt)
+                    bias = bt.data_ptr()
+                op = mlq.linear_op(fmt, wp, out_f, in_f, self.x[name].data_ptr(), rows, y.data_ptr(),
+                                   w_up_ptr=w_up, bias_ptr=bias)
+                ops[0].append(op)
+                ops[1].append(op)
+                self.launches.append(launches_of(mlq, rows, out_f, in_f, True, w_up is not None, ctx.sms))
+            self.names.append(name)
+            nb = weight_bytes(fmt, e - b, in_f)
+            self.op_bytes.append(2 * nb if (pair and name == pair[0]) else nb)
+        self.ops = ops
+        self.batch = [mlq.Batch(ops[0]), mlq.Batch(ops[1])]
+        self.single = [[mlq.Batch([op]) for op in ops[p]] for p in (0, 1)]
+        # rotating copies (an L2-sized matrix): one batch per copy
+        self.rot = None
+        if wl.get("rotate"):
+            name = mats[0][0]
+            copies = [self.w[name]] + [self.w[name].clone() for _ in range(wl["rotate"] - 1)]
+            self.keep += copies
+            rops = []
+            for c in copies:
+                op = mlq.LinearOp.from_buffer_copy(ops[0][0])
+                op.w = c.data_ptr()
+                rops.append(op)
+            self.rot = mlq.Batch(rops)
+        self.steps_run = 0
+        torch.cuda.synchronize(ctx.device)
+
+    def _weights(self, i, b, e, in_f):
+        """Packed blocks of rows [b, e) of matrix i: N(0, 0.02) from seed
+        1000 + i (synth.normal_torch at the rows' offset), quantized on the GPU."""
+        torch, mlq, pkg = self.ctx.torch, self.ctx.mlq, self.ctx.pkg
+        rb = ((in_f + 31) // 32) * mlq.BLOCK_BYTES[self.fmt]
+        out = torch.empty((e - b) * rb, dtype=torch.uint8, device=self.ctx.device)
+        chunk = max(8, (1 << 26) // in_f // 8 * 8)
+        for r0 in range(b, e, chunk):
+            r1 = min(e, r0 + chunk)
+            w32 = pkg.synth.normal_torch((r1 - r0, in_f), seed=1000 + i, std=0.02, device=self.ctx.device,
+                                         offset=r0 * in_f)
+            out[(r0 - b) * rb:(r1 - b) * rb] = mlq.quantize(self.fmt, w32)
+            del w32
+        return out
+
+    def _set_epochs(self, parity, epochs):
+        for g, ep in zip(self.gathers[parity], epochs):
+            g.epoch = ep
+
+    def step(self):
+        """One pass over the workload: one library call."""
+        if self.rot is not None:
+            self.rot.run(self.ctx.stream.cuda_stream)
+            return
+        parity, epochs = self.plan.next_step()
+        self._set_epochs(parity, epochs)
+        self.batch[parity].run(self.ctx.stream.cuda_stream)
+        self.steps_run += 1
+
+    def step_host(self, host_batches):
+        parity, epochs = self.plan.next_step()
+        self._set_epochs(parity, epochs)
+        host_batches[parity].run_host(self.ctx.local, self.ctx.stream.cuda_stream)
+
+    def per_launch_ms(self, rounds):
+        """Mean CUDA-event time of each op launched on its own (events around
+        every op of a step, `rounds` steps)."""
+        torch, s = self.ctx.torch, self.ctx.stream
+        n = len(self.names)
+        evs = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                for _ in range(n)] for _ in range(rounds)]
+        for r in range(rounds):
+            parity, epochs = self.plan.next_step()
+            self._set_epochs(parity, epochs)
+            for j in range(n):
+                evs[r][j][0].record(s)
+                self.single[parity][j].run(s.cuda_stream)
+                evs[r][j][1].record(s)
+        torch.cuda.synchronize(self.ctx.device)
+        return [statistics.mean(evs[r][j][0].elapsed_time(evs[r][j][1]) for r in range(rounds))
+                for j in range(n)]
+
+    def back_to_back_ms(self, j, reps):
+        """One local op launched `reps` times in a row between two events (the
+        launches overlap as inside a step).  None for a sharded op: its calls
+        are tied to the peers' calls."""
+        torch, s = self.ctx.torch, self.ctx.stream
+        if self.plan.place[self.names[j]] == "shard":
+            return None
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize(self.ctx.device)
+        e0.record(s)
+        for _ in range(reps):
+            self.single[0][j].run(s.cuda_stream)
+        e1.record(s)
+        e1.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    def parity_check(self):
+        """Every sharded matrix: the gathered y of its last call on this rank
+        against one local mlq_linear of the whole matrix (regenerated from
+        its seed) on the same x; max relative L2 error of an output row."""
+        torch, mlq = self.ctx.torch, self.ctx.mlq
+        worst = 0.0
+        for k, name in enumerate(self.plan.sharded):
+            i, (_, out_f, in_f) = next((i, m) for i, m in enumerate(self.wl["matrices"]) if m[0] == name)
+            parity = (self.plan.calls[name] - 1) & 1
+            got = self.ctx.sh.device_view(self.slab.local_ptr(parity, k), (self.rows, out_f)).clone()
+            full = self._weights(i, 0, out_f, in_f)
+            ref = mlq.linear(self.fmt, full, out_f, in_f, self.x[name])
+            torch.cuda.synchronize(self.ctx.device)
+            err = (torch.linalg.norm((got - ref).double(), dim=1) /
+                   torch.linalg.norm(ref.double(), dim=1).clamp_min(1e-30)).max().item()
+            worst = max(worst, err)
+            del full, ref, got
+        torch.cuda.empty_cache()
+        return self.ctx.max_over_ranks(worst)
 
 
-def make_inputs(torch, pkg, device, world=1, rank=0):
-    """Quantized weights on the device (this rank's rows) and x vectors."""
-    import importlib
-    sh = importlib.import_module("mini_llama_b200.sharding")
-    fmt = WORKLOAD["fmt"]
-    g = torch.Generator(device=device)
-    ws, xs_dev, xs_host, ranges = [], [], [], []
-    for i, (name, out_f, in_f) in enumerate(WORKLOAD["matrices"]):
-        place = placement(world)[name]
-        rg = sh.shard_rows(out_f, world, owners=[0] if place in ("local0", "bcast0") else None)
-        b, e = rg[rank]
-        ranges.append(rg)
-        g.manual_seed(1000 + i)
-        w32 = torch.randn((out_f, in_f), generator=g, device=device, dtype=torch.float32) * 0.02
-        ws.append(pkg.mlq.quantize(fmt, w32[b:e].contiguous()) if e > b else None)
+def run_workload(ctx, wl, steps, warmup, full=False, args=None):
+    """Times `steps` steps of a workload (after `warmup`); with `full`, also the
+    per-launch roofline, the back-to-back dominant launch, the e2e path and
+    (N > 1) the parity gate.  Returns a dict (on every rank)."""
+    torch, mlq = ctx.torch, ctx.mlq
+    st = Step(ctx, wl)
+    for _ in range(max(3, warmup)):
+        st.step()
+    torch.cuda.synchronize(ctx.device)
+    res = {}
+    if ctx.world > 1 and st.plan.sharded:
+        res["parity_max_rel_l2"] = st.parity_check()
+    clocks = ClockSampler(ctx.local)
+    with clocks:
+        ms = ctx.timed(lambda: [st.step() for _ in range(steps)])
+    per_step_bytes = st.bytes_step * (1 if not wl.get("rotate") else wl["rotate"])
+    res.update({"value": round(per_step_bytes * steps / (ms / 1e3) / 1e9, 2),
+                "ms_per_step": round(ms / steps, 5), "steps": steps, "clocks": clocks.summary(),
+                "gpu_launches_per_step": sum(st.launches) * (wl.get("rotate") or 1)})
+    # the dominant op of this rank and its roofline
+    rounds = max(5, min(steps, 200)) if full else 5
+    if wl.get("rotate"):
+        per_launch = ms / steps / wl["rotate"]
+        res["roofline"] = _roof(st.op_bytes[0], per_launch, None, wl, ctx, st, 0)
+    else:
+        per = st.per_launch_ms(rounds)
+        dj = max(range(len(st.names)), key=lambda j: st.op_bytes[j])
+        b2b = st.back_to_back_ms(dj, 50) if full else None
+        res["roofline"] = _roof(st.op_bytes[dj], per[dj], b2b, wl, ctx, st, dj)
+        res["roofline"]["per_launch_ms"] = {n: round(v, 5) for n, v in zip(st.names, per)}
+        res["roofline"]["all_launches_GBps"] = round(sum(st.op_bytes) / (sum(per) / 1e3) / 1e9, 1)
+    if full and not (args and args.no_e2e):
+        res["e2e"] = _e2e(ctx, st, steps)
+    del st
+    torch.cuda.empty_cache()
+    return res
+
+
+def _roof(nbytes, launch_ms, b2b_ms, wl, ctx, st, j):
+    mlq = ctx.mlq
+    peak, kind = hbm_peak()
+    name = st.names[j]
+    out_f, in_f = next((o, i) for n, o, i in wl["matrices"] if n == name)
+    b, e = st.plan.rows(name)
+    local = st.plan.place[name] != "shard"
+    gemm = local and mlq.takes_gemm(wl["rows"], out_f, in_f)
+    kernel = (f"gemm_tc_kernel<{wl['fmt']}>" if gemm else
+              f"gemv_stream_kernel<{wl['fmt']}, MT={min(wl['rows'], 8)}, "
+              f"{'integer' if wl['rows'] == 1 else 'fp32'} mode>") + f" ({name} launch, rank {ctx.rank})"
+    ach = nbytes / (launch_ms / 1e3) / 1e9
+    r = {"bound": "hbm", "kernel": kernel, "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
+         "frac": round(ach / peak, 4), "peak_kind": peak_kind_text(kind),
+         "traffic": None, "algorithmic_bytes_per_launch": nbytes, "launch_ms": round(launch_ms, 5)}
+    if b2b_ms:
+        r["launch_ms_back_to_back"] = round(b2b_ms, 5)
+        r["achieved_back_to_back"] = round(nbytes / (b2b_ms / 1e3) / 1e9, 1)
+        r["frac_back_to_back"] = round(nbytes / (b2b_ms / 1e3) / 1e9 / peak, 4)
+    if gemm:
+        flops = 2.0 * wl["rows"] * (e - b) * in_f
+        tpk, tkind = bf16_peak()
+        tach = flops / (launch_ms / 1e3) / 1e12
+        r.update({"bound": "tensor" if wl["rows"] >= 64 else "hbm",
+                  "tensor_achieved_TFLOPs": round(tach, 1), "tensor_peak_TFLOPs": tpk,
+                  "tensor_frac": round(tach / tpk, 4), "algorithmic_flops_per_launch": flops})
+        if wl["rows"] >= 64:
+            r.update({"achieved": round(tach, 1), "peak": tpk, "unit": "TFLOP/s", "frac": round(tach / tpk, 4),
+                      "peak_kind": peak_kind_text(tkind)})
+    return r
+
+
+def peak_kind_text(kind):
+    return "of measured (MEASURED_PEAKS.json)" if kind == "measured" else "of fallback"
+
+
+def _e2e(ctx, st, steps):
+    """The same step through mlq_linear_batch_host: pinned host x and y, the
+    copies and one synchronisation inside every step."""
+    torch, mlq = ctx.torch, ctx.mlq
+    hx, hy, host_batches = {}, {}, []
+    for p in (0, 1):
+        hops = []
+        for op, name in zip(st.ops[p], st.names):
+            if name not in hx:
+                hx[name] = st.x[name].cpu().pin_memory()
+                out_f = next(o for n, o, _ in st.wl["matrices"] if n == name)
+                hy[name] = torch.empty((st.rows, out_f), dtype=torch.float32).pin_memory()
+            h = mlq.LinearOp.from_buffer_copy(op)
+            h.x, h.y = hx[name].data_ptr(), hy[name].data_ptr()
+            hops.append(h)
+        host_batches.append(mlq.Batch(hops))
+    ke = max(3, min(steps, 300))
+    for _ in range(3):
+        st.step_host(host_batches)
+    ms = ctx.timed(lambda: [st.step_host(host_batches) for _ in range(ke)])
+    bytes_step = st.bytes_step
+    h2d = sum(4 * st.rows * next(i for n, _, i in st.wl["matrices"] if n == name) for name in st.names)
+    d2h = sum(4 * st.rows * next(o for n, o, _ in st.wl["matrices"] if n == name) for name in st.names)
+    return {"value": round(bytes_step * ke / (ms / 1e3) / 1e9, 2), "unit": UNIT,
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": ke,
+            "path": "mlq_linear_batch_host: the step's ops in one call, pinned host x/y, "
+                    "one stream synchronisation per step"}
+
+
+def formats_probe(ctx):
+    """Decode (batch 1) weight GB/s of one large matrix per format, launches
+    back to back, against the measured HBM peak: q8_0 and q4_1 at the
+    Llama-3-8B FFN shape 14336x4096 (configs 4 and 3), q4_0 at the Qwen2-7B
+    lm_head 152064x3584 (config 2)."""
+    torch, mlq, pkg = ctx.torch, ctx.mlq, ctx.pkg
+    peak, _ = hbm_peak()
+    out = {}
+    for fmt, (o, i) in [("q8_0", (14336, 4096)), ("q4_0", (152064, 3584)), ("q4_1", (14336, 4096))]:
+        w32 = pkg.synth.normal_torch((o, i), seed=4242, std=0.02, device=ctx.device)
+        w = mlq.quantize(fmt, w32)
         del w32
-        torch.cuda.empty_cache()  # keep only the packed weights resident
-        x = pkg.synth.normal((WORKLOAD["rows"], in_f), seed=2000 + i)
-        xs_host.append(x)
-        xs_dev.append(torch.from_numpy(x).to(device))
-    torch.cuda.synchronize(device)
-    return ws, xs_dev, xs_host, ranges
+        x = torch.from_numpy(pkg.synth.normal((1, i), seed=4243)).to(ctx.device)
+        y = torch.empty((1, o), device=ctx.device)
+        b = mlq.Batch([mlq.linear_op(fmt, w.data_ptr(), o, i, x.data_ptr(), 1, y.data_ptr())] * 20)
+        for _ in range(3):
+            b.run(ctx.stream.cuda_stream)
+        ms = ctx.timed(lambda: [b.run(ctx.stream.cuda_stream) for _ in range(10)]) / 200
+        gbs = weight_bytes(fmt, o, i) / (ms / 1e3) / 1e9
+        out[fmt] = {"matrix": [o, i], "launch_ms_back_to_back": round(ms, 5), "GBps": round(gbs, 1),
+                    "frac_of_measured_hbm": round(gbs / peak, 4)}
+        del w, x, y, b
+    torch.cuda.empty_cache()
+    return out
 
 
 def run_mlq(args):
-    import importlib
-
-    import torch
-    import torch.distributed as dist
-
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    device = torch.device("cuda", local)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
-    pkg = load_pkg()
-    mlq = pkg.mlq
-    sh = importlib.import_module("mini_llama_b200.sharding")
-    fmt = WORKLOAD["fmt"]
-    mats = WORKLOAD["matrices"]
-    rows = WORKLOAD["rows"]
-    ws, xs, xs_host, ranges = make_inputs(torch, pkg, device, world, rank)
-    bytes_step = sum(weight_bytes(fmt, o, i) for _, o, i in mats)
-    stream = torch.cuda.Stream(device)
-    sh_stream = stream.cuda_stream
-    L = mlq.lib()
-    fid = mlq.FORMATS[fmt]
-
-    # per matrix: a callable launching this rank's share of it
-    calls, ybufs, launches_per_step = [], [], 0
-    fused = WORKLOAD.get("fused", {})
-    pair = fused.get("pair")
-    if pair and world > 1 and any(placement(world)[n] != "local0" for n in pair):
-        raise SystemExit("bench: a SwiGLU pair is launched on one GPU (placement local0)")
-    group = None
-    if world > 1:
-        group = sh.PeerGroup(mlq, dist, rank, world)
-        flags = group.alloc(mlq.flag_bytes())
-    epoch = [0]
-    for j, (name, out_f, in_f) in enumerate(mats):
-        b, e = ranges[j][rank]
-        if world == 1 or placement(world)[name] == "local0":
-            if e == b:
-                calls.append(None)
-                ybufs.append(None)
-                continue
-            if pair and name == pair[1]:
-                # the up projection streams inside the gate's pair launch
-                calls.append(None)
-                ybufs.append(None)
-                continue
-            y = torch.empty((rows, out_f), dtype=torch.float32, device=device)
-            nb = ws[j].numel() // mlq.BLOCK_BYTES[fmt]
-            if pair and name == pair[0]:
-                ju = [m[0] for m in mats].index(pair[1])
-
-                def call(j=j, ju=ju, out_f=out_f, in_f=in_f, y=y, nb=nb):
-                    st = L.mlq_linear_swiglu(fid, ws[j].data_ptr(), ws[ju].data_ptr(), nb, out_f, in_f,
-                                             xs[j].data_ptr(), rows, y.data_ptr(), sh_stream)
-                    if st != 0:
-                        raise RuntimeError(L.mlq_last_error().decode())
-                    return y.data_ptr()
-            elif name in fused.get("bias", ()):
-                bias = torch.from_numpy(pkg.synth.normal((out_f,), seed=3000 + j, std=0.02)).to(device)
-
-                def call(j=j, out_f=out_f, in_f=in_f, y=y, nb=nb, bias=bias):
-                    st = L.mlq_linear_bias(fid, ws[j].data_ptr(), nb, out_f, in_f, xs[j].data_ptr(), rows,
-                                           bias.data_ptr(), y.data_ptr(), sh_stream)
-                    if st != 0:
-                        raise RuntimeError(L.mlq_last_error().decode())
-                    return y.data_ptr()
-            else:
-                def call(j=j, out_f=out_f, in_f=in_f, y=y, nb=nb):
-                    st = L.mlq_linear(fid, ws[j].data_ptr(), nb, out_f, in_f, xs[j].data_ptr(), rows,
-                                      y.data_ptr(), sh_stream)
-                    if st != 0:
-                        raise RuntimeError(L.mlq_last_error().decode())
-                    return y.data_ptr()
-            calls.append(call)
-            ybufs.append(lambda y=y: y.data_ptr())
-        else:
-            lin = sh.ShardedLinear(mlq, fmt, out_f, in_f, rows, ranges[j], rank, group, flags)
-
-            def call(j=j, lin=lin):
-                epoch[0] += 1
-                return lin(ws[j].data_ptr() if ws[j] is not None else 0, xs[j].data_ptr(), epoch[0],
-                           sh_stream)
-            calls.append(call)
-            ybufs.append(lambda lin=lin: lin.y_ptr(epoch[0]))
-        on_one_gpu = world == 1 or placement(world)[name] == "local0"
-        launches_per_step += launches_per_call(mlq, rows, out_f, in_f, on_one_gpu,
-                                               bool(pair) and name == pair[0])
-
-    def step(events=None):
-        for j, call in enumerate(calls):
-            if call is None:
-                continue
-            if events is not None:
-                events[j][0].record(stream)
-            call()
-            if events is not None:
-                events[j][1].record(stream)
-
-    with torch.cuda.stream(stream):
-        for _ in range(max(3, args.warmup)):
-            step()
-    torch.cuda.synchronize(device)
-
-    # ---- headline: K steps on the device, inputs resident in HBM ----
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize(device)
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
-        t0.record(stream)
-        with torch.cuda.stream(stream):
-            for _ in range(args.steps):
-                step()
-        t1.record(stream)
-        t1.synchronize()
-    ms = t0.elapsed_time(t1)
-    if world > 1:
-        tm = torch.tensor([ms], device=device)
-        dist.all_reduce(tm, op=dist.ReduceOp.MAX)
-        ms = float(tm.item())
-    torch.cuda.synchronize(device)
-    value = bytes_step * args.steps / (ms / 1e3) / 1e9
-
-    # ---- per-launch durations (CUDA events on the launching stream) ----
-    k2 = max(20, min(args.steps, 400))
-    evs = [[[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)]
-            for _ in mats] for _ in range(k2)]
-    if world > 1:
-        dist.barrier()
-    with torch.cuda.stream(stream):
-        for k in range(k2):
-            step(evs[k])
-    torch.cuda.synchronize(device)
-    per = {name: statistics.mean(evs[k][j][0].elapsed_time(evs[k][j][1]) for k in range(k2))
-           for j, (name, _, _) in enumerate(mats) if calls[j] is not None}
-    peak, peak_kind = hbm_peak()
-    # dominant launch: the largest share of weight bytes on this rank
-    def local_bytes(j):
-        b, e = ranges[j][rank]
-        nbytes = weight_bytes(fmt, e - b, mats[j][2])
-        return 2 * nbytes if pair and mats[j][0] == pair[0] else nbytes  # a pair launch reads both
-    dj = max((j for j in range(len(mats)) if calls[j] is not None), key=local_bytes)
-    dom, dom_bytes = mats[dj][0], local_bytes(dj)
-    achieved = dom_bytes / (per[dom] / 1e3) / 1e9
-    kernel_sum_ms = sum(per.values())
-    # the dominant matrix alone, R launches back to back between two events
-    # (consecutive launches overlap as in the step; the isolated per-launch
-    # figure above includes each launch's ramp and drain)
-    rb = 50
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize(device)
-    b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):
-        b0.record(stream)
-        for _ in range(rb):
-            calls[dj]()
-        b1.record(stream)
-    b1.synchronize()
-    b2b_ms = b0.elapsed_time(b1) / rb
-    if world > 1:
-        tm = torch.tensor([b2b_ms], device=device)
-        dist.all_reduce(tm, op=dist.ReduceOp.MAX)
-        b2b_ms = float(tm.item())
-    traffic = read_traffic() if world == 1 and WORKLOAD["name"] == WORKLOADS["qwen7b"]["name"] and dom == "lm_head" else None
-
-    # ---- e2e: host x / host y around every call, copies inside the timed region ----
-    e2e = None
-    if not args.no_e2e:
-        xh = [torch.from_numpy(x).pin_memory() for x in xs_host]
-        yh = [torch.empty((rows, o), dtype=torch.float32).pin_memory() for _, o, _ in mats]
-        ke = max(3, min(args.steps, 300))
-
-        def e2e_step():
-            if world == 1 and not fused:
-                for j, (name, out_f, in_f) in enumerate(mats):
-                    st = L.mlq_linear_host(fid, ws[j].data_ptr(), ws[j].numel() // mlq.BLOCK_BYTES[fmt],
-                                           out_f, in_f, xh[j].data_ptr(), rows, None,
-                                           yh[j].data_ptr(), local, sh_stream)
-                    if st != 0:
-                        raise RuntimeError(L.mlq_last_error().decode())
-                return
-            with torch.cuda.stream(stream):
-                for j, (name, out_f, in_f) in enumerate(mats):
-                    if calls[j] is None:
-                        continue
-                    xs[j].copy_(xh[j], non_blocking=True)
-                    yp = calls[j]()
-                    yh[j].copy_(sh.device_view(yp, (rows, out_f)), non_blocking=True)
-                stream.synchronize()
-        for _ in range(3):
-            e2e_step()
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize(device)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(ke):
-            e2e_step()
-        e1.record(stream)
-        e1.synchronize()
-        ems = e0.elapsed_time(e1)
-        if world > 1:
-            tm = torch.tensor([ems], device=device)
-            dist.all_reduce(tm, op=dist.ReduceOp.MAX)
-            ems = float(tm.item())
-        h2d = sum(4 * rows * i for j, (_, _, i) in enumerate(mats) if calls[j] is not None)
-        d2h = sum(4 * rows * o for j, (_, o, _) in enumerate(mats) if calls[j] is not None)
-        e2e = {"value": round(bytes_step * ke / (ems / 1e3) / 1e9, 2), "unit": UNIT,
-               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": ke,
-               "path": ("mlq_linear_host (device weights, pinned host x/y)" if world == 1 and not fused else
-                        "pinned x H2D + the step's device call + y D2H, per launch")}
-
-    err = mlq.device_error(local)
+    ctx = Ctx()
+    wl = dict(WORKLOADS[args.workload])
+    if args.only:
+        wl["matrices"] = [m for m in wl["matrices"] if m[0] == args.only]
+    head = run_workload(ctx, wl, args.steps, args.warmup, full=True, args=args)
+    if ctx.world == 1 and args.workload == "qwen7b" and "lm_head" in head["roofline"]["kernel"]:
+        head["roofline"]["traffic"] = read_traffic()
+    extra, formats = {}, None
+    if not args.no_extra and not args.only and args.workload == "qwen7b":
+        for name in (EXTRAS_N1 if ctx.world == 1 else EXTRAS_NGT1):
+            ew = WORKLOADS[name]
+            r = run_workload(ctx, ew, min(args.steps, 10 if name != "llama8b-b16" else 5), 3)
+            extra[name] = {"workload": ew["name"], "metric": ew["metric"], "value": r["value"], "unit": UNIT,
+                           "ms_per_step": r["ms_per_step"], "steps": r["steps"],
+                           "frac_of_measured_hbm": round(r["value"] / hbm_peak()[0], 4),
+                           "roofline": r["roofline"], "clocks": r["clocks"],
+                           **({"parity_max_rel_l2": r["parity_max_rel_l2"]} if "parity_max_rel_l2" in r else {})}
+        if ctx.world == 1:
+            formats = formats_probe(ctx)
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = reference_cpu_baseline(pkg, args.cpu_seconds)
-
-    # the dominant launch's kernel: sharded calls always stream; local calls
-    # follow the library's routing rule (MLQ_GEMM_ROWS_RULE)
-    dom_local = world == 1 or placement(world)[dom] == "local0"
-    dom_gemm = dom_local and mlq.takes_gemm(rows, mats[dj][1], mats[dj][2])
-    kernel = (f"gemv_stream_kernel<{fmt}, MT={rows}, integer mode>" if rows == 1 else
-              f"gemv_stream_kernel<{fmt}, MT={min(rows, 8)}, fp32 mode>" if not dom_gemm else
-              f"gemm_tc_kernel<{fmt}>") + f" ({dom} launch, rank 0)"
-    roof = {"bound": "hbm", "kernel": kernel, "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-            "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-            "traffic": traffic, "algorithmic_bytes_per_launch": dom_bytes,
-            "launch_ms": round(per[dom], 5),
-            "launch_ms_back_to_back": round(b2b_ms, 5),
-            "achieved_back_to_back": round(dom_bytes / (b2b_ms / 1e3) / 1e9, 1),
-            "all_launches_GBps": round(sum(local_bytes(j) for j in range(len(mats)) if calls[j] is not None)
-                                       / (kernel_sum_ms / 1e3) / 1e9, 1),
-            "per_launch_ms": {k: round(v, 5) for k, v in per.items()}}
-    if dom_gemm:
-        # the GEMM is tensor-bound: algorithmic flops of the dominant launch
-        # (2 * rows * its rows of W * in) against the measured bf16 peak
-        b_, e_ = ranges[dj][rank]
-        flops = 2.0 * rows * (e_ - b_) * mats[dj][2]
-        tpk, tpk_kind = bf16_peak()
-        tach = flops / (per[dom] / 1e3) / 1e12
-        roof.update({"bound": "tensor", "achieved": round(tach, 1), "peak": tpk, "unit": "TFLOP/s",
-                     "frac": round(tach / tpk, 4), "peak_kind": tpk_kind,
-                     "algorithmic_flops_per_launch": flops,
-                     "achieved_back_to_back": round(flops / (b2b_ms / 1e3) / 1e12, 1),
-                     "note": "three bf16 MMAs per K-step (x and W split into hi/lo): executed flops are ~3x"})
-    if rank == 0:
+    if ctx.rank == 0 and ctx.world == 1 and not args.no_cpu_baseline and not args.only:
+        cpu = reference_cpu_baseline(ctx.pkg, wl, args.cpu_seconds)
+    parity = [v.get("parity_max_rel_l2") for v in [head, *extra.values()] if "parity_max_rel_l2" in v]
+    dev_err = ctx.mlq.device_error(ctx.local)  # any kernel of the whole run that gave up
+    if ctx.rank == 0:
         line = {
-            "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5),
-            "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": f"fp32 activations x {fmt} weights",
-            "data": f"synthetic (seeded N(0,0.02) weights quantized to {fmt}; N(0,1) x)",
-            "config": {"workload": WORKLOAD["name"], "format": fmt, "batch": rows,
-                       "matrices": {n: [o, i] for n, o, i in mats},
-                       "weight_bytes_per_step": bytes_step,
-                       **({"fused": fused} if fused else {}),
-                       "placement": placement(world) if world > 1 else "all on one GPU",
-                       "l2": f"inputs larger than L2 ({bytes_step / 1e6:.1f} MB per step vs 126 MB L2); no flush"},
-            "roofline": roof,
-            "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps * launches_per_step,
-            "clocks": clocks.summary(), "device_error": err,
+            "metric": wl["metric"], "value": head["value"], "unit": UNIT, "n_gpus": ctx.world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": head["ms_per_step"],
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": f"fp32 activations x {wl['fmt']} weights",
+            "data": f"synthetic (seeded N(0,0.02) weights quantized to {wl['fmt']}; N(0,1) x)",
+            "config": config_of(wl, ctx.world),
+            "roofline": head["roofline"], "cpu_baseline": cpu, "e2e": head.get("e2e"),
+            "gpu_launches": args.steps * head["gpu_launches_per_step"],
+            "clocks": head["clocks"], "device_error": dev_err,
         }
+        if "parity_max_rel_l2" in head:
+            line["parity_max_rel_l2"] = head["parity_max_rel_l2"]
+        if extra:
+            line["extra"] = extra
+        if formats:
+            line["formats"] = formats
         print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.barrier()
-        group.close()
-        dist.destroy_process_group()
+    ctx.close()
+    if dev_err or any(p is None or p > 1e-3 for p in parity):
+        raise SystemExit(f"bench: device error {dev_err} or sharded results differ from the one-GPU "
+                         f"results (max rel L2 {parity})")
 
 
 def read_traffic():
@@ -627,14 +773,15 @@ def run_reference(args):
     if rank != 0:
         return  # single-process CPU code: only rank 0 runs and prints
     pkg = load_pkg()
-    fmt = WORKLOAD["fmt"]
-    base = {"impl": "reference", "metric": METRIC, "unit": UNIT, "n_gpus": world,
+    wl = WORKLOADS[args.workload]
+    fmt = wl["fmt"]
+    base = {"impl": "reference", "metric": wl["metric"], "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": f"fp32 activations x {fmt} weights",
             "data": f"synthetic (seeded N(0,0.02) weights quantized to {fmt}; N(0,1) x)",
-            "config": {"workload": WORKLOAD["name"], "format": fmt, "batch": WORKLOAD["rows"]}}
+            "config": config_of(wl, world)}
     try:
-        rc = ReferenceCPU()
+        rc = ReferenceCPU(wl)
     except FileNotFoundError as e:
         print(json.dumps({"impl": "reference", "unavailable": str(e)}), flush=True)
         return
@@ -647,7 +794,7 @@ def run_reference(args):
     total = sum(rc.step() for _ in range(args.steps))
     value = rc.bytes * args.steps / total / 1e9
     rc.release()
-    sample = (f"each step: linearQ40 over the first {frac:.2%} of every matrix's rows "
+    sample = (f"each step: linearQ{fmt[1]}{fmt[3]} over the first {frac:.2%} of every matrix's rows "
               f"({rc.bytes / MB:.1f} MB), ThreadPool threads = {rc.cores}, {rc.variant}")
     line = dict(base)
     line.update({
@@ -668,20 +815,15 @@ def main():
     ap.add_argument("--impl", default="mlq", choices=["mlq", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra", action="store_true", help="headline workload only")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--only", default=None,
                     help="run one matrix of the workload (qkv/o/gate/up/down/lm_head), for profiling")
     ap.add_argument("--workload", default="qwen7b", choices=sorted(WORKLOADS),
-                    help="qwen7b (default, the bench line) or a 70B-shaped scaling study")
+                    help="qwen7b (default, the bench line) or another BASELINE config")
     args = ap.parse_args()
-    global WORKLOAD, METRIC
-    WORKLOAD = dict(WORKLOADS[args.workload])
-    METRIC = WORKLOAD["metric"]
-    if args.only:
-        WORKLOAD["matrices"] = [m for m in WORKLOAD["matrices"] if m[0] == args.only]
-        if not WORKLOAD["matrices"]:
-            ap.error(f"--only: no matrix named {args.only!r}")
-        args.no_cpu_baseline = True
+    if args.only and not any(m[0] == args.only for m in WORKLOADS[args.workload]["matrices"]):
+        ap.error(f"--only: no matrix named {args.only!r}")
     if args.impl == "reference":
         run_reference(args)
     else:

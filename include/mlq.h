@@ -21,6 +21,15 @@
  *     is what the reference launches on).  Device-side entry points are
  *     asynchronous on that stream; *_host entry points are synchronous.
  *   - The current CUDA device must own every device pointer passed.
+ *   - Ordering with the previous kernel on the stream: the streaming GEMV is
+ *     launched with programmatic dependent launch, so it may start while the
+ *     kernel before it on the stream is still running.  It reads x and the
+ *     bias, and writes y, only after that kernel has completed; it streams
+ *     the WEIGHTS before.  So the weights must be complete before the
+ *     stream's previous kernel started, whenever that kernel lets its
+ *     dependents start early (this library's GEMV does; its quantizer and
+ *     the other kernels here do not, so a quantize followed by a linear on
+ *     one stream is ordered).
  */
 #ifndef MLQ_H_
 #define MLQ_H_
@@ -85,7 +94,9 @@ MLQ_API const char* mlq_status_string(mlq_status status);
 MLQ_API const char* mlq_last_error(void);
 
 /* Reads and clears the device-side error flag of `device` (non-zero after
- * a kernel gave up on a bounded wait).  Synchronizes that device. */
+ * a kernel gave up on a bounded wait).  Synchronizes that device.  When the
+ * flag was set it also resets the streaming GEMV's row-tile queues on that
+ * device, so launches after a failed one start clean. */
 MLQ_API mlq_status mlq_device_error(int device, int* code);
 
 /* ---------------------------------------------------------------------------
@@ -134,9 +145,15 @@ MLQ_API mlq_status mlq_linear(mlq_format fmt, const void* w, size_t block_count,
  * Same arguments, results and validation as mlq_linear.  The tensor-core
  * path keeps the bf16 hi/lo split of x in a static
  * MLQ_NOALLOC_SCRATCH_BYTES array of the library's device module instead
- * of a workspace; so a call with MLQ_GEMM_ROWS_RULE(rows, out_features,
- * in_features) true and rows * in_features * 4 bytes above that size returns
- * MLQ_ERR_RANGE before any CUDA call.  The array is one per
+ * of a workspace; so a call that takes the GEMM (MLQ_GEMM_ROWS_RULE(rows,
+ * out_features, in_features) true, 16-B aligned weights with a 16-B multiple
+ * row pitch, in_features % 8 == 0) and has rows * in_features * 4 bytes above
+ * that size returns MLQ_ERR_RANGE before any CUDA call; every other call
+ * takes the streaming GEMV, which needs no scratch, and is accepted at any
+ * size.  The GEMM's split-K partial sums share the array: the call uses the
+ * largest K split (at most mlq_linear's) whose partials fit next to the x
+ * split, so it can sum in another order than mlq_linear and differ from it
+ * by fp32 rounding.  The array is one per
  * device, shared by every call: calls ordered on one stream are fine,
  * calls whose kernels may overlap (several streams, several host threads)
  * race on it.  Nothing in it needs to start zeroed.  The first call on a
@@ -244,6 +261,56 @@ MLQ_API mlq_status mlq_linear_allgather(mlq_format fmt, const void* w_shard,
 
 /* Bytes of one rank's flag buffer for mlq_linear_allgather (256). */
 MLQ_API size_t mlq_flag_bytes(void);
+
+/* ---------------------------------------------------------------------------
+ * Batches: every quantized matmul of one decode step in one call
+ *
+ * The reference's forward pass (src/forward.cc:190-225, 425-435, 574-582,
+ * 741-742) makes one cudaQ*LinearDeviceInput call per matrix, each with its
+ * own host round trip.  A batch launches a list of products in list order
+ * on one stream with one call; the *_host form also moves every x to the
+ * device and every y back with a single synchronisation for the whole list.
+ * ------------------------------------------------------------------------- */
+
+/* Row-sharded form of one product in a batch: the arguments of
+ * mlq_linear_allgather that describe the shard and the gather.  The op's
+ * w / block_count are this rank's shard (rows [row_begin, row_end)); its y
+ * is ignored: the output lands in peer_y[rank] (and every peer's y). */
+typedef struct mlq_gather {
+    int world_size, rank;
+    int row_begin, row_end;
+    float* const* peer_y;         /* world_size pointers */
+    uint32_t* const* peer_flags;  /* world_size pointers */
+    uint32_t epoch;
+} mlq_gather;
+
+/* One product y[rows,out] = x[rows,in] W^T (+ bias), or -- w_up set -- the
+ * SwiGLU pair h = silu(x W^T) * (x W_up^T) of mlq_linear_swiglu. */
+typedef struct mlq_linear_op {
+    int fmt;                   /* mlq_format */
+    int out_features, in_features, rows;
+    const void* w;             /* device blocks (the shard when gather != NULL) */
+    const void* w_up;          /* device blocks of the up projection, or NULL */
+    size_t block_count;        /* blocks of w (and of w_up) */
+    const float* x;            /* device (mlq_linear_batch) or host (mlq_linear_batch_host) */
+    const float* bias;         /* DEVICE [out_features] bias, or NULL (not with w_up) */
+    float* y;                  /* device (mlq_linear_batch) or host (mlq_linear_batch_host) */
+    const mlq_gather* gather;  /* NULL: this GPU computes every row */
+} mlq_linear_op;
+
+/* Launches ops[0..n) in order on `stream`; asynchronous.  Every op is
+ * validated (as mlq_linear / mlq_linear_bias / mlq_linear_swiglu /
+ * mlq_linear_allgather) before the first launch, so a batch with a bad op
+ * launches nothing.  A gathered op takes no w_up. */
+MLQ_API mlq_status mlq_linear_batch(const mlq_linear_op* ops, int n, mlq_stream stream);
+
+/* mlq_linear_batch with HOST x and y (weights and bias on the device):
+ * copies every x to device staging, launches the products, copies every y
+ * back, then synchronises `stream` once.  Runs on `device`.  With pinned
+ * host buffers the copies are asynchronous DMA.  Calls on one device are
+ * serialised (the staging is per device). */
+MLQ_API mlq_status mlq_linear_batch_host(const mlq_linear_op* ops, int n, int device,
+                                         mlq_stream stream);
 
 /* Device memory shared with the other ranks' processes (CUDA IPC; plain
  * peer mappings, no multicast objects).  mlq_peer_alloc allocates `bytes`

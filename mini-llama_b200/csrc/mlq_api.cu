@@ -12,6 +12,7 @@
 #include <map>
 #include <mutex>
 #include <string>
+#include <vector>
 
 #include "mlq.h"
 #include "mlq_device.cuh"
@@ -294,9 +295,12 @@ mlq_status run_linear_noalloc(int fmt, const void* w, int out, int in, const flo
     std::call_once(s.once, [&] { s.err = cudaGetSymbolAddress(&s.ptr, g_mlq_noalloc_scratch); });
     if (s.err != cudaSuccess || s.ptr == nullptr)
         return fail_cuda("cudaGetSymbolAddress (static scratch)", s.err != cudaSuccess ? s.err : cudaErrorInvalidSymbol);
-    // split-K only when its partials fit the scratch next to the x split
+    // split-K as mlq_linear chooses it, lowered to the largest count whose
+    // partial sums fit the scratch next to the x split (1 always fits: the
+    // caller checked the x split against the scratch size)
     int split = mlq::gemm_split(out, in, rows, ds->sm_count);
-    if (mlq::gemm_workspace_bytes(in, rows, out, split) > (size_t)MLQ_NOALLOC_SCRATCH_BYTES) split = 1;
+    while (split > 1 && mlq::gemm_workspace_bytes(in, rows, out, split) > (size_t)MLQ_NOALLOC_SCRATCH_BYTES)
+        --split;
     e = mlq::launch_gemm(fmt, static_cast<const uint8_t*>(w), x, y, out, in, rows, nullptr, s.ptr, split,
                          ds->sm_count, ds->err_flag, stream);
     return e == cudaSuccess ? MLQ_OK : fail_cuda("gemm launch", e);
@@ -324,6 +328,82 @@ mlq_status set_device(int device) {
     e = cudaSetDevice(device);
     return e == cudaSuccess ? MLQ_OK : fail_cuda("cudaSetDevice", e);
 }
+
+// mlq_linear_allgather's checks (shard, peers, epoch), before any CUDA call.
+mlq_status validate_gather(int fmt, const void* w_shard, size_t shard_block_count, int out_features,
+                           int in_features, const float* x, int rows, const mlq_gather& g, const char* who) {
+    if (!known_format(fmt)) return fail(MLQ_ERR_FORMAT, std::string(who) + ": unknown block format");
+    if (in_features <= 0 || out_features <= 0 || rows <= 0)
+        return fail(MLQ_ERR_EMPTY, std::string(who) + ": empty tensors are not supported");
+    if (rows > 64) return fail(MLQ_ERR_RANGE, std::string(who) + ": at most 64 rows of x");
+    if (g.world_size < 1 || g.world_size > mlq::kMaxWorld || g.rank < 0 || g.rank >= g.world_size)
+        return fail(MLQ_ERR_COMM, std::string(who) + ": world_size must be 1..8 and 0 <= rank < world_size");
+    if (g.row_begin < 0 || g.row_end < g.row_begin || g.row_end > out_features)
+        return fail(MLQ_ERR_COMM, std::string(who) + ": row range outside [0, out_features]");
+    if (g.epoch == 0) return fail(MLQ_ERR_COMM, std::string(who) + ": epoch starts at 1");
+    if (!x || !g.peer_y || !g.peer_flags) return fail(MLQ_ERR_NULL, std::string(who) + ": null pointer");
+    for (int r = 0; r < g.world_size; ++r)
+        if (!g.peer_y[r] || !g.peer_flags[r])
+            return fail(MLQ_ERR_NULL, std::string(who) + ": null peer pointer for rank " + std::to_string(r));
+    const int shard_rows = g.row_end - g.row_begin;
+    const size_t expected = (size_t)shard_rows * (size_t)((in_features + mlq::kQK - 1) / mlq::kQK);
+    if (shard_block_count != expected)
+        return fail(MLQ_ERR_BLOCK_COUNT, std::string(who) + ": block count mismatch: expected " +
+                                             std::to_string(expected) + ", got " +
+                                             std::to_string(shard_block_count));
+    if (shard_rows > 0 && !w_shard) return fail(MLQ_ERR_NULL, std::string(who) + ": null weight pointer");
+    static const uint8_t kAligned[16] = {};
+    const void* wcheck = shard_rows > 0 ? w_shard : kAligned;
+    if (!streamable(fmt, wcheck, x, in_features) || reinterpret_cast<uintptr_t>(w_shard) % 16 != 0)
+        return fail(MLQ_ERR_SHAPE, std::string(who) +
+                                       ": needs 16-B aligned weights and x, an even block count per "
+                                       "row (q8_0/q4_0) and in_features % 4 == 0");
+    return MLQ_OK;
+}
+
+// The shard GEMV with the gather fused in (validated arguments).
+mlq_status run_gather(int fmt, const void* w_shard, int out_features, int in_features, const float* x,
+                      int rows, const float* bias, const mlq_gather& mg, cudaStream_t stream) {
+    Gather g;
+    g.world = mg.world_size;
+    g.rank = mg.rank;
+    g.row_offset = mg.row_begin;
+    g.y_stride = out_features;
+    g.ys = mg.peer_y;
+    g.flags = mg.peer_flags;
+    g.epoch = mg.epoch;
+    Epilogue ep;
+    ep.bias = bias;
+    return run_stream(fmt, w_shard, mg.row_end - mg.row_begin, in_features, x, rows, g, stream, ep);
+}
+
+// One op of a batch: validation (no CUDA call) ...
+mlq_status validate_op(const mlq_linear_op& op, int i, bool host) {
+    const std::string who = std::string(host ? "mlq_linear_batch_host" : "mlq_linear_batch") + " op " +
+                            std::to_string(i);
+    if (op.gather) {
+        if (op.w_up) return fail(MLQ_ERR_RANGE, who + ": a gathered op takes no up projection");
+        if (host && !op.y) return fail(MLQ_ERR_NULL, who + ": null host y");
+        return validate_gather(op.fmt, op.w, op.block_count, op.out_features, op.in_features, op.x, op.rows,
+                               *op.gather, who.c_str());
+    }
+    mlq_status st = validate_linear(op.fmt, op.w, op.block_count, op.out_features, op.in_features, op.x,
+                                    op.rows, op.y, who.c_str());
+    if (st != MLQ_OK) return st;
+    if (op.w_up && op.bias) return fail(MLQ_ERR_RANGE, who + ": a SwiGLU pair takes no bias");
+    return MLQ_OK;
+}
+
+// ... and its launch (x, y: device pointers).
+mlq_status run_op(const mlq_linear_op& op, const float* x, float* y, cudaStream_t stream) {
+    if (op.gather)
+        return run_gather(op.fmt, op.w, op.out_features, op.in_features, x, op.rows, op.bias, *op.gather, stream);
+    Epilogue ep;
+    ep.w2 = op.w_up;
+    ep.bias = op.bias;
+    return run_linear(op.fmt, op.w, op.out_features, op.in_features, x, op.rows, y, stream, ep);
+}
+
 
 }  // namespace
 
@@ -370,6 +450,9 @@ MLQ_API mlq_status mlq_device_error(int device, int* code) {
             int v = 0;
             if (e == cudaSuccess) e = cudaMemcpy(&v, ds->err_flag, sizeof(int), cudaMemcpyDeviceToHost);
             if (e == cudaSuccess) e = cudaMemset(ds->err_flag, 0, sizeof(int));
+            // a launch that gave up may have left its tile-queue pair counted
+            // but not reset: start every queue from zero again
+            if (e == cudaSuccess && v != 0) e = mlq::reset_tile_queues();
             if (e == cudaSuccess) e = cudaDeviceSynchronize();
             if (e != cudaSuccess) st = fail_cuda("mlq_device_error", e);
             *code = v;
@@ -402,8 +485,11 @@ MLQ_API mlq_status mlq_linear_noalloc(mlq_format fmt, const void* w, size_t bloc
         mlq_status st = validate_linear(fmt, w, block_count, out_features, in_features, x, rows, y,
                                         "mlq_linear_noalloc");
         if (st != MLQ_OK) return st;
+        // only a call that takes the tensor-core GEMM uses the scratch (the
+        // same routing test as mlq_linear: rows rule, alignment, in % 8)
         const size_t need = mlq::gemm_workspace_bytes(in_features, rows, out_features, 1);
-        if (MLQ_GEMM_ROWS_RULE(rows, out_features, in_features) && need > (size_t)MLQ_NOALLOC_SCRATCH_BYTES)
+        if (mlq::gemm_shape_ok(fmt, w, out_features, in_features, rows) &&
+            need > (size_t)MLQ_NOALLOC_SCRATCH_BYTES)
             return fail(MLQ_ERR_RANGE,
                         "mlq_linear_noalloc: rows * in_features * 4 = " + std::to_string(need) +
                             " bytes of x split exceed the " +
@@ -556,46 +642,86 @@ MLQ_API mlq_status mlq_linear_allgather(mlq_format fmt, const void* w_shard,
                                         uint32_t* const* peer_flags, int world_size, int rank,
                                         uint32_t epoch, mlq_stream stream) {
     try {
-        const char* who = "mlq_linear_allgather";
-        if (!known_format(fmt)) return fail(MLQ_ERR_FORMAT, std::string(who) + ": unknown block format");
-        if (in_features <= 0 || out_features <= 0 || rows <= 0)
-            return fail(MLQ_ERR_EMPTY, std::string(who) + ": empty tensors are not supported");
-        if (rows > 64) return fail(MLQ_ERR_RANGE, std::string(who) + ": at most 64 rows of x");
-        if (world_size < 1 || world_size > mlq::kMaxWorld || rank < 0 || rank >= world_size)
-            return fail(MLQ_ERR_COMM, std::string(who) + ": world_size must be 1..8 and 0 <= rank < world_size");
-        if (row_begin < 0 || row_end < row_begin || row_end > out_features)
-            return fail(MLQ_ERR_COMM, std::string(who) + ": row range outside [0, out_features]");
-        if (epoch == 0) return fail(MLQ_ERR_COMM, std::string(who) + ": epoch starts at 1");
-        if (!x || !peer_y || !peer_flags) return fail(MLQ_ERR_NULL, std::string(who) + ": null pointer");
-        for (int r = 0; r < world_size; ++r)
-            if (!peer_y[r] || !peer_flags[r])
-                return fail(MLQ_ERR_NULL, std::string(who) + ": null peer pointer for rank " + std::to_string(r));
-        const int shard_rows = row_end - row_begin;
-        const size_t expected = (size_t)shard_rows * (size_t)((in_features + mlq::kQK - 1) / mlq::kQK);
-        if (shard_block_count != expected)
-            return fail(MLQ_ERR_BLOCK_COUNT, std::string(who) + ": block count mismatch: expected " +
-                                                 std::to_string(expected) + ", got " +
-                                                 std::to_string(shard_block_count));
-        if (shard_rows > 0 && !w_shard) return fail(MLQ_ERR_NULL, std::string(who) + ": null weight pointer");
-        static const uint8_t kAligned[16] = {};
-        const void* wcheck = shard_rows > 0 ? w_shard : kAligned;
-        if (!streamable(fmt, wcheck, x, in_features) ||
-            reinterpret_cast<uintptr_t>(w_shard) % 16 != 0)
-            return fail(MLQ_ERR_SHAPE, std::string(who) +
-                                           ": needs 16-B aligned weights and x, an even block count per "
-                                           "row (q8_0/q4_0) and in_features % 4 == 0");
-        Gather g;
-        g.world = world_size;
-        g.rank = rank;
-        g.row_offset = row_begin;
-        g.y_stride = out_features;
-        g.ys = peer_y;
-        g.flags = peer_flags;
-        g.epoch = epoch;
-        return run_stream(fmt, w_shard, shard_rows, in_features, x, rows, g,
+        mlq_gather g{world_size, rank, row_begin, row_end, peer_y, peer_flags, epoch};
+        mlq_status st = validate_gather(fmt, w_shard, shard_block_count, out_features, in_features, x, rows, g,
+                                        "mlq_linear_allgather");
+        if (st != MLQ_OK) return st;
+        return run_gather(fmt, w_shard, out_features, in_features, x, rows, nullptr, g,
                           reinterpret_cast<cudaStream_t>(stream));
     } catch (...) {
         return fail(MLQ_ERR_CUDA, "mlq_linear_allgather: host exception");
+    }
+}
+
+MLQ_API mlq_status mlq_linear_batch(const mlq_linear_op* ops, int n, mlq_stream stream) {
+    try {
+        if (n < 0) return fail(MLQ_ERR_EMPTY, "mlq_linear_batch: negative op count");
+        if (n > 0 && !ops) return fail(MLQ_ERR_NULL, "mlq_linear_batch: null op list");
+        for (int i = 0; i < n; ++i) {
+            mlq_status st = validate_op(ops[i], i, false);
+            if (st != MLQ_OK) return st;
+        }
+        cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+        for (int i = 0; i < n; ++i) {
+            mlq_status st = run_op(ops[i], ops[i].x, ops[i].y, s);
+            if (st != MLQ_OK) return st;
+        }
+        return MLQ_OK;
+    } catch (...) {
+        return fail(MLQ_ERR_CUDA, "mlq_linear_batch: host exception");
+    }
+}
+
+MLQ_API mlq_status mlq_linear_batch_host(const mlq_linear_op* ops, int n, int device, mlq_stream stream) {
+    try {
+        if (n < 0) return fail(MLQ_ERR_EMPTY, "mlq_linear_batch_host: negative op count");
+        if (n > 0 && !ops) return fail(MLQ_ERR_NULL, "mlq_linear_batch_host: null op list");
+        for (int i = 0; i < n; ++i) {
+            mlq_status st = validate_op(ops[i], i, true);
+            if (st != MLQ_OK) return st;
+        }
+        if (n == 0) return MLQ_OK;
+        mlq_status st = set_device(device);
+        if (st != MLQ_OK) return st;
+        DeviceState* ds = device_state(device, &st);
+        if (!ds) return st;
+        cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+        std::lock_guard<std::mutex> lock(ds->host_mu);
+        // every op's x and y in one staging buffer each, 256-B aligned slices
+        std::vector<size_t> xo(n), yo(n);
+        size_t xt = 0, yt = 0;
+        for (int i = 0; i < n; ++i) {
+            xo[i] = xt;
+            yo[i] = yt;
+            xt += ((size_t)ops[i].rows * ops[i].in_features * sizeof(float) + 255) & ~(size_t)255;
+            if (!ops[i].gather) yt += ((size_t)ops[i].rows * ops[i].out_features * sizeof(float) + 255) & ~(size_t)255;
+        }
+        if ((st = ensure(&ds->x_stage, &ds->x_cap, xt)) != MLQ_OK) return st;
+        if (yt > 0 && (st = ensure(&ds->y_stage, &ds->y_cap, yt)) != MLQ_OK) return st;
+        char* xs = reinterpret_cast<char*>(ds->x_stage);
+        char* ys = reinterpret_cast<char*>(ds->y_stage);
+        cudaError_t e = cudaSuccess;
+        for (int i = 0; i < n && e == cudaSuccess; ++i)
+            e = cudaMemcpyAsync(xs + xo[i], ops[i].x, (size_t)ops[i].rows * ops[i].in_features * sizeof(float),
+                                cudaMemcpyHostToDevice, s);
+        if (e != cudaSuccess) return fail_cuda("cudaMemcpyAsync (x upload)", e);
+        for (int i = 0; i < n; ++i) {
+            st = run_op(ops[i], reinterpret_cast<const float*>(xs + xo[i]), reinterpret_cast<float*>(ys + yo[i]), s);
+            if (st != MLQ_OK) return st;
+        }
+        for (int i = 0; i < n && e == cudaSuccess; ++i) {
+            // a gathered op's full y is this rank's peer_y entry
+            const void* src = ops[i].gather ? static_cast<const void*>(ops[i].gather->peer_y[ops[i].gather->rank])
+                                            : static_cast<const void*>(ys + yo[i]);
+            e = cudaMemcpyAsync(ops[i].y, src, (size_t)ops[i].rows * ops[i].out_features * sizeof(float),
+                                cudaMemcpyDeviceToHost, s);
+        }
+        if (e != cudaSuccess) return fail_cuda("cudaMemcpyAsync (y download)", e);
+        e = cudaStreamSynchronize(s);
+        if (e != cudaSuccess) return fail_cuda("cudaStreamSynchronize", e);
+        return MLQ_OK;
+    } catch (...) {
+        return fail(MLQ_ERR_CUDA, "mlq_linear_batch_host: host exception");
     }
 }
 

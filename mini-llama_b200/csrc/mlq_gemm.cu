@@ -528,10 +528,14 @@ cudaError_t launch_gemm_f(const uint8_t* w, const float* x, float* y, int out, i
 
 }  // namespace
 
-bool gemm_supported(int fmt, const void* w, int out, int in, int rows) {
+bool gemm_shape_ok(int fmt, const void* w, int out, int in, int rows) {
     const long long row_bytes = (long long)((in + kQK - 1) / kQK) * block_bytes(fmt);
     return MLQ_GEMM_ROWS_RULE(rows, out, in) && reinterpret_cast<uintptr_t>(w) % 16 == 0 && row_bytes % 16 == 0 &&
-           in % 8 == 0 && encode_fn() != nullptr;
+           in % 8 == 0;
+}
+
+bool gemm_supported(int fmt, const void* w, int out, int in, int rows) {
+    return gemm_shape_ok(fmt, w, out, in, rows) && encode_fn() != nullptr;
 }
 
 int gemm_split(int out, int in, int rows, int sm_count) {

@@ -55,6 +55,8 @@
 
 #include <atomic>
 #include <cstring>
+#include <map>
+#include <mutex>
 
 #include "mlq_device.cuh"
 #include "mlq_kernels.h"
@@ -62,11 +64,19 @@
 
 namespace mlq {
 
-// Dynamic row-tile queues: one {next tile, finished CTAs} pair per launch,
-// taken round-robin from this ring (zero at module load; the last CTA of a
-// launch puts its pair back to zero).  A slot is reused only after 255 other
-// launches on the device, far more than can run at once.
-constexpr int kTileSlots = 256;
+// Dynamic row-tile queues: one {next tile, finished CTAs} pair per launch.
+// Each CUDA stream that launches a queued GEMV gets a ring of its own
+// (kStreamRings rings per device; streams beyond that use static row ranges),
+// and its launches take the ring's slots round-robin.  Launches on one stream
+// overlap at most pairwise (programmatic dependent launch), so a slot is free
+// again long before its ring comes back to it, whatever other streams do.
+// Every CTA of a launch counts itself in the pair's second word when its
+// producer is done with the queue -- on the normal path and after an abort --
+// and the last one puts the pair back to zero (it is zero at module load, and
+// mlq_device_error clears the whole array after a kernel reported an error).
+constexpr int kStreamRings = 64;
+constexpr int kSlotsPerRing = 32;
+constexpr int kTileSlots = kStreamRings * kSlotsPerRing;
 __device__ unsigned int g_gemv_tile_slots[2 * kTileSlots];
 
 namespace {
@@ -266,6 +276,20 @@ __device__ __forceinline__ void int_piece_store(const float v[16], int i, int la
 }
 
 constexpr int log2_of(int n) { return n <= 1 ? 0 : 1 + log2_of(n / 2); }
+
+// A CTA's producer is done taking tiles from the launch's queue {next, done}:
+// count it; the last CTA of the grid puts the pair back to zero.
+__device__ __forceinline__ void release_tile_queue(unsigned int* tiles) {
+    __threadfence();
+    if (atomicAdd(tiles + 1, 1u) == gridDim.x - 1) {
+        atomicExch(tiles, 0u);
+        atomicExch(tiles + 1, 0u);
+    }
+}
+
+// Sharded-call completion counter: CTAs that gave up add this bit with their
+// count, so the launch's last CTA knows not to publish the epoch.
+constexpr unsigned int kDonePoison = 1u << 16;
 
 // What a launch does after the sums: store y (+ bias, when the call has one:
 // a runtime check, so plain and bias calls share one kernel), or -- a
@@ -491,14 +515,7 @@ __global__ void __launch_bounds__(threads_for(MT), MINB)
             if (lane == 0) stage_row[s] = -1;
             __syncwarp();
             mbar_arrive(smem_u32(&full_bar[s]));
-            // the last CTA to finish puts the queue back to zero for a later launch
-            if (lane == 0) {
-                __threadfence();
-                if (atomicAdd(a.tiles + 1, 1u) == gridDim.x - 1) {
-                    atomicExch(a.tiles, 0u);
-                    atomicExch(a.tiles + 1, 0u);
-                }
-            }
+            if (lane == 0) release_tile_queue(a.tiles);
         }
         return;
     producer_drain:
@@ -511,21 +528,10 @@ __global__ void __launch_bounds__(threads_for(MT), MINB)
                 break;
             }
         }
+        // an aborting CTA is done with the queue too: it still counts, so the
+        // launch's last CTA resets the slot for the next launch that takes it
+        if (dyn && lane == 0) release_tile_queue(a.tiles);
         return;
-    }
-
-    // Bias of the first tile's row that this thread stores, loaded before any
-    // wait: like the weights it is read-only, so it need not wait for the
-    // previous kernel (one-token stores: the reduce-scatter's row of this
-    // lane; tile stores: row c % TR of thread c).  Later tiles load theirs
-    // when they start.
-    float bias_first = 0.f;
-    if (has_bias) {
-        if (!dyn && warp >= 1 && warp <= kConsumerWarps) {
-            const int i = (MT == 1 && a.ny == 1) ? (warp - 1) + (lane >> (5 - log2_of(RPW))) * kConsumerWarps
-                                                 : (int)(threadIdx.x - 32) % TR;
-            if (i < min(TR, nrows_cta)) bias_first = __ldg(a.bias + a.row_offset + r_begin + i);
-        }
     }
 
     if (INT && xres) {
@@ -629,6 +635,17 @@ __global__ void __launch_bounds__(threads_for(MT), MINB)
     // -------------------------------- consumers --------------------------------
     // y (and the peers' y) may still be read by the previous kernel
     grid_dependency_wait();
+    // Bias of the first tile's row that this thread stores (one-token stores:
+    // the reduce-scatter's row of this lane; tile stores: row c % TR of
+    // thread c), loaded after the wait above, so a bias written by the
+    // previous kernel in the stream is seen complete.  Later tiles load
+    // theirs when they start.
+    float bias_first = 0.f;
+    if (has_bias && !dyn) {
+        const int i = (MT == 1 && a.ny == 1) ? (warp - 1) + (lane >> (5 - log2_of(RPW))) * kConsumerWarps
+                                             : (int)(threadIdx.x - 32) % TR;
+        if (i < min(TR, nrows_cta)) bias_first = __ldg(a.bias + a.row_offset + r_begin + i);
+    }
     if (INT && xres && !mbar_wait(smem_u32(&xready_bar), 0u)) {
         report_error(a.err, 7);
         abort_flag = 1;
@@ -639,6 +656,9 @@ __global__ void __launch_bounds__(threads_for(MT), MINB)
     uint32_t xoff[8];
 #pragma unroll
     for (int p = 0; p < 8; ++p) xoff[p] = INT ? xcol<C::G>(lane, p & (2 * C::G - 1)) : (uint32_t)((lane ^ p) * 16);
+    // The consumer loop; returns the tiles this warp processed, or -1 when it
+    // gave up (a bounded wait ran out here or in another warp of the CTA).
+    auto consume = [&]() -> int {
     int s = 0;
     uint32_t ph = 0;
     int t = 0;  // after the loop: the tiles this CTA processed
@@ -650,7 +670,7 @@ __global__ void __launch_bounds__(threads_for(MT), MINB)
                 report_error(a.err, 1);
                 abort_flag = 1;
             }
-            if (*(volatile int*)&abort_flag) return;
+            if (*(volatile int*)&abort_flag) return -1;
             const int r0 = *(volatile int*)&stage_row[s];
             if (r0 < 0) break;
             row0 = r0;
@@ -698,7 +718,7 @@ __global__ void __launch_bounds__(threads_for(MT), MINB)
                 report_error(a.err, 1);
                 abort_flag = 1;
             }
-            if (*(volatile int*)&abort_flag) return;
+            if (*(volatile int*)&abort_flag) return -1;
             const uint32_t stage = smem_base + (uint32_t)s * C::W_BYTES;
             const int xslot = xres ? kt : s;
             const uint32_t xs = x_base + (uint32_t)xslot * C::XT_BYTES;
@@ -728,7 +748,7 @@ __global__ void __launch_bounds__(threads_for(MT), MINB)
                 report_error(a.err, 1);
                 abort_flag = 1;
             }
-            if (*(volatile int*)&abort_flag) return;
+            if (*(volatile int*)&abort_flag) return -1;
 
             if constexpr (INT) {
 #pragma unroll
@@ -892,7 +912,8 @@ __global__ void __launch_bounds__(threads_for(MT), MINB)
         if (lane == 0) mbar_arrive(smem_u32(&tile_bar));
         if (!mbar_wait(smem_u32(&tile_bar), (uint32_t)t & 1u)) {
             report_error(a.err, 5);
-            return;
+            abort_flag = 1;
+            return -1;
         }
         {
             const int c = threadIdx.x - 32;  // 0 .. 255
@@ -909,36 +930,50 @@ __global__ void __launch_bounds__(threads_for(MT), MINB)
             }
         }
     }
+    return t;
+    };
+    const int done_tiles = consume();
 
     if (a.world > 1) {
         // Sharded call: this CTA's rows are in every rank's y.  The last CTA
         // of this rank to finish publishes the epoch to every peer, then
-        // waits (bounded) until every rank's slice has landed here.
-        __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&tile_bar));
+        // waits (bounded) until every rank's slice has landed here.  Every
+        // CTA counts itself exactly once, also after giving up (then with
+        // kDonePoison), so the counter is back at zero for the next call and
+        // a launch with a failed CTA never publishes its epoch: the peers'
+        // waits then run out and report code 4 instead of reading a y with
+        // missing rows.
+        bool ok = done_tiles >= 0;
+        if (ok) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&tile_bar));
+        }
         if (threadIdx.x == 32) {
-            if (!mbar_wait(smem_u32(&tile_bar), (uint32_t)t & 1u)) {
+            if (ok && !mbar_wait(smem_u32(&tile_bar), (uint32_t)done_tiles & 1u)) {
                 report_error(a.err, 5);
-                return;
+                ok = false;
             }
+            if (*(volatile int*)&abort_flag) ok = false;
             // Ordering without system-wide fences per CTA: this CTA's y stores
             // (local and peer) happen before this point (tile_bar, CTA scope);
             // the GPU-scope acquire-release count carries them to the last CTA,
             // whose one system-scope release fence then publishes every CTA's
             // stores ahead of the epoch flags (the fence is cumulative).
-            const unsigned int prev = atom_add_acq_rel_gpu(a.done_counter, 1u);
-            if (prev == gridDim.x - 1) {
+            const unsigned int prev = atom_add_acq_rel_gpu(a.done_counter, ok ? 1u : 1u + kDonePoison);
+            if ((prev & (kDonePoison - 1u)) == gridDim.x - 1) {
                 *a.done_counter = 0u;  // every CTA of this launch has counted
-                fence_acq_rel_sys();
-                for (int r = 0; r < a.world; ++r) st_relaxed_sys(a.peer_flags[r] + a.rank, a.epoch);
-                const uint64_t t0 = global_ns();
-                for (int r = 0; r < a.world; ++r) {
-                    while ((int)(ld_acquire_sys(a.local_flags + r) - a.epoch) < 0) {
-                        if (global_ns() - t0 > kWaitLimitNs) {
-                            report_error(a.err, 4);
-                            return;
+                if (ok && prev < kDonePoison) {
+                    fence_acq_rel_sys();
+                    for (int r = 0; r < a.world; ++r) st_relaxed_sys(a.peer_flags[r] + a.rank, a.epoch);
+                    const uint64_t t0 = global_ns();
+                    for (int r = 0; r < a.world; ++r) {
+                        while ((int)(ld_acquire_sys(a.local_flags + r) - a.epoch) < 0) {
+                            if (global_ns() - t0 > kWaitLimitNs) {
+                                report_error(a.err, 4);
+                                return;
+                            }
+                            __nanosleep(64);
                         }
-                        __nanosleep(64);
                     }
                 }
             }
@@ -1016,10 +1051,30 @@ unsigned int* tile_slots(int dev) {
     return p;
 }
 
+// The ring of `stream` on device `dev`: rings are handed to streams in the
+// order they first launch a queued GEMV; -1 once all kStreamRings are taken
+// (that stream's launches then use static row ranges).
+struct StreamRings {
+    std::mutex mu;
+    std::map<cudaStream_t, int> ring;
+    std::atomic<unsigned int> seq[kStreamRings];
+};
+
+int stream_ring(StreamRings& sr, cudaStream_t stream) {
+    std::lock_guard<std::mutex> lock(sr.mu);
+    auto it = sr.ring.find(stream);
+    if (it != sr.ring.end()) return it->second;
+    if ((int)sr.ring.size() >= kStreamRings) return -1;
+    const int r = (int)sr.ring.size();
+    sr.ring.emplace(stream, r);
+    return r;
+}
+
 // A queue for one launch on `stream`, or null (static row ranges) when the
-// stream is being captured: a graph would replay the same slot forever.
+// stream is being captured (a graph would replay the same slot) or has no
+// ring.
 unsigned int* tile_queue(int dev, cudaStream_t stream) {
-    static std::atomic<unsigned int> seq[64];
+    static StreamRings rings[64];
     if (dev < 0 || dev >= 64) return nullptr;
     cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
     if (cudaStreamIsCapturing(stream, &cs) != cudaSuccess) {
@@ -1029,7 +1084,10 @@ unsigned int* tile_queue(int dev, cudaStream_t stream) {
     if (cs != cudaStreamCaptureStatusNone) return nullptr;
     unsigned int* base = tile_slots(dev);
     if (!base) return nullptr;
-    return base + 2u * (seq[dev].fetch_add(1u, std::memory_order_relaxed) % kTileSlots);
+    const int r = stream_ring(rings[dev], stream);
+    if (r < 0) return nullptr;
+    const unsigned int slot = rings[dev].seq[r].fetch_add(1u, std::memory_order_relaxed) % kSlotsPerRing;
+    return base + 2u * ((unsigned int)r * kSlotsPerRing + slot);
 }
 
 // MINB: CTAs per SM the kernel's registers and shared memory are sized for;
@@ -1186,6 +1244,17 @@ cudaError_t launch_gemv_generic(int fmt, const uint8_t* w, const float* x, float
         default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();
+}
+
+// Puts every tile-queue pair of the current device back to zero (after a
+// kernel gave up mid-launch; the caller has synchronised the device).
+cudaError_t reset_tile_queues() {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    unsigned int* base = tile_slots(dev);
+    if (!base) return cudaErrorInvalidSymbol;
+    return cudaMemset(base, 0, sizeof(unsigned int) * 2 * kTileSlots);
 }
 
 }  // namespace mlq

@@ -49,6 +49,10 @@ int gemv_tokens_per_pass(int rows_left);
 cudaError_t launch_gemv_stream(int fmt, const GemvArgs& args, int mt, int sm_count,
                                int smem_per_sm, cudaStream_t stream);
 
+// Zeroes the streaming GEMV's dynamic tile-queue ring of the current device
+// (called after a kernel reported an error, the device synchronised).
+cudaError_t reset_tile_queues();
+
 // Any-alignment fallback GEMV (one warp per output row).
 cudaError_t launch_gemv_generic(int fmt, const uint8_t* w, const float* x, float* y, int out,
                                 int in, int M, int bpr, cudaStream_t stream);
@@ -69,7 +73,9 @@ struct GemmArgs {
 };
 
 // True when the tcgen05 GEMM takes this call: MLQ_GEMM_ROWS_RULE(rows, out, in), weights 16-B
-// aligned with a 16-B multiple row pitch, in % 8 == 0.
+// aligned with a 16-B multiple row pitch, in % 8 == 0 (gemm_shape_ok, host values only), and
+// the driver's tensor-map encoder is reachable.
+bool gemm_shape_ok(int fmt, const void* w, int out, int in, int rows);
 bool gemm_supported(int fmt, const void* w, int out, int in, int rows);
 
 // Split-K ranges for a GEMM call on `sm_count` SMs: 1 when its output

@@ -34,6 +34,21 @@ class MLQError(RuntimeError):
 
 _lib = None
 _vp = ctypes.c_void_p
+
+
+class Gather(ctypes.Structure):
+    """struct mlq_gather (include/mlq.h): the shard and gather of one op."""
+    _fields_ = [("world_size", ctypes.c_int), ("rank", ctypes.c_int), ("row_begin", ctypes.c_int),
+                ("row_end", ctypes.c_int), ("peer_y", ctypes.c_void_p), ("peer_flags", ctypes.c_void_p),
+                ("epoch", ctypes.c_uint32)]
+
+
+class LinearOp(ctypes.Structure):
+    """struct mlq_linear_op (include/mlq.h): one product of a batch."""
+    _fields_ = [("fmt", ctypes.c_int), ("out_features", ctypes.c_int), ("in_features", ctypes.c_int),
+                ("rows", ctypes.c_int), ("w", ctypes.c_void_p), ("w_up", ctypes.c_void_p),
+                ("block_count", ctypes.c_size_t), ("x", ctypes.c_void_p), ("bias", ctypes.c_void_p),
+                ("y", ctypes.c_void_p), ("gather", ctypes.c_void_p)]
 _i = ctypes.c_int
 _sz = ctypes.c_size_t
 
@@ -65,6 +80,8 @@ def lib() -> ctypes.CDLL:
         L.mlq_flag_bytes.restype = _sz
         L.mlq_linear_allgather.argtypes = [_i, _vp, _sz, _i, _i, _i, _i, _vp, _i, _vp, _vp, _i, _i,
                                            ctypes.c_uint32, _vp]
+        L.mlq_linear_batch.argtypes = [ctypes.POINTER(LinearOp), _i, _vp]
+        L.mlq_linear_batch_host.argtypes = [ctypes.POINTER(LinearOp), _i, _i, _vp]
         L.mlq_peer_alloc.argtypes = [_sz, ctypes.POINTER(_vp), ctypes.c_char_p]
         L.mlq_peer_open.argtypes = [ctypes.c_char_p, ctypes.POINTER(_vp)]
         L.mlq_peer_close.argtypes = [_vp]
@@ -73,7 +90,7 @@ def lib() -> ctypes.CDLL:
                      "mlq_linear_host",
                      "mlq_linear_host_weight", "mlq_dequantize", "mlq_quantize", "mlq_device_error",
                      "mlq_linear_allgather", "mlq_peer_alloc", "mlq_peer_open", "mlq_peer_close",
-                     "mlq_peer_free"):
+                     "mlq_peer_free", "mlq_linear_batch", "mlq_linear_batch_host"):
             getattr(L, name).restype = _i
         _lib = L
     return _lib
@@ -312,3 +329,40 @@ def _fmt_name(fmt) -> str:
     if isinstance(fmt, str):
         return fmt
     return {v: k for k, v in FORMATS.items()}[int(fmt)]
+
+
+# ---------------------------------------------------------------------------
+# batches (mlq_linear_batch / mlq_linear_batch_host)
+# ---------------------------------------------------------------------------
+def linear_op(fmt, w_ptr: int, out_features: int, in_features: int, x_ptr: int, rows: int, y_ptr: int,
+              w_up_ptr: int | None = None, bias_ptr: int | None = None, gather=None) -> LinearOp:
+    """One op of a batch; pointers are device (or host, for run_host) addresses."""
+    return LinearOp(fmt_id(fmt), out_features, in_features, rows, w_ptr, w_up_ptr,
+                    blocks_per_row(in_features) * (out_features if gather is None
+                                                   else gather.row_end - gather.row_begin),
+                    x_ptr, bias_ptr, y_ptr, None if gather is None else ctypes.addressof(gather))
+
+
+def make_gather(world: int, rank: int, row_begin: int, row_end: int, peer_y_ptrs, peer_flag_ptrs,
+                epoch: int = 1):
+    """A Gather struct plus the pointer arrays it references (keep both alive)."""
+    ys = (ctypes.c_void_p * world)(*peer_y_ptrs)
+    fs = (ctypes.c_void_p * world)(*peer_flag_ptrs)
+    g = Gather(world, rank, row_begin, row_end, ctypes.addressof(ys), ctypes.addressof(fs), epoch)
+    g._keep = (ys, fs)
+    return g
+
+
+class Batch:
+    """A fixed list of ops, launched with one C call per run."""
+
+    def __init__(self, ops):
+        self.n = len(ops)
+        self.arr = (LinearOp * max(1, self.n))(*ops)
+
+    def run(self, stream) -> None:
+        check(lib().mlq_linear_batch(self.arr, self.n, _stream_handle(stream)))
+
+    def run_host(self, device: int = 0, stream=None) -> None:
+        check(lib().mlq_linear_batch_host(self.arr, self.n, device,
+                                          None if stream is None else _stream_handle(stream)))

@@ -12,7 +12,12 @@ Host-side pieces:
   * PeerGroup: per-rank IPC buffers exchanged through torch.distributed
     (plain CUDA IPC mappings, no multicast objects) -- y buffers (two, used
     alternately by consecutive calls) and the 256-byte flag buffer;
-  * ShardedLinear: one matrix's shard plus its call state (epoch counter).
+  * ShardedLinear: one matrix's shard plus its call state (epoch counter);
+  * StepPlan: placement of a decode step's matrices (sharded / rank 0) and
+    the epoch and y-buffer bookkeeping of their calls, for batches
+    (mlq_linear_batch) that launch a whole step at once;
+  * GatherSlab: the sharded matrices' y buffers of a step in two IPC
+    allocations (one per y parity).
 """
 from __future__ import annotations
 
@@ -134,3 +139,83 @@ def device_view(ptr: int, shape, dtype="float32"):
     import torch
     typestr = {"float32": "<f4", "int32": "<i4", "uint8": "|u1"}[dtype]
     return torch.as_tensor(_CudaArray(ptr, shape, typestr), device="cuda")
+
+
+class StepPlan:
+    """Placement and call bookkeeping of one decode step's matrices.
+
+    matrices: [(name, out_features, in_features)] in call order.  At world 1
+    every matrix runs locally.  At world > 1 a matrix named in `shard` is
+    row-sharded across every rank (fused gather); any other runs on rank 0
+    alone ("local0"), as north_star places small matrices on one GPU.
+
+    Sharded calls share one flag buffer per rank, so their epochs form one
+    sequence: every sharded call takes the next epoch, in the same order on
+    every rank.  Each sharded matrix alternates between two y buffers
+    (parity = how many times it was called, mod 2), so a rank that runs
+    ahead never writes a y that a slower peer may still be reading.
+    """
+
+    def __init__(self, matrices, world: int, rank: int, shard=()):
+        self.matrices = list(matrices)
+        self.world, self.rank = world, rank
+        self.place, self.ranges = {}, {}
+        for name, out_f, _ in self.matrices:
+            if world == 1:
+                self.place[name] = "local"
+                self.ranges[name] = [(0, out_f)]
+            elif name in shard:
+                self.place[name] = "shard"
+                self.ranges[name] = shard_rows(out_f, world)
+            else:
+                self.place[name] = "local0"
+                self.ranges[name] = shard_rows(out_f, world, owners=[0])
+        self.sharded = [n for n, _, _ in self.matrices if self.place[n] == "shard"]
+        self.epoch = 0
+        self.calls = {n: 0 for n in self.sharded}
+
+    def rows(self, name):
+        """This rank's (row_begin, row_end) of the matrix."""
+        rg = self.ranges[name]
+        return rg[self.rank] if self.world > 1 else rg[0]
+
+    def active(self, name) -> bool:
+        """Whether this rank makes a call for the matrix (sharded: every rank,
+        also one that owns no rows; local0: rank 0 only)."""
+        return self.place[name] in ("local", "shard") or self.rank == 0
+
+    def next_call(self, name):
+        """(epoch, y parity) of the matrix's next sharded call."""
+        self.epoch += 1
+        parity = self.calls[name] & 1
+        self.calls[name] += 1
+        return self.epoch, parity
+
+    def next_step(self):
+        """(y parity, [epoch per sharded matrix in call order]) of a whole step;
+        every sharded matrix must have been called equally often so far."""
+        counts = {self.calls[n] for n in self.sharded}
+        if len(counts) > 1:
+            raise RuntimeError("sharded matrices were called unequally often; a step needs one parity")
+        out = [self.next_call(n) for n in self.sharded]
+        return (out[0][1] if out else 0), [e for e, _ in out]
+
+
+class GatherSlab:
+    """The y buffers of every sharded matrix of a step, for both parities: two
+    IPC allocations (one per parity) sliced per matrix, 256-B aligned."""
+
+    def __init__(self, group: PeerGroup, nbytes_per_matrix):
+        self.offsets, off = [], 0
+        for nb in nbytes_per_matrix:
+            self.offsets.append(off)
+            off += (nb + 255) // 256 * 256
+        self.total = max(off, 256)
+        self.bufs = [group.alloc(self.total), group.alloc(self.total)]
+
+    def peer_ptrs(self, parity: int, k: int):
+        """Every rank's y of matrix k (parity buffer), mapped here."""
+        return [p + self.offsets[k] for p in self.bufs[parity].peers]
+
+    def local_ptr(self, parity: int, k: int) -> int:
+        return self.bufs[parity].local + self.offsets[k]

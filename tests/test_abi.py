@@ -169,10 +169,84 @@ def test_noalloc_range_rule_before_any_cuda_call(pkg):
         nb = mlq.block_count(out_f, in_f)
         return lib.mlq_linear_noalloc(8, 0x1000, nb, out_f, in_f, 0x2000, rows, 0x3000, None)
 
-    in_f = scratch // (4 * 5) + 64  # 5 rows of x exceed the scratch
+    # 5 rows of x exceed the scratch; a multiple of 256 values, so q8_0 rows
+    # have a 16-B multiple pitch (a GEMM condition)
+    in_f = (scratch // (4 * 5) // 256 + 1) * 256
     assert mlq.takes_gemm(9, 32, in_f) and 9 * in_f * 4 > scratch
     assert status(9, 32, in_f) == 9
     assert b"static scratch" in lib.mlq_last_error()
     big_out = -(-mlq.GEMM_LARGE_MIN_WEIGHTS // in_f)  # out * in >= 2^25
     assert mlq.takes_gemm(5, big_out, in_f) and status(5, big_out, in_f) == 9
     assert not mlq.takes_gemm(5, 32, in_f)  # a small matrix at 5 rows streams: no scratch needed
+    # Calls the GEMM cannot take (weights not 16-B aligned, or in % 8 != 0)
+    # stream through the GEMV, which needs no scratch: never MLQ_ERR_RANGE,
+    # whatever the size of x.  These calls pass the host checks and go on to
+    # CUDA, so they run only where there is no GPU to reach (the pointers
+    # are fake); there the first CUDA call fails with MLQ_ERR_CUDA.
+    import torch
+    if torch.cuda.is_available():
+        return
+    nb = mlq.block_count(32, in_f)
+    assert lib.mlq_linear_noalloc(8, 0x1002, nb, 32, in_f, 0x2000, 9, 0x3000, None) != 9
+    odd_in = in_f + 4  # in % 8 == 4
+    assert odd_in % 8 == 4 and mlq.takes_gemm(9, 32, odd_in)
+    assert lib.mlq_linear_noalloc(8, 0x1000, mlq.block_count(32, odd_in), 32, odd_in, 0x2000, 9,
+                                  0x3000, None) != 9
+
+
+def test_batch_structs_match_header(pkg, tmp_path):
+    """The ctypes mirrors of mlq_gather / mlq_linear_op have the header's
+    field offsets and sizes (a gcc-built probe prints them)."""
+    import shutil
+    import subprocess
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        pytest.skip("gcc not found")
+    mlq = pkg.mlq
+    checks = [("mlq_gather", mlq.Gather), ("mlq_linear_op", mlq.LinearOp)]
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "mlq.h"', "int main(void) {"]
+    for cname, cls in checks:
+        lines.append(f'  printf("%zu\\n", sizeof({cname}));')
+        for f, _ in cls._fields_:
+            lines.append(f'  printf("%zu\\n", offsetof({cname}, {f}));')
+    lines.append("  return 0;\n}")
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines) + "\n")
+    exe = tmp_path / "layout"
+    subprocess.run([gcc, "-std=c99", "-I", str(ROOT / "include"), str(src), "-o", str(exe)], check=True)
+    got = [int(v) for v in subprocess.run([str(exe)], check=True, capture_output=True,
+                                          text=True).stdout.split()]
+    want = []
+    for _, cls in checks:
+        want.append(ctypes.sizeof(cls))
+        want += [getattr(cls, f).offset for f, _ in cls._fields_]
+    assert got == want
+
+
+def test_batch_validates_every_op_before_any_cuda_call(pkg):
+    """A batch whose third op is bad launches nothing and names that op; the
+    host form checks the same things (pointers are fake: nothing runs)."""
+    mlq = pkg.mlq
+    lib = mlq.lib()
+    good = mlq.linear_op("q8_0", 0x1000, 4, 32, 0x2000, 1, 0x3000)
+    bad_blocks = mlq.LinearOp(8, 4, 32, 1, 0x1000, None, 3, 0x2000, None, 0x3000, None)
+    pair_bias = mlq.linear_op("q4_0", 0x1000, 4, 32, 0x2000, 1, 0x3000, w_up_ptr=0x1800, bias_ptr=0x4000)
+    for ops, code, text in [([good, good, bad_blocks], 5, b"op 2"),
+                            ([good, pair_bias], 9, b"takes no bias"),
+                            ([mlq.linear_op("q4_1", None, 4, 32, 0x2000, 1, 0x3000)], 2, b"op 0")]:
+        arr = (mlq.LinearOp * len(ops))(*ops)
+        assert lib.mlq_linear_batch(arr, len(ops), None) == code
+        assert text in lib.mlq_last_error()
+        assert lib.mlq_linear_batch_host(arr, len(ops), 0, None) == code
+    assert lib.mlq_linear_batch(None, -1, None) == 3
+    assert lib.mlq_linear_batch(None, 0, None) == 0  # an empty batch is a no-op
+    # a gathered op: mlq_linear_allgather's checks (epoch 0, a pair)
+    g = mlq.make_gather(2, 0, 0, 2, [0x5000, 0x6000], [0x7000, 0x8000], epoch=0)
+    op = mlq.linear_op("q4_0", 0x1000, 4, 32, 0x2000, 1, 0x3000, gather=g)
+    assert op.block_count == 2  # this rank's two rows
+    arr = (mlq.LinearOp * 1)(op)
+    assert lib.mlq_linear_batch(arr, 1, None) == 10
+    g.epoch = 1
+    arr[0].w_up = 0x1800
+    assert lib.mlq_linear_batch(arr, 1, None) == 9
+    assert b"no up projection" in lib.mlq_last_error()

@@ -93,14 +93,16 @@ def test_peer_that_never_signals_times_out(oracle, pkg):
     assert int(f1[0].item()) == 1 and int(f0[0].item()) == 1  # epoch published to both ranks
 
 
-def test_multi_gpu_allgather():
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_multi_gpu_allgather(world):
+    """torchrun worlds of 2, 4 and 8 GPUs (each as far as the box has GPUs):
+    every rank checks the gathered y against the oracle."""
     n = torch.cuda.device_count()
-    if n < 2:
-        pytest.skip("needs 2 GPUs")
-    world = 2 if n < 4 else 4
+    if n < world:
+        pytest.skip(f"needs {world} GPUs")
     cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run",
            "--nnodes=1", f"--nproc-per-node={world}", "--master-addr", "127.0.0.1",
-           "--master-port", "29533", str(ROOT / "tests" / "mp_allgather_worker.py")]
+           "--master-port", str(29533 + world), str(ROOT / "tests" / "mp_allgather_worker.py")]
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     r = subprocess.run(cmd, capture_output=True, text=True, env=env, cwd=str(ROOT))
     print(r.stdout[-3000:], r.stderr[-3000:])

@@ -1,0 +1,126 @@
+"""mlq_linear_batch / mlq_linear_batch_host (include/mlq.h) on the GPU.
+
+A batch launches the same kernels as the single-op entry points, in list
+order on one stream, so every op's output must equal the single call's bit
+for bit; and the oracle (the reference's fp32 sums) within the contract's
+relative L2 1e-3 per output vector.  The host form moves x and y itself
+and synchronises once; its y must equal the device batch's."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from conftest import rel_l2_rows
+
+pytestmark = pytest.mark.gpu
+torch = pytest.importorskip("torch")
+TOL = 1e-3
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def _case(pkg, oracle):
+    """Ops of one decode step: plain (integer-mode GEMV), bias, SwiGLU pair,
+    a 16-row GEMM, a 3-row fp32-mode GEMV and a gathered op in a world of
+    one; the matching single calls' outputs; the oracle's."""
+    mlq = pkg.mlq
+    specs = [("plain", "q4_0", 1000, 3584, 1), ("bias", "q8_0", 512, 1024, 1),
+             ("pair", "q4_1", 700, 2048, 1), ("gemm", "q8_0", 384, 1024, 16),
+             ("fp32", "q4_0", 640, 2048, 3), ("gather", "q4_0", 2048, 1024, 1)]
+    keep, ops, singles, refs, outs = [], [], [], [], []
+    for k, (kind, fmt, out_f, in_f, rows) in enumerate(specs):
+        wb = oracle.quantize(fmt, pkg.synth.normal((out_f, in_f), seed=500 + k, std=0.02))
+        x = pkg.synth.normal((rows, in_f), seed=600 + k)
+        w, xd = dev(wb), dev(x)
+        y = torch.full((rows, out_f), float("nan"), device="cuda")
+        keep += [w, xd, y]
+        if kind == "pair":
+            ub = oracle.quantize(fmt, pkg.synth.normal((out_f, in_f), seed=700 + k, std=0.02))
+            u = dev(ub)
+            keep.append(u)
+            ops.append(mlq.linear_op(fmt, w.data_ptr(), out_f, in_f, xd.data_ptr(), rows, y.data_ptr(),
+                                     w_up_ptr=u.data_ptr()))
+            singles.append(mlq.linear_swiglu(fmt, w, u, out_f, in_f, xd))
+            g = oracle.linear(fmt, x, wb, out_f)
+            refs.append(oracle.swiglu(g, oracle.linear(fmt, x, ub, out_f)))
+        elif kind == "bias":
+            b = pkg.synth.normal((out_f,), seed=800 + k, std=0.5)
+            bd = dev(b)
+            keep.append(bd)
+            ops.append(mlq.linear_op(fmt, w.data_ptr(), out_f, in_f, xd.data_ptr(), rows, y.data_ptr(),
+                                     bias_ptr=bd.data_ptr()))
+            singles.append(mlq.linear_bias(fmt, w, out_f, in_f, xd, bd))
+            refs.append(oracle.linear(fmt, x, wb, out_f) + b[None, :])
+        elif kind == "gather":
+            flags = torch.zeros(mlq.flag_bytes() // 4, dtype=torch.int32, device="cuda")
+            keep.append(flags)
+            g = mlq.make_gather(1, 0, 0, out_f, [y.data_ptr()], [flags.data_ptr()], epoch=1)
+            keep.append(g)
+            ops.append(mlq.linear_op(fmt, w.data_ptr(), out_f, in_f, xd.data_ptr(), rows, y.data_ptr(),
+                                     gather=g))
+            singles.append(mlq.linear(fmt, w, out_f, in_f, xd))
+            refs.append(oracle.linear(fmt, x, wb, out_f))
+        else:
+            ops.append(mlq.linear_op(fmt, w.data_ptr(), out_f, in_f, xd.data_ptr(), rows, y.data_ptr()))
+            singles.append(mlq.linear(fmt, w, out_f, in_f, xd))
+            refs.append(oracle.linear(fmt, x, wb, out_f))
+        outs.append(y)
+    return specs, keep, ops, singles, refs, outs
+
+
+def test_batch_equals_single_calls(pkg, oracle):
+    specs, keep, ops, singles, refs, outs = _case(pkg, oracle)
+    pkg.mlq.Batch(ops).run(None)
+    torch.cuda.synchronize()
+    for (kind, *_), y, one, ref in zip(specs, outs, singles, refs):
+        yn = y.cpu().numpy()
+        np.testing.assert_array_equal(yn, one.cpu().numpy(), err_msg=kind)
+        assert rel_l2_rows(yn, ref).max() <= TOL, kind
+    assert pkg.mlq.device_error(0) == 0
+
+
+def test_batch_host_equals_device_batch(pkg, oracle):
+    """Host x / host y (pinned), one synchronisation per batch, run twice
+    (the second call reuses the staging and, for the gathered op, the next
+    epoch)."""
+    mlq = pkg.mlq
+    specs, keep, ops, singles, refs, outs = _case(pkg, oracle)
+    hx, hy = [], []
+    host_ops = []
+    for op, (kind, fmt, out_f, in_f, rows) in zip(ops, specs):
+        x = torch.empty((rows, in_f), dtype=torch.float32).pin_memory()
+        y = torch.full((rows, out_f), float("nan"), dtype=torch.float32).pin_memory()
+        hx.append(x)
+        hy.append(y)
+        h = mlq.LinearOp.from_buffer_copy(op)
+        h.x, h.y = x.data_ptr(), y.data_ptr()
+        host_ops.append(h)
+    batch = mlq.Batch(host_ops)
+    for it in range(2):
+        for k, (kind, fmt, out_f, in_f, rows) in enumerate(specs):
+            hx[k].copy_(torch.from_numpy(pkg.synth.normal((rows, in_f), seed=900 + 10 * it + k)))
+            hy[k].fill_(float("nan"))
+        if it == 1:
+            keep[[i for i, o in enumerate(keep) if isinstance(o, mlq.Gather)][0]].epoch = 2
+        batch.run_host(0)
+        for k, (kind, fmt, out_f, in_f, rows) in enumerate(specs):
+            # the device batch on the same x gives the same y, bit for bit
+            xd = hx[k].cuda()
+            op = mlq.LinearOp.from_buffer_copy(ops[k])
+            op.x = xd.data_ptr()
+            if kind == "gather":
+                op.gather = None  # compare with a plain call on one GPU
+            yd = torch.empty((rows, out_f), device="cuda")
+            op.y = yd.data_ptr()
+            mlq.Batch([op]).run(None)
+            torch.cuda.synchronize()
+            np.testing.assert_array_equal(hy[k].numpy(), yd.cpu().numpy(), err_msg=f"{kind} call {it}")
+    assert mlq.device_error(0) == 0
