@@ -328,6 +328,8 @@ def launches_of(mlq, rows, out_f, in_f, gemm_ok, pair, sms):
     """Kernel launches of one library call: the GEMM is an x-split launch, the
     GEMM and (split-K) a reduction, per matrix of a pair plus the SwiGLU
     pass; the GEMV one launch per pass of <= 8 rows (pairs stream together)."""
+    if gemm_ok and mlq.takes_bgemm(rows, out_f, in_f):
+        return 7 if pair else 3  # x split, GEMM, fix-up (per matrix of a pair, plus SwiGLU)
     if gemm_ok and mlq.takes_gemm(rows, out_f, in_f):
         per = 2 + (gemm_split(out_f, in_f, rows, sms) > 1)
         return 2 * per + 1 if pair else per
@@ -616,8 +618,10 @@ def _roof(nbytes, launch_ms, b2b_ms, wl, ctx, st, j):
     out_f, in_f = next((o, i) for n, o, i in wl["matrices"] if n == name)
     b, e = st.plan.rows(name)
     local = st.plan.place[name] != "shard"
-    gemm = local and mlq.takes_gemm(wl["rows"], out_f, in_f)
-    kernel = (f"gemm_tc_kernel<{wl['fmt']}>" if gemm else
+    bgemm = local and mlq.takes_bgemm(wl["rows"], out_f, in_f)
+    gemm = bgemm or (local and mlq.takes_gemm(wl["rows"], out_f, in_f))
+    kernel = (f"bgemm_kernel<{wl['fmt']}> (batched decode)" if bgemm else
+              f"gemm_tc_kernel<{wl['fmt']}>" if gemm else
               f"gemv_stream_kernel<{wl['fmt']}, MT={min(wl['rows'], 8)}, "
               f"{'integer' if wl['rows'] == 1 else 'fp32'} mode>") + f" ({name} launch, rank {ctx.rank})"
     ach = nbytes / (launch_ms / 1e3) / 1e9

@@ -113,15 +113,28 @@ MLQ_API mlq_status mlq_linear(mlq_format fmt, const void* w, size_t block_count,
                               int out_features, int in_features, const float* x, int rows,
                               float* y, mlq_stream stream);
 
-/* Which kernel a call takes.  The tensor-core (tcgen05) GEMM's time hardly
+/* Which kernel a call takes.
+ *
+ * From MLQ_BGEMM_MIN_ROWS to MLQ_BGEMM_MAX_ROWS rows of x (batched decode),
+ * when in_features % 32 == 0 and the weights are 16-B aligned with a 16-B
+ * multiple row pitch: the batched-decode tensor-core GEMM (exact fp16
+ * weight codes, x split into fp16 hi/lo against a power-of-two block
+ * scale, one TMEM accumulator per 32-value block folded in fp32 on the CUDA
+ * cores; the work split evenly over the SMs, split row tiles summed by a
+ * second kernel in a fixed order).  Otherwise the rule below. */
+#define MLQ_BGEMM_MIN_ROWS 2
+#define MLQ_BGEMM_MAX_ROWS 32
+
+/* The tensor-core (tcgen05) GEMM's time hardly
  * depends on the rows of x (one decode of every weight per 128-row tile,
  * split along K when the tiles cannot fill the SMs), the streaming GEMV's
  * grows with every pass of <= 8 rows.  A call takes the GEMM when it has
  * at least MLQ_GEMM_MIN_ROWS rows of x, or at least MLQ_GEMM_LARGE_MIN_ROWS
  * rows on a matrix of at least MLQ_GEMM_LARGE_MIN_WEIGHTS weights
  * (out_features * in_features); MLQ_GEMM_ROWS_RULE(rows, out, in) is that
- * test.  The GEMM also needs 16-B aligned weights with a 16-B multiple row
- * pitch and in_features % 8 == 0; other calls take the streaming GEMV.
+ * test (for calls the batched-decode GEMM does not take).  The GEMM also
+ * needs 16-B aligned weights with a 16-B multiple row pitch and
+ * in_features % 8 == 0; other calls take the streaming GEMV.
  * (Measured on B200 at 8 rows: q4_0 8192x28672, GEMM 158 us vs GEMV
  * 213 us; q4_0 4608x3584, GEMM 24.8 us vs GEMV 18.6 us.) */
 #define MLQ_GEMM_MIN_ROWS 9
@@ -143,9 +156,11 @@ MLQ_API mlq_status mlq_linear(mlq_format fmt, const void* w, size_t block_count,
  * its per-stream workspace by free + malloc when a larger shape arrives).
  *
  * Same arguments, results and validation as mlq_linear.  The tensor-core
- * path keeps the bf16 hi/lo split of x in a static
+ * paths keep the split of x (and their partial sums) in a static
  * MLQ_NOALLOC_SCRATCH_BYTES array of the library's device module instead
- * of a workspace; so a call that takes the GEMM (MLQ_GEMM_ROWS_RULE(rows,
+ * of a workspace.  A call that mlq_linear gives the batched-decode GEMM
+ * runs it in the array when its scratch fits there, else the streaming
+ * GEMV (no scratch).  A call that takes the bf16 GEMM (MLQ_GEMM_ROWS_RULE(rows,
  * out_features, in_features) true, 16-B aligned weights with a 16-B multiple
  * row pitch, in_features % 8 == 0) and has rows * in_features * 4 bytes above
  * that size returns MLQ_ERR_RANGE before any CUDA call; every other call

@@ -17,12 +17,13 @@
 #include "mlq.h"
 #include "mlq_device.cuh"
 #include "mlq_kernels.h"
+#include "mlq_tmap.h"
 
 // Device-side error flag, one per device context (see mlq_device_error).
 __device__ int g_mlq_device_error = 0;
 
-// Scratch of mlq_linear_noalloc: the bf16 hi/lo split of x that its
-// tensor-core GEMM calls read.  It lives in the module's own device memory
+// Scratch of mlq_linear_noalloc: the split of x (and the partial sums) that
+// its tensor-core GEMM calls read.  It lives in the module's own device memory
 // (one copy per device context, created when the module loads), so that
 // entry point never calls cudaMalloc/cudaFree.  Every call on a device uses
 // this one array: a GEMM call rewrites the part it reads before reading it,
@@ -214,53 +215,92 @@ mlq_status run_stream(int fmt, const void* w, int out, int in, const float* x, i
     return MLQ_OK;
 }
 
+// Which kernel takes a call: the batched-decode GEMM for 2..32 rows of x,
+// the tcgen05 GEMM (bf16 hi/lo) for larger calls by MLQ_GEMM_ROWS_RULE, the
+// streaming GEMV otherwise (and the any-alignment GEMV for layouts the
+// streaming kernel does not take).
+enum class Route { kStream, kGeneric, kBgemm, kGemm };
+
+bool bgemm_supported(int fmt, const void* w, int out, int in, int rows) {
+    return mlq::bgemm_shape_ok(fmt, w, out, in, rows) && mlq::encode_fn() != nullptr;
+}
+
+Route route_of(int fmt, const void* w, const void* w2, int out, int in, const float* x, int rows) {
+    if (bgemm_supported(fmt, w, out, in, rows) && (w2 == nullptr || bgemm_supported(fmt, w2, out, in, rows)))
+        return Route::kBgemm;
+    if (mlq::gemm_supported(fmt, w, out, in, rows) && (w2 == nullptr || mlq::gemm_supported(fmt, w2, out, in, rows)))
+        return Route::kGemm;
+    if (streamable(fmt, w, x, in) && (w2 == nullptr || streamable(fmt, w2, x, in))) return Route::kStream;
+    return Route::kGeneric;
+}
+
+// The tensor-core and any-alignment routes of a call (`ws`: its workspace,
+// laid out as the route needs, then -- pair -- the up projection's output).
+mlq_status run_nonstream(Route rt, int fmt, const void* w, int out, int in, const float* x, int rows, float* y,
+                         cudaStream_t stream, const Epilogue& ep, DeviceState* ds, void* ws, size_t wbytes,
+                         int split) {
+    float* u = ep.w2 ? reinterpret_cast<float*>(static_cast<char*>(ws) + wbytes) : nullptr;
+    cudaError_t e = cudaSuccess;
+    if (rt == Route::kBgemm) {
+        e = mlq::launch_bgemm(fmt, static_cast<const uint8_t*>(w), x, y, out, in, rows, ep.bias, ws, ds->sm_count,
+                              ds->err_flag, stream);
+        if (e == cudaSuccess && ep.w2)
+            e = mlq::launch_bgemm(fmt, static_cast<const uint8_t*>(ep.w2), x, u, out, in, rows, nullptr, ws,
+                                  ds->sm_count, ds->err_flag, stream);
+        if (e != cudaSuccess) return fail_cuda("bgemm launch", e);
+    } else if (rt == Route::kGemm) {
+        // many rows of x: the tensor-core GEMM (bias in its store; a pair
+        // runs it per matrix, then one SwiGLU pass)
+        e = mlq::launch_gemm(fmt, static_cast<const uint8_t*>(w), x, y, out, in, rows, ep.bias, ws, split,
+                             ds->sm_count, ds->err_flag, stream);
+        if (e == cudaSuccess && ep.w2)
+            e = mlq::launch_gemm(fmt, static_cast<const uint8_t*>(ep.w2), x, u, out, in, rows, nullptr, ws, split,
+                                 ds->sm_count, ds->err_flag, stream);
+        if (e != cudaSuccess) return fail_cuda("gemm launch", e);
+    } else {
+        // layouts the streaming kernel does not take: the any-alignment GEMV
+        const int bpr = (in + mlq::kQK - 1) / mlq::kQK;
+        e = mlq::launch_gemv_generic(fmt, static_cast<const uint8_t*>(w), x, y, out, in, rows, bpr, stream);
+        if (e == cudaSuccess && ep.w2)
+            e = mlq::launch_gemv_generic(fmt, static_cast<const uint8_t*>(ep.w2), x, u, out, in, rows, bpr, stream);
+        if (e == cudaSuccess && ep.bias && !ep.w2) e = mlq::launch_add_bias(y, ep.bias, rows, out, stream);
+        if (e != cudaSuccess) return fail_cuda("gemv_generic launch", e);
+    }
+    if (ep.w2) {
+        e = mlq::launch_swiglu(y, u, (long long)rows * out, stream);
+        if (e != cudaSuccess) return fail_cuda("swiglu launch", e);
+    }
+    return MLQ_OK;
+}
+
 mlq_status run_linear(int fmt, const void* w, int out, int in, const float* x, int rows, float* y,
                       cudaStream_t stream, const Epilogue& ep = Epilogue()) {
-    const bool gemm = mlq::gemm_supported(fmt, w, out, in, rows) &&
-                      (ep.w2 == nullptr || mlq::gemm_supported(fmt, ep.w2, out, in, rows));
-    const bool stream_ok = streamable(fmt, w, x, in) && (ep.w2 == nullptr || streamable(fmt, ep.w2, x, in));
-    if (gemm || !stream_ok) {
+    const Route rt = route_of(fmt, w, ep.w2, out, in, x, rows);
+    if (rt != Route::kStream) {
         int dev = 0;
         cudaError_t e = cudaGetDevice(&dev);
         if (e != cudaSuccess) return fail_cuda("cudaGetDevice", e);
         mlq_status st = MLQ_OK;
         DeviceState* ds = device_state(dev, &st);
         if (!ds) return st;
-        // workspace: the GEMM's x split and split-K partials, then (pair) the
-        // up projection's output
-        const int split = gemm ? mlq::gemm_split(out, in, rows, ds->sm_count) : 1;
-        const size_t xsplit = gemm ? (mlq::gemm_workspace_bytes(in, rows, out, split) + 255) & ~(size_t)255 : 0;
+        // workspace: the route's own (x split, scales, partial sums), 256-B
+        // aligned, then (pair) the up projection's output
+        int split = 1;
+        size_t wb = 0;
+        if (rt == Route::kBgemm) {
+            wb = mlq::bgemm_workspace_bytes(fmt, in, rows, out, ds->sm_count);
+        } else if (rt == Route::kGemm) {
+            split = mlq::gemm_split(out, in, rows, ds->sm_count);
+            wb = mlq::gemm_workspace_bytes(in, rows, out, split);
+        }
+        wb = (wb + 255) & ~(size_t)255;
         const size_t ubytes = ep.w2 ? (size_t)rows * out * sizeof(float) : 0;
         void* ws = nullptr;
-        if (xsplit + ubytes > 0) {
-            st = stream_workspace(ds, stream, xsplit + ubytes, &ws);
+        if (wb + ubytes > 0) {
+            st = stream_workspace(ds, stream, wb + ubytes, &ws);
             if (st != MLQ_OK) return st;
         }
-        float* u = ep.w2 ? reinterpret_cast<float*>(static_cast<char*>(ws) + xsplit) : nullptr;
-        if (gemm) {
-            // many rows of x: the tensor-core GEMM (bias in its store; a pair
-            // runs it per matrix, then one SwiGLU pass)
-            e = mlq::launch_gemm(fmt, static_cast<const uint8_t*>(w), x, y, out, in, rows, ep.bias, ws, split,
-                                 ds->sm_count, ds->err_flag, stream);
-            if (e == cudaSuccess && ep.w2)
-                e = mlq::launch_gemm(fmt, static_cast<const uint8_t*>(ep.w2), x, u, out, in, rows, nullptr, ws,
-                                     split, ds->sm_count, ds->err_flag, stream);
-            if (e != cudaSuccess) return fail_cuda("gemm launch", e);
-        } else {
-            // layouts the streaming kernel does not take: the any-alignment GEMV
-            const int bpr = (in + mlq::kQK - 1) / mlq::kQK;
-            e = mlq::launch_gemv_generic(fmt, static_cast<const uint8_t*>(w), x, y, out, in, rows, bpr, stream);
-            if (e == cudaSuccess && ep.w2)
-                e = mlq::launch_gemv_generic(fmt, static_cast<const uint8_t*>(ep.w2), x, u, out, in, rows, bpr,
-                                             stream);
-            if (e == cudaSuccess && ep.bias && !ep.w2) e = mlq::launch_add_bias(y, ep.bias, rows, out, stream);
-            if (e != cudaSuccess) return fail_cuda("gemv_generic launch", e);
-        }
-        if (ep.w2) {
-            e = mlq::launch_swiglu(y, u, (long long)rows * out, stream);
-            if (e != cudaSuccess) return fail_cuda("swiglu launch", e);
-        }
-        return MLQ_OK;
+        return run_nonstream(rt, fmt, w, out, in, x, rows, y, stream, ep, ds, ws, wb, split);
     }
     Gather g;
     g.y_stride = out;
@@ -278,32 +318,45 @@ struct ScratchSlot {
 
 ScratchSlot g_scratch[kMaxDevices];
 
-// mlq_linear without any device allocation.  The GEMV kernels need no
-// scratch, so every call they take goes through run_linear unchanged; only
-// the tensor-core GEMM differs, reading its x split from the static array
-// instead of the per-stream workspace.
+// mlq_linear without any device allocation.  The streaming and
+// any-alignment GEMVs need no scratch, so the calls they take run as in
+// mlq_linear; the tensor-core kernels read their x split (and partial sums)
+// from the static array instead of the per-stream workspace.  A call that
+// mlq_linear would give the batched-decode GEMM whose scratch does not fit
+// the array runs the streaming GEMV (the bf16 GEMM's limit is checked by
+// the caller before any CUDA call).
 mlq_status run_linear_noalloc(int fmt, const void* w, int out, int in, const float* x, int rows,
                               float* y, cudaStream_t stream) {
-    if (!mlq::gemm_supported(fmt, w, out, in, rows)) return run_linear(fmt, w, out, in, x, rows, y, stream);
+    Route rt = route_of(fmt, w, nullptr, out, in, x, rows);
+    if (rt == Route::kStream || rt == Route::kGeneric) return run_linear(fmt, w, out, in, x, rows, y, stream);
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return fail_cuda("cudaGetDevice", e);
     mlq_status st = MLQ_OK;
     DeviceState* ds = device_state(dev, &st);
     if (!ds) return st;
-    ScratchSlot& s = g_scratch[dev];
-    std::call_once(s.once, [&] { s.err = cudaGetSymbolAddress(&s.ptr, g_mlq_noalloc_scratch); });
-    if (s.err != cudaSuccess || s.ptr == nullptr)
-        return fail_cuda("cudaGetSymbolAddress (static scratch)", s.err != cudaSuccess ? s.err : cudaErrorInvalidSymbol);
-    // split-K as mlq_linear chooses it, lowered to the largest count whose
-    // partial sums fit the scratch next to the x split (1 always fits: the
-    // caller checked the x split against the scratch size)
-    int split = mlq::gemm_split(out, in, rows, ds->sm_count);
-    while (split > 1 && mlq::gemm_workspace_bytes(in, rows, out, split) > (size_t)MLQ_NOALLOC_SCRATCH_BYTES)
-        --split;
-    e = mlq::launch_gemm(fmt, static_cast<const uint8_t*>(w), x, y, out, in, rows, nullptr, s.ptr, split,
-                         ds->sm_count, ds->err_flag, stream);
-    return e == cudaSuccess ? MLQ_OK : fail_cuda("gemm launch", e);
+    if (rt == Route::kBgemm &&
+        mlq::bgemm_workspace_bytes(fmt, in, rows, out, ds->sm_count) > (size_t)MLQ_NOALLOC_SCRATCH_BYTES) {
+        Gather g;
+        g.y_stride = out;
+        g.ys = &y;
+        if (streamable(fmt, w, x, in)) return run_stream(fmt, w, out, in, x, rows, g, stream);
+        return run_nonstream(Route::kGeneric, fmt, w, out, in, x, rows, y, stream, Epilogue(), ds, nullptr, 0, 1);
+    }
+    ScratchSlot& sl = g_scratch[dev];
+    std::call_once(sl.once, [&] { sl.err = cudaGetSymbolAddress(&sl.ptr, g_mlq_noalloc_scratch); });
+    if (sl.err != cudaSuccess || sl.ptr == nullptr)
+        return fail_cuda("cudaGetSymbolAddress (static scratch)", sl.err != cudaSuccess ? sl.err : cudaErrorInvalidSymbol);
+    int split = 1;
+    if (rt == Route::kGemm) {
+        // split-K as mlq_linear chooses it, lowered to the largest count whose
+        // partial sums fit the scratch next to the x split (1 always fits: the
+        // caller checked the x split against the scratch size)
+        split = mlq::gemm_split(out, in, rows, ds->sm_count);
+        while (split > 1 && mlq::gemm_workspace_bytes(in, rows, out, split) > (size_t)MLQ_NOALLOC_SCRATCH_BYTES)
+            --split;
+    }
+    return run_nonstream(rt, fmt, w, out, in, x, rows, y, stream, Epilogue(), ds, sl.ptr, 0, split);
 }
 
 // Grows a per-device staging buffer (called under host_mu, device current).
@@ -488,8 +541,8 @@ MLQ_API mlq_status mlq_linear_noalloc(mlq_format fmt, const void* w, size_t bloc
         // only a call that takes the tensor-core GEMM uses the scratch (the
         // same routing test as mlq_linear: rows rule, alignment, in % 8)
         const size_t need = mlq::gemm_workspace_bytes(in_features, rows, out_features, 1);
-        if (mlq::gemm_shape_ok(fmt, w, out_features, in_features, rows) &&
-            need > (size_t)MLQ_NOALLOC_SCRATCH_BYTES)
+        if (!mlq::bgemm_shape_ok(fmt, w, out_features, in_features, rows) &&
+            mlq::gemm_shape_ok(fmt, w, out_features, in_features, rows) && need > (size_t)MLQ_NOALLOC_SCRATCH_BYTES)
             return fail(MLQ_ERR_RANGE,
                         "mlq_linear_noalloc: rows * in_features * 4 = " + std::to_string(need) +
                             " bytes of x split exceed the " +

@@ -1,0 +1,653 @@
+// mlq_bgemm.cu -- batched-decode GEMM on the tensor cores: 2..32 rows of x
+// against a quantized matrix, the regime of batched decoding (a handful of
+// sequences, one new token each) where the work is still bound by reading
+// the weights once, but too many rows for the CUDA-core GEMV.
+//
+// The reference decodes a batch one token at a time through its GEMV
+// (forwardBatch -> forwardToken, src/batch.cc:32-55; q80/q40/q41LinearKernel,
+// src/cuda_quant.cu:78-182).  Same arithmetic contract here: exact weights,
+// fp32-level activations, fp32 accumulation; only the summation order
+// differs.
+//
+// Arithmetic, per 32-value block b of a weight row and token t:
+//   * The block's integer codes go to the tensor cores as fp16 values,
+//     exactly: q8_0 q in [-128, 127], q4_0 q - 8 in [-8, 7], q4_1 q in
+//     [0, 15].  (One byte permute drops a code into the mantissa of 1024.0,
+//     one packed subtract removes the 1024 + offset: ~1.3 operations per
+//     weight, one fp16 A tile.)
+//   * x is scaled per (token, block) by a power of two s >= max|x_block| and
+//     split x/s = xh + xl into two fp16 values (xsplit kernel below): exact
+//     to 2^-24 of s, the level of one fp32 rounding of the block's largest
+//     value.
+//   * One 128 x N x 32 product per block on the tensor cores (two kind::f16
+//     MMAs of K = 16) gives D[row][t] = sum q (xh + xl) over the block -- the
+//     hi and lo halves of x are the two halves of B (N = 2 x padded tokens)
+//     -- in a TMEM accumulator of its own.
+//   * CUDA-core "fold" warps read the block's accumulator and add
+//     d * (s * D) (+ m * sum(x) for q4_1) to the fp32 total of (row, t).
+//     The block scales never enter the tensor-core sums.
+//
+// CTA = 10 warps, one CTA per SM:
+//   warp 0     TMA producer: W chunks (8 blocks x 128 rows, 2-D tensor map
+//              over the AoS bytes) and the chunk's x tiles (fp16 [hi; lo],
+//              128-B swizzle).
+//   warp 1     TMEM allocation; lane 0 issues the MMAs and commits.
+//   warps 2-5  decode: thread = W row; codes -> fp16 A tile (swizzled,
+//              K-major), the block's d (and m) -> a per-accumulator slot.
+//   warps 6-9  fold: thread = W row = TMEM lane (one lane quarter per warp).
+// Work split ("stream-K"): the matrix is a list of (row tile, block) units;
+// CTA c takes the contiguous range [c W / G, (c + 1) W / G).  A row tile a
+// CTA covers whole is stored straight to y; the at most two partly covered
+// tiles at the ends of its range go to a workspace, and a second kernel adds
+// every split tile's parts in CTA order (deterministic) plus the bias.
+// Every mbarrier wait is bounded (2 s); no TMA multicast anywhere.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <atomic>
+
+#include "mlq.h"
+#include "mlq_device.cuh"
+#include "mlq_kernels.h"
+#include "mlq_tc.cuh"
+#include "mlq_tmap.h"
+
+namespace mlq {
+namespace {
+
+constexpr int BM = 128;             // W rows per tile = MMA M = TMEM lanes
+constexpr int KC = 256;             // values per W chunk
+constexpr int BPC = KC / kQK;       // blocks per chunk (8)
+constexpr int SPC = 4;              // A stages per chunk: two blocks (64 values) each
+constexpr int kPrepWarps = 4;       // warps 2..5
+constexpr int kFoldWarps = 4;       // warps 6..9
+constexpr int kThreads = 32 * (2 + kPrepWarps + kFoldWarps);
+constexpr int kSmemMax = 232448;    // dynamic shared memory per CTA (227 KB)
+constexpr int kMinBlocksPerCta = 16;
+
+constexpr int cmin(int a, int b) { return a < b ? a : b; }
+constexpr int pow2_at_least(int v) { return v <= 32 ? 32 : (v <= 64 ? 64 : (v <= 128 ? 128 : (v <= 256 ? 256 : 512))); }
+
+// TP: padded tokens (8, 16 or 32); the MMA's N is 2 TP (x hi, then x lo).
+template <int F, int TP>
+struct BCfg {
+    static constexpr int BS = Fmt<F>::kBlockBytes;
+    static constexpr int N = 2 * TP;
+    static constexpr int W_ROW = BPC * BS;             // 272 / 144 / 160 bytes of a row's chunk
+    static constexpr int W_ESZ = F == kQ8_0 ? 2 : 1;   // tensor-map element (inner box <= 256 elements)
+    static constexpr int W_TILE = BM * W_ROW;
+    static constexpr int B_SUB = N * 128;              // [hi; lo] x tile of 64 values (fp16, 128-B rows)
+    static constexpr int B_TILE = SPC * B_SUB;
+    static constexpr int C_STAGE = W_TILE + B_TILE;    // a chunk: W, then its x tiles
+    static constexpr int A_TILE = BM * 128;            // 128 rows x 64 fp16 codes
+    static constexpr int NSLOT = cmin(16, 512 / N);    // TMEM accumulators (one per block in flight)
+    static constexpr uint32_t TMEM_COLS = (uint32_t)pow2_at_least(NSLOT * N);
+    static constexpr int DM_BYTES = NSLOT * BM * 8;    // (d, m) per slot and row
+    static constexpr int fixed = DM_BYTES + 1024;      // + 1024-B alignment slack
+    static constexpr int CS = (3 * C_STAGE + 3 * A_TILE + fixed <= kSmemMax) ? 3 : 2;
+    static constexpr int AS = (CS * C_STAGE + 4 * A_TILE + fixed <= kSmemMax) ? 4 : 3;
+    static constexpr int SMEM = CS * C_STAGE + AS * A_TILE + fixed;
+    static_assert(SMEM <= kSmemMax, "bgemm stages must fit shared memory");
+    static_assert(W_TILE % 1024 == 0 && B_SUB % 1024 == 0 && C_STAGE % 1024 == 0 && A_TILE % 1024 == 0,
+                  "SW128 tiles need 1024-B alignment");
+    static_assert(W_ROW % 16 == 0, "W chunk row must be 16-byte granular");
+};
+
+struct BgemmArgs {
+    float* y;             // [T][out]
+    const float* bias;    // [out] or null
+    const float* sc;      // [kb][TP]: power-of-two block scale of x (NaN: the block holds NaN/Inf)
+    const float* xsum;    // [kb][TP]: block sums of x (q4_1), else null
+    float* part;          // [grid][2][TP][BM]: partial sums of partly covered row tiles
+    int out, in, T, kb;   // kb = blocks per row
+    long long total;      // units = row tiles x kb
+    int* err;
+};
+
+// The units [f0, f1) of CTA c among G.
+__host__ __device__ __forceinline__ long long unit_begin(long long total, int c, int G) {
+    return (long long)c * total / G;
+}
+
+// fp16 codes of one block (32 values) as 16 half2 words, element order.
+// Bytes b of a word u become half(1024 + b) by a byte permute under 0x64;
+// the packed subtract of `off` (1024 + the format's code offset) is exact.
+__device__ __forceinline__ uint32_t h2_sub(uint32_t h, uint32_t off2) {
+    __half2 r = __hsub2(*reinterpret_cast<const __half2*>(&h), *reinterpret_cast<const __half2*>(&off2));
+    return *reinterpret_cast<const uint32_t*>(&r);
+}
+
+template <int F>
+__device__ __forceinline__ void codes_f16(const uint32_t* qw, uint32_t (&c)[16]) {
+    if constexpr (F == kQ8_0) {
+        const uint32_t off2 = 0x64806480u;  // half2(1152, 1152): 1024 + 128
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const uint32_t u = qw[i] ^ 0x80808080u;  // q + 128, one byte each
+            c[2 * i] = h2_sub(__byte_perm(u, 0x64646464u, 0x4140), off2);
+            c[2 * i + 1] = h2_sub(__byte_perm(u, 0x64646464u, 0x4342), off2);
+        }
+    } else {
+        const uint32_t off2 = F == kQ4_0 ? 0x64086408u : 0x64006400u;  // 1024 + 8 / 1024
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {  // qs word i: elements 4i.. (low nibbles), 16 + 4i.. (high)
+            const uint32_t lo = qw[i] & 0x0F0F0F0Fu, hi = (qw[i] >> 4) & 0x0F0F0F0Fu;
+            c[2 * i] = h2_sub(__byte_perm(lo, 0x64646464u, 0x4140), off2);
+            c[2 * i + 1] = h2_sub(__byte_perm(lo, 0x64646464u, 0x4342), off2);
+            c[8 + 2 * i] = h2_sub(__byte_perm(hi, 0x64646464u, 0x4140), off2);
+            c[9 + 2 * i] = h2_sub(__byte_perm(hi, 0x64646464u, 0x4342), off2);
+        }
+    }
+}
+
+// Walks the CTA's range chunk by chunk: fn(tile, chunk, b_lo, b_hi) with
+// [b_lo, b_hi) the blocks of the tile's row that the CTA covers.
+template <typename Fn>
+__device__ __forceinline__ void for_each_chunk(long long f0, long long f1, int kb, Fn&& fn) {
+    if (f1 <= f0) return;
+    const long long t0 = f0 / kb, t1 = (f1 - 1) / kb;
+    for (long long t = t0; t <= t1; ++t) {
+        const int b_lo = (int)(f0 > t * kb ? f0 - t * kb : 0);
+        const int b_hi = (int)(f1 < (t + 1) * kb ? f1 - t * kb : kb);
+        for (int c = b_lo / BPC; c <= (b_hi - 1) / BPC; ++c)
+            if (!fn((int)t, c, b_lo, b_hi)) return;
+    }
+}
+
+template <int F, int TP>
+__global__ void __launch_bounds__(kThreads, 1)
+    bgemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x, BgemmArgs a) {
+    using C = BCfg<F, TP>;
+    constexpr int CS = C::CS, AS = C::AS, NSLOT = C::NSLOT, N = C::N;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    __shared__ __align__(8) uint64_t c_full[CS], c_empty[CS], a_full[AS], a_empty[AS];
+    __shared__ __align__(8) uint64_t s_full[NSLOT], s_empty[NSLOT], dm_full[NSLOT];
+    __shared__ __align__(8) uint64_t drain_bar, end_bar;
+    __shared__ uint32_t tmem_base_s;
+    __shared__ int abort_flag;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
+    auto w_st = [&](int s) { return base + (uint32_t)(s * C::C_STAGE); };
+    auto x_st = [&](int s) { return w_st(s) + (uint32_t)C::W_TILE; };
+    auto a_st = [&](int s) { return base + (uint32_t)(CS * C::C_STAGE + s * C::A_TILE); };
+    const uint32_t dm_base = base + (uint32_t)(CS * C::C_STAGE + AS * C::A_TILE);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < CS; ++s) {
+            mbar_init(smem_u32(&c_full[s]), 1);
+            mbar_init(smem_u32(&c_empty[s]), kPrepWarps + 1);  // decode warps + the chunk's last MMA commit
+        }
+        for (int s = 0; s < AS; ++s) {
+            mbar_init(smem_u32(&a_full[s]), kPrepWarps);
+            mbar_init(smem_u32(&a_empty[s]), 1);
+        }
+        for (int s = 0; s < NSLOT; ++s) {
+            mbar_init(smem_u32(&s_full[s]), 1);
+            mbar_init(smem_u32(&s_empty[s]), kFoldWarps);
+            mbar_init(smem_u32(&dm_full[s]), kPrepWarps);
+        }
+        mbar_init(smem_u32(&drain_bar), 1);
+        mbar_init(smem_u32(&end_bar), kThreads / 32);
+        abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) tmem_alloc(smem_u32(&tmem_base_s), C::TMEM_COLS);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_base_s;
+
+    const int G = gridDim.x;
+    const long long f0 = unit_begin(a.total, blockIdx.x, G), f1 = unit_begin(a.total, blockIdx.x + 1, G);
+    auto aborted = [&]() { return *(volatile int*)&abort_flag != 0; };
+    auto fail = [&](int code) {
+        report_error(a.err, code);
+        abort_flag = 1;
+    };
+
+    if (warp == 0) {
+        // ------------------------------ TMA producer ------------------------------
+        if (lane == 0) {
+            uint32_t cseq = 0;
+            for_each_chunk(f0, f1, a.kb, [&](int t, int c, int, int) {
+                const int s = (int)(cseq % CS);
+                if (!mbar_wait(smem_u32(&c_empty[s]), ((cseq / CS) & 1u) ^ 1u)) {
+                    fail(20);
+                    return false;
+                }
+                if (aborted()) return false;
+                const uint32_t fb = smem_u32(&c_full[s]);
+                mbar_arrive_expect_tx(fb, (uint32_t)(C::W_TILE + C::B_TILE));
+                tma_load_2d(w_st(s), &tm_w, c * (C::W_ROW / C::W_ESZ), t * BM, fb);
+#pragma unroll
+                for (int j = 0; j < SPC; ++j) tma_load_2d(x_st(s) + (uint32_t)(j * C::B_SUB), &tm_x, c * KC + j * 64, 0, fb);
+                ++cseq;
+                return true;
+            });
+            // the CTA's shared memory must outlive every copy still landing
+            for (uint32_t k = cseq >= (uint32_t)CS ? cseq - CS : 0; k < cseq; ++k)
+                if (!mbar_wait(smem_u32(&c_full[k % CS]), (k / CS) & 1u)) {
+                    report_error(a.err, 21);
+                    break;
+                }
+        }
+    } else if (warp == 1) {
+        // ------------------------------ MMA issuer ------------------------------
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_f16kind(false, BM, N);
+            uint32_t cseq = 0, aseq = 0, bseq = 0;
+            for_each_chunk(f0, f1, a.kb, [&](int, int c, int b_lo, int b_hi) {
+                const int cs = (int)(cseq % CS);
+                if (!mbar_wait(smem_u32(&c_full[cs]), (cseq / CS) & 1u)) {
+                    fail(22);
+                    return false;
+                }
+                for (int j = 0; j < SPC; ++j) {
+                    const int k0 = c * BPC + 2 * j;
+                    const bool v0 = k0 >= b_lo && k0 < b_hi, v1 = k0 + 1 >= b_lo && k0 + 1 < b_hi;
+                    if (!v0 && !v1) continue;
+                    const int as = (int)(aseq % AS);
+                    if (!mbar_wait(smem_u32(&a_full[as]), (aseq / AS) & 1u)) {
+                        fail(22);
+                        return false;
+                    }
+                    if (aborted()) return false;
+                    tc_fence_after();
+                    const uint64_t ad = sw128_desc(a_st(as));
+                    const uint64_t bd = sw128_desc(x_st(cs) + (uint32_t)(j * C::B_SUB));
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        if (!(h ? v1 : v0)) continue;
+                        const int slot = (int)(bseq % NSLOT);
+                        if (!mbar_wait(smem_u32(&s_empty[slot]), ((bseq / NSLOT) & 1u) ^ 1u)) {
+                            fail(22);
+                            return false;
+                        }
+                        tc_fence_after();
+                        const uint32_t td = tmem + (uint32_t)(slot * N);
+#pragma unroll
+                        for (int kk = 0; kk < 2; ++kk) {
+                            const uint64_t adv = (uint64_t)((h * 64 + kk * 32) >> 4);  // bytes along K / 16
+                            mma_f16kind(td, ad + adv, bd + adv, idesc, kk);
+                        }
+                        mma_commit(smem_u32(&s_full[slot]));
+                        ++bseq;
+                    }
+                    mma_commit(smem_u32(&a_empty[as]));
+                    ++aseq;
+                }
+                mma_commit(smem_u32(&c_empty[cs]));  // the chunk's x tiles are read
+                ++cseq;
+                return true;
+            });
+            // every MMA issued has completed before TMEM goes away
+            mma_commit(smem_u32(&drain_bar));
+            if (!mbar_wait(smem_u32(&drain_bar), 0u)) report_error(a.err, 23);
+        }
+    } else if (warp < 2 + kPrepWarps) {
+        // --------------------- decode: codes -> fp16 A tiles ---------------------
+        const int row = (warp - 2) * 32 + lane;
+        const uint32_t swz = (uint32_t)(row & 7);
+        uint32_t cseq = 0, aseq = 0, bseq = 0;
+        for_each_chunk(f0, f1, a.kb, [&](int, int c, int b_lo, int b_hi) {
+            const int cs = (int)(cseq % CS);
+            if (!mbar_wait(smem_u32(&c_full[cs]), (cseq / CS) & 1u)) {
+                fail(24);
+                return false;
+            }
+            const uint32_t wrow = w_st(cs) + (uint32_t)(row * C::W_ROW);
+            for (int j = 0; j < SPC; ++j) {
+                const int k0 = c * BPC + 2 * j;
+                const bool v0 = k0 >= b_lo && k0 < b_hi, v1 = k0 + 1 >= b_lo && k0 + 1 < b_hi;
+                if (!v0 && !v1) continue;
+                const int as = (int)(aseq % AS);
+                if (!mbar_wait(smem_u32(&a_empty[as]), ((aseq / AS) & 1u) ^ 1u)) {
+                    fail(24);
+                    return false;
+                }
+                if (aborted()) return false;
+                // the stage's two blocks: 2 BS bytes from a word boundary
+                constexpr int NW = 2 * C::BS / 4;
+                uint32_t w[NW + 1];
+#pragma unroll
+                for (int i = 0; i < NW; ++i) w[i] = lds_u32(wrow + (uint32_t)(j * 2 * C::BS + 4 * i));
+                w[NW] = 0;
+                const uint32_t arow = a_st(as) + (uint32_t)row * 128u;
+                float dm_d[2], dm_m[2];
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    uint32_t qw[8];
+                    uint32_t dbits, mbits = 0;
+                    if constexpr (F == kQ8_0) {
+                        // block 0: d = bytes 0-1, codes 2..33; block 1: d = 34-35, codes 36..67
+                        dbits = h ? (w[8] >> 16) : (w[0] & 0xFFFFu);
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) qw[i] = h ? w[9 + i] : __funnelshift_r(w[i], w[i + 1], 16);
+                    } else if constexpr (F == kQ4_0) {
+                        // block 0: d = 0-1, qs 2..17; block 1: d = 18-19, qs 20..35
+                        dbits = h ? (w[4] >> 16) : (w[0] & 0xFFFFu);
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) qw[i] = h ? w[5 + i] : __funnelshift_r(w[i], w[i + 1], 16);
+                    } else {
+                        // d, m, then qs: words 0 / 1..4 and 5 / 6..9
+                        dbits = w[5 * h] & 0xFFFFu;
+                        mbits = w[5 * h] >> 16;
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) qw[i] = w[5 * h + 1 + i];
+                    }
+                    dm_d[h] = half_bits_to_float(dbits);
+                    dm_m[h] = half_bits_to_float(mbits);
+                    if (!(h ? v1 : v0)) continue;  // no MMA reads this half
+                    uint32_t cw[16];
+                    codes_f16<F>(qw, cw);
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {  // 16-byte chunks 4h + q of the 64-value row
+                        const uint32_t cs16 = ((uint32_t)(4 * h + q) ^ swz) << 4;
+                        sts_u4(arow + cs16, make_uint4(cw[4 * q], cw[4 * q + 1], cw[4 * q + 2], cw[4 * q + 3]));
+                    }
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(&a_full[as]));
+                ++aseq;
+                // the blocks' scales for the fold, in the slots of their accumulators
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    if (!(h ? v1 : v0)) continue;
+                    const int slot = (int)(bseq % NSLOT);
+                    if (!mbar_wait(smem_u32(&s_empty[slot]), ((bseq / NSLOT) & 1u) ^ 1u)) {
+                        fail(24);
+                        return false;
+                    }
+                    sts_f2(dm_base + (uint32_t)((slot * BM + row) * 8), make_float2(dm_d[h], dm_m[h]));
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(smem_u32(&dm_full[slot]));
+                    ++bseq;
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&c_empty[cs]));  // W of this chunk is read
+            ++cseq;
+            return true;
+        });
+    } else {
+        // ------------------ fold: TMEM block sums -> fp32 totals ------------------
+        const int quarter = warp & 3;          // TMEM lanes 32 quarter .. + 31
+        const int row = quarter * 32 + lane;   // tile row
+        float acc[TP];
+#pragma unroll
+        for (int t = 0; t < TP; ++t) acc[t] = 0.f;
+        uint32_t bseq = 0;
+        int seg_tile = -1;
+        auto flush = [&](int t, int b_lo, int b_hi) {
+            // the CTA's segment of row tile t ends: y, or its part for the fix-up
+            const int o = t * BM + row;
+            if (b_lo == 0 && b_hi == a.kb) {
+                if (o < a.out) {
+                    const float bo = a.bias ? a.bias[o] : 0.f;
+#pragma unroll
+                    for (int tt = 0; tt < TP; ++tt)
+                        if (tt < a.T) a.y[(long long)tt * a.out + o] = a.bias ? __fadd_rn(acc[tt], bo) : acc[tt];
+                }
+            } else {
+                const int slot01 = f0 >= (long long)t * a.kb ? 0 : 1;
+                float* p = a.part + ((long long)blockIdx.x * 2 + slot01) * TP * BM;
+#pragma unroll
+                for (int tt = 0; tt < TP; ++tt) p[tt * BM + row] = acc[tt];
+            }
+#pragma unroll
+            for (int tt = 0; tt < TP; ++tt) acc[tt] = 0.f;
+        };
+        int last_t = -1, last_lo = 0, last_hi = 0;
+        for_each_chunk(f0, f1, a.kb, [&](int t, int c, int b_lo, int b_hi) {
+            if (t != seg_tile) {
+                if (seg_tile >= 0) flush(last_t, last_lo, last_hi);
+                seg_tile = t;
+            }
+            last_t = t;
+            last_lo = b_lo;
+            last_hi = b_hi;
+            const int kbeg = c * BPC > b_lo ? c * BPC : b_lo;
+            const int kend = (c + 1) * BPC < b_hi ? (c + 1) * BPC : b_hi;
+            for (int k = kbeg; k < kend; ++k) {
+                const int slot = (int)(bseq % NSLOT);
+                const uint32_t ph = (bseq / NSLOT) & 1u;
+                if (!mbar_wait(smem_u32(&s_full[slot]), ph) || !mbar_wait(smem_u32(&dm_full[slot]), ph)) {
+                    fail(25);
+                    return false;
+                }
+                tc_fence_after();
+                uint32_t v[N];
+                const uint32_t ta = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(slot * N);
+                if constexpr (N == 16) {
+                    tmem_ld16(ta, *reinterpret_cast<uint32_t(*)[16]>(v));
+                } else {
+#pragma unroll
+                    for (int q = 0; q < N / 32; ++q)
+                        tmem_ld32(ta + (uint32_t)(32 * q), *reinterpret_cast<uint32_t(*)[32]>(v + 32 * q));
+                }
+                const float2 dm = lds_f2(dm_base + (uint32_t)((slot * BM + row) * 8));
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(&s_empty[slot]));
+                // x block scales (and sums) of the block: TP values, the same for every lane
+                const float4* sp = reinterpret_cast<const float4*>(a.sc + (long long)k * TP);
+#pragma unroll
+                for (int q = 0; q < TP / 4; ++q) {
+                    const float4 s4 = __ldg(sp + q);
+                    const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int tt = 4 * q + u;
+                        const float dsum = __uint_as_float(v[tt]) + __uint_as_float(v[TP + tt]);
+                        acc[tt] = fmaf(dsum * sv[u], dm.x, acc[tt]);
+                    }
+                }
+                if constexpr (F == kQ4_1) {
+                    const float4* xp = reinterpret_cast<const float4*>(a.xsum + (long long)k * TP);
+#pragma unroll
+                    for (int q = 0; q < TP / 4; ++q) {
+                        const float4 s4 = __ldg(xp + q);
+                        acc[4 * q] = fmaf(dm.y, s4.x, acc[4 * q]);
+                        acc[4 * q + 1] = fmaf(dm.y, s4.y, acc[4 * q + 1]);
+                        acc[4 * q + 2] = fmaf(dm.y, s4.z, acc[4 * q + 2]);
+                        acc[4 * q + 3] = fmaf(dm.y, s4.w, acc[4 * q + 3]);
+                    }
+                }
+                ++bseq;
+            }
+            return !aborted();
+        });
+        if (last_t >= 0 && !aborted()) flush(last_t, last_lo, last_hi);
+    }
+
+    // every warp is done with TMEM and shared memory; warp 1 frees TMEM
+    __syncwarp();
+    if (lane == 0) mbar_arrive(smem_u32(&end_bar));
+    if (warp == 1) {
+        if (!mbar_wait(smem_u32(&end_bar), 0u)) report_error(a.err, 26);
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tmem, C::TMEM_COLS);
+    }
+}
+
+// x fp32 [T][in] -> the B operand fp16 [2 TP][in] (rows t: hi, TP + t: lo;
+// rows >= T zero), per (block, token) the power-of-two scale and (q4_1) the
+// block sum.  One warp per (block, token).
+template <int TP>
+__global__ void bgemm_xsplit_kernel(const float* __restrict__ x, int T, int in, int kb, __half* __restrict__ xb,
+                                    float* __restrict__ sc, float* __restrict__ xsum) {
+    const long long wid = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (wid >= (long long)kb * TP) return;
+    const int b = (int)(wid / TP), t = (int)(wid % TP);
+    const long long e = (long long)b * kQK + lane;
+    const float v = t < T ? x[(long long)t * in + e] : 0.f;
+    float mx = fabsf(v);
+    int bad = !(mx <= 3.402823466e38f);  // NaN or Inf
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+        bad |= __shfl_xor_sync(0xffffffffu, bad, off);
+    }
+    int ex = 0;
+    if (mx > 0.f && !bad) frexpf(mx, &ex);  // mx = f 2^ex, f in [0.5, 1): |v / 2^ex| < 1
+    const float xs = ldexpf(v, -ex);        // exact (a power-of-two scaling)
+    const __half h = __float2half_rn(xs);
+    const __half l = __float2half_rn(xs - __half2float(h));
+    xb[(long long)t * in + e] = h;
+    xb[(long long)(TP + t) * in + e] = l;
+    float s = v;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+    if (lane == 0) {
+        sc[(long long)b * TP + t] = bad ? __int_as_float(0x7fc00000) : ldexpf(1.0f, ex);
+        if (xsum) xsum[(long long)b * TP + t] = s;
+    }
+}
+
+// Split row tiles: y = the parts of every CTA that covers the tile, in CTA
+// order, plus the bias.  One thread per (tile, token, row).
+__global__ void bgemm_fixup_kernel(BgemmArgs a, int tp, int G) {
+    const long long tiles = (a.out + BM - 1) / BM;
+    const long long n = tiles * a.T * BM;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        const int r = (int)(i % BM);
+        const int tt = (int)((i / BM) % a.T);
+        const long long t = i / BM / a.T;
+        const int o = (int)(t * BM + r);
+        if (o >= a.out) continue;
+        // CTAs holding the tile's first and last unit
+        const long long u0 = t * a.kb, u1 = u0 + a.kb - 1;
+        int c0 = (int)(u0 * G / a.total), c1 = (int)(u1 * G / a.total);
+        while (c0 + 1 < G && unit_begin(a.total, c0 + 1, G) <= u0) ++c0;
+        while (c0 > 0 && unit_begin(a.total, c0, G) > u0) --c0;
+        while (c1 + 1 < G && unit_begin(a.total, c1 + 1, G) <= u1) ++c1;
+        while (c1 > 0 && unit_begin(a.total, c1, G) > u1) --c1;
+        if (c0 == c1) continue;  // one CTA covered it whole and stored y
+        float v = 0.f;
+        for (int c = c0; c <= c1; ++c) {
+            const int slot01 = unit_begin(a.total, c, G) >= u0 ? 0 : 1;
+            v = c == c0 ? a.part[(((long long)c * 2 + slot01) * tp + tt) * BM + r]
+                        : __fadd_rn(v, a.part[(((long long)c * 2 + slot01) * tp + tt) * BM + r]);
+        }
+        if (a.bias) v = __fadd_rn(v, a.bias[o]);
+        a.y[(long long)tt * a.out + o] = v;
+    }
+}
+
+int tp_for(int T) { return T <= 8 ? 8 : (T <= 16 ? 16 : 32); }
+
+int grid_for(long long total, int sm_count) {
+    long long g = (total + kMinBlocksPerCta - 1) / kMinBlocksPerCta;
+    if (g > sm_count) g = sm_count;
+    return g < 1 ? 1 : (int)g;
+}
+
+size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
+
+template <int F, int TP>
+cudaError_t launch_t(const uint8_t* w, const float* x, float* y, int out, int in, int T, const float* bias,
+                     void* ws, int sm_count, int* err, cudaStream_t stream) {
+    using C = BCfg<F, TP>;
+    const int kb = in / kQK;
+    char* p = static_cast<char*>(ws);
+    __half* xb = reinterpret_cast<__half*>(p);
+    p += align256((size_t)2 * TP * in * sizeof(__half));
+    float* sc = reinterpret_cast<float*>(p);
+    p += align256((size_t)kb * TP * sizeof(float));
+    float* xsum = nullptr;
+    if (F == kQ4_1) {
+        xsum = reinterpret_cast<float*>(p);
+        p += align256((size_t)kb * TP * sizeof(float));
+    }
+    float* part = reinterpret_cast<float*>(p);
+
+    const long long warps = (long long)kb * TP;
+    bgemm_xsplit_kernel<TP><<<(int)((warps * 32 + 255) / 256), 256, 0, stream>>>(x, T, in, kb, xb, sc, xsum);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+
+    const long long row_bytes = (long long)kb * C::BS;
+    CUtensorMap mw, mx;
+    if (!make_map_2d(&mw, F == kQ8_0 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8,
+                     const_cast<uint8_t*>(w), (uint64_t)(row_bytes / C::W_ESZ), (uint64_t)out, (uint64_t)row_bytes,
+                     (uint32_t)(C::W_ROW / C::W_ESZ), BM, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !make_map_2d(&mx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xb, (uint64_t)in, (uint64_t)(2 * TP), (uint64_t)in * 2, 64,
+                     (uint32_t)(2 * TP), CU_TENSOR_MAP_SWIZZLE_128B))
+        return cudaErrorInvalidValue;
+
+    static std::atomic<bool> attr_set[64];  // one value per instantiation: racing first calls agree
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 64 || !attr_set[dev].load(std::memory_order_acquire)) {
+        e = cudaFuncSetAttribute(bgemm_kernel<F, TP>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+        if (e != cudaSuccess) return e;
+        if (dev < 64) attr_set[dev].store(true, std::memory_order_release);
+    }
+    BgemmArgs a{};
+    a.y = y;
+    a.bias = bias;
+    a.sc = sc;
+    a.xsum = xsum;
+    a.part = part;
+    a.out = out;
+    a.in = in;
+    a.T = T;
+    a.kb = kb;
+    a.total = (long long)((out + BM - 1) / BM) * kb;
+    a.err = err;
+    const int G = grid_for(a.total, sm_count);
+    bgemm_kernel<F, TP><<<G, kThreads, C::SMEM, stream>>>(mw, mx, a);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    const long long n = (long long)((out + BM - 1) / BM) * T * BM;
+    const long long nb = (n + 255) / 256;
+    bgemm_fixup_kernel<<<(int)(nb < 4 * sm_count ? nb : 4 * sm_count), 256, 0, stream>>>(a, TP, G);
+    return cudaGetLastError();
+}
+
+template <int F>
+cudaError_t launch_f(const uint8_t* w, const float* x, float* y, int out, int in, int T, const float* bias, void* ws,
+                     int sm_count, int* err, cudaStream_t stream) {
+    switch (tp_for(T)) {
+        case 8: return launch_t<F, 8>(w, x, y, out, in, T, bias, ws, sm_count, err, stream);
+        case 16: return launch_t<F, 16>(w, x, y, out, in, T, bias, ws, sm_count, err, stream);
+        default: return launch_t<F, 32>(w, x, y, out, in, T, bias, ws, sm_count, err, stream);
+    }
+}
+
+}  // namespace
+
+bool bgemm_shape_ok(int fmt, const void* w, int out, int in, int rows) {
+    const long long row_bytes = (long long)((in + kQK - 1) / kQK) * block_bytes(fmt);
+    return rows >= MLQ_BGEMM_MIN_ROWS && rows <= kBgemmMaxRows && out > 0 && in % kQK == 0 &&
+           reinterpret_cast<uintptr_t>(w) % 16 == 0 && row_bytes % 16 == 0;
+}
+
+size_t bgemm_workspace_bytes(int fmt, int in, int rows, int out, int sm_count) {
+    const int tp = tp_for(rows);
+    const int kb = in / kQK;
+    const long long total = (long long)((out + BM - 1) / BM) * kb;
+    const int G = grid_for(total, sm_count);
+    size_t b = align256((size_t)2 * tp * in * 2) + align256((size_t)kb * tp * 4);
+    if (fmt == kQ4_1) b += align256((size_t)kb * tp * 4);
+    return b + (size_t)G * 2 * tp * BM * 4;
+}
+
+cudaError_t launch_bgemm(int fmt, const uint8_t* w, const float* x, float* y, int out, int in, int rows,
+                         const float* bias, void* ws, int sm_count, int* err, cudaStream_t stream) {
+    switch (fmt) {
+        case kQ8_0: return launch_f<kQ8_0>(w, x, y, out, in, rows, bias, ws, sm_count, err, stream);
+        case kQ4_0: return launch_f<kQ4_0>(w, x, y, out, in, rows, bias, ws, sm_count, err, stream);
+        case kQ4_1: return launch_f<kQ4_1>(w, x, y, out, in, rows, bias, ws, sm_count, err, stream);
+    }
+    return cudaErrorInvalidValue;
+}
+
+}  // namespace mlq

@@ -5,6 +5,8 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include "mlq.h"
+
 namespace mlq {
 
 // Arguments of the streaming GEMV (mlq_gemv.cu).
@@ -91,6 +93,22 @@ size_t gemm_workspace_bytes(int in, int rows, int out, int split);
 // gemm_workspace_bytes(in, rows, out, split) bytes.
 cudaError_t launch_gemm(int fmt, const uint8_t* w, const float* x, float* y, int out, int in, int rows,
                         const float* bias, void* ws, int split, int sm_count, int* err, cudaStream_t stream);
+
+// Batched-decode GEMM (mlq_bgemm.cu): 2..kBgemmMaxRows rows of x on the
+// tensor cores with exact fp16 weight codes and per-block fp32 folds.
+constexpr int kBgemmMaxRows = MLQ_BGEMM_MAX_ROWS;
+
+// Host-value conditions of the batched-decode GEMM: 2 <= rows <= 32,
+// in % 32 == 0, 16-B aligned weights with a 16-B multiple row pitch.
+bool bgemm_shape_ok(int fmt, const void* w, int out, int in, int rows);
+
+// Workspace of one launch: x split (fp16 hi/lo), block scales (and q4_1
+// block sums), and the split row tiles' partial sums.
+size_t bgemm_workspace_bytes(int fmt, int in, int rows, int out, int sm_count);
+
+// y[rows][out] = x W^T (+ bias); ws holds bgemm_workspace_bytes(...) bytes.
+cudaError_t launch_bgemm(int fmt, const uint8_t* w, const float* x, float* y, int out, int in, int rows,
+                         const float* bias, void* ws, int sm_count, int* err, cudaStream_t stream);
 
 // Quantize fp32 [rows][cols] -> blocks, reference rules (mlq_convert.cu).
 cudaError_t launch_quantize(int fmt, const float* src, long long rows, int cols, uint8_t* blocks,

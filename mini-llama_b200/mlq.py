@@ -213,6 +213,16 @@ GEMM_LARGE_MIN_ROWS = 5
 GEMM_LARGE_MIN_WEIGHTS = 1 << 25
 
 
+BGEMM_MIN_ROWS = 2
+BGEMM_MAX_ROWS = 32
+
+
+def takes_bgemm(rows: int, out_features: int, in_features: int) -> bool:
+    """Whether an aligned call takes the batched-decode GEMM (include/mlq.h:
+    MLQ_BGEMM_MIN_ROWS..MLQ_BGEMM_MAX_ROWS rows, in_features % 32 == 0)."""
+    return BGEMM_MIN_ROWS <= rows <= BGEMM_MAX_ROWS and in_features % 32 == 0
+
+
 def takes_gemm(rows: int, out_features: int, in_features: int) -> bool:
     """MLQ_GEMM_ROWS_RULE of include/mlq.h: the row/size part of the routing
     between the tensor-core GEMM and the streaming GEMV."""

@@ -158,40 +158,40 @@ def test_gemm_routing_rule_matches_header(pkg, tmp_path):
 
 def test_noalloc_range_rule_before_any_cuda_call(pkg):
     """mlq_linear_noalloc rejects, before any CUDA call, exactly the calls
-    that take the GEMM (MLQ_GEMM_ROWS_RULE) with an x split above the static
-    scratch: 9 rows on any matrix, 5 rows on a matrix of >= 2^25 weights.
+    that take the bf16 tensor-core GEMM (MLQ_GEMM_ROWS_RULE, not taken by the
+    batched-decode GEMM) with an x split above the static scratch.
     (Pointers are fake: a rejected call never touches them.)"""
     mlq = pkg.mlq
     lib = mlq.lib()
     scratch = mlq.NOALLOC_SCRATCH_BYTES
 
-    def status(rows, out_f, in_f):
+    def status(fmt, rows, out_f, in_f, w=0x1000):
         nb = mlq.block_count(out_f, in_f)
-        return lib.mlq_linear_noalloc(8, 0x1000, nb, out_f, in_f, 0x2000, rows, 0x3000, None)
+        return lib.mlq_linear_noalloc(fmt, w, nb, out_f, in_f, 0x2000, rows, 0x3000, None)
 
-    # 5 rows of x exceed the scratch; a multiple of 256 values, so q8_0 rows
-    # have a 16-B multiple pitch (a GEMM condition)
-    in_f = (scratch // (4 * 5) // 256 + 1) * 256
-    assert mlq.takes_gemm(9, 32, in_f) and 9 * in_f * 4 > scratch
-    assert status(9, 32, in_f) == 9
+    # 33 rows (above the batched-decode GEMM's 32) whose x split exceeds the
+    # scratch; a multiple of 256 values, so q8_0 rows have a 16-B multiple pitch
+    in_f = (scratch // (4 * 33) // 256 + 1) * 256
+    assert mlq.takes_gemm(33, 32, in_f) and not mlq.takes_bgemm(33, 32, in_f)
+    assert status(8, 33, 32, in_f) == 9
     assert b"static scratch" in lib.mlq_last_error()
-    big_out = -(-mlq.GEMM_LARGE_MIN_WEIGHTS // in_f)  # out * in >= 2^25
-    assert mlq.takes_gemm(5, big_out, in_f) and status(5, big_out, in_f) == 9
-    assert not mlq.takes_gemm(5, 32, in_f)  # a small matrix at 5 rows streams: no scratch needed
-    # Calls the GEMM cannot take (weights not 16-B aligned, or in % 8 != 0)
-    # stream through the GEMV, which needs no scratch: never MLQ_ERR_RANGE,
-    # whatever the size of x.  These calls pass the host checks and go on to
-    # CUDA, so they run only where there is no GPU to reach (the pointers
-    # are fake); there the first CUDA call fails with MLQ_ERR_CUDA.
+    # 9 rows with in % 32 == 16 (q4_1, 16-B row pitch): the bf16 GEMM, rejected
+    in_q41 = 14568 * 32 - 16
+    assert not mlq.takes_bgemm(9, 32, in_q41) and 9 * in_q41 * 4 > scratch
+    assert status(3, 9, 32, in_q41) == 9
+    # Calls no GEMM with this limit takes stream through the GEMV or run the
+    # batched-decode GEMM (which falls back to the GEMV when its scratch does
+    # not fit): never MLQ_ERR_RANGE.  These calls pass the host checks and go
+    # on to CUDA, so they run only where there is no GPU to reach (the
+    # pointers are fake); there the first CUDA call fails with MLQ_ERR_CUDA.
     import torch
     if torch.cuda.is_available():
         return
-    nb = mlq.block_count(32, in_f)
-    assert lib.mlq_linear_noalloc(8, 0x1002, nb, 32, in_f, 0x2000, 9, 0x3000, None) != 9
+    assert status(8, 9, 32, in_f) != 9            # batched-decode GEMM rows
+    assert status(8, 33, 32, in_f, w=0x1002) != 9  # weights not 16-B aligned
     odd_in = in_f + 4  # in % 8 == 4
-    assert odd_in % 8 == 4 and mlq.takes_gemm(9, 32, odd_in)
-    assert lib.mlq_linear_noalloc(8, 0x1000, mlq.block_count(32, odd_in), 32, odd_in, 0x2000, 9,
-                                  0x3000, None) != 9
+    assert odd_in % 8 == 4 and mlq.takes_gemm(33, 32, odd_in)
+    assert status(8, 33, 32, odd_in) != 9
 
 
 def test_batch_structs_match_header(pkg, tmp_path):
