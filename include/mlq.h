@@ -342,6 +342,56 @@ MLQ_API mlq_status mlq_peer_open(const mlq_ipc_handle* handle, void** ptr);
 MLQ_API mlq_status mlq_peer_close(void* ptr);
 MLQ_API mlq_status mlq_peer_free(void* ptr);
 
+/* ---------------------------------------------------------------------------
+ * GGUF ingestion: quantized blocks from a GGUF (v3) file straight to device
+ * memory.  Replaces GgufReader::load (src/gguf.cc:396-575),
+ * readGgufTensorRaw (src/gguf.cc:614-662) and loadQuantizedTensor
+ * (src/gguf_loader.cc:118-196), which read every tensor into host vectors
+ * before the upload.  The parser makes the reference's checks (magic,
+ * version 3, entry limits, repeated keys or names, 1..8 non-zero dims,
+ * general.alignment a power of two <= 1 MiB, whole blocks, tensor data
+ * inside the file) and fails with MLQ_ERR_FORMAT / MLQ_ERR_RANGE and a
+ * message (mlq_last_error).  A 2-D tensor of dims {in, out} (fastest first,
+ * as stored) is the reference's [out, in] matrix: `rows` = out, `row_bytes`
+ * = ceil(in / 32) blocks; a row range is a contiguous byte range of the
+ * file, so a rank of a row-sharded model reads only its own rows.
+ * ------------------------------------------------------------------------- */
+typedef struct mlq_gguf mlq_gguf; /* an open file: header, metadata, tensor table */
+
+typedef struct mlq_gguf_tensor {
+    const char* name;   /* valid until mlq_gguf_close */
+    int n_dims;
+    uint64_t dims[8];   /* fastest first */
+    uint32_t type;      /* ggml type: 0 f32, 1 f16, 2 q4_0, 3 q4_1, 8 q8_0 (others: nbytes 0) */
+    uint64_t offset;    /* from the start of the data section */
+    uint64_t nbytes;    /* bytes of data */
+    uint64_t rows;      /* product of dims[1..] */
+    uint64_t row_bytes; /* nbytes / rows */
+} mlq_gguf_tensor;
+
+MLQ_API mlq_status mlq_gguf_open(const char* path, mlq_gguf** file);
+MLQ_API void mlq_gguf_close(mlq_gguf* file);
+MLQ_API int64_t mlq_gguf_tensor_count(const mlq_gguf* file);
+/* Absolute file offset of the data section (aligned to general.alignment). */
+MLQ_API uint64_t mlq_gguf_data_offset(const mlq_gguf* file);
+/* Index of the tensor named `name`, or -1. */
+MLQ_API int64_t mlq_gguf_find(const mlq_gguf* file, const char* name);
+MLQ_API mlq_status mlq_gguf_tensor_info(const mlq_gguf* file, int64_t index, mlq_gguf_tensor* info);
+/* A scalar metadata value (integer types, bool; float types for _float). */
+MLQ_API mlq_status mlq_gguf_metadata_int(const mlq_gguf* file, const char* key, int64_t* value);
+MLQ_API mlq_status mlq_gguf_metadata_float(const mlq_gguf* file, const char* key, double* value);
+
+/* Rows [row_begin, row_end) of tensor `index` -- (row_end - row_begin) *
+ * row_bytes bytes, byte-identical to the file -- into device memory `dst`
+ * (dst_bytes at least that) on `device`, through two pinned 8 MiB staging
+ * buffers per host thread (a read overlaps the previous chunk's copy);
+ * returns after the copy has landed.  For a quantized matrix the result is
+ * what mlq_linear takes as w (the shard of mlq_linear_allgather for a row
+ * range). */
+MLQ_API mlq_status mlq_gguf_upload_rows(const mlq_gguf* file, int64_t index, int64_t row_begin,
+                                        int64_t row_end, void* dst, size_t dst_bytes, int device,
+                                        mlq_stream stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

@@ -460,6 +460,8 @@ mlq_status run_op(const mlq_linear_op& op, const float* x, float* y, cudaStream_
 
 }  // namespace
 
+void mlq::set_last_error(const char* msg) { t_last_error = msg ? msg : ""; }
+
 extern "C" {
 
 MLQ_API int mlq_built(void) { return 1; }

@@ -5,6 +5,8 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <string>
+
 #include "mlq.h"
 
 namespace mlq {
@@ -50,6 +52,10 @@ int gemv_tokens_per_pass(int rows_left);
 // memory each).  Needs no workspace.
 cudaError_t launch_gemv_stream(int fmt, const GemvArgs& args, int mt, int sm_count,
                                int smem_per_sm, cudaStream_t stream);
+
+// Sets the message mlq_last_error() returns on this host thread.
+void set_last_error(const char* msg);
+inline void set_last_error(const std::string& msg) { set_last_error(msg.c_str()); }
 
 // Zeroes the streaming GEMV's dynamic tile-queue ring of the current device
 // (called after a kernel reported an error, the device synchronised).

@@ -376,3 +376,91 @@ class Batch:
     def run_host(self, device: int = 0, stream=None) -> None:
         check(lib().mlq_linear_batch_host(self.arr, self.n, device,
                                           None if stream is None else _stream_handle(stream)))
+
+
+# ---------------------------------------------------------------------------
+# GGUF ingestion (mlq_gguf_*)
+# ---------------------------------------------------------------------------
+class GgufTensor(ctypes.Structure):
+    """struct mlq_gguf_tensor (include/mlq.h)."""
+    _fields_ = [("name", ctypes.c_char_p), ("n_dims", ctypes.c_int), ("dims", ctypes.c_uint64 * 8),
+                ("type", ctypes.c_uint32), ("offset", ctypes.c_uint64), ("nbytes", ctypes.c_uint64),
+                ("rows", ctypes.c_uint64), ("row_bytes", ctypes.c_uint64)]
+
+
+def _gguf_lib():
+    L = lib()
+    if not getattr(L, "_gguf_ready", False):
+        L.mlq_gguf_open.argtypes = [ctypes.c_char_p, ctypes.POINTER(_vp)]
+        L.mlq_gguf_open.restype = _i
+        L.mlq_gguf_close.argtypes = [_vp]
+        L.mlq_gguf_close.restype = None
+        L.mlq_gguf_tensor_count.argtypes = [_vp]
+        L.mlq_gguf_tensor_count.restype = ctypes.c_int64
+        L.mlq_gguf_data_offset.argtypes = [_vp]
+        L.mlq_gguf_data_offset.restype = ctypes.c_uint64
+        L.mlq_gguf_find.argtypes = [_vp, ctypes.c_char_p]
+        L.mlq_gguf_find.restype = ctypes.c_int64
+        L.mlq_gguf_tensor_info.argtypes = [_vp, ctypes.c_int64, ctypes.POINTER(GgufTensor)]
+        L.mlq_gguf_tensor_info.restype = _i
+        L.mlq_gguf_metadata_int.argtypes = [_vp, ctypes.c_char_p, ctypes.POINTER(ctypes.c_int64)]
+        L.mlq_gguf_metadata_int.restype = _i
+        L.mlq_gguf_metadata_float.argtypes = [_vp, ctypes.c_char_p, ctypes.POINTER(ctypes.c_double)]
+        L.mlq_gguf_metadata_float.restype = _i
+        L.mlq_gguf_upload_rows.argtypes = [_vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _vp, _sz, _i, _vp]
+        L.mlq_gguf_upload_rows.restype = _i
+        L._gguf_ready = True
+    return L
+
+
+class GgufFile:
+    """An open GGUF file (mlq_gguf_open); tensors() lists its table."""
+
+    def __init__(self, path):
+        L = _gguf_lib()
+        h = _vp()
+        check(L.mlq_gguf_open(str(path).encode(), ctypes.byref(h)))
+        self.h = h
+
+    def close(self) -> None:
+        if self.h:
+            _gguf_lib().mlq_gguf_close(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    @property
+    def data_offset(self) -> int:
+        return int(_gguf_lib().mlq_gguf_data_offset(self.h))
+
+    def info(self, index: int) -> dict:
+        t = GgufTensor()
+        check(_gguf_lib().mlq_gguf_tensor_info(self.h, index, ctypes.byref(t)))
+        return {"name": t.name.decode(), "dims": [int(t.dims[d]) for d in range(t.n_dims)], "type": int(t.type),
+                "offset": int(t.offset), "nbytes": int(t.nbytes), "rows": int(t.rows),
+                "row_bytes": int(t.row_bytes)}
+
+    def tensors(self) -> list:
+        return [self.info(i) for i in range(int(_gguf_lib().mlq_gguf_tensor_count(self.h)))]
+
+    def find(self, name: str) -> int:
+        return int(_gguf_lib().mlq_gguf_find(self.h, name.encode()))
+
+    def metadata_int(self, key: str) -> int:
+        v = ctypes.c_int64()
+        check(_gguf_lib().mlq_gguf_metadata_int(self.h, key.encode(), ctypes.byref(v)))
+        return int(v.value)
+
+    def metadata_float(self, key: str) -> float:
+        v = ctypes.c_double()
+        check(_gguf_lib().mlq_gguf_metadata_float(self.h, key.encode(), ctypes.byref(v)))
+        return float(v.value)
+
+    def upload_rows(self, index: int, row_begin: int, row_end: int, dst_ptr: int, dst_bytes: int,
+                    device: int = 0, stream=None) -> None:
+        check(_gguf_lib().mlq_gguf_upload_rows(self.h, index, row_begin, row_end, dst_ptr, dst_bytes, device,
+                                               None if stream is None else _stream_handle(stream)))

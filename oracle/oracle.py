@@ -227,3 +227,57 @@ class Reference:
                                       _fp(y))
         assert rc == 0, rc
         return y
+
+
+class ReferenceGguf:
+    """The reference's own GGUF reader (src/gguf.cc), compiled here into
+    oracle/_ref/libref_gguf.so behind oracle/ref/ref_gguf.cc."""
+
+    PATH = REF_DIR / "libref_gguf.so"
+
+    def __init__(self) -> None:
+        if not self.PATH.exists():
+            raise FileNotFoundError(f"{self.PATH} was not built (make -C oracle gguf)")
+        lib = ctypes.CDLL(str(self.PATH))
+        lib.ref_gguf_open.argtypes = [ctypes.c_char_p]
+        lib.ref_gguf_open.restype = ctypes.c_void_p
+        lib.ref_gguf_ok.argtypes = [ctypes.c_void_p]
+        lib.ref_gguf_error.argtypes = [ctypes.c_void_p]
+        lib.ref_gguf_error.restype = ctypes.c_char_p
+        lib.ref_gguf_data_offset.argtypes = [ctypes.c_void_p]
+        lib.ref_gguf_data_offset.restype = ctypes.c_uint64
+        lib.ref_gguf_count.argtypes = [ctypes.c_void_p]
+        lib.ref_gguf_count.restype = ctypes.c_int64
+        lib.ref_gguf_tensor.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_char_p, ctypes.c_int,
+                                        ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint32),
+                                        ctypes.POINTER(ctypes.c_uint64)]
+        lib.ref_gguf_read.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_uint64]
+        lib.ref_gguf_read.restype = ctypes.c_uint64
+        lib.ref_gguf_free.argtypes = [ctypes.c_void_p]
+        self.lib = lib
+
+    @classmethod
+    def available(cls) -> bool:
+        return cls.PATH.exists()
+
+    def load(self, path):
+        """(ok, error, data_offset, [tensor dicts], {index: bytes})."""
+        L = self.lib
+        h = L.ref_gguf_open(str(path).encode())
+        try:
+            if not L.ref_gguf_ok(h):
+                return False, L.ref_gguf_error(h).decode(), 0, [], {}
+            tensors, data = [], {}
+            for i in range(L.ref_gguf_count(h)):
+                name = ctypes.create_string_buffer(512)
+                dims = (ctypes.c_uint64 * 8)()
+                t, off = ctypes.c_uint32(), ctypes.c_uint64()
+                nd = L.ref_gguf_tensor(h, i, name, 512, dims, ctypes.byref(t), ctypes.byref(off))
+                tensors.append({"name": name.value.decode(), "dims": [int(dims[d]) for d in range(nd)],
+                                "type": int(t.value), "offset": int(off.value)})
+                buf = np.empty(1 << 24, np.uint8)
+                n = L.ref_gguf_read(h, i, buf.ctypes.data, buf.size)
+                data[i] = bytes(buf[:n])
+            return True, "", int(L.ref_gguf_data_offset(h)), tensors, data
+        finally:
+            L.ref_gguf_free(h)
