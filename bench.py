@@ -678,6 +678,54 @@ def _e2e(ctx, st, steps):
                     "one stream synchronisation per step"}
 
 
+def ref_gpu_baseline(ctx, wl, steps):
+    """The REFERENCE's own CUDA kernels (q80/q40/q41LinearKernel of
+    src/cuda_quant.cu, compiled for sm_100a into oracle/_ref/libref_gpu.so)
+    timed on this GPU on the same workload: the same seeded weights
+    (quantized on the device) and x, each step one launch per matrix with
+    the reference's own grid, CUDA events around the steps.  Also the
+    largest relative L2 difference of an output row between the reference's
+    kernel and this library on the last matrix (a cross-check on identical
+    device inputs)."""
+    torch, mlq, pkg = ctx.torch, ctx.mlq, ctx.pkg
+    sys.path.insert(0, str(ROOT))
+    try:
+        from oracle.oracle import ReferenceGpu  # baseline only, never the measured path
+        ref = ReferenceGpu()
+    except (FileNotFoundError, OSError) as e:
+        return {"unavailable": str(e)}
+    fmt, rows = wl["fmt"], wl["rows"]
+    s = ctx.stream.cuda_stream
+    mats = []
+    for i, (name, out_f, in_f) in enumerate(wl["matrices"]):
+        w32 = pkg.synth.normal_torch((out_f, in_f), seed=1000 + i, std=0.02, device=ctx.device)
+        w = mlq.quantize(fmt, w32)
+        del w32
+        x = torch.from_numpy(pkg.synth.normal((rows, in_f), seed=2000 + i)).to(ctx.device)
+        y = torch.empty((rows, out_f), device=ctx.device)
+        mats.append((name, out_f, in_f, w, x, y))
+    torch.cuda.empty_cache()
+
+    def step():
+        for name, out_f, in_f, w, x, y in mats:
+            ref.linear(fmt, x.data_ptr(), w.data_ptr(), y.data_ptr(), rows, in_f, out_f, s)
+
+    step()
+    k = max(3, min(steps, 10))
+    ms = ctx.timed(lambda: [step() for _ in range(k)]) / k
+    bytes_step = sum(weight_bytes(fmt, o, i) for _, o, i in wl["matrices"])
+    name, out_f, in_f, w, x, y = mats[-1]
+    mine = mlq.linear(fmt, w, out_f, in_f, x)
+    torch.cuda.synchronize(ctx.device)
+    diff = (torch.linalg.norm((mine - y).double(), dim=1) / torch.linalg.norm(y.double(), dim=1).clamp_min(1e-30)).max()
+    out = {"value": round(bytes_step / (ms / 1e3) / 1e9, 2), "unit": UNIT, "ms_per_step": round(ms, 4),
+           "steps": k, "kernels": f"reference q{fmt[1]}{fmt[3]}LinearKernel, src/cuda_quant.cu (sm_100a build)",
+           "max_rel_l2_vs_this_library": float(diff)}
+    del mats, mine
+    torch.cuda.empty_cache()
+    return out
+
+
 def formats_probe(ctx):
     """Decode (batch 1) weight GB/s of one large matrix per format, launches
     back to back, against the measured HBM peak: q8_0 and q4_1 at the
@@ -724,8 +772,9 @@ def run_mlq(args):
                            **({"parity_max_rel_l2": r["parity_max_rel_l2"]} if "parity_max_rel_l2" in r else {})}
         if ctx.world == 1:
             formats = formats_probe(ctx)
-    cpu = None
-    if ctx.rank == 0 and ctx.world == 1 and not args.no_cpu_baseline and not args.only:
+    cpu = refgpu = None
+    if ctx.world == 1 and not args.no_cpu_baseline and not args.only:
+        refgpu = ref_gpu_baseline(ctx, wl, args.steps)
         cpu = reference_cpu_baseline(ctx.pkg, wl, args.cpu_seconds)
     parity = [v.get("parity_max_rel_l2") for v in [head, *extra.values()] if "parity_max_rel_l2" in v]
     dev_err = ctx.mlq.device_error(ctx.local)  # any kernel of the whole run that gave up
@@ -737,7 +786,7 @@ def run_mlq(args):
             "dtype": f"fp32 activations x {wl['fmt']} weights",
             "data": f"synthetic (seeded N(0,0.02) weights quantized to {wl['fmt']}; N(0,1) x)",
             "config": config_of(wl, ctx.world),
-            "roofline": head["roofline"], "cpu_baseline": cpu, "e2e": head.get("e2e"),
+            "roofline": head["roofline"], "cpu_baseline": cpu, "ref_gpu_baseline": refgpu, "e2e": head.get("e2e"),
             "gpu_launches": args.steps * head["gpu_launches_per_step"],
             "clocks": head["clocks"], "device_error": dev_err,
         }

@@ -281,3 +281,30 @@ class ReferenceGguf:
             return True, "", int(L.ref_gguf_data_offset(h)), tensors, data
         finally:
             L.ref_gguf_free(h)
+
+
+class ReferenceGpu:
+    """The reference's own CUDA quant kernels (src/cuda_quant.cu,
+    q80/q40/q41LinearKernel) built for sm_100a into oracle/_ref/libref_gpu.so
+    behind oracle/ref/ref_gpu.cu; launched on caller-provided device memory."""
+
+    PATH = REF_DIR / "libref_gpu.so"
+
+    def __init__(self) -> None:
+        if not self.PATH.exists():
+            raise FileNotFoundError(f"{self.PATH} was not built (make -C oracle refgpu)")
+        lib = ctypes.CDLL(str(self.PATH))
+        lib.refgpu_linear.argtypes = [ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
+                                      ctypes.c_int, ctypes.c_int, ctypes.c_void_p]
+        lib.refgpu_linear.restype = ctypes.c_int
+        self.lib = lib
+
+    @classmethod
+    def available(cls) -> bool:
+        return cls.PATH.exists()
+
+    def linear(self, fmt: str, x_ptr: int, w_ptr: int, y_ptr: int, rows: int, in_f: int, out_f: int,
+               stream: int | None) -> None:
+        st = self.lib.refgpu_linear(FMT_IDS[fmt], x_ptr, w_ptr, y_ptr, rows, in_f, out_f, stream)
+        if st != 0:
+            raise RuntimeError(f"reference kernel launch failed ({st})")
