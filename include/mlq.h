@@ -242,6 +242,32 @@ MLQ_API mlq_status mlq_dequantize(mlq_format fmt, const void* w, size_t block_co
 MLQ_API mlq_status mlq_quantize(mlq_format fmt, const float* src, int rows, int cols,
                                 void* blocks, mlq_stream stream);
 
+/* Tensor of `src_type` (0 = fp32 values [rows][cols], or a block format)
+ * -> blocks of `dst_fmt`, on the device.  Replaces the reference's
+ * quantizeQtToQ80 / quantizeQtToQ40 (src/model.cc:94-149): fp32 input is
+ * quantized as mlq_quantize does; block input is dequantized and
+ * re-quantized per block in registers, bit-identical to the reference's
+ * quantizedTensorToF32 followed by quantizeTo*; a tensor already in the
+ * target format is copied unchanged (the reference leaves it as is).
+ * q4_1 targets use this library's q4_1 rule (see mlq_quantize). */
+MLQ_API mlq_status mlq_transcode(int src_type, const void* src, mlq_format dst_fmt, void* dst,
+                                 int rows, int cols, mlq_stream stream);
+
+/* One tensor of a model-level pass. */
+typedef struct mlq_quantize_op {
+    int src_type;      /* 0 = fp32, or a block format */
+    const void* src;   /* device */
+    int dst_fmt;       /* mlq_format */
+    void* dst;         /* device: rows * ceil(cols/32) blocks */
+    int rows, cols;
+} mlq_quantize_op;
+
+/* A whole model's linear weights in one call, in list order on `stream`
+ * (every op validated first): the device form of quantizeModelToQ80 /
+ * quantizeModelToQ40 (src/model.cc:110-149), which loop over lm_head and
+ * every layer's wq, wk, wv, wo, w_gate, w_up, w_down on the host. */
+MLQ_API mlq_status mlq_quantize_model(const mlq_quantize_op* ops, int n, mlq_stream stream);
+
 /* ---------------------------------------------------------------------------
  * Row-sharded linear with the all-gather fused into the kernel
  * (one process per GPU, peers reachable over NVLink)

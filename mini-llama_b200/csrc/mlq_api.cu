@@ -688,6 +688,57 @@ MLQ_API mlq_status mlq_quantize(mlq_format fmt, const float* src, int rows, int 
     }
 }
 
+MLQ_API mlq_status mlq_transcode(int src_type, const void* src, mlq_format dst_fmt, void* dst, int rows, int cols,
+                                 mlq_stream stream) {
+    try {
+        const char* who = "mlq_transcode";
+        if (src_type != 0 && !known_format(src_type))
+            return fail(MLQ_ERR_FORMAT, std::string(who) + ": source type must be 0 (fp32) or a block format");
+        if (!known_format(dst_fmt)) return fail(MLQ_ERR_FORMAT, std::string(who) + ": unknown block format");
+        if (rows <= 0 || cols <= 0) return fail(MLQ_ERR_EMPTY, std::string(who) + ": empty tensors are not supported");
+        if (!src || !dst) return fail(MLQ_ERR_NULL, std::string(who) + ": null pointer");
+        cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+        cudaError_t e;
+        if (src_type == 0) {
+            e = mlq::launch_quantize(dst_fmt, static_cast<const float*>(src), rows, cols, static_cast<uint8_t*>(dst), s);
+        } else if (src_type == (int)dst_fmt) {
+            // the reference leaves a tensor already in the target format untouched
+            e = cudaMemcpyAsync(dst, src, mlq_block_count(rows, cols) * mlq::block_bytes(dst_fmt),
+                                cudaMemcpyDeviceToDevice, s);
+        } else {
+            e = mlq::launch_transcode(src_type, static_cast<const uint8_t*>(src), dst_fmt, static_cast<uint8_t*>(dst),
+                                      rows, cols, s);
+        }
+        return e == cudaSuccess ? MLQ_OK : fail_cuda("transcode", e);
+    } catch (...) {
+        return fail(MLQ_ERR_CUDA, "mlq_transcode: host exception");
+    }
+}
+
+MLQ_API mlq_status mlq_quantize_model(const mlq_quantize_op* ops, int n, mlq_stream stream) {
+    try {
+        if (n < 0) return fail(MLQ_ERR_EMPTY, "mlq_quantize_model: negative op count");
+        if (n > 0 && !ops) return fail(MLQ_ERR_NULL, "mlq_quantize_model: null op list");
+        for (int i = 0; i < n; ++i) {
+            const mlq_quantize_op& o = ops[i];
+            const std::string who = "mlq_quantize_model op " + std::to_string(i);
+            if (o.src_type != 0 && !known_format(o.src_type))
+                return fail(MLQ_ERR_FORMAT, who + ": source type must be 0 (fp32) or a block format");
+            if (!known_format(o.dst_fmt)) return fail(MLQ_ERR_FORMAT, who + ": unknown block format");
+            if (o.rows <= 0 || o.cols <= 0) return fail(MLQ_ERR_EMPTY, who + ": empty tensors are not supported");
+            if (!o.src || !o.dst) return fail(MLQ_ERR_NULL, who + ": null pointer");
+        }
+        for (int i = 0; i < n; ++i) {
+            mlq_status st = mlq_transcode(ops[i].src_type, ops[i].src, (mlq_format)ops[i].dst_fmt, ops[i].dst,
+                                          ops[i].rows, ops[i].cols, stream);
+            if (st != MLQ_OK) return st;
+        }
+        return MLQ_OK;
+    } catch (...) {
+        return fail(MLQ_ERR_CUDA, "mlq_quantize_model: host exception");
+    }
+}
+
 MLQ_API size_t mlq_flag_bytes(void) { return kFlagBytes; }
 
 MLQ_API mlq_status mlq_linear_allgather(mlq_format fmt, const void* w_shard,

@@ -300,6 +300,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 return false;
             }
             const uint32_t wrow = w_st(cs) + (uint32_t)(row * C::W_ROW);
+#pragma unroll
             for (int j = 0; j < SPC; ++j) {
                 const int k0 = c * BPC + 2 * j;
                 const bool v0 = k0 >= b_lo && k0 < b_hi, v1 = k0 + 1 >= b_lo && k0 + 1 < b_hi;
@@ -310,11 +311,28 @@ __global__ void __launch_bounds__(kThreads, 1)
                     return false;
                 }
                 if (aborted()) return false;
-                // the stage's two blocks: 2 BS bytes from a word boundary
+                // the stage's two blocks: 2 BS bytes from byte j * 2 BS of the
+                // row's chunk (a word boundary), read as the 16-B units that
+                // cover them (rows are 17 / 9 / 10 units apart: the 8 lanes of
+                // a load phase hit distinct bank groups)
                 constexpr int NW = 2 * C::BS / 4;
+                const int sb = j * 2 * C::BS;
+                const int sh = (sb % 16) / 4;                 // words before the stage in its first unit
+                const int nu = (sh * 4 + 2 * C::BS + 15) / 16;
+                uint32_t wb[24];
+#pragma unroll
+                for (int u = 0; u < 6; ++u) {
+                    if (u < nu) {
+                        const uint4 t4 = lds_u4(wrow + (uint32_t)(16 * (sb / 16 + u)));
+                        wb[4 * u] = t4.x;
+                        wb[4 * u + 1] = t4.y;
+                        wb[4 * u + 2] = t4.z;
+                        wb[4 * u + 3] = t4.w;
+                    }
+                }
                 uint32_t w[NW + 1];
 #pragma unroll
-                for (int i = 0; i < NW; ++i) w[i] = lds_u32(wrow + (uint32_t)(j * 2 * C::BS + 4 * i));
+                for (int i = 0; i < NW; ++i) w[i] = wb[i + sh];
                 w[NW] = 0;
                 const uint32_t arow = a_st(as) + (uint32_t)row * 128u;
                 float dm_d[2], dm_m[2];
@@ -413,52 +431,86 @@ __global__ void __launch_bounds__(kThreads, 1)
             last_hi = b_hi;
             const int kbeg = c * BPC > b_lo ? c * BPC : b_lo;
             const int kend = (c + 1) * BPC < b_hi ? (c + 1) * BPC : b_hi;
-            for (int k = kbeg; k < kend; ++k) {
-                const int slot = (int)(bseq % NSLOT);
-                const uint32_t ph = (bseq / NSLOT) & 1u;
-                if (!mbar_wait(smem_u32(&s_full[slot]), ph) || !mbar_wait(smem_u32(&dm_full[slot]), ph)) {
-                    fail(25);
-                    return false;
+            // Blocks two at a time (one at a time for 64-column slots, whose
+            // registers would not fit twice): both accumulators' loads are in
+            // flight before one wait, and the x scales are requested before
+            // the barrier waits so their latency hides behind them.
+            constexpr int PAIR = N <= 32 ? 2 : 1;
+            for (int k = kbeg; k < kend;) {
+                const int nb = (PAIR == 2 && k + 1 < kend) ? 2 : 1;
+                float4 s4[2][TP / 4];
+#pragma unroll
+                for (int h = 0; h < PAIR; ++h) {
+                    if (h < nb) {
+                        const float4* sp = reinterpret_cast<const float4*>(a.sc + (long long)(k + h) * TP);
+#pragma unroll
+                        for (int q = 0; q < TP / 4; ++q) s4[h][q] = __ldg(sp + q);
+                    }
+                }
+                int slot[2];
+#pragma unroll
+                for (int h = 0; h < PAIR; ++h) {
+                    if (h < nb) {
+                        slot[h] = (int)((bseq + h) % NSLOT);
+                        const uint32_t ph = ((bseq + h) / NSLOT) & 1u;
+                        if (!mbar_wait(smem_u32(&s_full[slot[h]]), ph) || !mbar_wait(smem_u32(&dm_full[slot[h]]), ph)) {
+                            fail(25);
+                            return false;
+                        }
+                    }
                 }
                 tc_fence_after();
-                uint32_t v[N];
-                const uint32_t ta = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(slot * N);
-                if constexpr (N == 16) {
-                    tmem_ld16(ta, *reinterpret_cast<uint32_t(*)[16]>(v));
-                } else {
+                uint32_t v[PAIR][N];
+                const uint32_t tq = tmem + ((uint32_t)(quarter * 32) << 16);
 #pragma unroll
-                    for (int q = 0; q < N / 32; ++q)
-                        tmem_ld32(ta + (uint32_t)(32 * q), *reinterpret_cast<uint32_t(*)[32]>(v + 32 * q));
+                for (int h = 0; h < PAIR; ++h) {
+                    if (h < nb) {
+                        const uint32_t ta = tq + (uint32_t)(slot[h] * N);
+                        if constexpr (N == 16) {
+                            tmem_ld16_issue(ta, *reinterpret_cast<uint32_t(*)[16]>(v[h]));
+                        } else {
+#pragma unroll
+                            for (int q = 0; q < N / 32; ++q)
+                                tmem_ld32_issue(ta + (uint32_t)(32 * q), *reinterpret_cast<uint32_t(*)[32]>(v[h] + 32 * q));
+                        }
+                    }
                 }
-                const float2 dm = lds_f2(dm_base + (uint32_t)((slot * BM + row) * 8));
+                tmem_wait_ld(*reinterpret_cast<uint32_t(*)[PAIR * N]>(&v[0][0]));
+                float2 dm[2];
+#pragma unroll
+                for (int h = 0; h < PAIR; ++h)
+                    if (h < nb) dm[h] = lds_f2(dm_base + (uint32_t)((slot[h] * BM + row) * 8));
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(smem_u32(&s_empty[slot]));
-                // x block scales (and sums) of the block: TP values, the same for every lane
-                const float4* sp = reinterpret_cast<const float4*>(a.sc + (long long)k * TP);
+                if (lane == 0) {
 #pragma unroll
-                for (int q = 0; q < TP / 4; ++q) {
-                    const float4 s4 = __ldg(sp + q);
-                    const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
+                    for (int h = 0; h < PAIR; ++h)
+                        if (h < nb) mbar_arrive(smem_u32(&s_empty[slot[h]]));
+                }
 #pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const int tt = 4 * q + u;
-                        const float dsum = __uint_as_float(v[tt]) + __uint_as_float(v[TP + tt]);
-                        acc[tt] = fmaf(dsum * sv[u], dm.x, acc[tt]);
+                for (int h = 0; h < PAIR; ++h) {
+                    if (h < nb) {
+#pragma unroll
+                        for (int q = 0; q < TP / 4; ++q) {
+                            const float sv[4] = {s4[h][q].x, s4[h][q].y, s4[h][q].z, s4[h][q].w};
+#pragma unroll
+                            for (int u = 0; u < 4; ++u) {
+                                const int tt = 4 * q + u;
+                                const float dsum = __uint_as_float(v[h][tt]) + __uint_as_float(v[h][TP + tt]);
+                                acc[tt] = fmaf(dsum * sv[u], dm[h].x, acc[tt]);
+                            }
+                            if constexpr (F == kQ4_1) {  // + m * (block sum of x), loaded here: registers
+                                const float4 m4 = __ldg(reinterpret_cast<const float4*>(a.xsum + (long long)(k + h) * TP) + q);
+                                acc[4 * q] = fmaf(dm[h].y, m4.x, acc[4 * q]);
+                                acc[4 * q + 1] = fmaf(dm[h].y, m4.y, acc[4 * q + 1]);
+                                acc[4 * q + 2] = fmaf(dm[h].y, m4.z, acc[4 * q + 2]);
+                                acc[4 * q + 3] = fmaf(dm[h].y, m4.w, acc[4 * q + 3]);
+                            }
+                        }
                     }
                 }
-                if constexpr (F == kQ4_1) {
-                    const float4* xp = reinterpret_cast<const float4*>(a.xsum + (long long)k * TP);
-#pragma unroll
-                    for (int q = 0; q < TP / 4; ++q) {
-                        const float4 s4 = __ldg(xp + q);
-                        acc[4 * q] = fmaf(dm.y, s4.x, acc[4 * q]);
-                        acc[4 * q + 1] = fmaf(dm.y, s4.y, acc[4 * q + 1]);
-                        acc[4 * q + 2] = fmaf(dm.y, s4.z, acc[4 * q + 2]);
-                        acc[4 * q + 3] = fmaf(dm.y, s4.w, acc[4 * q + 3]);
-                    }
-                }
-                ++bseq;
+                bseq += (uint32_t)nb;
+                k += nb;
             }
             return !aborted();
         });

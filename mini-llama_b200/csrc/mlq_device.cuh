@@ -63,7 +63,8 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
 // out) records a code here and returns; the host reads it back with
 // mlq_device_error().  Codes: 1 = pipeline "full" wait, 2 = "empty" wait,
 // 3 = drain wait, 4 = peer flag wait, 5 = consumer rendezvous, 6 = x-tile
-// "empty" wait, 7 = resident x tiles ready wait, 12-16 = GEMM waits.
+// "empty" wait, 7 = resident x tiles ready wait, 8 = staged x copy wait,
+// 12-16 = GEMM waits, 20-26 = batched-decode GEMM waits.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void report_error(int* err, int code) {
     if (err) atomicCAS(err, 0, code);

@@ -231,6 +231,21 @@ __device__ __forceinline__ void int_piece_load(const float* x, int in, long long
     }
 }
 
+// The same piece from x staged in shared memory at `xst` (x[0] at xst).
+__device__ __forceinline__ void int_piece_load_smem(uint32_t xst, int in, long long k0, int i, int lane,
+                                                    float v[16]) {
+    const long long e0 = k0 + 16LL * (i * 32 + lane);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        float4 q4 = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (e0 + 4 * j < in) q4 = lds_f4(xst + (uint32_t)((e0 + 4 * j) * 4));
+        v[4 * j] = q4.x;
+        v[4 * j + 1] = q4.y;
+        v[4 * j + 2] = q4.z;
+        v[4 * j + 3] = q4.w;
+    }
+}
+
 // Slices of one piece into x tile `xs` (+ scale/sum pair into `ss`).  The two
 // lanes holding a block's halves are neighbours (shuffle partners).
 template <int G>
@@ -351,6 +366,7 @@ __global__ void __launch_bounds__(threads_for(MT), MINB)
     __shared__ float tile_res[2][MT * C::RT];  // per-tile results, double-buffered
     __shared__ __align__(8) uint64_t tile_bar;  // consumer warps' per-tile rendezvous
     __shared__ __align__(8) uint64_t xready_bar;  // INT resident mode: all x tiles built
+    __shared__ __align__(8) uint64_t xstage_bar;  // INT resident mode: x staged in shared memory
     __shared__ int stage_row[kMaxStages];         // dynamic mode: first row of each stage's tile (-1: end)
 
     const int warp = threadIdx.x >> 5;
@@ -374,6 +390,7 @@ __global__ void __launch_bounds__(threads_for(MT), MINB)
         }
         mbar_init(smem_u32(&tile_bar), kConsumerWarps);
         mbar_init(smem_u32(&xready_bar), kConsumerWarps + 1);
+        mbar_init(smem_u32(&xstage_bar), 1);
         abort_flag = 0;
         fence_mbar_init();
     }
@@ -539,16 +556,39 @@ __global__ void __launch_bounds__(threads_for(MT), MINB)
         // Resident integer mode: the consumers and the x loader split the
         // pieces of every K-tile between them, then meet on xready_bar.
         // x may be the previous kernel's output: wait for it (weights are
-        // read-only, so warp 0 started streaming them without waiting)
-        grid_dependency_wait();
+        // read-only, so warp 0 started streaming them without waiting).
+        // Staged: one lane copies all of x to shared memory with one bulk
+        // copy (one memory round trip) and the warps build the tiles from
+        // there; otherwise every warp loads its pieces from global memory.
+        const uint32_t xst = x_base + (uint32_t)a.ktiles * C::XT_BYTES;
+        bool staged_ok = true;
+        if (a.x_staged) {
+            if (warp == kXWarp && lane == 0) {
+                grid_dependency_wait();
+                mbar_arrive_expect_tx(smem_u32(&xstage_bar), (uint32_t)a.x_staged);
+                bulk_g2s(xst, a.x, (uint32_t)a.x_staged, smem_u32(&xstage_bar));
+            }
+            if (!mbar_wait(smem_u32(&xstage_bar), 0u)) {
+                report_error(a.err, 8);
+                abort_flag = 1;
+                staged_ok = false;
+            }
+        } else {
+            grid_dependency_wait();
+        }
         constexpr int NQ = 2 * C::G;
-        const int items = a.ktiles * NQ;
+        const int items = staged_ok ? a.ktiles * NQ : 0;
         for (int it = warp - 1; it < items; it += 2 * (kConsumerWarps + 1)) {
             // two pieces in flight per warp
             const int it2 = it + kConsumerWarps + 1;
             float v0[16], v1[16];
-            int_piece_load<C::G>(a.x, a.in, (long long)(it / NQ) * C::KTE, it % NQ, lane, v0);
-            if (it2 < items) int_piece_load<C::G>(a.x, a.in, (long long)(it2 / NQ) * C::KTE, it2 % NQ, lane, v1);
+            if (a.x_staged) {
+                int_piece_load_smem(xst, a.in, (long long)(it / NQ) * C::KTE, it % NQ, lane, v0);
+                if (it2 < items) int_piece_load_smem(xst, a.in, (long long)(it2 / NQ) * C::KTE, it2 % NQ, lane, v1);
+            } else {
+                int_piece_load<C::G>(a.x, a.in, (long long)(it / NQ) * C::KTE, it % NQ, lane, v0);
+                if (it2 < items) int_piece_load<C::G>(a.x, a.in, (long long)(it2 / NQ) * C::KTE, it2 % NQ, lane, v1);
+            }
             const uint32_t xs0 = x_base + (uint32_t)(it / NQ) * C::XT_BYTES;
             int_piece_store<C::G>(v0, it % NQ, lane, xs0, xs0 + C::X_BYTES);
             if (it2 < items) {
@@ -1104,8 +1144,18 @@ cudaError_t launch_stream_t(GemvArgs args, int sm_count, int smem_per_sm, cudaSt
     // Resident x (every K-tile's x tile kept, built once) when it fits next
     // to two weight stages; the fp32 mode also needs a barrier per K-tile.
     const long long xres_bytes = (long long)args.ktiles * C::XT_BYTES;
+    // one-token resident mode over three or more K-tiles: x staged in shared
+    // memory by one bulk copy (x 16-B aligned, in % 4 == 0: a 16-B multiple)
+    // when it fits next to the tiles and two weight stages
+    const long long stage_bytes = ((long long)args.in * 4 + 127) / 128 * 128;
+    args.x_staged = 0;
     int S, nx;
-    if (xres_bytes + 2LL * C::W_BYTES <= budget && (INT || args.ktiles <= kMaxStages)) {
+    if (INT && args.ktiles >= 3 && xres_bytes + stage_bytes + 2LL * C::W_BYTES <= budget) {
+        args.x_resident = 1;
+        args.x_staged = args.in * 4;
+        nx = args.ktiles;
+        S = (int)((budget - xres_bytes - stage_bytes) / C::W_BYTES);
+    } else if (xres_bytes + 2LL * C::W_BYTES <= budget && (INT || args.ktiles <= kMaxStages)) {
         args.x_resident = 1;
         nx = args.ktiles;
         S = (int)((budget - xres_bytes) / C::W_BYTES);
@@ -1118,7 +1168,8 @@ cudaError_t launch_stream_t(GemvArgs args, int sm_count, int smem_per_sm, cudaSt
     if (!args.x_resident) nx = S;
     if (S < 2) return cudaErrorInvalidConfiguration;
     args.nstages = S;
-    const int smem = S * C::W_BYTES + nx * C::XT_BYTES + 128;  // + the alignment slack
+    const int smem = S * C::W_BYTES + nx * C::XT_BYTES + (args.x_staged ? (int)stage_bytes : 0) +
+                     128;  // + the alignment slack
     // Every launch of this instantiation uses at most budget + 128 bytes
     // (stages and x slots are sized to the budget), so the attribute is set
     // to that once per device; concurrent first calls set the same value.

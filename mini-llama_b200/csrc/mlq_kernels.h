@@ -33,6 +33,8 @@ struct GemvArgs {
     int* err;                // device error flag
     int tma2d;               // weights streamed by 2-D tensor map (set by the launcher)
     int x_resident;          // ktiles <= nstages: x tiles built once, kept for every row tile
+    int x_staged;            // resident one-token mode: bytes of x copied to shared memory by one
+                             // bulk copy before the x tiles are built from it (0: built from global)
     unsigned int* tiles;     // dynamic row-tile queue {next, done} of this launch, or null
     // sharded calls only (world > 1): completion handshake
     int world, rank;
@@ -123,6 +125,11 @@ cudaError_t launch_quantize(int fmt, const float* src, long long rows, int cols,
 // Blocks -> fp32 [rows][cols], reference rules (mlq_convert.cu).
 cudaError_t launch_dequantize(int fmt, const uint8_t* blocks, long long rows, int cols, float* dst,
                               cudaStream_t stream);
+
+// Blocks of one format -> blocks of another (formats differ): the
+// reference's dequantize then quantize per block, bit for bit.
+cudaError_t launch_transcode(int src_fmt, const uint8_t* src, int dst_fmt, uint8_t* dst, long long rows, int cols,
+                             cudaStream_t stream);
 
 // y[r][c] += bias[c] for r < rows, c < cols.
 cudaError_t launch_add_bias(float* y, const float* bias, int rows, int cols, cudaStream_t stream);

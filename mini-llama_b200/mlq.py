@@ -464,3 +464,40 @@ class GgufFile:
                     device: int = 0, stream=None) -> None:
         check(_gguf_lib().mlq_gguf_upload_rows(self.h, index, row_begin, row_end, dst_ptr, dst_bytes, device,
                                                None if stream is None else _stream_handle(stream)))
+
+
+# ---------------------------------------------------------------------------
+# model-level quantization (mlq_transcode / mlq_quantize_model)
+# ---------------------------------------------------------------------------
+class QuantizeOp(ctypes.Structure):
+    """struct mlq_quantize_op (include/mlq.h)."""
+    _fields_ = [("src_type", ctypes.c_int), ("src", ctypes.c_void_p), ("dst_fmt", ctypes.c_int),
+                ("dst", ctypes.c_void_p), ("rows", ctypes.c_int), ("cols", ctypes.c_int)]
+
+
+def _convert_lib():
+    L = lib()
+    if not getattr(L, "_convert_ready", False):
+        L.mlq_transcode.argtypes = [_i, _vp, _i, _vp, _i, _i, _vp]
+        L.mlq_transcode.restype = _i
+        L.mlq_quantize_model.argtypes = [ctypes.POINTER(QuantizeOp), _i, _vp]
+        L.mlq_quantize_model.restype = _i
+        L._convert_ready = True
+    return L
+
+
+def transcode(src_type, src, dst_fmt, rows: int, cols: int, stream=None):
+    """A device tensor of `src_type` ("f32" or a block format) -> uint8 CUDA
+    blocks of `dst_fmt` (mlq_transcode)."""
+    import torch
+    st = 0 if src_type == "f32" else fmt_id(src_type)
+    out = torch.empty(weight_bytes(_fmt_name(dst_fmt), rows, cols), dtype=torch.uint8, device=src.device)
+    check(_convert_lib().mlq_transcode(st, src.data_ptr(), fmt_id(dst_fmt), out.data_ptr(), rows, cols,
+                                       _stream_handle(stream)))
+    return out
+
+
+def quantize_model(ops, stream=None) -> None:
+    """mlq_quantize_model over a list of QuantizeOp."""
+    arr = (QuantizeOp * max(1, len(ops)))(*ops)
+    check(_convert_lib().mlq_quantize_model(arr, len(ops), _stream_handle(stream)))

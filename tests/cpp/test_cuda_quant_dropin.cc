@@ -21,6 +21,7 @@
 #include "mini_llama/cuda_weight_upload.h"
 #include "mini_llama/quant.h"
 #include "mini_llama/threadpool.h"
+#include "mlq_model_quant.h"
 
 using namespace mini_llama;
 
@@ -199,6 +200,73 @@ void forwardPattern() {
     }
 }
 
+// The generate path quantizes after uploading (src/main.cc:559-564): the
+// reference's uploadLinearWeight puts F32 and Q4_1 weights on the GPU, the
+// host model is quantized with quantizeModelTo*'s per-tensor rule, and
+// quantizeUploadedWeights brings the device copies along.  The device blocks
+// must equal the reference's host quantization byte for byte, carry the new
+// type (so forward.cc's lookup by name and type finds them), and feed
+// cudaQ*LinearDeviceInput.
+void quantizeAfterUpload() {
+    const int out = 1000, in = 4096;
+    Tensor w({out, in});
+    for (size_t i = 0; i < w.size(); ++i) w.data[i] = 0.02f * std::sin(0.71f * static_cast<float>(i % 65537));
+    QuantizedTensor f32;
+    f32.type = QuantType::kF32;
+    f32.shape = {out, in};
+    f32.f32_data = w.data;
+    QuantizedTensor q41;
+    q41.type = QuantType::kQ41;
+    q41.shape = {out, in};
+    q41.q4_1_data = makeQ41(out, in);
+    for (QuantType target : {QuantType::kQ80, QuantType::kQ40}) {
+        CudaModelWeights storage;
+        storage.device_id = 0;
+        uploadLinearWeight(storage, f32, "layers.0.wq", 0);
+        uploadLinearWeight(storage, q41, "layers.0.wk", 0);
+        CHECK(storage.weights.size() == 2);
+        quantizeUploadedWeights(storage, target);
+        // the reference's host pass on the same tensors
+        const Tensor from41 = dequantizeFromQ41(q41.q4_1_data, q41.shape);
+        for (int k = 0; k < 2; ++k) {
+            const CudaUploadedWeight& cw = storage.weights[k];
+            CHECK(cw.type == target);
+            const Tensor& src = k == 0 ? w : from41;
+            std::vector<uint8_t> want;
+            if (target == QuantType::kQ80) {
+                auto b = quantizeToQ80(src);
+                want.assign(reinterpret_cast<const uint8_t*>(b.data()),
+                            reinterpret_cast<const uint8_t*>(b.data()) + b.size() * sizeof(BlockQ80));
+            } else {
+                auto b = quantizeToQ40(src);
+                want.assign(reinterpret_cast<const uint8_t*>(b.data()),
+                            reinterpret_cast<const uint8_t*>(b.data()) + b.size() * sizeof(BlockQ40));
+            }
+            CHECK(cw.buffer.bytes() == want.size());
+            std::vector<uint8_t> got(want.size());
+            cw.buffer.download(got.data(), got.size());
+            CHECK(got == want);
+            CHECK(cw.block_count == static_cast<size_t>(out) * (in / 32));
+        }
+        // the forward path on the re-quantized device weight
+        Tensor x({2, in});
+        for (size_t i = 0; i < x.size(); ++i) x.data[i] = std::cos(0.13f * static_cast<float>(i));
+        CudaTensor x_dev = cudaTensorFromHost(x, 0);
+        const CudaUploadedWeight& cw = storage.weights[0];
+        Tensor y, ref;
+        if (target == QuantType::kQ80) {
+            y = cudaQ80LinearDeviceInput(x_dev, cw.buffer.data(), cw.block_count, cw.shape, 0).download();
+            ref = linearQ80(x, quantizeToQ80(w), cw.shape);
+        } else {
+            y = cudaQ40LinearDeviceInput(x_dev, cw.buffer.data(), cw.block_count, cw.shape, 0).download();
+            ref = linearQ40(x, quantizeToQ40(w), cw.shape);
+        }
+        const double err = worstRelL2(y, ref, out);
+        std::printf("  quantize after upload, target type=%d: worst rel-L2 %.3g\n", static_cast<int>(target), err);
+        CHECK(err <= 1e-3);
+    }
+}
+
 }  // namespace
 
 int main() {
@@ -219,6 +287,7 @@ int main() {
         {"cuda_quant_device_variants", deviceVariants},
         {"cuda_quant_validation", validation},
         {"forward_linear_device_pattern", forwardPattern},
+        {"quantize_uploaded_weights_after_upload", quantizeAfterUpload},
     };
     for (const auto& t : tests) {
         const int before = g_failures;

@@ -22,4 +22,4 @@ def test_reference_api_runs_on_mlq():
     if r.returncode == 2:
         pytest.skip("no CUDA device")
     assert r.returncode == 0, r.stdout + r.stderr
-    assert r.stdout.count("[PASS]") == 5
+    assert r.stdout.count("[PASS]") == 6

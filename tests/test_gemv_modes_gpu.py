@@ -72,7 +72,8 @@ def test_integer_mode_non_finite_x_propagates(oracle, pkg, bad):
 
 def test_dynamic_tile_queue_survives_ring_wrap(oracle, pkg):
     """A matrix with >= 8 row tiles per CTA (dynamic queue) launched 600 times
-    in a row: the slot ring (256) wraps twice; every y equals the first."""
+    in a row: the stream's ring of 32 slots wraps many times; every y equals
+    the first."""
     fmt, out_f, in_f = "q4_0", 80000, 1024
     blocks = weights(oracle, pkg, fmt, out_f, in_f, 6)
     w = dev(blocks)
@@ -149,8 +150,8 @@ def test_tile_queues_two_streams_and_a_stalled_launch(oracle, pkg):
                          [y.data_ptr() for y in ys], [f.data_ptr() for f in flags], 0, 1, sa.cuda_stream)
     for i in range(300):
         mlq.linear(fmt, w, out_f, in_f, x, yb[i], stream=sb)
-        if i % 8 == 7 and i // 8 < 40:
-            mlq.linear(fmt, w, out_f, in_f, x, ya[i // 8], stream=sa)
+        if i % 7 == 6 and i // 7 < 40:  # the 40 launches of stream A, spread over B's 300
+            mlq.linear(fmt, w, out_f, in_f, x, ya[i // 7], stream=sa)
     torch.cuda.synchronize()
     assert mlq.device_error(0) == 4  # the stalled launch gave up; the queues are reset
     bad = [i for i, y in enumerate(yb) if not torch.equal(y, first)]

@@ -27,9 +27,8 @@ def test_upload_whole_and_sharded(tmp_path, oracle, pkg, fmt, gtype, out_f, in_f
     mlq = pkg.mlq
     blocks = gw.quantized(oracle, fmt, out_f, in_f, 7, pkg.synth)
     # a second tensor first, so the matrix sits at a non-zero offset
-    raw = gw.build([("general.alignment", gw.U32, 64)],
-                   [("norm", [in_f], 0, np.ones(in_f, np.float32).tobytes()),
-                    ("w", [in_f, out_f], gtype, blocks)])
+    raw = gw.build([], [("norm", [in_f], 0, np.ones(in_f, np.float32).tobytes()),
+                        ("w", [in_f, out_f], gtype, blocks)], alignment=64)
     path = tmp_path / "w.gguf"
     path.write_bytes(raw)
     nbytes = len(blocks)

@@ -182,3 +182,17 @@ def test_oracle_matches_reference_build_random(oracle, reference, pkg, fmt):
         assert np.array_equal(bo, br)
         x = pkg.synth.normal((3, cols), seed=60 + trial)
         assert np.array_equal(bits(oracle.linear(fmt, x, bo, rows)), bits(reference.linear(fmt, x, br, rows)))
+
+
+@pytest.mark.parametrize("src", ["q8_0", "q4_0"])
+@pytest.mark.parametrize("dst", ["q8_0", "q4_0"])
+def test_requantize_rule_matches_reference(oracle, reference, pkg, src, dst):
+    """The oracle's dequantize-then-quantize (the GPU transcode's checker)
+    equals the reference's own dequantizeFrom* + quantizeTo* (its
+    quantizeQtToQ80/Q40 rule, src/model.cc:94-149) byte for byte."""
+    rows, cols = 9, 100
+    w = pkg.synth.normal((rows, cols), seed=5, std=0.02)
+    b = reference.quantize(src, w)
+    mine = oracle.quantize(dst, oracle.dequantize(src, b, rows, cols))
+    ref = reference.quantize(dst, reference.dequantize(src, b, rows, cols))
+    np.testing.assert_array_equal(mine, ref)
