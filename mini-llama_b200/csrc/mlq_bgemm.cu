@@ -27,14 +27,19 @@
 //     d * (s * D) (+ m * sum(x) for q4_1) to the fp32 total of (row, t).
 //     The block scales never enter the tensor-core sums.
 //
-// CTA = 10 warps, one CTA per SM:
-//   warp 0     TMA producer: W chunks (8 blocks x 128 rows, 2-D tensor map
-//              over the AoS bytes) and the chunk's x tiles (fp16 [hi; lo],
-//              128-B swizzle).
-//   warp 1     TMEM allocation; lane 0 issues the MMAs and commits.
-//   warps 2-5  decode: thread = W row; codes -> fp16 A tile (swizzled,
-//              K-major), the block's d (and m) -> a per-accumulator slot.
-//   warps 6-9  fold: thread = W row = TMEM lane (one lane quarter per warp).
+// CTA = 14 warps, one CTA per SM:
+//   warp 0      TMA producer: W chunks (8 blocks x 128 rows, 2-D tensor map
+//               over the AoS bytes) and the chunk's x tiles (fp16 [hi; lo],
+//               128-B swizzle).
+//   warp 1      TMEM allocation; lane 0 issues the MMAs and commits.
+//   warps 2-9   decode: two threads per W row, each turning two blocks of an
+//               A stage (4 blocks, K = 128) into fp16 codes in its 64-value
+//               sub-tile (swizzled, K-major).
+//   warps 10-13 fold: thread = W row = TMEM lane (one lane quarter per
+//               warp); a block's scale d (and q4_1 minimum m) is read from
+//               the W chunk in shared memory.
+// A stage's blocks are committed as one TMEM group: one barrier per four
+// blocks between the MMA thread and the decode / fold warps.
 // Work split ("stream-K"): the matrix is a list of (row tile, block) units;
 // CTA c takes the contiguous range [c W / G, (c + 1) W / G).  A row tile a
 // CTA covers whole is stored straight to y; the at most two partly covered
@@ -47,6 +52,7 @@
 #include <stdint.h>
 
 #include <atomic>
+#include <type_traits>
 
 #include "mlq.h"
 #include "mlq_device.cuh"
@@ -60,11 +66,13 @@ namespace {
 constexpr int BM = 128;             // W rows per tile = MMA M = TMEM lanes
 constexpr int KC = 256;             // values per W chunk
 constexpr int BPC = KC / kQK;       // blocks per chunk (8)
-constexpr int SPC = 4;              // A stages per chunk: two blocks (64 values) each
-constexpr int kPrepWarps = 4;       // warps 2..5
-constexpr int kFoldWarps = 4;       // warps 6..9
-constexpr int kThreads = 32 * (2 + kPrepWarps + kFoldWarps);
-constexpr int kSmemMax = 232448;    // dynamic shared memory per CTA (227 KB)
+constexpr int SB = 4;               // blocks per A stage (K = 128: two 64-value sub-tiles)
+constexpr int SPC = BPC / SB;       // A stages per chunk (2)
+constexpr int kDecodeWarps = 8;     // warps 2..9: two per row (one 64-value sub-tile each)
+constexpr int kFoldWarps = 4;       // warps 10..13: one per TMEM lane quarter
+constexpr int kFoldWarp0 = 2 + kDecodeWarps;
+constexpr int kThreads = 32 * (2 + kDecodeWarps + kFoldWarps);
+constexpr int kSmemMax = 232448 - 1024;  // dynamic shared memory per CTA: 227 KB less the static part
 constexpr int kMinBlocksPerCta = 16;
 
 constexpr int cmin(int a, int b) { return a < b ? a : b; }
@@ -79,18 +87,26 @@ struct BCfg {
     static constexpr int W_ESZ = F == kQ8_0 ? 2 : 1;   // tensor-map element (inner box <= 256 elements)
     static constexpr int W_TILE = BM * W_ROW;
     static constexpr int B_SUB = N * 128;              // [hi; lo] x tile of 64 values (fp16, 128-B rows)
-    static constexpr int B_TILE = SPC * B_SUB;
-    static constexpr int C_STAGE = W_TILE + B_TILE;    // a chunk: W, then its x tiles
-    static constexpr int A_TILE = BM * 128;            // 128 rows x 64 fp16 codes
-    static constexpr int NSLOT = cmin(16, 512 / N);    // TMEM accumulators (one per block in flight)
-    static constexpr uint32_t TMEM_COLS = (uint32_t)pow2_at_least(NSLOT * N);
-    static constexpr int DM_BYTES = NSLOT * BM * 8;    // (d, m) per slot and row
-    static constexpr int fixed = DM_BYTES + 1024;      // + 1024-B alignment slack
-    static constexpr int CS = (3 * C_STAGE + 3 * A_TILE + fixed <= kSmemMax) ? 3 : 2;
-    static constexpr int AS = (CS * C_STAGE + 4 * A_TILE + fixed <= kSmemMax) ? 4 : 3;
-    static constexpr int SMEM = CS * C_STAGE + AS * A_TILE + fixed;
+    static constexpr int B_TILE = (KC / 64) * B_SUB;
+    // the chunk's x block scales (and q4_1 block sums): [8 blocks][TP] floats each
+    static constexpr int SC_BYTES = BPC * TP * 4 * (F == kQ4_1 ? 2 : 1);
+    static constexpr int C_STAGE = (W_TILE + B_TILE + SC_BYTES + 1023) / 1024 * 1024;  // W, x tiles, x scales
+    // A (fp16 codes) lives in TMEM: an A stage is 4 blocks x 32 values x
+    // 2 B / 4 B per column = 64 columns; the accumulator groups (4 blocks x N
+    // columns each) take the rest of the 512 columns
+    static constexpr int AS = 2;
+    static constexpr int A_COLS = SB * kQK / 2;
+    static constexpr int ACC_COL0 = AS * A_COLS;
+    static constexpr int NG = cmin(8, (512 - ACC_COL0) / (SB * N));
+    static constexpr uint32_t TMEM_COLS = 512;
+    static constexpr int fixed = 1024;                 // 1024-B alignment slack
+    static constexpr int CS = cmin(4, (kSmemMax - fixed) / C_STAGE);
+    // at least half an SM's shared memory, so no two CTAs share an SM (each
+    // allocates all 512 TMEM columns)
+    static constexpr int SMEM = CS * C_STAGE + fixed < 120 * 1024 ? 120 * 1024 : CS * C_STAGE + fixed;
+    static_assert(NG >= 1 && CS >= 2, "bgemm stages must fit");
     static_assert(SMEM <= kSmemMax, "bgemm stages must fit shared memory");
-    static_assert(W_TILE % 1024 == 0 && B_SUB % 1024 == 0 && C_STAGE % 1024 == 0 && A_TILE % 1024 == 0,
+    static_assert(W_TILE % 1024 == 0 && B_SUB % 1024 == 0,
                   "SW128 tiles need 1024-B alignment");
     static_assert(W_ROW % 16 == 0, "W chunk row must be 16-byte granular");
 };
@@ -160,10 +176,10 @@ template <int F, int TP>
 __global__ void __launch_bounds__(kThreads, 1)
     bgemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x, BgemmArgs a) {
     using C = BCfg<F, TP>;
-    constexpr int CS = C::CS, AS = C::AS, NSLOT = C::NSLOT, N = C::N;
+    constexpr int CS = C::CS, AS = C::AS, NG = C::NG, N = C::N;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     __shared__ __align__(8) uint64_t c_full[CS], c_empty[CS], a_full[AS], a_empty[AS];
-    __shared__ __align__(8) uint64_t s_full[NSLOT], s_empty[NSLOT], dm_full[NSLOT];
+    __shared__ __align__(8) uint64_t g_full[NG], g_empty[NG];
     __shared__ __align__(8) uint64_t drain_bar, end_bar;
     __shared__ uint32_t tmem_base_s;
     __shared__ int abort_flag;
@@ -173,22 +189,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
     auto w_st = [&](int s) { return base + (uint32_t)(s * C::C_STAGE); };
     auto x_st = [&](int s) { return w_st(s) + (uint32_t)C::W_TILE; };
-    auto a_st = [&](int s) { return base + (uint32_t)(CS * C::C_STAGE + s * C::A_TILE); };
-    const uint32_t dm_base = base + (uint32_t)(CS * C::C_STAGE + AS * C::A_TILE);
+    auto sc_st = [&](int s) { return x_st(s) + (uint32_t)C::B_TILE; };  // [8][TP] scales, then (q4_1) [8][TP] sums
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < CS; ++s) {
             mbar_init(smem_u32(&c_full[s]), 1);
-            mbar_init(smem_u32(&c_empty[s]), kPrepWarps + 1);  // decode warps + the chunk's last MMA commit
+            // decode warps (W codes), fold warps (W scales) and the chunk's last MMA commit (x tiles)
+            mbar_init(smem_u32(&c_empty[s]), kDecodeWarps + kFoldWarps + 1);
         }
         for (int s = 0; s < AS; ++s) {
-            mbar_init(smem_u32(&a_full[s]), kPrepWarps);
+            mbar_init(smem_u32(&a_full[s]), kDecodeWarps);
             mbar_init(smem_u32(&a_empty[s]), 1);
         }
-        for (int s = 0; s < NSLOT; ++s) {
-            mbar_init(smem_u32(&s_full[s]), 1);
-            mbar_init(smem_u32(&s_empty[s]), kFoldWarps);
-            mbar_init(smem_u32(&dm_full[s]), kPrepWarps);
+        for (int g = 0; g < NG; ++g) {
+            mbar_init(smem_u32(&g_full[g]), 1);
+            mbar_init(smem_u32(&g_empty[g]), kFoldWarps);
         }
         mbar_init(smem_u32(&drain_bar), 1);
         mbar_init(smem_u32(&end_bar), kThreads / 32);
@@ -200,6 +215,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tmem_base_s;
+    launch_dependents();  // the fix-up kernel may be scheduled; it waits for this grid
 
     const int G = gridDim.x;
     const long long f0 = unit_begin(a.total, blockIdx.x, G), f1 = unit_begin(a.total, blockIdx.x + 1, G);
@@ -208,10 +224,41 @@ __global__ void __launch_bounds__(kThreads, 1)
         report_error(a.err, code);
         abort_flag = 1;
     };
+    // valid-block mask of A stage j of chunk c (bit b: block c * 8 + 4 j + b)
+    auto stage_mask = [&](int c, int j, int b_lo, int b_hi) {
+        unsigned m = 0;
+#pragma unroll
+        for (int b = 0; b < SB; ++b) {
+            const int k = c * BPC + SB * j + b;
+            if (k >= b_lo && k < b_hi) m |= 1u << b;
+        }
+        return m;
+    };
 
     if (warp == 0) {
         // ------------------------------ TMA producer ------------------------------
         if (lane == 0) {
+            // The weights are read-only here: the first CS chunks of W are
+            // requested before the wait for the x-split kernel (programmatic
+            // dependent launch), their x tiles and scales after it.
+            auto issue_x = [&](int s, int c) {
+                const uint32_t fb = smem_u32(&c_full[s]);
+#pragma unroll
+                for (int q = 0; q < KC / 64; ++q) tma_load_2d(x_st(s) + (uint32_t)(q * C::B_SUB), &tm_x, c * KC + q * 64, 0, fb);
+                // x block scales (and sums) of the chunk's 8 blocks: the arrays
+                // are padded to whole chunks, so this never reads past them
+                bulk_g2s(sc_st(s), a.sc + (long long)c * BPC * TP, (uint32_t)(BPC * TP * 4), fb);
+                if constexpr (F == kQ4_1)
+                    bulk_g2s(sc_st(s) + (uint32_t)(BPC * TP * 4), a.xsum + (long long)c * BPC * TP, (uint32_t)(BPC * TP * 4), fb);
+            };
+            int pend_s[CS], pend_c[CS], npend = 0;
+            bool dep = false;
+            auto flush_pending = [&]() {
+                grid_dependency_wait();
+                dep = true;
+                for (int k = 0; k < npend; ++k) issue_x(pend_s[k], pend_c[k]);
+                npend = 0;
+            };
             uint32_t cseq = 0;
             for_each_chunk(f0, f1, a.kb, [&](int t, int c, int, int) {
                 const int s = (int)(cseq % CS);
@@ -221,13 +268,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 if (aborted()) return false;
                 const uint32_t fb = smem_u32(&c_full[s]);
-                mbar_arrive_expect_tx(fb, (uint32_t)(C::W_TILE + C::B_TILE));
+                mbar_arrive_expect_tx(fb, (uint32_t)(C::W_TILE + C::B_TILE + C::SC_BYTES));
                 tma_load_2d(w_st(s), &tm_w, c * (C::W_ROW / C::W_ESZ), t * BM, fb);
-#pragma unroll
-                for (int j = 0; j < SPC; ++j) tma_load_2d(x_st(s) + (uint32_t)(j * C::B_SUB), &tm_x, c * KC + j * 64, 0, fb);
+                if (dep) {
+                    issue_x(s, c);
+                } else {
+                    pend_s[npend] = s;
+                    pend_c[npend] = c;
+                    if (++npend == CS) flush_pending();
+                }
                 ++cseq;
                 return true;
             });
+            if (!dep) flush_pending();
             // the CTA's shared memory must outlive every copy still landing
             for (uint32_t k = cseq >= (uint32_t)CS ? cseq - CS : 0; k < cseq; ++k)
                 if (!mbar_wait(smem_u32(&c_full[k % CS]), (k / CS) & 1u)) {
@@ -237,9 +290,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp == 1) {
         // ------------------------------ MMA issuer ------------------------------
+        // per A stage: its valid blocks, each into its own accumulator of the
+        // stage's TMEM group, one commit for the group and one for the A stage
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_f16kind(false, BM, N);
-            uint32_t cseq = 0, aseq = 0, bseq = 0;
+            uint32_t cseq = 0, aseq = 0;
             for_each_chunk(f0, f1, a.kb, [&](int, int c, int b_lo, int b_hi) {
                 const int cs = (int)(cseq % CS);
                 if (!mbar_wait(smem_u32(&c_full[cs]), (cseq / CS) & 1u)) {
@@ -247,36 +302,30 @@ __global__ void __launch_bounds__(kThreads, 1)
                     return false;
                 }
                 for (int j = 0; j < SPC; ++j) {
-                    const int k0 = c * BPC + 2 * j;
-                    const bool v0 = k0 >= b_lo && k0 < b_hi, v1 = k0 + 1 >= b_lo && k0 + 1 < b_hi;
-                    if (!v0 && !v1) continue;
-                    const int as = (int)(aseq % AS);
-                    if (!mbar_wait(smem_u32(&a_full[as]), (aseq / AS) & 1u)) {
+                    const unsigned m = stage_mask(c, j, b_lo, b_hi);
+                    if (!m) continue;
+                    const int as = (int)(aseq % AS), g = (int)(aseq % NG);
+                    if (!mbar_wait(smem_u32(&a_full[as]), (aseq / AS) & 1u) ||
+                        !mbar_wait(smem_u32(&g_empty[g]), ((aseq / NG) & 1u) ^ 1u)) {
                         fail(22);
                         return false;
                     }
                     if (aborted()) return false;
                     tc_fence_after();
-                    const uint64_t ad = sw128_desc(a_st(as));
-                    const uint64_t bd = sw128_desc(x_st(cs) + (uint32_t)(j * C::B_SUB));
 #pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        if (!(h ? v1 : v0)) continue;
-                        const int slot = (int)(bseq % NSLOT);
-                        if (!mbar_wait(smem_u32(&s_empty[slot]), ((bseq / NSLOT) & 1u) ^ 1u)) {
-                            fail(22);
-                            return false;
-                        }
-                        tc_fence_after();
-                        const uint32_t td = tmem + (uint32_t)(slot * N);
+                    for (int b = 0; b < SB; ++b) {
+                        if (!(m >> b & 1u)) continue;
+                        // A: the block's 16 columns of the A stage in TMEM (8 per K = 16)
+                        const uint32_t ta = tmem + (uint32_t)(as * C::A_COLS + b * 16);
+                        const uint64_t bd = sw128_desc(x_st(cs) + (uint32_t)((2 * j + (b >> 1)) * C::B_SUB));
+                        const uint32_t td = tmem + (uint32_t)(C::ACC_COL0 + (g * SB + b) * N);
 #pragma unroll
                         for (int kk = 0; kk < 2; ++kk) {
-                            const uint64_t adv = (uint64_t)((h * 64 + kk * 32) >> 4);  // bytes along K / 16
-                            mma_f16kind(td, ad + adv, bd + adv, idesc, kk);
+                            const uint64_t adv = (uint64_t)(((b & 1) * 64 + kk * 32) >> 4);  // B bytes along K / 16
+                            mma_f16kind_ta(td, ta + (uint32_t)(kk * 8), bd + adv, idesc, kk);
                         }
-                        mma_commit(smem_u32(&s_full[slot]));
-                        ++bseq;
                     }
+                    mma_commit(smem_u32(&g_full[g]));
                     mma_commit(smem_u32(&a_empty[as]));
                     ++aseq;
                 }
@@ -288,11 +337,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             mma_commit(smem_u32(&drain_bar));
             if (!mbar_wait(smem_u32(&drain_bar), 0u)) report_error(a.err, 23);
         }
-    } else if (warp < 2 + kPrepWarps) {
+    } else if (warp < kFoldWarp0) {
         // --------------------- decode: codes -> fp16 A tiles ---------------------
-        const int row = (warp - 2) * 32 + lane;
-        const uint32_t swz = (uint32_t)(row & 7);
-        uint32_t cseq = 0, aseq = 0, bseq = 0;
+        // two threads per W row: `half` h fills the stage's 64-value sub-tile
+        // h (blocks 2h, 2h + 1 of the stage)
+        // a warp writes only its TMEM lane quarter (warp % 4): its rows
+        const int row = (warp & 3) * 32 + lane;
+        const int half = (warp - 2) >> 2;
+        const uint32_t tlane = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+        uint32_t cseq = 0, aseq = 0;
         for_each_chunk(f0, f1, a.kb, [&](int, int c, int b_lo, int b_hi) {
             const int cs = (int)(cseq % CS);
             if (!mbar_wait(smem_u32(&c_full[cs]), (cseq / CS) & 1u)) {
@@ -302,93 +355,78 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t wrow = w_st(cs) + (uint32_t)(row * C::W_ROW);
 #pragma unroll
             for (int j = 0; j < SPC; ++j) {
-                const int k0 = c * BPC + 2 * j;
-                const bool v0 = k0 >= b_lo && k0 < b_hi, v1 = k0 + 1 >= b_lo && k0 + 1 < b_hi;
-                if (!v0 && !v1) continue;
+                const unsigned m = stage_mask(c, j, b_lo, b_hi);
+                if (!m) continue;
                 const int as = (int)(aseq % AS);
                 if (!mbar_wait(smem_u32(&a_empty[as]), ((aseq / AS) & 1u) ^ 1u)) {
                     fail(24);
                     return false;
                 }
                 if (aborted()) return false;
-                // the stage's two blocks: 2 BS bytes from byte j * 2 BS of the
-                // row's chunk (a word boundary), read as the 16-B units that
-                // cover them (rows are 17 / 9 / 10 units apart: the 8 lanes of
-                // a load phase hit distinct bank groups)
-                constexpr int NW = 2 * C::BS / 4;
-                const int sb = j * 2 * C::BS;
-                const int sh = (sb % 16) / 4;                 // words before the stage in its first unit
-                const int nu = (sh * 4 + 2 * C::BS + 15) / 16;
-                uint32_t wb[24];
+                tc_fence_after();  // the MMAs that read this A stage are complete
+                const unsigned mine = (m >> (2 * half)) & 3u;
+                // the two halves as compile-time cases, so every register index
+                // below is a constant
+                auto decode_half = [&](auto HALF) {
+                    constexpr int half = decltype(HALF)::value;
+                    // this thread's two blocks: 2 BS bytes from byte (4 j + 2 half) BS
+                    // of the row's chunk (a word boundary), read as the 16-B units
+                    // that cover them (rows are 17 / 9 / 10 units apart: the 8
+                    // lanes of a load phase hit distinct bank groups)
+                    constexpr int NW = 2 * C::BS / 4;
+                    const int sb = (SB * j + 2 * half) * C::BS;
+                    const int sh = (sb % 16) / 4;
+                    const int nu = (sh * 4 + 2 * C::BS + 15) / 16;
+                    uint32_t wb[24];
 #pragma unroll
-                for (int u = 0; u < 6; ++u) {
-                    if (u < nu) {
-                        const uint4 t4 = lds_u4(wrow + (uint32_t)(16 * (sb / 16 + u)));
-                        wb[4 * u] = t4.x;
-                        wb[4 * u + 1] = t4.y;
-                        wb[4 * u + 2] = t4.z;
-                        wb[4 * u + 3] = t4.w;
+                    for (int u = 0; u < 6; ++u) {
+                        if (u < nu) {
+                            const uint4 t4 = lds_u4(wrow + (uint32_t)(16 * (sb / 16 + u)));
+                            wb[4 * u] = t4.x;
+                            wb[4 * u + 1] = t4.y;
+                            wb[4 * u + 2] = t4.z;
+                            wb[4 * u + 3] = t4.w;
+                        }
                     }
+                    uint32_t w[NW + 1];
+#pragma unroll
+                    for (int i = 0; i < NW; ++i) w[i] = wb[i + sh];
+                    w[NW] = 0;
+                    const uint32_t arow = tlane + (uint32_t)(as * C::A_COLS + 2 * half * 16);
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        if (!(mine >> h & 1u)) continue;  // no MMA reads this block
+                        uint32_t qw[8];
+                        if constexpr (F == kQ8_0) {
+                            // block 0: codes at bytes 2..33; block 1: 36..67
+#pragma unroll
+                            for (int i = 0; i < 8; ++i) qw[i] = h ? w[9 + i] : __funnelshift_r(w[i], w[i + 1], 16);
+                        } else if constexpr (F == kQ4_0) {
+                            // block 0: qs at bytes 2..17; block 1: 20..35
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) qw[i] = h ? w[5 + i] : __funnelshift_r(w[i], w[i + 1], 16);
+                        } else {
+                            // (d, m) then qs: words 0 / 1..4 and 5 / 6..9
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) qw[i] = w[5 * h + 1 + i];
+                        }
+                        uint32_t cw[16];
+                        codes_f16<F>(qw, cw);
+                        tmem_st16(arow + (uint32_t)(h * 16), cw);  // the block's 16 columns of this row
+                    }
+                };
+                if (mine) {
+                    if (half) decode_half(std::integral_constant<int, 1>{});
+                    else decode_half(std::integral_constant<int, 0>{});
                 }
-                uint32_t w[NW + 1];
-#pragma unroll
-                for (int i = 0; i < NW; ++i) w[i] = wb[i + sh];
-                w[NW] = 0;
-                const uint32_t arow = a_st(as) + (uint32_t)row * 128u;
-                float dm_d[2], dm_m[2];
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    uint32_t qw[8];
-                    uint32_t dbits, mbits = 0;
-                    if constexpr (F == kQ8_0) {
-                        // block 0: d = bytes 0-1, codes 2..33; block 1: d = 34-35, codes 36..67
-                        dbits = h ? (w[8] >> 16) : (w[0] & 0xFFFFu);
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) qw[i] = h ? w[9 + i] : __funnelshift_r(w[i], w[i + 1], 16);
-                    } else if constexpr (F == kQ4_0) {
-                        // block 0: d = 0-1, qs 2..17; block 1: d = 18-19, qs 20..35
-                        dbits = h ? (w[4] >> 16) : (w[0] & 0xFFFFu);
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) qw[i] = h ? w[5 + i] : __funnelshift_r(w[i], w[i + 1], 16);
-                    } else {
-                        // d, m, then qs: words 0 / 1..4 and 5 / 6..9
-                        dbits = w[5 * h] & 0xFFFFu;
-                        mbits = w[5 * h] >> 16;
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) qw[i] = w[5 * h + 1 + i];
-                    }
-                    dm_d[h] = half_bits_to_float(dbits);
-                    dm_m[h] = half_bits_to_float(mbits);
-                    if (!(h ? v1 : v0)) continue;  // no MMA reads this half
-                    uint32_t cw[16];
-                    codes_f16<F>(qw, cw);
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {  // 16-byte chunks 4h + q of the 64-value row
-                        const uint32_t cs16 = ((uint32_t)(4 * h + q) ^ swz) << 4;
-                        sts_u4(arow + cs16, make_uint4(cw[4 * q], cw[4 * q + 1], cw[4 * q + 2], cw[4 * q + 3]));
-                    }
-                }
-                fence_proxy_async_smem();
+                tmem_wait_st();
+                tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(smem_u32(&a_full[as]));
                 ++aseq;
-                // the blocks' scales for the fold, in the slots of their accumulators
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    if (!(h ? v1 : v0)) continue;
-                    const int slot = (int)(bseq % NSLOT);
-                    if (!mbar_wait(smem_u32(&s_empty[slot]), ((bseq / NSLOT) & 1u) ^ 1u)) {
-                        fail(24);
-                        return false;
-                    }
-                    sts_f2(dm_base + (uint32_t)((slot * BM + row) * 8), make_float2(dm_d[h], dm_m[h]));
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(smem_u32(&dm_full[slot]));
-                    ++bseq;
-                }
             }
             __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(&c_empty[cs]));  // W of this chunk is read
+            if (lane == 0) mbar_arrive(smem_u32(&c_empty[cs]));  // W codes of this chunk are read
             ++cseq;
             return true;
         });
@@ -399,7 +437,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         float acc[TP];
 #pragma unroll
         for (int t = 0; t < TP; ++t) acc[t] = 0.f;
-        uint32_t bseq = 0;
+        uint32_t cseq = 0, aseq = 0;
         int seg_tile = -1;
         auto flush = [&](int t, int b_lo, int b_hi) {
             // the CTA's segment of row tile t ends: y, or its part for the fix-up
@@ -421,6 +459,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int tt = 0; tt < TP; ++tt) acc[tt] = 0.f;
         };
         int last_t = -1, last_lo = 0, last_hi = 0;
+        const uint32_t tq = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)C::ACC_COL0;
         for_each_chunk(f0, f1, a.kb, [&](int t, int c, int b_lo, int b_hi) {
             if (t != seg_tile) {
                 if (seg_tile >= 0) flush(last_t, last_lo, last_hi);
@@ -429,89 +468,97 @@ __global__ void __launch_bounds__(kThreads, 1)
             last_t = t;
             last_lo = b_lo;
             last_hi = b_hi;
-            const int kbeg = c * BPC > b_lo ? c * BPC : b_lo;
-            const int kend = (c + 1) * BPC < b_hi ? (c + 1) * BPC : b_hi;
-            // Blocks two at a time (one at a time for 64-column slots, whose
-            // registers would not fit twice): both accumulators' loads are in
-            // flight before one wait, and the x scales are requested before
-            // the barrier waits so their latency hides behind them.
-            constexpr int PAIR = N <= 32 ? 2 : 1;
-            for (int k = kbeg; k < kend;) {
-                const int nb = (PAIR == 2 && k + 1 < kend) ? 2 : 1;
-                float4 s4[2][TP / 4];
-#pragma unroll
-                for (int h = 0; h < PAIR; ++h) {
-                    if (h < nb) {
-                        const float4* sp = reinterpret_cast<const float4*>(a.sc + (long long)(k + h) * TP);
-#pragma unroll
-                        for (int q = 0; q < TP / 4; ++q) s4[h][q] = __ldg(sp + q);
-                    }
-                }
-                int slot[2];
-#pragma unroll
-                for (int h = 0; h < PAIR; ++h) {
-                    if (h < nb) {
-                        slot[h] = (int)((bseq + h) % NSLOT);
-                        const uint32_t ph = ((bseq + h) / NSLOT) & 1u;
-                        if (!mbar_wait(smem_u32(&s_full[slot[h]]), ph) || !mbar_wait(smem_u32(&dm_full[slot[h]]), ph)) {
-                            fail(25);
-                            return false;
-                        }
-                    }
+            const int cs = (int)(cseq % CS);
+            // the chunk's W bytes hold each block's scale d (and minimum m)
+            if (!mbar_wait(smem_u32(&c_full[cs]), (cseq / CS) & 1u)) {
+                fail(25);
+                return false;
+            }
+            const uint32_t wrow = w_st(cs) + (uint32_t)(row * C::W_ROW);
+            for (int j = 0; j < SPC; ++j) {
+                const unsigned m = stage_mask(c, j, b_lo, b_hi);
+                if (!m) continue;
+                const int g = (int)(aseq % NG);
+                if (!mbar_wait(smem_u32(&g_full[g]), (aseq / NG) & 1u)) {
+                    fail(25);
+                    return false;
                 }
                 tc_fence_after();
-                uint32_t v[PAIR][N];
-                const uint32_t tq = tmem + ((uint32_t)(quarter * 32) << 16);
+                // the group's accumulators, PB blocks per TMEM wait (two while
+                // their registers fit); x scales come from the chunk's stage
+                constexpr int PB = N <= 32 ? 2 : 1;
+                // fold of block b's tokens [t0, t0 + NT): D = hi + lo columns
+                auto fold_tokens = [&](int b, int t0, const uint32_t* hi, const uint32_t* lo, int nt) {
+                    const uint32_t boff = wrow + (uint32_t)((SB * j + b) * C::BS);
+                    const float d = half_bits_to_float(lds_u16(boff));
+                    const uint32_t sb = sc_st(cs) + (uint32_t)((SB * j + b) * TP * 4);
 #pragma unroll
-                for (int h = 0; h < PAIR; ++h) {
-                    if (h < nb) {
-                        const uint32_t ta = tq + (uint32_t)(slot[h] * N);
-                        if constexpr (N == 16) {
-                            tmem_ld16_issue(ta, *reinterpret_cast<uint32_t(*)[16]>(v[h]));
-                        } else {
+                    for (int q = 0; q < 4; ++q) {
+                        if (4 * q >= nt) break;
+                        const float4 s4 = lds_f4(sb + 4u * (t0 + 4 * q));  // the same address in every lane
+                        const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
 #pragma unroll
-                            for (int q = 0; q < N / 32; ++q)
-                                tmem_ld32_issue(ta + (uint32_t)(32 * q), *reinterpret_cast<uint32_t(*)[32]>(v[h] + 32 * q));
+                        for (int u = 0; u < 4; ++u) {
+                            const int tt = 4 * q + u;
+                            const float dsum = __uint_as_float(hi[tt]) + __uint_as_float(lo[tt]);
+                            acc[t0 + tt] = fmaf(dsum * sv[u], d, acc[t0 + tt]);
+                        }
+                    }
+                    if constexpr (F == kQ4_1) {  // + m * (block sum of x)
+                        const float mn = half_bits_to_float(lds_u16(boff + 2u));
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            if (4 * q >= nt) break;
+                            const float4 m4 = lds_f4(sb + (uint32_t)(BPC * TP * 4) + 4u * (t0 + 4 * q));
+                            acc[t0 + 4 * q] = fmaf(mn, m4.x, acc[t0 + 4 * q]);
+                            acc[t0 + 4 * q + 1] = fmaf(mn, m4.y, acc[t0 + 4 * q + 1]);
+                            acc[t0 + 4 * q + 2] = fmaf(mn, m4.z, acc[t0 + 4 * q + 2]);
+                            acc[t0 + 4 * q + 3] = fmaf(mn, m4.w, acc[t0 + 4 * q + 3]);
+                        }
+                    }
+                };
+                if constexpr (N <= 32) {
+                    // TP <= 16: one load holds a block's hi and lo columns; two
+                    // blocks per TMEM wait
+#pragma unroll
+                    for (int b2 = 0; b2 < SB; b2 += PB) {
+                        uint32_t v[PB][N];
+#pragma unroll
+                        for (int h = 0; h < PB; ++h) {
+                            if (!(m >> (b2 + h) & 1u)) continue;
+                            const uint32_t ta = tq + (uint32_t)((g * SB + b2 + h) * N);
+                            if constexpr (N == 16) tmem_ld16_issue(ta, *reinterpret_cast<uint32_t(*)[16]>(v[h]));
+                            else tmem_ld32_issue(ta, *reinterpret_cast<uint32_t(*)[32]>(v[h]));
+                        }
+                        tmem_wait_ld(*reinterpret_cast<uint32_t(*)[PB * N]>(&v[0][0]));
+#pragma unroll
+                        for (int h = 0; h < PB; ++h)
+                            if (m >> (b2 + h) & 1u) fold_tokens(b2 + h, 0, v[h], v[h] + TP, TP);
+                    }
+                } else {
+                    // TP = 32: sixteen tokens at a time (their hi and lo columns)
+#pragma unroll 1
+                    for (int b = 0; b < SB; ++b) {
+                        if (!(m >> b & 1u)) continue;
+                        const uint32_t ta = tq + (uint32_t)((g * SB + b) * N);
+#pragma unroll
+                        for (int t0 = 0; t0 < TP; t0 += 16) {
+                            uint32_t v[32];
+                            tmem_ld16_issue(ta + (uint32_t)t0, *reinterpret_cast<uint32_t(*)[16]>(v));
+                            tmem_ld16_issue(ta + (uint32_t)(TP + t0), *reinterpret_cast<uint32_t(*)[16]>(v + 16));
+                            tmem_wait_ld(v);
+                            fold_tokens(b, t0, v, v + 16, 16);
                         }
                     }
                 }
-                tmem_wait_ld(*reinterpret_cast<uint32_t(*)[PAIR * N]>(&v[0][0]));
-                float2 dm[2];
-#pragma unroll
-                for (int h = 0; h < PAIR; ++h)
-                    if (h < nb) dm[h] = lds_f2(dm_base + (uint32_t)((slot[h] * BM + row) * 8));
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) {
-#pragma unroll
-                    for (int h = 0; h < PAIR; ++h)
-                        if (h < nb) mbar_arrive(smem_u32(&s_empty[slot[h]]));
-                }
-#pragma unroll
-                for (int h = 0; h < PAIR; ++h) {
-                    if (h < nb) {
-#pragma unroll
-                        for (int q = 0; q < TP / 4; ++q) {
-                            const float sv[4] = {s4[h][q].x, s4[h][q].y, s4[h][q].z, s4[h][q].w};
-#pragma unroll
-                            for (int u = 0; u < 4; ++u) {
-                                const int tt = 4 * q + u;
-                                const float dsum = __uint_as_float(v[h][tt]) + __uint_as_float(v[h][TP + tt]);
-                                acc[tt] = fmaf(dsum * sv[u], dm[h].x, acc[tt]);
-                            }
-                            if constexpr (F == kQ4_1) {  // + m * (block sum of x), loaded here: registers
-                                const float4 m4 = __ldg(reinterpret_cast<const float4*>(a.xsum + (long long)(k + h) * TP) + q);
-                                acc[4 * q] = fmaf(dm[h].y, m4.x, acc[4 * q]);
-                                acc[4 * q + 1] = fmaf(dm[h].y, m4.y, acc[4 * q + 1]);
-                                acc[4 * q + 2] = fmaf(dm[h].y, m4.z, acc[4 * q + 2]);
-                                acc[4 * q + 3] = fmaf(dm[h].y, m4.w, acc[4 * q + 3]);
-                            }
-                        }
-                    }
-                }
-                bseq += (uint32_t)nb;
-                k += nb;
+                if (lane == 0) mbar_arrive(smem_u32(&g_empty[g]));
+                ++aseq;
             }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&c_empty[cs]));  // W scales of this chunk are read
+            ++cseq;
             return !aborted();
         });
         if (last_t >= 0 && !aborted()) flush(last_t, last_lo, last_hi);
@@ -534,6 +581,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <int TP>
 __global__ void bgemm_xsplit_kernel(const float* __restrict__ x, int T, int in, int kb, __half* __restrict__ xb,
                                     float* __restrict__ sc, float* __restrict__ xsum) {
+    launch_dependents();  // the GEMM may start streaming its weights
     const long long wid = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (wid >= (long long)kb * TP) return;
@@ -566,6 +614,7 @@ __global__ void bgemm_xsplit_kernel(const float* __restrict__ x, int T, int in, 
 // Split row tiles: y = the parts of every CTA that covers the tile, in CTA
 // order, plus the bias.  One thread per (tile, token, row).
 __global__ void bgemm_fixup_kernel(BgemmArgs a, int tp, int G) {
+    grid_dependency_wait();  // every CTA of the GEMM has stored its parts
     const long long tiles = (a.out + BM - 1) / BM;
     const long long n = tiles * a.T * BM;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
@@ -611,12 +660,15 @@ cudaError_t launch_t(const uint8_t* w, const float* x, float* y, int out, int in
     char* p = static_cast<char*>(ws);
     __half* xb = reinterpret_cast<__half*>(p);
     p += align256((size_t)2 * TP * in * sizeof(__half));
+    // scales and sums padded to whole 8-block chunks (the kernel copies a
+    // chunk's worth at a time)
+    const size_t kbp = (size_t)(kb + BPC - 1) / BPC * BPC;
     float* sc = reinterpret_cast<float*>(p);
-    p += align256((size_t)kb * TP * sizeof(float));
+    p += align256(kbp * TP * sizeof(float));
     float* xsum = nullptr;
     if (F == kQ4_1) {
         xsum = reinterpret_cast<float*>(p);
-        p += align256((size_t)kb * TP * sizeof(float));
+        p += align256(kbp * TP * sizeof(float));
     }
     float* part = reinterpret_cast<float*>(p);
 
@@ -655,13 +707,27 @@ cudaError_t launch_t(const uint8_t* w, const float* x, float* y, int out, int in
     a.total = (long long)((out + BM - 1) / BM) * kb;
     a.err = err;
     const int G = grid_for(a.total, sm_count);
-    bgemm_kernel<F, TP><<<G, kThreads, C::SMEM, stream>>>(mw, mx, a);
-    e = cudaGetLastError();
+    // the GEMM and the fix-up each start while the kernel before them drains
+    // (programmatic dependent launch); both wait on the device for the data
+    // they need
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(G);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = (size_t)C::SMEM;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, bgemm_kernel<F, TP>, mw, mx, a);
     if (e != cudaSuccess) return e;
     const long long n = (long long)((out + BM - 1) / BM) * T * BM;
     const long long nb = (n + 255) / 256;
-    bgemm_fixup_kernel<<<(int)(nb < 4 * sm_count ? nb : 4 * sm_count), 256, 0, stream>>>(a, TP, G);
-    return cudaGetLastError();
+    cfg.gridDim = dim3((unsigned)(nb < 4 * sm_count ? nb : 4 * sm_count));
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = 0;
+    return cudaLaunchKernelEx(&cfg, bgemm_fixup_kernel, a, (int)TP, G);
 }
 
 template <int F>
@@ -687,8 +753,9 @@ size_t bgemm_workspace_bytes(int fmt, int in, int rows, int out, int sm_count) {
     const int kb = in / kQK;
     const long long total = (long long)((out + BM - 1) / BM) * kb;
     const int G = grid_for(total, sm_count);
-    size_t b = align256((size_t)2 * tp * in * 2) + align256((size_t)kb * tp * 4);
-    if (fmt == kQ4_1) b += align256((size_t)kb * tp * 4);
+    const size_t kbp = (size_t)(kb + BPC - 1) / BPC * BPC;
+    size_t b = align256((size_t)2 * tp * in * 2) + align256(kbp * tp * 4);
+    if (fmt == kQ4_1) b += align256(kbp * tp * 4);
     return b + (size_t)G * 2 * tp * BM * 4;
 }
 
