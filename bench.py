@@ -325,11 +325,12 @@ def gemm_split(out_f, in_f, rows, sms):
 
 
 def launches_of(mlq, rows, out_f, in_f, gemm_ok, pair, sms):
-    """Kernel launches of one library call: the GEMM is an x-split launch, the
-    GEMM and (split-K) a reduction, per matrix of a pair plus the SwiGLU
-    pass; the GEMV one launch per pass of <= 8 rows (pairs stream together)."""
+    """Kernel launches of one library call: the batched-decode GEMM is an
+    x-split launch and the GEMM; the bf16 GEMM an x-split launch, the GEMM
+    and (split-K) a reduction; per matrix of a pair plus the SwiGLU pass; the
+    GEMV one launch per pass of <= 8 rows (pairs stream together)."""
     if gemm_ok and mlq.takes_bgemm(rows, out_f, in_f):
-        return 7 if pair else 3  # x split, GEMM, fix-up (per matrix of a pair, plus SwiGLU)
+        return 5 if pair else 2  # x split, GEMM (per matrix of a pair, plus SwiGLU)
     if gemm_ok and mlq.takes_gemm(rows, out_f, in_f):
         per = 2 + (gemm_split(out_f, in_f, rows, sms) > 1)
         return 2 * per + 1 if pair else per

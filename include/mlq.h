@@ -21,15 +21,16 @@
  *     is what the reference launches on).  Device-side entry points are
  *     asynchronous on that stream; *_host entry points are synchronous.
  *   - The current CUDA device must own every device pointer passed.
- *   - Ordering with the previous kernel on the stream: the streaming GEMV is
- *     launched with programmatic dependent launch, so it may start while the
- *     kernel before it on the stream is still running.  It reads x and the
- *     bias, and writes y, only after that kernel has completed; it streams
- *     the WEIGHTS before.  So the weights must be complete before the
- *     stream's previous kernel started, whenever that kernel lets its
- *     dependents start early (this library's GEMV does; its quantizer and
- *     the other kernels here do not, so a quantize followed by a linear on
- *     one stream is ordered).
+ *   - Ordering with the previous kernel on the stream: the streaming GEMV and
+ *     the batched-decode GEMM (its x split and the GEMM) are launched with
+ *     programmatic dependent launch, so they may start while the kernel
+ *     before them on the stream is still running.  They read x and the bias,
+ *     and write y and their workspace, only after that kernel has completed;
+ *     they stream the WEIGHTS before.  So the weights must be complete before
+ *     the stream's previous kernel started, whenever that kernel lets its
+ *     dependents start early (this library's GEMV and batched-decode GEMM
+ *     do; its quantizer and the other kernels here do not, so a quantize
+ *     followed by a linear on one stream is ordered).
  */
 #ifndef MLQ_H_
 #define MLQ_H_

@@ -15,37 +15,43 @@
 //     [0, 15].  (One byte permute drops a code into the mantissa of 1024.0,
 //     one packed subtract removes the 1024 + offset: ~1.3 operations per
 //     weight, one fp16 A tile.)
-//   * x is scaled per (token, block) by a power of two s >= max|x_block| and
-//     split x/s = xh + xl into two fp16 values (xsplit kernel below): exact
-//     to 2^-24 of s, the level of one fp32 rounding of the block's largest
-//     value.
-//   * One 128 x N x 32 product per block on the tensor cores (two kind::f16
-//     MMAs of K = 16) gives D[row][t] = sum q (xh + xl) over the block -- the
-//     hi and lo halves of x are the two halves of B (N = 2 x padded tokens)
-//     -- in a TMEM accumulator of its own.
+//   * x is scaled per token by a power of two s_t > max|x_t| over the whole
+//     row and split x/s_t = xh + xl into two fp16 values (xsplit kernel
+//     below): exact to 2^-25 of s_t, the level of one fp32 rounding of the
+//     token's largest value.
+//   * Per block, the tensor cores form Dh[row][t] = sum q xh and Dl[row][t] =
+//     sum q xl in one TMEM accumulator of the block: two kind::f16 MMAs of
+//     128 x N x 16, N = 2 x padded tokens (the hi rows of x, then the lo
+//     rows, are the B operand).  An MMA costs about the same for any N up to
+//     64, so hi and lo share one instruction.
 //   * CUDA-core "fold" warps read the block's accumulator and add
-//     d * (s * D) (+ m * sum(x) for q4_1) to the fp32 total of (row, t).
-//     The block scales never enter the tensor-core sums.
+//     d * (Dh + Dl) (+ m * sum(x / s_t) for q4_1) to the fp32 total of
+//     (row, t); the total is multiplied by s_t once, when it is stored.  The
+//     block scales never enter the tensor-core sums.
 //
 // CTA = 14 warps, one CTA per SM:
 //   warp 0      TMA producer: W chunks (8 blocks x 128 rows, 2-D tensor map
 //               over the AoS bytes) and the chunk's x tiles (fp16 [hi; lo],
 //               128-B swizzle).
 //   warp 1      TMEM allocation; lane 0 issues the MMAs and commits.
-//   warps 2-9   decode: two threads per W row, each turning two blocks of an
-//               A stage (4 blocks, K = 128) into fp16 codes in its 64-value
-//               sub-tile (swizzled, K-major).
+//   warps 2-9   decode: two threads per W row, each turning its half of an
+//               A stage's blocks into fp16 codes in TMEM (the MMA's A
+//               operand).
 //   warps 10-13 fold: thread = W row = TMEM lane (one lane quarter per
 //               warp); a block's scale d (and q4_1 minimum m) is read from
 //               the W chunk in shared memory.
-// A stage's blocks are committed as one TMEM group: one barrier per four
-// blocks between the MMA thread and the decode / fold warps.
+// A stage's blocks (four; two with 32 padded tokens) are committed as one
+// TMEM group: one barrier per stage between the MMA thread and the decode /
+// fold warps.
 // Work split ("stream-K"): the matrix is a list of (row tile, block) units;
 // CTA c takes the contiguous range [c W / G, (c + 1) W / G).  A row tile a
 // CTA covers whole is stored straight to y; the at most two partly covered
-// tiles at the ends of its range go to a workspace, and a second kernel adds
-// every split tile's parts in CTA order (deterministic) plus the bias.
-// Every mbarrier wait is bounded (2 s); no TMA multicast anywhere.
+// tiles at the ends of its range go to a workspace, and the last CTA to
+// finish a split tile (a counter per tile) adds its parts in CTA order
+// (deterministic) plus the bias.
+// Two launches per call: the x split, then the GEMM, each with programmatic
+// dependent launch (the GEMM streams its first weight chunks while the split
+// runs).  Every mbarrier wait is bounded (2 s); no TMA multicast anywhere.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -66,9 +72,7 @@ namespace {
 constexpr int BM = 128;             // W rows per tile = MMA M = TMEM lanes
 constexpr int KC = 256;             // values per W chunk
 constexpr int BPC = KC / kQK;       // blocks per chunk (8)
-constexpr int SB = 4;               // blocks per A stage (K = 128: two 64-value sub-tiles)
-constexpr int SPC = BPC / SB;       // A stages per chunk (2)
-constexpr int kDecodeWarps = 8;     // warps 2..9: two per row (one 64-value sub-tile each)
+constexpr int kDecodeWarps = 8;     // warps 2..9: two per row
 constexpr int kFoldWarps = 4;       // warps 10..13: one per TMEM lane quarter
 constexpr int kFoldWarp0 = 2 + kDecodeWarps;
 constexpr int kThreads = 32 * (2 + kDecodeWarps + kFoldWarps);
@@ -76,27 +80,31 @@ constexpr int kSmemMax = 232448 - 1024;  // dynamic shared memory per CTA: 227 K
 constexpr int kMinBlocksPerCta = 16;
 
 constexpr int cmin(int a, int b) { return a < b ? a : b; }
-constexpr int pow2_at_least(int v) { return v <= 32 ? 32 : (v <= 64 ? 64 : (v <= 128 ? 128 : (v <= 256 ? 256 : 512))); }
+constexpr int kBadExp = 0x7fffffff;  // token exponent of an x row holding NaN / Inf
 
 // TP: padded tokens (8, 16 or 32); the MMA's N is 2 TP (x hi, then x lo).
 template <int F, int TP>
 struct BCfg {
     static constexpr int BS = Fmt<F>::kBlockBytes;
     static constexpr int N = 2 * TP;
+    // blocks per A stage = per TMEM accumulator group: 4 (K = 128), or 2 at
+    // 32 tokens so that three groups still fit
+    static constexpr int SB = TP == 32 ? 2 : 4;
+    static constexpr int SPC = BPC / SB;               // A stages per chunk
     static constexpr int W_ROW = BPC * BS;             // 272 / 144 / 160 bytes of a row's chunk
     static constexpr int W_ESZ = F == kQ8_0 ? 2 : 1;   // tensor-map element (inner box <= 256 elements)
     static constexpr int W_TILE = BM * W_ROW;
-    static constexpr int B_SUB = N * 128;              // [hi; lo] x tile of 64 values (fp16, 128-B rows)
+    static constexpr int B_SUB = 2 * TP * 128;         // [hi; lo] x tile of 64 values (fp16, 128-B rows)
     static constexpr int B_TILE = (KC / 64) * B_SUB;
-    // the chunk's x block scales (and q4_1 block sums): [8 blocks][TP] floats each
-    static constexpr int SC_BYTES = BPC * TP * 4 * (F == kQ4_1 ? 2 : 1);
-    static constexpr int C_STAGE = (W_TILE + B_TILE + SC_BYTES + 1023) / 1024 * 1024;  // W, x tiles, x scales
-    // A (fp16 codes) lives in TMEM: an A stage is 4 blocks x 32 values x
-    // 2 B / 4 B per column = 64 columns; the accumulator groups (4 blocks x N
-    // columns each) take the rest of the 512 columns
-    static constexpr int AS = 2;
+    // q4_1: the chunk's x block sums, [8 blocks][TP] floats
+    static constexpr int SC_BYTES = F == kQ4_1 ? BPC * TP * 4 : 0;
+    static constexpr int C_STAGE = (W_TILE + B_TILE + SC_BYTES + 1023) / 1024 * 1024;  // W, x tiles, x sums
+    // A (fp16 codes) lives in TMEM: a block is 32 values x 2 B / 4 B per
+    // column = 16 columns; 128 columns of A stages, the accumulator groups
+    // (SB blocks x N columns each) take the rest of the 512 columns
     static constexpr int A_COLS = SB * kQK / 2;
-    static constexpr int ACC_COL0 = AS * A_COLS;
+    static constexpr int AS = 128 / A_COLS;
+    static constexpr int ACC_COL0 = 128;
     static constexpr int NG = cmin(8, (512 - ACC_COL0) / (SB * N));
     static constexpr uint32_t TMEM_COLS = 512;
     static constexpr int fixed = 1024;                 // 1024-B alignment slack
@@ -114,17 +122,21 @@ struct BCfg {
 struct BgemmArgs {
     float* y;             // [T][out]
     const float* bias;    // [out] or null
-    const float* sc;      // [kb][TP]: power-of-two block scale of x (NaN: the block holds NaN/Inf)
-    const float* xsum;    // [kb][TP]: block sums of x (q4_1), else null
+    const int* tok_exp;   // [TP]: x row t was scaled by 2^-tok_exp[t] (kBadExp: it holds NaN / Inf)
+    const float* xsum;    // [kb rounded up to 8][TP]: block sums of the scaled x (q4_1), else null
     float* part;          // [grid][2][TP][BM]: partial sums of partly covered row tiles
+    int* tile_cnt;        // [row tiles]: CTAs done with a split tile (zeroed by the x-split kernel)
     int out, in, T, kb;   // kb = blocks per row
-    long long total;      // units = row tiles x kb
+    int total;            // units = row tiles x kb (<= kMaxUnits)
     int* err;
 };
 
-// The units [f0, f1) of CTA c among G.
-__host__ __device__ __forceinline__ long long unit_begin(long long total, int c, int G) {
-    return (long long)c * total / G;
+// The units [f0, f1) of CTA c among G.  total x G < 2^31 (kMaxUnits and at
+// most 256 CTAs), so 32-bit arithmetic (a 64-bit division costs hundreds of
+// instructions on the device).
+constexpr int kMaxUnits = 1 << 23;
+__host__ __device__ __forceinline__ int unit_begin(int total, int c, int G) {
+    return (int)((unsigned)c * (unsigned)total / (unsigned)G);
 }
 
 // fp16 codes of one block (32 values) as 16 half2 words, element order.
@@ -161,14 +173,14 @@ __device__ __forceinline__ void codes_f16(const uint32_t* qw, uint32_t (&c)[16])
 // Walks the CTA's range chunk by chunk: fn(tile, chunk, b_lo, b_hi) with
 // [b_lo, b_hi) the blocks of the tile's row that the CTA covers.
 template <typename Fn>
-__device__ __forceinline__ void for_each_chunk(long long f0, long long f1, int kb, Fn&& fn) {
+__device__ __forceinline__ void for_each_chunk(int f0, int f1, int kb, Fn&& fn) {
     if (f1 <= f0) return;
-    const long long t0 = f0 / kb, t1 = (f1 - 1) / kb;
-    for (long long t = t0; t <= t1; ++t) {
-        const int b_lo = (int)(f0 > t * kb ? f0 - t * kb : 0);
-        const int b_hi = (int)(f1 < (t + 1) * kb ? f1 - t * kb : kb);
+    const int t0 = f0 / kb, t1 = (f1 - 1) / kb;
+    for (int t = t0; t <= t1; ++t) {
+        const int b_lo = f0 > t * kb ? f0 - t * kb : 0;
+        const int b_hi = f1 < (t + 1) * kb ? f1 - t * kb : kb;
         for (int c = b_lo / BPC; c <= (b_hi - 1) / BPC; ++c)
-            if (!fn((int)t, c, b_lo, b_hi)) return;
+            if (!fn(t, c, b_lo, b_hi)) return;
     }
 }
 
@@ -176,20 +188,21 @@ template <int F, int TP>
 __global__ void __launch_bounds__(kThreads, 1)
     bgemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x, BgemmArgs a) {
     using C = BCfg<F, TP>;
-    constexpr int CS = C::CS, AS = C::AS, NG = C::NG, N = C::N;
+    constexpr int CS = C::CS, AS = C::AS, NG = C::NG, N = C::N, SB = C::SB, SPC = C::SPC;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     __shared__ __align__(8) uint64_t c_full[CS], c_empty[CS], a_full[AS], a_empty[AS];
     __shared__ __align__(8) uint64_t g_full[NG], g_empty[NG];
     __shared__ __align__(8) uint64_t drain_bar, end_bar;
     __shared__ uint32_t tmem_base_s;
     __shared__ int abort_flag;
+    __shared__ int fix_tile[2];  // split tiles (first / last of the range) this CTA finished last, else -1
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
     auto w_st = [&](int s) { return base + (uint32_t)(s * C::C_STAGE); };
     auto x_st = [&](int s) { return w_st(s) + (uint32_t)C::W_TILE; };
-    auto sc_st = [&](int s) { return x_st(s) + (uint32_t)C::B_TILE; };  // [8][TP] scales, then (q4_1) [8][TP] sums
+    auto sc_st = [&](int s) { return x_st(s) + (uint32_t)C::B_TILE; };  // q4_1: [8][TP] x block sums
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < CS; ++s) {
@@ -208,6 +221,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_init(smem_u32(&drain_bar), 1);
         mbar_init(smem_u32(&end_bar), kThreads / 32);
         abort_flag = 0;
+        fix_tile[0] = fix_tile[1] = -1;
         fence_mbar_init();
     }
     if (warp == 1) tmem_alloc(smem_u32(&tmem_base_s), C::TMEM_COLS);
@@ -215,16 +229,36 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tmem_base_s;
-    launch_dependents();  // the fix-up kernel may be scheduled; it waits for this grid
+    // the next kernel on the stream may be scheduled; whatever it reads from
+    // this one, it waits for this grid to complete
+    launch_dependents();
 
     const int G = gridDim.x;
-    const long long f0 = unit_begin(a.total, blockIdx.x, G), f1 = unit_begin(a.total, blockIdx.x + 1, G);
+    const int f0 = unit_begin(a.total, blockIdx.x, G), f1 = unit_begin(a.total, blockIdx.x + 1, G);
     auto aborted = [&]() { return *(volatile int*)&abort_flag != 0; };
     auto fail = [&](int code) {
         report_error(a.err, code);
         abort_flag = 1;
     };
-    // valid-block mask of A stage j of chunk c (bit b: block c * 8 + 4 j + b)
+    // the fold warps' own barrier (named barrier 1)
+    auto fold_bar_sync = [&]() { asm volatile("bar.sync 1, %0;" ::"n"(kFoldWarps * 32) : "memory"); };
+    // y of token tt and row o from an unscaled total (bias bo)
+    auto store_y = [&](int tt, int o, float v, float bo) {
+        const int e = a.tok_exp[tt];
+        v = e == kBadExp ? __int_as_float(0x7fc00000) : ldexpf(v, e);
+        a.y[(long long)tt * a.out + o] = a.bias ? __fadd_rn(v, bo) : v;
+    };
+    // the CTAs [c0, c1] whose ranges cover row tile t
+    auto tile_ctas = [&](int t, int& c0, int& c1) {
+        const int u0 = t * a.kb, u1 = u0 + a.kb - 1;
+        c0 = (int)((unsigned)u0 * (unsigned)G / (unsigned)a.total);
+        c1 = (int)((unsigned)u1 * (unsigned)G / (unsigned)a.total);
+        while (c0 + 1 < G && unit_begin(a.total, c0 + 1, G) <= u0) ++c0;
+        while (c0 > 0 && unit_begin(a.total, c0, G) > u0) --c0;
+        while (c1 + 1 < G && unit_begin(a.total, c1 + 1, G) <= u1) ++c1;
+        while (c1 > 0 && unit_begin(a.total, c1, G) > u1) --c1;
+    };
+    // valid-block mask of A stage j of chunk c (bit b: block c * 8 + SB j + b)
     auto stage_mask = [&](int c, int j, int b_lo, int b_hi) {
         unsigned m = 0;
 #pragma unroll
@@ -240,16 +274,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             // The weights are read-only here: the first CS chunks of W are
             // requested before the wait for the x-split kernel (programmatic
-            // dependent launch), their x tiles and scales after it.
+            // dependent launch), their x tiles (and x sums) after it.
             auto issue_x = [&](int s, int c) {
                 const uint32_t fb = smem_u32(&c_full[s]);
 #pragma unroll
                 for (int q = 0; q < KC / 64; ++q) tma_load_2d(x_st(s) + (uint32_t)(q * C::B_SUB), &tm_x, c * KC + q * 64, 0, fb);
-                // x block scales (and sums) of the chunk's 8 blocks: the arrays
-                // are padded to whole chunks, so this never reads past them
-                bulk_g2s(sc_st(s), a.sc + (long long)c * BPC * TP, (uint32_t)(BPC * TP * 4), fb);
+                // q4_1: x block sums of the chunk's 8 blocks (the array is
+                // padded to whole chunks, so this never reads past it)
                 if constexpr (F == kQ4_1)
-                    bulk_g2s(sc_st(s) + (uint32_t)(BPC * TP * 4), a.xsum + (long long)c * BPC * TP, (uint32_t)(BPC * TP * 4), fb);
+                    bulk_g2s(sc_st(s), a.xsum + (long long)c * BPC * TP, (uint32_t)(BPC * TP * 4), fb);
             };
             int pend_s[CS], pend_c[CS], npend = 0;
             bool dep = false;
@@ -297,32 +330,36 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t cseq = 0, aseq = 0;
             for_each_chunk(f0, f1, a.kb, [&](int, int c, int b_lo, int b_hi) {
                 const int cs = (int)(cseq % CS);
-                if (!mbar_wait(smem_u32(&c_full[cs]), (cseq / CS) & 1u)) {
-                    fail(22);
-                    return false;
-                }
+                // operand addresses: per-stage bases plus compile-time offsets
+                const uint64_t bd0 = sw128_desc(x_st(cs));
+#pragma unroll
                 for (int j = 0; j < SPC; ++j) {
                     const unsigned m = stage_mask(c, j, b_lo, b_hi);
                     if (!m) continue;
                     const int as = (int)(aseq % AS), g = (int)(aseq % NG);
-                    if (!mbar_wait(smem_u32(&a_full[as]), (aseq / AS) & 1u) ||
-                        !mbar_wait(smem_u32(&g_empty[g]), ((aseq / NG) & 1u) ^ 1u)) {
+                    // The one wait per stage: the decode warps arrive on a_full
+                    // after their own waits for the chunk's tiles (c_full) and
+                    // for the fold to release the stage's accumulator group
+                    // (g_empty).  Each wait here sits between MMAs and idles
+                    // the tensor pipe for its latency.
+                    if (!mbar_wait(smem_u32(&a_full[as]), (aseq / AS) & 1u)) {
                         fail(22);
                         return false;
                     }
-                    if (aborted()) return false;
                     tc_fence_after();
+                    const uint32_t ta0 = tmem + (uint32_t)(as * C::A_COLS);
+                    const uint32_t td0 = tmem + (uint32_t)(C::ACC_COL0 + g * SB * N);
 #pragma unroll
                     for (int b = 0; b < SB; ++b) {
                         if (!(m >> b & 1u)) continue;
-                        // A: the block's 16 columns of the A stage in TMEM (8 per K = 16)
-                        const uint32_t ta = tmem + (uint32_t)(as * C::A_COLS + b * 16);
-                        const uint64_t bd = sw128_desc(x_st(cs) + (uint32_t)((2 * j + (b >> 1)) * C::B_SUB));
-                        const uint32_t td = tmem + (uint32_t)(C::ACC_COL0 + (g * SB + b) * N);
+                        const int k = SB * j + b;  // block of the chunk: x sub-tile k / 2, K bytes (k & 1) * 64
 #pragma unroll
                         for (int kk = 0; kk < 2; ++kk) {
-                            const uint64_t adv = (uint64_t)(((b & 1) * 64 + kk * 32) >> 4);  // B bytes along K / 16
-                            mma_f16kind_ta(td, ta + (uint32_t)(kk * 8), bd + adv, idesc, kk);
+                            // A: the block's 16 columns in TMEM (8 per K = 16);
+                            // B: all 2 TP rows (hi, lo) of the sub-tile
+                            const uint64_t boff = (uint64_t)(((k >> 1) * C::B_SUB + (k & 1) * 64 + kk * 32) >> 4);
+                            mma_f16kind_ta(td0 + (uint32_t)(b * N), ta0 + (uint32_t)(b * 16 + kk * 8), bd0 + boff,
+                                           idesc, kk);
                         }
                     }
                     mma_commit(smem_u32(&g_full[g]));
@@ -339,8 +376,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp < kFoldWarp0) {
         // --------------------- decode: codes -> fp16 A tiles ---------------------
-        // two threads per W row: `half` h fills the stage's 64-value sub-tile
-        // h (blocks 2h, 2h + 1 of the stage)
+        // two threads per W row, `half` h: with four blocks per stage, blocks
+        // 2h and 2h + 1 of the stage; with two, block h
         // a warp writes only its TMEM lane quarter (warp % 4): its rows
         const int row = (warp & 3) * 32 + lane;
         const int half = (warp - 2) >> 2;
@@ -364,17 +401,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 if (aborted()) return false;
                 tc_fence_after();  // the MMAs that read this A stage are complete
-                const unsigned mine = (m >> (2 * half)) & 3u;
+                // the pair of blocks this thread reads (pb, pb + 1 of the chunk:
+                // 4 j + 2 half, or 2 j) and the ones of them it decodes (bit h:
+                // block pb + h)
+                const unsigned mine = SB == 4 ? (m >> (2 * half)) & 3u : m & (1u << half);
                 // the two halves as compile-time cases, so every register index
                 // below is a constant
                 auto decode_half = [&](auto HALF) {
                     constexpr int half = decltype(HALF)::value;
-                    // this thread's two blocks: 2 BS bytes from byte (4 j + 2 half) BS
-                    // of the row's chunk (a word boundary), read as the 16-B units
-                    // that cover them (rows are 17 / 9 / 10 units apart: the 8
-                    // lanes of a load phase hit distinct bank groups)
+                    // the pair: 2 BS bytes from byte pb BS of the row's chunk (pb
+                    // even: a word boundary), read as the 16-B units that cover
+                    // them (rows are 17 / 9 / 10 units apart: the 8 lanes of a
+                    // load phase hit distinct bank groups)
                     constexpr int NW = 2 * C::BS / 4;
-                    const int sb = (SB * j + 2 * half) * C::BS;
+                    const int pbc = SB == 4 ? SB * j + 2 * half : SB * j;  // pb, from the compile-time half
+                    const int sb = pbc * C::BS;
                     const int sh = (sb % 16) / 4;
                     const int nu = (sh * 4 + 2 * C::BS + 15) / 16;
                     uint32_t wb[24];
@@ -392,7 +433,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int i = 0; i < NW; ++i) w[i] = wb[i + sh];
                     w[NW] = 0;
-                    const uint32_t arow = tlane + (uint32_t)(as * C::A_COLS + 2 * half * 16);
+                    const uint32_t arow = tlane + (uint32_t)(as * C::A_COLS + (pbc - SB * j) * 16);
 #pragma unroll
                     for (int h = 0; h < 2; ++h) {
                         if (!(mine >> h & 1u)) continue;  // no MMA reads this block
@@ -421,7 +462,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 tmem_wait_st();
                 tc_fence_before();
-                __syncwarp();
+                // the first decode warp also waits for the fold to release the
+                // stage's accumulator group, so the MMA thread needs no wait of
+                // its own for it
+                bool ok = true;
+                if (warp == 2 && lane == 0)
+                    ok = mbar_wait(smem_u32(&g_empty[aseq % NG]), ((aseq / NG) & 1u) ^ 1u);
+                if (!__all_sync(0xffffffffu, ok)) {
+                    fail(24);
+                    return false;
+                }
                 if (lane == 0) mbar_arrive(smem_u32(&a_full[as]));
                 ++aseq;
             }
@@ -434,26 +484,41 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ------------------ fold: TMEM block sums -> fp32 totals ------------------
         const int quarter = warp & 3;          // TMEM lanes 32 quarter .. + 31
         const int row = quarter * 32 + lane;   // tile row
+        // tokens folded: T rounded up to 4 (the rest of the TP columns are zero)
+        const int nt = (a.T + 3) & ~3;
+        grid_dependency_wait();  // the token exponents come from the x-split kernel
         float acc[TP];
 #pragma unroll
         for (int t = 0; t < TP; ++t) acc[t] = 0.f;
         uint32_t cseq = 0, aseq = 0;
         int seg_tile = -1;
         auto flush = [&](int t, int b_lo, int b_hi) {
-            // the CTA's segment of row tile t ends: y, or its part for the fix-up
+            // the CTA's segment of row tile t ends
             const int o = t * BM + row;
+            const float bo = (a.bias && o < a.out) ? a.bias[o] : 0.f;
             if (b_lo == 0 && b_hi == a.kb) {
                 if (o < a.out) {
-                    const float bo = a.bias ? a.bias[o] : 0.f;
 #pragma unroll
-                    for (int tt = 0; tt < TP; ++tt)
-                        if (tt < a.T) a.y[(long long)tt * a.out + o] = a.bias ? __fadd_rn(acc[tt], bo) : acc[tt];
+                    for (int tt = 0; tt < TP; ++tt) {
+                        if (tt >= a.T) break;
+                        store_y(tt, o, acc[tt], bo);
+                    }
                 }
             } else {
-                const int slot01 = f0 >= (long long)t * a.kb ? 0 : 1;
+                // A split tile: the part goes to the workspace (unscaled); the
+                // last of the tile's CTAs to finish adds the parts in CTA order
+                // (the same order whichever CTA is last) and stores y.
+                const int slot01 = f0 >= t * a.kb ? 0 : 1;
                 float* p = a.part + ((long long)blockIdx.x * 2 + slot01) * TP * BM;
 #pragma unroll
                 for (int tt = 0; tt < TP; ++tt) p[tt * BM + row] = acc[tt];
+                fold_bar_sync();  // every fold thread's part is stored
+                if (warp == kFoldWarp0 && lane == 0) {
+                    int c0, c1;
+                    tile_ctas(t, c0, c1);
+                    __threadfence();
+                    if (atomicAdd(&a.tile_cnt[t], 1) == c1 - c0) fix_tile[slot01] = t;  // the whole CTA sums it at the end
+                }
             }
 #pragma unroll
             for (int tt = 0; tt < TP; ++tt) acc[tt] = 0.f;
@@ -484,32 +549,25 @@ __global__ void __launch_bounds__(kThreads, 1)
                     return false;
                 }
                 tc_fence_after();
-                // the group's accumulators, PB blocks per TMEM wait (two while
-                // their registers fit); x scales come from the chunk's stage
-                constexpr int PB = N <= 32 ? 2 : 1;
-                // fold of block b's tokens [t0, t0 + NT): D = hi + lo columns
-                auto fold_tokens = [&](int b, int t0, const uint32_t* hi, const uint32_t* lo, int nt) {
+                // acc[t0 + u] += d * (hi[u] + lo[u]) (+ m * xsum[t0 + u]), u < TC,
+                // for block b of the stage
+                constexpr int TC = TP < 16 ? TP : 16;  // tokens per fold step
+                constexpr int PB = TP == 32 ? 1 : 2;   // blocks per TMEM wait
+                auto fold_block = [&](int b, int t0, const uint32_t* hi, const uint32_t* lo) {
                     const uint32_t boff = wrow + (uint32_t)((SB * j + b) * C::BS);
                     const float d = half_bits_to_float(lds_u16(boff));
-                    const uint32_t sb = sc_st(cs) + (uint32_t)((SB * j + b) * TP * 4);
 #pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        if (4 * q >= nt) break;
-                        const float4 s4 = lds_f4(sb + 4u * (t0 + 4 * q));  // the same address in every lane
-                        const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
-#pragma unroll
-                        for (int u = 0; u < 4; ++u) {
-                            const int tt = 4 * q + u;
-                            const float dsum = __uint_as_float(hi[tt]) + __uint_as_float(lo[tt]);
-                            acc[t0 + tt] = fmaf(dsum * sv[u], d, acc[t0 + tt]);
-                        }
+                    for (int u = 0; u < TC; ++u) {
+                        if (t0 + u >= nt) break;
+                        acc[t0 + u] = fmaf(__uint_as_float(hi[u]) + __uint_as_float(lo[u]), d, acc[t0 + u]);
                     }
-                    if constexpr (F == kQ4_1) {  // + m * (block sum of x)
+                    if constexpr (F == kQ4_1) {
                         const float mn = half_bits_to_float(lds_u16(boff + 2u));
+                        const uint32_t sb = sc_st(cs) + (uint32_t)(((SB * j + b) * TP + t0) * 4);
 #pragma unroll
-                        for (int q = 0; q < 4; ++q) {
-                            if (4 * q >= nt) break;
-                            const float4 m4 = lds_f4(sb + (uint32_t)(BPC * TP * 4) + 4u * (t0 + 4 * q));
+                        for (int q = 0; q < TC / 4; ++q) {
+                            if (t0 + 4 * q >= nt) break;
+                            const float4 m4 = lds_f4(sb + 16u * q);  // the same address in every lane
                             acc[t0 + 4 * q] = fmaf(mn, m4.x, acc[t0 + 4 * q]);
                             acc[t0 + 4 * q + 1] = fmaf(mn, m4.y, acc[t0 + 4 * q + 1]);
                             acc[t0 + 4 * q + 2] = fmaf(mn, m4.z, acc[t0 + 4 * q + 2]);
@@ -517,38 +575,30 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                     }
                 };
-                if constexpr (N <= 32) {
-                    // TP <= 16: one load holds a block's hi and lo columns; two
-                    // blocks per TMEM wait
+                // a block's accumulator: hi columns [0, TP), lo columns [TP, 2 TP)
+#pragma unroll
+                for (int t0 = 0; t0 < TP; t0 += TC) {
+                    if (t0 >= nt) break;
 #pragma unroll
                     for (int b2 = 0; b2 < SB; b2 += PB) {
-                        uint32_t v[PB][N];
+                        uint32_t v[PB][2 * TC];
 #pragma unroll
                         for (int h = 0; h < PB; ++h) {
                             if (!(m >> (b2 + h) & 1u)) continue;
                             const uint32_t ta = tq + (uint32_t)((g * SB + b2 + h) * N);
-                            if constexpr (N == 16) tmem_ld16_issue(ta, *reinterpret_cast<uint32_t(*)[16]>(v[h]));
-                            else tmem_ld32_issue(ta, *reinterpret_cast<uint32_t(*)[32]>(v[h]));
+                            if constexpr (TP == 8) {
+                                tmem_ld16_issue(ta, *reinterpret_cast<uint32_t(*)[16]>(v[h]));
+                            } else if constexpr (TP == 16) {
+                                tmem_ld32_issue(ta, *reinterpret_cast<uint32_t(*)[32]>(v[h]));
+                            } else {
+                                tmem_ld16_issue(ta + (uint32_t)t0, *reinterpret_cast<uint32_t(*)[16]>(v[h]));
+                                tmem_ld16_issue(ta + (uint32_t)(TP + t0), *reinterpret_cast<uint32_t(*)[16]>(v[h] + 16));
+                            }
                         }
-                        tmem_wait_ld(*reinterpret_cast<uint32_t(*)[PB * N]>(&v[0][0]));
+                        tmem_wait_ld(*reinterpret_cast<uint32_t(*)[PB * 2 * TC]>(&v[0][0]));
 #pragma unroll
                         for (int h = 0; h < PB; ++h)
-                            if (m >> (b2 + h) & 1u) fold_tokens(b2 + h, 0, v[h], v[h] + TP, TP);
-                    }
-                } else {
-                    // TP = 32: sixteen tokens at a time (their hi and lo columns)
-#pragma unroll 1
-                    for (int b = 0; b < SB; ++b) {
-                        if (!(m >> b & 1u)) continue;
-                        const uint32_t ta = tq + (uint32_t)((g * SB + b) * N);
-#pragma unroll
-                        for (int t0 = 0; t0 < TP; t0 += 16) {
-                            uint32_t v[32];
-                            tmem_ld16_issue(ta + (uint32_t)t0, *reinterpret_cast<uint32_t(*)[16]>(v));
-                            tmem_ld16_issue(ta + (uint32_t)(TP + t0), *reinterpret_cast<uint32_t(*)[16]>(v + 16));
-                            tmem_wait_ld(v);
-                            fold_tokens(b, t0, v, v + 16, 16);
-                        }
+                            if (m >> (b2 + h) & 1u) fold_block(b2 + h, t0, v[h], v[h] + TC);
                     }
                 }
                 tc_fence_before();
@@ -573,80 +623,171 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         tmem_dealloc(tmem, C::TMEM_COLS);
     }
+
+    // Split tiles this CTA finished last: y = the parts of the tile's CTAs
+    // added in CTA order, scaled, plus the bias.  Every thread of the CTA
+    // takes up to 8 (row, token) outputs and issues the loads of their parts
+    // (four CTAs at a time) together.
+    __syncthreads();
+    for (int k = 0; k < 2; ++k) {
+        const int t = fix_tile[k];
+        if (t < 0 || aborted()) continue;
+        __threadfence();  // the other CTAs' parts (their counter increments came first)
+        int c0, c1;
+        tile_ctas(t, c0, c1);
+        const int u0 = t * a.kb;
+        const int n_out = a.T * BM;
+        constexpr int U = 8;
+        for (int base = 0; base < n_out; base += U * kThreads) {
+            float v[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) v[u] = 0.f;
+            for (int c = c0; c <= c1; c += 4) {
+                const float* pp[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const int cc = c + q <= c1 ? c + q : c1;
+                    const int sl = unit_begin(a.total, cc, G) >= u0 ? 0 : 1;
+                    pp[q] = a.part + ((long long)cc * 2 + sl) * TP * BM;
+                }
+                float pv[U][4];
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    const int i = base + u * kThreads + (int)threadIdx.x;
+#pragma unroll
+                    for (int q = 0; q < 4; ++q)
+                        pv[u][q] = (i < n_out && c + q <= c1) ? __ldcg(pp[q] + (i / BM) * BM + i % BM) : 0.f;
+                }
+#pragma unroll
+                for (int u = 0; u < U; ++u)
+#pragma unroll
+                    for (int q = 0; q < 4; ++q)
+                        if (c + q <= c1) v[u] = c + q == c0 ? pv[u][q] : __fadd_rn(v[u], pv[u][q]);
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int i = base + u * kThreads + (int)threadIdx.x;
+                const int r = i % BM, tt = i / BM, o = t * BM + r;
+                if (i < n_out && o < a.out) store_y(tt, o, v[u], a.bias ? a.bias[o] : 0.f);
+            }
+        }
+    }
 }
 
 // x fp32 [T][in] -> the B operand fp16 [2 TP][in] (rows t: hi, TP + t: lo;
-// rows >= T zero), per (block, token) the power-of-two scale and (q4_1) the
-// block sum.  One warp per (block, token).
-template <int TP>
-__global__ void bgemm_xsplit_kernel(const float* __restrict__ x, int T, int in, int kb, __half* __restrict__ xb,
-                                    float* __restrict__ sc, float* __restrict__ xsum) {
-    launch_dependents();  // the GEMM may start streaming its weights
-    const long long wid = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    const int lane = threadIdx.x & 31;
-    if (wid >= (long long)kb * TP) return;
-    const int b = (int)(wid / TP), t = (int)(wid % TP);
-    const long long e = (long long)b * kQK + lane;
-    const float v = t < T ? x[(long long)t * in + e] : 0.f;
-    float mx = fabsf(v);
-    int bad = !(mx <= 3.402823466e38f);  // NaN or Inf
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-        bad |= __shfl_xor_sync(0xffffffffu, bad, off);
-    }
-    int ex = 0;
-    if (mx > 0.f && !bad) frexpf(mx, &ex);  // mx = f 2^ex, f in [0.5, 1): |v / 2^ex| < 1
-    const float xs = ldexpf(v, -ex);        // exact (a power-of-two scaling)
-    const __half h = __float2half_rn(xs);
-    const __half l = __float2half_rn(xs - __half2float(h));
-    xb[(long long)t * in + e] = h;
-    xb[(long long)(TP + t) * in + e] = l;
-    float s = v;
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-    if (lane == 0) {
-        sc[(long long)b * TP + t] = bad ? __int_as_float(0x7fc00000) : ldexpf(1.0f, ex);
-        if (xsum) xsum[(long long)b * TP + t] = s;
-    }
-}
+// rows >= T zero), the exponent e_t of each token's power-of-two scale
+// (2^e_t > max|x_t|) and, for q4_1, the block sums of x / 2^e_t.  One CTA
+// per padded token: a max pass over the row, then the split pass (x stays
+// in registers between them up to 16384 values).  Block 0 also zeroes the
+// GEMM's split-tile counters.
+constexpr int kSplitThreads = 512;
+constexpr int kSplitRegs = 8;  // float4 per thread kept between the passes
 
-// Split row tiles: y = the parts of every CTA that covers the tile, in CTA
-// order, plus the bias.  One thread per (tile, token, row).
-__global__ void bgemm_fixup_kernel(BgemmArgs a, int tp, int G) {
-    grid_dependency_wait();  // every CTA of the GEMM has stored its parts
-    const long long tiles = (a.out + BM - 1) / BM;
-    const long long n = tiles * a.T * BM;
-    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
-        const int r = (int)(i % BM);
-        const int tt = (int)((i / BM) % a.T);
-        const long long t = i / BM / a.T;
-        const int o = (int)(t * BM + r);
-        if (o >= a.out) continue;
-        // CTAs holding the tile's first and last unit
-        const long long u0 = t * a.kb, u1 = u0 + a.kb - 1;
-        int c0 = (int)(u0 * G / a.total), c1 = (int)(u1 * G / a.total);
-        while (c0 + 1 < G && unit_begin(a.total, c0 + 1, G) <= u0) ++c0;
-        while (c0 > 0 && unit_begin(a.total, c0, G) > u0) --c0;
-        while (c1 + 1 < G && unit_begin(a.total, c1 + 1, G) <= u1) ++c1;
-        while (c1 > 0 && unit_begin(a.total, c1, G) > u1) --c1;
-        if (c0 == c1) continue;  // one CTA covered it whole and stored y
-        float v = 0.f;
-        for (int c = c0; c <= c1; ++c) {
-            const int slot01 = unit_begin(a.total, c, G) >= u0 ? 0 : 1;
-            v = c == c0 ? a.part[(((long long)c * 2 + slot01) * tp + tt) * BM + r]
-                        : __fadd_rn(v, a.part[(((long long)c * 2 + slot01) * tp + tt) * BM + r]);
+template <int TP>
+__global__ void __launch_bounds__(kSplitThreads)
+    bgemm_xsplit_kernel(const float* __restrict__ x, int T, int in, __half* __restrict__ xb,
+                        int* __restrict__ tok_exp, float* __restrict__ xsum, int* __restrict__ tile_cnt,
+                        int tiles) {
+    launch_dependents();     // the GEMM may start streaming its weights
+    grid_dependency_wait();  // x, and the workspace the previous call on the stream used
+    __shared__ float red[kSplitThreads / 32];
+    __shared__ int ex_s;
+    const int t = blockIdx.x;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (t == 0)
+        for (int i = threadIdx.x; i < tiles; i += kSplitThreads) tile_cnt[i] = 0;
+    const int in4 = in / 4;
+    const float* xrow = x + (long long)t * in;
+    const bool vec = (reinterpret_cast<uintptr_t>(xrow) & 15u) == 0;  // the caller's x may be offset
+    auto load4 = [&](int i) {
+        if (vec) return reinterpret_cast<const float4*>(xrow)[i];
+        return make_float4(xrow[4 * i], xrow[4 * i + 1], xrow[4 * i + 2], xrow[4 * i + 3]);
+    };
+    const bool keep = in4 <= kSplitRegs * kSplitThreads;
+    float4 kv[kSplitRegs];
+    float mx = 0.f;
+    int bad = 0;
+    auto scan = [&](const float4& v) {
+        const float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+        mx = fmaxf(mx, m);
+        // NaN / Inf anywhere (fmaxf drops NaN, so test every value)
+        bad |= !(fabsf(v.x) <= 3.402823466e38f) | !(fabsf(v.y) <= 3.402823466e38f) |
+               !(fabsf(v.z) <= 3.402823466e38f) | !(fabsf(v.w) <= 3.402823466e38f);
+    };
+    if (keep) {
+#pragma unroll
+        for (int r = 0; r < kSplitRegs; ++r) {
+            const int i = threadIdx.x + r * kSplitThreads;
+            kv[r] = (t < T && i < in4) ? load4(i) : make_float4(0.f, 0.f, 0.f, 0.f);
+            scan(kv[r]);
         }
-        if (a.bias) v = __fadd_rn(v, a.bias[o]);
-        a.y[(long long)tt * a.out + o] = v;
+    } else if (t < T) {
+        for (int i = threadIdx.x; i < in4; i += kSplitThreads) scan(load4(i));
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    if (lane == 0) red[warp] = mx;
+    bad = __syncthreads_or(bad);
+    if (threadIdx.x == 0) {
+        float m = 0.f;
+        for (int w = 0; w < kSplitThreads / 32; ++w) m = fmaxf(m, red[w]);
+        int ex = 0;
+        if (m > 0.f && !bad) frexpf(m, &ex);  // m = f 2^ex, f in [0.5, 1): |x / 2^ex| < 1
+        ex_s = ex;
+        tok_exp[t] = bad ? kBadExp : ex;
+    }
+    __syncthreads();
+    const int ex = bad ? 0 : ex_s;
+    __half* hi = xb + (long long)t * in;
+    __half* lo = xb + (long long)(TP + t) * in;
+    auto split = [&](int i, float4 v) {
+        // exact power-of-two scaling, then the fp16 hi / lo split
+        const float s[4] = {ldexpf(v.x, -ex), ldexpf(v.y, -ex), ldexpf(v.z, -ex), ldexpf(v.w, -ex)};
+        __half h[4], l[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            h[k] = __float2half_rn(s[k]);
+            l[k] = __float2half_rn(s[k] - __half2float(h[k]));
+        }
+        if (i < in4) {
+            *reinterpret_cast<__half2*>(hi + 4 * i) = __halves2half2(h[0], h[1]);
+            *reinterpret_cast<__half2*>(hi + 4 * i + 2) = __halves2half2(h[2], h[3]);
+            *reinterpret_cast<__half2*>(lo + 4 * i) = __halves2half2(l[0], l[1]);
+            *reinterpret_cast<__half2*>(lo + 4 * i + 2) = __halves2half2(l[2], l[3]);
+        }
+        if (xsum) {
+            // 8 lanes hold a block's 32 values (in4 is a multiple of 8)
+            float sum = (s[0] + s[1]) + (s[2] + s[3]);
+            sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+            sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+            sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+            if ((lane & 7) == 0 && i < in4) xsum[(long long)(i / 8) * TP + t] = sum;
+        }
+    };
+    // warp-uniform trip counts: the sums shuffle across all 32 lanes
+    if (keep) {
+#pragma unroll
+        for (int r = 0; r < kSplitRegs; ++r) {
+            const int i = threadIdx.x + r * kSplitThreads;
+            if (r * kSplitThreads + warp * 32 >= in4) break;
+            split(i, bad ? make_float4(0.f, 0.f, 0.f, 0.f) : kv[r]);
+        }
+    } else {
+        for (int base = warp * 32; base < in4; base += kSplitThreads) {
+            const int i = base + lane;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (i < in4 && t < T && !bad) v = load4(i);
+            split(i, v);
+        }
     }
 }
 
 int tp_for(int T) { return T <= 8 ? 8 : (T <= 16 ? 16 : 32); }
 
-int grid_for(long long total, int sm_count) {
+int grid_for(int total, int sm_count) {
     long long g = (total + kMinBlocksPerCta - 1) / kMinBlocksPerCta;
     if (g > sm_count) g = sm_count;
+    if (g > 256) g = 256;  // total x G < 2^31
     return g < 1 ? 1 : (int)g;
 }
 
@@ -660,21 +801,34 @@ cudaError_t launch_t(const uint8_t* w, const float* x, float* y, int out, int in
     char* p = static_cast<char*>(ws);
     __half* xb = reinterpret_cast<__half*>(p);
     p += align256((size_t)2 * TP * in * sizeof(__half));
-    // scales and sums padded to whole 8-block chunks (the kernel copies a
-    // chunk's worth at a time)
-    const size_t kbp = (size_t)(kb + BPC - 1) / BPC * BPC;
-    float* sc = reinterpret_cast<float*>(p);
-    p += align256(kbp * TP * sizeof(float));
+    int* tok_exp = reinterpret_cast<int*>(p);
+    p += align256((size_t)TP * sizeof(int));
     float* xsum = nullptr;
     if (F == kQ4_1) {
+        // padded to whole 8-block chunks (the kernel copies a chunk's worth at a time)
+        const size_t kbp = (size_t)(kb + BPC - 1) / BPC * BPC;
         xsum = reinterpret_cast<float*>(p);
         p += align256(kbp * TP * sizeof(float));
     }
+    int* tile_cnt = reinterpret_cast<int*>(p);
+    const int tiles = (out + BM - 1) / BM;
+    p += align256((size_t)tiles * sizeof(int));
     float* part = reinterpret_cast<float*>(p);
 
-    const long long warps = (long long)kb * TP;
-    bgemm_xsplit_kernel<TP><<<(int)((warps * 32 + 255) / 256), 256, 0, stream>>>(x, T, in, kb, xb, sc, xsum);
-    cudaError_t e = cudaGetLastError();
+    // both launches may start while the kernel before them drains
+    // (programmatic dependent launch); each waits on the device for the data
+    // it reads
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(TP);
+    cfg.blockDim = dim3(kSplitThreads);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, bgemm_xsplit_kernel<TP>, x, T, in, xb, tok_exp, xsum, tile_cnt, tiles);
     if (e != cudaSuccess) return e;
 
     const long long row_bytes = (long long)kb * C::BS;
@@ -697,37 +851,21 @@ cudaError_t launch_t(const uint8_t* w, const float* x, float* y, int out, int in
     BgemmArgs a{};
     a.y = y;
     a.bias = bias;
-    a.sc = sc;
+    a.tok_exp = tok_exp;
     a.xsum = xsum;
     a.part = part;
     a.out = out;
     a.in = in;
     a.T = T;
     a.kb = kb;
-    a.total = (long long)((out + BM - 1) / BM) * kb;
+    a.total = ((out + BM - 1) / BM) * kb;
     a.err = err;
+    a.tile_cnt = tile_cnt;
     const int G = grid_for(a.total, sm_count);
-    // the GEMM and the fix-up each start while the kernel before them drains
-    // (programmatic dependent launch); both wait on the device for the data
-    // they need
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(G);
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = (size_t)C::SMEM;
-    cfg.stream = stream;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&cfg, bgemm_kernel<F, TP>, mw, mx, a);
-    if (e != cudaSuccess) return e;
-    const long long n = (long long)((out + BM - 1) / BM) * T * BM;
-    const long long nb = (n + 255) / 256;
-    cfg.gridDim = dim3((unsigned)(nb < 4 * sm_count ? nb : 4 * sm_count));
-    cfg.blockDim = dim3(256);
-    cfg.dynamicSmemBytes = 0;
-    return cudaLaunchKernelEx(&cfg, bgemm_fixup_kernel, a, (int)TP, G);
+    return cudaLaunchKernelEx(&cfg, bgemm_kernel<F, TP>, mw, mx, a);
 }
 
 template <int F>
@@ -745,17 +883,19 @@ cudaError_t launch_f(const uint8_t* w, const float* x, float* y, int out, int in
 bool bgemm_shape_ok(int fmt, const void* w, int out, int in, int rows) {
     const long long row_bytes = (long long)((in + kQK - 1) / kQK) * block_bytes(fmt);
     return rows >= MLQ_BGEMM_MIN_ROWS && rows <= kBgemmMaxRows && out > 0 && in % kQK == 0 &&
-           reinterpret_cast<uintptr_t>(w) % 16 == 0 && row_bytes % 16 == 0;
+           reinterpret_cast<uintptr_t>(w) % 16 == 0 && row_bytes % 16 == 0 &&
+           (long long)((out + BM - 1) / BM) * (in / kQK) <= kMaxUnits;
 }
 
 size_t bgemm_workspace_bytes(int fmt, int in, int rows, int out, int sm_count) {
     const int tp = tp_for(rows);
     const int kb = in / kQK;
-    const long long total = (long long)((out + BM - 1) / BM) * kb;
+    const int total = ((out + BM - 1) / BM) * kb;
     const int G = grid_for(total, sm_count);
     const size_t kbp = (size_t)(kb + BPC - 1) / BPC * BPC;
-    size_t b = align256((size_t)2 * tp * in * 2) + align256(kbp * tp * 4);
+    size_t b = align256((size_t)2 * tp * in * 2) + align256((size_t)tp * 4);
     if (fmt == kQ4_1) b += align256(kbp * tp * 4);
+    b += align256((size_t)((out + BM - 1) / BM) * 4);
     return b + (size_t)G * 2 * tp * BM * 4;
 }
 

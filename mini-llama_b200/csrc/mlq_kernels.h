@@ -103,15 +103,17 @@ cudaError_t launch_gemm(int fmt, const uint8_t* w, const float* x, float* y, int
                         const float* bias, void* ws, int split, int sm_count, int* err, cudaStream_t stream);
 
 // Batched-decode GEMM (mlq_bgemm.cu): 2..kBgemmMaxRows rows of x on the
-// tensor cores with exact fp16 weight codes and per-block fp32 folds.
+// tensor cores with exact fp16 weight codes, x split per token into fp16
+// hi / lo, and per-block fp32 folds.  Two launches: the x split, the GEMM.
 constexpr int kBgemmMaxRows = MLQ_BGEMM_MAX_ROWS;
 
 // Host-value conditions of the batched-decode GEMM: 2 <= rows <= 32,
-// in % 32 == 0, 16-B aligned weights with a 16-B multiple row pitch.
+// in % 32 == 0, 16-B aligned weights with a 16-B multiple row pitch, at
+// most 2^23 (row tile, block) units.
 bool bgemm_shape_ok(int fmt, const void* w, int out, int in, int rows);
 
-// Workspace of one launch: x split (fp16 hi/lo), block scales (and q4_1
-// block sums), and the split row tiles' partial sums.
+// Workspace of one launch: x split (fp16 hi/lo), token exponents (and q4_1
+// block sums), split-tile counters and the split row tiles' partial sums.
 size_t bgemm_workspace_bytes(int fmt, int in, int rows, int out, int sm_count);
 
 // y[rows][out] = x W^T (+ bias); ws holds bgemm_workspace_bytes(...) bytes.

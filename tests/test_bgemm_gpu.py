@@ -3,12 +3,13 @@ oracle, through the C ABI (mlq_linear routes 2..32 rows of x with
 in_features % 32 == 0 to it).
 
 Tolerance (the contract): relative L2 error of every output vector (row of
-y) <= 1e-3.  Covered: every format; 2..32 rows (padded token counts 8, 16,
+y) <= 1e-3.  Covered: every format; 2..32 rows (padded token counts 16 and
 32); partial row tiles; K extents that end inside a 256-value chunk;
 matrices whose row tiles the work split cuts across CTAs (the fix-up pass),
 at the BASELINE config-4 and config-5 shapes; the fused bias and SwiGLU
 pair; NaN/Inf propagation; activations spanning six orders of magnitude in
-one block; and bit-identical repeats (the split and its fix-up are
+one block, outlier channels, token rows of very different magnitudes and an
+x that is not 16-byte aligned; and bit-identical repeats (the split and its fix-up are
 deterministic)."""
 from __future__ import annotations
 
@@ -89,8 +90,8 @@ def test_bgemm_bias_and_swiglu(oracle, pkg, fmt):
 
 
 def test_bgemm_wide_dynamic_range(oracle, pkg):
-    """One value per block 1e3, the rest ~1e-3 (the power-of-two block scale
-    keeps the small values at 2^-24 of the block's largest)."""
+    """One value per block 1e3, the rest ~1e-3 (the power-of-two token scale
+    keeps every value to 2^-25 of the token's largest)."""
     fmt, out_f, in_f, rows = "q4_0", 384, 4096, 6
     blocks = weights(oracle, pkg, fmt, out_f, in_f, 31)
     x = pkg.synth.normal((rows, in_f), seed=32, std=1e-3)
@@ -117,3 +118,40 @@ def test_bgemm_zero_x(oracle, pkg):
     blocks = weights(oracle, pkg, fmt, out_f, in_f, 51)
     y = pkg.mlq.linear(fmt, dev(blocks), out_f, in_f, torch.zeros((5, in_f), device="cuda")).cpu().numpy()
     np.testing.assert_array_equal(y, np.zeros((5, out_f), np.float32))
+
+
+def test_bgemm_outliers_and_token_magnitudes(oracle, pkg):
+    """Decoder activations carry a few outlier channels ~1000x the rest; the
+    tokens of a batch may differ by many orders of magnitude (each token has
+    its own power-of-two scale, applied after the sum)."""
+    fmt, out_f, in_f, rows = "q8_0", 1000, 4096, 9
+    blocks = weights(oracle, pkg, fmt, out_f, in_f, 61)
+    x = pkg.synth.normal((rows, in_f), seed=62)
+    x[:, [7, 1000, 2049, 4000]] *= 2000.0
+    x[2] *= 1e-30
+    x[3] *= 1e30
+    x[4] *= 2.0 ** -100
+    x[5] = 0.0
+    y = pkg.mlq.linear(fmt, dev(blocks), out_f, in_f, dev(x)).cpu().numpy()
+    ref = oracle.linear(fmt, x, blocks, out_f)
+    assert np.isfinite(y).all()
+    np.testing.assert_array_equal(y[5], np.zeros(out_f, np.float32))
+    keep = [r for r in range(rows) if r != 5]
+    assert rel_l2_rows(y[keep], ref[keep]).max() <= TOL
+    assert pkg.mlq.device_error(0) == 0
+
+
+@pytest.mark.parametrize("fmt", ["q4_0", "q4_1"])
+def test_bgemm_unaligned_x(oracle, pkg, fmt):
+    """x starting 4 bytes past a 16-byte boundary (a view into a larger
+    buffer) is read element by element."""
+    out_f, in_f, rows = 640, 1024, 5
+    blocks = weights(oracle, pkg, fmt, out_f, in_f, 71)
+    x = pkg.synth.normal((rows, in_f), seed=72)
+    buf = torch.empty(rows * in_f + 1, device="cuda")
+    xv = buf[1:].view(rows, in_f)
+    xv.copy_(dev(x))
+    assert xv.data_ptr() % 16 == 4
+    y = pkg.mlq.linear(fmt, dev(blocks), out_f, in_f, xv).cpu().numpy()
+    assert rel_l2_rows(y, oracle.linear(fmt, x, blocks, out_f)).max() <= TOL
+    assert pkg.mlq.device_error(0) == 0
