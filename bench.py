@@ -52,13 +52,23 @@ def llama8b_layers():
     return mats + [("lm_head", 128256, 4096)]
 
 
+def llama8b_shared_x():
+    """K and V read Q's x, up reads gate's x (src/forward.cc:425-435, 574-582)."""
+    share = {}
+    for l in range(32):
+        share.update({f"l{l}.k": f"l{l}.q", f"l{l}.v": f"l{l}.q", f"l{l}.up": f"l{l}.gate"})
+    return share
+
+
 QWEN7B = [("qkv", 4608, 3584), ("o", 3584, 3584), ("gate", 18944, 3584), ("up", 18944, 3584),
           ("down", 3584, 18944), ("lm_head", 152064, 3584)]
 LLAMA70B = [("gate", 28672, 8192), ("up", 28672, 8192), ("down", 8192, 28672), ("lm_head", 128256, 8192)]
 
 # At N > 1 the matrices named in "shard" are row-sharded across every GPU
 # (fused all-gather); the others run on rank 0 (north_star: FFN and lm_head
-# sharded, small matrices on one GPU).
+# sharded, small matrices on one GPU).  "share_x": matrices that read another
+# matrix's x, as in the model (the library runs consecutive batched-decode
+# matrices on one x as one grouped launch).
 WORKLOADS = {
     "qwen7b": {
         "name": "qwen2-7b-layer+lm_head q4_0 decode (BASELINE configs[1])",
@@ -92,7 +102,7 @@ WORKLOADS = {
     "llama8b-b16": {
         "name": "llama-3-8b 32 layers + lm_head q8_0 batched decode, batch 16 (BASELINE configs[3])",
         "metric": "effective weight GB/s (q8_0 batched decode, Llama-3-8B, batch 16)",
-        "fmt": "q8_0", "rows": 16, "matrices": llama8b_layers(),
+        "fmt": "q8_0", "rows": 16, "matrices": llama8b_layers(), "share_x": llama8b_shared_x(),
         "shard": {n for n, _, _ in llama8b_layers() if n.split(".")[-1] in ("gate", "up", "down", "lm_head")},
     },
     "llama70b": {
@@ -104,6 +114,7 @@ WORKLOADS = {
         "name": "llama-3-70b FFN + lm_head q4_0 decode shards, batch 8 (BASELINE configs[4])",
         "metric": "effective weight GB/s (q4_0 decode, Llama-3-70B FFN + lm_head, batch 8)",
         "fmt": "q4_0", "rows": 8, "matrices": LLAMA70B, "shard": {"gate", "up", "down", "lm_head"},
+        "share_x": {"up": "gate"},
     },
 }
 # measured after the headline in the default run (extra key of the line)
@@ -424,7 +435,11 @@ class Step:
                 self.w[name] = None
             else:
                 self.w[name] = self._weights(i, b, e, in_f)
-            self.x[name] = torch.from_numpy(pkg.synth.normal((rows, in_f), seed=2000 + i)).to(ctx.device)
+            src = wl.get("share_x", {}).get(name)
+            if src is not None:
+                self.x[name] = self.x[src]  # the model's shared input (defined earlier in the list)
+            else:
+                self.x[name] = torch.from_numpy(pkg.synth.normal((rows, in_f), seed=2000 + i)).to(ctx.device)
         torch.cuda.empty_cache()
         # per op (call order): the matrix, the launch count, the ops of both y parities
         shard_names = self.plan.sharded
@@ -435,12 +450,14 @@ class Step:
         self.gathers = [[], []]
         self.names, self.op_bytes, self.launches = [], [], []
         ops = [[], []]
+        grp = None  # (x pointer, matrices) of the open batched-decode group
         for i, (name, out_f, in_f) in enumerate(mats):
             if not self.plan.active(name) or (pair and name == pair[1]):
                 continue
             b, e = self.plan.rows(name)
             wp = self.w[name].data_ptr() if self.w[name] is not None else 0
             if self.plan.place[name] == "shard":
+                grp = None  # a gathered op is never grouped
                 k = shard_names.index(name)
                 for p in (0, 1):
                     g = mlq.make_gather(ctx.world, ctx.rank, b, e, self.slab.peer_ptrs(p, k),
@@ -448,7 +465,10 @@ class Step:
                     self.gathers[p].append(g)
                     ops[p].append(mlq.linear_op(fmt, wp, out_f, in_f, self.x[name].data_ptr(), rows,
                                                 self.slab.local_ptr(p, k), gather=g))
-                self.launches.append(launches_of(mlq, rows, e - b, in_f, False, False, ctx.sms))
+                # a shard takes the batched-decode GEMM or the streaming GEMV
+                # (the sharded call has no bf16 GEMM route)
+                self.launches.append(launches_of(mlq, rows, e - b, in_f, mlq.takes_bgemm(rows, e - b, in_f), False,
+                                                 ctx.sms))
             else:
                 y = torch.empty((rows, out_f), dtype=torch.float32, device=ctx.device)
                 self.y[name] = y
@@ -463,7 +483,19 @@ class Step:
                                    w_up_ptr=w_up, bias_ptr=bias)
                 ops[0].append(op)
                 ops[1].append(op)
-                self.launches.append(launches_of(mlq, rows, out_f, in_f, True, w_up is not None, ctx.sms))
+                n_l = launches_of(mlq, rows, out_f, in_f, True, w_up is not None, ctx.sms)
+                # the library runs consecutive batched-decode ops on one x as
+                # one grouped launch (up to 4 matrices): no launches of their own
+                xp = self.x[name].data_ptr()
+                if w_up is None and mlq.takes_bgemm(rows, out_f, in_f):
+                    if grp is not None and grp[0] == xp and grp[1] < 4:
+                        grp = (xp, grp[1] + 1)
+                        n_l = 0
+                    else:
+                        grp = (xp, 1)
+                else:
+                    grp = None
+                self.launches.append(n_l)
             self.names.append(name)
             nb = weight_bytes(fmt, e - b, in_f)
             self.op_bytes.append(2 * nb if (pair and name == pair[0]) else nb)
@@ -619,7 +651,7 @@ def _roof(nbytes, launch_ms, b2b_ms, wl, ctx, st, j):
     out_f, in_f = next((o, i) for n, o, i in wl["matrices"] if n == name)
     b, e = st.plan.rows(name)
     local = st.plan.place[name] != "shard"
-    bgemm = local and mlq.takes_bgemm(wl["rows"], out_f, in_f)
+    bgemm = mlq.takes_bgemm(wl["rows"], e - b, in_f) if e > b else False
     gemm = bgemm or (local and mlq.takes_gemm(wl["rows"], out_f, in_f))
     kernel = (f"bgemm_kernel<{wl['fmt']}> (batched decode)" if bgemm else
               f"gemm_tc_kernel<{wl['fmt']}>" if gemm else

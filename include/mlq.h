@@ -119,11 +119,13 @@ MLQ_API mlq_status mlq_linear(mlq_format fmt, const void* w, size_t block_count,
  * From MLQ_BGEMM_MIN_ROWS to MLQ_BGEMM_MAX_ROWS rows of x (batched decode),
  * when in_features % 32 == 0 and the weights are 16-B aligned with a 16-B
  * multiple row pitch: the batched-decode tensor-core GEMM (exact fp16
- * weight codes, x split into fp16 hi/lo against a power-of-two block
- * scale, one TMEM accumulator per 32-value block folded in fp32 on the CUDA
- * cores; the work split evenly over the SMs, split row tiles summed by a
- * second kernel in a fixed order).  Otherwise the rule below. */
-#define MLQ_BGEMM_MIN_ROWS 2
+ * weight codes, each row of x split into fp16 hi/lo against a power-of-two
+ * scale of its own, one TMEM accumulator per 32-value block folded in fp32
+ * on the CUDA cores; the work split evenly over the SMs, a split row tile
+ * summed in a fixed order by the last of its CTAs to finish).  Two rows
+ * take the streaming GEMV's two-row pass, which is faster there.
+ * Otherwise the rule below. */
+#define MLQ_BGEMM_MIN_ROWS 3
 #define MLQ_BGEMM_MAX_ROWS 32
 
 /* The tensor-core (tcgen05) GEMM's time hardly

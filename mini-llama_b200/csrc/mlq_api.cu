@@ -215,7 +215,7 @@ mlq_status run_stream(int fmt, const void* w, int out, int in, const float* x, i
     return MLQ_OK;
 }
 
-// Which kernel takes a call: the batched-decode GEMM for 2..32 rows of x,
+// Which kernel takes a call: the batched-decode GEMM for 3..32 rows of x,
 // the tcgen05 GEMM (bf16 hi/lo) for larger calls by MLQ_GEMM_ROWS_RULE, the
 // streaming GEMV otherwise (and the any-alignment GEMV for layouts the
 // streaming kernel does not take).
@@ -242,11 +242,17 @@ mlq_status run_nonstream(Route rt, int fmt, const void* w, int out, int in, cons
     float* u = ep.w2 ? reinterpret_cast<float*>(static_cast<char*>(ws) + wbytes) : nullptr;
     cudaError_t e = cudaSuccess;
     if (rt == Route::kBgemm) {
-        e = mlq::launch_bgemm(fmt, static_cast<const uint8_t*>(w), x, y, out, in, rows, ep.bias, ws, ds->sm_count,
-                              ds->err_flag, stream);
-        if (e == cudaSuccess && ep.w2)
-            e = mlq::launch_bgemm(fmt, static_cast<const uint8_t*>(ep.w2), x, u, out, in, rows, nullptr, ws,
+        if (ep.w2) {
+            // the pair as one grouped launch: gate rows to y, up rows to u
+            const uint8_t* wm[2] = {static_cast<const uint8_t*>(w), static_cast<const uint8_t*>(ep.w2)};
+            float* ym[2] = {y, u};
+            const int om[2] = {out, out};
+            e = mlq::launch_bgemm_group(fmt, 2, wm, ym, om, nullptr, x, in, rows, ws, ds->sm_count, ds->err_flag,
+                                        stream);
+        } else {
+            e = mlq::launch_bgemm(fmt, static_cast<const uint8_t*>(w), x, y, out, in, rows, ep.bias, ws,
                                   ds->sm_count, ds->err_flag, stream);
+        }
         if (e != cudaSuccess) return fail_cuda("bgemm launch", e);
     } else if (rt == Route::kGemm) {
         // many rows of x: the tensor-core GEMM (bias in its store; a pair
@@ -288,7 +294,8 @@ mlq_status run_linear(int fmt, const void* w, int out, int in, const float* x, i
         int split = 1;
         size_t wb = 0;
         if (rt == Route::kBgemm) {
-            wb = mlq::bgemm_workspace_bytes(fmt, in, rows, out, ds->sm_count);
+            const int om[2] = {out, out};
+            wb = mlq::bgemm_group_workspace_bytes(fmt, in, rows, om, ep.w2 ? 2 : 1, ds->sm_count);
         } else if (rt == Route::kGemm) {
             split = mlq::gemm_split(out, in, rows, ds->sm_count);
             wb = mlq::gemm_workspace_bytes(in, rows, out, split);
@@ -414,9 +421,39 @@ mlq_status validate_gather(int fmt, const void* w_shard, size_t shard_block_coun
     return MLQ_OK;
 }
 
-// The shard GEMV with the gather fused in (validated arguments).
+// The shard's product with the gather fused in (validated arguments): the
+// batched-decode GEMM for the rows it takes, else the streaming GEMV; both
+// store every value to each rank's y and end with the same epoch handshake.
 mlq_status run_gather(int fmt, const void* w_shard, int out_features, int in_features, const float* x,
                       int rows, const float* bias, const mlq_gather& mg, cudaStream_t stream) {
+    const int shard = mg.row_end - mg.row_begin;
+    if (shard > 0 && bgemm_supported(fmt, w_shard, shard, in_features, rows)) {
+        int dev = 0;
+        cudaError_t e = cudaGetDevice(&dev);
+        if (e != cudaSuccess) return fail_cuda("cudaGetDevice", e);
+        mlq_status st = MLQ_OK;
+        DeviceState* ds = device_state(dev, &st);
+        if (!ds) return st;
+        void* ws = nullptr;
+        st = stream_workspace(ds, stream, mlq::bgemm_workspace_bytes(fmt, in_features, rows, shard, ds->sm_count),
+                              &ws);
+        if (st != MLQ_OK) return st;
+        mlq::BgemmGather bg;
+        bg.world = mg.world_size;
+        bg.rank = mg.rank;
+        bg.row_offset = mg.row_begin;
+        bg.y_stride = out_features;
+        bg.epoch = mg.epoch;
+        for (int r = 0; r < mg.world_size; ++r) {
+            bg.ys[r] = mg.peer_y[r];
+            bg.peer_flags[r] = mg.peer_flags[r];
+        }
+        bg.local_flags = mg.peer_flags[mg.rank];
+        bg.done_counter = reinterpret_cast<unsigned int*>(mg.peer_flags[mg.rank] + kDoneWord);
+        e = mlq::launch_bgemm(fmt, static_cast<const uint8_t*>(w_shard), x, nullptr, shard, in_features, rows,
+                              bias ? bias + mg.row_begin : nullptr, ws, ds->sm_count, ds->err_flag, stream, &bg);
+        return e == cudaSuccess ? MLQ_OK : fail_cuda("bgemm launch", e);
+    }
     Gather g;
     g.world = mg.world_size;
     g.rank = mg.rank;
@@ -455,6 +492,60 @@ mlq_status run_op(const mlq_linear_op& op, const float* x, float* y, cudaStream_
     ep.w2 = op.w_up;
     ep.bias = op.bias;
     return run_linear(op.fmt, op.w, op.out_features, op.in_features, x, op.rows, y, stream, ep);
+}
+
+// A batch's ops in order, consecutive plain ops that share x (the same
+// device x, format, in_features and rows) and all take the batched-decode
+// GEMM running as one grouped launch (up to kBgemmMaxGroup): Q, K and V of a
+// layer read one x (src/forward.cc:425-435).  xs[i] / ys[i]: op i's device
+// x and y.
+mlq_status run_ops(const mlq_linear_op* ops, int n, const float* const* xs, float* const* ys, cudaStream_t stream) {
+    auto groupable = [&](int i) {
+        const mlq_linear_op& o = ops[i];
+        return !o.gather && !o.w_up && route_of(o.fmt, o.w, nullptr, o.out_features, o.in_features, xs[i], o.rows) ==
+                                           Route::kBgemm;
+    };
+    for (int i = 0; i < n;) {
+        int j = i + 1;
+        if (groupable(i))
+            while (j < n && j - i < mlq::kBgemmMaxGroup && groupable(j) && xs[j] == xs[i] &&
+                   ops[j].fmt == ops[i].fmt && ops[j].in_features == ops[i].in_features &&
+                   ops[j].rows == ops[i].rows)
+                ++j;
+        if (j - i == 1) {
+            mlq_status st = run_op(ops[i], xs[i], ys[i], stream);
+            if (st != MLQ_OK) return st;
+            i = j;
+            continue;
+        }
+        int dev = 0;
+        cudaError_t e = cudaGetDevice(&dev);
+        if (e != cudaSuccess) return fail_cuda("cudaGetDevice", e);
+        mlq_status st = MLQ_OK;
+        DeviceState* ds = device_state(dev, &st);
+        if (!ds) return st;
+        const uint8_t* wm[mlq::kBgemmMaxGroup];
+        float* ym[mlq::kBgemmMaxGroup];
+        int om[mlq::kBgemmMaxGroup];
+        const float* bm[mlq::kBgemmMaxGroup];
+        for (int k = i; k < j; ++k) {
+            wm[k - i] = static_cast<const uint8_t*>(ops[k].w);
+            ym[k - i] = ys[k];
+            om[k - i] = ops[k].out_features;
+            bm[k - i] = ops[k].bias;
+        }
+        void* ws = nullptr;
+        st = stream_workspace(
+            ds, stream,
+            mlq::bgemm_group_workspace_bytes(ops[i].fmt, ops[i].in_features, ops[i].rows, om, j - i, ds->sm_count),
+            &ws);
+        if (st != MLQ_OK) return st;
+        e = mlq::launch_bgemm_group(ops[i].fmt, j - i, wm, ym, om, bm, xs[i], ops[i].in_features, ops[i].rows, ws,
+                                    ds->sm_count, ds->err_flag, stream);
+        if (e != cudaSuccess) return fail_cuda("bgemm launch", e);
+        i = j;
+    }
+    return MLQ_OK;
 }
 
 
@@ -768,11 +859,13 @@ MLQ_API mlq_status mlq_linear_batch(const mlq_linear_op* ops, int n, mlq_stream 
             if (st != MLQ_OK) return st;
         }
         cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+        std::vector<const float*> xs(n);
+        std::vector<float*> ys(n);
         for (int i = 0; i < n; ++i) {
-            mlq_status st = run_op(ops[i], ops[i].x, ops[i].y, s);
-            if (st != MLQ_OK) return st;
+            xs[i] = ops[i].x;
+            ys[i] = ops[i].y;
         }
-        return MLQ_OK;
+        return run_ops(ops, n, xs.data(), ys.data(), s);
     } catch (...) {
         return fail(MLQ_ERR_CUDA, "mlq_linear_batch: host exception");
     }
@@ -793,14 +886,26 @@ MLQ_API mlq_status mlq_linear_batch_host(const mlq_linear_op* ops, int n, int de
         if (!ds) return st;
         cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
         std::lock_guard<std::mutex> lock(ds->host_mu);
-        // every op's x and y in one staging buffer each, 256-B aligned slices
+        // every op's x and y in one staging buffer each, 256-B aligned
+        // slices; ops with the same host x (pointer and size) share one upload
         std::vector<size_t> xo(n), yo(n);
+        std::vector<bool> upload(n, true);
         size_t xt = 0, yt = 0;
         for (int i = 0; i < n; ++i) {
-            xo[i] = xt;
             yo[i] = yt;
-            xt += ((size_t)ops[i].rows * ops[i].in_features * sizeof(float) + 255) & ~(size_t)255;
             if (!ops[i].gather) yt += ((size_t)ops[i].rows * ops[i].out_features * sizeof(float) + 255) & ~(size_t)255;
+            int same = -1;
+            for (int k = 0; k < i && same < 0; ++k)
+                if (upload[k] && ops[k].x == ops[i].x && ops[k].rows == ops[i].rows &&
+                    ops[k].in_features == ops[i].in_features)
+                    same = k;
+            if (same >= 0) {
+                xo[i] = xo[same];
+                upload[i] = false;
+                continue;
+            }
+            xo[i] = xt;
+            xt += ((size_t)ops[i].rows * ops[i].in_features * sizeof(float) + 255) & ~(size_t)255;
         }
         if ((st = ensure(&ds->x_stage, &ds->x_cap, xt)) != MLQ_OK) return st;
         if (yt > 0 && (st = ensure(&ds->y_stage, &ds->y_cap, yt)) != MLQ_OK) return st;
@@ -808,13 +913,18 @@ MLQ_API mlq_status mlq_linear_batch_host(const mlq_linear_op* ops, int n, int de
         char* ys = reinterpret_cast<char*>(ds->y_stage);
         cudaError_t e = cudaSuccess;
         for (int i = 0; i < n && e == cudaSuccess; ++i)
-            e = cudaMemcpyAsync(xs + xo[i], ops[i].x, (size_t)ops[i].rows * ops[i].in_features * sizeof(float),
-                                cudaMemcpyHostToDevice, s);
+            if (upload[i])
+                e = cudaMemcpyAsync(xs + xo[i], ops[i].x, (size_t)ops[i].rows * ops[i].in_features * sizeof(float),
+                                    cudaMemcpyHostToDevice, s);
         if (e != cudaSuccess) return fail_cuda("cudaMemcpyAsync (x upload)", e);
+        std::vector<const float*> xd(n);
+        std::vector<float*> yd(n);
         for (int i = 0; i < n; ++i) {
-            st = run_op(ops[i], reinterpret_cast<const float*>(xs + xo[i]), reinterpret_cast<float*>(ys + yo[i]), s);
-            if (st != MLQ_OK) return st;
+            xd[i] = reinterpret_cast<const float*>(xs + xo[i]);
+            yd[i] = reinterpret_cast<float*>(ys + yo[i]);
         }
+        st = run_ops(ops, n, xd.data(), yd.data(), s);
+        if (st != MLQ_OK) return st;
         for (int i = 0; i < n && e == cudaSuccess; ++i) {
             // a gathered op's full y is this rank's peer_y entry
             const void* src = ops[i].gather ? static_cast<const void*>(ops[i].gather->peer_y[ops[i].gather->rank])

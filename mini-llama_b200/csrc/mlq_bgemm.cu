@@ -1,4 +1,4 @@
-// mlq_bgemm.cu -- batched-decode GEMM on the tensor cores: 2..32 rows of x
+// mlq_bgemm.cu -- batched-decode GEMM on the tensor cores: 3..32 rows of x
 // against a quantized matrix, the regime of batched decoding (a handful of
 // sequences, one new token each) where the work is still bound by reading
 // the weights once, but too many rows for the CUDA-core GEMV.
@@ -81,6 +81,12 @@ constexpr int kMinBlocksPerCta = 16;
 
 constexpr int cmin(int a, int b) { return a < b ? a : b; }
 constexpr int kBadExp = 0x7fffffff;  // token exponent of an x row holding NaN / Inf
+constexpr unsigned int kBgemmDonePoison = 1u << 16;  // added to the completion count by a CTA that gave up
+
+// the weights' tensor maps of a launch's matrices
+struct WMaps {
+    CUtensorMap m[kBgemmMaxGroup];
+};
 
 // TP: padded tokens (8, 16 or 32); the MMA's N is 2 TP (x hi, then x lo).
 template <int F, int TP>
@@ -119,14 +125,31 @@ struct BCfg {
     static_assert(W_ROW % 16 == 0, "W chunk row must be 16-byte granular");
 };
 
+// A launch computes 1..kBgemmMaxGroup matrices that share x (and the
+// format and in_features): their row tiles one after another, tiles
+// [tile0[m], tile0[m + 1]) being matrix m's.
 struct BgemmArgs {
-    float* y;             // [T][out]
-    const float* bias;    // [out] or null
+    int nmat;
+    int tile0[kBgemmMaxGroup + 1];
+    int out_m[kBgemmMaxGroup];             // rows of matrix m
+    float* ym[kBgemmMaxGroup];             // y of matrix m, [T][out_m] (nmat > 1)
+    const float* bias_m[kBgemmMaxGroup];   // bias of matrix m ([out_m]) or null
+    // nmat == 1: output copies (this GPU's y, then -- sharded -- the peers'), [T][y_stride]
+    float* ys[kMaxWorld];
+    int ny;                // copies
+    int y_stride;          // features of a y row
+    int row_offset;        // y column of this launch's row 0
     const int* tok_exp;   // [TP]: x row t was scaled by 2^-tok_exp[t] (kBadExp: it holds NaN / Inf)
     const float* xsum;    // [kb rounded up to 8][TP]: block sums of the scaled x (q4_1), else null
     float* part;          // [grid][2][TP][BM]: partial sums of partly covered row tiles
     int* tile_cnt;        // [row tiles]: CTAs done with a split tile (zeroed by the x-split kernel)
-    int out, in, T, kb;   // kb = blocks per row
+    // sharded calls (world > 1): the completion handshake
+    int world, rank;
+    uint32_t epoch;
+    uint32_t* peer_flags[kMaxWorld];
+    uint32_t* local_flags;
+    unsigned int* done_counter;
+    int in, T, kb;        // kb = blocks per row
     int total;            // units = row tiles x kb (<= kMaxUnits)
     int* err;
 };
@@ -186,7 +209,7 @@ __device__ __forceinline__ void for_each_chunk(int f0, int f1, int kb, Fn&& fn) 
 
 template <int F, int TP>
 __global__ void __launch_bounds__(kThreads, 1)
-    bgemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x, BgemmArgs a) {
+    bgemm_kernel(const __grid_constant__ WMaps tm_w, const __grid_constant__ CUtensorMap tm_x, BgemmArgs a) {
     using C = BCfg<F, TP>;
     constexpr int CS = C::CS, AS = C::AS, NG = C::NG, N = C::N, SB = C::SB, SPC = C::SPC;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -196,6 +219,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __shared__ uint32_t tmem_base_s;
     __shared__ int abort_flag;
     __shared__ int fix_tile[2];  // split tiles (first / last of the range) this CTA finished last, else -1
+    __shared__ int tok_exp_s[TP];  // the token exponents (fold warps, after the x split)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -242,11 +266,50 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     // the fold warps' own barrier (named barrier 1)
     auto fold_bar_sync = [&]() { asm volatile("bar.sync 1, %0;" ::"n"(kFoldWarps * 32) : "memory"); };
-    // y of token tt and row o from an unscaled total (bias bo)
-    auto store_y = [&](int tt, int o, float v, float bo) {
-        const int e = a.tok_exp[tt];
-        v = e == kBadExp ? __int_as_float(0x7fc00000) : ldexpf(v, e);
-        a.y[(long long)tt * a.out + o] = a.bias ? __fadd_rn(v, bo) : v;
+    // Per-matrix arguments by constant indices only: a kernel-parameter
+    // array indexed at run time is read far more slowly.
+    auto pick = [](const auto& arr, int m) {
+        auto v = arr[0];
+#pragma unroll
+        for (int k = 1; k < kBgemmMaxGroup; ++k)
+            if (m == k) v = arr[k];
+        return v;
+    };
+    // the matrix of row tile t
+    auto mat_of = [&](int t) {
+        int m = 0;
+#pragma unroll
+        for (int k = 1; k < kBgemmMaxGroup; ++k)
+            if (k < a.nmat && t >= a.tile0[k]) m = k;
+        return m;
+    };
+    // y of token tt from an unscaled total: times 2^e_t (a multiply by an
+    // exact power of two while 2^e_t is a normal float: the same correctly
+    // rounded result as ldexpf), plus the bias bo if has_bias
+    auto scaled = [&](int tt, float v, bool has_bias, float bo) {
+        const int e = tok_exp_s[tt];
+        if (e >= -126 && e <= 127) v = __fmul_rn(v, __int_as_float((e + 127) << 23));
+        else v = e == kBadExp ? __int_as_float(0x7fc00000) : ldexpf(v, e);
+        return has_bias ? __fadd_rn(v, bo) : v;
+    };
+    // where matrix m's row o of token 0 goes, and the stride between tokens
+    auto y_row = [&](int m, int o, long long& stride) {
+        if (a.nmat == 1) {
+            stride = a.y_stride;
+            return a.ys[0] + a.row_offset + o;
+        }
+        stride = pick(a.out_m, m);
+        return pick(a.ym, m) + o;
+    };
+    // the stores of one value: y, and -- sharded -- every peer's y
+    auto store_y = [&](float* yp, long long off, float v) {
+        yp[off] = v;
+        if (a.ny > 1) {
+            const long long base = yp + off - a.ys[0];
+#pragma unroll
+            for (int d = 1; d < kMaxWorld; ++d)
+                if (d < a.ny) a.ys[d][base] = v;
+        }
     };
     // the CTAs [c0, c1] whose ranges cover row tile t
     auto tile_ctas = [&](int t, int& c0, int& c1) {
@@ -302,7 +365,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (aborted()) return false;
                 const uint32_t fb = smem_u32(&c_full[s]);
                 mbar_arrive_expect_tx(fb, (uint32_t)(C::W_TILE + C::B_TILE + C::SC_BYTES));
-                tma_load_2d(w_st(s), &tm_w, c * (C::W_ROW / C::W_ESZ), t * BM, fb);
+                const int m = mat_of(t);
+                tma_load_2d(w_st(s), &tm_w.m[m], c * (C::W_ROW / C::W_ESZ), (t - pick(a.tile0, m)) * BM, fb);
                 if (dep) {
                     issue_x(s, c);
                 } else {
@@ -487,6 +551,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         // tokens folded: T rounded up to 4 (the rest of the TP columns are zero)
         const int nt = (a.T + 3) & ~3;
         grid_dependency_wait();  // the token exponents come from the x-split kernel
+        if (threadIdx.x - 32 * kFoldWarp0 < TP) tok_exp_s[threadIdx.x - 32 * kFoldWarp0] = a.tok_exp[threadIdx.x - 32 * kFoldWarp0];
+        fold_bar_sync();
         float acc[TP];
 #pragma unroll
         for (int t = 0; t < TP; ++t) acc[t] = 0.f;
@@ -494,14 +560,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         int seg_tile = -1;
         auto flush = [&](int t, int b_lo, int b_hi) {
             // the CTA's segment of row tile t ends
-            const int o = t * BM + row;
-            const float bo = (a.bias && o < a.out) ? a.bias[o] : 0.f;
+            const int m = mat_of(t);
+            const int o = (t - pick(a.tile0, m)) * BM + row;
+            const int om = pick(a.out_m, m);
+            const float* bm = pick(a.bias_m, m);
+            const float bo = (bm && o < om) ? bm[o] : 0.f;
             if (b_lo == 0 && b_hi == a.kb) {
-                if (o < a.out) {
+                if (o < om) {
+                    long long ys;
+                    float* yp = y_row(m, o, ys);
 #pragma unroll
                     for (int tt = 0; tt < TP; ++tt) {
                         if (tt >= a.T) break;
-                        store_y(tt, o, acc[tt], bo);
+                        store_y(yp, tt * ys, scaled(tt, acc[tt], bm != nullptr, bo));
                     }
                 }
             } else {
@@ -516,8 +587,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (warp == kFoldWarp0 && lane == 0) {
                     int c0, c1;
                     tile_ctas(t, c0, c1);
-                    __threadfence();
-                    if (atomicAdd(&a.tile_cnt[t], 1) == c1 - c0) fix_tile[slot01] = t;  // the whole CTA sums it at the end
+                    __threadfence();  // this CTA's part, before its count
+                    if (atomicAdd(&a.tile_cnt[t], 1) == c1 - c0) {
+                        __threadfence();  // the other CTAs' parts (their counts came first)
+                        fix_tile[slot01] = t;  // summed after the loop, past a fold barrier
+                    }
                 }
             }
 #pragma unroll
@@ -612,6 +686,51 @@ __global__ void __launch_bounds__(kThreads, 1)
             return !aborted();
         });
         if (last_t >= 0 && !aborted()) flush(last_t, last_lo, last_hi);
+        // Split tiles this CTA finished last: y = the tile's parts added in
+        // CTA order, scaled, plus the bias.  A fold thread owns a row; the
+        // loads of all its parts (16 tokens x 4 CTAs at a time) go out together.
+        fold_bar_sync();
+        for (int k = 0; k < 2; ++k) {
+            const int t = fix_tile[k];
+            if (t < 0 || aborted()) continue;
+            const int m = mat_of(t);
+            const int o = (t - pick(a.tile0, m)) * BM + row;
+            if (o >= pick(a.out_m, m)) continue;
+            int c0, c1;
+            tile_ctas(t, c0, c1);
+            const int u0 = t * a.kb;
+            const float* bm = pick(a.bias_m, m);
+            const float bo = bm ? bm[o] : 0.f;
+            long long ys;
+            float* yp = y_row(m, o, ys);
+            constexpr int TG = TP < 16 ? TP : 16;
+#pragma unroll
+            for (int g = 0; g < TP; g += TG) {
+                if (g >= a.T) break;
+                float v[TG];
+#pragma unroll
+                for (int u = 0; u < TG; ++u) v[u] = 0.f;
+                for (int c = c0; c <= c1; c += 4) {
+                    float pv[4][TG];
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const int cc = c + q <= c1 ? c + q : c1;
+                        const int sl = unit_begin(a.total, cc, G) >= u0 ? 0 : 1;
+                        const float* pp = a.part + (((long long)cc * 2 + sl) * TP + g) * BM + row;
+#pragma unroll
+                        for (int u = 0; u < TG; ++u) pv[q][u] = __ldcg(pp + u * BM);
+                    }
+#pragma unroll
+                    for (int q = 0; q < 4; ++q)
+                        if (c + q <= c1)
+#pragma unroll
+                            for (int u = 0; u < TG; ++u) v[u] = c + q == c0 ? pv[q][u] : __fadd_rn(v[u], pv[q][u]);
+                }
+#pragma unroll
+                for (int u = 0; u < TG; ++u)
+                    if (g + u < a.T) store_y(yp, (g + u) * ys, scaled(g + u, v[u], bm != nullptr, bo));
+            }
+        }
     }
 
     // every warp is done with TMEM and shared memory; warp 1 frees TMEM
@@ -624,51 +743,36 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_dealloc(tmem, C::TMEM_COLS);
     }
 
-    // Split tiles this CTA finished last: y = the parts of the tile's CTAs
-    // added in CTA order, scaled, plus the bias.  Every thread of the CTA
-    // takes up to 8 (row, token) outputs and issues the loads of their parts
-    // (four CTAs at a time) together.
-    __syncthreads();
-    for (int k = 0; k < 2; ++k) {
-        const int t = fix_tile[k];
-        if (t < 0 || aborted()) continue;
-        __threadfence();  // the other CTAs' parts (their counter increments came first)
-        int c0, c1;
-        tile_ctas(t, c0, c1);
-        const int u0 = t * a.kb;
-        const int n_out = a.T * BM;
-        constexpr int U = 8;
-        for (int base = 0; base < n_out; base += U * kThreads) {
-            float v[U];
-#pragma unroll
-            for (int u = 0; u < U; ++u) v[u] = 0.f;
-            for (int c = c0; c <= c1; c += 4) {
-                const float* pp[4];
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const int cc = c + q <= c1 ? c + q : c1;
-                    const int sl = unit_begin(a.total, cc, G) >= u0 ? 0 : 1;
-                    pp[q] = a.part + ((long long)cc * 2 + sl) * TP * BM;
+    if (a.world > 1) {
+        // Sharded call: this CTA's rows are in every rank's y.  Every CTA
+        // counts itself once (with kBgemmDonePoison after giving up), so the
+        // counter is back at zero for the next call; the last CTA publishes
+        // the epoch to every rank, unless one gave up (then the peers' waits
+        // run out and report code 4), and waits until every rank's slice
+        // has landed here.  Ordering: this CTA's y stores happen before the
+        // GPU-scope acquire-release count (__syncthreads, CTA scope); the
+        // last CTA's one system-scope fence then publishes every CTA's stores
+        // ahead of the flags (the fence is cumulative).
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            const bool ok = !aborted();
+            const unsigned int prev = atom_add_acq_rel_gpu(a.done_counter, ok ? 1u : 1u + kBgemmDonePoison);
+            if ((prev & (kBgemmDonePoison - 1u)) == gridDim.x - 1) {
+                *a.done_counter = 0u;  // every CTA of this launch has counted
+                if (ok && prev < kBgemmDonePoison) {
+                    fence_acq_rel_sys();
+                    for (int r = 0; r < a.world; ++r) st_relaxed_sys(a.peer_flags[r] + a.rank, a.epoch);
+                    const uint64_t t0 = global_ns();
+                    for (int r = 0; r < a.world; ++r) {
+                        while ((int)(ld_acquire_sys(a.local_flags + r) - a.epoch) < 0) {
+                            if (global_ns() - t0 > kWaitLimitNs) {
+                                report_error(a.err, 4);
+                                return;
+                            }
+                            __nanosleep(64);
+                        }
+                    }
                 }
-                float pv[U][4];
-#pragma unroll
-                for (int u = 0; u < U; ++u) {
-                    const int i = base + u * kThreads + (int)threadIdx.x;
-#pragma unroll
-                    for (int q = 0; q < 4; ++q)
-                        pv[u][q] = (i < n_out && c + q <= c1) ? __ldcg(pp[q] + (i / BM) * BM + i % BM) : 0.f;
-                }
-#pragma unroll
-                for (int u = 0; u < U; ++u)
-#pragma unroll
-                    for (int q = 0; q < 4; ++q)
-                        if (c + q <= c1) v[u] = c + q == c0 ? pv[u][q] : __fadd_rn(v[u], pv[u][q]);
-            }
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-                const int i = base + u * kThreads + (int)threadIdx.x;
-                const int r = i % BM, tt = i / BM, o = t * BM + r;
-                if (i < n_out && o < a.out) store_y(tt, o, v[u], a.bias ? a.bias[o] : 0.f);
             }
         }
     }
@@ -793,11 +897,21 @@ int grid_for(int total, int sm_count) {
 
 size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
 
+// One matrix of a launch.
+struct GroupMat {
+    const uint8_t* w;
+    float* y;
+    int out;
+    const float* bias;
+};
+
 template <int F, int TP>
-cudaError_t launch_t(const uint8_t* w, const float* x, float* y, int out, int in, int T, const float* bias,
-                     void* ws, int sm_count, int* err, cudaStream_t stream) {
+cudaError_t launch_t(const GroupMat* mats, int nmat, const float* x, int in, int T, void* ws, int sm_count, int* err,
+                     cudaStream_t stream, const BgemmGather* g) {
     using C = BCfg<F, TP>;
     const int kb = in / kQK;
+    int tiles = 0;
+    for (int m = 0; m < nmat; ++m) tiles += (mats[m].out + BM - 1) / BM;
     char* p = static_cast<char*>(ws);
     __half* xb = reinterpret_cast<__half*>(p);
     p += align256((size_t)2 * TP * in * sizeof(__half));
@@ -811,9 +925,30 @@ cudaError_t launch_t(const uint8_t* w, const float* x, float* y, int out, int in
         p += align256(kbp * TP * sizeof(float));
     }
     int* tile_cnt = reinterpret_cast<int*>(p);
-    const int tiles = (out + BM - 1) / BM;
     p += align256((size_t)tiles * sizeof(int));
     float* part = reinterpret_cast<float*>(p);
+
+    const long long row_bytes = (long long)kb * C::BS;
+    WMaps mw{};
+    for (int m = 0; m < nmat; ++m)
+        if (!make_map_2d(&mw.m[m], F == kQ8_0 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8,
+                         const_cast<uint8_t*>(mats[m].w), (uint64_t)(row_bytes / C::W_ESZ), (uint64_t)mats[m].out,
+                         (uint64_t)row_bytes, (uint32_t)(C::W_ROW / C::W_ESZ), BM, CU_TENSOR_MAP_SWIZZLE_NONE))
+            return cudaErrorInvalidValue;
+    CUtensorMap mx;
+    if (!make_map_2d(&mx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xb, (uint64_t)in, (uint64_t)(2 * TP), (uint64_t)in * 2, 64,
+                     (uint32_t)(2 * TP), CU_TENSOR_MAP_SWIZZLE_128B))
+        return cudaErrorInvalidValue;
+
+    static std::atomic<bool> attr_set[64];  // one value per instantiation: racing first calls agree
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaError_t e = cudaSuccess;
+    if (dev >= 64 || !attr_set[dev].load(std::memory_order_acquire)) {
+        e = cudaFuncSetAttribute(bgemm_kernel<F, TP>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+        if (e != cudaSuccess) return e;
+        if (dev < 64) attr_set[dev].store(true, std::memory_order_release);
+    }
 
     // both launches may start while the kernel before them drains
     // (programmatic dependent launch); each waits on the device for the data
@@ -828,37 +963,44 @@ cudaError_t launch_t(const uint8_t* w, const float* x, float* y, int out, int in
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, bgemm_xsplit_kernel<TP>, x, T, in, xb, tok_exp, xsum, tile_cnt, tiles);
+    e = cudaLaunchKernelEx(&cfg, bgemm_xsplit_kernel<TP>, x, T, in, xb, tok_exp, xsum, tile_cnt, tiles);
     if (e != cudaSuccess) return e;
 
-    const long long row_bytes = (long long)kb * C::BS;
-    CUtensorMap mw, mx;
-    if (!make_map_2d(&mw, F == kQ8_0 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8,
-                     const_cast<uint8_t*>(w), (uint64_t)(row_bytes / C::W_ESZ), (uint64_t)out, (uint64_t)row_bytes,
-                     (uint32_t)(C::W_ROW / C::W_ESZ), BM, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-        !make_map_2d(&mx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xb, (uint64_t)in, (uint64_t)(2 * TP), (uint64_t)in * 2, 64,
-                     (uint32_t)(2 * TP), CU_TENSOR_MAP_SWIZZLE_128B))
-        return cudaErrorInvalidValue;
-
-    static std::atomic<bool> attr_set[64];  // one value per instantiation: racing first calls agree
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev >= 64 || !attr_set[dev].load(std::memory_order_acquire)) {
-        e = cudaFuncSetAttribute(bgemm_kernel<F, TP>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-        if (e != cudaSuccess) return e;
-        if (dev < 64) attr_set[dev].store(true, std::memory_order_release);
-    }
     BgemmArgs a{};
-    a.y = y;
-    a.bias = bias;
+    a.nmat = nmat;
+    a.tile0[0] = 0;
+    for (int m = 0; m < nmat; ++m) {
+        a.tile0[m + 1] = a.tile0[m] + (mats[m].out + BM - 1) / BM;
+        a.out_m[m] = mats[m].out;
+        a.ym[m] = mats[m].y;
+        a.bias_m[m] = mats[m].bias;
+    }
+    if (g) {
+        for (int r = 0; r < g->world; ++r) {
+            a.ys[r] = g->ys[r];
+            a.peer_flags[r] = g->peer_flags[r];
+        }
+        a.ny = g->world;
+        a.y_stride = g->y_stride;
+        a.row_offset = g->row_offset;
+        a.world = g->world;
+        a.rank = g->rank;
+        a.epoch = g->epoch;
+        a.local_flags = g->local_flags;
+        a.done_counter = g->done_counter;
+    } else {
+        a.ys[0] = mats[0].y;
+        a.ny = 1;
+        a.y_stride = mats[0].out;
+        a.world = 1;
+    }
     a.tok_exp = tok_exp;
     a.xsum = xsum;
     a.part = part;
-    a.out = out;
     a.in = in;
     a.T = T;
     a.kb = kb;
-    a.total = ((out + BM - 1) / BM) * kb;
+    a.total = tiles * kb;
     a.err = err;
     a.tile_cnt = tile_cnt;
     const int G = grid_for(a.total, sm_count);
@@ -869,13 +1011,23 @@ cudaError_t launch_t(const uint8_t* w, const float* x, float* y, int out, int in
 }
 
 template <int F>
-cudaError_t launch_f(const uint8_t* w, const float* x, float* y, int out, int in, int T, const float* bias, void* ws,
-                     int sm_count, int* err, cudaStream_t stream) {
+cudaError_t launch_f(const GroupMat* mats, int nmat, const float* x, int in, int T, void* ws, int sm_count, int* err,
+                     cudaStream_t stream, const BgemmGather* g) {
     switch (tp_for(T)) {
-        case 8: return launch_t<F, 8>(w, x, y, out, in, T, bias, ws, sm_count, err, stream);
-        case 16: return launch_t<F, 16>(w, x, y, out, in, T, bias, ws, sm_count, err, stream);
-        default: return launch_t<F, 32>(w, x, y, out, in, T, bias, ws, sm_count, err, stream);
+        case 8: return launch_t<F, 8>(mats, nmat, x, in, T, ws, sm_count, err, stream, g);
+        case 16: return launch_t<F, 16>(mats, nmat, x, in, T, ws, sm_count, err, stream, g);
+        default: return launch_t<F, 32>(mats, nmat, x, in, T, ws, sm_count, err, stream, g);
     }
+}
+
+cudaError_t launch_fmt(int fmt, const GroupMat* mats, int nmat, const float* x, int in, int rows, void* ws,
+                       int sm_count, int* err, cudaStream_t stream, const BgemmGather* g) {
+    switch (fmt) {
+        case kQ8_0: return launch_f<kQ8_0>(mats, nmat, x, in, rows, ws, sm_count, err, stream, g);
+        case kQ4_0: return launch_f<kQ4_0>(mats, nmat, x, in, rows, ws, sm_count, err, stream, g);
+        case kQ4_1: return launch_f<kQ4_1>(mats, nmat, x, in, rows, ws, sm_count, err, stream, g);
+    }
+    return cudaErrorInvalidValue;
 }
 
 }  // namespace
@@ -899,14 +1051,31 @@ size_t bgemm_workspace_bytes(int fmt, int in, int rows, int out, int sm_count) {
     return b + (size_t)G * 2 * tp * BM * 4;
 }
 
+size_t bgemm_group_workspace_bytes(int fmt, int in, int rows, const int* out, int nmat, int sm_count) {
+    int tiles = 0;
+    for (int m = 0; m < nmat; ++m) tiles += (out[m] + BM - 1) / BM;
+    return bgemm_workspace_bytes(fmt, in, rows, tiles * BM, sm_count);
+}
+
 cudaError_t launch_bgemm(int fmt, const uint8_t* w, const float* x, float* y, int out, int in, int rows,
-                         const float* bias, void* ws, int sm_count, int* err, cudaStream_t stream) {
-    switch (fmt) {
-        case kQ8_0: return launch_f<kQ8_0>(w, x, y, out, in, rows, bias, ws, sm_count, err, stream);
-        case kQ4_0: return launch_f<kQ4_0>(w, x, y, out, in, rows, bias, ws, sm_count, err, stream);
-        case kQ4_1: return launch_f<kQ4_1>(w, x, y, out, in, rows, bias, ws, sm_count, err, stream);
+                         const float* bias, void* ws, int sm_count, int* err, cudaStream_t stream,
+                         const BgemmGather* g) {
+    const GroupMat m{w, y, out, bias};
+    return launch_fmt(fmt, &m, 1, x, in, rows, ws, sm_count, err, stream, g);
+}
+
+cudaError_t launch_bgemm_group(int fmt, int nmat, const uint8_t* const* w, float* const* y, const int* out,
+                               const float* const* bias, const float* x, int in, int rows, void* ws, int sm_count,
+                               int* err, cudaStream_t stream) {
+    if (nmat < 1 || nmat > kBgemmMaxGroup) return cudaErrorInvalidValue;
+    GroupMat mats[kBgemmMaxGroup];
+    long long units = 0;
+    for (int m = 0; m < nmat; ++m) {
+        mats[m] = GroupMat{w[m], y[m], out[m], bias ? bias[m] : nullptr};
+        units += (long long)((out[m] + BM - 1) / BM) * (in / kQK);
     }
-    return cudaErrorInvalidValue;
+    if (units > kMaxUnits) return cudaErrorInvalidValue;
+    return launch_fmt(fmt, mats, nmat, x, in, rows, ws, sm_count, err, stream, nullptr);
 }
 
 }  // namespace mlq

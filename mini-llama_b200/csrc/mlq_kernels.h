@@ -116,9 +116,40 @@ bool bgemm_shape_ok(int fmt, const void* w, int out, int in, int rows);
 // block sums), split-tile counters and the split row tiles' partial sums.
 size_t bgemm_workspace_bytes(int fmt, int in, int rows, int out, int sm_count);
 
+// A row-sharded call (world > 1): this rank's `out` rows are rows
+// [row_offset, row_offset + out) of a y with y_stride features; every value
+// is stored to each rank's y (ys[r], peer memory), then the launch's last
+// CTA publishes `epoch` to every rank's flags and waits (bounded) for every
+// rank's (the streaming GEMV's sharded-call protocol).
+struct BgemmGather {
+    int world = 1, rank = 0;
+    int row_offset = 0, y_stride = 0;
+    float* ys[kMaxWorld] = {};
+    uint32_t epoch = 0;
+    uint32_t* peer_flags[kMaxWorld] = {};
+    uint32_t* local_flags = nullptr;
+    unsigned int* done_counter = nullptr;
+};
+
+// Matrices one batched-decode launch may compute (sharing x).
+constexpr int kBgemmMaxGroup = 4;
+
+// Workspace of a grouped launch over nmat matrices of out[m] rows.
+size_t bgemm_group_workspace_bytes(int fmt, int in, int rows, const int* out, int nmat, int sm_count);
+
+// y[m][rows][out[m]] = x W[m]^T (+ bias[m]) for nmat <= kBgemmMaxGroup
+// matrices sharing x, format and in_features (each bgemm_shape_ok): one x
+// split, one GEMM launch over all their row tiles.  bias may be null, or an
+// array of nmat (possibly null) pointers.
+cudaError_t launch_bgemm_group(int fmt, int nmat, const uint8_t* const* w, float* const* y, const int* out,
+                               const float* const* bias, const float* x, int in, int rows, void* ws, int sm_count,
+                               int* err, cudaStream_t stream);
+
 // y[rows][out] = x W^T (+ bias); ws holds bgemm_workspace_bytes(...) bytes.
+// With g (a sharded call), y is unused: the output goes to g->ys.
 cudaError_t launch_bgemm(int fmt, const uint8_t* w, const float* x, float* y, int out, int in, int rows,
-                         const float* bias, void* ws, int sm_count, int* err, cudaStream_t stream);
+                         const float* bias, void* ws, int sm_count, int* err, cudaStream_t stream,
+                         const BgemmGather* g = nullptr);
 
 // Quantize fp32 [rows][cols] -> blocks, reference rules (mlq_convert.cu).
 cudaError_t launch_quantize(int fmt, const float* src, long long rows, int cols, uint8_t* blocks,

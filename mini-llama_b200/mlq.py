@@ -213,7 +213,7 @@ GEMM_LARGE_MIN_ROWS = 5
 GEMM_LARGE_MIN_WEIGHTS = 1 << 25
 
 
-BGEMM_MIN_ROWS = 2
+BGEMM_MIN_ROWS = 3
 BGEMM_MAX_ROWS = 32
 
 

@@ -64,24 +64,27 @@ def test_arguments_validated(pkg):
     assert e.value.status == 2
 
 
-def test_peer_that_never_signals_times_out(oracle, pkg):
+@pytest.mark.parametrize("rows", [1, 8])
+def test_peer_that_never_signals_times_out(oracle, pkg, rows):
     """Rank 0 of a world of two whose rank 1 never runs: the handshake wait
     must end after its 2 s bound with device error code 4, and rank 0's own
     rows must still be in y.  (The flag nothing sets is the only failure
-    injected; no fault, no hang.)"""
+    injected; no fault, no hang.)  One row takes the streaming GEMV, eight
+    the batched-decode GEMM; both end with the same handshake."""
     mlq = pkg.mlq
     fmt, out_f, in_f = "q4_0", 1024, 2048
     blocks = oracle.quantize(fmt, pkg.synth.normal((out_f, in_f), seed=41, std=0.02))
-    x = pkg.synth.normal((1, in_f), seed=42)
+    x = pkg.synth.normal((rows, in_f), seed=42)
     half = 512
     bpr = in_f // 32
+    assert mlq.takes_bgemm(rows, half, in_f) == (rows == 8)
     w_d, x_d = dev(blocks[: half * bpr * 18]), dev(x)
-    y0 = torch.zeros((1, out_f), dtype=torch.float32, device="cuda")
-    y1 = torch.zeros((1, out_f), dtype=torch.float32, device="cuda")  # the absent peer's y
+    y0 = torch.zeros((rows, out_f), dtype=torch.float32, device="cuda")
+    y1 = torch.zeros((rows, out_f), dtype=torch.float32, device="cuda")  # the absent peer's y
     f0 = torch.zeros(mlq.flag_bytes() // 4, dtype=torch.int32, device="cuda")
     f1 = torch.zeros(mlq.flag_bytes() // 4, dtype=torch.int32, device="cuda")
     assert mlq.device_error(0) == 0
-    mlq.linear_allgather(fmt, w_d.data_ptr(), half * bpr, out_f, in_f, 0, half, x_d.data_ptr(), 1,
+    mlq.linear_allgather(fmt, w_d.data_ptr(), half * bpr, out_f, in_f, 0, half, x_d.data_ptr(), rows,
                          [y0.data_ptr(), y1.data_ptr()], [f0.data_ptr(), f1.data_ptr()], 0, 1,
                          torch.cuda.current_stream().cuda_stream)
     torch.cuda.synchronize()

@@ -124,3 +124,59 @@ def test_batch_host_equals_device_batch(pkg, oracle):
             torch.cuda.synchronize()
             np.testing.assert_array_equal(hy[k].numpy(), yd.cpu().numpy(), err_msg=f"{kind} call {it}")
     assert mlq.device_error(0) == 0
+
+
+@pytest.mark.parametrize("rows", [4, 16])
+def test_batch_groups_ops_sharing_x(pkg, oracle, rows):
+    """Consecutive ops that read one x and take the batched-decode GEMM run
+    as one grouped launch (Q, K, V of a layer; up to four matrices): each
+    op's y within the contract of the oracle and within 1e-5 of the op run
+    alone (a grouped launch splits the work at other points, so the fp32
+    sums of split row tiles may round differently).  The op list: q, k, v
+    (one with a bias) on x0, a matrix on x1 (ends the group), five matrices
+    on x2 (a group of four, then one), and a SwiGLU pair on x2 (its own
+    group of two)."""
+    mlq = pkg.mlq
+    fmt, in_f = "q8_0", 2048
+    specs = [(0, 1024), (0, 256), (0, 256), (1, 640), (2, 300), (2, 128), (2, 1000), (2, 512), (2, 384)]
+    xs = [pkg.synth.normal((rows, in_f), seed=900 + k) for k in range(3)]
+    xd = [dev(x) for x in xs]
+    keep, ops, refs, singles, outs = [], [], [], [], []
+    for k, (xi, out_f) in enumerate(specs):
+        wb = oracle.quantize(fmt, pkg.synth.normal((out_f, in_f), seed=950 + k, std=0.02))
+        w = dev(wb)
+        y = torch.full((rows, out_f), float("nan"), device="cuda")
+        keep.append(w)
+        outs.append(y)
+        assert mlq.takes_bgemm(rows, out_f, in_f)
+        ref = oracle.linear(fmt, xs[xi], wb, out_f)
+        if k == 1:
+            b = pkg.synth.normal((out_f,), seed=990, std=0.5)
+            bd = dev(b)
+            keep.append(bd)
+            ops.append(mlq.linear_op(fmt, w.data_ptr(), out_f, in_f, xd[xi].data_ptr(), rows, y.data_ptr(),
+                                     bias_ptr=bd.data_ptr()))
+            singles.append(mlq.linear_bias(fmt, w, out_f, in_f, xd[xi], bd))
+            ref = ref + b[None, :]
+        else:
+            ops.append(mlq.linear_op(fmt, w.data_ptr(), out_f, in_f, xd[xi].data_ptr(), rows, y.data_ptr()))
+            singles.append(mlq.linear(fmt, w, out_f, in_f, xd[xi]))
+        refs.append(ref)
+    gb = oracle.quantize(fmt, pkg.synth.normal((700, in_f), seed=991, std=0.02))
+    ub = oracle.quantize(fmt, pkg.synth.normal((700, in_f), seed=992, std=0.02))
+    g, u = dev(gb), dev(ub)
+    h = torch.full((rows, 700), float("nan"), device="cuda")
+    keep += [g, u, h]
+    ops.append(mlq.linear_op(fmt, g.data_ptr(), 700, in_f, xd[2].data_ptr(), rows, h.data_ptr(),
+                             w_up_ptr=u.data_ptr()))
+    refs.append(oracle.swiglu(oracle.linear(fmt, xs[2], gb, 700), oracle.linear(fmt, xs[2], ub, 700)))
+    singles.append(None)
+    outs.append(h)
+    mlq.Batch(ops).run(torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    for k, (y, ref, single) in enumerate(zip(outs, refs, singles)):
+        yn = y.cpu().numpy()
+        assert rel_l2_rows(yn, ref).max() <= TOL, k
+        if single is not None:
+            assert rel_l2_rows(yn, single.cpu().numpy()).max() <= 1e-5, k
+    assert mlq.device_error(0) == 0

@@ -1,10 +1,10 @@
 """The batched-decode tensor-core GEMM (csrc/mlq_bgemm.cu) against the CPU
-oracle, through the C ABI (mlq_linear routes 2..32 rows of x with
+oracle, through the C ABI (mlq_linear routes 3..32 rows of x with
 in_features % 32 == 0 to it).
 
 Tolerance (the contract): relative L2 error of every output vector (row of
-y) <= 1e-3.  Covered: every format; 2..32 rows (padded token counts 16 and
-32); partial row tiles; K extents that end inside a 256-value chunk;
+y) <= 1e-3.  Covered: every format; 3..32 rows (padded token counts 8, 16
+and 32); partial row tiles; K extents that end inside a 256-value chunk;
 matrices whose row tiles the work split cuts across CTAs (the fix-up pass),
 at the BASELINE config-4 and config-5 shapes; the fused bias and SwiGLU
 pair; NaN/Inf propagation; activations spanning six orders of magnitude in
@@ -43,7 +43,7 @@ def test_bgemm_matches_oracle(oracle, pkg, fmt, shape):
     out_f, in_f = shape
     blocks = weights(oracle, pkg, fmt, out_f, in_f, seed=out_f + in_f)
     w = dev(blocks)
-    for rows in (2, 3, 7, 8, 9, 16, 17, 32):
+    for rows in (3, 4, 7, 8, 9, 16, 17, 32):
         assert pkg.mlq.takes_bgemm(rows, out_f, in_f)
         x = pkg.synth.normal((rows, in_f), seed=rows * 7 + in_f)
         y = pkg.mlq.linear(fmt, w, out_f, in_f, dev(x)).cpu().numpy()
