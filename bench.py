@@ -74,6 +74,9 @@ WORKLOADS = {
         "name": "qwen2-7b-layer+lm_head q4_0 decode (BASELINE configs[1])",
         "metric": "effective weight GB/s (q4_0 decode GEMV, Qwen2-7B layer + lm_head, batch 1)",
         "fmt": "q4_0", "rows": 1, "matrices": QWEN7B,
+        # qkv and o stay whole on rank 0: a sharded launch has a fixed cost
+        # (stores to every rank, the system-scope release) that outweighs
+        # half of a 5-9 MB matrix
         "shard": {"gate", "up", "down", "lm_head"},
     },
     # The same layer through the fused entry points: the q/k/v bias added in
@@ -460,8 +463,9 @@ class Step:
                 grp = None  # a gathered op is never grouped
                 k = shard_names.index(name)
                 for p in (0, 1):
+                    # publish only: the step ends with one mlq_gather_wait
                     g = mlq.make_gather(ctx.world, ctx.rank, b, e, self.slab.peer_ptrs(p, k),
-                                        ctx.flags.peers, epoch=1)
+                                        ctx.flags.peers, epoch=1, defer_wait=True)
                     self.gathers[p].append(g)
                     ops[p].append(mlq.linear_op(fmt, wp, out_f, in_f, self.x[name].data_ptr(), rows,
                                                 self.slab.local_ptr(p, k), gather=g))
@@ -500,6 +504,9 @@ class Step:
             nb = weight_bytes(fmt, e - b, in_f)
             self.op_bytes.append(2 * nb if (pair and name == pair[0]) else nb)
         self.ops = ops
+        # the step's one cross-rank wait: every rank's highest epoch of the step
+        self.waiter = (mlq.make_gather(ctx.world, ctx.rank, 0, 0, [0] * ctx.world, ctx.flags.peers, epoch=1)
+                       if shard_names else None)
         self.batch = [mlq.Batch(ops[0]), mlq.Batch(ops[1])]
         self.single = [[mlq.Batch([op]) for op in ops[p]] for p in (0, 1)]
         # rotating copies (an L2-sized matrix): one batch per copy
@@ -535,6 +542,13 @@ class Step:
     def _set_epochs(self, parity, epochs):
         for g, ep in zip(self.gathers[parity], epochs):
             g.epoch = ep
+        if self.waiter is not None and epochs:
+            self.waiter.epoch = max(epochs)
+
+    def _wait(self, stream):
+        """The deferred wait of the step's sharded ops (their y complete here)."""
+        if self.waiter is not None:
+            self.ctx.mlq.gather_wait(self.waiter, stream)
 
     def step(self):
         """One pass over the workload: one library call."""
@@ -544,6 +558,7 @@ class Step:
         parity, epochs = self.plan.next_step()
         self._set_epochs(parity, epochs)
         self.batch[parity].run(self.ctx.stream.cuda_stream)
+        self._wait(self.ctx.stream.cuda_stream)
         self.steps_run += 1
 
     def step_host(self, host_batches):
@@ -553,7 +568,9 @@ class Step:
 
     def per_launch_ms(self, rounds):
         """Mean CUDA-event time of each op launched on its own (events around
-        every op of a step, `rounds` steps)."""
+        every op of a step, `rounds` steps).  Each round is queued behind a
+        ~1 ms sleep kernel, so the host has launched the whole round before
+        the GPU reaches it and no event pair spans GPU idle time."""
         torch, s = self.ctx.torch, self.ctx.stream
         n = len(self.names)
         evs = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
@@ -561,10 +578,13 @@ class Step:
         for r in range(rounds):
             parity, epochs = self.plan.next_step()
             self._set_epochs(parity, epochs)
+            with torch.cuda.stream(s):
+                torch.cuda._sleep(2_000_000)
             for j in range(n):
                 evs[r][j][0].record(s)
                 self.single[parity][j].run(s.cuda_stream)
                 evs[r][j][1].record(s)
+            self._wait(s.cuda_stream)  # outside the events: the ranks stay in step
         torch.cuda.synchronize(self.ctx.device)
         return [statistics.mean(evs[r][j][0].elapsed_time(evs[r][j][1]) for r in range(rounds))
                 for j in range(n)]

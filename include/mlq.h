@@ -319,14 +319,31 @@ MLQ_API size_t mlq_flag_bytes(void);
 /* Row-sharded form of one product in a batch: the arguments of
  * mlq_linear_allgather that describe the shard and the gather.  The op's
  * w / block_count are this rank's shard (rows [row_begin, row_end)); its y
- * is ignored: the output lands in peer_y[rank] (and every peer's y). */
+ * is ignored: the output lands in peer_y[rank] (and every peer's y).
+ *
+ * defer_wait = 0: as mlq_linear_allgather, the op's last kernel ends once
+ * every rank's rows have landed in this GPU's y.  defer_wait = 1: it ends
+ * after publishing this rank's epoch; whoever reads y first calls
+ * mlq_gather_wait (in stream order), so a step of several sharded products
+ * pays one cross-rank wait instead of one per product.  Each rank's epochs
+ * must rise from op to op on one flag array: a wait for epoch E then also
+ * covers every earlier epoch of that array.  mlq_linear_batch_host waits
+ * before it copies the y of a deferred op back. */
 typedef struct mlq_gather {
     int world_size, rank;
     int row_begin, row_end;
     float* const* peer_y;         /* world_size pointers */
     uint32_t* const* peer_flags;  /* world_size pointers */
     uint32_t epoch;
+    int defer_wait;               /* 0: wait in the op; 1: mlq_gather_wait later */
 } mlq_gather;
+
+/* Waits, in stream order on `stream`, until every rank of g has published
+ * an epoch >= g->epoch to this rank's flags (g->peer_flags[g->rank]): the
+ * y of every deferred op with that epoch or an earlier one is then complete
+ * here.  One tiny kernel, bounded (2 s, then device error code 4, see
+ * mlq_device_error); nothing to launch in a world of one. */
+MLQ_API mlq_status mlq_gather_wait(const mlq_gather* g, mlq_stream stream);
 
 /* One product y[rows,out] = x[rows,in] W^T (+ bias), or -- w_up set -- the
  * SwiGLU pair h = silu(x W^T) * (x W_up^T) of mlq_linear_swiglu. */

@@ -150,6 +150,7 @@ struct Gather {
     float* const* ys = nullptr;  // world output bases (plain call: &y)
     uint32_t* const* flags = nullptr;
     uint32_t epoch = 0;
+    bool wait = true;  // false: publish the epoch only (a deferred wait follows)
 };
 
 bool streamable(int fmt, const void* w, const float* x, int in) {
@@ -199,6 +200,7 @@ mlq_status run_stream(int fmt, const void* w, int out, int in, const float* x, i
         for (int r = 0; r < g.world; ++r) a.peer_flags[r] = g.flags[r];
         a.local_flags = g.flags[g.rank];
         a.done_counter = reinterpret_cast<unsigned int*>(g.flags[g.rank] + kDoneWord);
+        a.wait = g.wait ? 1 : 0;
     }
     for (int m0 = 0; m0 < rows;) {
         const int mt = mlq::gemv_tokens_per_pass(rows - m0);
@@ -401,6 +403,7 @@ mlq_status validate_gather(int fmt, const void* w_shard, size_t shard_block_coun
     if (g.row_begin < 0 || g.row_end < g.row_begin || g.row_end > out_features)
         return fail(MLQ_ERR_COMM, std::string(who) + ": row range outside [0, out_features]");
     if (g.epoch == 0) return fail(MLQ_ERR_COMM, std::string(who) + ": epoch starts at 1");
+    if (g.defer_wait != 0 && g.defer_wait != 1) return fail(MLQ_ERR_COMM, std::string(who) + ": defer_wait must be 0 or 1");
     if (!x || !g.peer_y || !g.peer_flags) return fail(MLQ_ERR_NULL, std::string(who) + ": null pointer");
     for (int r = 0; r < g.world_size; ++r)
         if (!g.peer_y[r] || !g.peer_flags[r])
@@ -450,6 +453,7 @@ mlq_status run_gather(int fmt, const void* w_shard, int out_features, int in_fea
         }
         bg.local_flags = mg.peer_flags[mg.rank];
         bg.done_counter = reinterpret_cast<unsigned int*>(mg.peer_flags[mg.rank] + kDoneWord);
+        bg.wait = mg.defer_wait ? 0 : 1;
         e = mlq::launch_bgemm(fmt, static_cast<const uint8_t*>(w_shard), x, nullptr, shard, in_features, rows,
                               bias ? bias + mg.row_begin : nullptr, ws, ds->sm_count, ds->err_flag, stream, &bg);
         return e == cudaSuccess ? MLQ_OK : fail_cuda("bgemm launch", e);
@@ -462,6 +466,7 @@ mlq_status run_gather(int fmt, const void* w_shard, int out_features, int in_fea
     g.ys = mg.peer_y;
     g.flags = mg.peer_flags;
     g.epoch = mg.epoch;
+    g.wait = !mg.defer_wait;
     Epilogue ep;
     ep.bias = bias;
     return run_stream(fmt, w_shard, mg.row_end - mg.row_begin, in_features, x, rows, g, stream, ep);
@@ -832,6 +837,33 @@ MLQ_API mlq_status mlq_quantize_model(const mlq_quantize_op* ops, int n, mlq_str
 
 MLQ_API size_t mlq_flag_bytes(void) { return kFlagBytes; }
 
+// The deferred wait of a sharded op (validated gather), in stream order.
+mlq_status run_gather_wait(const mlq_gather& g, cudaStream_t stream) {
+    if (g.world_size == 1) return MLQ_OK;  // one rank: stream order is all there is to wait for
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return fail_cuda("cudaGetDevice", e);
+    mlq_status st = MLQ_OK;
+    DeviceState* ds = device_state(dev, &st);
+    if (!ds) return st;
+    e = mlq::launch_gather_wait(g.peer_flags[g.rank], g.world_size, g.epoch, ds->err_flag, stream);
+    return e == cudaSuccess ? MLQ_OK : fail_cuda("gather wait launch", e);
+}
+
+MLQ_API mlq_status mlq_gather_wait(const mlq_gather* g, mlq_stream stream) {
+    try {
+        if (!g) return fail(MLQ_ERR_NULL, "mlq_gather_wait: null gather");
+        if (g->world_size < 1 || g->world_size > mlq::kMaxWorld || g->rank < 0 || g->rank >= g->world_size)
+            return fail(MLQ_ERR_COMM, "mlq_gather_wait: world_size must be 1..8 and 0 <= rank < world_size");
+        if (g->epoch == 0) return fail(MLQ_ERR_COMM, "mlq_gather_wait: epoch starts at 1");
+        if (!g->peer_flags || !g->peer_flags[g->rank])
+            return fail(MLQ_ERR_NULL, "mlq_gather_wait: null flag pointer for this rank");
+        return run_gather_wait(*g, reinterpret_cast<cudaStream_t>(stream));
+    } catch (...) {
+        return fail(MLQ_ERR_CUDA, "mlq_gather_wait: host exception");
+    }
+}
+
 MLQ_API mlq_status mlq_linear_allgather(mlq_format fmt, const void* w_shard,
                                         size_t shard_block_count, int out_features,
                                         int in_features, int row_begin, int row_end,
@@ -925,6 +957,10 @@ MLQ_API mlq_status mlq_linear_batch_host(const mlq_linear_op* ops, int n, int de
         }
         st = run_ops(ops, n, xd.data(), yd.data(), s);
         if (st != MLQ_OK) return st;
+        // deferred sharded ops: every rank's rows in y before it is copied back
+        for (int i = 0; i < n; ++i)
+            if (ops[i].gather && ops[i].gather->defer_wait && (st = run_gather_wait(*ops[i].gather, s)) != MLQ_OK)
+                return st;
         for (int i = 0; i < n && e == cudaSuccess; ++i) {
             // a gathered op's full y is this rank's peer_y entry
             const void* src = ops[i].gather ? static_cast<const void*>(ops[i].gather->peer_y[ops[i].gather->rank])

@@ -149,6 +149,7 @@ struct BgemmArgs {
     uint32_t* peer_flags[kMaxWorld];
     uint32_t* local_flags;
     unsigned int* done_counter;
+    int wait;  // 1: wait for every rank after publishing; 0: publish only
     int in, T, kb;        // kb = blocks per row
     int total;            // units = row tiles x kb (<= kMaxUnits)
     int* err;
@@ -763,7 +764,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     fence_acq_rel_sys();
                     for (int r = 0; r < a.world; ++r) st_relaxed_sys(a.peer_flags[r] + a.rank, a.epoch);
                     const uint64_t t0 = global_ns();
-                    for (int r = 0; r < a.world; ++r) {
+                    for (int r = 0; r < (a.wait ? a.world : 0); ++r) {
                         while ((int)(ld_acquire_sys(a.local_flags + r) - a.epoch) < 0) {
                             if (global_ns() - t0 > kWaitLimitNs) {
                                 report_error(a.err, 4);
@@ -988,6 +989,7 @@ cudaError_t launch_t(const GroupMat* mats, int nmat, const float* x, int in, int
         a.epoch = g->epoch;
         a.local_flags = g->local_flags;
         a.done_counter = g->done_counter;
+        a.wait = g->wait;
     } else {
         a.ys[0] = mats[0].y;
         a.ny = 1;

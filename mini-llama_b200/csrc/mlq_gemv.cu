@@ -1006,7 +1006,7 @@ __global__ void __launch_bounds__(threads_for(MT), MINB)
                     fence_acq_rel_sys();
                     for (int r = 0; r < a.world; ++r) st_relaxed_sys(a.peer_flags[r] + a.rank, a.epoch);
                     const uint64_t t0 = global_ns();
-                    for (int r = 0; r < a.world; ++r) {
+                    for (int r = 0; r < (a.wait ? a.world : 0); ++r) {
                         while ((int)(ld_acquire_sys(a.local_flags + r) - a.epoch) < 0) {
                             if (global_ns() - t0 > kWaitLimitNs) {
                                 report_error(a.err, 4);
@@ -1306,6 +1306,35 @@ cudaError_t reset_tile_queues() {
     unsigned int* base = tile_slots(dev);
     if (!base) return cudaErrorInvalidSymbol;
     return cudaMemset(base, 0, sizeof(unsigned int) * 2 * kTileSlots);
+}
+
+}  // namespace mlq
+
+namespace mlq {
+namespace {
+
+// The deferred half of a sharded call's handshake (one thread): every
+// rank's epoch word here at least `epoch`, bounded as the in-kernel wait.
+__global__ void gather_wait_kernel(const uint32_t* flags, int world, uint32_t epoch, int* err) {
+    if (threadIdx.x != 0) return;
+    const uint64_t t0 = global_ns();
+    for (int r = 0; r < world; ++r) {
+        while ((int)(ld_acquire_sys(flags + r) - epoch) < 0) {
+            if (global_ns() - t0 > kWaitLimitNs) {
+                report_error(err, 4);
+                return;
+            }
+            __nanosleep(64);
+        }
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_gather_wait(const uint32_t* local_flags, int world, uint32_t epoch, int* err,
+                               cudaStream_t stream) {
+    gather_wait_kernel<<<1, 32, 0, stream>>>(local_flags, world, epoch, err);
+    return cudaGetLastError();
 }
 
 }  // namespace mlq

@@ -42,6 +42,7 @@ struct GemvArgs {
     uint32_t* peer_flags[8];     // rank r's flag words, mapped here
     uint32_t* local_flags;       // this rank's flag words (world entries)
     unsigned int* done_counter;  // this rank's CTA completion counter
+    int wait;                    // 1: wait for every rank after publishing; 0: publish only
 };
 
 constexpr int kMaxWorld = 8;
@@ -129,7 +130,13 @@ struct BgemmGather {
     uint32_t* peer_flags[kMaxWorld] = {};
     uint32_t* local_flags = nullptr;
     unsigned int* done_counter = nullptr;
+    int wait = 1;  // 1: wait for every rank after publishing; 0: publish only
 };
+
+// Waits (bounded, one thread) until local_flags[r] >= epoch for every
+// rank r < world: the deferred half of a sharded call's handshake.
+cudaError_t launch_gather_wait(const uint32_t* local_flags, int world, uint32_t epoch, int* err,
+                               cudaStream_t stream);
 
 // Matrices one batched-decode launch may compute (sharing x).
 constexpr int kBgemmMaxGroup = 4;

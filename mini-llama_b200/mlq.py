@@ -40,7 +40,7 @@ class Gather(ctypes.Structure):
     """struct mlq_gather (include/mlq.h): the shard and gather of one op."""
     _fields_ = [("world_size", ctypes.c_int), ("rank", ctypes.c_int), ("row_begin", ctypes.c_int),
                 ("row_end", ctypes.c_int), ("peer_y", ctypes.c_void_p), ("peer_flags", ctypes.c_void_p),
-                ("epoch", ctypes.c_uint32)]
+                ("epoch", ctypes.c_uint32), ("defer_wait", ctypes.c_int)]
 
 
 class LinearOp(ctypes.Structure):
@@ -82,6 +82,7 @@ def lib() -> ctypes.CDLL:
                                            ctypes.c_uint32, _vp]
         L.mlq_linear_batch.argtypes = [ctypes.POINTER(LinearOp), _i, _vp]
         L.mlq_linear_batch_host.argtypes = [ctypes.POINTER(LinearOp), _i, _i, _vp]
+        L.mlq_gather_wait.argtypes = [ctypes.POINTER(Gather), _vp]
         L.mlq_peer_alloc.argtypes = [_sz, ctypes.POINTER(_vp), ctypes.c_char_p]
         L.mlq_peer_open.argtypes = [ctypes.c_char_p, ctypes.POINTER(_vp)]
         L.mlq_peer_close.argtypes = [_vp]
@@ -90,7 +91,7 @@ def lib() -> ctypes.CDLL:
                      "mlq_linear_host",
                      "mlq_linear_host_weight", "mlq_dequantize", "mlq_quantize", "mlq_device_error",
                      "mlq_linear_allgather", "mlq_peer_alloc", "mlq_peer_open", "mlq_peer_close",
-                     "mlq_peer_free", "mlq_linear_batch", "mlq_linear_batch_host"):
+                     "mlq_peer_free", "mlq_linear_batch", "mlq_linear_batch_host", "mlq_gather_wait"):
             getattr(L, name).restype = _i
         _lib = L
     return _lib
@@ -354,13 +355,20 @@ def linear_op(fmt, w_ptr: int, out_features: int, in_features: int, x_ptr: int, 
 
 
 def make_gather(world: int, rank: int, row_begin: int, row_end: int, peer_y_ptrs, peer_flag_ptrs,
-                epoch: int = 1):
-    """A Gather struct plus the pointer arrays it references (keep both alive)."""
+                epoch: int = 1, defer_wait: bool = False):
+    """A Gather struct plus the pointer arrays it references (keep both alive).
+    defer_wait: the op only publishes its epoch; gather_wait() waits later."""
     ys = (ctypes.c_void_p * world)(*peer_y_ptrs)
     fs = (ctypes.c_void_p * world)(*peer_flag_ptrs)
-    g = Gather(world, rank, row_begin, row_end, ctypes.addressof(ys), ctypes.addressof(fs), epoch)
+    g = Gather(world, rank, row_begin, row_end, ctypes.addressof(ys), ctypes.addressof(fs), epoch,
+               1 if defer_wait else 0)
     g._keep = (ys, fs)
     return g
+
+
+def gather_wait(g: Gather, stream=None) -> None:
+    """mlq_gather_wait: in stream order, every rank's epoch >= g.epoch here."""
+    check(lib().mlq_gather_wait(ctypes.byref(g), _stream_handle(stream)))
 
 
 class Batch:

@@ -124,6 +124,17 @@ class ShardedLinear:
                                   self.flags.peers, self.rank, epoch, stream)
         return yb.local
 
+    def deferred(self, w_shard_ptr: int, x_ptr: int, epoch: int, stream: int | None) -> int:
+        """The same product as a batch op that only publishes its epoch,
+        then the separate wait (mlq_gather_wait); returns the local y."""
+        yb = self.ybuf[epoch & 1]
+        g = self.mlq.make_gather(self.world, self.rank, self.begin, self.end, yb.peers, self.flags.peers,
+                                 epoch=epoch, defer_wait=True)
+        op = self.mlq.linear_op(self.fmt, w_shard_ptr, self.out, self.inp, x_ptr, self.rows, yb.local, gather=g)
+        self.mlq.Batch([op]).run(stream)
+        self.mlq.gather_wait(g, stream)
+        return yb.local
+
 
 class _CudaArray:
     __slots__ = ("__cuda_array_interface__",)

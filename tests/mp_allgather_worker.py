@@ -3,7 +3,8 @@ tests/test_allgather_gpu.py through torchrun, one process per GPU).
 
 Every rank holds its row shard of each matrix (drawn on its GPU from the
 matrix's seed at the shard's offset and quantized there), calls the fused
-shard-GEMV + gather three times, and checks the FULL y on its own GPU
+shard-GEMV + gather three times (the third as a batch op with a deferred
+wait, then mlq_gather_wait), and checks the FULL y on its own GPU
 against the CPU oracle: every row for matrices up to 8192 rows, otherwise a
 sample of rows that includes every shard's first and last row.  The cases
 include the BASELINE config-5 shapes (Llama-3-70B lm_head 128256x8192 and
@@ -81,7 +82,9 @@ def main():
             x = pkg.synth.normal((rows, in_f), seed=1000 * ci + it)
             xd = torch.from_numpy(x).to(dev)
             epoch += 1
-            yptr = lin(shard.data_ptr() if shard is not None else 0, xd.data_ptr(), epoch, stream)
+            # the third call: publish in the op, wait in mlq_gather_wait
+            call = lin.deferred if it == 2 else lin
+            yptr = call(shard.data_ptr() if shard is not None else 0, xd.data_ptr(), epoch, stream)
             torch.cuda.synchronize()
             y = sh.device_view(yptr, (rows, out_f)).cpu().numpy()[:, check]
             ref = orc.linear(fmt, x, blocks, len(check))

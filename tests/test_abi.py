@@ -250,3 +250,22 @@ def test_batch_validates_every_op_before_any_cuda_call(pkg):
     arr[0].w_up = 0x1800
     assert lib.mlq_linear_batch(arr, 1, None) == 9
     assert b"no up projection" in lib.mlq_last_error()
+
+
+def test_gather_wait_validates_before_any_cuda_call(pkg):
+    """mlq_gather_wait and a deferred gathered op check their arguments on
+    the host first (pointers are fake: nothing runs)."""
+    mlq = pkg.mlq
+    lib = mlq.lib()
+    assert lib.mlq_gather_wait(None, None) == 2
+    g = mlq.make_gather(2, 2, 0, 4, [0x3000, 0x3100], [0x4000, 0x4100], epoch=1, defer_wait=True)
+    assert lib.mlq_gather_wait(ctypes.byref(g), None) == 10  # rank outside the world
+    g = mlq.make_gather(2, 1, 0, 4, [0x3000, 0x3100], [0x4000, 0x4100], epoch=0, defer_wait=True)
+    assert lib.mlq_gather_wait(ctypes.byref(g), None) == 10  # epoch 0
+    assert b"epoch" in lib.mlq_last_error()
+    g = mlq.make_gather(1, 0, 0, 4, [0x3000], [0x4000], epoch=1)
+    g.defer_wait = 2
+    op = mlq.linear_op("q8_0", 0x1000, 4, 32, 0x2000, 1, 0x3000, gather=g)
+    arr = (mlq.LinearOp * 1)(op)
+    assert lib.mlq_linear_batch(arr, 1, None) == 10
+    assert b"defer_wait" in lib.mlq_last_error()

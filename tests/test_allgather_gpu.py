@@ -111,3 +111,27 @@ def test_multi_gpu_allgather(world):
     print(r.stdout[-3000:], r.stderr[-3000:])
     assert r.returncode == 0
     assert r.stdout.count("ALLGATHER OK") == world
+
+
+@pytest.mark.parametrize("rows", [1, 8])
+def test_world_of_one_deferred_wait(oracle, pkg, rows):
+    """A batch op with defer_wait in a world of one: mlq_gather_wait has no
+    peer to wait for (stream order covers this rank) and y is complete
+    after it.  One row takes the streaming GEMV, eight the batched-decode
+    GEMM."""
+    mlq = pkg.mlq
+    fmt, out_f, in_f = "q4_0", 1000, 2048
+    blocks = oracle.quantize(fmt, pkg.synth.normal((out_f, in_f), seed=51, std=0.02))
+    x = pkg.synth.normal((rows, in_f), seed=52)
+    w_d, x_d = dev(blocks), dev(x)
+    y = torch.full((rows, out_f), 7.0, dtype=torch.float32, device="cuda")
+    flags = torch.zeros(mlq.flag_bytes() // 4, dtype=torch.int32, device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+    for epoch in (1, 2, 3):
+        g = mlq.make_gather(1, 0, 0, out_f, [y.data_ptr()], [flags.data_ptr()], epoch=epoch, defer_wait=True)
+        op = mlq.linear_op(fmt, w_d.data_ptr(), out_f, in_f, x_d.data_ptr(), rows, y.data_ptr(), gather=g)
+        mlq.Batch([op]).run(s)
+        mlq.gather_wait(g, s)
+        torch.cuda.synchronize()
+    assert rel_l2_rows(y.cpu().numpy(), oracle.linear(fmt, x, blocks, out_f)).max() <= 1e-3
+    assert mlq.device_error(0) == 0
