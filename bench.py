@@ -515,6 +515,18 @@ class Step:
             nb = weight_bytes(fmt, e - b, in_f)
             self.op_bytes.append(2 * nb if (pair and name == pair[0]) else nb)
         self.ops = ops
+        # a run of independent one-launch GEMVs (one token or two, local) ends
+        # with the library's join launch
+        run = 0
+        for name, out_f, in_f in mats:
+            one = (self.plan.active(name) and self.plan.place[name] != "shard" and
+                   rows <= 2 and not mlq.takes_bgemm(rows, out_f, in_f) and not mlq.takes_gemm(rows, out_f, in_f))
+            if one:
+                run += 1
+            else:
+                self.launches.append(1 if run >= 2 else 0)
+                run = 0
+        self.launches.append(1 if run >= 2 else 0)
         # the step's one cross-rank wait: every rank's highest epoch of the step
         self.waiter = (mlq.make_gather(ctx.world, ctx.rank, 0, 0, [0] * ctx.world, ctx.flags.peers, epoch=1)
                        if shard_names else None)

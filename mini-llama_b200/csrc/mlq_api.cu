@@ -170,7 +170,8 @@ struct Epilogue {
 // Streams `out` rows starting at w through the streaming GEMV, one launch
 // per <= 8 rows of x.
 mlq_status run_stream(int fmt, const void* w, int out, int in, const float* x, int rows,
-                      const Gather& g, cudaStream_t stream, const Epilogue& ep = Epilogue()) {
+                      const Gather& g, cudaStream_t stream, const Epilogue& ep = Epilogue(),
+                      int pdl_mode = mlq::kPdlNormal) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return fail_cuda("cudaGetDevice", e);
@@ -196,6 +197,7 @@ mlq_status run_stream(int fmt, const void* w, int out, int in, const float* x, i
     a.err = ds->err_flag;
     a.rank = g.rank;
     a.epoch = g.epoch;
+    a.pdl_mode = pdl_mode;
     if (g.world > 1) {
         for (int r = 0; r < g.world; ++r) a.peer_flags[r] = g.flags[r];
         a.local_flags = g.flags[g.rank];
@@ -282,7 +284,7 @@ mlq_status run_nonstream(Route rt, int fmt, const void* w, int out, int in, cons
 }
 
 mlq_status run_linear(int fmt, const void* w, int out, int in, const float* x, int rows, float* y,
-                      cudaStream_t stream, const Epilogue& ep = Epilogue()) {
+                      cudaStream_t stream, const Epilogue& ep = Epilogue(), int pdl_mode = mlq::kPdlNormal) {
     const Route rt = route_of(fmt, w, ep.w2, out, in, x, rows);
     if (rt != Route::kStream) {
         int dev = 0;
@@ -314,7 +316,7 @@ mlq_status run_linear(int fmt, const void* w, int out, int in, const float* x, i
     Gather g;
     g.y_stride = out;
     g.ys = &y;
-    return run_stream(fmt, w, out, in, x, rows, g, stream, ep);
+    return run_stream(fmt, w, out, in, x, rows, g, stream, ep, pdl_mode);
 }
 
 // Device address of g_mlq_noalloc_scratch, looked up once per device (with
@@ -499,18 +501,65 @@ mlq_status run_op(const mlq_linear_op& op, const float* x, float* y, cudaStream_
     return run_linear(op.fmt, op.w, op.out_features, op.in_features, x, op.rows, y, stream, ep);
 }
 
-// A batch's ops in order, consecutive plain ops that share x (the same
-// device x, format, in_features and rows) and all take the batched-decode
-// GEMM running as one grouped launch (up to kBgemmMaxGroup): Q, K and V of a
-// layer read one x (src/forward.cc:425-435).  xs[i] / ys[i]: op i's device
-// x and y.
+// A batch's ops in order.
+//  * Consecutive plain ops that share x (the same device x, format,
+//    in_features and rows) and all take the batched-decode GEMM run as one
+//    grouped launch (up to kBgemmMaxGroup): Q, K and V of a layer read one x
+//    (src/forward.cc:425-435).
+//  * Consecutive ops that take one streaming-GEMV launch each and do not
+//    touch one another's outputs (no op's x, bias or y overlaps an earlier
+//    op's y, no op's y overlaps an earlier op's x) run back to back: the
+//    first waits for the kernel before the batch, the others read x at once,
+//    and a join launch closes the run, so what follows sees every y.
+// xs[i] / ys[i]: op i's device x and y.
 mlq_status run_ops(const mlq_linear_op* ops, int n, const float* const* xs, float* const* ys, cudaStream_t stream) {
     auto groupable = [&](int i) {
         const mlq_linear_op& o = ops[i];
         return !o.gather && !o.w_up && route_of(o.fmt, o.w, nullptr, o.out_features, o.in_features, xs[i], o.rows) ==
                                            Route::kBgemm;
     };
+    auto one_gemv = [&](int i) {
+        const mlq_linear_op& o = ops[i];
+        return !o.gather && o.rows <= mlq::gemv_tokens_per_pass(o.rows) &&
+               route_of(o.fmt, o.w, o.w_up, o.out_features, o.in_features, xs[i], o.rows) == Route::kStream;
+    };
+    auto overlap = [](const void* a, size_t na, const void* b, size_t nb) {
+        const uintptr_t pa = reinterpret_cast<uintptr_t>(a), pb = reinterpret_cast<uintptr_t>(b);
+        return a && b && pa < pb + nb && pb < pa + na;
+    };
+    auto ybytes = [&](int i) { return (size_t)ops[i].rows * ops[i].out_features * sizeof(float); };
+    auto xbytes = [&](int i) { return (size_t)ops[i].rows * ops[i].in_features * sizeof(float); };
+    // op j may run without waiting for ops [i, j)
+    auto independent = [&](int i, int j) {
+        for (int k = i; k < j; ++k) {
+            if (overlap(xs[j], xbytes(j), ys[k], ybytes(k)) || overlap(ys[j], ybytes(j), ys[k], ybytes(k)) ||
+                overlap(ys[j], ybytes(j), xs[k], xbytes(k)) ||
+                overlap(ops[j].bias, ops[j].out_features * sizeof(float), ys[k], ybytes(k)) ||
+                overlap(ys[j], ybytes(j), ops[k].bias, ops[k].out_features * sizeof(float)))
+                return false;
+        }
+        return true;
+    };
     for (int i = 0; i < n;) {
+        // a run of independent one-launch GEMVs
+        int r = i;
+        if (one_gemv(i))
+            for (r = i + 1; r < n && one_gemv(r) && independent(i, r); ++r) {
+            }
+        if (r - i >= 2) {
+            for (int k = i; k < r; ++k) {
+                Epilogue ep;
+                ep.w2 = ops[k].w_up;
+                ep.bias = ops[k].bias;
+                mlq_status st = run_linear(ops[k].fmt, ops[k].w, ops[k].out_features, ops[k].in_features, xs[k],
+                                           ops[k].rows, ys[k], stream, ep, k == i ? mlq::kPdlFirst : mlq::kPdlNoWait);
+                if (st != MLQ_OK) return st;
+            }
+            cudaError_t e = mlq::launch_join(stream);
+            if (e != cudaSuccess) return fail_cuda("join launch", e);
+            i = r;
+            continue;
+        }
         int j = i + 1;
         if (groupable(i))
             while (j < n && j - i < mlq::kBgemmMaxGroup && groupable(j) && xs[j] == xs[i] &&

@@ -395,8 +395,14 @@ __global__ void __launch_bounds__(threads_for(MT), MINB)
         fence_mbar_init();
     }
     __syncthreads();
-    // The next kernel in the stream may come up on SMs this grid frees.
-    launch_dependents();
+    // The next kernel in the stream may come up on SMs this grid frees (a
+    // kPdlFirst launch lets it only after its own wait, in the consumers).
+    if (a.pdl_mode != kPdlFirst) launch_dependents();
+    // the wait for the previous kernel before x is read (none in a run of
+    // independent launches: the run's first launch has waited)
+    auto dep_wait = [&]() {
+        if (a.pdl_mode != kPdlNoWait) grid_dependency_wait();
+    };
 
     // balanced row ranges in units of 8 rows (the 2-D boxes' height)
     const long long units = (a.out + 7) / 8;
@@ -564,7 +570,7 @@ __global__ void __launch_bounds__(threads_for(MT), MINB)
         bool staged_ok = true;
         if (a.x_staged) {
             if (warp == kXWarp && lane == 0) {
-                grid_dependency_wait();
+                dep_wait();
                 mbar_arrive_expect_tx(smem_u32(&xstage_bar), (uint32_t)a.x_staged);
                 bulk_g2s(xst, a.x, (uint32_t)a.x_staged, smem_u32(&xstage_bar));
             }
@@ -574,7 +580,7 @@ __global__ void __launch_bounds__(threads_for(MT), MINB)
                 staged_ok = false;
             }
         } else {
-            grid_dependency_wait();
+            dep_wait();
         }
         constexpr int NQ = 2 * C::G;
         const int items = staged_ok ? a.ktiles * NQ : 0;
@@ -610,7 +616,7 @@ __global__ void __launch_bounds__(threads_for(MT), MINB)
         // tiles ride the stage ring, up to S stages ahead of the consumers.
         // x may be the previous kernel's output: wait for it (weights are
         // read-only, so warp 0 started streaming them without waiting)
-        grid_dependency_wait();
+        dep_wait();
         const int nt = xres ? min(ntiles, 1) : ntiles;
         int s = 0;
         uint32_t ph = 0;
@@ -674,7 +680,8 @@ __global__ void __launch_bounds__(threads_for(MT), MINB)
 
     // -------------------------------- consumers --------------------------------
     // y (and the peers' y) may still be read by the previous kernel
-    grid_dependency_wait();
+    dep_wait();
+    if (a.pdl_mode == kPdlFirst) launch_dependents();
     // Bias of the first tile's row that this thread stores (one-token stores:
     // the reduce-scatter's row of this lane; tile stores: row c % TR of
     // thread c), loaded after the wait above, so a bias written by the
@@ -1337,4 +1344,15 @@ cudaError_t launch_gather_wait(const uint32_t* local_flags, int world, uint32_t 
     return cudaGetLastError();
 }
 
+}  // namespace mlq
+
+namespace mlq {
+namespace {
+__global__ void join_kernel() {}
+}  // namespace
+
+cudaError_t launch_join(cudaStream_t stream) {
+    join_kernel<<<1, 32, 0, stream>>>();
+    return cudaGetLastError();
+}
 }  // namespace mlq

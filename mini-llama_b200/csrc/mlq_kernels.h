@@ -43,6 +43,12 @@ struct GemvArgs {
     uint32_t* local_flags;       // this rank's flag words (world entries)
     unsigned int* done_counter;  // this rank's CTA completion counter
     int wait;                    // 1: wait for every rank after publishing; 0: publish only
+    // ordering with the previous kernel (programmatic dependent launch):
+    // kPdlNormal waits for it before reading x, and lets the next kernel
+    // start at once; kPdlFirst waits too, but lets the next kernel start only
+    // after that wait; kPdlNoWait reads x at once (the previous kernel was a
+    // kPdlFirst / kPdlNoWait launch whose outputs this one does not touch)
+    int pdl_mode;
 };
 
 constexpr int kMaxWorld = 8;
@@ -132,6 +138,13 @@ struct BgemmGather {
     unsigned int* done_counter = nullptr;
     int wait = 1;  // 1: wait for every rank after publishing; 0: publish only
 };
+
+constexpr int kPdlNormal = 0, kPdlFirst = 1, kPdlNoWait = 2;
+
+// An empty kernel launched without programmatic dependent launch: it and
+// everything after it on the stream start once every earlier kernel has
+// completed (closes a run of kPdlNoWait launches).
+cudaError_t launch_join(cudaStream_t stream);
 
 // Waits (bounded, one thread) until local_flags[r] >= epoch for every
 // rank r < world: the deferred half of a sharded call's handshake.

@@ -180,3 +180,44 @@ def test_batch_groups_ops_sharing_x(pkg, oracle, rows):
         if single is not None:
             assert rel_l2_rows(yn, single.cpu().numpy()).max() <= 1e-5, k
     assert mlq.device_error(0) == 0
+
+
+def test_batch_gemv_runs_respect_dependencies(pkg, oracle):
+    """One-token ops that do not touch one another's outputs run back to
+    back without waiting for each other; an op that reads an earlier op's y
+    (a chain) or overwrites an earlier op's x must still see, or leave, the
+    right data.  Ops: y1 = W1 x0; y2 = W2 y1 (reads y1); y3 = W3 x3;
+    y4 = W4 x4; then W5 x3 written into x4's buffer (after op 4 read it)."""
+    mlq = pkg.mlq
+    fmt = "q4_0"
+    n = 1024
+    ws, keep = [], []
+    for k in range(5):
+        wb = oracle.quantize(fmt, pkg.synth.normal((n, n), seed=1100 + k, std=0.02))
+        ws.append((wb, dev(wb)))
+    x0 = pkg.synth.normal((1, n), seed=1200)
+    x3 = pkg.synth.normal((1, n), seed=1201)
+    x4 = pkg.synth.normal((1, n), seed=1202)
+    x0d, x3d, x4d = dev(x0), dev(x3), dev(x4)
+    y1 = torch.full((1, n), float("nan"), device="cuda")
+    y2 = torch.full((1, n), float("nan"), device="cuda")
+    y3 = torch.full((1, n), float("nan"), device="cuda")
+    y4 = torch.full((1, n), float("nan"), device="cuda")
+    ops = [mlq.linear_op(fmt, ws[0][1].data_ptr(), n, n, x0d.data_ptr(), 1, y1.data_ptr()),
+           mlq.linear_op(fmt, ws[1][1].data_ptr(), n, n, y1.data_ptr(), 1, y2.data_ptr()),   # reads y1
+           mlq.linear_op(fmt, ws[2][1].data_ptr(), n, n, x3d.data_ptr(), 1, y3.data_ptr()),
+           mlq.linear_op(fmt, ws[3][1].data_ptr(), n, n, x4d.data_ptr(), 1, y4.data_ptr()),
+           mlq.linear_op(fmt, ws[4][1].data_ptr(), n, n, x3d.data_ptr(), 1, x4d.data_ptr())]  # overwrites x4 after op 4 read it
+    mlq.Batch(ops).run(torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    r1 = oracle.linear(fmt, x0, ws[0][0], n)
+    r2 = oracle.linear(fmt, y1.cpu().numpy(), ws[1][0], n)
+    r3 = oracle.linear(fmt, x3, ws[2][0], n)
+    r4 = oracle.linear(fmt, x4, ws[3][0], n)
+    r5 = oracle.linear(fmt, x3, ws[4][0], n)
+    assert rel_l2_rows(y1.cpu().numpy(), r1).max() <= TOL
+    assert rel_l2_rows(y2.cpu().numpy(), r2).max() <= TOL
+    assert rel_l2_rows(y3.cpu().numpy(), r3).max() <= TOL
+    assert rel_l2_rows(y4.cpu().numpy(), r4).max() <= TOL  # op 4 read x4 before op 5 overwrote it
+    assert rel_l2_rows(x4d.cpu().numpy(), r5).max() <= TOL
+    assert mlq.device_error(0) == 0
