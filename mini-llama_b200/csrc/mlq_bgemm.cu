@@ -29,7 +29,7 @@
 //     (row, t); the total is multiplied by s_t once, when it is stored.  The
 //     block scales never enter the tensor-core sums.
 //
-// CTA = 14 warps, one CTA per SM:
+// CTA = 18 warps, one CTA per SM:
 //   warp 0      TMA producer: W chunks (8 blocks x 128 rows, 2-D tensor map
 //               over the AoS bytes) and the chunk's x tiles (fp16 [hi; lo],
 //               128-B swizzle).
@@ -37,9 +37,9 @@
 //   warps 2-9   decode: two threads per W row, each turning its half of an
 //               A stage's blocks into fp16 codes in TMEM (the MMA's A
 //               operand).
-//   warps 10-13 fold: thread = W row = TMEM lane (one lane quarter per
-//               warp); a block's scale d (and q4_1 minimum m) is read from
-//               the W chunk in shared memory.
+//   warps 10-17 fold: thread = W row = TMEM lane; two warps per lane
+//               quarter, one per half of the tokens; a block's scale d (and
+//               q4_1 minimum m) is read from the W chunk in shared memory.
 // A stage's blocks (four; two with 32 padded tokens) are committed as one
 // TMEM group: one barrier per stage between the MMA thread and the decode /
 // fold warps.
@@ -73,9 +73,12 @@ constexpr int BM = 128;             // W rows per tile = MMA M = TMEM lanes
 constexpr int KC = 256;             // values per W chunk
 constexpr int BPC = KC / kQK;       // blocks per chunk (8)
 constexpr int kDecodeWarps = 8;     // warps 2..9: two per row
-constexpr int kFoldWarps = 4;       // warps 10..13: one per TMEM lane quarter
+// fold warps from warp 10 on: two per TMEM lane quarter, one per half of
+// the tokens (measured faster than one per quarter at 8, 16 and 32 padded
+// tokens, though 18 warps leave 96 registers per thread, 14 leave 128)
 constexpr int kFoldWarp0 = 2 + kDecodeWarps;
-constexpr int kThreads = 32 * (2 + kDecodeWarps + kFoldWarps);
+constexpr int fold_warps(int) { return 8; }
+constexpr int threads_of(int tp) { return 32 * (2 + kDecodeWarps + fold_warps(tp)); }
 constexpr int kSmemMax = 232448 - 1024;  // dynamic shared memory per CTA: 227 KB less the static part
 constexpr int kMinBlocksPerCta = 16;
 
@@ -209,10 +212,11 @@ __device__ __forceinline__ void for_each_chunk(int f0, int f1, int kb, Fn&& fn) 
 }
 
 template <int F, int TP>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(threads_of(TP), 1)
     bgemm_kernel(const __grid_constant__ WMaps tm_w, const __grid_constant__ CUtensorMap tm_x, BgemmArgs a) {
     using C = BCfg<F, TP>;
     constexpr int CS = C::CS, AS = C::AS, NG = C::NG, N = C::N, SB = C::SB, SPC = C::SPC;
+    constexpr int kFoldWarps = fold_warps(TP), kThreads = threads_of(TP);
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     __shared__ __align__(8) uint64_t c_full[CS], c_empty[CS], a_full[AS], a_empty[AS];
     __shared__ __align__(8) uint64_t g_full[NG], g_empty[NG];
@@ -547,16 +551,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         });
     } else {
         // ------------------ fold: TMEM block sums -> fp32 totals ------------------
+        // Two warps per TMEM lane quarter, each owning half of the tokens:
+        // thread = W row = TMEM lane, tokens [tb, tb + TH).
+        constexpr int TH = TP * 4 / kFoldWarps;  // tokens per fold warp
         const int quarter = warp & 3;          // TMEM lanes 32 quarter .. + 31
         const int row = quarter * 32 + lane;   // tile row
-        // tokens folded: T rounded up to 4 (the rest of the TP columns are zero)
-        const int nt = (a.T + 3) & ~3;
+        const int tb = ((warp - kFoldWarp0) >> 2) * TH;
+        // tokens folded here: T rounded up to 4, less tb (the padding columns are zero)
+        const int nt = min(TH, max(0, ((a.T + 3) & ~3) - tb));
         grid_dependency_wait();  // the token exponents come from the x-split kernel
         if (threadIdx.x - 32 * kFoldWarp0 < TP) tok_exp_s[threadIdx.x - 32 * kFoldWarp0] = a.tok_exp[threadIdx.x - 32 * kFoldWarp0];
         fold_bar_sync();
-        float acc[TP];
+        float acc[TH];
 #pragma unroll
-        for (int t = 0; t < TP; ++t) acc[t] = 0.f;
+        for (int t = 0; t < TH; ++t) acc[t] = 0.f;
         uint32_t cseq = 0, aseq = 0;
         int seg_tile = -1;
         auto flush = [&](int t, int b_lo, int b_hi) {
@@ -571,9 +579,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                     long long ys;
                     float* yp = y_row(m, o, ys);
 #pragma unroll
-                    for (int tt = 0; tt < TP; ++tt) {
-                        if (tt >= a.T) break;
-                        store_y(yp, tt * ys, scaled(tt, acc[tt], bm != nullptr, bo));
+                    for (int u = 0; u < TH; ++u) {
+                        if (tb + u >= a.T) break;
+                        store_y(yp, (tb + u) * ys, scaled(tb + u, acc[u], bm != nullptr, bo));
                     }
                 }
             } else {
@@ -583,7 +591,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int slot01 = f0 >= t * a.kb ? 0 : 1;
                 float* p = a.part + ((long long)blockIdx.x * 2 + slot01) * TP * BM;
 #pragma unroll
-                for (int tt = 0; tt < TP; ++tt) p[tt * BM + row] = acc[tt];
+                for (int u = 0; u < TH; ++u) p[(tb + u) * BM + row] = acc[u];
                 fold_bar_sync();  // every fold thread's part is stored
                 if (warp == kFoldWarp0 && lane == 0) {
                     int c0, c1;
@@ -596,7 +604,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
 #pragma unroll
-            for (int tt = 0; tt < TP; ++tt) acc[tt] = 0.f;
+            for (int u = 0; u < TH; ++u) acc[u] = 0.f;
         };
         int last_t = -1, last_lo = 0, last_hi = 0;
         const uint32_t tq = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)C::ACC_COL0;
@@ -624,56 +632,47 @@ __global__ void __launch_bounds__(kThreads, 1)
                     return false;
                 }
                 tc_fence_after();
-                // acc[t0 + u] += d * (hi[u] + lo[u]) (+ m * xsum[t0 + u]), u < TC,
-                // for block b of the stage
-                constexpr int TC = TP < 16 ? TP : 16;  // tokens per fold step
-                constexpr int PB = TP == 32 ? 1 : 2;   // blocks per TMEM wait
-                auto fold_block = [&](int b, int t0, const uint32_t* hi, const uint32_t* lo) {
-                    const uint32_t boff = wrow + (uint32_t)((SB * j + b) * C::BS);
-                    const float d = half_bits_to_float(lds_u16(boff));
-#pragma unroll
-                    for (int u = 0; u < TC; ++u) {
-                        if (t0 + u >= nt) break;
-                        acc[t0 + u] = fmaf(__uint_as_float(hi[u]) + __uint_as_float(lo[u]), d, acc[t0 + u]);
-                    }
-                    if constexpr (F == kQ4_1) {
-                        const float mn = half_bits_to_float(lds_u16(boff + 2u));
-                        const uint32_t sb = sc_st(cs) + (uint32_t)(((SB * j + b) * TP + t0) * 4);
-#pragma unroll
-                        for (int q = 0; q < TC / 4; ++q) {
-                            if (t0 + 4 * q >= nt) break;
-                            const float4 m4 = lds_f4(sb + 16u * q);  // the same address in every lane
-                            acc[t0 + 4 * q] = fmaf(mn, m4.x, acc[t0 + 4 * q]);
-                            acc[t0 + 4 * q + 1] = fmaf(mn, m4.y, acc[t0 + 4 * q + 1]);
-                            acc[t0 + 4 * q + 2] = fmaf(mn, m4.z, acc[t0 + 4 * q + 2]);
-                            acc[t0 + 4 * q + 3] = fmaf(mn, m4.w, acc[t0 + 4 * q + 3]);
-                        }
-                    }
-                };
-                // a block's accumulator: hi columns [0, TP), lo columns [TP, 2 TP)
-#pragma unroll
-                for (int t0 = 0; t0 < TP; t0 += TC) {
-                    if (t0 >= nt) break;
+                if (nt > 0) {
+                    // PB blocks of the stage per TMEM wait, this warp's token
+                    // columns of each (hi [tb, tb + TH), lo [TP + tb, ..))
+                    constexpr int PB = TH <= 4 ? SB : (TH == 8 ? 2 : 1);
 #pragma unroll
                     for (int b2 = 0; b2 < SB; b2 += PB) {
-                        uint32_t v[PB][2 * TC];
+                        uint32_t v[PB][2 * TH];
 #pragma unroll
                         for (int h = 0; h < PB; ++h) {
                             if (!(m >> (b2 + h) & 1u)) continue;
-                            const uint32_t ta = tq + (uint32_t)((g * SB + b2 + h) * N);
-                            if constexpr (TP == 8) {
-                                tmem_ld16_issue(ta, *reinterpret_cast<uint32_t(*)[16]>(v[h]));
-                            } else if constexpr (TP == 16) {
-                                tmem_ld32_issue(ta, *reinterpret_cast<uint32_t(*)[32]>(v[h]));
-                            } else {
-                                tmem_ld16_issue(ta + (uint32_t)t0, *reinterpret_cast<uint32_t(*)[16]>(v[h]));
-                                tmem_ld16_issue(ta + (uint32_t)(TP + t0), *reinterpret_cast<uint32_t(*)[16]>(v[h] + 16));
+                            const uint32_t ta = tq + (uint32_t)((g * SB + b2 + h) * N + tb);
+                            tmem_ld_issue<TH>(ta, v[h]);
+                            tmem_ld_issue<TH>(ta + (uint32_t)TP, v[h] + TH);
+                        }
+                        tmem_wait_ld(*reinterpret_cast<uint32_t(*)[PB * 2 * TH]>(&v[0][0]));
+#pragma unroll
+                        for (int h = 0; h < PB; ++h) {
+                            const int b = b2 + h;
+                            if (!(m >> b & 1u)) continue;
+                            // acc[u] += d * (hi[u] + lo[u]) (+ m * xsum[tb + u])
+                            const uint32_t boff = wrow + (uint32_t)((SB * j + b) * C::BS);
+                            const float d = half_bits_to_float(lds_u16(boff));
+#pragma unroll
+                            for (int u = 0; u < TH; ++u) {
+                                if (u >= nt) break;
+                                acc[u] = fmaf(__uint_as_float(v[h][u]) + __uint_as_float(v[h][TH + u]), d, acc[u]);
+                            }
+                            if constexpr (F == kQ4_1) {
+                                const float mn = half_bits_to_float(lds_u16(boff + 2u));
+                                const uint32_t sb = sc_st(cs) + (uint32_t)(((SB * j + b) * TP + tb) * 4);
+#pragma unroll
+                                for (int q = 0; q < TH / 4; ++q) {
+                                    if (4 * q >= nt) break;
+                                    const float4 m4 = lds_f4(sb + 16u * q);  // the same address in every lane
+                                    acc[4 * q] = fmaf(mn, m4.x, acc[4 * q]);
+                                    acc[4 * q + 1] = fmaf(mn, m4.y, acc[4 * q + 1]);
+                                    acc[4 * q + 2] = fmaf(mn, m4.z, acc[4 * q + 2]);
+                                    acc[4 * q + 3] = fmaf(mn, m4.w, acc[4 * q + 3]);
+                                }
                             }
                         }
-                        tmem_wait_ld(*reinterpret_cast<uint32_t(*)[PB * 2 * TC]>(&v[0][0]));
-#pragma unroll
-                        for (int h = 0; h < PB; ++h)
-                            if (m >> (b2 + h) & 1u) fold_block(b2 + h, t0, v[h], v[h] + TC);
                     }
                 }
                 tc_fence_before();
@@ -688,12 +687,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         });
         if (last_t >= 0 && !aborted()) flush(last_t, last_lo, last_hi);
         // Split tiles this CTA finished last: y = the tile's parts added in
-        // CTA order, scaled, plus the bias.  A fold thread owns a row; the
-        // loads of all its parts (16 tokens x 4 CTAs at a time) go out together.
+        // CTA order, scaled, plus the bias.  A fold thread owns a row and its
+        // tokens; the loads of its parts (2-4 CTAs at a time) go out together.
         fold_bar_sync();
         for (int k = 0; k < 2; ++k) {
             const int t = fix_tile[k];
-            if (t < 0 || aborted()) continue;
+            if (t < 0 || aborted() || tb >= a.T) continue;
             const int m = mat_of(t);
             const int o = (t - pick(a.tile0, m)) * BM + row;
             if (o >= pick(a.out_m, m)) continue;
@@ -704,33 +703,29 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float bo = bm ? bm[o] : 0.f;
             long long ys;
             float* yp = y_row(m, o, ys);
-            constexpr int TG = TP < 16 ? TP : 16;
+            float v[TH];
 #pragma unroll
-            for (int g = 0; g < TP; g += TG) {
-                if (g >= a.T) break;
-                float v[TG];
+            for (int u = 0; u < TH; ++u) v[u] = 0.f;
+            constexpr int QF = TH >= 16 ? 2 : 4;  // CTAs' parts per round of loads
+            for (int c = c0; c <= c1; c += QF) {
+                float pv[QF][TH];
 #pragma unroll
-                for (int u = 0; u < TG; ++u) v[u] = 0.f;
-                for (int c = c0; c <= c1; c += 4) {
-                    float pv[4][TG];
+                for (int q = 0; q < QF; ++q) {
+                    const int cc = c + q <= c1 ? c + q : c1;
+                    const int sl = unit_begin(a.total, cc, G) >= u0 ? 0 : 1;
+                    const float* pp = a.part + (((long long)cc * 2 + sl) * TP + tb) * BM + row;
 #pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        const int cc = c + q <= c1 ? c + q : c1;
-                        const int sl = unit_begin(a.total, cc, G) >= u0 ? 0 : 1;
-                        const float* pp = a.part + (((long long)cc * 2 + sl) * TP + g) * BM + row;
-#pragma unroll
-                        for (int u = 0; u < TG; ++u) pv[q][u] = __ldcg(pp + u * BM);
-                    }
-#pragma unroll
-                    for (int q = 0; q < 4; ++q)
-                        if (c + q <= c1)
-#pragma unroll
-                            for (int u = 0; u < TG; ++u) v[u] = c + q == c0 ? pv[q][u] : __fadd_rn(v[u], pv[q][u]);
+                    for (int u = 0; u < TH; ++u) pv[q][u] = __ldcg(pp + u * BM);
                 }
 #pragma unroll
-                for (int u = 0; u < TG; ++u)
-                    if (g + u < a.T) store_y(yp, (g + u) * ys, scaled(g + u, v[u], bm != nullptr, bo));
+                for (int q = 0; q < QF; ++q)
+                    if (c + q <= c1)
+#pragma unroll
+                        for (int u = 0; u < TH; ++u) v[u] = c + q == c0 ? pv[q][u] : __fadd_rn(v[u], pv[q][u]);
             }
+#pragma unroll
+            for (int u = 0; u < TH; ++u)
+                if (tb + u < a.T) store_y(yp, (tb + u) * ys, scaled(tb + u, v[u], bm != nullptr, bo));
         }
     }
 
@@ -1007,7 +1002,7 @@ cudaError_t launch_t(const GroupMat* mats, int nmat, const float* x, int in, int
     a.tile_cnt = tile_cnt;
     const int G = grid_for(a.total, sm_count);
     cfg.gridDim = dim3(G);
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3(threads_of(TP));
     cfg.dynamicSmemBytes = (size_t)C::SMEM;
     return cudaLaunchKernelEx(&cfg, bgemm_kernel<F, TP>, mw, mx, a);
 }

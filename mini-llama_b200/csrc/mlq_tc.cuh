@@ -113,6 +113,24 @@ __device__ __forceinline__ void tmem_ld32_issue(uint32_t taddr, uint32_t (&v)[32
         : "r"(taddr));
 }
 
+__device__ __forceinline__ void tmem_ld4_issue(uint32_t taddr, uint32_t (&v)[4]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
+                 : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_ld8_issue(uint32_t taddr, uint32_t (&v)[8]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+                   "=r"(v[7])
+                 : "r"(taddr));
+}
+
+// N consecutive 32-bit columns (N = 4, 8, 16) of this warp's 32 TMEM lanes,
+// without the wait.
+template <int N>
+__device__ __forceinline__ void tmem_ld_issue(uint32_t taddr, uint32_t* v);
+
 __device__ __forceinline__ void tmem_ld16_issue(uint32_t taddr, uint32_t (&v)[16]) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
@@ -120,6 +138,19 @@ __device__ __forceinline__ void tmem_ld16_issue(uint32_t taddr, uint32_t (&v)[16
           "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
           "=r"(v[14]), "=r"(v[15])
         : "r"(taddr));
+}
+
+template <>
+__device__ __forceinline__ void tmem_ld_issue<4>(uint32_t taddr, uint32_t* v) {
+    tmem_ld4_issue(taddr, *reinterpret_cast<uint32_t(*)[4]>(v));
+}
+template <>
+__device__ __forceinline__ void tmem_ld_issue<8>(uint32_t taddr, uint32_t* v) {
+    tmem_ld8_issue(taddr, *reinterpret_cast<uint32_t(*)[8]>(v));
+}
+template <>
+__device__ __forceinline__ void tmem_ld_issue<16>(uint32_t taddr, uint32_t* v) {
+    tmem_ld16_issue(taddr, *reinterpret_cast<uint32_t(*)[16]>(v));
 }
 
 // Waits for this thread's TMEM loads; the registers of the loads are passed
