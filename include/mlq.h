@@ -368,7 +368,10 @@ MLQ_API mlq_status mlq_linear_batch(const mlq_linear_op* ops, int n, mlq_stream 
 /* mlq_linear_batch with HOST x and y (weights and bias on the device):
  * copies every x to device staging, launches the products, copies every y
  * back, then synchronises `stream` once.  Runs on `device`.  With pinned
- * host buffers the copies are asynchronous DMA.  Calls on one device are
+ * host buffers the copies are asynchronous DMA.  Ops with the same host x
+ * share one upload; consecutive ops whose host x (or y) buffers follow on
+ * directly (one pinned buffer, laid out in op order, each x and y a
+ * multiple of 256 bytes) share one copy.  Calls on one device are
  * serialised (the staging is per device). */
 MLQ_API mlq_status mlq_linear_batch_host(const mlq_linear_op* ops, int n, int device,
                                          mlq_stream stream);

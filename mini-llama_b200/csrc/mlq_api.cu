@@ -992,11 +992,29 @@ MLQ_API mlq_status mlq_linear_batch_host(const mlq_linear_op* ops, int n, int de
         if (yt > 0 && (st = ensure(&ds->y_stage, &ds->y_cap, yt)) != MLQ_OK) return st;
         char* xs = reinterpret_cast<char*>(ds->x_stage);
         char* ys = reinterpret_cast<char*>(ds->y_stage);
+        // Copies in op order; one copy per run of ops whose host buffers and
+        // staging slices both follow on directly (a caller that lays its x,
+        // or its y, out back to back in one pinned buffer gets one copy per
+        // direction: each copy costs a DMA setup).
+        struct Copy {
+            char* dst;
+            const char* src;
+            size_t bytes;
+        };
+        auto add = [](std::vector<Copy>& v, void* dst, const void* src, size_t bytes) {
+            char* d = static_cast<char*>(dst);
+            const char* sp = static_cast<const char*>(src);
+            if (!v.empty() && v.back().dst + v.back().bytes == d && v.back().src + v.back().bytes == sp)
+                v.back().bytes += bytes;
+            else
+                v.push_back(Copy{d, sp, bytes});
+        };
+        std::vector<Copy> ups;
+        for (int i = 0; i < n; ++i)
+            if (upload[i]) add(ups, xs + xo[i], ops[i].x, (size_t)ops[i].rows * ops[i].in_features * sizeof(float));
         cudaError_t e = cudaSuccess;
-        for (int i = 0; i < n && e == cudaSuccess; ++i)
-            if (upload[i])
-                e = cudaMemcpyAsync(xs + xo[i], ops[i].x, (size_t)ops[i].rows * ops[i].in_features * sizeof(float),
-                                    cudaMemcpyHostToDevice, s);
+        for (size_t k = 0; k < ups.size() && e == cudaSuccess; ++k)
+            e = cudaMemcpyAsync(ups[k].dst, ups[k].src, ups[k].bytes, cudaMemcpyHostToDevice, s);
         if (e != cudaSuccess) return fail_cuda("cudaMemcpyAsync (x upload)", e);
         std::vector<const float*> xd(n);
         std::vector<float*> yd(n);
@@ -1010,13 +1028,15 @@ MLQ_API mlq_status mlq_linear_batch_host(const mlq_linear_op* ops, int n, int de
         for (int i = 0; i < n; ++i)
             if (ops[i].gather && ops[i].gather->defer_wait && (st = run_gather_wait(*ops[i].gather, s)) != MLQ_OK)
                 return st;
-        for (int i = 0; i < n && e == cudaSuccess; ++i) {
+        std::vector<Copy> downs;
+        for (int i = 0; i < n; ++i) {
             // a gathered op's full y is this rank's peer_y entry
             const void* src = ops[i].gather ? static_cast<const void*>(ops[i].gather->peer_y[ops[i].gather->rank])
                                             : static_cast<const void*>(ys + yo[i]);
-            e = cudaMemcpyAsync(ops[i].y, src, (size_t)ops[i].rows * ops[i].out_features * sizeof(float),
-                                cudaMemcpyDeviceToHost, s);
+            add(downs, ops[i].y, src, (size_t)ops[i].rows * ops[i].out_features * sizeof(float));
         }
+        for (size_t k = 0; k < downs.size() && e == cudaSuccess; ++k)
+            e = cudaMemcpyAsync(downs[k].dst, downs[k].src, downs[k].bytes, cudaMemcpyDeviceToHost, s);
         if (e != cudaSuccess) return fail_cuda("cudaMemcpyAsync (y download)", e);
         e = cudaStreamSynchronize(s);
         if (e != cudaSuccess) return fail_cuda("cudaStreamSynchronize", e);
