@@ -21,9 +21,9 @@
 //     token's largest value.
 //   * Per block, the tensor cores form Dh[row][t] = sum q xh and Dl[row][t] =
 //     sum q xl in one TMEM accumulator of the block: two kind::f16 MMAs of
-//     128 x N x 16, N = 2 x padded tokens (the hi rows of x, then the lo
-//     rows, are the B operand).  An MMA costs about the same for any N up to
-//     64, so hi and lo share one instruction.
+//     128 x N x 16, N = 2 x padded tokens (the hi and lo rows of x, per
+//     half of the tokens, are the B operand).  An MMA costs about the same
+//     for any N up to 64, so hi and lo share one instruction.
 //   * CUDA-core "fold" warps read the block's accumulator and add
 //     d * (Dh + Dl) (+ m * sum(x / s_t) for q4_1) to the fp32 total of
 //     (row, t); the total is multiplied by s_t once, when it is stored.  The
@@ -91,7 +91,9 @@ struct WMaps {
     CUtensorMap m[kBgemmMaxGroup];
 };
 
-// TP: padded tokens (8, 16 or 32); the MMA's N is 2 TP (x hi, then x lo).
+// TP: padded tokens (8, 16 or 32); the MMA's N is 2 TP: per half of the
+// tokens, their hi rows of x then their lo rows (so a fold warp's columns,
+// one half's hi and lo, are adjacent in TMEM: one load per block).
 template <int F, int TP>
 struct BCfg {
     static constexpr int BS = Fmt<F>::kBlockBytes;
@@ -633,8 +635,8 @@ __global__ void __launch_bounds__(threads_of(TP), 1)
                 }
                 tc_fence_after();
                 if (nt > 0) {
-                    // PB blocks of the stage per TMEM wait, this warp's token
-                    // columns of each (hi [tb, tb + TH), lo [TP + tb, ..))
+                    // PB blocks of the stage per TMEM wait, this warp's 2 TH
+                    // columns of each (its tokens' hi, then their lo)
                     constexpr int PB = TH <= 4 ? SB : (TH == 8 ? 2 : 1);
 #pragma unroll
                     for (int b2 = 0; b2 < SB; b2 += PB) {
@@ -642,9 +644,8 @@ __global__ void __launch_bounds__(threads_of(TP), 1)
 #pragma unroll
                         for (int h = 0; h < PB; ++h) {
                             if (!(m >> (b2 + h) & 1u)) continue;
-                            const uint32_t ta = tq + (uint32_t)((g * SB + b2 + h) * N + tb);
-                            tmem_ld_issue<TH>(ta, v[h]);
-                            tmem_ld_issue<TH>(ta + (uint32_t)TP, v[h] + TH);
+                            const uint32_t ta = tq + (uint32_t)((g * SB + b2 + h) * N + 2 * tb);
+                            tmem_ld_issue<2 * TH>(ta, v[h]);
                         }
                         tmem_wait_ld(*reinterpret_cast<uint32_t(*)[PB * 2 * TH]>(&v[0][0]));
 #pragma unroll
@@ -774,8 +775,9 @@ __global__ void __launch_bounds__(threads_of(TP), 1)
     }
 }
 
-// x fp32 [T][in] -> the B operand fp16 [2 TP][in] (rows t: hi, TP + t: lo;
-// rows >= T zero), the exponent e_t of each token's power-of-two scale
+// x fp32 [T][in] -> the B operand fp16 [2 TP][in] (token t of half
+// h = t / (TP/2), i = t % (TP/2): hi in row h TP + i, lo in row h TP +
+// TP/2 + i; tokens >= T zero), the exponent e_t of each token's power-of-two scale
 // (2^e_t > max|x_t|) and, for q4_1, the block sums of x / 2^e_t.  One CTA
 // per padded token: a max pass over the row, then the split pass (x stays
 // in registers between them up to 16384 values).  Block 0 also zeroes the
@@ -838,8 +840,9 @@ __global__ void __launch_bounds__(kSplitThreads)
     }
     __syncthreads();
     const int ex = bad ? 0 : ex_s;
-    __half* hi = xb + (long long)t * in;
-    __half* lo = xb + (long long)(TP + t) * in;
+    constexpr int TH = TP / 2;  // tokens per fold warp
+    __half* hi = xb + (long long)((t / TH) * TP + t % TH) * in;
+    __half* lo = hi + (long long)TH * in;
     auto split = [&](int i, float4 v) {
         // exact power-of-two scaling, then the fp16 hi / lo split
         const float s[4] = {ldexpf(v.x, -ex), ldexpf(v.y, -ex), ldexpf(v.z, -ex), ldexpf(v.w, -ex)};

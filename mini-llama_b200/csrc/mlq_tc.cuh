@@ -126,8 +126,8 @@ __device__ __forceinline__ void tmem_ld8_issue(uint32_t taddr, uint32_t (&v)[8])
                  : "r"(taddr));
 }
 
-// N consecutive 32-bit columns (N = 4, 8, 16) of this warp's 32 TMEM lanes,
-// without the wait.
+// N consecutive 32-bit columns (N = 4, 8, 16, 32) of this warp's 32 TMEM
+// lanes, without the wait.
 template <int N>
 __device__ __forceinline__ void tmem_ld_issue(uint32_t taddr, uint32_t* v);
 
@@ -151,6 +151,10 @@ __device__ __forceinline__ void tmem_ld_issue<8>(uint32_t taddr, uint32_t* v) {
 template <>
 __device__ __forceinline__ void tmem_ld_issue<16>(uint32_t taddr, uint32_t* v) {
     tmem_ld16_issue(taddr, *reinterpret_cast<uint32_t(*)[16]>(v));
+}
+template <>
+__device__ __forceinline__ void tmem_ld_issue<32>(uint32_t taddr, uint32_t* v) {
+    tmem_ld32_issue(taddr, *reinterpret_cast<uint32_t(*)[32]>(v));
 }
 
 // Waits for this thread's TMEM loads; the registers of the loads are passed
