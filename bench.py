@@ -463,6 +463,7 @@ class Step:
                                                   for n in shard_names])
         self.gathers = [[], []]
         self.names, self.op_bytes, self.launches = [], [], []
+        self.one_run = False  # every op of the step in one run launch (set below)
         ops = [[], []]
         grp = None  # (x pointer, matrices) of the open batched-decode group
         for i, (name, out_f, in_f) in enumerate(mats):
@@ -515,18 +516,25 @@ class Step:
             nb = weight_bytes(fmt, e - b, in_f)
             self.op_bytes.append(2 * nb if (pair and name == pair[0]) else nb)
         self.ops = ops
-        # a run of independent one-launch GEMVs (one token or two, local) ends
-        # with the library's join launch
-        run = 0
-        for name, out_f, in_f in mats:
-            one = (self.plan.active(name) and self.plan.place[name] != "shard" and
+        # A run of independent one-launch GEMVs (one token or two, local):
+        # one-row ops that all join a run take two launches per 8 ops (the x
+        # slicing and the persistent run kernel) instead of one launch each;
+        # other runs end with the library's join launch.
+        run = []
+        for name, out_f, in_f in mats + [(None, 0, 0)]:
+            one = (name is not None and self.plan.active(name) and self.plan.place[name] != "shard" and
+                   not (pair and name == pair[1]) and
                    rows <= 2 and not mlq.takes_bgemm(rows, out_f, in_f) and not mlq.takes_gemm(rows, out_f, in_f))
             if one:
-                run += 1
-            else:
-                self.launches.append(1 if run >= 2 else 0)
-                run = 0
-        self.launches.append(1 if run >= 2 else 0)
+                run.append((name, in_f))
+                continue
+            if len(run) >= 2:
+                if all(mlq.joins_run(fmt, rows, i) and not (pair and n == pair[0]) for n, i in run):
+                    self.launches.append(2 * -(-len(run) // mlq.RUN_MAX_OPS) - len(run))
+                    self.one_run = len(run) == len(self.names)
+                else:
+                    self.launches.append(1)
+            run = []
         # the step's one cross-rank wait: every rank's highest epoch of the step
         self.waiter = (mlq.make_gather(ctx.world, ctx.rank, 0, 0, [0] * ctx.world, ctx.flags.peers, epoch=1)
                        if shard_names else None)
@@ -680,6 +688,22 @@ def run_workload(ctx, wl, steps, warmup, full=False, args=None):
         res["roofline"] = _roof(st.op_bytes[dj], per[dj], b2b, wl, ctx, st, dj)
         res["roofline"]["per_launch_ms"] = {n: round(v, 5) for n, v in zip(st.names, per)}
         res["roofline"]["all_launches_GBps"] = round(sum(st.op_bytes) / (sum(per) / 1e3) / 1e9, 1)
+        if st.one_run:
+            # the step is one run launch (all ops local, one row each): that
+            # kernel is the timed region's dominant kernel; the single-op
+            # figures stay beside it
+            single = res["roofline"]
+            step_ms = ms / steps
+            ach = sum(st.op_bytes) / (step_ms / 1e3) / 1e9
+            peak, kind = hbm_peak()
+            res["roofline"] = {
+                "bound": "hbm",
+                "kernel": f"gemv_run_kernel<{wl['fmt']}> (the step's {len(st.names)} products in one persistent "
+                          f"launch, after its x-slicing launch; rank {ctx.rank})",
+                "achieved": round(ach, 1), "peak": peak, "unit": "GB/s", "frac": round(ach / peak, 4),
+                "peak_kind": peak_kind_text(kind), "traffic": None,
+                "algorithmic_bytes_per_launch": sum(st.op_bytes), "launch_ms": round(step_ms, 5),
+                "single_op_launches": single}
     if full and not (args and args.no_e2e):
         res["e2e"] = _e2e(ctx, st, steps)
     del st
@@ -859,8 +883,13 @@ def run_mlq(args):
     if args.only:
         wl["matrices"] = [m for m in wl["matrices"] if m[0] == args.only]
     head = run_workload(ctx, wl, args.steps, args.warmup, full=True, args=args)
-    if ctx.world == 1 and args.workload == "qwen7b" and "lm_head" in head["roofline"]["kernel"]:
-        head["roofline"]["traffic"] = read_traffic()
+    if ctx.world == 1 and args.workload == "qwen7b" and not args.only:
+        roof = head["roofline"]
+        if "gemv_run_kernel" in roof["kernel"]:
+            roof["traffic"] = read_traffic("gemv_run_q4_0_decode_step.txt")
+            roof["single_op_launches"]["traffic"] = read_traffic("gemv_q4_0_lm_head.txt")
+        elif "lm_head" in roof["kernel"]:
+            roof["traffic"] = read_traffic("gemv_q4_0_lm_head.txt")
     extra, formats = {}, None
     if not args.no_extra and not args.only and args.workload == "qwen7b":
         for name in (EXTRAS_N1 if ctx.world == 1 else EXTRAS_NGT1):
@@ -904,9 +933,10 @@ def run_mlq(args):
                          f"results (max rel L2 {parity})")
 
 
-def read_traffic():
-    """DRAM bytes per lm_head launch from the committed ncu summary, if any."""
-    p = ROOT / "profiles" / "gemv_q4_0_lm_head.txt"
+def read_traffic(summary):
+    """DRAM bytes per launch from a committed ncu summary under profiles/
+    (its traffic_bytes_per_launch line), if any."""
+    p = ROOT / "profiles" / summary
     if not p.exists():
         return None
     for line in p.read_text().splitlines():

@@ -501,6 +501,18 @@ mlq_status run_op(const mlq_linear_op& op, const float* x, float* y, cudaStream_
     return run_linear(op.fmt, op.w, op.out_features, op.in_features, x, op.rows, y, stream, ep);
 }
 
+// A batch op as a member of a run of one-row products.
+mlq::GemvRunOp run_op_of(const mlq_linear_op& op, const float* x, float* y) {
+    mlq::GemvRunOp r;
+    r.w = static_cast<const uint8_t*>(op.w);
+    r.x = x;
+    r.y = y;
+    r.bias = op.bias;
+    r.out = op.out_features;
+    r.in = op.in_features;
+    return r;
+}
+
 // A batch's ops in order.
 //  * Consecutive plain ops that share x (the same device x, format,
 //    in_features and rows) and all take the batched-decode GEMM run as one
@@ -508,9 +520,12 @@ mlq_status run_op(const mlq_linear_op& op, const float* x, float* y, cudaStream_
 //    (src/forward.cc:425-435).
 //  * Consecutive ops that take one streaming-GEMV launch each and do not
 //    touch one another's outputs (no op's x, bias or y overlaps an earlier
-//    op's y, no op's y overlaps an earlier op's x) run back to back: the
-//    first waits for the kernel before the batch, the others read x at once,
-//    and a join launch closes the run, so what follows sees every y.
+//    op's y, no op's y overlaps an earlier op's x) form a run.  A run of
+//    one-row ops of one format in the run kernel's layout takes one
+//    persistent launch (per kGemvRunMaxOps ops; launch_gemv_run).  Other
+//    runs go back to back: the first waits for the kernel before the batch,
+//    the others read x at once, and a join launch closes the run, so what
+//    follows sees every y.
 // xs[i] / ys[i]: op i's device x and y.
 mlq_status run_ops(const mlq_linear_op* ops, int n, const float* const* xs, float* const* ys, cudaStream_t stream) {
     auto groupable = [&](int i) {
@@ -546,6 +561,33 @@ mlq_status run_ops(const mlq_linear_op* ops, int n, const float* const* xs, floa
         if (one_gemv(i))
             for (r = i + 1; r < n && one_gemv(r) && independent(i, r); ++r) {
             }
+        // ... one row of x each, one format, the run kernel's layout: one
+        // persistent launch per kGemvRunMaxOps ops
+        bool as_run = r - i >= 2;
+        for (int k = i; as_run && k < r; ++k)
+            as_run = ops[k].rows == 1 && !ops[k].w_up && ops[k].fmt == ops[i].fmt &&
+                     mlq::gemv_run_ok(ops[k].fmt, run_op_of(ops[k], xs[k], ys[k]));
+        if (as_run) {
+            int dev = 0;
+            cudaError_t e = cudaGetDevice(&dev);
+            if (e != cudaSuccess) return fail_cuda("cudaGetDevice", e);
+            mlq_status st = MLQ_OK;
+            DeviceState* ds = device_state(dev, &st);
+            if (!ds) return st;
+            for (int k = i; k < r; k += mlq::kGemvRunMaxOps) {
+                const int nk = r - k < mlq::kGemvRunMaxOps ? r - k : mlq::kGemvRunMaxOps;
+                mlq::GemvRunOp run[mlq::kGemvRunMaxOps];
+                for (int q = 0; q < nk; ++q) run[q] = run_op_of(ops[k + q], xs[k + q], ys[k + q]);
+                void* ws = nullptr;
+                st = stream_workspace(ds, stream, mlq::gemv_run_workspace_bytes(ops[i].fmt, run, nk), &ws);
+                if (st != MLQ_OK) return st;
+                e = mlq::launch_gemv_run(ops[i].fmt, run, nk, ws, ds->sm_count, ds->smem_per_sm, ds->err_flag,
+                                         stream);
+                if (e != cudaSuccess) return fail_cuda("gemv run launch", e);
+            }
+            i = r;
+            continue;
+        }
         if (r - i >= 2) {
             for (int k = i; k < r; ++k) {
                 Epilogue ep;

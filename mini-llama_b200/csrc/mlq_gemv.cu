@@ -290,6 +290,62 @@ __device__ __forceinline__ void int_piece_store(const float v[16], int i, int la
     if (half == 0) sts_f2(ss + (uint32_t)blk * 8u, make_float2(fmaf(0.0f, sum, mx * (1.0f / 127.0f)), sum));
 }
 
+// One K-tile of one lane in integer mode: the lane-group words wv[r] of RPW
+// rows against the x tile at xs (slices; xoff[q] this lane's column in quad
+// q's rows) and the lane's (scale, x sum) pairs at ss, folded into tot[r].
+template <int F, int RPW>
+__device__ __forceinline__ void int_ktile(const uint32_t (&wv)[RPW][GemvCfg<F, 1, RPW, true>::WPG], uint32_t xs,
+                                          uint32_t ss, const uint32_t (&xoff)[8], float (&tot)[RPW][1]) {
+    constexpr int G = Fmt<F>::kGroupBlocks;
+#pragma unroll
+    for (int bg = 0; bg < G; ++bg) {
+        const float2 sc = lds_f2(ss + (uint32_t)bg * 8u);
+        uint4 xq[6];  // (slice, half): x slices of this lane's block bg
+#pragma unroll
+        for (int k = 0; k < 6; ++k) xq[k] = lds_u4(xs + (uint32_t)(bg * 6 + k) * 512u + xoff[2 * bg + (k & 1)]);
+#pragma unroll
+        for (int r = 0; r < RPW; ++r) {
+            uint32_t c[8];
+            if constexpr (F == kQ8_0) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) c[j] = qs_word<F>(wv[r], bg, j);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const uint32_t qw = qs_word<F>(wv[r], bg, j);
+                    c[j] = qw & 0x0F0F0F0Fu;
+                    c[4 + j] = (qw >> 4) & 0x0F0F0F0Fu;
+                }
+            }
+            int acc[3];
+#pragma unroll
+            for (int sl = 0; sl < 3; ++sl) {
+                const uint4 lo = xq[2 * sl], hi = xq[2 * sl + 1];
+                int v = __dp4a((int)c[0], (int)lo.x, 0);
+                v = __dp4a((int)c[1], (int)lo.y, v);
+                v = __dp4a((int)c[2], (int)lo.z, v);
+                v = __dp4a((int)c[3], (int)lo.w, v);
+                v = __dp4a((int)c[4], (int)hi.x, v);
+                v = __dp4a((int)c[5], (int)hi.y, v);
+                v = __dp4a((int)c[6], (int)hi.z, v);
+                v = __dp4a((int)c[7], (int)hi.w, v);
+                acc[sl] = v;
+            }
+            const float qx =
+                sc.x * fmaf(__int2float_rn(acc[1] * 254 + acc[2]), kInvSlice2, __int2float_rn(acc[0]));
+            const float d = half_bits_to_float(d_bits<F>(wv[r], bg));
+            if constexpr (F == kQ4_0) {
+                tot[r][0] = fmaf(d, fmaf(-8.0f, sc.y, qx), tot[r][0]);
+            } else if constexpr (F == kQ4_1) {
+                tot[r][0] = fmaf(d, qx, tot[r][0]);
+                tot[r][0] = fmaf(half_bits_to_float(wv[r][0] >> 16), sc.y, tot[r][0]);
+            } else {
+                tot[r][0] = fmaf(d, qx, tot[r][0]);
+            }
+        }
+    }
+}
+
 constexpr int log2_of(int n) { return n <= 1 ? 0 : 1 + log2_of(n / 2); }
 
 // A CTA's producer is done taking tiles from the launch's queue {next, done}:
@@ -798,54 +854,7 @@ __global__ void __launch_bounds__(threads_for(MT), MINB)
             if (*(volatile int*)&abort_flag) return -1;
 
             if constexpr (INT) {
-#pragma unroll
-                for (int bg = 0; bg < C::G; ++bg) {
-                    const float2 sc = lds_f2(ss + (uint32_t)bg * 8u);
-                    uint4 xq[6];  // (slice, half): x slices of this lane's block bg
-#pragma unroll
-                    for (int k = 0; k < 6; ++k)
-                        xq[k] = lds_u4(xs + (uint32_t)(bg * 6 + k) * 512u + xoff[2 * bg + (k & 1)]);
-#pragma unroll
-                    for (int r = 0; r < RPW; ++r) {
-                        uint32_t c[8];
-                        if constexpr (F == kQ8_0) {
-#pragma unroll
-                            for (int j = 0; j < 8; ++j) c[j] = qs_word<F>(wv[r], bg, j);
-                        } else {
-#pragma unroll
-                            for (int j = 0; j < 4; ++j) {
-                                const uint32_t qw = qs_word<F>(wv[r], bg, j);
-                                c[j] = qw & 0x0F0F0F0Fu;
-                                c[4 + j] = (qw >> 4) & 0x0F0F0F0Fu;
-                            }
-                        }
-                        int acc[3];
-#pragma unroll
-                        for (int sl = 0; sl < 3; ++sl) {
-                            const uint4 lo = xq[2 * sl], hi = xq[2 * sl + 1];
-                            int v = __dp4a((int)c[0], (int)lo.x, 0);
-                            v = __dp4a((int)c[1], (int)lo.y, v);
-                            v = __dp4a((int)c[2], (int)lo.z, v);
-                            v = __dp4a((int)c[3], (int)lo.w, v);
-                            v = __dp4a((int)c[4], (int)hi.x, v);
-                            v = __dp4a((int)c[5], (int)hi.y, v);
-                            v = __dp4a((int)c[6], (int)hi.z, v);
-                            v = __dp4a((int)c[7], (int)hi.w, v);
-                            acc[sl] = v;
-                        }
-                        const float qx = sc.x * fmaf(__int2float_rn(acc[1] * 254 + acc[2]), kInvSlice2,
-                                                     __int2float_rn(acc[0]));
-                        const float d = half_bits_to_float(d_bits<F>(wv[r], bg));
-                        if constexpr (F == kQ4_0) {
-                            tot[r][0] = fmaf(d, fmaf(-8.0f, sc.y, qx), tot[r][0]);
-                        } else if constexpr (F == kQ4_1) {
-                            tot[r][0] = fmaf(d, qx, tot[r][0]);
-                            tot[r][0] = fmaf(half_bits_to_float(wv[r][0] >> 16), sc.y, tot[r][0]);
-                        } else {
-                            tot[r][0] = fmaf(d, qx, tot[r][0]);
-                        }
-                    }
-                }
+                int_ktile<F, RPW>(wv, xs, ss, xoff, tot);
             } else {
 #pragma unroll
             for (int bg = 0; bg < C::G; ++bg) {
@@ -1024,6 +1033,287 @@ __global__ void __launch_bounds__(threads_for(MT), MINB)
                     }
                 }
             }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// A run of independent one-row products in one launch.
+//
+// Launched one by one, each product of a decode step pays a launch's
+// start-up: a CTA's first weights land ~2.5 us after it starts, its x tiles
+// are built meanwhile, and the next launch's CTAs find the SMs' shared
+// memory taken until the last CTA of the previous one leaves.  A run instead:
+//  * gemv_run_xprep_kernel slices every op's x once (integer mode, in the
+//    x-tile layout the consumers read) into a workspace that stays in L2;
+//  * gemv_run_kernel (persistent, two CTAs per SM) takes row tiles of all
+//    ops from one queue -- ops with the most K-tiles first, so the long
+//    tiles start early -- and each stage brings its weights (2-D tensor map)
+//    and, into a ring of x slots, the stage's x tile (one bulk copy).  Its
+//    producer streams the first stages' weights before the grid dependency
+//    (weights are read-only) and copies x tiles only after it.
+// The decode per K-tile is the streaming kernel's integer mode (int_ktile).
+// ---------------------------------------------------------------------------
+constexpr int kRunThreads = 32 * (1 + kConsumerWarps);
+
+struct RunOpDev {
+    float* y;
+    const float* bias;
+    int out;
+    int ktiles;
+    int unit0;  // this op's first row tile in the launch's queue order
+    int xt0;    // this op's first x tile in the workspace
+};
+
+struct RunArgs {
+    RunOpDev op[kGemvRunMaxOps];
+    int nop;
+    int units;               // row tiles of all ops
+    const uint8_t* xtiles;   // workspace: XT_BYTES per x tile
+    unsigned int* tiles;     // queue {next, done}, or null: strided static tiles
+    int nstages, nxslots;
+    int* err;
+};
+
+struct RunXprepArgs {
+    const float* x[kGemvRunMaxOps];
+    int in[kGemvRunMaxOps];
+    int xt0[kGemvRunMaxOps];
+    int nop;
+    uint8_t* xtiles;
+};
+
+// One CTA per x tile: warp i slices piece i of the tile (int_piece_*), then
+// the CTA copies the finished tile out with 16-byte stores.
+template <int F>
+__global__ void __launch_bounds__(64 * Fmt<F>::kGroupBlocks)
+    gemv_run_xprep_kernel(const __grid_constant__ RunXprepArgs a) {
+    using C = GemvCfg<F, 1, 4, true>;  // the x-tile layout does not depend on the rows per warp
+    __shared__ __align__(16) uint8_t tile[C::XT_BYTES];
+    launch_dependents();    // the run kernel may start streaming weights
+    grid_dependency_wait();  // x may be the previous kernel's output
+    const int t = blockIdx.x;
+    int o = 0;
+    for (int k = 1; k < a.nop; ++k)
+        if (t >= a.xt0[k]) o = k;
+    const int kt = t - a.xt0[o];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float v[16];
+    int_piece_load<C::G>(a.x[o], a.in[o], (long long)kt * C::KTE, warp, lane, v);
+    const uint32_t xs = smem_u32(tile);
+    int_piece_store<C::G>(v, warp, lane, xs, xs + C::X_BYTES);
+    __syncthreads();
+    const uint4* src = reinterpret_cast<const uint4*>(tile);
+    uint4* dst = reinterpret_cast<uint4*>(a.xtiles + (size_t)t * C::XT_BYTES);
+    for (int k = threadIdx.x; k < C::XT_BYTES / 16; k += blockDim.x) dst[k] = src[k];
+}
+
+template <int F, int RPW>
+__global__ void __launch_bounds__(kRunThreads, 2)
+    gemv_run_kernel(const __grid_constant__ RunArgs a, const __grid_constant__ WMaps<kGemvRunMaxOps> wm) {
+    using C = GemvCfg<F, 1, RPW, true>;
+    constexpr int TR = C::RT;
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ __align__(8) uint64_t full_bar[kMaxStages];   // a stage's weights landed
+    __shared__ __align__(8) uint64_t empty_bar[kMaxStages];  // ... and are in the consumers' registers
+    __shared__ __align__(8) uint64_t xfull_bar[kMaxStages];  // an x slot's tile landed
+    __shared__ __align__(8) uint64_t xempty_bar[kMaxStages]; // ... and is consumed
+    __shared__ int stage_unit[kMaxStages];                   // row tile of each stage (-1: end)
+    __shared__ int abort_flag;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int S = a.nstages, NX = a.nxslots;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kMaxStages; ++s) {
+            mbar_init(smem_u32(&full_bar[s]), 32);
+            mbar_init(smem_u32(&empty_bar[s]), kConsumerWarps);
+            mbar_init(smem_u32(&xfull_bar[s]), 1);
+            mbar_init(smem_u32(&xempty_bar[s]), kConsumerWarps);
+        }
+        abort_flag = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+    launch_dependents();
+    const uint32_t smem_base = (smem_u32(smem) + 127u) & ~127u;
+    const uint32_t x_base = smem_base + (uint32_t)S * C::W_BYTES;
+    // op of row tile u: ops are laid out in queue order by unit0
+    auto op_of = [&](int u) {
+        int o = 0;
+        for (int k = 1; k < a.nop; ++k)
+            if (u >= a.op[k].unit0) o = k;
+        return o;
+    };
+
+    if (warp == 0) {
+        // ------------------------------ producer ------------------------------
+        const uint64_t wpol = l2_evict_first_policy();
+        uint32_t seq = 0;      // stages issued
+        uint32_t xissued = 0;  // x copies issued (stages [0, xissued))
+        int s = 0;
+        uint32_t ph = 0;
+        bool dep = false;
+        int pend[kMaxStages];  // (op << 16 | kt) of stages whose x copy waits for the dependency
+        auto issue_x = [&](uint32_t k, int o, int kt) {
+            const uint32_t xb = smem_u32(&xfull_bar[k % (uint32_t)NX]);
+            mbar_arrive_expect_tx(xb, (uint32_t)C::XT_BYTES);
+            bulk_g2s(x_base + (k % (uint32_t)NX) * (uint32_t)C::XT_BYTES,
+                     a.xtiles + (size_t)(a.op[o].xt0 + kt) * C::XT_BYTES, (uint32_t)C::XT_BYTES, xb);
+        };
+        // the grid dependency, then the x copies of stages [xissued, end)
+        auto flush_pending = [&](uint32_t end) {
+            grid_dependency_wait();
+            dep = true;
+            if (lane == 0)
+                for (uint32_t k = xissued; k < end; ++k) issue_x(k, pend[k] >> 16, pend[k] & 0xFFFF);
+            xissued = end;
+        };
+        unsigned int ticket = 0;
+        if (lane == 0) ticket = a.tiles ? atomicAdd(a.tiles, 1u) : blockIdx.x;
+        for (int n = 1;; ++n) {
+            const int u = (int)__shfl_sync(0xffffffffu, ticket, 0);
+            if (u >= a.units) break;
+            if (lane == 0) ticket = a.tiles ? atomicAdd(a.tiles, 1u) : blockIdx.x + (unsigned int)n * gridDim.x;
+            const int o = op_of(u);
+            const long long row0 = (long long)(u - a.op[o].unit0) * TR;
+            const int nrows = (int)min((long long)TR, (long long)a.op[o].out - row0);
+            const int nbox = (nrows + 7) / 8 * C::NREG;
+            for (int kt = 0; kt < a.op[o].ktiles; ++kt, ++seq) {
+                bool ok = mbar_wait(smem_u32(&empty_bar[s]), ph ^ 1u);
+                if (ok)
+                    ok = mbar_wait(smem_u32(&xempty_bar[seq % (uint32_t)NX]), ((seq / (uint32_t)NX) & 1u) ^ 1u);
+                if (!ok) {
+                    report_error(a.err, 2);
+                    abort_flag = 1;
+                }
+                if (*(volatile int*)&abort_flag) goto producer_drain;
+                const uint32_t stage = smem_base + (uint32_t)s * C::W_BYTES;
+                const uint32_t fb = smem_u32(&full_bar[s]);
+                if (lane == 0) {
+                    stage_unit[s] = u;
+                    mbar_expect_tx(fb, (uint32_t)(nbox * 8 * C::BOXB));
+                }
+                __syncwarp();
+                if (lane < nbox) {
+                    const int reg = lane % C::NREG, b = lane / C::NREG;
+                    tma_load_2d_hint(stage + (uint32_t)(reg * C::REGION + b * 8 * C::BOXB), &wm.m[o],
+                                     kt * C::NREG * C::BOXW + reg * C::BOXW, (int)(row0 + 8 * b), fb, wpol);
+                }
+                mbar_arrive(fb);
+                __syncwarp();
+                if (dep) {
+                    if (lane == 0) issue_x(seq, o, kt);
+                    xissued = seq + 1;
+                } else {
+                    pend[seq] = (o << 16) | kt;
+                    // S stages of weights in flight: the x tiles now
+                    if (seq + 1 == (uint32_t)S) flush_pending(seq + 1);
+                }
+                if (++s == S) {
+                    s = 0;
+                    ph ^= 1u;
+                }
+            }
+        }
+        if (!dep) flush_pending(seq);
+        // end marker for the consumers: a stage with no bytes and row tile -1
+        if (!mbar_wait(smem_u32(&empty_bar[s]), ph ^ 1u)) {
+            report_error(a.err, 2);
+            abort_flag = 1;
+        }
+        if (*(volatile int*)&abort_flag) goto producer_drain;
+        if (lane == 0) stage_unit[s] = -1;
+        __syncwarp();
+        mbar_arrive(smem_u32(&full_bar[s]));
+        if (a.tiles && lane == 0) release_tile_queue(a.tiles);
+        return;
+    producer_drain:
+        // Abort: wait (bounded) for the copies still in flight into this CTA.
+        for (uint32_t k = (seq >= (uint32_t)S ? seq - (uint32_t)S : 0); k < seq; ++k) {
+            if (!mbar_wait(smem_u32(&full_bar[k % (uint32_t)S]), (k / (uint32_t)S) & 1u)) {
+                report_error(a.err, 3);
+                break;
+            }
+        }
+        for (uint32_t k = (xissued >= (uint32_t)NX ? xissued - (uint32_t)NX : 0); k < xissued; ++k) {
+            if (!mbar_wait(smem_u32(&xfull_bar[k % (uint32_t)NX]), (k / (uint32_t)NX) & 1u)) {
+                report_error(a.err, 3);
+                break;
+            }
+        }
+        if (a.tiles && lane == 0) release_tile_queue(a.tiles);
+        return;
+    }
+
+    // -------------------------------- consumers --------------------------------
+    const int wc = warp - 1;
+    uint32_t xoff[8];
+#pragma unroll
+    for (int p = 0; p < 8; ++p) xoff[p] = xcol<C::G>(lane, p & (2 * C::G - 1));
+    uint32_t soff[RPW];  // this lane's group in each of its rows' box rows
+#pragma unroll
+    for (int r = 0; r < RPW; ++r) {
+        constexpr int LPR = 32 / C::NREG;
+        soff[r] = (uint32_t)((lane / LPR) * C::REGION + (wc + r * kConsumerWarps) * C::BOXB + (lane % LPR) * C::GB);
+    }
+    int s = 0;
+    uint32_t ph = 0, seq = 0;
+    for (;;) {
+        if (!mbar_wait(smem_u32(&full_bar[s]), ph)) {
+            report_error(a.err, 1);
+            abort_flag = 1;
+        }
+        if (*(volatile int*)&abort_flag) return;
+        const int u = *(volatile int*)&stage_unit[s];
+        if (u < 0) break;
+        const int o = op_of(u);
+        const long long row0 = (long long)(u - a.op[o].unit0) * TR;
+        const int nrows = (int)min((long long)TR, (long long)a.op[o].out - row0);
+        const int kts = a.op[o].ktiles;
+        float tot[RPW][1];
+#pragma unroll
+        for (int r = 0; r < RPW; ++r) tot[r][0] = 0.f;
+        for (int kt = 0; kt < kts; ++kt, ++seq) {
+            if (kt > 0 && !mbar_wait(smem_u32(&full_bar[s]), ph)) {
+                report_error(a.err, 1);
+                abort_flag = 1;
+            }
+            if (*(volatile int*)&abort_flag) return;
+            // 2-D boxes: bytes past a row's end and rows past the matrix
+            // arrive as zeros (tensor-map bounds)
+            const uint32_t stage = smem_base + (uint32_t)s * C::W_BYTES;
+            uint32_t wv[RPW][C::WPG];
+#pragma unroll
+            for (int r = 0; r < RPW; ++r)
+#pragma unroll
+                for (int j = 0; j < C::WPG; ++j) wv[r][j] = lds_u32(stage + soff[r] + 4 * j);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&empty_bar[s]));
+            const uint32_t xk = seq % (uint32_t)NX;
+            if (!mbar_wait(smem_u32(&xfull_bar[xk]), (seq / (uint32_t)NX) & 1u)) {
+                report_error(a.err, 1);
+                abort_flag = 1;
+            }
+            if (*(volatile int*)&abort_flag) return;
+            const uint32_t xs = x_base + xk * (uint32_t)C::XT_BYTES;
+            int_ktile<F, RPW>(wv, xs, xs + C::X_BYTES + (uint32_t)lane * C::G * 8, xoff, tot);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&xempty_bar[xk]));
+            if (++s == S) {
+                s = 0;
+                ph ^= 1u;
+            }
+        }
+        // reduce-scatter the RPW row sums; the lead lane of each row stores it
+        float v = reduce_rows<RPW>(tot, lane);
+        const int r = lane >> (5 - log2_of(RPW));
+        const int i = wc + r * kConsumerWarps;
+        if ((lane & (31 >> log2_of(RPW))) == 0 && i < nrows) {
+            const long long row = row0 + i;
+            const float* bias = a.op[o].bias;
+            if (bias) v = __fadd_rn(v, bias[row]);
+            a.op[o].y[row] = v;
         }
     }
 }
@@ -1262,7 +1552,129 @@ cudaError_t dispatch_mt(const GemvArgs& args, int sm_count, int smem_per_sm, cud
     }
 }
 
+int ktiles_of(int fmt, int in) {
+    const int bpr = (in + kQK - 1) / kQK;
+    const int gpr = bpr / (fmt == kQ4_1 ? 1 : 2);
+    return (gpr + 31) / 32;
+}
+
+template <int F>
+cudaError_t launch_run_t(const GemvRunOp* ops, int nop, void* ws, int sm_count, int smem_per_sm, int* err,
+                         cudaStream_t stream) {
+    constexpr int RPW = rpw_for<F>();
+    using C = GemvCfg<F, 1, RPW, true>;
+    if (nop < 1 || nop > kGemvRunMaxOps) return cudaErrorInvalidValue;
+    // queue order: most K-tiles first (a stable order otherwise)
+    int ord[kGemvRunMaxOps];
+    for (int k = 0; k < nop; ++k) ord[k] = k;
+    for (int k = 1; k < nop; ++k)
+        for (int j = k; j > 0 && ktiles_of(F, ops[ord[j]].in) > ktiles_of(F, ops[ord[j - 1]].in); --j) {
+            const int t = ord[j];
+            ord[j] = ord[j - 1];
+            ord[j - 1] = t;
+        }
+    RunArgs ra;
+    std::memset(&ra, 0, sizeof(ra));
+    RunXprepArgs xa;
+    std::memset(&xa, 0, sizeof(xa));
+    WMaps<kGemvRunMaxOps> wm;
+    std::memset(&wm, 0, sizeof(wm));
+    int units = 0, xt = 0;
+    for (int k = 0; k < nop; ++k) {
+        const GemvRunOp& op = ops[ord[k]];
+        const long long row_bytes = (long long)((op.in + kQK - 1) / kQK) * Fmt<F>::kBlockBytes;
+        if (!make_map_2d(&wm.m[k], CU_TENSOR_MAP_DATA_TYPE_UINT64, const_cast<uint8_t*>(op.w),
+                         (uint64_t)(row_bytes / 8), (uint64_t)op.out, (uint64_t)row_bytes, (uint32_t)C::BOXW, 8u,
+                         CU_TENSOR_MAP_SWIZZLE_NONE))
+            return cudaErrorInvalidValue;
+        const int kts = ktiles_of(F, op.in);
+        ra.op[k] = RunOpDev{op.y, op.bias, op.out, kts, units, xt};
+        xa.x[k] = op.x;
+        xa.in[k] = op.in;
+        xa.xt0[k] = xt;
+        units += (op.out + C::RT - 1) / C::RT;
+        xt += kts;
+    }
+    ra.nop = xa.nop = nop;
+    ra.units = units;
+    ra.xtiles = static_cast<const uint8_t*>(ws);
+    xa.xtiles = static_cast<uint8_t*>(ws);
+    ra.err = err;
+    // Two CTAs per SM: S weight stages and NX >= S x slots per CTA (an x
+    // slot is held from its copy until the stage is consumed; the first S
+    // stages' x copies wait for the grid dependency, so S slots must be free
+    // then).
+    const int budget = smem_per_sm / 2 - 1024 - 1024 - 128;
+    int S = budget / (C::W_BYTES + C::XT_BYTES);
+    if (S > kMaxStages) S = kMaxStages;
+    if (S < 2) return cudaErrorInvalidConfiguration;
+    int NX = (budget - S * C::W_BYTES) / C::XT_BYTES;
+    if (NX > kMaxStages) NX = kMaxStages;
+    if (NX < S) return cudaErrorInvalidConfiguration;
+    ra.nstages = S;
+    ra.nxslots = NX;
+    const int smem = S * C::W_BYTES + NX * C::XT_BYTES + 128;
+    static std::atomic<bool> attr_done[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 64 || !attr_done[dev].load(std::memory_order_acquire)) {
+        cudaError_t e = cudaFuncSetAttribute(gemv_run_kernel<F, RPW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             budget + 128);
+        if (e != cudaSuccess) return e;
+        if (dev < 64) attr_done[dev].store(true, std::memory_order_release);
+    }
+    int grid = 2 * sm_count;
+    if (grid > units) grid = units;
+    ra.tiles = tile_queue(dev, stream);  // null while capturing: strided static tiles
+
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cx = {};
+    cx.gridDim = dim3(xt);
+    cx.blockDim = dim3(64 * C::G);
+    cx.stream = stream;
+    cx.attrs = attr;
+    cx.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cx, gemv_run_xprep_kernel<F>, xa);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kRunThreads);
+    cfg.dynamicSmemBytes = (size_t)smem;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, gemv_run_kernel<F, RPW>, ra, wm);
+}
+
 }  // namespace
+
+bool gemv_run_ok(int fmt, const GemvRunOp& op) {
+    if (fmt != kQ8_0 && fmt != kQ4_0 && fmt != kQ4_1) return false;
+    if (op.out < 1 || op.in < 1 || !op.w || !op.x || !op.y) return false;
+    const int bpr = (op.in + kQK - 1) / kQK;
+    const long long row_bytes = (long long)bpr * block_bytes(fmt);
+    return reinterpret_cast<uintptr_t>(op.w) % 16 == 0 && reinterpret_cast<uintptr_t>(op.x) % 16 == 0 &&
+           row_bytes % 16 == 0 && bpr % (fmt == kQ4_1 ? 1 : 2) == 0 && op.in % 4 == 0 && encode_fn() != nullptr;
+}
+
+size_t gemv_run_workspace_bytes(int fmt, const GemvRunOp* ops, int nop) {
+    size_t tiles = 0;
+    for (int k = 0; k < nop; ++k) tiles += (size_t)ktiles_of(fmt, ops[k].in);
+    const size_t xt = fmt == kQ4_1 ? GemvCfg<kQ4_1, 1, 4, true>::XT_BYTES : GemvCfg<kQ4_0, 1, 4, true>::XT_BYTES;
+    return tiles * xt;
+}
+
+cudaError_t launch_gemv_run(int fmt, const GemvRunOp* ops, int nop, void* ws, int sm_count, int smem_per_sm,
+                            int* err, cudaStream_t stream) {
+    switch (fmt) {
+        case kQ8_0: return launch_run_t<kQ8_0>(ops, nop, ws, sm_count, smem_per_sm, err, stream);
+        case kQ4_0: return launch_run_t<kQ4_0>(ops, nop, ws, sm_count, smem_per_sm, err, stream);
+        case kQ4_1: return launch_run_t<kQ4_1>(ops, nop, ws, sm_count, smem_per_sm, err, stream);
+    }
+    return cudaErrorInvalidValue;
+}
 
 int gemv_tokens_per_pass(int rows_left) {
     return rows_left >= 5 ? 8 : (rows_left >= 3 ? 4 : (rows_left == 2 ? 2 : 1));

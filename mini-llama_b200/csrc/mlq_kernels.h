@@ -62,6 +62,33 @@ int gemv_tokens_per_pass(int rows_left);
 cudaError_t launch_gemv_stream(int fmt, const GemvArgs& args, int mt, int sm_count,
                                int smem_per_sm, cudaStream_t stream);
 
+// A run of independent one-row products in one persistent launch (plus a
+// small launch that slices every op's x once into the workspace): one
+// tile queue over all ops' row tiles, so the ops do not each pay a launch's
+// start-up.  All ops of a run share the format.
+constexpr int kGemvRunMaxOps = 8;
+struct GemvRunOp {
+    const uint8_t* w;
+    const float* x;      // [in], one row
+    float* y;            // [out]
+    const float* bias;   // [out] or null
+    int out, in;
+};
+
+// True when an op can join a run: one row of x, weights and x 16-B aligned
+// with a 16-B multiple row pitch (2-D tensor map), whole lane-groups per
+// row, in % 4 == 0, and the driver's tensor-map encoder reachable.
+bool gemv_run_ok(int fmt, const GemvRunOp& op);
+
+// Workspace of a run: the sliced x tiles of every op.
+size_t gemv_run_workspace_bytes(int fmt, const GemvRunOp* ops, int nop);
+
+// y[k] = x[k] W[k]^T (+ bias[k]) for nop <= kGemvRunMaxOps ops that pass
+// gemv_run_ok and do not touch one another's outputs; waits for the
+// previous kernel on the stream before reading any x, bias or writing y.
+cudaError_t launch_gemv_run(int fmt, const GemvRunOp* ops, int nop, void* ws, int sm_count, int smem_per_sm,
+                            int* err, cudaStream_t stream);
+
 // Sets the message mlq_last_error() returns on this host thread.
 void set_last_error(const char* msg);
 inline void set_last_error(const std::string& msg) { set_last_error(msg.c_str()); }

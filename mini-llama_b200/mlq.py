@@ -231,6 +231,20 @@ def takes_gemm(rows: int, out_features: int, in_features: int) -> bool:
                                       and out_features * in_features >= GEMM_LARGE_MIN_WEIGHTS)
 
 
+RUN_MAX_OPS = 8  # ops per persistent launch of a run (mlq_linear_batch)
+
+
+def joins_run(fmt, rows: int, in_features: int) -> bool:
+    """Whether a batch op with 16-byte aligned weights and x can join a
+    one-launch run of independent products (mlq_linear_batch): one row of
+    x, a row pitch that is a multiple of 16 bytes, whole lane-groups per
+    row (q8_0 / q4_0: an even block count), in_features % 4 == 0."""
+    name = _fmt_name(fmt)
+    bpr = (in_features + 31) // 32
+    return (rows == 1 and in_features % 4 == 0 and (bpr * BLOCK_BYTES[name]) % 16 == 0
+            and (name == "q4_1" or bpr % 2 == 0))
+
+
 def linear_noalloc(fmt, w, out_features: int, in_features: int, x, y, stream=None):
     """mlq_linear_noalloc: like linear() but the library allocates no device
     memory (the caller passes y; calls that take the GEMM need rows * in * 4 bytes <=

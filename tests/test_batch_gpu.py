@@ -221,3 +221,87 @@ def test_batch_gemv_runs_respect_dependencies(pkg, oracle):
     assert rel_l2_rows(y4.cpu().numpy(), r4).max() <= TOL  # op 4 read x4 before op 5 overwrote it
     assert rel_l2_rows(x4d.cpu().numpy(), r5).max() <= TOL
     assert mlq.device_error(0) == 0
+
+
+def _run_case(pkg, oracle, fmt, shapes, bias_at=(), seed=1300):
+    """One-row ops of one format on distinct x and y: the batch runs them as
+    one persistent launch per eight ops.  Returns the batch's ops, outputs,
+    the matching single calls' outputs and the oracle's."""
+    mlq = pkg.mlq
+    keep, ops, outs, singles, refs, xds = [], [], [], [], [], []
+    for k, (out_f, in_f) in enumerate(shapes):
+        wb = oracle.quantize(fmt, pkg.synth.normal((out_f, in_f), seed=seed + k, std=0.02))
+        x = pkg.synth.normal((1, in_f), seed=seed + 100 + k)
+        w, xd = dev(wb), dev(x)
+        y = torch.full((1, out_f), float("nan"), device="cuda")
+        keep.append(w)
+        xds.append(xd)
+        ref = oracle.linear(fmt, x, wb, out_f)
+        if k in bias_at:
+            b = pkg.synth.normal((out_f,), seed=seed + 200 + k, std=0.5)
+            bd = dev(b)
+            keep.append(bd)
+            ops.append(mlq.linear_op(fmt, w.data_ptr(), out_f, in_f, xd.data_ptr(), 1, y.data_ptr(),
+                                     bias_ptr=bd.data_ptr()))
+            singles.append(mlq.linear_bias(fmt, w, out_f, in_f, xd, bd))
+            ref = ref + b[None, :]
+        else:
+            ops.append(mlq.linear_op(fmt, w.data_ptr(), out_f, in_f, xd.data_ptr(), 1, y.data_ptr()))
+            singles.append(mlq.linear(fmt, w, out_f, in_f, xd))
+        outs.append(y)
+        refs.append(ref)
+    return keep, xds, ops, outs, singles, refs
+
+
+@pytest.mark.parametrize("fmt", ["q8_0", "q4_0", "q4_1"])
+def test_batch_run_of_one_row_ops(pkg, oracle, fmt):
+    """A run of independent one-row ops (ten: two persistent launches) with
+    mixed shapes -- a long K (10 K-tiles), partial K-tiles, row counts that
+    are not tile multiples, a single row, biases -- gives every op's y bit
+    for bit as the op run alone (the same integer-mode decode and summation
+    order), and within the contract of the oracle."""
+    shapes = [(1000, 3584), (4096, 18944), (1, 1024), (333, 2048), (2500, 4096), (64, 1280),
+              (700, 3584), (129, 5120), (4100, 1024), (90, 2304)]
+    keep, xds, ops, outs, singles, refs = _run_case(pkg, oracle, fmt, shapes, bias_at=(1, 4, 9))
+    pkg.mlq.Batch(ops).run(torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    for k, (y, one, ref) in enumerate(zip(outs, singles, refs)):
+        yn = y.cpu().numpy()
+        np.testing.assert_array_equal(yn, one.cpu().numpy(), err_msg=f"op {k} {shapes[k]}")
+        assert rel_l2_rows(yn, ref).max() <= TOL, k
+    assert pkg.mlq.device_error(0) == 0
+
+
+def test_batch_run_in_a_cuda_graph(pkg, oracle):
+    """The same run captured in a CUDA graph (no tile queue while capturing:
+    each CTA takes a fixed stride of row tiles) and replayed twice on new x
+    values: every y equal to the op run alone."""
+    mlq = pkg.mlq
+    fmt = "q4_0"
+    shapes = [(3584, 3584), (512, 3584), (18944, 3584), (3584, 18944)]
+    keep, xds, ops, outs, singles, refs = _run_case(pkg, oracle, fmt, shapes, bias_at=(1,), seed=1500)
+    batch = mlq.Batch(ops)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        batch.run(s.cuda_stream)  # sizes the stream's workspace before the capture
+    s.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        batch.run(s.cuda_stream)
+    for it in range(2):
+        for k, x in enumerate(xds):
+            x.copy_(torch.from_numpy(pkg.synth.normal(tuple(x.shape), seed=1600 + 10 * it + k)))
+        for y in outs:
+            y.fill_(float("nan"))
+        torch.cuda.synchronize()
+        g.replay()
+        torch.cuda.synchronize()
+        for k, ((out_f, in_f), y, op) in enumerate(zip(shapes, outs, ops)):
+            one = mlq.LinearOp.from_buffer_copy(op)
+            yd = torch.empty((1, out_f), device="cuda")
+            one.y = yd.data_ptr()
+            mlq.Batch([one]).run(None)
+            torch.cuda.synchronize()
+            np.testing.assert_array_equal(y.cpu().numpy(), yd.cpu().numpy(), err_msg=f"replay {it} op {k}")
+    del g
+    assert mlq.device_error(0) == 0
