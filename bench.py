@@ -391,6 +391,7 @@ class Ctx:
             self.group = self.sh.PeerGroup(self.mlq, dist, self.rank, self.world)
             self.flags = self.group.alloc(self.mlq.flag_bytes())
         self.tok = torch.zeros(1, device=self.device)
+        self.epoch = 0  # last epoch published on self.flags (every workload continues it)
 
     def max_over_ranks(self, v):
         if self.world == 1:
@@ -434,7 +435,8 @@ class Step:
         self.ctx, self.wl = ctx, wl
         fmt, rows, mats = wl["fmt"], wl["rows"], wl["matrices"]
         self.fmt, self.rows = fmt, rows
-        self.plan = sh.StepPlan(mats, ctx.world, ctx.rank, shard=wl["shard"])
+        # epochs continue the sequence of every earlier workload on ctx.flags
+        self.plan = sh.StepPlan(mats, ctx.world, ctx.rank, shard=wl["shard"], epoch0=ctx.epoch)
         fused = wl.get("fused", {})
         pair = fused.get("pair")
         if pair and ctx.world > 1:
@@ -516,28 +518,40 @@ class Step:
             nb = weight_bytes(fmt, e - b, in_f)
             self.op_bytes.append(2 * nb if (pair and name == pair[0]) else nb)
         self.ops = ops
-        # A run of independent one-launch GEMVs (one token or two, local):
-        # one-row ops that all join a run take two launches per 8 ops (the x
-        # slicing and the persistent run kernel) instead of one launch each;
-        # other runs end with the library's join launch.
-        run = []
-        for name, out_f, in_f in mats + [(None, 0, 0)]:
-            one = (name is not None and self.plan.active(name) and self.plan.place[name] != "shard" and
-                   not (pair and name == pair[1]) and
-                   rows <= 2 and not mlq.takes_bgemm(rows, out_f, in_f) and not mlq.takes_gemm(rows, out_f, in_f))
-            if one:
-                run.append((name, in_f))
+        # How the library launches the step (mlq_linear_batch): consecutive
+        # one-row ops that join a run (local or gathered) take two launches
+        # per 8 ops -- the x slicing and the persistent run kernel -- instead
+        # of one launch each; other runs of local one-launch GEMVs end with
+        # the library's join launch.
+        seq = [(n, o, i) for n, o, i in mats if self.plan.active(n) and not (pair and n == pair[1])]
+
+        def member(n, i):
+            return rows == 1 and mlq.joins_run(fmt, rows, i) and not (pair and n == pair[0])
+
+        def one_gemv(n, o, i):
+            return (self.plan.place[n] != "shard" and rows <= 2 and not mlq.takes_bgemm(rows, o, i)
+                    and not mlq.takes_gemm(rows, o, i))
+        k = 0
+        while k < len(seq):
+            j = k
+            while j < len(seq) and member(seq[j][0], seq[j][2]):
+                j += 1
+            if j - k >= 2:
+                self.launches.append(2 * -(-(j - k) // mlq.RUN_MAX_OPS) - (j - k))
+                self.one_run = j - k == len(seq)
+                k = j
                 continue
-            if len(run) >= 2:
-                if all(mlq.joins_run(fmt, rows, i) and not (pair and n == pair[0]) for n, i in run):
-                    self.launches.append(2 * -(-len(run) // mlq.RUN_MAX_OPS) - len(run))
-                    self.one_run = len(run) == len(self.names)
-                else:
-                    self.launches.append(1)
-            run = []
+            j = k
+            while j < len(seq) and one_gemv(*seq[j]):
+                j += 1
+            if j - k >= 2:
+                self.launches.append(1)
+            k = max(j, k + 1)
         # the step's one cross-rank wait: every rank's highest epoch of the step
         self.waiter = (mlq.make_gather(ctx.world, ctx.rank, 0, 0, [0] * ctx.world, ctx.flags.peers, epoch=1)
                        if shard_names else None)
+        if self.waiter is not None and ctx.world > 1:
+            self.launches.append(1)  # mlq_gather_wait's kernel, once per step
         self.batch = [mlq.Batch(ops[0]), mlq.Batch(ops[1])]
         self.single = [[mlq.Batch([op]) for op in ops[p]] for p in (0, 1)]
         # rotating copies (an L2-sized matrix): one batch per copy
@@ -641,7 +655,7 @@ class Step:
         against one local mlq_linear of the whole matrix (regenerated from
         its seed) on the same x; max relative L2 error of an output row."""
         torch, mlq = self.ctx.torch, self.ctx.mlq
-        worst = 0.0
+        worst, where = 0.0, None
         for k, name in enumerate(self.plan.sharded):
             i, (_, out_f, in_f) = next((i, m) for i, m in enumerate(self.wl["matrices"]) if m[0] == name)
             parity = (self.plan.calls[name] - 1) & 1
@@ -651,9 +665,17 @@ class Step:
             torch.cuda.synchronize(self.ctx.device)
             err = (torch.linalg.norm((got - ref).double(), dim=1) /
                    torch.linalg.norm(ref.double(), dim=1).clamp_min(1e-30)).max().item()
-            worst = max(worst, err)
+            if err > worst:
+                # the shard (writing rank) whose rows differ most
+                shard_err = []
+                for r, (b, e) in enumerate(self.plan.ranges[name]):
+                    d = (got[:, b:e] - ref[:, b:e]).double().norm().item() if e > b else 0.0
+                    shard_err.append(round(d / max(ref[:, b:e].double().norm().item(), 1e-30), 4) if e > b else 0.0)
+                worst, where = err, {"matrix": name, "rank": self.ctx.rank, "shard_rel_l2": shard_err}
             del full, ref, got
         torch.cuda.empty_cache()
+        if where is not None and worst > 1e-3:
+            print(f"bench: parity of {where}: {worst:.3e}", file=sys.stderr, flush=True)
         return self.ctx.max_over_ranks(worst)
 
 
@@ -706,6 +728,7 @@ def run_workload(ctx, wl, steps, warmup, full=False, args=None):
                 "single_op_launches": single}
     if full and not (args and args.no_e2e):
         res["e2e"] = _e2e(ctx, st, steps)
+    ctx.epoch = st.plan.epoch
     del st
     torch.cuda.empty_cache()
     return res

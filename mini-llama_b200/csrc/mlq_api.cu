@@ -501,15 +501,36 @@ mlq_status run_op(const mlq_linear_op& op, const float* x, float* y, cudaStream_
     return run_linear(op.fmt, op.w, op.out_features, op.in_features, x, op.rows, y, stream, ep);
 }
 
-// A batch op as a member of a run of one-row products.
+// A batch op as a member of a run of one-row products (x, y: its device x
+// and y).  A gathered op streams its shard's rows into every rank's y.
 mlq::GemvRunOp run_op_of(const mlq_linear_op& op, const float* x, float* y) {
     mlq::GemvRunOp r;
+    std::memset(&r, 0, sizeof(r));
     r.w = static_cast<const uint8_t*>(op.w);
     r.x = x;
-    r.y = y;
-    r.bias = op.bias;
-    r.out = op.out_features;
     r.in = op.in_features;
+    r.world = 1;
+    if (!op.gather) {
+        r.bias = op.bias;
+        r.out = op.out_features;
+        r.y[0] = y;
+        r.ny = 1;
+        return r;
+    }
+    const mlq_gather& g = *op.gather;
+    r.out = g.row_end - g.row_begin;
+    r.bias = op.bias ? op.bias + g.row_begin : nullptr;
+    r.row_offset = g.row_begin;
+    r.ny = g.world_size;
+    for (int d = 0; d < g.world_size && d < mlq::kMaxWorld; ++d) r.y[d] = g.peer_y[d];
+    if (g.world_size > 1) {
+        r.world = g.world_size;
+        r.rank = g.rank;
+        for (int d = 0; d < g.world_size && d < mlq::kMaxWorld; ++d) r.flags[d] = g.peer_flags[d];
+        r.done_counter = reinterpret_cast<unsigned int*>(g.peer_flags[g.rank] + kDoneWord);
+        r.epoch = g.epoch;
+        r.wait = g.defer_wait ? 0 : 1;
+    }
     return r;
 }
 
@@ -518,13 +539,15 @@ mlq::GemvRunOp run_op_of(const mlq_linear_op& op, const float* x, float* y) {
 //    in_features and rows) and all take the batched-decode GEMM run as one
 //    grouped launch (up to kBgemmMaxGroup): Q, K and V of a layer read one x
 //    (src/forward.cc:425-435).
-//  * Consecutive ops that take one streaming-GEMV launch each and do not
-//    touch one another's outputs (no op's x, bias or y overlaps an earlier
-//    op's y, no op's y overlaps an earlier op's x) form a run.  A run of
-//    one-row ops of one format in the run kernel's layout takes one
-//    persistent launch (per kGemvRunMaxOps ops; launch_gemv_run).  Other
-//    runs go back to back: the first waits for the kernel before the batch,
-//    the others read x at once, and a join launch closes the run, so what
+//  * Consecutive ops that do not touch one another's outputs (no op's x,
+//    bias or y overlaps an earlier op's y, no op's y overlaps an earlier
+//    op's x) form a run.  A run of one-row ops of one format in the run
+//    kernel's layout -- plain, bias or gathered (the gathered ones sharing
+//    their flag words) -- takes one persistent launch per kGemvRunMaxOps ops
+//    (launch_gemv_run; the launch publishes once for all its gathered ops).
+//    Otherwise a run of ops that each take one streaming-GEMV launch goes
+//    back to back: the first waits for the kernel before the batch, the
+//    others read x at once, and a join launch closes the run, so what
 //    follows sees every y.
 // xs[i] / ys[i]: op i's device x and y.
 mlq_status run_ops(const mlq_linear_op* ops, int n, const float* const* xs, float* const* ys, cudaStream_t stream) {
@@ -555,19 +578,31 @@ mlq_status run_ops(const mlq_linear_op* ops, int n, const float* const* xs, floa
         }
         return true;
     };
+    // op i can join a run launch
+    auto run_member = [&](int i) {
+        const mlq_linear_op& o = ops[i];
+        if (o.rows != 1 || o.w_up) return false;
+        if (!o.gather && route_of(o.fmt, o.w, nullptr, o.out_features, o.in_features, xs[i], 1) != Route::kStream)
+            return false;
+        return mlq::gemv_run_ok(o.fmt, run_op_of(o, xs[i], ys[i]));
+    };
+    // op j's gather (if any) matches the gathers of ops [i, j)
+    auto run_compatible = [&](int i, int j) {
+        const mlq::GemvRunOp b = run_op_of(ops[j], xs[j], ys[j]);
+        for (int k = i; k < j; ++k)
+            if (!mlq::gemv_run_compatible(run_op_of(ops[k], xs[k], ys[k]), b)) return false;
+        return true;
+    };
     for (int i = 0; i < n;) {
-        // a run of independent one-launch GEMVs
+        // a run of independent one-row ops: one persistent launch per
+        // kGemvRunMaxOps ops
         int r = i;
-        if (one_gemv(i))
-            for (r = i + 1; r < n && one_gemv(r) && independent(i, r); ++r) {
+        if (run_member(i))
+            for (r = i + 1; r < n && run_member(r) && ops[r].fmt == ops[i].fmt && independent(i, r) &&
+                            run_compatible(i, r);
+                 ++r) {
             }
-        // ... one row of x each, one format, the run kernel's layout: one
-        // persistent launch per kGemvRunMaxOps ops
-        bool as_run = r - i >= 2;
-        for (int k = i; as_run && k < r; ++k)
-            as_run = ops[k].rows == 1 && !ops[k].w_up && ops[k].fmt == ops[i].fmt &&
-                     mlq::gemv_run_ok(ops[k].fmt, run_op_of(ops[k], xs[k], ys[k]));
-        if (as_run) {
+        if (r - i >= 2) {
             int dev = 0;
             cudaError_t e = cudaGetDevice(&dev);
             if (e != cudaSuccess) return fail_cuda("cudaGetDevice", e);
@@ -588,6 +623,11 @@ mlq_status run_ops(const mlq_linear_op* ops, int n, const float* const* xs, floa
             i = r;
             continue;
         }
+        // a run of independent one-launch GEMVs
+        r = i;
+        if (one_gemv(i))
+            for (r = i + 1; r < n && one_gemv(r) && independent(i, r); ++r) {
+            }
         if (r - i >= 2) {
             for (int k = i; k < r; ++k) {
                 Epilogue ep;

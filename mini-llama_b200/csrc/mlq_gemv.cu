@@ -1057,8 +1057,9 @@ __global__ void __launch_bounds__(threads_for(MT), MINB)
 constexpr int kRunThreads = 32 * (1 + kConsumerWarps);
 
 struct RunOpDev {
-    float* y;
-    const float* bias;
+    float* ys[kMaxWorld];  // row i goes to ys[d][row_offset + i], d < ny
+    const float* bias;     // [out] of this op's rows, or null
+    int ny, row_offset;
     int out;
     int ktiles;
     int unit0;  // this op's first row tile in the launch's queue order
@@ -1073,6 +1074,16 @@ struct RunArgs {
     unsigned int* tiles;     // queue {next, done}, or null: strided static tiles
     int nstages, nxslots;
     int* err;
+    // Sharded ops (done_counter not null): every CTA counts itself when its
+    // stores are done; the last one publishes `epoch` (the highest of the
+    // run's sharded ops) to every rank's flags, and with `wait` waits until
+    // every rank has published it here (the streaming GEMV's protocol).
+    int world, rank;
+    uint32_t* peer_flags[kMaxWorld];
+    uint32_t* local_flags;
+    unsigned int* done_counter;
+    uint32_t epoch;
+    int wait;
 };
 
 struct RunXprepArgs {
@@ -1119,6 +1130,7 @@ __global__ void __launch_bounds__(kRunThreads, 2)
     __shared__ __align__(8) uint64_t xfull_bar[kMaxStages];  // an x slot's tile landed
     __shared__ __align__(8) uint64_t xempty_bar[kMaxStages]; // ... and is consumed
     __shared__ int stage_unit[kMaxStages];                   // row tile of each stage (-1: end)
+    __shared__ __align__(8) uint64_t done_bar;                // consumer warps' stores issued
     __shared__ int abort_flag;
 
     const int warp = threadIdx.x >> 5;
@@ -1131,6 +1143,7 @@ __global__ void __launch_bounds__(kRunThreads, 2)
             mbar_init(smem_u32(&xfull_bar[s]), 1);
             mbar_init(smem_u32(&xempty_bar[s]), kConsumerWarps);
         }
+        mbar_init(smem_u32(&done_bar), kConsumerWarps);
         abort_flag = 0;
         fence_mbar_init();
     }
@@ -1257,6 +1270,9 @@ __global__ void __launch_bounds__(kRunThreads, 2)
         constexpr int LPR = 32 / C::NREG;
         soff[r] = (uint32_t)((lane / LPR) * C::REGION + (wc + r * kConsumerWarps) * C::BOXB + (lane % LPR) * C::GB);
     }
+    // The consumer loop; false when it gave up (a bounded wait ran out here
+    // or in another warp of the CTA).
+    auto consume = [&]() -> bool {
     int s = 0;
     uint32_t ph = 0, seq = 0;
     for (;;) {
@@ -1264,9 +1280,9 @@ __global__ void __launch_bounds__(kRunThreads, 2)
             report_error(a.err, 1);
             abort_flag = 1;
         }
-        if (*(volatile int*)&abort_flag) return;
+        if (*(volatile int*)&abort_flag) return false;
         const int u = *(volatile int*)&stage_unit[s];
-        if (u < 0) break;
+        if (u < 0) return true;
         const int o = op_of(u);
         const long long row0 = (long long)(u - a.op[o].unit0) * TR;
         const int nrows = (int)min((long long)TR, (long long)a.op[o].out - row0);
@@ -1279,7 +1295,7 @@ __global__ void __launch_bounds__(kRunThreads, 2)
                 report_error(a.err, 1);
                 abort_flag = 1;
             }
-            if (*(volatile int*)&abort_flag) return;
+            if (*(volatile int*)&abort_flag) return false;
             // 2-D boxes: bytes past a row's end and rows past the matrix
             // arrive as zeros (tensor-map bounds)
             const uint32_t stage = smem_base + (uint32_t)s * C::W_BYTES;
@@ -1295,7 +1311,7 @@ __global__ void __launch_bounds__(kRunThreads, 2)
                 report_error(a.err, 1);
                 abort_flag = 1;
             }
-            if (*(volatile int*)&abort_flag) return;
+            if (*(volatile int*)&abort_flag) return false;
             const uint32_t xs = x_base + xk * (uint32_t)C::XT_BYTES;
             int_ktile<F, RPW>(wv, xs, xs + C::X_BYTES + (uint32_t)lane * C::G * 8, xoff, tot);
             __syncwarp();
@@ -1313,7 +1329,49 @@ __global__ void __launch_bounds__(kRunThreads, 2)
             const long long row = row0 + i;
             const float* bias = a.op[o].bias;
             if (bias) v = __fadd_rn(v, bias[row]);
-            a.op[o].y[row] = v;
+            const long long off = a.op[o].row_offset + row;
+            for (int d = 0; d < a.op[o].ny; ++d) a.op[o].ys[d][off] = v;
+        }
+    }
+    };
+    const bool ok = consume();
+
+    if (a.done_counter) {
+        // Sharded ops in the run: the same completion protocol as a sharded
+        // streaming GEMV.  This CTA's stores (local and peer) happen before
+        // done_bar (CTA scope); the GPU-scope acquire-release count carries
+        // them to the last CTA, whose system-scope release fence publishes
+        // every CTA's stores ahead of the epoch flags.  A CTA that gave up
+        // counts with kDonePoison, and the launch then never publishes.
+        if (ok) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&done_bar));
+        }
+        if (threadIdx.x == 32) {
+            bool good = ok;
+            if (good && !mbar_wait(smem_u32(&done_bar), 0u)) {
+                report_error(a.err, 5);
+                good = false;
+            }
+            if (*(volatile int*)&abort_flag) good = false;
+            const unsigned int prev = atom_add_acq_rel_gpu(a.done_counter, good ? 1u : 1u + kDonePoison);
+            if ((prev & (kDonePoison - 1u)) == gridDim.x - 1) {
+                *a.done_counter = 0u;  // every CTA of this launch has counted
+                if (good && prev < kDonePoison) {
+                    fence_acq_rel_sys();
+                    for (int r = 0; r < a.world; ++r) st_relaxed_sys(a.peer_flags[r] + a.rank, a.epoch);
+                    const uint64_t t0 = global_ns();
+                    for (int r = 0; r < (a.wait ? a.world : 0); ++r) {
+                        while ((int)(ld_acquire_sys(a.local_flags + r) - a.epoch) < 0) {
+                            if (global_ns() - t0 > kWaitLimitNs) {
+                                report_error(a.err, 4);
+                                return;
+                            }
+                            __nanosleep(64);
+                        }
+                    }
+                }
+            }
         }
     }
 }
@@ -1580,20 +1638,46 @@ cudaError_t launch_run_t(const GemvRunOp* ops, int nop, void* ws, int sm_count, 
     WMaps<kGemvRunMaxOps> wm;
     std::memset(&wm, 0, sizeof(wm));
     int units = 0, xt = 0;
+    const GemvRunOp* sharded = nullptr;  // the run's first sharded op
     for (int k = 0; k < nop; ++k) {
         const GemvRunOp& op = ops[ord[k]];
         const long long row_bytes = (long long)((op.in + kQK - 1) / kQK) * Fmt<F>::kBlockBytes;
-        if (!make_map_2d(&wm.m[k], CU_TENSOR_MAP_DATA_TYPE_UINT64, const_cast<uint8_t*>(op.w),
+        if (op.out > 0 &&
+            !make_map_2d(&wm.m[k], CU_TENSOR_MAP_DATA_TYPE_UINT64, const_cast<uint8_t*>(op.w),
                          (uint64_t)(row_bytes / 8), (uint64_t)op.out, (uint64_t)row_bytes, (uint32_t)C::BOXW, 8u,
                          CU_TENSOR_MAP_SWIZZLE_NONE))
             return cudaErrorInvalidValue;
         const int kts = ktiles_of(F, op.in);
-        ra.op[k] = RunOpDev{op.y, op.bias, op.out, kts, units, xt};
+        RunOpDev& d = ra.op[k];
+        for (int r = 0; r < op.ny; ++r) d.ys[r] = op.y[r];
+        d.bias = op.bias;
+        d.ny = op.ny;
+        d.row_offset = op.row_offset;
+        d.out = op.out;
+        d.ktiles = kts;
+        d.unit0 = units;
+        d.xt0 = xt;
+        if (op.world > 1) {
+            if (sharded && !gemv_run_compatible(*sharded, op)) return cudaErrorInvalidValue;
+            if (!sharded) {
+                sharded = &op;
+                ra.epoch = op.epoch;
+            }
+            if ((int)(op.epoch - ra.epoch) > 0) ra.epoch = op.epoch;
+            ra.wait |= op.wait;
+        }
         xa.x[k] = op.x;
         xa.in[k] = op.in;
         xa.xt0[k] = xt;
         units += (op.out + C::RT - 1) / C::RT;
         xt += kts;
+    }
+    if (sharded) {
+        ra.world = sharded->world;
+        ra.rank = sharded->rank;
+        for (int r = 0; r < sharded->world; ++r) ra.peer_flags[r] = sharded->flags[r];
+        ra.local_flags = sharded->flags[sharded->rank];
+        ra.done_counter = sharded->done_counter;
     }
     ra.nop = xa.nop = nop;
     ra.units = units;
@@ -1625,6 +1709,7 @@ cudaError_t launch_run_t(const GemvRunOp* ops, int nop, void* ws, int sm_count, 
     }
     int grid = 2 * sm_count;
     if (grid > units) grid = units;
+    if (grid < 1) grid = 1;  // a rank holding no rows still runs the handshake
     ra.tiles = tile_queue(dev, stream);  // null while capturing: strided static tiles
 
     cudaLaunchAttribute attr[1];
@@ -1652,11 +1737,22 @@ cudaError_t launch_run_t(const GemvRunOp* ops, int nop, void* ws, int sm_count, 
 
 bool gemv_run_ok(int fmt, const GemvRunOp& op) {
     if (fmt != kQ8_0 && fmt != kQ4_0 && fmt != kQ4_1) return false;
-    if (op.out < 1 || op.in < 1 || !op.w || !op.x || !op.y) return false;
+    if (op.out < 0 || (op.out == 0 && op.world <= 1) || op.in < 1 || (op.out > 0 && !op.w) || !op.x) return false;
+    if (op.ny < 1 || op.ny > kMaxWorld || (op.world > 1 && (op.ny != op.world || !op.done_counter))) return false;
+    for (int d = 0; d < op.ny; ++d)
+        if (!op.y[d]) return false;
     const int bpr = (op.in + kQK - 1) / kQK;
     const long long row_bytes = (long long)bpr * block_bytes(fmt);
     return reinterpret_cast<uintptr_t>(op.w) % 16 == 0 && reinterpret_cast<uintptr_t>(op.x) % 16 == 0 &&
            row_bytes % 16 == 0 && bpr % (fmt == kQ4_1 ? 1 : 2) == 0 && op.in % 4 == 0 && encode_fn() != nullptr;
+}
+
+bool gemv_run_compatible(const GemvRunOp& a, const GemvRunOp& b) {
+    if (a.world <= 1 || b.world <= 1) return true;
+    if (a.world != b.world || a.rank != b.rank || a.done_counter != b.done_counter) return false;
+    for (int r = 0; r < a.world; ++r)
+        if (a.flags[r] != b.flags[r]) return false;
+    return true;
 }
 
 size_t gemv_run_workspace_bytes(int fmt, const GemvRunOp* ops, int nop) {

@@ -68,17 +68,30 @@ cudaError_t launch_gemv_stream(int fmt, const GemvArgs& args, int mt, int sm_cou
 // start-up.  All ops of a run share the format.
 constexpr int kGemvRunMaxOps = 8;
 struct GemvRunOp {
-    const uint8_t* w;
+    const uint8_t* w;    // the op's `out` rows (null allowed when out == 0)
     const float* x;      // [in], one row
-    float* y;            // [out]
-    const float* bias;   // [out] or null
+    const float* bias;   // [out] (the op's rows) or null
     int out, in;
+    // Where the rows go: y[d][row_offset + i] for d < ny.  A plain op: ny 1,
+    // row_offset 0.  A row-sharded op (world > 1): every rank's y (ny =
+    // world, this rank's at index rank), after which the launch publishes
+    // epoch to every rank's flags (the streaming GEMV's sharded protocol).
+    float* y[kMaxWorld];
+    int ny, row_offset;
+    int world, rank;
+    uint32_t* flags[kMaxWorld];  // every rank's flag words (world > 1)
+    unsigned int* done_counter;  // this rank's CTA completion counter (world > 1)
+    uint32_t epoch;
+    int wait;                    // 1: wait for every rank after publishing
 };
 
 // True when an op can join a run: one row of x, weights and x 16-B aligned
 // with a 16-B multiple row pitch (2-D tensor map), whole lane-groups per
-// row, in % 4 == 0, and the driver's tensor-map encoder reachable.
+// row, in % 4 == 0, and the driver's tensor-map encoder reachable.  The
+// sharded ops of one run must share world, rank and flag words
+// (gemv_run_compatible).
 bool gemv_run_ok(int fmt, const GemvRunOp& op);
+bool gemv_run_compatible(const GemvRunOp& a, const GemvRunOp& b);
 
 // Workspace of a run: the sliced x tiles of every op.
 size_t gemv_run_workspace_bytes(int fmt, const GemvRunOp* ops, int nop);

@@ -167,7 +167,11 @@ class StepPlan:
     ahead never writes a y that a slower peer may still be reading.
     """
 
-    def __init__(self, matrices, world: int, rank: int, shard=()):
+    def __init__(self, matrices, world: int, rank: int, shard=(), epoch0: int = 0):
+        """epoch0: the last epoch already published on the flag words these
+        calls use (a plan that follows another on the same flags continues
+        its sequence; a restarted sequence would find its waits satisfied by
+        the older, higher epochs)."""
         self.matrices = list(matrices)
         self.world, self.rank = world, rank
         self.place, self.ranges = {}, {}
@@ -182,7 +186,7 @@ class StepPlan:
                 self.place[name] = "local0"
                 self.ranges[name] = shard_rows(out_f, world, owners=[0])
         self.sharded = [n for n, _, _ in self.matrices if self.place[n] == "shard"]
-        self.epoch = 0
+        self.epoch = epoch0
         self.calls = {n: 0 for n in self.sharded}
 
     def rows(self, name):

@@ -8,7 +8,8 @@ wait, then mlq_gather_wait), and checks the FULL y on its own GPU
 against the CPU oracle: every row for matrices up to 8192 rows, otherwise a
 sample of rows that includes every shard's first and last row.  The cases
 include the BASELINE config-5 shapes (Llama-3-70B lm_head 128256x8192 and
-gate 28672x8192, q4_0, batch 1 and 8)."""
+gate 28672x8192, q4_0, batch 1 and 8).  A last phase runs three sharded
+matrices and a local one as one batch (one persistent run launch per rank)."""
 from __future__ import annotations
 
 import importlib
@@ -48,6 +49,64 @@ def sample_rows(out_f, ranges):
         if e > b:
             rows.update((b, e - 1))
     return np.array(sorted(rows))
+
+
+def run_phase(mlq, orc, group, flags, rank, world, dev, stream, epoch):
+    """A batch the library runs as one persistent launch: three row-sharded
+    one-row q4_0 matrices (deferred gathers sharing the flag words) and one
+    local matrix, then one mlq_gather_wait for the highest epoch; three
+    steps, every full y checked on this rank against the oracle."""
+    fmt = "q4_0"
+    mats = [(4608, 3584), (18944, 3584), (3584, 18944)]
+    lins, shards, blocks, checks = [], [], [], []
+    for k, (out_f, in_f) in enumerate(mats):
+        seed = 300 + k
+        ranges = sh.shard_rows(out_f, world)
+        b, e = ranges[rank]
+        w32 = pkg.synth.normal_torch((e - b, in_f), seed=seed, std=0.02, device=dev, offset=b * in_f)
+        shards.append(mlq.quantize(fmt, w32))
+        del w32
+        check = sample_rows(out_f, ranges)
+        wrows = np.concatenate([pkg.synth.normal_torch((1, in_f), seed=seed, std=0.02,
+                                                       offset=int(r) * in_f).numpy() for r in check])
+        blocks.append(orc.quantize(fmt, wrows))
+        checks.append(check)
+        lins.append(sh.ShardedLinear(mlq, fmt, out_f, in_f, 1, ranges, rank, group, flags))
+    lblocks = orc.quantize(fmt, pkg.synth.normal((1024, 3584), seed=310, std=0.02))
+    lw = torch.from_numpy(lblocks).to(dev)
+    ly = torch.empty((1, 1024), device=dev)
+    worst = 0.0
+    for it in range(3):
+        xs = [pkg.synth.normal((1, in_f), seed=5000 + 10 * it + k) for k, (_, in_f) in enumerate(mats)]
+        xl = pkg.synth.normal((1, 3584), seed=5100 + it)
+        xds = [torch.from_numpy(x).to(dev) for x in xs]
+        xld = torch.from_numpy(xl).to(dev)
+        ops, gs, yptrs = [], [], []
+        for k, lin in enumerate(lins):
+            epoch += 1
+            yb = lin.ybuf[epoch & 1]
+            g = mlq.make_gather(world, rank, lin.begin, lin.end, yb.peers, flags.peers, epoch=epoch,
+                                defer_wait=True)
+            gs.append(g)
+            yptrs.append(yb.local)
+            ops.append(mlq.linear_op(fmt, shards[k].data_ptr(), lin.out, lin.inp, xds[k].data_ptr(), 1, yb.local,
+                                     gather=g))
+        ops.append(mlq.linear_op(fmt, lw.data_ptr(), 1024, 3584, xld.data_ptr(), 1, ly.data_ptr()))
+        mlq.Batch(ops).run(stream)
+        mlq.gather_wait(gs[-1], stream)
+        torch.cuda.synchronize()
+        for k, (out_f, in_f) in enumerate(mats):
+            y = sh.device_view(yptrs[k], (1, out_f)).cpu().numpy()[:, checks[k]]
+            ref = orc.linear(fmt, xs[k], blocks[k], len(checks[k]))
+            err = (np.linalg.norm(y - ref, axis=1) / np.linalg.norm(ref, axis=1)).max()
+            worst = max(worst, err)
+            assert err <= 1e-3, (rank, "run", k, it, err)
+        ref = orc.linear(fmt, xl, lblocks, 1024)
+        err = (np.linalg.norm(ly.cpu().numpy() - ref, axis=1) / np.linalg.norm(ref, axis=1)).max()
+        worst = max(worst, err)
+        assert err <= 1e-3, (rank, "run local", it, err)
+        dist.barrier()
+    return epoch, worst
 
 
 def main():
@@ -94,6 +153,8 @@ def main():
         del shard
         torch.cuda.empty_cache()
         dist.barrier()
+    epoch, w_run = run_phase(mlq, orc, group, flags, rank, world, dev, stream, epoch)
+    worst = max(worst, w_run)
     code = mlq.device_error(local)
     assert code == 0, code
     dist.barrier()

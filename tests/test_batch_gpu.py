@@ -7,6 +7,8 @@ relative L2 1e-3 per output vector.  The host form moves x and y itself
 and synchronises once; its y must equal the device batch's."""
 from __future__ import annotations
 
+import ctypes
+
 import numpy as np
 import pytest
 
@@ -304,4 +306,33 @@ def test_batch_run_in_a_cuda_graph(pkg, oracle):
             torch.cuda.synchronize()
             np.testing.assert_array_equal(y.cpu().numpy(), yd.cpu().numpy(), err_msg=f"replay {it} op {k}")
     del g
+    assert mlq.device_error(0) == 0
+
+
+def test_batch_run_with_gathered_ops_in_a_world_of_one(pkg, oracle):
+    """Gathered one-row ops (a world of one; one with a deferred wait, one
+    with a bias) join a run with plain ops: every y bit for bit as the op
+    run alone, and within the contract of the oracle."""
+    mlq = pkg.mlq
+    fmt = "q8_0"
+    shapes = [(2048, 4096), (1000, 2048), (4096, 1024), (512, 4096)]
+    keep, xds, ops, outs, singles, refs = _run_case(pkg, oracle, fmt, shapes, bias_at=(3,), seed=1700)
+    flags = torch.zeros(mlq.flag_bytes() // 4, dtype=torch.int32, device="cuda")
+    gathers = []
+    for k in (1, 3):
+        out_f = shapes[k][0]
+        g = mlq.make_gather(1, 0, 0, out_f, [outs[k].data_ptr()], [flags.data_ptr()], epoch=1,
+                            defer_wait=(k == 1))
+        gathers.append(g)
+        op = mlq.LinearOp.from_buffer_copy(ops[k])
+        op.gather = ctypes.addressof(g)
+        op.block_count = mlq.blocks_per_row(shapes[k][1]) * out_f
+        ops[k] = op
+    pkg.mlq.Batch(ops).run(torch.cuda.current_stream().cuda_stream)
+    mlq.gather_wait(gathers[0], torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    for k, (y, one, ref) in enumerate(zip(outs, singles, refs)):
+        yn = y.cpu().numpy()
+        np.testing.assert_array_equal(yn, one.cpu().numpy(), err_msg=f"op {k}")
+        assert rel_l2_rows(yn, ref).max() <= TOL, k
     assert mlq.device_error(0) == 0

@@ -140,6 +140,9 @@ def _plan_worker(rank, world, port, q):
            "steps": steps, "singles": singles, "after": after,
            "y": [[slab.peer_ptrs(p, k) for k in range(len(plan.sharded))] for p in (0, 1)],
            "local": [slab.local_ptr(p, 0) for p in (0, 1)]}
+    # a later plan on the same flag words continues the epoch sequence
+    nxt = sh.StepPlan(mats, world, rank, shard={"gate", "lm_head"}, epoch0=plan.epoch)
+    res["next_plan"] = (plan.epoch, nxt.next_step())
     plan.calls["gate"] += 1  # unequal call counts cannot form a step
     try:
         plan.next_step()
@@ -173,6 +176,8 @@ def test_step_plan_gloo():
     # three steps of four sharded calls: epochs 1..12, parities 0, 1, 0
     assert r0["steps"] == r1["steps"]
     assert [p for p, _ in r0["steps"]] == [0, 1, 0]
+    last, (par, eps) = r0["next_plan"]
+    assert r0["next_plan"] == r1["next_plan"] and par == 0 and eps == [last + 1, last + 2]
     assert [e for _, es in r0["steps"] for e in es] == list(range(1, 13))
     assert r0["singles"] == r1["singles"] == [(13, 1), (14, 1), (15, 1), (16, 1)]
     assert r0["after"] == r1["after"] == (0, [17, 18, 19, 20])
