@@ -21,9 +21,10 @@
  *     is what the reference launches on).  Device-side entry points are
  *     asynchronous on that stream; *_host entry points are synchronous.
  *   - The current CUDA device must own every device pointer passed.
- *   - Ordering with the previous kernel on the stream: the streaming GEMV and
- *     the batched-decode GEMM (its x split and the GEMM) are launched with
- *     programmatic dependent launch, so they may start while the kernel
+ *   - Ordering with the previous kernel on the stream: the streaming GEMV,
+ *     the batched-decode GEMM (its x split and the GEMM) and a batch's run
+ *     launch (its x slicing and the run kernel, see mlq_linear_batch) are
+ *     launched with programmatic dependent launch, so they may start while the kernel
  *     before them on the stream is still running.  They read x and the bias,
  *     and write y and their workspace, only after that kernel has completed;
  *     they stream the WEIGHTS before.  So the weights must be complete before
@@ -362,7 +363,21 @@ typedef struct mlq_linear_op {
 /* Launches ops[0..n) in order on `stream`; asynchronous.  Every op is
  * validated (as mlq_linear / mlq_linear_bias / mlq_linear_swiglu /
  * mlq_linear_allgather) before the first launch, so a batch with a bad op
- * launches nothing.  A gathered op takes no w_up. */
+ * launches nothing.  A gathered op takes no w_up.
+ *
+ * Consecutive ops that do not touch one another's outputs (no op's x, bias
+ * or y overlaps an earlier one's y, no y overlaps an earlier x) and take
+ * one row of x each -- one format, weights and x 16-byte aligned, a row
+ * pitch that is a multiple of 16 bytes, in_features % 4 == 0, plain, bias
+ * or gathered -- form a run: one persistent launch per
+ * MLQ_BATCH_RUN_MAX_OPS ops (after one small launch that slices every op's
+ * x), so the ops share the SMs instead of each paying a launch's start-up.
+ * Each y equals the op run alone, bit for bit.  The gathered ops of a run
+ * must share their flag arrays (world, rank, peer_flags); the launch
+ * publishes once, when all its ops are done, the highest epoch among them.
+ * A run uses the stream's workspace (grown on first use: make the first
+ * call of the largest batch before capturing the stream in a graph). */
+#define MLQ_BATCH_RUN_MAX_OPS 8
 MLQ_API mlq_status mlq_linear_batch(const mlq_linear_op* ops, int n, mlq_stream stream);
 
 /* mlq_linear_batch with HOST x and y (weights and bias on the device):

@@ -66,7 +66,7 @@ cudaError_t launch_gemv_stream(int fmt, const GemvArgs& args, int mt, int sm_cou
 // small launch that slices every op's x once into the workspace): one
 // tile queue over all ops' row tiles, so the ops do not each pay a launch's
 // start-up.  All ops of a run share the format.
-constexpr int kGemvRunMaxOps = 8;
+constexpr int kGemvRunMaxOps = MLQ_BATCH_RUN_MAX_OPS;
 struct GemvRunOp {
     const uint8_t* w;    // the op's `out` rows (null allowed when out == 0)
     const float* x;      // [in], one row

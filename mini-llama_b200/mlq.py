@@ -231,7 +231,7 @@ def takes_gemm(rows: int, out_features: int, in_features: int) -> bool:
                                       and out_features * in_features >= GEMM_LARGE_MIN_WEIGHTS)
 
 
-RUN_MAX_OPS = 8  # ops per persistent launch of a run (mlq_linear_batch)
+RUN_MAX_OPS = 8  # MLQ_BATCH_RUN_MAX_OPS: ops per persistent launch of a run (mlq_linear_batch)
 
 
 def joins_run(fmt, rows: int, in_features: int) -> bool:

@@ -139,8 +139,9 @@ def test_gemm_routing_rule_matches_header(pkg, tmp_path):
               (152064, 3584)]
     src = tmp_path / "rule.c"
     lines = ['#include <stdio.h>', '#include "mlq.h"', "int main(void) {",
-             '  printf("%d %d %lld\\n", MLQ_GEMM_MIN_ROWS, MLQ_GEMM_LARGE_MIN_ROWS, '
-             "(long long)MLQ_GEMM_LARGE_MIN_WEIGHTS);"]
+             '  printf("%d %d %lld %d %d %d\\n", MLQ_GEMM_MIN_ROWS, MLQ_GEMM_LARGE_MIN_ROWS, '
+             "(long long)MLQ_GEMM_LARGE_MIN_WEIGHTS, MLQ_BGEMM_MIN_ROWS, MLQ_BGEMM_MAX_ROWS, "
+             "MLQ_BATCH_RUN_MAX_OPS);"]
     for r in rows:
         for o, i in shapes:
             lines.append(f'  printf("%d\\n", (int)(MLQ_GEMM_ROWS_RULE({r}, {o}, {i})));')
@@ -150,7 +151,8 @@ def test_gemm_routing_rule_matches_header(pkg, tmp_path):
     subprocess.run([gcc, "-std=c99", "-I", str(ROOT / "include"), str(src), "-o", str(exe)], check=True)
     out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split("\n")
     mlq = pkg.mlq
-    assert out[0].split() == [str(mlq.GEMM_MIN_ROWS), str(mlq.GEMM_LARGE_MIN_ROWS), str(mlq.GEMM_LARGE_MIN_WEIGHTS)]
+    assert out[0].split() == [str(v) for v in (mlq.GEMM_MIN_ROWS, mlq.GEMM_LARGE_MIN_ROWS, mlq.GEMM_LARGE_MIN_WEIGHTS,
+                                               mlq.BGEMM_MIN_ROWS, mlq.BGEMM_MAX_ROWS, mlq.RUN_MAX_OPS)]
     got = [int(v) for v in out[1:] if v.strip()]
     want = [int(mlq.takes_gemm(r, o, i)) for r in rows for o, i in shapes]
     assert got == want
