@@ -329,7 +329,8 @@ MLQ_API size_t mlq_flag_bytes(void);
  * pays one cross-rank wait instead of one per product.  Each rank's epochs
  * must rise from op to op on one flag array: a wait for epoch E then also
  * covers every earlier epoch of that array.  mlq_linear_batch_host waits
- * before it copies the y of a deferred op back. */
+ * before it copies the y of a deferred op back: once per flag array, for
+ * the highest epoch among its deferred ops. */
 typedef struct mlq_gather {
     int world_size, rank;
     int row_begin, row_end;

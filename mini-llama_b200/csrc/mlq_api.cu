@@ -1106,10 +1106,25 @@ MLQ_API mlq_status mlq_linear_batch_host(const mlq_linear_op* ops, int n, int de
         }
         st = run_ops(ops, n, xd.data(), yd.data(), s);
         if (st != MLQ_OK) return st;
-        // deferred sharded ops: every rank's rows in y before it is copied back
-        for (int i = 0; i < n; ++i)
-            if (ops[i].gather && ops[i].gather->defer_wait && (st = run_gather_wait(*ops[i].gather, s)) != MLQ_OK)
-                return st;
+        // deferred sharded ops: every rank's rows in y before it is copied
+        // back.  One wait per flag array (this rank's flag words), for the
+        // highest epoch among its ops: epochs rise from op to op on one
+        // array, so that wait covers the others.
+        std::vector<mlq_gather> waits;
+        for (int i = 0; i < n; ++i) {
+            if (!ops[i].gather || !ops[i].gather->defer_wait) continue;
+            const mlq_gather& g = *ops[i].gather;
+            bool merged = false;
+            for (mlq_gather& w : waits)
+                if (w.world_size == g.world_size && w.peer_flags[w.rank] == g.peer_flags[g.rank]) {
+                    if ((int)(g.epoch - w.epoch) > 0) w.epoch = g.epoch;
+                    merged = true;
+                    break;
+                }
+            if (!merged) waits.push_back(g);
+        }
+        for (const mlq_gather& w : waits)
+            if ((st = run_gather_wait(w, s)) != MLQ_OK) return st;
         std::vector<Copy> downs;
         for (int i = 0; i < n; ++i) {
             // a gathered op's full y is this rank's peer_y entry
