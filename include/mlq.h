@@ -29,9 +29,10 @@
  *     and write y and their workspace, only after that kernel has completed;
  *     they stream the WEIGHTS before.  So the weights must be complete before
  *     the stream's previous kernel started, whenever that kernel lets its
- *     dependents start early (this library's GEMV and batched-decode GEMM
- *     do; its quantizer and the other kernels here do not, so a quantize
- *     followed by a linear on one stream is ordered).
+ *     dependents start early (this library's GEMV, batched-decode GEMM, run
+ *     launches and mlq_gather_wait's kernel do; its quantizer and the other
+ *     kernels here do not, so a quantize followed by a linear on one stream
+ *     is ordered).
  */
 #ifndef MLQ_H_
 #define MLQ_H_

@@ -1831,6 +1831,10 @@ namespace {
 // The deferred half of a sharded call's handshake (one thread): every
 // rank's epoch word here at least `epoch`, bounded as the in-kernel wait.
 __global__ void gather_wait_kernel(const uint32_t* flags, int world, uint32_t epoch, int* err) {
+    // the next kernel (a GEMV, batched-decode or run launch of the next
+    // step) may start streaming its weights; it reads x and writes y only
+    // after this kernel has completed (griddepcontrol.wait)
+    launch_dependents();
     if (threadIdx.x != 0) return;
     const uint64_t t0 = global_ns();
     for (int r = 0; r < world; ++r) {
