@@ -52,21 +52,25 @@ def sample_rows(out_f, ranges):
 
 
 def run_phase(mlq, orc, group, flags, rank, world, dev, stream, epoch):
-    """A batch the library runs as one persistent launch: three row-sharded
-    one-row q4_0 matrices (deferred gathers sharing the flag words) and one
-    local matrix, then one mlq_gather_wait for the highest epoch; three
-    steps, every full y checked on this rank against the oracle."""
+    """A batch the library runs as one persistent launch: four row-sharded
+    one-row q4_0 matrices (deferred gathers sharing the flag words; the last
+    one's rows all on rank 0, so every other rank's op has an empty shard)
+    and one local matrix, then one mlq_gather_wait for the highest epoch;
+    three steps, every full y checked on this rank against the oracle."""
     fmt = "q4_0"
-    mats = [(4608, 3584), (18944, 3584), (3584, 18944)]
+    mats = [(4608, 3584, None), (18944, 3584, None), (3584, 18944, None), (1024, 3584, [0])]
     lins, shards, blocks, checks = [], [], [], []
-    for k, (out_f, in_f) in enumerate(mats):
+    for k, (out_f, in_f, owners) in enumerate(mats):
         seed = 300 + k
-        ranges = sh.shard_rows(out_f, world)
+        ranges = sh.shard_rows(out_f, world, owners=owners)
         b, e = ranges[rank]
-        w32 = pkg.synth.normal_torch((e - b, in_f), seed=seed, std=0.02, device=dev, offset=b * in_f)
-        shards.append(mlq.quantize(fmt, w32))
-        del w32
-        check = sample_rows(out_f, ranges)
+        shard = None
+        if e > b:
+            w32 = pkg.synth.normal_torch((e - b, in_f), seed=seed, std=0.02, device=dev, offset=b * in_f)
+            shard = mlq.quantize(fmt, w32)
+            del w32
+        shards.append(shard)
+        check = sample_rows(out_f, [rg for rg in ranges if rg[1] > rg[0]])
         wrows = np.concatenate([pkg.synth.normal_torch((1, in_f), seed=seed, std=0.02,
                                                        offset=int(r) * in_f).numpy() for r in check])
         blocks.append(orc.quantize(fmt, wrows))
@@ -77,7 +81,7 @@ def run_phase(mlq, orc, group, flags, rank, world, dev, stream, epoch):
     ly = torch.empty((1, 1024), device=dev)
     worst = 0.0
     for it in range(3):
-        xs = [pkg.synth.normal((1, in_f), seed=5000 + 10 * it + k) for k, (_, in_f) in enumerate(mats)]
+        xs = [pkg.synth.normal((1, in_f), seed=5000 + 10 * it + k) for k, (_, in_f, _) in enumerate(mats)]
         xl = pkg.synth.normal((1, 3584), seed=5100 + it)
         xds = [torch.from_numpy(x).to(dev) for x in xs]
         xld = torch.from_numpy(xl).to(dev)
@@ -89,13 +93,13 @@ def run_phase(mlq, orc, group, flags, rank, world, dev, stream, epoch):
                                 defer_wait=True)
             gs.append(g)
             yptrs.append(yb.local)
-            ops.append(mlq.linear_op(fmt, shards[k].data_ptr(), lin.out, lin.inp, xds[k].data_ptr(), 1, yb.local,
-                                     gather=g))
+            wp = shards[k].data_ptr() if shards[k] is not None else 0
+            ops.append(mlq.linear_op(fmt, wp, lin.out, lin.inp, xds[k].data_ptr(), 1, yb.local, gather=g))
         ops.append(mlq.linear_op(fmt, lw.data_ptr(), 1024, 3584, xld.data_ptr(), 1, ly.data_ptr()))
         mlq.Batch(ops).run(stream)
         mlq.gather_wait(gs[-1], stream)
         torch.cuda.synchronize()
-        for k, (out_f, in_f) in enumerate(mats):
+        for k, (out_f, in_f, _) in enumerate(mats):
             y = sh.device_view(yptrs[k], (1, out_f)).cpu().numpy()[:, checks[k]]
             ref = orc.linear(fmt, xs[k], blocks[k], len(checks[k]))
             err = (np.linalg.norm(y - ref, axis=1) / np.linalg.norm(ref, axis=1)).max()
