@@ -388,8 +388,11 @@ MLQ_API mlq_status mlq_linear_batch(const mlq_linear_op* ops, int n, mlq_stream 
  * host buffers the copies are asynchronous DMA.  Ops with the same host x
  * share one upload; consecutive ops whose host x (or y) buffers follow on
  * directly (one pinned buffer, laid out in op order, each x and y a
- * multiple of 256 bytes) share one copy.  Calls on one device are
- * serialised (the staging is per device). */
+ * multiple of 256 bytes) share one copy.  When the y to download is large
+ * (>= 256 KB), the last rows of the largest plain one-row op run as a
+ * second launch while every other y is copied back on an internal stream
+ * (each y is the same, bit for bit).  Calls on one device are serialised
+ * (the staging is per device). */
 MLQ_API mlq_status mlq_linear_batch_host(const mlq_linear_op* ops, int n, int device,
                                          mlq_stream stream);
 

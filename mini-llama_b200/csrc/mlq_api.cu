@@ -69,6 +69,11 @@ struct DeviceState {
     float* x_stage = nullptr;
     float* y_stage = nullptr;
     size_t x_cap = 0, y_cap = 0;
+    // mlq_linear_batch_host's download stream and its two events (created
+    // on first use, kept): the y of a step's first part is copied back here
+    // while the last rows of its largest product compute
+    cudaStream_t copy_stream = nullptr;
+    cudaEvent_t part_done = nullptr, copies_done = nullptr;
 };
 
 DeviceState g_dev[kMaxDevices];
@@ -1034,6 +1039,14 @@ MLQ_API mlq_status mlq_linear_batch(const mlq_linear_op* ops, int n, mlq_stream 
     }
 }
 
+// mlq_linear_batch_host splits a step when its y download is at least
+// kSplitMinDownload bytes and a plain one-row op has at least kSplitMinRows
+// rows; kHbmOverPcie is the ratio of weight-streaming to download speed it
+// assumes when sizing the second part (B200 HBM against a PCIe Gen5 link).
+constexpr size_t kSplitMinDownload = 256 * 1024;
+constexpr int kSplitMinRows = 4096;
+constexpr double kHbmOverPcie = 128.0;
+
 MLQ_API mlq_status mlq_linear_batch_host(const mlq_linear_op* ops, int n, int device, mlq_stream stream) {
     try {
         if (n < 0) return fail(MLQ_ERR_EMPTY, "mlq_linear_batch_host: negative op count");
@@ -1104,7 +1117,43 @@ MLQ_API mlq_status mlq_linear_batch_host(const mlq_linear_op* ops, int n, int de
             xd[i] = reinterpret_cast<const float*>(xs + xo[i]);
             yd[i] = reinterpret_cast<float*>(ys + yo[i]);
         }
-        st = run_ops(ops, n, xd.data(), yd.data(), s);
+        // A large download overlaps the step's last compute: the rows
+        // [split_row, out) of the largest plain one-row op run as a second
+        // launch, and every other y range is copied back on the download
+        // stream while they compute.  Each row's arithmetic is the same.
+        int split_op = -1, split_row = 0;
+        {
+            size_t ybytes = 0;
+            for (int i = 0; i < n; ++i) ybytes += (size_t)ops[i].rows * ops[i].out_features * sizeof(float);
+            for (int i = 0; i < n; ++i)
+                if (!ops[i].gather && !ops[i].w_up && ops[i].rows == 1 && ops[i].out_features >= kSplitMinRows &&
+                    (split_op < 0 || ops[i].out_features > ops[split_op].out_features))
+                    split_op = i;
+            if (ybytes < kSplitMinDownload) split_op = -1;
+            if (split_op >= 0) {
+                // the second part's weights take about as long to stream as
+                // the first part's y to copy back (HBM ~kHbmOverPcie x PCIe)
+                const mlq_linear_op& o = ops[split_op];
+                const double wrow = (double)mlq_block_count(1, o.in_features) * mlq::block_bytes(o.fmt);
+                const double rows_b = kHbmOverPcie * (double)ybytes / (wrow + kHbmOverPcie * sizeof(float));
+                // (an op too small to hide the download is not split)
+                const int rb = (int)rows_b / 256 * 256;
+                if (rb < 256 || rb > o.out_features - 256) split_op = -1;
+                else split_row = o.out_features - rb;
+            }
+            if (split_op >= 0 && !ds->copy_stream) {
+                e = cudaStreamCreateWithFlags(&ds->copy_stream, cudaStreamNonBlocking);
+                if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ds->part_done, cudaEventDisableTiming);
+                if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ds->copies_done, cudaEventDisableTiming);
+                if (e != cudaSuccess) return fail_cuda("download stream setup", e);
+            }
+        }
+        std::vector<mlq_linear_op> ops_a(ops, ops + n);
+        if (split_op >= 0) {
+            ops_a[split_op].out_features = split_row;
+            ops_a[split_op].block_count = mlq_block_count(split_row, ops[split_op].in_features);
+        }
+        st = run_ops(ops_a.data(), n, xd.data(), yd.data(), s);
         if (st != MLQ_OK) return st;
         // deferred sharded ops: every rank's rows in y before it is copied
         // back.  One wait per flag array (this rank's flag words), for the
@@ -1130,11 +1179,37 @@ MLQ_API mlq_status mlq_linear_batch_host(const mlq_linear_op* ops, int n, int de
             // a gathered op's full y is this rank's peer_y entry
             const void* src = ops[i].gather ? static_cast<const void*>(ops[i].gather->peer_y[ops[i].gather->rank])
                                             : static_cast<const void*>(ys + yo[i]);
-            add(downs, ops[i].y, src, (size_t)ops[i].rows * ops[i].out_features * sizeof(float));
+            add(downs, ops[i].y, src, (size_t)ops[i].rows * ops_a[i].out_features * sizeof(float));
+        }
+        cudaStream_t ds_s = s;  // where the first part's y goes back
+        if (split_op >= 0) {
+            // the first part done: its y back on the download stream while
+            // the second part computes on `s`
+            e = cudaEventRecord(ds->part_done, s);
+            if (e == cudaSuccess) e = cudaStreamWaitEvent(ds->copy_stream, ds->part_done, 0);
+            if (e != cudaSuccess) return fail_cuda("download stream order", e);
+            ds_s = ds->copy_stream;
         }
         for (size_t k = 0; k < downs.size() && e == cudaSuccess; ++k)
-            e = cudaMemcpyAsync(downs[k].dst, downs[k].src, downs[k].bytes, cudaMemcpyDeviceToHost, s);
+            e = cudaMemcpyAsync(downs[k].dst, downs[k].src, downs[k].bytes, cudaMemcpyDeviceToHost, ds_s);
         if (e != cudaSuccess) return fail_cuda("cudaMemcpyAsync (y download)", e);
+        if (split_op >= 0) {
+            const mlq_linear_op& o = ops[split_op];
+            const size_t row_bytes = mlq_block_count(1, o.in_features) * mlq::block_bytes(o.fmt);
+            mlq_linear_op b = o;
+            b.w = static_cast<const uint8_t*>(o.w) + (size_t)split_row * row_bytes;
+            b.out_features = o.out_features - split_row;
+            b.block_count = mlq_block_count(b.out_features, o.in_features);
+            b.bias = o.bias ? o.bias + split_row : nullptr;
+            const float* xb = xd[split_op];
+            float* yb = yd[split_op] + split_row;
+            st = run_ops(&b, 1, &xb, &yb, s);
+            if (st != MLQ_OK) return st;
+            e = cudaMemcpyAsync(o.y + split_row, yb, (size_t)b.out_features * sizeof(float), cudaMemcpyDeviceToHost, s);
+            if (e == cudaSuccess) e = cudaEventRecord(ds->copies_done, ds->copy_stream);
+            if (e == cudaSuccess) e = cudaStreamWaitEvent(s, ds->copies_done, 0);
+            if (e != cudaSuccess) return fail_cuda("cudaMemcpyAsync (y download, last part)", e);
+        }
         e = cudaStreamSynchronize(s);
         if (e != cudaSuccess) return fail_cuda("cudaStreamSynchronize", e);
         return MLQ_OK;

@@ -336,3 +336,44 @@ def test_batch_run_with_gathered_ops_in_a_world_of_one(pkg, oracle):
         np.testing.assert_array_equal(yn, one.cpu().numpy(), err_msg=f"op {k}")
         assert rel_l2_rows(yn, ref).max() <= TOL, k
     assert mlq.device_error(0) == 0
+
+
+def test_batch_host_overlaps_the_download(pkg, oracle):
+    """A host batch whose y download is large (here 401 KB): the largest
+    plain one-row op's last rows run as a second launch while the rest of
+    y is copied back.  Every y equals the device batch's bit for bit (each
+    row's arithmetic is the same), twice in a row, and the big op's rows on
+    both sides of the split match the oracle."""
+    mlq = pkg.mlq
+    specs = [("q8_0", 2048, 4096), ("q4_0", 98304, 1024)]
+    keep, dev_ops, host_ops, hx, hy, refs = [], [], [], [], [], []
+    for k, (fmt, out_f, in_f) in enumerate(specs):
+        wb = oracle.quantize(fmt, pkg.synth.normal((out_f, in_f), seed=1800 + k, std=0.02))
+        w = dev(wb)
+        x = torch.from_numpy(pkg.synth.normal((1, in_f), seed=1900 + k)).pin_memory()
+        yh = torch.full((1, out_f), float("nan")).pin_memory()
+        xd = x.cuda()
+        yd = torch.full((1, out_f), float("nan"), device="cuda")
+        keep += [w, xd, yd]
+        dev_ops.append(mlq.linear_op(fmt, w.data_ptr(), out_f, in_f, xd.data_ptr(), 1, yd.data_ptr()))
+        host_ops.append(mlq.linear_op(fmt, w.data_ptr(), out_f, in_f, x.data_ptr(), 1, yh.data_ptr()))
+        hx.append(x)
+        hy.append(yh)
+        refs.append((wb, yd))
+    mlq.Batch(dev_ops).run(None)
+    torch.cuda.synchronize()
+    hb = mlq.Batch(host_ops)
+    for it in range(2):
+        for y in hy:
+            y.fill_(float("nan"))
+        hb.run_host(0)
+        for k, (y, (_, yd)) in enumerate(zip(hy, refs)):
+            np.testing.assert_array_equal(y.numpy(), yd.cpu().numpy(), err_msg=f"op {k} call {it}")
+    # the big op's rows (every 37th, and the last 256: both sides of the
+    # split point) against the oracle
+    fmt, out_f, in_f = specs[1]
+    rows = np.unique(np.r_[0:out_f:37, out_f - 256:out_f])
+    wb = refs[1][0].reshape(out_f, -1)[rows]
+    ref = oracle.linear(fmt, hx[1].numpy(), wb.reshape(-1), len(rows))
+    assert rel_l2_rows(hy[1].numpy()[:, rows], ref).max() <= TOL
+    assert mlq.device_error(0) == 0
