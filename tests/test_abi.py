@@ -271,3 +271,19 @@ def test_gather_wait_validates_before_any_cuda_call(pkg):
     arr = (mlq.LinearOp * 1)(op)
     assert lib.mlq_linear_batch(arr, 1, None) == 10
     assert b"defer_wait" in lib.mlq_last_error()
+
+
+def test_joins_run_follows_the_header_rule(pkg):
+    """mlq.joins_run (the bench's mirror of which batch ops join a run
+    launch) follows include/mlq.h's rule: one row of x, in_features % 4 == 0,
+    a row pitch that is a multiple of 16 bytes, and (q8_0, q4_0) an even
+    block count per row."""
+    mlq = pkg.mlq
+    for fmt, bb in (("q8_0", 34), ("q4_0", 18), ("q4_1", 20)):
+        for in_f in (128, 896, 1024, 1152, 1280, 2048, 2112, 3584, 4096, 4100, 14336, 18944):
+            bpr = (in_f + 31) // 32
+            want = in_f % 4 == 0 and (bpr * bb) % 16 == 0 and (fmt == "q4_1" or bpr % 2 == 0)
+            assert mlq.joins_run(fmt, 1, in_f) == want, (fmt, in_f)
+            assert not mlq.joins_run(fmt, 2, in_f)
+    # the bench's decode step: every product joins
+    assert all(mlq.joins_run("q4_0", 1, i) for i in (3584, 18944))
