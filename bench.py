@@ -466,6 +466,14 @@ class Step:
         self.gathers = [[], []]
         self.names, self.op_bytes, self.launches = [], [], []
         self.one_run = False  # every op of the step in one run launch (set below)
+        # A step whose ops all join one run launch (one row each, at most
+        # RUN_MAX_OPS of them) publishes once, at the end of that launch: its
+        # gathers wait there too (defer_wait 0), with no separate wait kernel.
+        # Otherwise every gathered op only publishes and the step ends with
+        # one mlq_gather_wait.
+        active = [(n, i) for n, _, i in mats if self.plan.active(n) and not (pair and n == pair[1])]
+        one_launch = (rows == 1 and not pair and 2 <= len(active) <= mlq.RUN_MAX_OPS
+                      and all(mlq.joins_run(fmt, rows, i) for _, i in active))
         ops = [[], []]
         grp = None  # (x pointer, matrices) of the open batched-decode group
         for i, (name, out_f, in_f) in enumerate(mats):
@@ -477,9 +485,8 @@ class Step:
                 grp = None  # a gathered op is never grouped
                 k = shard_names.index(name)
                 for p in (0, 1):
-                    # publish only: the step ends with one mlq_gather_wait
                     g = mlq.make_gather(ctx.world, ctx.rank, b, e, self.slab.peer_ptrs(p, k),
-                                        ctx.flags.peers, epoch=1, defer_wait=True)
+                                        ctx.flags.peers, epoch=1, defer_wait=not one_launch)
                     self.gathers[p].append(g)
                     ops[p].append(mlq.linear_op(fmt, wp, out_f, in_f, self.x[name].data_ptr(), rows,
                                                 self.slab.local_ptr(p, k), gather=g))
@@ -549,7 +556,7 @@ class Step:
             k = max(j, k + 1)
         # the step's one cross-rank wait: every rank's highest epoch of the step
         self.waiter = (mlq.make_gather(ctx.world, ctx.rank, 0, 0, [0] * ctx.world, ctx.flags.peers, epoch=1)
-                       if shard_names else None)
+                       if shard_names and not one_launch else None)
         if self.waiter is not None and ctx.world > 1:
             self.launches.append(1)  # mlq_gather_wait's kernel, once per step
         self.batch = [mlq.Batch(ops[0]), mlq.Batch(ops[1])]

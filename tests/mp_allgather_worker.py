@@ -55,8 +55,9 @@ def run_phase(mlq, orc, group, flags, rank, world, dev, stream, epoch):
     """A batch the library runs as one persistent launch: four row-sharded
     one-row q4_0 matrices (deferred gathers sharing the flag words; the last
     one's rows all on rank 0, so every other rank's op has an empty shard)
-    and one local matrix, then one mlq_gather_wait for the highest epoch;
-    three steps, every full y checked on this rank against the oracle."""
+    and one local matrix, then one mlq_gather_wait for the highest epoch
+    (the middle step instead waits inside the run launch); three steps,
+    every full y checked on this rank against the oracle."""
     fmt = "q4_0"
     mats = [(4608, 3584, None), (18944, 3584, None), (3584, 18944, None), (1024, 3584, [0])]
     lins, shards, blocks, checks = [], [], [], []
@@ -89,15 +90,18 @@ def run_phase(mlq, orc, group, flags, rank, world, dev, stream, epoch):
         for k, lin in enumerate(lins):
             epoch += 1
             yb = lin.ybuf[epoch & 1]
+            # steps 0 and 2: publish in the launch, wait in mlq_gather_wait;
+            # step 1: the run launch itself waits for every rank
             g = mlq.make_gather(world, rank, lin.begin, lin.end, yb.peers, flags.peers, epoch=epoch,
-                                defer_wait=True)
+                                defer_wait=(it != 1))
             gs.append(g)
             yptrs.append(yb.local)
             wp = shards[k].data_ptr() if shards[k] is not None else 0
             ops.append(mlq.linear_op(fmt, wp, lin.out, lin.inp, xds[k].data_ptr(), 1, yb.local, gather=g))
         ops.append(mlq.linear_op(fmt, lw.data_ptr(), 1024, 3584, xld.data_ptr(), 1, ly.data_ptr()))
         mlq.Batch(ops).run(stream)
-        mlq.gather_wait(gs[-1], stream)
+        if it != 1:
+            mlq.gather_wait(gs[-1], stream)
         torch.cuda.synchronize()
         for k, (out_f, in_f, _) in enumerate(mats):
             y = sh.device_view(yptrs[k], (1, out_f)).cpu().numpy()[:, checks[k]]
